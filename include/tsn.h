@@ -1,0 +1,164 @@
+/* tsn.h — C ABI of the B200 (sm_100a) MMDiT denoising path of thinksound-native.
+ *
+ * Three faces, each replacing one layer of the reference (paths relative to the reference repo):
+ *   device face   tsn_device_* / tsn_alloc / tsn_dispatch / tsn_commit   -> src/gpu.h Device (src/gpu.mm)
+ *   runtime face  tsn_gemm / tsn_gemv / tsn_conv / tsn_cfg_euler ...     -> src/net.h Runtime (src/net.mm)
+ *   model face    tsn_dit_*                                              -> src/models.h DitModel
+ *                 (src/dit.cpp, src/dit_fwd.cpp) and the sampler loop of src/pipeline.cpp:126-155
+ *
+ * Conventions: every call returns TSN_OK (0) or a TSN_ERR_* code; tsn_last_error() gives the
+ * message of the last failure on the calling thread. Pointers named *_dev are device (or
+ * managed) addresses; *_host are host addresses; "any" pointers may be either (cudaMemcpyDefault).
+ * All work is issued on the device's stream (tsn_device_set_stream); calls that return results to
+ * the host synchronise that stream. No entry point falls back to the CPU: without a usable
+ * sm_100 device every compute call fails with TSN_ERR_CUDA.
+ */
+#ifndef TSN_H
+#define TSN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    TSN_OK = 0,
+    TSN_ERR_ARG = 1,          /* bad argument or unsupported geometry */
+    TSN_ERR_CUDA = 2,         /* CUDA runtime/driver error, or no usable device */
+    TSN_ERR_IO = 3,           /* file not found / unreadable */
+    TSN_ERR_FORMAT = 4,       /* malformed GGUF */
+    TSN_ERR_MISSING = 5,      /* a tensor the DiT needs is absent or mis-shaped */
+    TSN_ERR_OOM = 6,          /* device allocation failed */
+    TSN_ERR_UNSUPPORTED = 7,  /* kernel name or mode not provided by this build */
+    TSN_ERR_TIMEOUT = 8,      /* a device-side wait gave up (kernel reported through the error word) */
+    TSN_ERR_STATE = 9         /* call out of order (e.g. forward before prepare) */
+};
+
+/* Operand type of the tensor-core GEMMs. F16 matches the reference's device weights
+ * (BF16 GGUF values converted with the reference's f32->f16 rule, src/net.mm:141-168). */
+enum { TSN_COMPUTE_F16 = 0, TSN_COMPUTE_BF16 = 1 };
+
+const char * tsn_last_error(void);
+int tsn_version(void);
+
+/* ------------------------------------------------------------------ device face (src/gpu.h) */
+typedef struct tsn_device tsn_device;
+
+/* Device::init (src/gpu.h:25). Binds CUDA device `ordinal`; creates a private stream. */
+int tsn_device_create(int ordinal, tsn_device ** out);
+/* Device::~Device (src/gpu.h:22). Frees every buffer tsn_alloc returned (the reference has no free). */
+int tsn_device_destroy(tsn_device * dev);
+/* Use an external cudaStream_t (e.g. the caller's framework stream) for all later work. */
+int tsn_device_set_stream(tsn_device * dev, void * cuda_stream);
+void * tsn_device_stream(tsn_device * dev);
+/* Device::alloc (src/gpu.h:26, src/gpu.mm:52-64): zeroed managed memory, so the pointer is
+ * valid on host and device like the reference's unified-memory Buf.p. 0 bytes -> 16 bytes. */
+int tsn_alloc(tsn_device * dev, size_t bytes, void ** out);
+/* Device::wrap (src/gpu.h:28, src/gpu.mm:66-87): register caller memory without copying. */
+int tsn_wrap(tsn_device * dev, const void * p, size_t bytes, void ** out);
+/* Device::begin (src/gpu.h:31). */
+int tsn_begin(tsn_device * dev);
+/* Device::dispatch (src/gpu.h:34-38): run the reference kernel `kernel` by name with its Metal
+ * param block. grid/block are advisory (Metal threadgroup semantics); each kernel uses its own
+ * CUDA launch geometry. Unknown names -> TSN_ERR_UNSUPPORTED (the reference logs and skips). */
+int tsn_dispatch(tsn_device * dev, const char * kernel, const uint32_t grid[3], const uint32_t block[3],
+                 const void * const * bufs, int nbufs, const void * params, size_t nparams);
+/* Device::commit (src/gpu.h:39): synchronise the stream; records the queue time for last_gpu_ms. */
+int tsn_commit(tsn_device * dev);
+/* Device::exec_width (src/gpu.h:40): 32 for every provided kernel, 0 for unknown names. */
+uint32_t tsn_exec_width(tsn_device * dev, const char * kernel);
+/* Device::last_gpu_ms (src/gpu.h:41). */
+double tsn_last_gpu_ms(tsn_device * dev);
+
+/* ------------------------------------------------------------------ runtime face (src/net.h) */
+/* Runtime::gemm (src/net.h:23-24): Y[M,N] = X[M,K]·W[N,K]^T (+bias), X/Y f32, W f16 (wf16=1) or
+ * f32 (wf16=0), leading dimensions in elements (0 = dense). */
+int tsn_gemm(tsn_device * dev, int wf16, const void * W, const void * X, void * Y, const void * bias,
+             uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy);
+/* Runtime::gemv (src/net.h:25-26). */
+int tsn_gemv(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias,
+             uint32_t N, uint32_t K, uint32_t ldw, int wf16);
+/* Runtime::conv (src/net.h:29-31): conv1d of x [T,IC] with W (GGUF [K,IC,OC], i.e. [OC][IC][K]). */
+int tsn_conv(tsn_device * dev, int wf16, const void * W, const void * bias, const void * x, void * y,
+             uint32_t T, uint32_t OL, uint32_t IC, uint32_t OC, uint32_t K, uint32_t stride, uint32_t pad,
+             uint32_t dil, int convt);
+/* Runtime elementwise helpers (src/net.h:36-48). */
+int tsn_silu(tsn_device * dev, void * x, size_t n);
+int tsn_copy(tsn_device * dev, const void * x, void * y, size_t n);
+int tsn_swiglu(tsn_device * dev, const void * a, const void * b, void * y, size_t n);
+int tsn_add(tsn_device * dev, const void * a, const void * b, void * y, size_t n);
+int tsn_add_bcast_col(tsn_device * dev, const void * x, const void * v, void * y, uint32_t S, uint32_t H);
+/* Runtime::cfg_euler (src/net.h:46-47): x += dt·(fu + cfg·(fc − fu)). */
+int tsn_cfg_euler(tsn_device * dev, const void * fc, const void * fu, void * x, size_t n, float cfg, float dt);
+int tsn_mean_cols(tsn_device * dev, const void * x, void * y, uint32_t S, uint32_t H);
+
+/* ------------------------------------------------------------------ model face (src/models.h) */
+typedef struct tsn_dit tsn_dit;
+
+typedef struct tsn_dit_geom {
+    uint32_t H, NH, F, depth, fused_depth, latent_dim;
+    float rope_theta, t_max_period;
+} tsn_dit_geom;
+
+/* DitModel::load (src/models.h:67, src/dit.cpp:29-46): read the GGUF, upload its BF16 tensors to
+ * HBM and convert them there (qkv rows de-interleaved, conv weights reordered to [OC][K][IC],
+ * FFN w1/w3 interleaved). compute_type: TSN_COMPUTE_F16 or TSN_COMPUTE_BF16. */
+int tsn_dit_load(tsn_device * dev, const char * gguf_path, int compute_type, tsn_dit ** out);
+/* Same model from the seeded synthetic fixture generated on the device: bit-identical to loading
+ * the file tsn_gguf_write_synthetic writes for the same geometry and seed. */
+int tsn_dit_load_synthetic(tsn_device * dev, const tsn_dit_geom * g, uint64_t seed, int compute_type, tsn_dit ** out);
+int tsn_dit_free(tsn_dit * m);
+int tsn_dit_get_geom(tsn_dit * m, tsn_dit_geom * out);
+size_t tsn_dit_weight_bytes(tsn_dit * m);
+
+/* Fix the sequence geometry and allocate every activation buffer (src/dit.cpp:63-88):
+ * T latent rows, clip_S clip rows, text_S text rows; arms = 2 runs cond and uncond batched in one
+ * forward (CFG), arms = 1 runs a single arm (the 2-GPU CFG split). */
+int tsn_dit_prepare(tsn_dit * m, uint32_t T, uint32_t clip_S, uint32_t text_S, uint32_t arms);
+
+/* Per-generation conditioning, the outputs of DitModel::prep_conditioning / prep_text_arm
+ * (src/dit.cpp:55-192): clip_pp [C,H], sync_gather [T,H] shared by the arms; text_pp [arms][TS,H]
+ * and gcmlp [arms][H] per arm (cond first). Any-pointers; copied into the model. */
+int tsn_dit_set_conditioning(tsn_dit * m, const float * clip_pp, const float * sync_gather,
+                             const float * text_pp, const float * gcmlp);
+/* Latent x [T,64] (any-pointer in / out). */
+int tsn_dit_set_x(tsn_dit * m, const float * x);
+int tsn_dit_get_x(tsn_dit * m, float * x_out);
+
+/* DitModel::forward (src/dit_fwd.cpp:104-304) for every arm at once at flow time t; writes
+ * flow [arms][T,64] to flow_out (any-pointer). Runs as a replayed CUDA graph. */
+int tsn_dit_forward(tsn_dit * m, float t, float * flow_out);
+/* The same forward run eagerly, keeping the reference's per-tap tensors (src/dit_fwd.cpp:151-301). */
+int tsn_dit_forward_taps(tsn_dit * m, float t, float * flow_out);
+/* Copy tap `name` of arm `arm` from the last tsn_dit_forward_taps, in the reference's row-major
+ * layout, into out (n floats at most). Returns the tap length through *len. */
+int tsn_dit_tap(tsn_dit * m, const char * name, int arm, float * out, size_t n, size_t * len);
+
+/* One sampler step (src/pipeline.cpp:146-148): both forwards + cfg_euler, x updated in place on the
+ * device. Requires arms = 2. */
+int tsn_dit_step(tsn_dit * m, float t, float cfg, float dt);
+/* The Euler loop of src/pipeline.cpp:142-155 (t = 1 - s/steps, dt = t_{s+1} - t_s) over `steps`. */
+int tsn_dit_sample(tsn_dit * m, int steps, float cfg);
+/* Run `n` more steps of the schedule installed by the last tsn_dit_schedule (for timing loops). */
+int tsn_dit_schedule(tsn_dit * m, int steps, float cfg);
+int tsn_dit_run_steps(tsn_dit * m, int n);
+/* End-to-end step through host memory: copy x_host_in to the device, one step, copy x back. */
+int tsn_dit_step_host(tsn_dit * m, const float * x_host_in, float * x_host_out, float t, float cfg, float dt);
+/* Number of kernels one step (forward + cfg_euler + schedule advance) launches. */
+int tsn_dit_kernels_per_step(tsn_dit * m);
+/* Per-kernel-class device time of one eagerly launched step, measured with CUDA events around
+ * each launch: out[0] tensor-core GEMM ms, out[1] attention ms, out[2] other ms, out[3] GEMM
+ * FLOPs, out[4] GEMM launches. */
+int tsn_dit_profile_step(tsn_dit * m, double * out5);
+
+/* ------------------------------------------------------------------ fixtures */
+/* Write the seeded synthetic DiT GGUF (with_prep adds the conditioning-prep tensors). Host only. */
+int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TSN_H */

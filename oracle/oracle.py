@@ -1,0 +1,123 @@
+"""Python access to the CPU oracle (TEST INFRASTRUCTURE — the parity checker).
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference legs may use this
+module. It wraps:
+  * lib/liboracle.so  — the CPU restatement of the reference's DiT path (port.cpp + kernels.cpp)
+  * _ref/ts_ref_dit   — the reference's own host code (src/dit.cpp, src/dit_fwd.cpp, src/net.mm,
+                        src/gguf.cpp) built over a CPU Device; present only where it was built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "lib", "liboracle.so")
+REF_BIN = os.path.join(HERE, "_ref", "ts_ref_dit")
+
+TAPS = ["t_emb", "global_c", "extended_c", "x_in", "text_xn", "a0_q", "a0_k", "a0_v", "a0_out",
+        "jb0_lat", "jb0_clip", "jb0_text", "after_joint", "after_fused", "final_fx", "final_mod", "flow"]
+
+_F = C.POINTER(C.c_float)
+
+
+def _f(a):
+    return a.ctypes.data_as(_F) if a is not None else None
+
+
+class Oracle:
+    def __init__(self, gguf: str):
+        self.L = C.CDLL(LIB)
+        L = self.L
+        L.oracle_load.restype = C.c_void_p
+        L.oracle_load.argtypes = [C.c_char_p]
+        L.oracle_free.argtypes = [C.c_void_p]
+        L.oracle_info.argtypes = [C.c_void_p, C.POINTER(C.c_int)]
+        L.oracle_threads.restype = C.c_int
+        L.oracle_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, C.c_float, _F, _F, _F, _F, _F, C.c_int]
+        L.oracle_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, C.c_float, C.c_float, C.c_float,
+                                  _F, _F, _F, _F, _F, _F, _F, _F]
+        L.oracle_tap.restype = C.c_longlong
+        L.oracle_tap.argtypes = [C.c_void_p, C.c_char_p, _F, C.c_longlong]
+        self.h = L.oracle_load(gguf.encode())
+        if not self.h:
+            raise RuntimeError(f"oracle could not load {gguf}")
+        info = (C.c_int * 6)()
+        L.oracle_info(self.h, info)
+        self.H, self.NH, self.F, self.depth, self.fused_depth, self.latent_dim = list(info)
+
+    def close(self):
+        if self.h:
+            self.L.oracle_free(self.h)
+            self.h = None
+
+    def threads(self) -> int:
+        return self.L.oracle_threads()
+
+    def forward(self, T, C_, TS, x, t, clip_pp, sync_gather, text_pp, gcmlp, taps=False):
+        flow = np.zeros((T, self.latent_dim), np.float32)
+        args = [np.ascontiguousarray(a, dtype=np.float32) for a in (x, clip_pp, sync_gather, text_pp, gcmlp)]
+        self.L.oracle_forward(self.h, T, C_, TS, _f(args[0]), t, _f(args[1]), _f(args[2]), _f(args[3]),
+                              _f(args[4]), _f(flow), int(taps))
+        return flow
+
+    def tap(self, name: str) -> np.ndarray:
+        n = self.L.oracle_tap(self.h, name.encode(), None, 0)
+        if n < 0:
+            raise KeyError(name)
+        out = np.empty(n, np.float32)
+        self.L.oracle_tap(self.h, name.encode(), _f(out), n)
+        return out
+
+    def step(self, T, C_, TS, x, t, cfg, dt, clip_pp, sync_gather, tp_c, gc_c, tp_u, gc_u):
+        x = np.array(x, np.float32, copy=True)
+        fc = np.zeros_like(x)
+        fu = np.zeros_like(x)
+        a = [np.ascontiguousarray(v, dtype=np.float32) for v in (clip_pp, sync_gather, tp_c, gc_c, tp_u, gc_u)]
+        self.L.oracle_step(self.h, T, C_, TS, _f(x), t, cfg, dt, *[_f(v) for v in a], _f(fc), _f(fu))
+        return x, fc, fu
+
+
+def have_ref() -> bool:
+    return os.access(REF_BIN, os.X_OK)
+
+
+def write_inputs(d: str, inputs: dict):
+    os.makedirs(d, exist_ok=True)
+    for k, v in inputs.items():
+        np.ascontiguousarray(v, dtype=np.float32).tofile(os.path.join(d, f"{k}.bin"))
+
+
+def run_ref(mode: str, gguf: str, T: int, C_: int, TS: int, in_dir: str, out_dir: str, *args, threads=None,
+            timeout=3600):
+    """Run the reference-built driver; returns its stdout (JSON for step/sample)."""
+    os.makedirs(out_dir, exist_ok=True)
+    env = dict(os.environ)
+    if threads:
+        env["OMP_NUM_THREADS"] = str(threads)
+    cmd = [REF_BIN, mode, gguf, str(T), str(C_), str(TS), in_dir, out_dir] + [str(a) for a in args]
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout)
+    if r.returncode != 0:
+        raise RuntimeError(f"ts_ref_dit failed ({r.returncode}): {r.stderr[-2000:]}")
+    return r.stdout
+
+
+def read_ref_taps(out_dir: str) -> dict:
+    taps = {}
+    for name in TAPS:
+        p = os.path.join(out_dir, f"nat_{name}.bin") if name != "flow" else os.path.join(out_dir, "flow.bin")
+        if os.path.exists(p):
+            taps[name] = np.fromfile(p, np.float32)
+    return taps
+
+
+def parse_json_line(s: str) -> dict:
+    for line in s.splitlines()[::-1]:
+        line = line.strip()
+        if line.startswith("{"):
+            return json.loads(line)
+    raise ValueError("no JSON line in output")

@@ -1,0 +1,141 @@
+"""The CPU oracle against the reference's own host code and the committed golden vectors.
+
+* port vs reference build: oracle/port.cpp restates src/dit_fwd.cpp; oracle/_ref/ts_ref_dit runs
+  the reference's src/dit_fwd.cpp, src/dit.cpp, src/net.mm and src/gguf.cpp unmodified over the
+  same scalar kernels. They must agree bit for bit on every tap the reference dumps
+  (src/dit_fwd.cpp:151-301) and on a full CFG step (src/pipeline.cpp:146-148).
+* golden: tests/golden/*.npz were produced by the reference build (make_golden.py); the port
+  must reproduce them wherever the reference tree is absent (the GPU hosts).
+"""
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import SEED, TINY, TINY_SEQ, make_geom, make_inputs, rel_l2
+
+import tsn
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+needs_ref = pytest.mark.skipif(not O.have_ref(), reason="oracle/_ref not built (reference tree absent)")
+
+
+def _inputs():
+    return make_inputs(TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"], TINY["H"])
+
+
+@needs_ref
+def test_port_matches_reference_build_forward(tiny_gguf, tmp_path):
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = _inputs()
+    O.write_inputs(str(tmp_path / "in"), inp)
+    O.run_ref("forward", tiny_gguf, T, C, TS, str(tmp_path / "in"), str(tmp_path / "out"), 0.5, "cond")
+    ref = O.read_ref_taps(str(tmp_path / "out"))
+    orc = O.Oracle(tiny_gguf)
+    flow = orc.forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"], inp["text_pp_cond"],
+                       inp["gcmlp_cond"], taps=True)
+    assert set(ref) == set(O.TAPS)
+    for name in O.TAPS:
+        mine = flow.ravel() if name == "flow" else orc.tap(name)
+        assert mine.shape == ref[name].shape, name
+        assert np.array_equal(mine, ref[name]), f"tap {name} differs: rel-L2 {rel_l2(mine, ref[name])}"
+
+
+@needs_ref
+def test_port_matches_reference_build_step(tiny_gguf, tmp_path):
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = _inputs()
+    O.write_inputs(str(tmp_path / "in"), inp)
+    dt = (1.0 - 1.0 / 24) - 1.0
+    O.run_ref("step", tiny_gguf, T, C, TS, str(tmp_path / "in"), str(tmp_path / "out"), 1.0, 5.0, dt)
+    x_ref = np.fromfile(str(tmp_path / "out" / "x_out.bin"), np.float32).reshape(T, 64)
+    orc = O.Oracle(tiny_gguf)
+    x, fc, fu = orc.step(T, C, TS, inp["x"], 1.0, 5.0, np.float32(dt), inp["clip_pp"], inp["sync_gather"],
+                         inp["text_pp_cond"], inp["gcmlp_cond"], inp["text_pp_unc"], inp["gcmlp_unc"])
+    assert np.array_equal(x, x_ref)
+    assert not np.array_equal(fc, fu)   # the arms see different conditioning
+
+
+def _golden(name):
+    p = os.path.join(GOLDEN, name)
+    if not os.path.exists(p):
+        pytest.skip(f"{name} not generated")
+    return dict(np.load(p))
+
+
+def test_synthetic_gguf_bytes_pinned(tiny_gguf):
+    g = _golden("tiny_forward.npz")
+    h = hashlib.sha256(open(tiny_gguf, "rb").read()).hexdigest()
+    assert h == str(g["gguf_sha256"]), "synthetic weight generator drifted from the golden fixture"
+
+
+def test_port_reproduces_golden_forward(tiny_gguf):
+    g = _golden("tiny_forward.npz")
+    T, C, TS = int(g["T"]), int(g["C"]), int(g["TS"])
+    orc = O.Oracle(tiny_gguf)
+    flow = orc.forward(T, C, TS, g["in_x"], float(g["t"]), g["in_clip_pp"], g["in_sync_gather"],
+                       g["in_text_pp_cond"], g["in_gcmlp_cond"], taps=True)
+    assert np.array_equal(flow.ravel(), g["tap_flow"])
+    for name in O.TAPS:
+        if name != "flow":
+            assert np.array_equal(orc.tap(name), g[f"tap_{name}"]), name
+
+
+def test_port_reproduces_golden_sample(tiny_gguf):
+    g = _golden("tiny_sample.npz")
+    T, C, TS = int(g["T"]), int(g["C"]), int(g["TS"])
+    orc = O.Oracle(tiny_gguf)
+    x = g["in_x"].copy()
+    steps, cfg = int(g["steps"]), float(g["cfg"])
+    for s in range(steps):   # src/pipeline.cpp:142-148
+        t_curr = np.float32(1.0) - np.float32(s) / np.float32(steps)
+        t_prev = np.float32(1.0) - np.float32(s + 1) / np.float32(steps)
+        x, _, _ = orc.step(T, C, TS, x, float(t_curr), cfg, float(np.float32(t_prev - t_curr)), g["in_clip_pp"],
+                           g["in_sync_gather"], g["in_text_pp_cond"], g["in_gcmlp_cond"], g["in_text_pp_unc"],
+                           g["in_gcmlp_unc"])
+    assert np.array_equal(x, g["x_final"])
+
+
+def _splitmix64(x):
+    M = (1 << 64) - 1
+    x = (x + 0x9E3779B97F4A7C15) & M
+    x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & M
+    x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & M
+    return x ^ (x >> 31)
+
+
+def _normal(key, idx):
+    s = 0
+    for j in range(3):
+        r = _splitmix64((key + 3 * idx + j) & ((1 << 64) - 1))
+        s += (r & 0xFFFF) + ((r >> 16) & 0xFFFF) + ((r >> 32) & 0xFFFF) + (r >> 48)
+    return np.float32(s - 393210) * np.float32(1.0 / 65536.0)
+
+
+def _key(name, seed):
+    h = 1469598103934665603
+    for ch in name.encode():
+        h = ((h ^ ch) * 1099511628211) & ((1 << 64) - 1)
+    return _splitmix64(h ^ _splitmix64(seed))
+
+
+def _bf16(f):
+    u = int(np.float32(f).view(np.uint32))
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFFFFFF
+    return u >> 16
+
+
+def test_synthetic_values_match_independent_restatement(tiny_gguf):
+    """The C generator (include/tsn_synth.h) against a pure-Python restatement, read back from the file."""
+    from gguf_read import read_tensor
+    key = _key("t_embed.mlp.0.weight", SEED)
+    got = read_tensor(tiny_gguf, "t_embed.mlp.0.weight", 16)
+    want = np.array([_bf16(_normal(key, i) * np.float32(0.02)) for i in range(16)], np.uint16)
+    assert np.array_equal(got, want)
+    key = _key("joint_blocks.0.latent_block.attn.q_norm.weight", SEED)
+    got = read_tensor(tiny_gguf, "joint_blocks.0.latent_block.attn.q_norm.weight", 16)
+    want = np.array([np.float32(1.0) + _normal(key, i) * np.float32(0.02) for i in range(16)], np.float32)
+    assert np.array_equal(got, want)

@@ -1,0 +1,421 @@
+// api.cu — the C ABI of include/tsn.h over DeviceCtx / Model (runtime.h) and the named-kernel
+// compat layer (compat.cu).
+#include <cmath>
+#include <cstring>
+#include <memory>
+
+#include "compat.h"
+#include "gguf_io.h"
+#include "runtime.h"
+
+using namespace tsn;
+
+namespace tsn { const std::string & last_error(); }
+
+struct tsn_device { DeviceCtx ctx; };
+struct tsn_dit { Model m; };
+
+#define CKR(expr)                                                                                   \
+    do {                                                                                            \
+        cudaError_t e_ = (expr);                                                                    \
+        if (e_ != cudaSuccess) return fail(TSN_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+#define TRY(expr) do { int rc_ = (expr); if (rc_) return rc_; } while (0)
+
+extern "C" {
+
+const char * tsn_last_error(void) { return tsn::last_error().c_str(); }
+int tsn_version(void) { return 1; }
+
+// ------------------------------------------------------------------------------- device face
+int tsn_device_create(int ordinal, tsn_device ** out) {
+    if (!out) return fail(TSN_ERR_ARG, "null out");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) return fail(TSN_ERR_CUDA, "no CUDA device");
+    if (ordinal < 0 || ordinal >= n) return fail(TSN_ERR_ARG, "device ordinal out of range");
+    cudaDeviceProp prop{};
+    CKR(cudaGetDeviceProperties(&prop, ordinal));
+    if (prop.major != 10) return fail(TSN_ERR_CUDA, std::string("needs an sm_100 (B200) device, found ") + prop.name);
+    auto d = std::make_unique<tsn_device>();
+    d->ctx.ordinal = ordinal;
+    TRY(d->ctx.activate());
+    CKR(cudaStreamCreateWithFlags(&d->ctx.stream, cudaStreamNonBlocking));
+    d->ctx.own_stream = true;
+    CKR(cudaMalloc(&d->ctx.d_err, 64));
+    CKR(cudaMemset(d->ctx.d_err, 0, 64));
+    CKR(cudaEventCreate(&d->ctx.ev0));
+    CKR(cudaEventCreate(&d->ctx.ev1));
+    *out = d.release();
+    return TSN_OK;
+}
+
+int tsn_device_destroy(tsn_device * dev) {
+    if (!dev) return TSN_OK;
+    DeviceCtx & c = dev->ctx;
+    c.activate();
+    cudaStreamSynchronize(c.stream);
+    for (void * p : c.managed) cudaFree(p);
+    if (c.scratch) cudaFree(c.scratch);
+    if (c.d_err) cudaFree(c.d_err);
+    if (c.ev0) cudaEventDestroy(c.ev0);
+    if (c.ev1) cudaEventDestroy(c.ev1);
+    if (c.own_stream && c.stream) cudaStreamDestroy(c.stream);
+    delete dev;
+    return TSN_OK;
+}
+
+int tsn_device_set_stream(tsn_device * dev, void * s) {
+    if (!dev) return fail(TSN_ERR_ARG, "null device");
+    DeviceCtx & c = dev->ctx;
+    if (c.own_stream && c.stream) { cudaStreamSynchronize(c.stream); cudaStreamDestroy(c.stream); }
+    c.stream = (cudaStream_t) s;
+    c.own_stream = false;
+    return TSN_OK;
+}
+
+void * tsn_device_stream(tsn_device * dev) { return dev ? (void *) dev->ctx.stream : nullptr; }
+
+int tsn_alloc(tsn_device * dev, size_t bytes, void ** out) {
+    if (!dev || !out) return fail(TSN_ERR_ARG, "null argument");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    TRY(dev->ctx.activate());
+    if (bytes == 0) bytes = 16;
+    void * p = nullptr;
+    if (cudaMallocManaged(&p, bytes) != cudaSuccess) return fail(TSN_ERR_OOM, "managed allocation failed");
+    CKR(cudaMemset(p, 0, bytes));
+    CKR(cudaDeviceSynchronize());
+    dev->ctx.managed.push_back(p);
+    *out = p;
+    return TSN_OK;
+}
+
+int tsn_wrap(tsn_device * dev, const void * p, size_t bytes, void ** out) {
+    if (!dev || !out) return fail(TSN_ERR_ARG, "null argument");
+    // Managed/device memory is used as is; host memory is pinned in place (no copy).
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) == cudaSuccess && a.type != cudaMemoryTypeUnregistered) { *out = (void *) p; return TSN_OK; }
+    cudaGetLastError();
+    CKR(cudaHostRegister((void *) p, bytes, cudaHostRegisterMapped));
+    void * d = nullptr;
+    CKR(cudaHostGetDevicePointer(&d, (void *) p, 0));
+    *out = d;
+    return TSN_OK;
+}
+
+int tsn_begin(tsn_device * dev) {
+    if (!dev) return fail(TSN_ERR_ARG, "null device");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    if (dev->ctx.pending) TRY(dev->ctx.sync());
+    dev->ctx.pending = false;
+    return TSN_OK;
+}
+
+int tsn_dispatch(tsn_device * dev, const char * kernel, const uint32_t grid[3], const uint32_t block[3],
+                 const void * const * bufs, int nbufs, const void * params, size_t nparams) {
+    if (!dev || !kernel) return fail(TSN_ERR_ARG, "null argument");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    DeviceCtx & c = dev->ctx;
+    TRY(c.activate());
+    if (!c.pending) { CKR(cudaEventRecord(c.ev0, c.stream)); c.pending = true; }
+    return compat_dispatch(c, kernel, grid, block, bufs, nbufs, params, nparams);
+}
+
+int tsn_commit(tsn_device * dev) {
+    if (!dev) return fail(TSN_ERR_ARG, "null device");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    DeviceCtx & c = dev->ctx;
+    TRY(c.activate());
+    if (!c.pending) return TSN_OK;
+    CKR(cudaEventRecord(c.ev1, c.stream));
+    TRY(c.sync());
+    float ms = 0.0f;
+    CKR(cudaEventElapsedTime(&ms, c.ev0, c.ev1));
+    c.last_ms = ms;
+    c.pending = false;
+    return TSN_OK;
+}
+
+uint32_t tsn_exec_width(tsn_device * dev, const char * kernel) {
+    return dev && kernel && compat_has(kernel) ? 32u : 0u;
+}
+
+double tsn_last_gpu_ms(tsn_device * dev) { return dev ? dev->ctx.last_ms : 0.0; }
+
+// ------------------------------------------------------------------------------- runtime face
+#define RT_BEGIN                                                         \
+    if (!dev) return fail(TSN_ERR_ARG, "null device");                  \
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);                        \
+    DeviceCtx & c = dev->ctx;                                            \
+    TRY(c.activate());                                                   \
+    if (!c.pending) { CKR(cudaEventRecord(c.ev0, c.stream)); c.pending = true; }
+
+int tsn_gemm(tsn_device * dev, int wf16, const void * W, const void * X, void * Y, const void * bias,
+             uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy) {
+    RT_BEGIN
+    return compat_gemm(c, wf16, W, X, Y, bias, M, N, K, ldx ? ldx : K, ldw ? ldw : K, ldy ? ldy : N);
+}
+int tsn_gemv(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias, uint32_t N, uint32_t K,
+             uint32_t ldw, int wf16) {
+    RT_BEGIN
+    return compat_gemv(c, wf16, W, X, Y, bias, N, K, ldw ? ldw : K);
+}
+int tsn_conv(tsn_device * dev, int wf16, const void * W, const void * bias, const void * x, void * y, uint32_t T,
+             uint32_t OL, uint32_t IC, uint32_t OC, uint32_t K, uint32_t stride, uint32_t pad, uint32_t dil, int convt) {
+    RT_BEGIN
+    return compat_conv(c, wf16, W, bias, x, y, T, OL, IC, OC, K, stride, pad, dil, convt);
+}
+int tsn_silu(tsn_device * dev, void * x, size_t n) { RT_BEGIN return compat_elementwise(c, "silu_", x, nullptr, nullptr, n, 0, 0); }
+int tsn_copy(tsn_device * dev, const void * x, void * y, size_t n) { RT_BEGIN return compat_elementwise(c, "copy_", x, nullptr, y, n, 0, 0); }
+int tsn_swiglu(tsn_device * dev, const void * a, const void * b, void * y, size_t n) { RT_BEGIN return compat_elementwise(c, "swiglu_", a, b, y, n, 0, 0); }
+int tsn_add(tsn_device * dev, const void * a, const void * b, void * y, size_t n) { RT_BEGIN return compat_elementwise(c, "add_", a, b, y, n, 0, 0); }
+int tsn_add_bcast_col(tsn_device * dev, const void * x, const void * v, void * y, uint32_t S, uint32_t H) {
+    RT_BEGIN return compat_elementwise(c, "add_bcast_col", x, v, y, (size_t) S * H, H, 0);
+}
+int tsn_cfg_euler(tsn_device * dev, const void * fc, const void * fu, void * x, size_t n, float cfg, float dt) {
+    RT_BEGIN return compat_cfg_euler(c, fc, fu, x, n, cfg, dt);
+}
+int tsn_mean_cols(tsn_device * dev, const void * x, void * y, uint32_t S, uint32_t H) {
+    RT_BEGIN return compat_mean_cols(c, x, y, S, H);
+}
+
+// ------------------------------------------------------------------------------- model face
+static int new_model(tsn_device * dev, int compute_type, tsn_dit ** out, const std::string * path,
+                     const tsn_dit_geom * g, uint64_t seed) {
+    if (!dev || !out) return fail(TSN_ERR_ARG, "null argument");
+    if (compute_type != TSN_COMPUTE_F16 && compute_type != TSN_COMPUTE_BF16) return fail(TSN_ERR_ARG, "bad compute type");
+    *out = nullptr;
+    TRY(dev->ctx.activate());
+    auto m = std::make_unique<tsn_dit>();
+    m->m.dev = &dev->ctx;
+    m->m.bf16 = compute_type;
+    DitGeom dg;
+    if (g) {
+        dg.H = g->H; dg.NH = g->NH; dg.F = g->F; dg.depth = g->depth; dg.fused_depth = g->fused_depth;
+        dg.latent_dim = g->latent_dim; dg.rope_theta = g->rope_theta; dg.t_max_period = g->t_max_period;
+    }
+    std::string err;
+    TRY(load_model(m->m, path, g ? &dg : nullptr, seed, err));
+    *out = m.release();
+    return TSN_OK;
+}
+
+int tsn_dit_load(tsn_device * dev, const char * path, int compute_type, tsn_dit ** out) {
+    if (!path) return fail(TSN_ERR_ARG, "null path");
+    std::string p(path);
+    return new_model(dev, compute_type, out, &p, nullptr, 0);
+}
+
+int tsn_dit_load_synthetic(tsn_device * dev, const tsn_dit_geom * g, uint64_t seed, int compute_type, tsn_dit ** out) {
+    if (!g) return fail(TSN_ERR_ARG, "null geometry");
+    return new_model(dev, compute_type, out, nullptr, g, seed);
+}
+
+int tsn_dit_free(tsn_dit * m) {
+    if (m) { if (m->m.dev) cudaStreamSynchronize(m->m.dev->stream); delete m; }
+    return TSN_OK;
+}
+
+int tsn_dit_get_geom(tsn_dit * m, tsn_dit_geom * o) {
+    if (!m || !o) return fail(TSN_ERR_ARG, "null argument");
+    const DitGeom & g = m->m.g;
+    *o = tsn_dit_geom{g.H, g.NH, g.F, g.depth, g.fused_depth, g.latent_dim, g.rope_theta, g.t_max_period};
+    return TSN_OK;
+}
+
+size_t tsn_dit_weight_bytes(tsn_dit * m) { return m ? m->m.arena_used : 0; }
+
+#define M_BEGIN                                                        \
+    if (!m) return fail(TSN_ERR_ARG, "null model");                    \
+    Model & M = m->m;                                                  \
+    TRY(M.dev->activate());
+#define NEED_PREPARED if (!M.prepared) return fail(TSN_ERR_STATE, "call tsn_dit_prepare first");
+
+int tsn_dit_prepare(tsn_dit * m, uint32_t T, uint32_t C, uint32_t TS, uint32_t arms) {
+    M_BEGIN
+    return M.prepare((int) T, (int) C, (int) TS, (int) arms);
+}
+
+int tsn_dit_set_conditioning(tsn_dit * m, const float * clip_pp, const float * sync_gather, const float * text_pp,
+                             const float * gcmlp) {
+    M_BEGIN NEED_PREPARED
+    const size_t H = M.g.H;
+    cudaStream_t s = M.dev->stream;
+    CKR(cudaMemcpyAsync(M.clip_pp, clip_pp, (size_t) M.C * H * 4, cudaMemcpyDefault, s));
+    CKR(cudaMemcpyAsync(M.sync_gather, sync_gather, (size_t) M.T * H * 4, cudaMemcpyDefault, s));
+    CKR(cudaMemcpyAsync(M.text_pp, text_pp, (size_t) M.B * M.TS * H * 4, cudaMemcpyDefault, s));
+    CKR(cudaMemcpyAsync(M.gcmlp, gcmlp, (size_t) M.B * H * 4, cudaMemcpyDefault, s));
+    CKR(cudaStreamSynchronize(s));
+    return TSN_OK;
+}
+
+int tsn_dit_set_x(tsn_dit * m, const float * x) {
+    M_BEGIN NEED_PREPARED
+    CKR(cudaMemcpyAsync(M.x, x, (size_t) M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
+    CKR(cudaStreamSynchronize(M.dev->stream));
+    return TSN_OK;
+}
+
+int tsn_dit_get_x(tsn_dit * m, float * x) {
+    M_BEGIN NEED_PREPARED
+    CKR(cudaMemcpyAsync(x, M.x, (size_t) M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
+    return M.dev->sync();
+}
+
+int tsn_dit_forward(tsn_dit * m, float t, float * flow_out) {
+    M_BEGIN NEED_PREPARED
+    TRY(M.set_time(t, 0.0f));
+    CKR(cudaGraphLaunch(M.gx_fwd, M.dev->stream));
+    if (flow_out)
+        CKR(cudaMemcpyAsync(flow_out, M.flow, (size_t) M.B * M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
+    return M.dev->sync();
+}
+
+int tsn_dit_forward_taps(tsn_dit * m, float t, float * flow_out) {
+    M_BEGIN NEED_PREPARED
+    std::vector<Op> ops;
+    TRY(M.build_ops(ops, 2, 0.0f));
+    TRY(M.set_time(t, 0.0f));
+    TRY(M.run_ops(ops));
+    if (flow_out)
+        CKR(cudaMemcpyAsync(flow_out, M.flow, (size_t) M.B * M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
+    return M.dev->sync();
+}
+
+static int read_tap(Model & M, const std::string & name, int arm, std::vector<float> & out) {
+    auto it = M.taps.find(name);
+    if (it == M.taps.end()) return fail(TSN_ERR_ARG, "no tap " + name + " (run tsn_dit_forward_taps)");
+    std::vector<uint8_t> raw(it->second.bytes);
+    CKR(cudaMemcpy(raw.data(), it->second.dev, raw.size(), cudaMemcpyDeviceToHost));
+    it->second.convert(raw, arm, out);
+    return TSN_OK;
+}
+
+int tsn_dit_tap(tsn_dit * m, const char * name, int arm, float * out, size_t n, size_t * len) {
+    M_BEGIN NEED_PREPARED
+    if (!name || arm < 0 || arm >= M.B) return fail(TSN_ERR_ARG, "bad tap name or arm");
+    TRY(M.dev->sync());
+    std::vector<float> v;
+    if (std::string(name) == "a0_out") {   // joint attention output rows [lat | clip | text]
+        std::vector<float> a, b, c;
+        TRY(read_tap(M, "a0_out_l", arm, a));
+        TRY(read_tap(M, "a0_out_c", arm, b));
+        TRY(read_tap(M, "a0_out_t", arm, c));
+        v = a; v.insert(v.end(), b.begin(), b.end()); v.insert(v.end(), c.begin(), c.end());
+    } else {
+        TRY(read_tap(M, name, arm, v));
+    }
+    if (len) *len = v.size();
+    if (out) std::memcpy(out, v.data(), std::min(n, v.size()) * 4);
+    return TSN_OK;
+}
+
+static int ensure_step_graph(Model & M, float cfg) {
+    if (M.gx_step && M.step_cfg == cfg) return TSN_OK;
+    TRY(M.build_ops(M.ops_step, 1, cfg));
+    TRY(M.capture(M.ops_step, &M.gx_step));
+    M.step_cfg = cfg;
+    return TSN_OK;
+}
+
+int tsn_dit_step(tsn_dit * m, float t, float cfg, float dt) {
+    M_BEGIN NEED_PREPARED
+    if (M.B != 2) return fail(TSN_ERR_STATE, "tsn_dit_step needs arms = 2");
+    TRY(ensure_step_graph(M, cfg));
+    TRY(M.set_time(t, dt));
+    CKR(cudaGraphLaunch(M.gx_step, M.dev->stream));
+    return M.dev->sync();
+}
+
+int tsn_dit_schedule(tsn_dit * m, int steps, float cfg) {
+    M_BEGIN NEED_PREPARED
+    if (M.B != 2) return fail(TSN_ERR_STATE, "the sampler needs arms = 2");
+    if (steps < 1 || steps > M.max_steps) return fail(TSN_ERR_ARG, "steps out of range");
+    TRY(ensure_step_graph(M, cfg));
+    // src/pipeline.cpp:142-145
+    std::vector<float> tb((size_t) steps * M.g.H), dts(steps);
+    for (int s = 0; s < steps; ++s) {
+        float t_curr = 1.0f - (float) s / steps;
+        float t_prev = 1.0f - (float) (s + 1) / steps;
+        dts[s] = t_prev - t_curr;
+        M.temb_host(t_curr, tb.data() + (size_t) s * M.g.H);
+    }
+    CKR(cudaMemcpy(M.temb_tab, tb.data(), tb.size() * 4, cudaMemcpyHostToDevice));
+    CKR(cudaMemcpy(M.dt_tab, dts.data(), dts.size() * 4, cudaMemcpyHostToDevice));
+    CKR(cudaMemsetAsync(M.step, 0, 4, M.dev->stream));
+    M.sched_steps = steps;
+    return TSN_OK;
+}
+
+int tsn_dit_run_steps(tsn_dit * m, int n) {
+    M_BEGIN NEED_PREPARED
+    if (!M.gx_step) return fail(TSN_ERR_STATE, "call tsn_dit_schedule first");
+    for (int i = 0; i < n; ++i) CKR(cudaGraphLaunch(M.gx_step, M.dev->stream));
+    return TSN_OK;
+}
+
+int tsn_dit_sample(tsn_dit * m, int steps, float cfg) {
+    TRY(tsn_dit_schedule(m, steps, cfg));
+    TRY(tsn_dit_run_steps(m, steps));
+    return m->m.dev->sync();
+}
+
+int tsn_dit_step_host(tsn_dit * m, const float * x_in, float * x_out, float t, float cfg, float dt) {
+    M_BEGIN NEED_PREPARED
+    if (M.B != 2) return fail(TSN_ERR_STATE, "tsn_dit_step_host needs arms = 2");
+    TRY(ensure_step_graph(M, cfg));
+    const size_t bytes = (size_t) M.T * M.g.latent_dim * 4;
+    std::vector<float> tb(M.g.H);
+    M.temb_host(t, tb.data());
+    cudaStream_t s = M.dev->stream;
+    CKR(cudaMemcpyAsync(M.x, x_in, bytes, cudaMemcpyHostToDevice, s));
+    CKR(cudaMemcpyAsync(M.temb_tab, tb.data(), M.g.H * 4, cudaMemcpyHostToDevice, s));
+    CKR(cudaMemcpyAsync(M.dt_tab, &dt, 4, cudaMemcpyHostToDevice, s));
+    CKR(cudaMemsetAsync(M.step, 0, 4, s));
+    CKR(cudaGraphLaunch(M.gx_step, s));
+    CKR(cudaMemcpyAsync(x_out, M.x, bytes, cudaMemcpyDeviceToHost, s));
+    return M.dev->sync();
+}
+
+int tsn_dit_kernels_per_step(tsn_dit * m) {
+    if (!m || !m->m.prepared) return 0;
+    return (int) m->m.ops_fwd.size() + 2;
+}
+
+int tsn_dit_profile_step(tsn_dit * m, double * out5) {
+    M_BEGIN NEED_PREPARED
+    if (!out5) return fail(TSN_ERR_ARG, "null out");
+    const std::vector<Op> & ops = M.ops_fwd;
+    std::vector<cudaEvent_t> ev(ops.size() + 1);
+    for (auto & e : ev) CKR(cudaEventCreate(&e));
+    cudaStream_t s = M.dev->stream;
+    CKR(cudaEventRecord(ev[0], s));
+    for (size_t i = 0; i < ops.size(); ++i) {
+        cudaError_t e = ops[i].fn(s);
+        if (e != cudaSuccess) return fail(TSN_ERR_CUDA, "launch " + ops[i].name + ": " + cudaGetErrorString(e));
+        CKR(cudaEventRecord(ev[i + 1], s));
+    }
+    TRY(M.dev->sync());
+    double t[3] = {0, 0, 0}, fl = 0, n = 0;
+    for (size_t i = 0; i < ops.size(); ++i) {
+        float ms = 0;
+        CKR(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+        t[ops[i].kind] += ms;
+        if (ops[i].kind == 0) { fl += ops[i].flops; n += 1; }
+    }
+    for (auto & e : ev) cudaEventDestroy(e);
+    out5[0] = t[0]; out5[1] = t[1]; out5[2] = t[2]; out5[3] = fl; out5[4] = n;
+    return TSN_OK;
+}
+
+int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep) {
+    if (!path || !g) return fail(TSN_ERR_ARG, "null argument");
+    DitGeom dg;
+    dg.H = g->H; dg.NH = g->NH; dg.F = g->F; dg.depth = g->depth; dg.fused_depth = g->fused_depth;
+    dg.latent_dim = g->latent_dim; dg.rope_theta = g->rope_theta; dg.t_max_period = g->t_max_period;
+    std::string err;
+    if (!write_synthetic_gguf(path, dg, seed, with_prep != 0, err)) return fail(TSN_ERR_IO, err);
+    return TSN_OK;
+}
+
+} // extern "C"

@@ -1,0 +1,102 @@
+// dit_schema.cpp — tensor inventory of the MMDiT (see dit_schema.h for the reference citations).
+#include "dit_schema.h"
+
+#include "../../include/tsn_synth.h"
+
+namespace tsn {
+
+namespace {
+struct Builder {
+    std::vector<TensorSpec> v;
+    void mat(const std::string & n, uint64_t in, uint64_t out) {            // linear [out,in]
+        TensorSpec t; t.name = n; t.n_dims = 2; t.ne[0] = in; t.ne[1] = out; v.push_back(t);
+    }
+    void conv(const std::string & n, uint64_t K, uint64_t IC, uint64_t OC) {  // conv1d [OC,IC,K]
+        TensorSpec t; t.name = n; t.n_dims = 3; t.ne[0] = K; t.ne[1] = IC; t.ne[2] = OC; v.push_back(t);
+    }
+    void vec(const std::string & n, uint64_t len, int init = TSN_INIT_NORMAL, float scale = 0.02f) {
+        TensorSpec t; t.name = n; t.n_dims = 1; t.ne[0] = len; t.type = GG_F32; t.init = init; t.scale = scale;
+        v.push_back(t);
+    }
+    void f32mat(const std::string & n, uint64_t in, uint64_t rows, float scale) {
+        TensorSpec t; t.name = n; t.n_dims = 2; t.ne[0] = in; t.ne[1] = rows; t.type = GG_F32; t.scale = scale;
+        v.push_back(t);
+    }
+    void linear(const std::string & p, uint64_t in, uint64_t out) { mat(p + ".weight", in, out); vec(p + ".bias", out); }
+};
+} // namespace
+
+std::vector<TensorSpec> dit_schema(const DitGeom & g, bool with_prep) {
+    Builder b;
+    const uint64_t H = g.H, F = g.F, L = g.latent_dim, hd = g.hd();
+    // timestep MLP                                             src/dit_fwd.cpp:122-128
+    b.linear("t_embed.mlp.0", H, H);
+    b.linear("t_embed.mlp.2", H, H);
+    // audio_input_proj: conv k3 L->H (+bias), convmlp          src/dit_fwd.cpp:143-149
+    b.conv("audio_input_proj.0.weight", 3, L, H);
+    b.vec("audio_input_proj.0.bias", H);
+    b.conv("audio_input_proj.2.w1.weight", 3, H, F);
+    b.conv("audio_input_proj.2.w3.weight", 3, H, F);
+    b.conv("audio_input_proj.2.w2.weight", 3, F, H);
+    auto block = [&](const std::string & bp, uint64_t chunks, bool post, bool conv_post) {
+        b.linear(bp + ".adaLN_modulation.1", H, chunks * H);
+        b.linear(bp + ".attn.qkv", H, 3 * H);
+        b.vec(bp + ".attn.q_norm.weight", hd, TSN_INIT_ONE_PLUS, 0.02f);
+        b.vec(bp + ".attn.k_norm.weight", hd, TSN_INIT_ONE_PLUS, 0.02f);
+        if (!post) return;
+        if (conv_post) {
+            b.conv(bp + ".linear1.weight", 3, H, H);
+            b.vec(bp + ".linear1.bias", H);
+            b.conv(bp + ".ffn.w1.weight", 3, H, F);
+            b.conv(bp + ".ffn.w3.weight", 3, H, F);
+            b.conv(bp + ".ffn.w2.weight", 3, F, H);
+        } else {
+            b.linear(bp + ".linear1", H, H);
+            b.mat(bp + ".ffn.w1.weight", H, F);
+            b.mat(bp + ".ffn.w3.weight", H, F);
+            b.mat(bp + ".ffn.w2.weight", F, H);
+        }
+    };
+    // joint blocks; the last one is pre_only (clip/text 2H mod, no post)   src/dit_fwd.cpp:180-257
+    for (uint32_t i = 0; i < g.n_joint(); ++i) {
+        const bool pre_only = i + 1 == g.n_joint();
+        const std::string jb = "joint_blocks." + std::to_string(i);
+        block(jb + ".latent_block", 6, true, true);
+        block(jb + ".clip_block", pre_only ? 2 : 6, !pre_only, true);
+        block(jb + ".text_block", pre_only ? 2 : 6, !pre_only, false);
+    }
+    // fused blocks                                             src/dit_fwd.cpp:268-279
+    for (uint32_t i = 0; i < g.fused_depth; ++i) block("fused_blocks." + std::to_string(i), 6, true, true);
+    // final layer                                              src/dit_fwd.cpp:288-303
+    b.linear("final_layer.adaLN_modulation.1", H, 2 * H);
+    b.conv("final_layer.conv.weight", 7, H, L);
+    b.vec("final_layer.conv.bias", L);
+    if (with_prep) {                                            // src/dit.cpp:92-192, pipeline.cpp:86-106
+        b.f32mat("sync_pos_emb", 768, 8, 0.02f);
+        b.conv("sync_input_proj.0.weight", 7, 768, H);
+        b.vec("sync_input_proj.0.bias", H);
+        b.conv("sync_input_proj.2.w1.weight", 3, H, F);
+        b.conv("sync_input_proj.2.w3.weight", 3, H, F);
+        b.conv("sync_input_proj.2.w2.weight", 3, F, H);
+        b.linear("clip_input_proj.0", 1024, H);
+        b.conv("clip_input_proj.2.w1.weight", 3, H, F);
+        b.conv("clip_input_proj.2.w3.weight", 3, H, F);
+        b.conv("clip_input_proj.2.w2.weight", 3, F, H);
+        b.linear("clip_cond_proj", 1024, H);
+        b.linear("text_input_proj.0", 2048, H);
+        b.mat("text_input_proj.2.w1.weight", H, F);
+        b.mat("text_input_proj.2.w3.weight", H, F);
+        b.mat("text_input_proj.2.w2.weight", F, H);
+        b.linear("text_cond_proj", 1024, H);
+        b.mat("global_cond_mlp.w1.weight", H, F);
+        b.mat("global_cond_mlp.w3.weight", H, F);
+        b.mat("global_cond_mlp.w2.weight", F, H);
+        b.vec("empty_clip_feat", 1024, TSN_INIT_NORMAL, 1.0f);
+        b.vec("empty_sync_feat", 768, TSN_INIT_NORMAL, 1.0f);
+        b.f32mat("empty_string_feat", 1024, 77, 1.0f);
+        b.f32mat("empty_t5_feat", 2048, 77, 1.0f);
+    }
+    return b.v;
+}
+
+} // namespace tsn

@@ -1,0 +1,38 @@
+// dit_schema.h — the tensor inventory of the ThinkSound MMDiT GGUF and the synthetic fixture.
+//
+// Names, shapes (GGUF ne order: ne[0] fastest) and which tensors exist follow the reference's
+// use of them: DitModel::forward (src/dit_fwd.cpp:104-304), DitModel::load (src/dit.cpp:29-46),
+// prep_conditioning / prep_text_arm (src/dit.cpp:55-192) and the pipeline's empty features
+// (src/pipeline.cpp:86-106). Linear weights [out,in] are ne = {in, out}; conv1d weights
+// [OC,IC,K] are ne = {K, IC, OC} (src/net.h:109-110).
+#pragma once
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace tsn {
+
+struct DitGeom {
+    uint32_t H = 1024, NH = 16, F = 4096, depth = 21, fused_depth = 14, latent_dim = 64;
+    float rope_theta = 10000.0f, t_max_period = 1.0f;
+    uint32_t n_joint() const { return depth - fused_depth; }
+    uint32_t hd() const { return H / NH; }
+};
+
+enum : uint32_t { GG_F32 = 0, GG_F16 = 1, GG_BF16 = 30 };
+
+struct TensorSpec {
+    std::string name;
+    uint32_t n_dims = 0;
+    uint64_t ne[4] = {1, 1, 1, 1};
+    uint32_t type = GG_BF16;
+    int init = 0;          // tsn_init_kind
+    float scale = 0.02f;
+    uint64_t nelem() const { uint64_t n = 1; for (uint32_t d = 0; d < n_dims; ++d) n *= ne[d]; return n; }
+};
+
+// with_prep adds the once-per-generation conditioning weights (sync/clip/text projections,
+// global_cond_mlp, empty features) that DitModel::prep_* and the pipeline read.
+std::vector<TensorSpec> dit_schema(const DitGeom & g, bool with_prep);
+
+} // namespace tsn

@@ -1,0 +1,295 @@
+// gemm_tc.cuh — the BF16/F16 tcgen05 GEMM and implicit-GEMM conv1d of the DiT path.
+//
+// Replaces the reference's im2col + MetalPerformancePrimitives matmul2d pair
+// (shaders/ops_conv.metal:265-283 + shaders/gemm_mpp.metal:18-60, driven by Runtime::gemm /
+// Runtime::conv, src/net.mm:14-49): Y = X·W^T (+bias), f32 accumulate, for every dense
+// projection and every stride-1 conv of the forward.
+//
+// Layout. Activations are [B][rows][K_in] (B = CFG arms), read through a 3-D TMA view
+// {K_in, rows, B} with a box {64, bt, bb}, bt*bb = 128: one 128-row M tile holds bb batches of bt
+// consecutive time rows. A conv with `taps` taps and left padding `pad` walks its K loop over
+// (tap, 64-channel block) and shifts the box by tap-pad rows; rows outside [0, rows) of each batch
+// are zero-filled by TMA, which is exactly the conv's zero padding per batch — no im2col buffer.
+// Weights are [N][taps*K_in], conv weights reordered at load from [OC][IC][K] to [OC][K][IC].
+//
+// Pipeline (one output tile per CTA, 192 threads):
+//   warp 4      TMA producer: A box + B box per 64-wide K block into a STAGES-deep smem ring
+//   warp 5      TMEM allocation + single-thread tcgen05.mma issue (M=128, N=BN, K=16 x 4)
+//   warps 0-3   epilogue: tcgen05.ld rows from TMEM, fused op, global stores
+// Split-K (grid.z) writes f32 partials to a workspace; the last CTA of a tile (arrival counter)
+// sums them in split order 0..S-1 and runs the epilogue, so results are deterministic.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace tsn {
+
+enum GemmEpi : int {
+    EPI_F32 = 0,       // out f32 = acc (+bias)
+    EPI_F16 = 1,       // out f16 = acc (+bias)
+    EPI_F16_SILU = 2,  // out f16 = silu(acc + bias)
+    EPI_SWIGLU = 3,    // columns in groups of 128 = [64 w1 | 64 w3] -> out f16 = silu(a)*b
+    EPI_GATE = 4,      // res f32 += (acc + bias) * mod[row][gate_off + n]
+    EPI_QKV = 5,       // bias, per-head RMSNorm(q,k), RoPE(q,k), f16 head-major q/k/v
+};
+
+struct GemmArgs {
+    int rows, B, bt, bb, m_tiles_t, N, k_blocks, ic_blocks, pad, splits, kb_per_split;
+    float * ws;              // split-K partials
+    int * counters;          // split-K arrival counters, one per output tile, self-resetting
+    int * err;               // device error word
+    const float * bias;      // [N] or null
+    void * out;              // EPI_F32/F16*/SWIGLU output, EPI_GATE residual (f32)
+    long long ldo, out_bs;   // row stride and batch stride of out (elements)
+    const float * mod;       // EPI_GATE modulation rows
+    long long mod_ld, mod_bs;  // row stride; per-batch stride (per-row mods: rows*mod_ld)
+    int mod_per_row, gate_off;
+    // EPI_QKV
+    const float * qn; const float * kn;   // per-head RMSNorm gains [64]
+    const float2 * rope;                  // [rows][32] (cos, sin) or null (text stream)
+    int H, s_off, S_pad, NH;
+    __half * q; __half * k; __half * v;   // [B][NH][S_pad][64]
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+    static constexpr int A_BYTES = 128 * 128;
+    static constexpr int B_BYTES = BN * 128;
+    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int BAR_OFF = STAGES * STAGE;
+    static constexpr int TOTAL = BAR_OFF + 256 + 1024;   // + barriers + alignment slack
+};
+
+__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+
+template <int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const GemmArgs a, const int ab_bf16) {
+    using L = GemmSmem<BN, STAGES>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
+    uint64_t * empty = full + STAGES;
+    uint64_t * tfull = empty + STAGES;
+    uint32_t * tslot = (uint32_t *) (tfull + 1);
+    volatile int * abort_flag = (volatile int *) (tslot + 1);
+    volatile int * last_flag = abort_flag + 1;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = blockIdx.y % a.m_tiles_t, mb = blockIdx.y / a.m_tiles_t;
+    const int t0 = mt * a.bt, b0 = mb * a.bb, n0 = blockIdx.x * BN;
+    const int kb_begin = blockIdx.z * a.kb_per_split;
+    const int kb_end = min(a.k_blocks, kb_begin + a.kb_per_split);
+    const int nk = kb_end - kb_begin;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(tfull, 1);
+        *abort_flag = 0;
+        *last_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 4 && lane == 0) { tma_prefetch(&tmA); tma_prefetch(&tmB); }
+    if (warp == 5) tmem_alloc(tslot, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % STAGES;
+                if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_EMPTY))
+                    break;
+                const int kb = kb_begin + i;
+                const int tap = kb / a.ic_blocks, ic0 = (kb % a.ic_blocks) * 64;
+                uint8_t * sa = smem + s * L::STAGE;
+                mbar_expect_tx(&full[s], L::STAGE);
+                tma_load_3d(sa, &tmA, &full[s], ic0, t0 + tap - a.pad, b0);
+                tma_load_2d(sa + L::A_BYTES, &tmB, &full[s], kb * 64, n0);
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(BN, ab_bf16);
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&full[s], (i / STAGES) & 1, abort_flag, a.err, DEV_TIMEOUT_FULL)) break;
+                tc_fence_after();
+                const uint8_t * sa = smem + s * L::STAGE;
+                const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + L::A_BYTES);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    umma_f16(tmem, ad + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, (i | k) != 0);
+                umma_commit(&empty[s]);
+            }
+            umma_commit(tfull);
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const bool ok = mbar_wait(tfull, 0, abort_flag, a.err, DEV_TIMEOUT_TMEM) && !*abort_flag;
+        tc_fence_after();
+        const int r = warp * 32 + lane;
+        const int b = b0 + r / a.bt, t = t0 + r % a.bt;
+        const bool valid = ok && t < a.rows && b < a.B;
+        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        const int S = a.splits;
+        bool reduce = false;
+        if (S > 1) {
+            // partial -> workspace [tile][split][BN/4][128] float4
+            float4 * wp = (float4 *) a.ws + ((size_t) tile * S + blockIdx.z) * (BN / 4) * 128;
+            for (int c = 0; c < BN; c += 32) {
+                float v[32];
+                tmem_ld32(trow + c, v);
+                if (ok) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        __stcg(&wp[(size_t) (c / 4 + j) * 128 + r], make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
+                }
+            }
+            __threadfence();
+            epi_bar();
+            if (r == 0) {
+                const int prev = atomicAdd(&a.counters[tile], 1);
+                *last_flag = (prev == S - 1);
+            }
+            epi_bar();
+            reduce = *last_flag != 0;
+            if (!reduce) goto teardown;
+            __threadfence();
+        }
+        {
+            const float4 * wbase = (const float4 *) a.ws + (size_t) tile * S * (BN / 4) * 128;
+            // 32 accumulated columns starting at column c of the tile
+            auto load32 = [&](int c, float * v) {
+                if (!reduce) { tmem_ld32(trow + c, v); return; }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    float4 s4 = __ldcg(&wbase[(size_t) (c / 4 + j) * 128 + r]);
+                    for (int sp = 1; sp < S; ++sp) {
+                        const float4 p4 = __ldcg(&wbase[((size_t) sp * (BN / 4) + c / 4 + j) * 128 + r]);
+                        s4.x += p4.x; s4.y += p4.y; s4.z += p4.z; s4.w += p4.w;
+                    }
+                    v[4 * j] = s4.x; v[4 * j + 1] = s4.y; v[4 * j + 2] = s4.z; v[4 * j + 3] = s4.w;
+                }
+            };
+            if constexpr (EPI == EPI_SWIGLU) {
+                static_assert(BN % 128 == 0, "swiglu tiles hold whole [64 a | 64 b] groups");
+                for (int g = 0; g < BN; g += 128) {
+                    for (int j = 0; j < 64; j += 32) {
+                        float va[32], vb[32];
+                        load32(g + j, va);
+                        load32(g + 64 + j, vb);
+                        if (valid) {
+                            const long long nout = (long long) (n0 + g) / 2 + j;
+                            __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + nout;
+#pragma unroll
+                            for (int q = 0; q < 32; q += 8) {
+                                __align__(16) __half h[8];
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(va[q + e]) * vb[q + e]);
+                                *(uint4 *) (o + q) = *(const uint4 *) h;
+                            }
+                        }
+                    }
+                }
+            } else if constexpr (EPI == EPI_QKV) {
+                for (int c = 0; c < BN; c += 64) {
+                    float v[64];
+                    load32(c, v);
+                    load32(c + 32, v + 32);
+                    if (valid) {
+                        const int n = n0 + c, which = n / a.H, head = (n % a.H) >> 6;
+#pragma unroll
+                        for (int e = 0; e < 64; ++e) v[e] += a.bias[n + e];
+                        if (which < 2) {
+                            const float * g = which == 0 ? a.qn : a.kn;
+                            float ss = 0.0f;
+#pragma unroll
+                            for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
+                            const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+#pragma unroll
+                            for (int e = 0; e < 64; ++e) v[e] = v[e] * inv * g[e];
+                            if (a.rope) {
+                                const float2 * cs = a.rope + (size_t) t * 32;
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    const float2 w = cs[j];
+                                    const float x0 = v[2 * j], x1 = v[2 * j + 1];
+                                    v[2 * j] = x0 * w.x - x1 * w.y;
+                                    v[2 * j + 1] = x0 * w.y + x1 * w.x;
+                                }
+                            }
+                        }
+                        __half * dst = which == 0 ? a.q : which == 1 ? a.k : a.v;
+                        dst += (((size_t) b * a.NH + head) * a.S_pad + a.s_off + t) * 64;
+#pragma unroll
+                        for (int q = 0; q < 64; q += 8) {
+                            __align__(16) __half h[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(v[q + e]);
+                            *(uint4 *) (dst + q) = *(const uint4 *) h;
+                        }
+                    }
+                }
+            } else {
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    load32(c, v);
+                    if (!valid) continue;
+                    const int n = n0 + c;
+                    if (a.bias) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] += a.bias[n + e];
+                    }
+                    if constexpr (EPI == EPI_F32) {
+                        float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+#pragma unroll
+                        for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+                    } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU) {
+                        __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+#pragma unroll
+                        for (int q = 0; q < 32; q += 8) {
+                            __align__(16) __half h[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e)
+                                h[e] = __float2half_rn(EPI == EPI_F16_SILU ? silu_f(v[q + e]) : v[q + e]);
+                            *(uint4 *) (o + q) = *(const uint4 *) h;
+                        }
+                    } else if constexpr (EPI == EPI_GATE) {
+                        float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+                        const float * g = a.mod + (long long) b * a.mod_bs + (a.mod_per_row ? (long long) t * a.mod_ld : 0) +
+                                          a.gate_off + n;
+#pragma unroll
+                        for (int q = 0; q < 32; q += 4) {
+                            float4 x = *(float4 *) (o + q);
+                            const float4 gg = *(const float4 *) (g + q);
+                            x.x += v[q] * gg.x; x.y += v[q + 1] * gg.y; x.z += v[q + 2] * gg.z; x.w += v[q + 3] * gg.w;
+                            *(float4 *) (o + q) = x;
+                        }
+                    }
+                }
+            }
+            if (reduce && r == 0) a.counters[tile] = 0;
+        }
+    teardown:;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+    if (*abort_flag && threadIdx.x == 0) {
+        // let TMA copies that were issued but never consumed land before the CTA's smem is reused
+        const uint64_t t1 = global_ns();
+        while (global_ns() - t1 < 20000ull) {}
+    }
+}
+
+} // namespace tsn

@@ -1,0 +1,417 @@
+// kernels.cu — the DiT path's non-GEMM device kernels (sm_100a).
+//
+//   attn_kernel      fused joint attention: replaces attn_qk + softmax_rows + attn_pav
+//                    (shaders/gemm_attn.metal:96-202). Flash-style online softmax over 64-key
+//                    tiles, f16 tensor-core QK^T and PV (mma.sync m16n8k16, f32 accumulate);
+//                    the [NH,S,S] f32 probability tensor of the reference never exists.
+//   adaln_kernel     adaln_ln (shaders/ops_conv.metal:127-144), one warp per row, writing the
+//                    f16 A operand of the next GEMM directly.
+//   gemv_kernel      batched gemv_h (shaders/gemm_attn.metal:48-64): warp per output row, 16-B
+//                    weight loads, every CFG arm from one weight read.
+//   cond_kernel      the per-forward conditioning adds and SiLUs (src/dit_fwd.cpp:131-140) and
+//                    the stream restarts (src/dit_fwd.cpp:166-167) in one pass.
+//   cfg_euler_kernel cfg_euler (shaders/ops_conv.metal:194-201) reading dt from the schedule.
+//   prep_* / synth   load-time weight conversion and synthetic weight generation.
+#include <cstdint>
+
+#include "../../include/tsn_synth.h"
+#include "kernels.h"
+
+namespace tsn {
+
+// =============================================================================== attention
+namespace {
+__device__ __forceinline__ void cp_async16(void * dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// [64 rows][128 B] f16 tile, 16-byte chunk c of row r stored at chunk c ^ (r & 7)
+__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t) ((r * 8 + (c ^ (r & 7))) * 16); }
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2, uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2, uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float * c, const uint32_t * a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *(uint32_t *) &h;
+}
+} // namespace
+
+__global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+    __shared__ __align__(128) uint8_t sQ[64 * 128];
+    __shared__ __align__(128) uint8_t sK[2][64 * 128];
+    __shared__ __align__(128) uint8_t sV[2][64 * 128];
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t head = ((size_t) b * a.NH + h) * (size_t) a.S_pad * 64;
+    const __half * Qg = a.q + head + (size_t) qt * 64 * 64;
+    const __half * Kg = a.k + head;
+    const __half * Vg = a.v + head;
+    auto load_tile = [&](uint8_t * dst, const __half * src) {
+        for (int i = tid; i < 512; i += 128) {
+            const int r = i >> 3, c = i & 7;
+            cp_async16(dst + swz(r, c), src + r * 64 + c * 8);
+        }
+    };
+    load_tile(sQ, Qg);
+    load_tile(sK[0], Kg);
+    load_tile(sV[0], Vg);
+    cp_commit();
+
+    const int nkt = (a.S + 63) >> 6;
+    const int mat = lane >> 3, mrow = lane & 7;
+    uint32_t qf[4][4];
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+
+    for (int j = 0; j < nkt; ++j) {
+        if (j + 1 < nkt) {
+            load_tile(sK[(j + 1) & 1], Kg + (size_t) (j + 1) * 64 * 64);
+            load_tile(sV[(j + 1) & 1], Vg + (size_t) (j + 1) * 64 * 64);
+        }
+        cp_commit();
+        cp_wait1();
+        __syncthreads();
+        if (j == 0) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const int row = warp * 16 + (mat & 1) * 8 + mrow, ch = 2 * kk + (mat >> 1);
+                ldsm_x4(smem_u32(sQ) + swz(row, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+            }
+        }
+        const uint32_t kb = smem_u32(sK[j & 1]), vb = smem_u32(sV[j & 1]);
+        float s[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+            for (int p = 0; p < 4; ++p) {
+                uint32_t r0, r1, r2, r3;
+                const int key = 16 * p + (mat >> 1) * 8 + mrow, ch = 2 * kk + (mat & 1);
+                ldsm_x4(kb + swz(key, ch), r0, r1, r2, r3);
+                mma16816(s[2 * p], qf[kk], r0, r1);
+                mma16816(s[2 * p + 1], qf[kk], r2, r3);
+            }
+        }
+        // scale, mask keys >= S, online softmax (base 2)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            const int key = j * 64 + nt * 8 + 2 * (lane & 3);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const bool ok = key + e < a.S;
+                s[nt][e] = ok ? s[nt][e] * a.scale_log2 : -INFINITY;
+                s[nt][2 + e] = ok ? s[nt][2 + e] * a.scale_log2 : -INFINITY;
+                mx0 = fmaxf(mx0, s[nt][e]);
+                mx1 = fmaxf(mx1, s[nt][2 + e]);
+            }
+        }
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+            mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+        m0 = mn0; m1 = mn1;
+        float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+            s[nt][0] = exp2f(s[nt][0] - mn0); s[nt][1] = exp2f(s[nt][1] - mn0);
+            s[nt][2] = exp2f(s[nt][2] - mn1); s[nt][3] = exp2f(s[nt][3] - mn1);
+            ps0 += s[nt][0] + s[nt][1];
+            ps1 += s[nt][2] + s[nt][3];
+        }
+        l0 = l0 * al0 + ps0;
+        l1 = l1 * al1 + ps1;
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) { o[dt][0] *= al0; o[dt][1] *= al0; o[dt][2] *= al1; o[dt][3] *= al1; }
+        // O += P V
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t pa[4];
+            pa[0] = pack_h2(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = pack_h2(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint32_t r0, r1, r2, r3;
+                const int key = 16 * kk + (mat & 1) * 8 + mrow, ch = 2 * q + (mat >> 1);
+                ldsm_x4_t(vb + swz(key, ch), r0, r1, r2, r3);
+                mma16816(o[2 * q], pa, r0, r1);
+                mma16816(o[2 * q + 1], pa, r2, r3);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+        l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int s_row = qt * 64 + warp * 16 + (lane >> 2) + half * 8;
+        if (s_row >= a.S) continue;
+        __half * dst;
+        if (s_row < a.n0) dst = a.out0 + ((size_t) b * a.n0 + s_row) * a.H;
+        else if (s_row < a.n0 + a.n1) dst = a.out1 + ((size_t) b * a.n1 + (s_row - a.n0)) * a.H;
+        else dst = a.out2 + ((size_t) b * a.n2 + (s_row - a.n0 - a.n1)) * a.H;
+        dst += h * 64 + 2 * (lane & 3);
+        const float inv = half ? i1 : i0;
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt)
+            *(__half2 *) (dst + dt * 8) = __floats2half2_rn(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+    }
+}
+
+cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s) {
+    dim3 grid((a.S + 63) / 64, a.NH, a.B);
+    attn_kernel<<<grid, 128, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+// =============================================================================== adaLN
+template <int NV>
+__global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
+    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (gw >= a.B * a.rows) return;
+    const int b = gw / a.rows, t = gw % a.rows;
+    const float * xr = a.x + (long long) b * a.x_bs + (long long) t * a.H;
+    float4 v[NV];
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        v[i] = *(const float4 *) (xr + (i * 32 + lane) * 4);
+        sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    const float mean = sum / (float) a.H;
+    float var = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const float dx = v[i].x - mean, dy = v[i].y - mean, dz = v[i].z - mean, dw = v[i].w - mean;
+        var += (dx * dx + dy * dy) + (dz * dz + dw * dw);
+    }
+#pragma unroll
+    for (int off = 16; off; off >>= 1) var += __shfl_xor_sync(0xffffffffu, var, off);
+    const float inv = 1.0f / sqrtf(var / (float) a.H + a.eps);
+    const float * m = a.mod + (long long) b * a.mod_bs + (a.per_row ? (long long) t * a.mod_ld : 0) + a.base;
+    __half * o = a.out + (long long) b * a.out_bs + (long long) t * a.H;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int c = (i * 32 + lane) * 4;
+        const float4 sh = *(const float4 *) (m + c), sc = *(const float4 *) (m + a.H + c);
+        __align__(8) __half hv[4];
+        hv[0] = __float2half_rn((v[i].x - mean) * inv * (1.0f + sc.x) + sh.x);
+        hv[1] = __float2half_rn((v[i].y - mean) * inv * (1.0f + sc.y) + sh.y);
+        hv[2] = __float2half_rn((v[i].z - mean) * inv * (1.0f + sc.z) + sh.z);
+        hv[3] = __float2half_rn((v[i].w - mean) * inv * (1.0f + sc.w) + sh.w);
+        *(uint2 *) (o + c) = *(const uint2 *) hv;
+    }
+}
+
+cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s) {
+    const int nrows = a.B * a.rows;
+    const dim3 grid((nrows + 7) / 8);
+    switch (a.H / 128) {
+        case 1: adaln_kernel<1><<<grid, 256, 0, s>>>(a); break;
+        case 2: adaln_kernel<2><<<grid, 256, 0, s>>>(a); break;
+        case 4: adaln_kernel<4><<<grid, 256, 0, s>>>(a); break;
+        case 8: adaln_kernel<8><<<grid, 256, 0, s>>>(a); break;
+        case 12: adaln_kernel<12><<<grid, 256, 0, s>>>(a); break;
+        case 16: adaln_kernel<16><<<grid, 256, 0, s>>>(a); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+// =============================================================================== GEMV
+__device__ __forceinline__ void cvt8(uint4 w, int bf16, float * f) {
+    const uint16_t * h = (const uint16_t *) &w;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        f[e] = bf16 ? __uint_as_float((uint32_t) h[e] << 16) : __half2float(__ushort_as_half(h[e]));
+}
+
+__global__ void __launch_bounds__(256) gemv_kernel(const GemvJob * jobs, int ab_bf16) {
+    const GemvJob j = jobs[blockIdx.y];
+    const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (n >= j.N) return;
+    const float * x = j.x + (j.x_step ? (long long) (*j.x_step) * j.x_step_stride : 0);
+    const uint16_t * w = (const uint16_t *) j.W + (size_t) n * j.K;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int k = lane * 8; k < j.K; k += 256) {
+        float wf[8];
+        cvt8(__ldg((const uint4 *) (w + k)), ab_bf16, wf);
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+            if (bb >= j.nb) break;
+            const float * xb = x + bb * j.x_bs + k;
+            const float4 x0 = *(const float4 *) xb, x1 = *(const float4 *) (xb + 4);
+            acc[bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
+                       wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
+        }
+    }
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) {
+        if (bb >= j.nb) break;
+        float v = acc[bb];
+#pragma unroll
+        for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        if (lane == 0) {
+            if (j.bias) v += j.bias[n];
+            if (j.act == 1) v = v / (1.0f + expf(-v));
+            j.y[bb * j.y_bs + n] = v;
+        }
+    }
+}
+
+cudaError_t launch_gemv(const GemvJob * jobs_dev, int njobs, int max_n, int ab_bf16, cudaStream_t s) {
+    dim3 grid((max_n + 7) / 8, njobs);
+    gemv_kernel<<<grid, 256, 0, s>>>(jobs_dev, ab_bf16);
+    return cudaGetLastError();
+}
+
+// =============================================================================== conditioning
+__device__ __forceinline__ float silu_d(float v) { return v / (1.0f + expf(-v)); }
+
+__global__ void cond_kernel(const CondArgs a) {
+    const long long nA = (long long) a.B * a.H;
+    const long long nB = nA + (long long) a.B * a.T * a.H;
+    const long long nC = nB + (long long) a.B * a.C * a.H;
+    const long long nD = nC + (long long) a.B * a.TS * a.H;
+    const long long nE = nD + (long long) a.B * a.T * a.L;
+    for (long long i = blockIdx.x * (long long) blockDim.x + threadIdx.x; i < nE; i += (long long) gridDim.x * blockDim.x) {
+        if (i < nA) {
+            const int b = (int) (i / a.H), c = (int) (i % a.H);
+            const float gc = a.gcmlp[(long long) b * a.H + c] + a.te[c];           // dit_fwd.cpp:131
+            a.gc_silu[i] = silu_d(gc);                                             // dit_fwd.cpp:140
+            if (a.tap_gc) a.tap_gc[i] = gc;
+        } else if (i < nB) {
+            const long long r = i - nA;
+            const int c = (int) (r % a.H);
+            const long long bt = r / a.H;
+            const int t = (int) (bt % a.T), b = (int) (bt / a.T);
+            const float gc = a.gcmlp[(long long) b * a.H + c] + a.te[c];
+            const float e = a.sync_gather[(long long) t * a.H + c] + gc;           // dit_fwd.cpp:135
+            a.extc16[r] = __float2half_rn(silu_d(e));                              // dit_fwd.cpp:136-137
+            if (a.tap_extc) a.tap_extc[r] = e;
+        } else if (i < nC) {
+            const long long r = i - nB;                                            // dit_fwd.cpp:166
+            a.clip_s[r] = a.clip_pp[r % ((long long) a.C * a.H)];
+        } else if (i < nD) {
+            const long long r = i - nC;                                            // dit_fwd.cpp:167
+            a.text_s[r] = a.text_pp[r];
+        } else {
+            const long long r = i - nD;
+            a.x16[r] = __float2half_rn(a.x[r % ((long long) a.T * a.L)]);
+        }
+    }
+}
+
+cudaError_t launch_cond(const CondArgs & a, cudaStream_t s) {
+    cond_kernel<<<592, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+// =============================================================================== sampler
+__global__ void cfg_euler_kernel(const float * flow2, float * x, int n, float cfg, const float * dt_table,
+                                 const int * step, float dt_const) {
+    const float dt = dt_table ? dt_table[*step] : dt_const;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const float fc = flow2[i], fu = flow2[n + i];
+        const float v = __fadd_rn(fu, __fmul_rn(__fsub_rn(fc, fu), cfg));
+        x[i] = __fadd_rn(x[i], __fmul_rn(dt, v));
+    }
+}
+__global__ void step_advance_kernel(int * step) { *step += 1; }
+
+cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, float cfg, const float * dt_table,
+                             const int * step, float dt_const, cudaStream_t s) {
+    cfg_euler_kernel<<<(n + 255) / 256, 256, 0, s>>>(flow2, x, n, cfg, dt_table, step, dt_const);
+    return cudaGetLastError();
+}
+cudaError_t launch_step_advance(int * step, cudaStream_t s) {
+    step_advance_kernel<<<1, 1, 0, s>>>(step);
+    return cudaGetLastError();
+}
+
+// =============================================================================== weights
+__device__ __forceinline__ float src_value(const void * src, int type, size_t i) {
+    if (type == 30) return tsn_bf16_to_f32(((const uint16_t *) src)[i]);
+    if (type == 1) {   // the reference's host f16 path flushes f16 subnormals (src/gguf.cpp:203-211)
+        const uint16_t u = ((const uint16_t *) src)[i];
+        if (((u >> 10) & 0x1F) == 0) return (u & 0x8000) ? -0.0f : 0.0f;
+        return tsn_f16_to_f32(u);
+    }
+    return ((const float *) src)[i];
+}
+
+__global__ void prep_weight_kernel(uint16_t * dst, const void * src, const void * src2, int type, int out_bf16,
+                                   long long N, int IC, int taps, int mode, int Hq) {
+    const long long Kt = (long long) IC * taps;
+    const long long total = N * Kt;
+    for (long long idx = blockIdx.x * (long long) blockDim.x + threadIdx.x; idx < total;
+         idx += (long long) gridDim.x * blockDim.x) {
+        const long long n = idx / Kt, kk = idx % Kt;
+        const int tap = (int) (kk / IC), ic = (int) (kk % IC);
+        const void * s = src;
+        long long row = n;
+        if (mode == 1) row = (n % Hq) * 3 + n / Hq;
+        else if (mode == 2) { const long long g = n >> 7, w = n & 127; s = w < 64 ? src : src2; row = g * 64 + (w & 63); }
+        const float f = src_value(s, type, (size_t) row * Kt + (size_t) ic * taps + tap);
+        dst[idx] = out_bf16 ? tsn_f32_to_bf16(f) : tsn_ref_f32_to_f16(f);
+    }
+}
+
+__global__ void prep_vec_kernel(float * dst, const void * src, int type, long long n, int mode, int Hq) {
+    for (long long i = blockIdx.x * (long long) blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x) {
+        const long long si = mode == 1 ? (i % Hq) * 3 + i / Hq : i;
+        dst[i] = src_value(src, type, (size_t) si);
+    }
+}
+
+__global__ void synth_kernel(void * dst, long long n, uint64_t key, int type, int init, float scale) {
+    for (long long i = blockIdx.x * (long long) blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x) {
+        const float v = tsn_init_value(key, (uint64_t) i, init, scale);
+        if (type == 0) ((float *) dst)[i] = v;
+        else ((uint16_t *) dst)[i] = tsn_f32_to_bf16(v);
+    }
+}
+
+cudaError_t launch_prep_weight(void * dst, const void * src, const void * src2, int src_type, int out_bf16,
+                               long long N, int IC, int taps, int mode, int Hq, cudaStream_t s) {
+    prep_weight_kernel<<<1184, 256, 0, s>>>((uint16_t *) dst, src, src2, src_type, out_bf16, N, IC, taps, mode, Hq);
+    return cudaGetLastError();
+}
+cudaError_t launch_prep_vec(float * dst, const void * src, int src_type, long long n, int mode, int Hq, cudaStream_t s) {
+    prep_vec_kernel<<<148, 256, 0, s>>>(dst, src, src_type, n, mode, Hq);
+    return cudaGetLastError();
+}
+cudaError_t launch_synth(void * dst, long long n, uint64_t key, int type, int init, float scale, cudaStream_t s) {
+    synth_kernel<<<1184, 256, 0, s>>>(dst, n, key, type, init, scale);
+    return cudaGetLastError();
+}
+
+} // namespace tsn

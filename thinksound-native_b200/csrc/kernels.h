@@ -1,0 +1,97 @@
+// kernels.h — host-side launch wrappers of the DiT path's device kernels (see kernels.cu,
+// gemm.cu). All launches are asynchronous on the given stream; none allocates.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "gemm_tc.cuh"
+
+namespace tsn {
+
+// ---- GEMM / implicit conv (gemm.cu) ----
+struct GemmLaunch {
+    CUtensorMap ta, tb;
+    GemmArgs args;
+    dim3 grid;
+    int bn = 0, epi = 0, stages = 0, ab_bf16 = 0;
+    size_t smem = 0;
+};
+// Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] 16-bit activation buffer.
+bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t rows, uint64_t B,
+                  uint32_t bt, uint32_t bb, int bf16);
+// Encode a 2-D TMA view {K, N} of an [N][K] 16-bit weight matrix with a {64, bn} box.
+bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16);
+cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
+size_t gemm_smem_bytes(int bn, int stages);
+int gemm_stages(int bn);
+
+// ---- attention (kernels.cu) ----
+struct AttnArgs {
+    const __half * q; const __half * k; const __half * v;   // [B][NH][S_pad][64]
+    int B, NH, S, S_pad;
+    float scale_log2;                                        // softmax scale * log2(e)
+    // output streams: joint row s < n0 -> out0 row s; s < n0+n1 -> out1; else out2
+    __half * out0; __half * out1; __half * out2;             // [B][n_i][H]
+    int n0, n1, n2, H;
+};
+cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s);
+
+// ---- adaLN LayerNorm + modulation -> f16 GEMM operand ----
+struct AdaLnArgs {
+    const float * x; long long x_bs;        // [B][rows][H] f32
+    const float * mod; long long mod_bs, mod_ld; int per_row, base;
+    __half * out; long long out_bs;         // [B][rows][H] f16
+    int B, rows, H;
+    float eps;
+};
+cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s);
+
+// ---- batched GEMV y[b][n] = act(W[n,:]·x[b,:] + bias[n]) ----
+struct GemvJob {
+    const void * W; const float * bias;
+    const float * x; long long x_bs;
+    const int * x_step; long long x_step_stride;   // x += (*x_step) * stride when x_step != null
+    float * y; long long y_bs;
+    int N, K, nb, act;                             // act: 0 none, 1 silu
+};
+cudaError_t launch_gemv(const GemvJob * jobs_dev, int njobs, int max_n, int ab_bf16, cudaStream_t s);
+
+// ---- per-forward conditioning prologue (src/dit_fwd.cpp:131-140, 166-167) ----
+struct CondArgs {
+    const float * te;            // [H]  t_embed output
+    const float * gcmlp;         // [B][H]
+    const float * sync_gather;   // [T][H]
+    const float * clip_pp;       // [C][H]
+    const float * text_pp;       // [B][TS][H]
+    const float * x;             // [T][L]
+    float * gc_silu;             // [B][H]
+    __half * extc16;             // [B][T][H]  silu(sync_gather + gcmlp + te)
+    float * clip_s;              // [B][C][H]
+    float * text_s;              // [B][TS][H]
+    __half * x16;                // [B][T][L]
+    float * tap_gc;              // [B][H]     global_c before silu (nullable)
+    float * tap_extc;            // [B][T][H]  extended_c before silu (nullable)
+    int B, T, C, TS, H, L;
+};
+cudaError_t launch_cond(const CondArgs & a, cudaStream_t s);
+
+// ---- x += dt * (fu + cfg * (fc - fu)) (src/pipeline.cpp:148, shaders/ops_conv.metal:194-201) ----
+cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, float cfg, const float * dt_table,
+                             const int * step, float dt_const, cudaStream_t s);
+cudaError_t launch_step_advance(int * step, cudaStream_t s);
+
+// ---- weight preparation ----
+// dst[n][tap*IC + ic] = cvt(src[row(n)][ic][tap]) for conv sources ([OC][IC][K], K=taps) or
+// dst[n][k] = cvt(src[row(n)][k]) for linear sources (taps = 1). row(n) by mode:
+//   0 identity; 1 qkv de-interleave (row j*Hq + c <- 3c + j); 2 [64 w1 | 64 w3] interleave.
+// src_type: 0 f32, 1 f16, 30 bf16 (GGUF types); out_bf16 selects the compute operand type.
+cudaError_t launch_prep_weight(void * dst, const void * src, const void * src2, int src_type, int out_bf16,
+                               long long N, int IC, int taps, int mode, int Hq, cudaStream_t s);
+// f32 vector copy with optional qkv permutation (mode 1) from any GGUF float type.
+cudaError_t launch_prep_vec(float * dst, const void * src, int src_type, long long n, int mode, int Hq, cudaStream_t s);
+// synthetic tensor values, bit-identical to synth_fill_host (include/tsn_synth.h)
+cudaError_t launch_synth(void * dst, long long n, uint64_t key, int type, int init, float scale, cudaStream_t s);
+
+} // namespace tsn

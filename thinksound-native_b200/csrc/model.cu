@@ -1,0 +1,693 @@
+// model.cu — the MMDiT on the device: weight loading/conversion, buffers, the planned launch list
+// of one forward (both CFG arms batched), CUDA-graph replay and per-tap capture.
+//
+// The op sequence restates DitModel::forward (src/dit_fwd.cpp:104-304) with the reference's
+// dispatches fused: adaLN LayerNorm writes the f16 GEMM operand; the qkv GEMM epilogue does the
+// bias, per-head RMSNorm, RoPE and the q|k|v split (qkv_split3 / rms_head / rope_pairs,
+// src/dit_fwd.cpp:30-48); linear1 and w2 epilogues do gate_add (src/dit_fwd.cpp:62-64, 78-80);
+// the w1/w3 GEMM does SwiGLU (src/dit_fwd.cpp:73-75); attention is one kernel; the clip/text
+// adaLN GEMVs of all joint blocks depend only on global_c and run as one batched launch at the
+// start of the forward.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <memory>
+
+#include "../../include/tsn_synth.h"
+#include "gguf_io.h"
+#include "runtime.h"
+
+namespace tsn {
+
+static thread_local std::string g_err;
+int fail(int code, const std::string & msg) { g_err = msg; return code; }
+void clear_error() { g_err.clear(); }
+const std::string & last_error() { return g_err; }
+
+#define CKR(expr)                                                                                   \
+    do {                                                                                            \
+        cudaError_t e_ = (expr);                                                                    \
+        if (e_ != cudaSuccess) return fail(TSN_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+// ------------------------------------------------------------------------------ device context
+int DeviceCtx::activate() {
+    CKR(cudaSetDevice(ordinal));
+    return TSN_OK;
+}
+
+int DeviceCtx::check_device_error() {
+    int h = 0;
+    CKR(cudaMemcpy(&h, d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (h != 0) {
+        CKR(cudaMemset(d_err, 0, sizeof(int)));
+        static const char * what[] = {"ok", "TMA load never landed (full barrier)", "stage never released (empty barrier)",
+                                      "accumulator never completed (tmem barrier)", "bad kernel arguments"};
+        return fail(TSN_ERR_TIMEOUT, std::string("device wait gave up: ") + (h >= 0 && h <= 4 ? what[h] : "unknown"));
+    }
+    return TSN_OK;
+}
+
+int DeviceCtx::sync() {
+    CKR(cudaStreamSynchronize(stream));
+    return check_device_error();
+}
+
+// ------------------------------------------------------------------------------ weights
+namespace {
+
+struct Src {
+    virtual ~Src() = default;
+    virtual const GgufTensorInfo * info(const std::string & name) = 0;
+    // copy/generate the raw GGUF bytes of `name` into device memory dst
+    virtual int stage(const GgufTensorInfo & t, void * dst, cudaStream_t s) = 0;
+};
+
+struct FileSrc : Src {
+    Gguf f;
+    const GgufTensorInfo * info(const std::string & name) override { return f.find(name); }
+    int stage(const GgufTensorInfo & t, void * dst, cudaStream_t s) override {
+        CKR(cudaMemcpyAsync(dst, t.data, t.nbytes, cudaMemcpyHostToDevice, s));
+        return TSN_OK;
+    }
+};
+
+struct SynthSrc : Src {
+    uint64_t seed = 0;
+    std::map<std::string, TensorSpec> specs;
+    std::map<std::string, GgufTensorInfo> infos;
+    SynthSrc(const DitGeom & g, uint64_t sd) : seed(sd) {
+        for (const TensorSpec & s : dit_schema(g, false)) {
+            specs[s.name] = s;
+            GgufTensorInfo t;
+            t.name = s.name;
+            t.n_dims = s.n_dims;
+            for (int d = 0; d < 4; ++d) t.ne[d] = s.ne[d];
+            t.type = s.type;
+            t.nbytes = s.nelem() * (s.type == GG_F32 ? 4 : 2);
+            infos[s.name] = t;
+        }
+    }
+    const GgufTensorInfo * info(const std::string & name) override {
+        auto it = infos.find(name);
+        return it == infos.end() ? nullptr : &it->second;
+    }
+    int stage(const GgufTensorInfo & t, void * dst, cudaStream_t s) override {
+        const TensorSpec & sp = specs[t.name];
+        CKR(launch_synth(dst, (long long) sp.nelem(), tsn_stream_key(sp.name.c_str(), seed), (int) sp.type, sp.init, sp.scale, s));
+        return TSN_OK;
+    }
+};
+
+struct Loader {
+    Model & m;
+    Src & src;
+    cudaStream_t s;
+    void * stA = nullptr, * stB = nullptr;
+    size_t st_bytes = 0;
+    bool dry = false;          // first pass: only sum the arena size
+    size_t need = 0;
+
+    static size_t al(size_t b) { return (b + 255) & ~(size_t) 255; }
+    void * take(size_t bytes) {
+        if (dry) { need += al(bytes); return nullptr; }
+        return m.arena_take(bytes);
+    }
+    int find(const std::string & name, uint32_t dims, const uint64_t * ne, const GgufTensorInfo ** out) {
+        const GgufTensorInfo * t = src.info(name);
+        if (!t) return fail(TSN_ERR_MISSING, "missing tensor " + name);
+        bool ok = t->n_dims == dims && (t->type == GG_F32 || t->type == GG_F16 || t->type == GG_BF16);
+        for (uint32_t d = 0; ok && d < dims; ++d) ok = t->ne[d] == ne[d];
+        if (!ok) return fail(TSN_ERR_MISSING, "tensor " + name + " has an unexpected shape or type");
+        if (t->nbytes > st_bytes && !dry) return fail(TSN_ERR_ARG, "staging too small for " + name);
+        if (dry) st_bytes = std::max(st_bytes, (size_t) t->nbytes);
+        *out = t;
+        return TSN_OK;
+    }
+    // kind: 0 linear [N,K_in], 1 conv [OC=N][IC=K_in][taps], 2 qkv linear (rows de-interleaved)
+    int weight(const std::string & name, int kind, int N, int K_in, int taps, uint16_t ** dst) {
+        const GgufTensorInfo * t;
+        const uint64_t lin[2] = {(uint64_t) K_in, (uint64_t) N};
+        const uint64_t cnv[3] = {(uint64_t) taps, (uint64_t) K_in, (uint64_t) N};
+        int rc = kind == 1 ? find(name, 3, cnv, &t) : find(name, 2, lin, &t);
+        if (rc) return rc;
+        *dst = (uint16_t *) take((size_t) N * K_in * taps * 2);
+        if (dry) return TSN_OK;
+        if ((rc = src.stage(*t, stA, s))) return rc;
+        CKR(launch_prep_weight(*dst, stA, nullptr, (int) t->type, m.bf16, N, K_in, kind == 1 ? taps : 1,
+                               kind == 2 ? 1 : 0, (int) m.g.H, s));
+        return TSN_OK;
+    }
+    int vec(const std::string & name, int n, int mode, float ** dst) {
+        const GgufTensorInfo * t;
+        const uint64_t ne[1] = {(uint64_t) n};
+        int rc = find(name, 1, ne, &t);
+        if (rc) return rc;
+        *dst = (float *) take((size_t) n * 4);
+        if (dry) return TSN_OK;
+        if ((rc = src.stage(*t, stA, s))) return rc;
+        CKR(launch_prep_vec(*dst, stA, (int) t->type, n, mode, (int) m.g.H, s));
+        return TSN_OK;
+    }
+    int linear(const std::string & p, int kind, int N, int K_in, int taps, bool bias, Lin & L) {
+        L.N = N; L.K_in = K_in; L.taps = kind == 1 ? taps : 1;
+        int rc = weight(p + ".weight", kind, N, K_in, taps, &L.w);
+        if (!rc && bias) rc = vec(p + ".bias", N, kind == 2 ? 1 : 0, &L.b);
+        return rc;
+    }
+    // w1 and w3 interleaved in [64 w1 rows | 64 w3 rows] groups -> one [2F][taps*K_in] matrix
+    int w13(const std::string & p, bool conv, int F, int K_in, Lin & L) {
+        L.N = 2 * F; L.K_in = K_in; L.taps = conv ? 3 : 1;
+        const GgufTensorInfo * t1, * t3;
+        const uint64_t lin[2] = {(uint64_t) K_in, (uint64_t) F};
+        const uint64_t cnv[3] = {3, (uint64_t) K_in, (uint64_t) F};
+        int rc = conv ? find(p + ".w1.weight", 3, cnv, &t1) : find(p + ".w1.weight", 2, lin, &t1);
+        if (!rc) rc = conv ? find(p + ".w3.weight", 3, cnv, &t3) : find(p + ".w3.weight", 2, lin, &t3);
+        if (rc) return rc;
+        if (t1->type != t3->type) return fail(TSN_ERR_MISSING, p + ": w1/w3 types differ");
+        L.w = (uint16_t *) take((size_t) 2 * F * K_in * L.taps * 2);
+        if (dry) return TSN_OK;
+        if ((rc = src.stage(*t1, stA, s)) || (rc = src.stage(*t3, stB, s))) return rc;
+        CKR(launch_prep_weight(L.w, stA, stB, (int) t1->type, m.bf16, 2 * F, K_in, L.taps, 2, 0, s));
+        return TSN_OK;
+    }
+    int block(const std::string & bp, int chunks, bool post, bool conv, Blk & b) {
+        const int H = (int) m.g.H, F = (int) m.g.F;
+        b.chunks = chunks; b.post = post; b.conv = conv;
+        int rc = linear(bp + ".adaLN_modulation.1", 0, chunks * H, H, 1, true, b.ada);
+        if (!rc) rc = linear(bp + ".attn.qkv", 2, 3 * H, H, 1, true, b.qkv);
+        if (!rc) rc = vec(bp + ".attn.q_norm.weight", (int) m.g.hd(), 0, &b.qn);
+        if (!rc) rc = vec(bp + ".attn.k_norm.weight", (int) m.g.hd(), 0, &b.kn);
+        if (rc || !post) return rc;
+        rc = linear(bp + ".linear1", conv ? 1 : 0, H, H, 3, true, b.l1);
+        if (!rc) rc = w13(bp + ".ffn", conv, F, H, b.w13);
+        if (!rc) rc = linear(bp + ".ffn.w2", conv ? 1 : 0, H, F, 3, false, b.w2);
+        return rc;
+    }
+    int all() {
+        const DitGeom & g = m.g;
+        const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim;
+        int rc = linear("t_embed.mlp.0", 0, H, H, 1, true, m.te0);
+        if (!rc) rc = linear("t_embed.mlp.2", 0, H, H, 1, true, m.te2);
+        if (!rc) rc = linear("audio_input_proj.0", 1, H, L, 3, true, m.ain0);
+        if (!rc) rc = w13("audio_input_proj.2", true, F, H, m.ain13);
+        if (!rc) rc = linear("audio_input_proj.2.w2", 1, H, F, 3, false, m.ain2);
+        const int nj = (int) g.n_joint();
+        m.jl.resize(nj); m.jc.resize(nj); m.jt.resize(nj); m.fb.resize(g.fused_depth);
+        for (int i = 0; !rc && i < nj; ++i) {
+            const bool pre_only = i == nj - 1;
+            const std::string jb = "joint_blocks." + std::to_string(i);
+            rc = block(jb + ".latent_block", 6, true, true, m.jl[i]);
+            if (!rc) rc = block(jb + ".clip_block", pre_only ? 2 : 6, !pre_only, true, m.jc[i]);
+            if (!rc) rc = block(jb + ".text_block", pre_only ? 2 : 6, !pre_only, false, m.jt[i]);
+        }
+        for (uint32_t i = 0; !rc && i < g.fused_depth; ++i)
+            rc = block("fused_blocks." + std::to_string(i), 6, true, true, m.fb[i]);
+        if (!rc) rc = linear("final_layer.adaLN_modulation.1", 0, 2 * H, H, 1, true, m.fada);
+        if (!rc) rc = linear("final_layer.conv", 1, L, H, 7, true, m.fconv);
+        return rc;
+    }
+};
+
+int check_geom(const DitGeom & g) {
+    if (g.NH == 0 || g.H % g.NH || g.hd() != 64) return fail(TSN_ERR_ARG, "head dim must be 64");
+    if (g.H % 256 || g.H > 2048) return fail(TSN_ERR_ARG, "hidden size must be a multiple of 256, at most 2048");
+    if (g.F % 128) return fail(TSN_ERR_ARG, "FFN width must be a multiple of 128");
+    if (g.latent_dim != 64) return fail(TSN_ERR_ARG, "latent_dim must be 64");
+    if (g.depth <= g.fused_depth) return fail(TSN_ERR_ARG, "need at least one joint block");
+    return TSN_OK;
+}
+
+} // namespace
+
+Model::~Model() {
+    if (dev) dev->activate();
+    release_activations();
+    if (arena) cudaFree(arena);
+}
+
+void * Model::arena_take(size_t bytes) {
+    const size_t b = (bytes + 255) & ~(size_t) 255;
+    if (arena_used + b > arena_bytes) return nullptr;
+    void * p = (char *) arena + arena_used;
+    arena_used += b;
+    return p;
+}
+
+int load_model(Model & m, const std::string * path, const DitGeom * sg, uint64_t seed, std::string & err) {
+    std::unique_ptr<Src> src;
+    if (path) {
+        auto fs = std::make_unique<FileSrc>();
+        if (!fs->f.open(*path, err)) return fail(err.rfind("cannot", 0) == 0 ? TSN_ERR_IO : TSN_ERR_FORMAT, err);
+        // DitModel::load (src/dit.cpp:29-46)
+        const Gguf & f = fs->f;
+        m.g.H = (uint32_t) f.num("dit.hidden_dim", 1024);
+        m.g.NH = (uint32_t) f.num("dit.num_heads", 16);
+        m.g.depth = (uint32_t) f.num("dit.depth", 21);
+        m.g.fused_depth = (uint32_t) f.num("dit.fused_depth", 14);
+        m.g.latent_dim = (uint32_t) f.num("dit.latent_dim", 64);
+        m.g.rope_theta = (float) f.num("dit.rope_theta", 10000.0);
+        m.g.t_max_period = (float) f.num("dit.t_embed_max_period", 1.0);
+        const GgufTensorInfo * w1 = f.find("joint_blocks.0.latent_block.ffn.w1.weight");
+        m.g.F = (w1 && w1->n_dims >= 3) ? (uint32_t) w1->ne[2] : 2816;
+        src = std::move(fs);
+    } else {
+        m.g = *sg;
+        src = std::make_unique<SynthSrc>(*sg, seed);
+    }
+    int rc = check_geom(m.g);
+    if (rc) return rc;
+    Loader dry{m, *src, m.dev->stream};
+    dry.dry = true;
+    if ((rc = dry.all())) return rc;
+    CKR(cudaMalloc(&m.arena, dry.need));
+    m.arena_bytes = dry.need;
+    m.arena_used = 0;
+    Loader ld{m, *src, m.dev->stream};
+    ld.st_bytes = dry.st_bytes;
+    CKR(cudaMalloc(&ld.stA, ld.st_bytes));
+    CKR(cudaMalloc(&ld.stB, ld.st_bytes));
+    rc = ld.all();
+    cudaError_t se = cudaStreamSynchronize(m.dev->stream);
+    cudaFree(ld.stA);
+    cudaFree(ld.stB);
+    if (rc) return rc;
+    if (se != cudaSuccess) return fail(TSN_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(se));
+    return TSN_OK;
+}
+
+// ------------------------------------------------------------------------------ activations
+void Model::release_activations() {
+    if (gx_fwd) { cudaGraphExecDestroy(gx_fwd); gx_fwd = nullptr; }
+    if (gx_step) { cudaGraphExecDestroy(gx_step); gx_step = nullptr; }
+    for (void * p : act) cudaFree(p);
+    act.clear();
+    taps.clear();
+    ops_fwd.clear();
+    ops_step.clear();
+    prepared = false;
+}
+
+// reference timestep embedding on the host (src/dit_fwd.cpp:112-119)
+void Model::temb_host(float t, float * out) const {
+    const int H_ = (int) g.H, half = H_ / 2;
+    const float fscale_t = 10000.0f / g.t_max_period;
+    for (int kk = 0; kk < half; ++kk) {
+        float fr = fscale_t * powf(10000.0f, -2.0f * kk / (float) H_);
+        out[kk] = cosf(t * fr);
+        out[half + kk] = sinf(t * fr);
+    }
+}
+
+int Model::prepare(int T_, int C_, int TS_, int B_) {
+    if (T_ < 1 || C_ < 1 || TS_ < 1 || (B_ != 1 && B_ != 2)) return fail(TSN_ERR_ARG, "bad geometry for prepare");
+    release_activations();
+    T = T_; C = C_; TS = TS_; B = B_;
+    S = T + C + TS;
+    S_pad = (S + 63) / 64 * 64;
+    const size_t H = g.H, F = g.F, L = g.latent_dim, NJ = g.n_joint();
+    auto al = [&](size_t bytes, void ** p) -> int {
+        CKR(cudaMalloc(p, bytes));
+        CKR(cudaMemset(*p, 0, bytes));
+        act.push_back(*p);
+        return TSN_OK;
+    };
+#define ALLOC(ptr, bytes) do { int rc_ = al((bytes), (void **) &(ptr)); if (rc_) return rc_; } while (0)
+    ALLOC(x, T * L * 4);
+    ALLOC(clip_pp, C * H * 4);
+    ALLOC(sync_gather, T * H * 4);
+    ALLOC(text_pp, B * TS * H * 4);
+    ALLOC(gcmlp, B * H * 4);
+    ALLOC(te_h, H * 4);
+    ALLOC(te, H * 4);
+    ALLOC(gc_silu, B * H * 4);
+    ALLOC(lat, B * T * H * 4);
+    ALLOC(clip_s, B * C * H * 4);
+    ALLOC(text_s, B * TS * H * 4);
+    ALLOC(modl, B * T * 6 * H * 4);
+    ALLOC(modf, B * T * 2 * H * 4);
+    ALLOC(modc, NJ * B * 6 * H * 4);
+    ALLOC(modt, NJ * B * 6 * H * 4);
+    ALLOC(flow, B * T * L * 4);
+    ALLOC(x16, B * T * L * 2);
+    ALLOC(extc16, B * T * H * 2);
+    ALLOC(xn_l, B * T * H * 2);
+    ALLOC(xn_c, B * C * H * 2);
+    ALLOC(xn_t, B * TS * H * 2);
+    ALLOC(att_l, B * T * H * 2);
+    ALLOC(att_c, B * C * H * 2);
+    ALLOC(att_t, B * TS * H * 2);
+    ALLOC(h_l, B * T * F * 2);
+    ALLOC(h_c, B * C * F * 2);
+    ALLOC(h_t, B * TS * F * 2);
+    ALLOC(q, B * g.NH * S_pad * 64 * 2);
+    ALLOC(k, B * g.NH * S_pad * 64 * 2);
+    ALLOC(v, B * g.NH * S_pad * 64 * 2);
+    ALLOC(rope_l, T * 32 * sizeof(float2));
+    ALLOC(rope_c, C * 32 * sizeof(float2));
+    ALLOC(temb_tab, (size_t) max_steps * H * 4);
+    ALLOC(dt_tab, (size_t) max_steps * 4);
+    ALLOC(step, 64);
+    ws_bytes = (size_t) 48 << 20;
+    ALLOC(ws, ws_bytes);
+    n_counters = 1 << 16;
+    counters_used = 0;
+    ALLOC(counters, (size_t) n_counters * 4);
+    ALLOC(tap_gc, B * H * 4);
+    ALLOC(tap_extc, B * T * H * 4);
+    n_mod_jobs = 2 * (int) NJ;
+    ALLOC(jobs, (size_t) (2 + n_mod_jobs) * sizeof(GemvJob));
+#undef ALLOC
+    // RoPE tables: rope_pairs (shaders/ops_conv.metal:156-169) with positions 0..rows-1
+    // (src/dit_fwd.cpp:171-179); clip positions are scaled by T/C (src/dit_fwd.cpp:170).
+    {
+        const float clip_fscale = (float) T / (float) C;
+        std::vector<float2> tl((size_t) T * 32), tc((size_t) C * 32);
+        for (int j = 0; j < 32; ++j) {
+            const float inv = powf(g.rope_theta, -2.0f * (float) j / 64.0f);
+            for (int t = 0; t < T; ++t) {
+                const float ang = (float) t * 1.0f * inv;
+                tl[(size_t) t * 32 + j] = make_float2(cosf(ang), sinf(ang));
+            }
+            for (int t = 0; t < C; ++t) {
+                const float ang = (float) t * clip_fscale * inv;
+                tc[(size_t) t * 32 + j] = make_float2(cosf(ang), sinf(ang));
+            }
+        }
+        CKR(cudaMemcpy(rope_l, tl.data(), tl.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        CKR(cudaMemcpy(rope_c, tc.data(), tc.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    }
+    // GEMV jobs: t_embed.mlp.0 (+silu) from the step's temb row, t_embed.mlp.2, then the clip and
+    // text adaLN modulations of every joint block from silu(global_c) (src/dit_fwd.cpp:122-128, 195-207)
+    {
+        std::vector<GemvJob> j(2 + n_mod_jobs);
+        j[0] = GemvJob{te0.w, te0.b, temb_tab, 0, step, (long long) H, te_h, 0, (int) H, (int) H, 1, 1};
+        j[1] = GemvJob{te2.w, te2.b, te_h, 0, nullptr, 0, te, 0, (int) H, (int) H, 1, 0};
+        for (size_t i = 0; i < NJ; ++i) {
+            j[2 + 2 * i] = GemvJob{jc[i].ada.w, jc[i].ada.b, gc_silu, (long long) H, nullptr, 0,
+                                   modc + i * B * 6 * H, (long long) (6 * H), jc[i].ada.N, (int) H, B, 0};
+            j[3 + 2 * i] = GemvJob{jt[i].ada.w, jt[i].ada.b, gc_silu, (long long) H, nullptr, 0,
+                                   modt + i * B * 6 * H, (long long) (6 * H), jt[i].ada.N, (int) H, B, 0};
+        }
+        CKR(cudaMemcpy(jobs, j.data(), j.size() * sizeof(GemvJob), cudaMemcpyHostToDevice));
+    }
+    prepared = true;
+    int rc = build_ops(ops_fwd, 0, 0.0f);
+    if (rc) return rc;
+    return capture(ops_fwd, &gx_fwd);
+}
+
+// ------------------------------------------------------------------------------ planning
+namespace {
+struct Plan {
+    Model & m;
+    std::vector<Op> & ops;
+
+    // Pick the tile width and split-K factor with a small cost model (per K-block time of one
+    // CTA, waves over 148 SMs, split-K partial traffic), then encode both TMA views.
+    int gemm(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, int epi, GemmLaunch & g) {
+        const int B = m.B;
+        const int bt = B >= 2 ? 64 : 128, bb = 128 / bt;
+        const int mtt = (rows + bt - 1) / bt, mtb = (B + bb - 1) / bb;
+        const int N = W.N, kb = W.taps * K_in / 64;
+        if (K_in % 64 || kb < 1) return fail(TSN_ERR_ARG, std::string(name) + ": K not a multiple of 64");
+        double best = 1e30;
+        int bn_best = 0, s_best = 1;
+        for (int bn : {256, 128, 64}) {
+            if (N % bn) continue;
+            if (epi == EPI_SWIGLU && bn % 128) continue;
+            if (epi == EPI_QKV && bn % 64) continue;
+            const double kcost = bn == 256 ? 0.37 : bn == 128 ? 0.24 : 0.18;
+            const int tiles = mtt * mtb * (N / bn);
+            for (int s = 1; s <= 16 && s <= kb; ++s) {
+                const int kbps = (kb + s - 1) / s;
+                if ((kb + kbps - 1) / kbps != s) continue;
+                if (s > 1 && (size_t) tiles * s * bn * 128 * 4 > m.ws_bytes) continue;
+                if (s > 1 && m.counters_used + tiles > m.n_counters) continue;
+                const int ctas = tiles * s, waves = (ctas + 147) / 148;
+                const double cost = waves * (kbps * kcost + 2.0 + (s > 1 ? (s + 1) * bn * 512.0 / 135e3 : 0.0));
+                if (cost < best - 1e-9) { best = cost; bn_best = bn; s_best = s; }
+            }
+        }
+        if (!bn_best) return fail(TSN_ERR_ARG, std::string(name) + ": no tile fits N=" + std::to_string(N));
+        const int tiles = mtt * mtb * (N / bn_best);
+        g = GemmLaunch{};
+        g.bn = bn_best;
+        g.epi = epi;
+        g.stages = gemm_stages(bn_best);
+        g.smem = gemm_smem_bytes(bn_best, g.stages);
+        g.ab_bf16 = m.bf16;
+        g.grid = dim3(N / bn_best, mtt * mtb, s_best);
+        if (!make_act_map(&g.ta, A, K_in, rows, B, bt, bb, m.bf16) ||
+            !make_w_map(&g.tb, W.w, (uint64_t) W.taps * K_in, N, bn_best, m.bf16))
+            return fail(TSN_ERR_CUDA, std::string(name) + ": tensor map encode failed");
+        GemmArgs & a = g.args;
+        a.rows = rows; a.B = B; a.bt = bt; a.bb = bb; a.m_tiles_t = mtt; a.N = N;
+        a.k_blocks = kb; a.ic_blocks = K_in / 64; a.pad = pad;
+        a.splits = s_best; a.kb_per_split = (kb + s_best - 1) / s_best;
+        a.ws = m.ws;
+        a.counters = m.counters + m.counters_used;
+        if (s_best > 1) m.counters_used += tiles;
+        a.err = m.dev->d_err;
+        a.bias = W.b;
+        return TSN_OK;
+    }
+    void push(const char * name, const GemmLaunch & g, double flops) {
+        ops.push_back(Op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name});
+    }
+    static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
+
+    int out_f32(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * out, int ldo) {
+        GemmLaunch g;
+        int rc = gemm(name, A, K_in, rows, W, pad, EPI_F32, g);
+        if (rc) return rc;
+        g.args.out = out; g.args.ldo = ldo; g.args.out_bs = (long long) rows * ldo;
+        push(name, g, fl(m.B, rows, W));
+        return TSN_OK;
+    }
+    int out_f16(const char * name, int epi, const void * A, int K_in, int rows, const Lin & W, int pad, __half * out, int ldo) {
+        GemmLaunch g;
+        int rc = gemm(name, A, K_in, rows, W, pad, epi, g);
+        if (rc) return rc;
+        g.args.out = out; g.args.ldo = ldo; g.args.out_bs = (long long) rows * ldo;
+        push(name, g, fl(m.B, rows, W));
+        return TSN_OK;
+    }
+    int gate(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * res,
+             const float * mod, int per_row, long long mod_ld, long long mod_bs, int gate_idx) {
+        GemmLaunch g;
+        int rc = gemm(name, A, K_in, rows, W, pad, EPI_GATE, g);
+        if (rc) return rc;
+        g.args.out = res; g.args.ldo = m.g.H; g.args.out_bs = (long long) rows * m.g.H;
+        g.args.mod = mod; g.args.mod_per_row = per_row; g.args.mod_ld = mod_ld; g.args.mod_bs = mod_bs;
+        g.args.gate_off = gate_idx * (int) m.g.H;
+        push(name, g, fl(m.B, rows, W));
+        return TSN_OK;
+    }
+    int qkv(const char * name, const __half * A, int rows, const Blk & b, int s_off, const float2 * rope) {
+        GemmLaunch g;
+        int rc = gemm(name, A, m.g.H, rows, b.qkv, 0, EPI_QKV, g);
+        if (rc) return rc;
+        GemmArgs & a = g.args;
+        a.qn = b.qn; a.kn = b.kn; a.rope = rope; a.H = m.g.H; a.s_off = s_off; a.S_pad = m.S_pad; a.NH = m.g.NH;
+        a.q = m.q; a.k = m.k; a.v = m.v;
+        push(name, g, fl(m.B, rows, b.qkv));
+        return TSN_OK;
+    }
+    void adaln(const char * name, const float * x, int rows, const float * mod, int per_row, long long mod_ld,
+               long long mod_bs, int base, __half * out) {
+        AdaLnArgs a{x, (long long) rows * m.g.H, mod, mod_bs, mod_ld, per_row, base, out, (long long) rows * m.g.H,
+                    m.B, rows, (int) m.g.H, 1e-5f};
+        ops.push_back(Op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name});
+    }
+    void attention(int S, int n0, int n1, int n2) {
+        AttnArgs a{m.q, m.k, m.v, m.B, (int) m.g.NH, S, m.S_pad, 0.125f * 1.4426950408889634f,
+                   m.att_l, m.att_c, m.att_t, n0, n1, n2, (int) m.g.H};
+        const double flops = 4.0 * m.B * (double) S * S * m.g.H;
+        ops.push_back(Op{[a](cudaStream_t s) { return launch_attention(a, s); }, 1, flops, "attention"});
+    }
+    // post_attn (src/dit_fwd.cpp:51-81) for one stream, all arms
+    int post(const Blk & b, float * x, const __half * att, __half * xn, __half * h, int rows, const float * mod,
+             int per_row, long long mod_ld, long long mod_bs) {
+        const int H = (int) m.g.H, F = (int) m.g.F, pad = b.conv ? 1 : 0;
+        int rc = gate("linear1", att, H, rows, b.l1, pad, x, mod, per_row, mod_ld, mod_bs, 2);
+        if (rc) return rc;
+        adaln("adaln_ffn", x, rows, mod, per_row, mod_ld, mod_bs, 3 * H, xn);
+        if ((rc = out_f16("ffn_w13", EPI_SWIGLU, xn, H, rows, b.w13, pad, h, F))) return rc;
+        return gate("ffn_w2", h, F, rows, b.w2, pad, x, mod, per_row, mod_ld, mod_bs, 5);
+    }
+    void tap(const std::string & name, const void * src, size_t bytes,
+             std::function<void(const std::vector<uint8_t> &, int, std::vector<float> &)> cvt) {
+        TapBuf & tb = m.taps[name];
+        if (!tb.dev || tb.bytes != bytes) {
+            if (tb.dev) cudaFree(tb.dev);
+            cudaMalloc(&tb.dev, bytes);
+            tb.bytes = bytes;
+        }
+        tb.convert = std::move(cvt);
+        void * dst = tb.dev;
+        ops.push_back(Op{[dst, src, bytes](cudaStream_t s) { return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s); },
+                         2, 0.0, "tap:" + name});
+    }
+};
+
+// converters from device tap layouts to the reference's per-arm row-major f32 layout
+auto cvt_f32_arm(size_t per_arm) {
+    return [per_arm](const std::vector<uint8_t> & raw, int arm, std::vector<float> & out) {
+        out.resize(per_arm);
+        const float * f = (const float *) raw.data();
+        const size_t avail = raw.size() / 4;
+        const size_t base = per_arm * (size_t) arm;
+        for (size_t i = 0; i < per_arm; ++i) out[i] = base + i < avail ? f[base + i] : NAN;
+    };
+}
+float h2f_host(uint16_t h) { return tsn_f16_to_f32(h); }
+auto cvt_f16_arm(size_t per_arm) {
+    return [per_arm](const std::vector<uint8_t> & raw, int arm, std::vector<float> & out) {
+        out.resize(per_arm);
+        const uint16_t * hh = (const uint16_t *) raw.data();
+        for (size_t i = 0; i < per_arm; ++i) out[i] = h2f_host(hh[per_arm * (size_t) arm + i]);
+    };
+}
+} // namespace
+
+int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
+    ops.clear();
+    if (mode != 2) counters_used = 0;
+    Plan p{*this, ops};
+    const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim, NJ = (int) g.n_joint();
+    const bool tp = mode == 2;
+    const long long lat_mod_bs = (long long) T * 6 * H;
+    int rc;
+    // t-embedding MLP and conditioning                           src/dit_fwd.cpp:111-140
+    GemvJob * jb = jobs;
+    const int nmj = n_mod_jobs;
+    const int bfl = bf16;
+    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb, 1, H, bfl, s); }, 2, 0, "t_embed.0"});
+    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb + 1, 1, H, bfl, s); }, 2, 0, "t_embed.2"});
+    CondArgs ca{te, gcmlp, sync_gather, clip_pp, text_pp, x, gc_silu, extc16, clip_s, text_s, x16,
+                tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L};
+    ops.push_back(Op{[ca](cudaStream_t s) { return launch_cond(ca, s); }, 2, 0, "cond"});
+    ops.push_back(Op{[jb, nmj, H, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, bfl, s); }, 2, 0, "adaln_gemv"});
+    if (tp) {
+        const size_t sH = (size_t) H, sTH = (size_t) T * H;
+        p.tap("t_emb", te, sH * 4, [sH](const std::vector<uint8_t> & raw, int, std::vector<float> & out) {
+            out.assign((const float *) raw.data(), (const float *) raw.data() + sH);
+        });
+        p.tap("global_c", tap_gc, (size_t) B * sH * 4, cvt_f32_arm(sH));
+        p.tap("extended_c", tap_extc, (size_t) B * sTH * 4, cvt_f32_arm(sTH));
+    }
+    // audio_input_proj: conv k3 + silu, convmlp                   src/dit_fwd.cpp:143-149
+    if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H))) return rc;
+    if ((rc = p.out_f16("audio_in.w13", EPI_SWIGLU, xn_l, H, T, ain13, 1, h_l, F))) return rc;
+    if ((rc = p.out_f32("audio_in.w2", h_l, F, T, ain2, 1, lat, H))) return rc;
+    if (tp) p.tap("x_in", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    // joint blocks                                                src/dit_fwd.cpp:180-257
+    for (int i = 0; i < NJ; ++i) {
+        const bool pre_only = i == NJ - 1;
+        float * mc = modc + (size_t) i * B * 6 * H, * mt = modt + (size_t) i * B * 6 * H;
+        if ((rc = p.out_f32("latent_adaln", extc16, H, T, jl[i].ada, 0, modl, 6 * H))) return rc;
+        p.adaln("adaln_attn", lat, T, modl, 1, 6 * H, lat_mod_bs, 0, xn_l);
+        if ((rc = p.qkv("qkv_lat", xn_l, T, jl[i], 0, rope_l))) return rc;
+        p.adaln("adaln_attn", clip_s, C, mc, 0, 0, 6 * H, 0, xn_c);
+        if ((rc = p.qkv("qkv_clip", xn_c, C, jc[i], T, rope_c))) return rc;
+        p.adaln("adaln_attn", text_s, TS, mt, 0, 0, 6 * H, 0, xn_t);
+        if ((rc = p.qkv("qkv_text", xn_t, TS, jt[i], T + C, nullptr))) return rc;
+        if (tp && i == 0) {
+            p.tap("text_xn", xn_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
+            const int NH = (int) g.NH, Sp = S_pad, S_ = S;
+            for (const char * nm : {"a0_q", "a0_k", "a0_v"}) {
+                const __half * src = nm[3] == 'q' ? q : nm[3] == 'k' ? k : v;
+                p.tap(nm, src, (size_t) B * NH * Sp * 64 * 2,
+                      [NH, Sp, S_, H](const std::vector<uint8_t> & raw, int arm, std::vector<float> & out) {
+                          const uint16_t * hh = (const uint16_t *) raw.data();
+                          out.resize((size_t) S_ * H);
+                          for (int s = 0; s < S_; ++s)
+                              for (int h = 0; h < NH; ++h)
+                                  for (int d = 0; d < 64; ++d)
+                                      out[(size_t) s * H + h * 64 + d] =
+                                          h2f_host(hh[(((size_t) arm * NH + h) * Sp + s) * 64 + d]);
+                      });
+            }
+        }
+        p.attention(S, T, C, TS);
+        if ((rc = p.post(jl[i], lat, att_l, xn_l, h_l, T, modl, 1, 6 * H, lat_mod_bs))) return rc;
+        if (!pre_only) {
+            if ((rc = p.post(jc[i], clip_s, att_c, xn_c, h_c, C, mc, 0, 0, 6 * H))) return rc;
+            if ((rc = p.post(jt[i], text_s, att_t, xn_t, h_t, TS, mt, 0, 0, 6 * H))) return rc;
+        }
+        if (tp && i == 0) {
+            // a0_out is the concatenation [lat | clip | text] of these three (tsn_dit_tap joins them)
+            p.tap("a0_out_l", att_l, (size_t) B * T * H * 2, cvt_f16_arm((size_t) T * H));
+            p.tap("a0_out_c", att_c, (size_t) B * C * H * 2, cvt_f16_arm((size_t) C * H));
+            p.tap("a0_out_t", att_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
+            p.tap("jb0_lat", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+            p.tap("jb0_clip", clip_s, (size_t) B * C * H * 4, cvt_f32_arm((size_t) C * H));
+            p.tap("jb0_text", text_s, (size_t) B * TS * H * 4, cvt_f32_arm((size_t) TS * H));
+        }
+    }
+    if (tp) p.tap("after_joint", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    // fused blocks                                                src/dit_fwd.cpp:268-279
+    for (size_t i = 0; i < fb.size(); ++i) {
+        if ((rc = p.out_f32("latent_adaln", extc16, H, T, fb[i].ada, 0, modl, 6 * H))) return rc;
+        p.adaln("adaln_attn", lat, T, modl, 1, 6 * H, lat_mod_bs, 0, xn_l);
+        if ((rc = p.qkv("qkv_lat", xn_l, T, fb[i], 0, rope_l))) return rc;
+        p.attention(T, T, 0, 0);
+        if ((rc = p.post(fb[i], lat, att_l, xn_l, h_l, T, modl, 1, 6 * H, lat_mod_bs))) return rc;
+    }
+    if (tp) p.tap("after_fused", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    // final layer                                                 src/dit_fwd.cpp:287-303
+    if ((rc = p.out_f32("final_adaln", extc16, H, T, fada, 0, modf, 2 * H))) return rc;
+    p.adaln("adaln_final", lat, T, modf, 1, 2 * H, (long long) T * 2 * H, 0, xn_l);
+    if (tp) {
+        p.tap("final_fx", xn_l, (size_t) B * T * H * 2, cvt_f16_arm((size_t) T * H));
+        p.tap("final_mod", modf, (size_t) B * T * 2 * H * 4, cvt_f32_arm((size_t) T * 2 * H));
+    }
+    if ((rc = p.out_f32("final_conv", xn_l, H, T, fconv, 3, flow, L))) return rc;
+    if (tp) p.tap("flow", flow, (size_t) B * T * L * 4, cvt_f32_arm((size_t) T * L));
+    if (mode == 1) {   // sampler update (src/pipeline.cpp:148) and schedule advance
+        float * fl = flow, * xx = x;
+        const float * dtt = dt_tab;
+        int * st = step;
+        const int n = T * L;
+        ops.push_back(Op{[fl, xx, n, cfg, dtt, st](cudaStream_t s) { return launch_cfg_euler(fl, xx, n, cfg, dtt, st, 0.0f, s); },
+                         2, 0, "cfg_euler"});
+        ops.push_back(Op{[st](cudaStream_t s) { return launch_step_advance(st, s); }, 2, 0, "step_advance"});
+    }
+    return TSN_OK;
+}
+
+int Model::run_ops(const std::vector<Op> & ops) {
+    for (const Op & o : ops) {
+        cudaError_t e = o.fn(dev->stream);
+        if (e != cudaSuccess) return fail(TSN_ERR_CUDA, "launch " + o.name + ": " + cudaGetErrorString(e));
+    }
+    return TSN_OK;
+}
+
+int Model::capture(const std::vector<Op> & ops, cudaGraphExec_t * out) {
+    if (*out) { cudaGraphExecDestroy(*out); *out = nullptr; }
+    cudaGraph_t graph = nullptr;
+    CKR(cudaStreamBeginCapture(dev->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = run_ops(ops);
+    cudaError_t e = cudaStreamEndCapture(dev->stream, &graph);
+    if (rc) { if (graph) cudaGraphDestroy(graph); return rc; }
+    if (e != cudaSuccess) return fail(TSN_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+    e = cudaGraphInstantiate(out, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return fail(TSN_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    return TSN_OK;
+}
+
+// temb row 0 and dt row 0 for a single forward/step at time t; schedule position 0
+int Model::set_time(float t, float dt) {
+    std::vector<float> tb(g.H);
+    temb_host(t, tb.data());
+    CKR(cudaMemcpyAsync(temb_tab, tb.data(), g.H * 4, cudaMemcpyHostToDevice, dev->stream));
+    CKR(cudaMemcpyAsync(dt_tab, &dt, 4, cudaMemcpyHostToDevice, dev->stream));
+    CKR(cudaMemsetAsync(step, 0, 4, dev->stream));
+    CKR(cudaStreamSynchronize(dev->stream));   // host sources above are stack/local memory
+    return TSN_OK;
+}
+
+} // namespace tsn

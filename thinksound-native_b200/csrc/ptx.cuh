@@ -1,0 +1,152 @@
+// ptx.cuh — sm_100a building blocks: mbarriers, TMA tensor loads, tcgen05 (UMMA + TMEM).
+//
+// Every wait on an mbarrier is bounded: after TSN_WAIT_NS of wall time (globaltimer) it records
+// an error code in a device-global word, raises the CTA's abort flag and returns false, so a
+// broken pipeline ends the kernel with a status the host reads instead of hanging the GPU.
+// No TMA load here uses .multicast::cluster.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+
+namespace tsn {
+
+#ifndef TSN_WAIT_NS
+#define TSN_WAIT_NS 2000000000ull   // 2 s: every legitimate wait in these kernels is microseconds
+#endif
+
+// error codes written to the device error word
+enum : int { DEV_OK = 0, DEV_TIMEOUT_FULL = 1, DEV_TIMEOUT_EMPTY = 2, DEV_TIMEOUT_TMEM = 3, DEV_BAD_ARGS = 4 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return (uint32_t) __cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t * bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait. abort_flag is a CTA-shared word: once any role gives up, the others stop too.
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity, volatile int * abort_flag,
+                                          int * err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > TSN_WAIT_NS) {
+                *abort_flag = 1;
+                if (err) atomicCAS(err, 0, code);
+                return false;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- TMA (no multicast)
+__device__ __forceinline__ void tma_prefetch(const CUtensorMap * m) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t) m) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void * dst, const CUtensorMap * m, uint64_t * bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"((uint64_t) m), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d(void * dst, const CUtensorMap * m, uint64_t * bar, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"((uint64_t) m), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+__device__ __forceinline__ void tmem_alloc(uint32_t * slot, uint32_t ncols) {      // whole warp
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {     // whole warp
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] · B[smem]^T, M=128, one elected thread issues.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+// Arrive once on bar when every tcgen05 op issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t * bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle, 8-row core groups 1024 B apart.
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void * smem_tile) {
+    const uint32_t a = smem_u32(smem_tile);
+    uint64_t d = 0;
+    d |= (uint64_t) ((a & 0x3FFFFu) >> 4);          // start address   [0,14)
+    d |= (uint64_t) 1u << 16;                        // LBO (unused for swizzled K-major) [16,30)
+    d |= (uint64_t) (1024u >> 4) << 32;              // SBO = 1024 B    [32,46)
+    d |= (uint64_t) 1u << 46;                        // descriptor version (sm100) [46,48)
+    d |= (uint64_t) 2u << 61;                        // layout: SWIZZLE_128B [61,64)
+    return d;
+}
+
+// Instruction descriptor, kind::f16: f32 accumulate, A/B both f16 (ab_bf16=0) or both bf16 (1),
+// both K-major, M=128, N=n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n, int ab_bf16) {
+    return (1u << 4)                                   // D format f32
+         | ((uint32_t) ab_bf16 << 7) | ((uint32_t) ab_bf16 << 10)
+         | ((uint32_t) (n >> 3) << 17)
+         | ((uint32_t) (128 >> 4) << 24);
+}
+
+// 32 lanes x 32 consecutive f32 columns from TMEM into registers (one row per thread).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float * v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// named barrier over the 128 epilogue threads (warps 0-3)
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+} // namespace tsn

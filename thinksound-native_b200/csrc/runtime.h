@@ -1,0 +1,115 @@
+// runtime.h — host-side state behind the C ABI (include/tsn.h): the device context and the
+// MMDiT model (weights in HBM, activation buffers, planned launches, CUDA graphs, taps).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tsn.h"
+#include "dit_schema.h"
+#include "kernels.h"
+
+namespace tsn {
+
+int fail(int code, const std::string & msg);
+void clear_error();
+
+struct DeviceCtx {
+    int ordinal = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    int * d_err = nullptr;           // device error word written by bounded waits
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    double last_ms = 0.0;
+    bool pending = false;            // work issued since the last commit
+    std::mutex mu;
+    std::vector<void *> managed;     // tsn_alloc buffers (freed with the device)
+    // compat path scratch: f32 -> f16 operand staging, grown on demand
+    void * scratch = nullptr;
+    size_t scratch_bytes = 0;
+    int activate();                  // cudaSetDevice(ordinal)
+    int check_device_error();        // after a sync: TSN_ERR_TIMEOUT if a kernel gave up
+    int sync();                      // stream sync + device error word
+};
+
+struct Lin {
+    uint16_t * w = nullptr;   // [N][taps*K_in] f16/bf16
+    float * b = nullptr;      // [N] or null
+    int N = 0, K_in = 0, taps = 1;
+};
+
+struct Blk {
+    Lin ada, qkv, l1, w13, w2;
+    float * qn = nullptr, * kn = nullptr;
+    int chunks = 6;
+    bool post = false, conv = true;
+};
+
+struct Op {
+    std::function<cudaError_t(cudaStream_t)> fn;
+    int kind = 2;          // 0 tensor-core GEMM, 1 attention, 2 other
+    double flops = 0.0;
+    std::string name;
+};
+
+struct TapBuf {
+    void * dev = nullptr;
+    size_t bytes = 0;
+    std::function<void(const std::vector<uint8_t> &, int, std::vector<float> &)> convert;
+};
+
+struct Model {
+    DeviceCtx * dev = nullptr;
+    DitGeom g;
+    int bf16 = 0;
+    Lin te0, te2, ain0, ain13, ain2, fada, fconv;
+    std::vector<Blk> jl, jc, jt, fb;
+    void * arena = nullptr;
+    size_t arena_bytes = 0, arena_used = 0;
+
+    // geometry (tsn_dit_prepare)
+    bool prepared = false;
+    int T = 0, C = 0, TS = 0, B = 0, S = 0, S_pad = 0;
+    std::vector<void *> act;
+    float * x = nullptr, * clip_pp = nullptr, * sync_gather = nullptr, * text_pp = nullptr, * gcmlp = nullptr;
+    float * te_h = nullptr, * te = nullptr, * gc_silu = nullptr, * lat = nullptr, * clip_s = nullptr, * text_s = nullptr;
+    float * modl = nullptr, * modf = nullptr, * modc = nullptr, * modt = nullptr, * flow = nullptr;
+    __half * x16 = nullptr, * extc16 = nullptr, * xn_l = nullptr, * xn_c = nullptr, * xn_t = nullptr;
+    __half * att_l = nullptr, * att_c = nullptr, * att_t = nullptr, * h_l = nullptr, * h_c = nullptr, * h_t = nullptr;
+    __half * q = nullptr, * k = nullptr, * v = nullptr;
+    float2 * rope_l = nullptr, * rope_c = nullptr;
+    float * temb_tab = nullptr, * dt_tab = nullptr;
+    int * step = nullptr;
+    int max_steps = 1024;
+    float * ws = nullptr;
+    size_t ws_bytes = 0;
+    int * counters = nullptr;
+    int n_counters = 0, counters_used = 0;
+    GemvJob * jobs = nullptr;
+    int n_mod_jobs = 0;
+    float * tap_gc = nullptr, * tap_extc = nullptr;
+    std::map<std::string, TapBuf> taps;
+
+    std::vector<Op> ops_fwd, ops_step;
+    cudaGraphExec_t gx_fwd = nullptr, gx_step = nullptr;
+    float step_cfg = 0.0f;
+    int sched_steps = 0;
+
+    ~Model();
+    void * arena_take(size_t bytes);
+    int prepare(int T, int C, int TS, int B);
+    int build_ops(std::vector<Op> & ops, int mode, float cfg);   // mode 0 forward, 1 step, 2 taps
+    int run_ops(const std::vector<Op> & ops);
+    int capture(const std::vector<Op> & ops, cudaGraphExec_t * out);
+    int set_time(float t, float dt);
+    void temb_host(float t, float * out) const;
+    void release_activations();
+};
+
+int load_model(Model & m, const std::string * gguf_path, const DitGeom * synth_geom, uint64_t seed, std::string & err);
+
+} // namespace tsn

@@ -1,0 +1,278 @@
+"""ctypes binding of the C ABI in include/tsn.h (libtsn.so, built in this directory).
+
+The classes mirror the reference's C++ faces: :class:`Device` is ``tn::gpu::Device``
+(src/gpu.h), its runtime methods are ``tn::Runtime`` (src/net.h), and :class:`Dit` is
+``tn::DitModel`` (src/models.h) plus the sampler loop of src/pipeline.cpp. Every call raises
+:class:`TsnError` on a non-zero status. There is no CPU path: without the library or an sm_100
+device the calls fail.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtsn.so")
+
+TSN_COMPUTE_F16 = 0
+TSN_COMPUTE_BF16 = 1
+
+_ERRS = {1: "ARG", 2: "CUDA", 3: "IO", 4: "FORMAT", 5: "MISSING", 6: "OOM", 7: "UNSUPPORTED",
+         8: "TIMEOUT", 9: "STATE"}
+
+
+class TsnError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"TSN_ERR_{_ERRS.get(code, code)}: {msg}")
+        self.code = code
+
+
+class Geom(C.Structure):
+    _fields_ = [("H", C.c_uint32), ("NH", C.c_uint32), ("F", C.c_uint32), ("depth", C.c_uint32),
+                ("fused_depth", C.c_uint32), ("latent_dim", C.c_uint32), ("rope_theta", C.c_float),
+                ("t_max_period", C.c_float)]
+
+    def as_dict(self):
+        return {f: getattr(self, f) for f, _ in self._fields_}
+
+
+def geom(H=1024, NH=16, F=4096, depth=21, fused_depth=14, latent_dim=64, rope_theta=10000.0,
+         t_max_period=1.0) -> Geom:
+    return Geom(H, NH, F, depth, fused_depth, latent_dim, rope_theta, t_max_period)
+
+
+_lib = None
+
+# (name, restype, argtypes)
+_SIGS = [
+    ("tsn_last_error", C.c_char_p, []),
+    ("tsn_version", C.c_int, []),
+    ("tsn_device_create", C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    ("tsn_device_destroy", C.c_int, [C.c_void_p]),
+    ("tsn_device_set_stream", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("tsn_device_stream", C.c_void_p, [C.c_void_p]),
+    ("tsn_alloc", C.c_int, [C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p)]),
+    ("tsn_wrap", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p)]),
+    ("tsn_begin", C.c_int, [C.c_void_p]),
+    ("tsn_dispatch", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                               C.POINTER(C.c_void_p), C.c_int, C.c_void_p, C.c_size_t]),
+    ("tsn_commit", C.c_int, [C.c_void_p]),
+    ("tsn_exec_width", C.c_uint32, [C.c_void_p, C.c_char_p]),
+    ("tsn_last_gpu_ms", C.c_double, [C.c_void_p]),
+    ("tsn_gemm", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                           C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+    ("tsn_gemv", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
+                           C.c_uint32, C.c_uint32, C.c_int]),
+    ("tsn_conv", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                           C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32,
+                           C.c_uint32, C.c_uint32, C.c_int]),
+    ("tsn_silu", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    ("tsn_copy", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    ("tsn_swiglu", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    ("tsn_add", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t]),
+    ("tsn_add_bcast_col", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
+    ("tsn_cfg_euler", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_float]),
+    ("tsn_mean_cols", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
+    ("tsn_dit_load", C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.POINTER(C.c_void_p)]),
+    ("tsn_dit_load_synthetic", C.c_int, [C.c_void_p, C.POINTER(Geom), C.c_uint64, C.c_int, C.POINTER(C.c_void_p)]),
+    ("tsn_dit_free", C.c_int, [C.c_void_p]),
+    ("tsn_dit_get_geom", C.c_int, [C.c_void_p, C.POINTER(Geom)]),
+    ("tsn_dit_weight_bytes", C.c_size_t, [C.c_void_p]),
+    ("tsn_dit_prepare", C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+    ("tsn_dit_set_conditioning", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("tsn_dit_set_x", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("tsn_dit_get_x", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("tsn_dit_forward", C.c_int, [C.c_void_p, C.c_float, C.c_void_p]),
+    ("tsn_dit_forward_taps", C.c_int, [C.c_void_p, C.c_float, C.c_void_p]),
+    ("tsn_dit_tap", C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_size_t)]),
+    ("tsn_dit_step", C.c_int, [C.c_void_p, C.c_float, C.c_float, C.c_float]),
+    ("tsn_dit_sample", C.c_int, [C.c_void_p, C.c_int, C.c_float]),
+    ("tsn_dit_schedule", C.c_int, [C.c_void_p, C.c_int, C.c_float]),
+    ("tsn_dit_run_steps", C.c_int, [C.c_void_p, C.c_int]),
+    ("tsn_dit_step_host", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float, C.c_float]),
+    ("tsn_dit_kernels_per_step", C.c_int, [C.c_void_p]),
+    ("tsn_dit_profile_step", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
+    ("tsn_gguf_write_synthetic", C.c_int, [C.c_char_p, C.POINTER(Geom), C.c_uint64, C.c_int]),
+]
+
+EXPORTED = [s[0] for s in _SIGS]
+
+
+def lib():
+    """Load libtsn.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise TsnError(2, f"{LIB_PATH} not built (run __graft_entry__.build())")
+        L = C.CDLL(LIB_PATH)
+        for name, res, args in _SIGS:
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(rc: int):
+    if rc != 0:
+        msg = lib().tsn_last_error()
+        raise TsnError(rc, msg.decode() if msg else "")
+
+
+def _p(x):
+    """Address of a torch tensor / numpy array / int / None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    if hasattr(x, "ctypes"):
+        return x.ctypes.data
+    raise TypeError(type(x))
+
+
+class Device:
+    """tn::gpu::Device + tn::Runtime over one CUDA device."""
+
+    def __init__(self, ordinal: int = 0, stream: int | None = None):
+        h = C.c_void_p()
+        check(lib().tsn_device_create(ordinal, C.byref(h)))
+        self.h = h
+        if stream is not None:
+            check(lib().tsn_device_set_stream(self.h, C.c_void_p(stream)))
+
+    def close(self):
+        if self.h:
+            lib().tsn_device_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # --- gpu.h Device
+    def alloc(self, nbytes: int) -> int:
+        p = C.c_void_p()
+        check(lib().tsn_alloc(self.h, nbytes, C.byref(p)))
+        return p.value
+
+    def dispatch(self, kernel: str, grid, block, bufs, params: bytes = b""):
+        g = (C.c_uint32 * 3)(*grid)
+        b = (C.c_uint32 * 3)(*block)
+        arr = (C.c_void_p * max(1, len(bufs)))(*[_p(x) for x in bufs])
+        pb = C.create_string_buffer(params, len(params)) if params else None
+        check(lib().tsn_dispatch(self.h, kernel.encode(), g, b, arr, len(bufs), pb, len(params)))
+
+    def commit(self):
+        check(lib().tsn_commit(self.h))
+
+    def last_gpu_ms(self) -> float:
+        return lib().tsn_last_gpu_ms(self.h)
+
+    def exec_width(self, kernel: str) -> int:
+        return lib().tsn_exec_width(self.h, kernel.encode())
+
+    # --- net.h Runtime
+    def gemm(self, wf16, W, X, Y, bias, M, N, K, ldx=0, ldw=0, ldy=0):
+        check(lib().tsn_gemm(self.h, int(wf16), _p(W), _p(X), _p(Y), _p(bias), M, N, K, ldx, ldw, ldy))
+
+    def gemv(self, W, X, Y, bias, N, K, ldw=0, wf16=True):
+        check(lib().tsn_gemv(self.h, _p(W), _p(X), _p(Y), _p(bias), N, K, ldw, int(wf16)))
+
+    def conv(self, wf16, W, bias, x, y, T, OL, IC, OC, K, stride=1, pad=0, dil=1, convt=False):
+        check(lib().tsn_conv(self.h, int(wf16), _p(W), _p(bias), _p(x), _p(y), T, OL, IC, OC, K, stride, pad,
+                             dil, int(convt)))
+
+    def cfg_euler(self, fc, fu, x, n, cfg, dt):
+        check(lib().tsn_cfg_euler(self.h, _p(fc), _p(fu), _p(x), n, cfg, dt))
+
+
+class Dit:
+    """tn::DitModel on the device, with the CFG-batched fast path."""
+
+    def __init__(self, dev: Device, gguf: str | None = None, synthetic: Geom | None = None, seed: int = 4242,
+                 compute: int = TSN_COMPUTE_F16):
+        self.dev = dev
+        h = C.c_void_p()
+        if gguf is not None:
+            check(lib().tsn_dit_load(dev.h, gguf.encode(), compute, C.byref(h)))
+        else:
+            g = synthetic or geom()
+            check(lib().tsn_dit_load_synthetic(dev.h, C.byref(g), seed, compute, C.byref(h)))
+        self.h = h
+        g = Geom()
+        check(lib().tsn_dit_get_geom(self.h, C.byref(g)))
+        self.geom = g
+        self.T = self.C = self.TS = self.arms = 0
+
+    def close(self):
+        if self.h:
+            lib().tsn_dit_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def weight_bytes(self) -> int:
+        return lib().tsn_dit_weight_bytes(self.h)
+
+    def prepare(self, T: int, C_: int, TS: int, arms: int = 2):
+        check(lib().tsn_dit_prepare(self.h, T, C_, TS, arms))
+        self.T, self.C, self.TS, self.arms = T, C_, TS, arms
+
+    def set_conditioning(self, clip_pp, sync_gather, text_pp, gcmlp):
+        check(lib().tsn_dit_set_conditioning(self.h, _p(clip_pp), _p(sync_gather), _p(text_pp), _p(gcmlp)))
+
+    def set_x(self, x):
+        check(lib().tsn_dit_set_x(self.h, _p(x)))
+
+    def get_x(self, out):
+        check(lib().tsn_dit_get_x(self.h, _p(out)))
+
+    def forward(self, t: float, flow_out):
+        check(lib().tsn_dit_forward(self.h, t, _p(flow_out)))
+
+    def forward_taps(self, t: float, flow_out=None):
+        check(lib().tsn_dit_forward_taps(self.h, t, _p(flow_out)))
+
+    def tap(self, name: str, arm: int = 0):
+        import numpy as np
+        n = C.c_size_t()
+        check(lib().tsn_dit_tap(self.h, name.encode(), arm, None, 0, C.byref(n)))
+        out = np.empty(n.value, dtype=np.float32)
+        check(lib().tsn_dit_tap(self.h, name.encode(), arm, out.ctypes.data, n.value, C.byref(n)))
+        return out
+
+    def step(self, t: float, cfg: float, dt: float):
+        check(lib().tsn_dit_step(self.h, t, cfg, dt))
+
+    def sample(self, steps: int, cfg: float):
+        check(lib().tsn_dit_sample(self.h, steps, cfg))
+
+    def schedule(self, steps: int, cfg: float):
+        check(lib().tsn_dit_schedule(self.h, steps, cfg))
+
+    def run_steps(self, n: int):
+        check(lib().tsn_dit_run_steps(self.h, n))
+
+    def step_host(self, x_in, x_out, t: float, cfg: float, dt: float):
+        check(lib().tsn_dit_step_host(self.h, _p(x_in), _p(x_out), t, cfg, dt))
+
+    def kernels_per_step(self) -> int:
+        return lib().tsn_dit_kernels_per_step(self.h)
+
+    def profile_step(self):
+        out = (C.c_double * 5)()
+        check(lib().tsn_dit_profile_step(self.h, out))
+        return {"gemm_ms": out[0], "attn_ms": out[1], "other_ms": out[2], "gemm_flops": out[3],
+                "gemm_launches": int(out[4])}
+
+
+def write_synthetic_gguf(path: str, g: Geom, seed: int = 4242, with_prep: bool = False):
+    check(lib().tsn_gguf_write_synthetic(path.encode(), C.byref(g), seed, int(with_prep)))
