@@ -1,0 +1,161 @@
+"""Parity of the fused CUDA forward / sampler (model face) against the CPU oracle.
+
+Gates (north star): flow rel-L2 <= 1e-3 per step, every block tap the reference dumps
+(src/dit_fwd.cpp:151-301) <= 2e-3, repeated GPU runs bit-identical
+(tools/parity_dump.cpp:136-149). The oracle restates the reference bit-exactly (test_oracle.py).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+import tsn
+from conftest import SEED, TINY, TINY_SEQ, WIDE, WIDE_SEQ, make_geom, make_inputs, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+FLOW_TOL = 1e-3
+TAP_TOL = 2e-3
+
+
+@pytest.fixture(scope="module")
+def dev():
+    d = tsn.Device(0)
+    yield d
+    d.close()
+
+
+def gpu_model(dev, gguf, inp, T, C, TS, compute=tsn.TSN_COMPUTE_F16, synthetic=None):
+    m = tsn.Dit(dev, gguf=gguf, synthetic=synthetic, compute=compute)
+    m.prepare(T, C, TS, 2)
+    m.set_conditioning(inp["clip_pp"], inp["sync_gather"], np.stack([inp["text_pp_cond"], inp["text_pp_unc"]]),
+                       np.stack([inp["gcmlp_cond"], inp["gcmlp_unc"]]))
+    m.set_x(inp["x"])
+    return m
+
+
+def check_taps(m, orc, inp, T, C, TS, t, tap_tol=TAP_TOL, flow_tol=FLOW_TOL):
+    flow = np.zeros((2, T, 64), np.float32)
+    m.forward_taps(t, flow)
+    report = {}
+    for arm, sfx in ((0, "cond"), (1, "unc")):
+        ref_flow = orc.forward(T, C, TS, inp["x"], t, inp["clip_pp"], inp["sync_gather"], inp[f"text_pp_{sfx}"],
+                               inp[f"gcmlp_{sfx}"], taps=True)
+        for name in O.TAPS:
+            ref = ref_flow.ravel() if name == "flow" else orc.tap(name)
+            got = m.tap(name, arm)
+            assert got.shape == ref.shape, (name, got.shape, ref.shape)
+            e = rel_l2(got, ref)
+            report[(arm, name)] = e
+        report[(arm, "flow_out")] = rel_l2(flow[arm], ref_flow)
+    bad = {k: v for k, v in report.items() if v > (flow_tol if k[1] in ("flow", "flow_out") else tap_tol)}
+    worst = sorted(report.items(), key=lambda kv: -kv[1])[:6]
+    assert not bad, f"over tolerance: {bad}; worst: {worst}"
+    return report
+
+
+def test_tiny_forward_taps_vs_oracle(dev, tiny_gguf):
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    check_taps(m, O.Oracle(tiny_gguf), inp, T, C, TS, 0.5)
+
+
+def test_tiny_golden_flow(dev, tiny_gguf):
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "tiny_forward.npz")))
+    T, C, TS = int(g["T"]), int(g["C"]), int(g["TS"])
+    inp = {k[3:]: g[k] for k in g if k.startswith("in_")}
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    flow = np.zeros((2, T, 64), np.float32)
+    m.forward(float(g["t"]), flow)
+    assert rel_l2(flow[0], g["tap_flow"]) < FLOW_TOL
+
+
+def test_graph_replay_deterministic_and_equal_to_eager(dev, tiny_gguf):
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    a = np.zeros((2, T, 64), np.float32)
+    b = np.zeros_like(a)
+    c = np.zeros_like(a)
+    m.forward(0.25, a)
+    m.forward(0.25, b)
+    m.forward_taps(0.25, c)
+    assert np.array_equal(a, b), "repeat forward not bit-identical"
+    assert np.array_equal(a, c), "graph replay differs from eager launch"
+
+
+def test_synthetic_device_weights_equal_file(dev, tiny_gguf):
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    a = np.zeros((2, T, 64), np.float32)
+    b = np.zeros_like(a)
+    gpu_model(dev, tiny_gguf, inp, T, C, TS).forward(0.5, a)
+    gpu_model(dev, None, inp, T, C, TS, synthetic=make_geom(**TINY)).forward(0.5, b)
+    assert np.array_equal(a, b)
+
+
+def test_tiny_sample_vs_golden(dev, tiny_gguf):
+    g = dict(np.load(os.path.join(os.path.dirname(__file__), "golden", "tiny_sample.npz")))
+    T, C, TS = int(g["T"]), int(g["C"]), int(g["TS"])
+    inp = {k[3:]: g[k] for k in g if k.startswith("in_")}
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    m.sample(int(g["steps"]), float(g["cfg"]))
+    x = np.zeros((T, 64), np.float32)
+    m.get_x(x)
+    # CFG 5 amplifies per-step flow error ~5x into x; 4 steps accumulate
+    assert rel_l2(x, g["x_final"]) < 5e-3
+
+
+def test_tiny_step_vs_oracle(dev, tiny_gguf):
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"], seed=SEED + 1)
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    t, dt = 1.0, float(np.float32(1.0 - 1.0 / 24) - np.float32(1.0))
+    m.step(t, 5.0, dt)
+    x = np.zeros((T, 64), np.float32)
+    m.get_x(x)
+    orc = O.Oracle(tiny_gguf)
+    xr, fc, fu = orc.step(T, C, TS, inp["x"], t, 5.0, dt, inp["clip_pp"], inp["sync_gather"], inp["text_pp_cond"],
+                          inp["gcmlp_cond"], inp["text_pp_unc"], inp["gcmlp_unc"])
+    # compare the update dt*(fu + 5(fc - fu)) itself: x carries the unchanged noise
+    assert rel_l2(x - inp["x"], xr - inp["x"]) < 5 * FLOW_TOL
+
+
+def test_bf16_operands_report(dev, tiny_gguf):
+    """BF16 operands (north-star wording) against the f16-weight reference: reported, looser gate."""
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS, compute=tsn.TSN_COMPUTE_BF16)
+    flow = np.zeros((2, T, 64), np.float32)
+    m.forward(0.5, flow)
+    ref = O.Oracle(tiny_gguf).forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"],
+                                      inp["text_pp_cond"], inp["gcmlp_cond"])
+    e = rel_l2(flow[0], ref)
+    print(f"bf16 flow rel-L2 {e:.3g}")
+    assert e < 2e-2
+
+
+def test_wide_forward_taps_vs_oracle(dev, wide_gguf):
+    """Real widths (H=1024, 16 heads, F=4096) at the 8 s geometry, 2 joint + 1 fused block."""
+    T, C, TS = WIDE_SEQ["T"], WIDE_SEQ["C"], WIDE_SEQ["TS"]
+    inp = make_inputs(T, C, TS, WIDE["H"])
+    m = gpu_model(dev, wide_gguf, inp, T, C, TS)
+    check_taps(m, O.Oracle(wide_gguf), inp, T, C, TS, 0.5)
+
+
+def test_single_arm_matches_batched(dev, tiny_gguf):
+    """arms=1 (one CFG arm per GPU) gives the same flow as the arms=2 batch."""
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    both = np.zeros((2, T, 64), np.float32)
+    gpu_model(dev, tiny_gguf, inp, T, C, TS).forward(0.5, both)
+    for arm, sfx in ((0, "cond"), (1, "unc")):
+        m = tsn.Dit(dev, gguf=tiny_gguf)
+        m.prepare(T, C, TS, 1)
+        m.set_conditioning(inp["clip_pp"], inp["sync_gather"], inp[f"text_pp_{sfx}"], inp[f"gcmlp_{sfx}"])
+        m.set_x(inp["x"])
+        one = np.zeros((1, T, 64), np.float32)
+        m.forward(0.5, one)
+        assert rel_l2(one[0], both[arm]) < 1e-5

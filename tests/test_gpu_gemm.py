@@ -1,0 +1,99 @@
+"""The tcgen05 GEMM / conv behind the runtime face (Runtime::gemm / Runtime::conv, src/net.mm:14-49).
+
+Mirrors tools/gemm_bench.cpp and tools/conv_bench.cpp of the reference: seeded inputs, weights
+N(0,1)*0.03 rounded to f16, outputs NaN-filled so unwritten elements show up, a guard band
+checked for clobbering, shapes of the real DiT. The CPU reference is float64 on the same f16
+weights; X is rounded to f16 by the kernel, so the tight check uses f16-rounded X (kernel
+exactness) and the loose one the raw f32 X (the drop-in error budget).
+"""
+import numpy as np
+import pytest
+
+import tsn
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+SHAPES = [  # (M, N, K, bias, xpad, ypad, tag)   tools/gemm_bench.cpp:32-47, DiT rows doubled for CFG
+    (376, 6144, 1024, True, 0, 0, "latent adaLN"),
+    (376, 3072, 1024, True, 0, 0, "latent qkv"),
+    (154, 4096, 1024, False, 0, 0, "text ffn w1"),
+    (154, 1024, 4096, False, 0, 0, "text ffn w2"),
+    (1024, 1024, 1024, True, 0, 0, "square"),
+    (43, 1024, 3072, True, 0, 0, "odd M"),
+    (16, 1024, 1024, True, 64, 0, "ldx pad"),
+    (77, 1024, 1024, True, 0, 2048, "ldy pad"),
+    (1, 6144, 1024, True, 0, 0, "M=1"),
+    (50, 100, 72, True, 0, 0, "CUDA-core shape"),
+]
+
+
+@pytest.fixture(scope="module")
+def dev():
+    d = tsn.Device(0)
+    yield d
+    d.close()
+
+
+@pytest.mark.parametrize("M,N,K,bias,xpad,ypad,tag", SHAPES)
+def test_gemm_runtime_face(dev, M, N, K, bias, xpad, ypad, tag):
+    rng = np.random.default_rng(7)
+    ldx, ldy = K + xpad, N + ypad
+    x = rng.standard_normal((M, ldx), dtype=np.float32)
+    w16 = (rng.standard_normal((N, K), dtype=np.float32) * 0.03).astype(np.float16)
+    b = rng.standard_normal(N, dtype=np.float32)
+    X = torch.from_numpy(x).cuda()
+    W = torch.from_numpy(w16.view(np.uint16).astype(np.int16)).cuda()
+    B = torch.from_numpy(b).cuda()
+    Y = torch.full((M * ldy + 8,), float("nan"), dtype=torch.float32, device="cuda")
+    dev.gemm(True, W, X, Y, B if bias else None, M, N, K, ldx, K, ldy)
+    dev.commit()
+    y = Y.cpu().numpy()
+    assert np.isnan(y[M * ldy:]).all(), "wrote past the output"
+    y = y[:M * ldy].reshape(M, ldy)
+    if ypad:
+        assert np.isnan(y[:, N:]).all(), "clobbered the row padding"
+    y = y[:, :N]
+    wf = w16.astype(np.float64)
+    ref_exact = x[:, :K].astype(np.float16).astype(np.float64) @ wf.T + (b if bias else 0)
+    ref_f32 = x[:, :K].astype(np.float64) @ wf.T + (b if bias else 0)
+    assert not np.isnan(y).any(), "unwritten outputs"
+    tc = K % 64 == 0 and N % 64 == 0
+    assert rel_l2(y, ref_exact if tc else ref_f32) < 1e-5, tag
+    assert rel_l2(y, ref_f32) < 1e-3, tag
+
+
+CONV_CASES = [  # (T, IC, OC, K, pad, bias, tag)  tools/conv_bench.cpp:14-26 (DiT rows)
+    (172, 1024, 2816, 3, 1, False, "latent ffn w1 k3"),
+    (172, 1024, 1024, 3, 1, True, "latent linear1 k3"),
+    (172, 64, 1024, 3, 1, True, "audio_input_proj.0"),
+    (172, 1024, 64, 7, 3, True, "final conv k7"),
+    (64, 1024, 2816, 3, 1, False, "clip ffn w1"),
+]
+
+
+@pytest.mark.parametrize("T,IC,OC,K,pad,bias,tag", CONV_CASES)
+def test_conv_runtime_face(dev, T, IC, OC, K, pad, bias, tag):
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((T, IC), dtype=np.float32)
+    w16 = (rng.standard_normal((OC, IC, K), dtype=np.float32) * 0.03).astype(np.float16)
+    b = rng.standard_normal(OC, dtype=np.float32)
+    X = torch.from_numpy(x).cuda()
+    W = torch.from_numpy(w16.view(np.uint16).astype(np.int16)).cuda()
+    B = torch.from_numpy(b).cuda()
+    Y = torch.full((T, OC), float("nan"), dtype=torch.float32, device="cuda")
+    dev.conv(True, W, B if bias else None, X, Y, T, T, IC, OC, K, 1, pad, 1)
+    dev.commit()
+    y = Y.cpu().numpy()
+    xp = np.zeros((T + 2 * pad, IC))
+    xp[pad:pad + T] = x.astype(np.float16).astype(np.float64)
+    ref = np.zeros((T, OC))
+    wf = w16.astype(np.float64)
+    for k in range(K):
+        ref += xp[k:k + T] @ wf[:, :, k].T
+    if bias:
+        ref += b
+    assert not np.isnan(y).any()
+    assert rel_l2(y, ref) < 1e-5, tag

@@ -46,6 +46,7 @@ int tsn_device_create(int ordinal, tsn_device ** out) {
     CKR(cudaMemset(d->ctx.d_err, 0, 64));
     CKR(cudaEventCreate(&d->ctx.ev0));
     CKR(cudaEventCreate(&d->ctx.ev1));
+    CKR(configure_gemm_kernels());
     *out = d.release();
     return TSN_OK;
 }

@@ -86,20 +86,22 @@ KernelFn kernel_for(int bn, int epi) {
 }
 } // namespace
 
+// Set the dynamic shared-memory limit of every instantiation once, outside any stream capture.
+cudaError_t configure_gemm_kernels() {
+    for (int bn : {64, 128, 256})
+        for (int epi = 0; epi < 6; ++epi) {
+            KernelFn fn = kernel_for(bn, epi);
+            if (!fn) continue;
+            cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int) gemm_smem_bytes(bn, gemm_stages(bn)));
+            if (e != cudaSuccess) return e;
+        }
+    return cudaSuccess;
+}
+
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
     KernelFn fn = kernel_for(g.bn, g.epi);
     if (!fn) return cudaErrorInvalidValue;
-    static std::mutex mu;
-    static bool configured[3][6] = {};
-    const int bi = g.bn == 64 ? 0 : g.bn == 128 ? 1 : 2;
-    {
-        std::lock_guard<std::mutex> lk(mu);
-        if (!configured[bi][g.epi]) {
-            cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) g.smem);
-            if (e != cudaSuccess) return e;
-            configured[bi][g.epi] = true;
-        }
-    }
     fn<<<g.grid, 192, g.smem, s>>>(g.ta, g.tb, g.args, g.ab_bf16);
     return cudaGetLastError();
 }

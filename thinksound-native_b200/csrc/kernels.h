@@ -24,6 +24,7 @@ bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t ro
 // Encode a 2-D TMA view {K, N} of an [N][K] 16-bit weight matrix with a {64, bn} box.
 bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16);
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
+cudaError_t configure_gemm_kernels();
 size_t gemm_smem_bytes(int bn, int stages);
 int gemm_stages(int bn);
 
