@@ -1,0 +1,353 @@
+"""MMDiT CFG denoise steps/s on B200 (BASELINE.json metric), one JSON line on rank 0.
+
+A step is one rectified-flow Euler step of the sampler (src/pipeline.cpp:146-148): the 21-block
+MMDiT forward for the cond and uncond arms (batched) plus the CFG-Euler update, on the 8 s
+geometry of BASELINE config 2/3 (T=188 latent rows, 64 clip rows, 77 text rows, H=1024, 16 heads,
+F=4096) with seeded synthetic weights N(0,0.02) generated on the device.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl tsn|reference]
+
+Multi-GPU (torchrun, one process per GPU): every rank samples its own generation (data-parallel
+generations) with no cross-GPU traffic in the timed region; value is the
+steps of all ranks divided by the slowest rank's device time (weak scaling).
+
+--impl reference times the reference's own CPU implementation of the path (the reference's
+src/dit_fwd.cpp built over the scalar kernel transliteration in oracle/_ref; the oracle port when
+that build is absent) on the host cores, same config and metric; rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "thinksound-native_b200"))
+
+METRIC = "MMDiT CFG denoise steps/s (8 s audio) at 1/2/4/8 B200; % of step roofline"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=48)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="tsn", choices=["tsn", "reference"])
+    ap.add_argument("--T", type=int, default=188)
+    ap.add_argument("--C", type=int, default=64)
+    ap.add_argument("--TS", type=int, default=77)
+    ap.add_argument("--H", type=int, default=1024)
+    ap.add_argument("--F", type=int, default=4096)
+    ap.add_argument("--depth", type=int, default=21)
+    ap.add_argument("--fused", type=int, default=14)
+    ap.add_argument("--cfg", type=float, default=5.0)
+    ap.add_argument("--seed", type=int, default=4242)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    return ap.parse_args()
+
+
+def geom_kwargs(a):
+    return dict(H=a.H, NH=a.H // 64, F=a.F, depth=a.depth, fused_depth=a.fused)
+
+
+def workload(a):
+    return {"workload": f"config2/3: {a.depth}-block MMDiT CFG Euler step ({a.depth - a.fused} joint + {a.fused} fused), "
+                        f"8 s audio geometry, cond+uncond batched",
+            "T": a.T, "clip_S": a.C, "text_S": a.TS, "H": a.H, "heads": a.H // 64, "F": a.F, "cfg": a.cfg,
+            "weights": "synthetic BF16 N(0,0.02) -> f16 operands (reference weight conversion)",
+            "l2": "inputs larger than L2: every step streams ~3.1 GB of weights from HBM (L2 126 MB)"}
+
+
+# ------------------------------------------------------------------------------------ FLOPs
+def step_flops_bytes(a):
+    """Algorithmic FLOPs (2*M*N*K over every GEMM/conv/GEMV + 4*S^2*H attention, both arms) and
+    weight bytes (BF16/f16 once per step) of one CFG step, counted from src/dit_fwd.cpp:104-304."""
+    H, F, L, T, C, TS, B = a.H, a.F, 64, a.T, a.C, a.TS, 2
+    nj, nf = a.depth - a.fused, a.fused
+    params = 0
+    fl = 0
+
+    def lin(rows, n, k):
+        nonlocal params, fl
+        params += n * k
+        fl += 2 * B * rows * n * k
+
+    lin(1, H, H); lin(1, H, H)                       # t_embed (M=1 per arm on the reference)
+    lin(T, H, 3 * L); lin(T, 2 * F, 3 * H); lin(T, H, 3 * F)    # audio_input_proj
+    for i in range(nj):
+        pre = i == nj - 1
+        lin(T, 6 * H, H); lin(T, 3 * H, H)
+        lin(1, (2 if pre else 6) * H, H); lin(C, 3 * H, H)
+        lin(1, (2 if pre else 6) * H, H); lin(TS, 3 * H, H)
+        lin(T, H, 3 * H); lin(T, 2 * F, 3 * H); lin(T, H, 3 * F)
+        if not pre:
+            lin(C, H, 3 * H); lin(C, 2 * F, 3 * H); lin(C, H, 3 * F)
+            lin(TS, H, H); lin(TS, 2 * F, H); lin(TS, H, F)
+        S = T + C + TS
+        fl += 4 * B * S * S * H
+    for _ in range(nf):
+        lin(T, 6 * H, H); lin(T, 3 * H, H)
+        lin(T, H, 3 * H); lin(T, 2 * F, 3 * H); lin(T, H, 3 * F)
+        fl += 4 * B * T * T * H
+    lin(T, 2 * H, H); lin(T, L, 7 * H)
+    return fl, 2 * params
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------ clocks
+class Clocks:
+    def __init__(self, gpu_index, enabled=True):
+        self.proc = None
+        self.path = None
+        if not enabled:
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                try:
+                    rows.append((float(f[1]), float(f[2]), f[5:9]))
+                except ValueError:
+                    pass
+        os.unlink(self.path)
+        if not rows:
+            return None
+        load = [r for r in rows if r[0] > 0.5 * r[1]] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in load for i, v in enumerate(r[2]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in load), "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(rows), "samples_under_load": len(load), "reasons": reasons}
+
+
+# ------------------------------------------------------------------------------------ CPU arms
+def cpu_reference_steps(a, reps, threads):
+    """Time `reps` CFG steps of the reference's host code (oracle/_ref) or the oracle port on the
+    host cores; returns (seconds per step list, kind, sample description)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    import tsn
+
+    tmp = tempfile.mkdtemp(prefix="tsn_cpu_")
+    gguf = os.path.join(tmp, "dit.gguf")
+    tsn.write_synthetic_gguf(gguf, tsn.geom(**geom_kwargs(a)), a.seed)
+    rng = np.random.default_rng(a.seed)
+    f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
+    inp = {"x": f(a.T, 64), "clip_pp": f(a.C, a.H), "sync_gather": f(a.T, a.H), "text_pp_cond": f(a.TS, a.H),
+           "text_pp_unc": f(a.TS, a.H), "gcmlp_cond": f(a.H), "gcmlp_unc": f(a.H)}
+    try:
+        if O.have_ref():
+            O.write_inputs(os.path.join(tmp, "in"), inp)
+            out = O.run_ref("step", gguf, a.T, a.C, a.TS, os.path.join(tmp, "in"), os.path.join(tmp, "out"),
+                            0.5, a.cfg, -1.0 / 24, reps, threads=threads)
+            secs = O.parse_json_line(out)["seconds"]
+            kind = "reference"
+        else:
+            os.environ["OMP_NUM_THREADS"] = str(threads)
+            orc = O.Oracle(gguf)
+            secs = []
+            x = inp["x"]
+            for _ in range(reps):
+                t0 = time.perf_counter()
+                x, _, _ = orc.step(a.T, a.C, a.TS, x, 0.5, a.cfg, -1.0 / 24, inp["clip_pp"], inp["sync_gather"],
+                                   inp["text_pp_cond"], inp["gcmlp_cond"], inp["text_pp_unc"], inp["gcmlp_unc"])
+                secs.append(time.perf_counter() - t0)
+            kind = "port"
+    finally:
+        for fn in os.listdir(tmp):
+            p = os.path.join(tmp, fn)
+            if os.path.isdir(p):
+                for g in os.listdir(p):
+                    os.unlink(os.path.join(p, g))
+                os.rmdir(p)
+            else:
+                os.unlink(p)
+        os.rmdir(tmp)
+    sample = (f"{len(secs)} full CFG step(s) ({a.depth} blocks, T={a.T}, clip {a.C}, text {a.TS}, both arms + cfg_euler) "
+              f"of the {'reference host code (src/dit_fwd.cpp) over the scalar kernel transliteration' if kind == 'reference' else 'oracle port'}, "
+              f"f32 activations, OpenMP over output rows")
+    return secs, kind, sample
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    reps = a.warmup + a.steps
+    secs, kind, sample = cpu_reference_steps(a, reps, threads)
+    timed = secs[a.warmup:] if len(secs) > a.warmup else secs
+    value = len(timed) / sum(timed)
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference", "value": value, "unit": "steps/s", "n_gpus": a.gpus,
+        "steps": len(timed), "warmup": a.warmup, "ms_per_step": 1e3 * sum(timed) / len(timed),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload(a),
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": threads, "kind": kind, "sample": sample},
+        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------------------------------ GPU arm
+def run_tsn(a):
+    import numpy as np
+    import torch
+
+    import tsn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    stream = torch.cuda.Stream()
+    dev = tsn.Device(local, stream=stream.cuda_stream)
+    m = tsn.Dit(dev, synthetic=tsn.geom(**geom_kwargs(a)), seed=a.seed)
+    m.prepare(a.T, a.C, a.TS, 2)
+    rng = np.random.default_rng(a.seed + 1000 * rank)     # per-rank generation (config 5: seeds per generation)
+    f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
+    m.set_conditioning(f(a.C, a.H), f(a.T, a.H), f(2, a.TS, a.H), f(2, a.H))
+    m.set_x(f(a.T, 64))
+    total = a.warmup + a.steps
+    m.schedule(min(total, 1024), a.cfg)
+
+    with torch.cuda.stream(stream):
+        m.run_steps(a.warmup)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        clocks = Clocks(local, enabled=not a.no_clocks)
+        time.sleep(0.3 if clocks.proc else 0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        m.run_steps(a.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        clk = clocks.stop()
+    x = np.zeros((a.T, 64), np.float32)
+    m.get_x(x)
+    finite = bool(np.isfinite(x).all())
+
+    # e2e: the public host-buffer step (tsn_dit_step_host): H2D of x and the step's schedule row,
+    # the step, D2H of x, every step
+    e2e_ms = None
+    h2d = a.T * 64 * 4 + a.H * 4 + 4
+    d2h = a.T * 64 * 4
+    if not a.no_e2e:
+        xin = torch.from_numpy(f(a.T, 64)).pin_memory()
+        xout = torch.empty_like(xin).pin_memory()
+        for _ in range(2):
+            m.step_host(xin, xout, 0.5, a.cfg, -1.0 / 24)
+        if dist:
+            dist.barrier()
+        with torch.cuda.stream(stream):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for i in range(a.steps):
+                m.step_host(xout if i else xin, xout, 0.5, a.cfg, -1.0 / 24)
+            s1.record(stream)
+            torch.cuda.synchronize()
+            e2e_ms = s0.elapsed_time(s1)
+
+    prof = m.profile_step()
+    kps = m.kernels_per_step()
+    times = torch.tensor([ms, e2e_ms or 0.0], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = float(times[0]), float(times[1]) if e2e_ms is not None else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        secs, kind, sample = cpu_reference_steps(a, 1, threads)
+        cpu = {"value": 1.0 / secs[-1], "unit": "steps/s", "cores": threads, "kind": kind, "sample": sample}
+
+    if rank == 0:
+        flops, wbytes = step_flops_bytes(a)
+        hbm, tf_burst, tf_sus, src = peaks()
+        step_ms = ms / a.steps
+        compute_ms = flops / (tf_sus * 1e12) * 1e3
+        hbm_ms = wbytes / (hbm * 1e9) * 1e3
+        bound_ms = max(compute_ms, hbm_ms)
+        g_ms = prof["gemm_ms"]
+        g_tf = prof["gemm_flops"] / (g_ms * 1e-3) / 1e12 if g_ms > 0 else 0.0
+        out = {
+            "metric": METRIC, "value": world * a.steps / (ms * 1e-3), "unit": "steps/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 (split hi+lo activations), f32 accumulate", "data": "synthetic",
+            "config": dict(workload(a), parallelism=f"dp{world} (one generation per GPU, no data-path collective)"),
+            "roofline": {"bound": "tensor", "achieved": g_tf, "peak": tf_sus, "unit": "TFLOP/s",
+                         "frac": g_tf / tf_sus, "traffic": None,
+                         "kernel": "gemm_tc_kernel (tcgen05 GEMM / implicit conv), all launches of one step",
+                         "peak_source": f"{src} bf16_tflops_sustained",
+                         "algorithmic_flops_per_step": prof["gemm_flops"], "gemm_ms_per_step": g_ms,
+                         "gemm_launches_per_step": prof["gemm_launches"], "attention_ms_per_step": prof["attn_ms"],
+                         "other_ms_per_step": prof["other_ms"]},
+            "step_roofline": {"algorithmic_gflop": flops / 1e9, "weight_gb": wbytes / 1e9, "compute_ms": compute_ms,
+                              "hbm_ms": hbm_ms, "bound": "tensor" if compute_ms >= hbm_ms else "hbm",
+                              "roofline_ms": bound_ms, "frac": bound_ms / step_ms,
+                              "peaks": f"{src}: {tf_sus} TFLOP/s sustained bf16, {hbm} GB/s"},
+            "cpu_baseline": cpu,
+            "e2e": ({"value": world * a.steps / (e2e_ms * 1e-3), "unit": "steps/s", "h2d_bytes_per_step": h2d,
+                     "d2h_bytes_per_step": d2h} if e2e_ms else None),
+            "gpu_launches": kps * a.steps,
+            "clocks": clk,
+            "x_finite": finite,
+        }
+        print(json.dumps(out), flush=True)
+    m.close()
+    dev.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_tsn(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -49,6 +49,7 @@ def check_taps(m, orc, inp, T, C, TS, t, tap_tol=TAP_TOL, flow_tol=FLOW_TOL):
             e = rel_l2(got, ref)
             report[(arm, name)] = e
         report[(arm, "flow_out")] = rel_l2(flow[arm], ref_flow)
+    print("tap rel-L2:", {f"{k[0]}:{k[1]}": round(v, 7) for k, v in report.items()})
     bad = {k: v for k, v in report.items() if v > (flow_tol if k[1] in ("flow", "flow_out") else tap_tol)}
     worst = sorted(report.items(), key=lambda kv: -kv[1])[:6]
     assert not bad, f"over tolerance: {bad}; worst: {worst}"
@@ -123,18 +124,11 @@ def test_tiny_step_vs_oracle(dev, tiny_gguf):
     assert rel_l2(x - inp["x"], xr - inp["x"]) < 5 * FLOW_TOL
 
 
-def test_bf16_operands_report(dev, tiny_gguf):
-    """BF16 operands (north-star wording) against the f16-weight reference: reported, looser gate."""
-    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
-    inp = make_inputs(T, C, TS, TINY["H"])
-    m = gpu_model(dev, tiny_gguf, inp, T, C, TS, compute=tsn.TSN_COMPUTE_BF16)
-    flow = np.zeros((2, T, 64), np.float32)
-    m.forward(0.5, flow)
-    ref = O.Oracle(tiny_gguf).forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"],
-                                      inp["text_pp_cond"], inp["gcmlp_cond"])
-    e = rel_l2(flow[0], ref)
-    print(f"bf16 flow rel-L2 {e:.3g}")
-    assert e < 2e-2
+def test_bf16_operands_rejected(dev, tiny_gguf):
+    """BF16 operands are refused loudly (they cannot meet the 1e-3 flow gate), not silently downgraded."""
+    with pytest.raises(tsn.TsnError) as e:
+        tsn.Dit(dev, gguf=tiny_gguf, compute=tsn.TSN_COMPUTE_BF16)
+    assert e.value.code == 7
 
 
 def test_wide_forward_taps_vs_oracle(dev, wide_gguf):
@@ -159,3 +153,22 @@ def test_single_arm_matches_batched(dev, tiny_gguf):
         one = np.zeros((1, T, 64), np.float32)
         m.forward(0.5, one)
         assert rel_l2(one[0], both[arm]) < 1e-5
+
+
+FULL = dict(H=1024, NH=16, F=4096, depth=21, fused_depth=14)
+
+
+@pytest.fixture(scope="module")
+def full_gguf(tmp_path_factory):
+    p = str(tmp_path_factory.mktemp("gguf_full") / "full.gguf")
+    tsn.write_synthetic_gguf(p, make_geom(**FULL), SEED)
+    yield p
+    os.unlink(p)
+
+
+def test_full_depth_forward_vs_oracle(dev, full_gguf):
+    """the full 21-block MMDiT (7 joint + 14 fused), 8 s geometry, t = 0.5."""
+    T, C, TS = WIDE_SEQ["T"], WIDE_SEQ["C"], WIDE_SEQ["TS"]
+    inp = make_inputs(T, C, TS, FULL["H"])
+    m = gpu_model(dev, full_gguf, inp, T, C, TS)
+    check_taps(m, O.Oracle(full_gguf), inp, T, C, TS, 0.5)

@@ -3,8 +3,8 @@
 Mirrors tools/gemm_bench.cpp and tools/conv_bench.cpp of the reference: seeded inputs, weights
 N(0,1)*0.03 rounded to f16, outputs NaN-filled so unwritten elements show up, a guard band
 checked for clobbering, shapes of the real DiT. The CPU reference is float64 on the same f16
-weights; X is rounded to f16 by the kernel, so the tight check uses f16-rounded X (kernel
-exactness) and the loose one the raw f32 X (the drop-in error budget).
+weights and the f32 X: the runtime face passes X as a split f16 operand (hi + lo), so the
+tensor-core product matches the f32-activation product to f32 accumulation error.
 """
 import numpy as np
 import pytest
@@ -57,12 +57,9 @@ def test_gemm_runtime_face(dev, M, N, K, bias, xpad, ypad, tag):
         assert np.isnan(y[:, N:]).all(), "clobbered the row padding"
     y = y[:, :N]
     wf = w16.astype(np.float64)
-    ref_exact = x[:, :K].astype(np.float16).astype(np.float64) @ wf.T + (b if bias else 0)
-    ref_f32 = x[:, :K].astype(np.float64) @ wf.T + (b if bias else 0)
+    ref = x[:, :K].astype(np.float64) @ wf.T + (b if bias else 0)
     assert not np.isnan(y).any(), "unwritten outputs"
-    tc = K % 64 == 0 and N % 64 == 0
-    assert rel_l2(y, ref_exact if tc else ref_f32) < 1e-5, tag
-    assert rel_l2(y, ref_f32) < 1e-3, tag
+    assert rel_l2(y, ref) < 1e-5, tag
 
 
 CONV_CASES = [  # (T, IC, OC, K, pad, bias, tag)  tools/conv_bench.cpp:14-26 (DiT rows)
@@ -88,7 +85,7 @@ def test_conv_runtime_face(dev, T, IC, OC, K, pad, bias, tag):
     dev.commit()
     y = Y.cpu().numpy()
     xp = np.zeros((T + 2 * pad, IC))
-    xp[pad:pad + T] = x.astype(np.float16).astype(np.float64)
+    xp[pad:pad + T] = x.astype(np.float64)
     ref = np.zeros((T, OC))
     wf = w16.astype(np.float64)
     for k in range(K):

@@ -47,6 +47,7 @@ int tsn_device_create(int ordinal, tsn_device ** out) {
     CKR(cudaEventCreate(&d->ctx.ev0));
     CKR(cudaEventCreate(&d->ctx.ev1));
     CKR(configure_gemm_kernels());
+    CKR(configure_attention());
     *out = d.release();
     return TSN_OK;
 }
@@ -184,7 +185,10 @@ int tsn_mean_cols(tsn_device * dev, const void * x, void * y, uint32_t S, uint32
 static int new_model(tsn_device * dev, int compute_type, tsn_dit ** out, const std::string * path,
                      const tsn_dit_geom * g, uint64_t seed) {
     if (!dev || !out) return fail(TSN_ERR_ARG, "null argument");
-    if (compute_type != TSN_COMPUTE_F16 && compute_type != TSN_COMPUTE_BF16) return fail(TSN_ERR_ARG, "bad compute type");
+    if (compute_type == TSN_COMPUTE_BF16)
+        return fail(TSN_ERR_UNSUPPORTED, "BF16 operands are not provided: the reference's device weights are f16 and "
+                                         "BF16 rounding of activations misses the 1e-3 flow gate; use TSN_COMPUTE_F16");
+    if (compute_type != TSN_COMPUTE_F16) return fail(TSN_ERR_ARG, "bad compute type");
     *out = nullptr;
     TRY(dev->ctx.activate());
     auto m = std::make_unique<tsn_dit>();

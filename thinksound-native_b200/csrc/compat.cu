@@ -221,10 +221,14 @@ __global__ void k_gemm_simple(const void * W, int wf16, const float * X, float *
     if (m < p.M && n < p.N) Y[(size_t) m * p.ldy + n] = acc + (p.bias_mode ? bias[n] : 0.0f);
 }
 
+// f32 [M][ldx] -> split f16 operand: hi [M][K] at out, lo [M][K] at out + M*K
 __global__ void k_f32_to_f16(const float * x, uint32_t M, uint32_t K, uint32_t ldx, __half * out) {
     GRID_STRIDE(i, (long long) M * K) {
         const uint32_t m = (uint32_t) (i / K), k = (uint32_t) (i % K);
-        out[i] = __float2half_rn(x[(size_t) m * ldx + k]);
+        const float v = x[(size_t) m * ldx + k];
+        const __half h = __float2half_rn(v);
+        out[i] = h;
+        out[i + (long long) M * K] = __float2half_rn(v - __half2float(h));
     }
 }
 
@@ -321,33 +325,28 @@ int compat_gemm(DeviceCtx & c, int wf16, const void * W, const void * X, void * 
         k_gemm_simple<<<grid, dim3(16, 16), 0, c.stream>>>(W, wf16, (const float *) X, (float *) Y, (const float *) bias, p);
         return launched("gemm_simple");
     }
-    // X -> f16 [M][K], then the tcgen05 GEMM with one batch of 128-row tiles
-    int rc = ensure_scratch(c, (size_t) M * K * 2);
+    // X -> split f16 operand (hi | lo), then the tcgen05 GEMM with one batch of 128-row tiles;
+    // weights whose rows are ldw apart are first packed to a dense [N][K] copy for the TMA view.
+    const size_t xa_bytes = ((size_t) 2 * M * K * 2 + 255) & ~(size_t) 255;
+    int rc = ensure_scratch(c, xa_bytes + (ldw != K ? (size_t) N * K * 2 : 0));
     if (rc) return rc;
     __half * xa = (__half *) c.scratch;
     k_f32_to_f16<<<nblk((long long) M * K), 256, 0, c.stream>>>((const float *) X, M, K, ldx, xa);
     if ((rc = launched("f32_to_f16"))) return rc;
+    const void * wd = W;
+    if (ldw != K) {
+        wd = (char *) c.scratch + xa_bytes;
+        cudaError_t e = cudaMemcpy2DAsync((void *) wd, (size_t) K * 2, W, (size_t) ldw * 2, (size_t) K * 2, N,
+                                          cudaMemcpyDefault, c.stream);
+        if (e != cudaSuccess) return fail(TSN_ERR_CUDA, std::string("compat gemm: pack W: ") + cudaGetErrorString(e));
+    }
     const int bn = N % 256 == 0 ? 256 : N % 128 == 0 ? 128 : 64;
     GemmLaunch g{};
-    g.bn = bn; g.epi = EPI_F32; g.stages = gemm_stages(bn); g.smem = gemm_smem_bytes(bn, g.stages); g.ab_bf16 = 0;
+    g.bn = bn; g.epi = EPI_F32; g.split = true; g.smem = gemm_smem_bytes(bn, true); g.ab_bf16 = 0;
     g.grid = dim3(N / bn, (M + 127) / 128, 1);
-    if (!make_act_map(&g.ta, xa, K, M, 1, 128, 1, 0)) return fail(TSN_ERR_CUDA, "compat gemm: A map");
-    // weight rows are ldw apart: view them as a [N][ldw] matrix, of which the K-box walk reads K
-    const cuuint64_t ld = ldw;
-    (void) ld;
-    if (ldw != K) {
-        // copy the K used columns into a dense f16 matrix so the TMA view has stride K
-        rc = ensure_scratch(c, (size_t) M * K * 2 + (size_t) N * K * 2 + 256);
-        if (rc) return rc;
-        xa = (__half *) c.scratch;
-        k_f32_to_f16<<<nblk((long long) M * K), 256, 0, c.stream>>>((const float *) X, M, K, ldx, xa);
-        __half * wd = (__half *) ((char *) c.scratch + (((size_t) M * K * 2 + 255) & ~(size_t) 255));
-        cudaMemcpy2DAsync(wd, (size_t) K * 2, W, (size_t) ldw * 2, (size_t) K * 2, N, cudaMemcpyDefault, c.stream);
-        if (!make_act_map(&g.ta, xa, K, M, 1, 128, 1, 0) || !make_w_map(&g.tb, wd, K, N, bn, 0))
-            return fail(TSN_ERR_CUDA, "compat gemm: maps");
-    } else if (!make_w_map(&g.tb, W, K, N, bn, 0)) {
-        return fail(TSN_ERR_CUDA, "compat gemm: W map");
-    }
+    if (!make_act_map(&g.ta, xa, K, M, 1, 128, 1, 0) || !make_act_map(&g.ta2, xa + (size_t) M * K, K, M, 1, 128, 1, 0) ||
+        !make_w_map(&g.tb, wd, K, N, bn, 0))
+        return fail(TSN_ERR_CUDA, "compat gemm: tensor maps");
     GemmArgs & a = g.args;
     a.rows = (int) M; a.B = 1; a.bt = 128; a.bb = 1; a.m_tiles_t = (int) ((M + 127) / 128); a.N = (int) N;
     a.k_blocks = (int) (K / 64); a.ic_blocks = (int) (K / 64); a.pad = 0; a.splits = 1; a.kb_per_split = a.k_blocks;

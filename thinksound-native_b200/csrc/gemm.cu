@@ -47,40 +47,44 @@ bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int gemm_stages(int bn) { return bn == 256 ? 4 : bn == 128 ? 6 : 8; }
+// Pipeline depth: as many stages as fit in ~192 KB of shared memory.
+constexpr int stages_for(int bn, bool split) {
+    return split ? (bn == 256 ? 3 : bn == 128 ? 4 : 5) : (bn == 256 ? 4 : bn == 128 ? 6 : 8);
+}
+int gemm_stages(int bn, bool split) { return stages_for(bn, split); }
 
-size_t gemm_smem_bytes(int bn, int stages) {
-    return (size_t) stages * (128 * 128 + bn * 128) + 256 + 1024;
+size_t gemm_smem_bytes(int bn, bool split) {
+    return (size_t) stages_for(bn, split) * ((split ? 2 : 1) * 128 * 128 + bn * 128) + 256 + 1024;
 }
 
 namespace {
-using KernelFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs, int);
+using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs, int);
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool SPLIT>
 KernelFn pick() {
-    constexpr int ST = BN == 256 ? 4 : BN == 128 ? 6 : 8;
-    static_assert(GemmSmem<BN, ST>::TOTAL <= 232448, "smem budget");
-    return (KernelFn) gemm_tc_kernel<BN, EPI, ST>;
+    constexpr int ST = stages_for(BN, SPLIT);
+    static_assert(GemmSmem<BN, ST, SPLIT>::TOTAL <= 232448, "smem budget");
+    return (KernelFn) gemm_tc_kernel<BN, EPI, ST, SPLIT>;
 }
 
-template <int BN>
+template <int BN, bool SPLIT>
 KernelFn pick_epi(int epi) {
     switch (epi) {
-        case EPI_F32: return pick<BN, EPI_F32>();
-        case EPI_F16: return pick<BN, EPI_F16>();
-        case EPI_F16_SILU: return pick<BN, EPI_F16_SILU>();
-        case EPI_SWIGLU: if constexpr (BN % 128 == 0) return pick<BN, EPI_SWIGLU>(); else return nullptr;
-        case EPI_GATE: return pick<BN, EPI_GATE>();
-        case EPI_QKV: return pick<BN, EPI_QKV>();
+        case EPI_F32: return pick<BN, EPI_F32, SPLIT>();
+        case EPI_F16: return pick<BN, EPI_F16, SPLIT>();
+        case EPI_F16_SILU: return pick<BN, EPI_F16_SILU, SPLIT>();
+        case EPI_SWIGLU: if constexpr (BN % 128 == 0) return pick<BN, EPI_SWIGLU, SPLIT>(); else return nullptr;
+        case EPI_GATE: return pick<BN, EPI_GATE, SPLIT>();
+        case EPI_QKV: return pick<BN, EPI_QKV, SPLIT>();
     }
     return nullptr;
 }
 
-KernelFn kernel_for(int bn, int epi) {
+KernelFn kernel_for(int bn, int epi, bool split) {
     switch (bn) {
-        case 64: return pick_epi<64>(epi);
-        case 128: return pick_epi<128>(epi);
-        case 256: return pick_epi<256>(epi);
+        case 64: return split ? pick_epi<64, true>(epi) : pick_epi<64, false>(epi);
+        case 128: return split ? pick_epi<128, true>(epi) : pick_epi<128, false>(epi);
+        case 256: return split ? pick_epi<256, true>(epi) : pick_epi<256, false>(epi);
     }
     return nullptr;
 }
@@ -88,21 +92,22 @@ KernelFn kernel_for(int bn, int epi) {
 
 // Set the dynamic shared-memory limit of every instantiation once, outside any stream capture.
 cudaError_t configure_gemm_kernels() {
-    for (int bn : {64, 128, 256})
-        for (int epi = 0; epi < 6; ++epi) {
-            KernelFn fn = kernel_for(bn, epi);
-            if (!fn) continue;
-            cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int) gemm_smem_bytes(bn, gemm_stages(bn)));
-            if (e != cudaSuccess) return e;
-        }
+    for (int split = 0; split < 2; ++split)
+        for (int bn : {64, 128, 256})
+            for (int epi = 0; epi < 6; ++epi) {
+                KernelFn fn = kernel_for(bn, epi, split != 0);
+                if (!fn) continue;
+                cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int) gemm_smem_bytes(bn, split != 0));
+                if (e != cudaSuccess) return e;
+            }
     return cudaSuccess;
 }
 
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
-    KernelFn fn = kernel_for(g.bn, g.epi);
+    KernelFn fn = kernel_for(g.bn, g.epi, g.split);
     if (!fn) return cudaErrorInvalidValue;
-    fn<<<g.grid, 192, g.smem, s>>>(g.ta, g.tb, g.args, g.ab_bf16);
+    fn<<<g.grid, 192, g.smem, s>>>(g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
     return cudaGetLastError();
 }
 

@@ -18,6 +18,12 @@
 //   warps 0-3   epilogue: tcgen05.ld rows from TMEM, fused op, global stores
 // Split-K (grid.z) writes f32 partials to a workspace; the last CTA of a tile (arrival counter)
 // sums them in split order 0..S-1 and runs the epilogue, so results are deterministic.
+//
+// Split operands (SPLIT=true). The reference keeps activations in f32; one f16 rounding of every
+// GEMM input costs ~2.8e-4 relative error per site and ~1.8e-3 on the 21-block flow. A split
+// operand stores A = A_hi + A_lo with A_hi = f16(A), A_lo = f16(A - A_hi) (~22-bit mantissa);
+// the kernel loads both tiles and issues hi and lo UMMAs into the same f32 TMEM accumulator
+// against the same f16 weight tile, so the product equals the f32-activation GEMM to ~2^-22.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -51,24 +57,41 @@ struct GemmArgs {
     const float2 * rope;                  // [rows][32] (cos, sin) or null (text stream)
     int H, s_off, S_pad, NH;
     __half * q; __half * k; __half * v;   // [B][NH][S_pad][64]
+    long long out_lo;                     // element offset of the lo half of a split f16 output (0: none)
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool SPLIT>
 struct GemmSmem {
     static constexpr int A_BYTES = 128 * 128;
+    static constexpr int NA = SPLIT ? 2 : 1;
     static constexpr int B_BYTES = BN * 128;
-    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int B_OFF = NA * A_BYTES;
+    static constexpr int STAGE = NA * A_BYTES + B_BYTES;
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int TOTAL = BAR_OFF + 256 + 1024;   // + barriers + alignment slack
 };
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
 
-template <int BN, int EPI, int STAGES>
+// store 8 f32 values as f16 at o, and their rounding residuals at o + lo (when lo != 0)
+__device__ __forceinline__ void store8_split(__half * o, long long lo, const float * v) {
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(v[e]);
+    *(uint4 *) o = *(const uint4 *) h;
+    if (lo) {
+        __align__(16) __half l[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) l[e] = __float2half_rn(v[e] - __half2float(h[e]));
+        *(uint4 *) (o + lo) = *(const uint4 *) l;
+    }
+}
+
+template <int BN, int EPI, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const GemmArgs a, const int ab_bf16) {
-    using L = GemmSmem<BN, STAGES>;
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+               const __grid_constant__ CUtensorMap tmB, const GemmArgs a, const int ab_bf16) {
+    using L = GemmSmem<BN, STAGES, SPLIT>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
@@ -92,7 +115,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         *last_flag = 0;
         fence_mbar_init();
     }
-    if (warp == 4 && lane == 0) { tma_prefetch(&tmA); tma_prefetch(&tmB); }
+    if (warp == 4 && lane == 0) {
+        tma_prefetch(&tmA);
+        if (SPLIT) tma_prefetch(&tmA2);
+        tma_prefetch(&tmB);
+    }
     if (warp == 5) tmem_alloc(tslot, BN);
     tc_fence_before();
     __syncthreads();
@@ -110,7 +137,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 uint8_t * sa = smem + s * L::STAGE;
                 mbar_expect_tx(&full[s], L::STAGE);
                 tma_load_3d(sa, &tmA, &full[s], ic0, t0 + tap - a.pad, b0);
-                tma_load_2d(sa + L::A_BYTES, &tmB, &full[s], kb * 64, n0);
+                if (SPLIT) tma_load_3d(sa + L::A_BYTES, &tmA2, &full[s], ic0, t0 + tap - a.pad, b0);
+                tma_load_2d(sa + L::B_OFF, &tmB, &full[s], kb * 64, n0);
             }
         }
     } else if (warp == 5) {
@@ -121,10 +149,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 if (!mbar_wait(&full[s], (i / STAGES) & 1, abort_flag, a.err, DEV_TIMEOUT_FULL)) break;
                 tc_fence_after();
                 const uint8_t * sa = smem + s * L::STAGE;
-                const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + L::A_BYTES);
+                const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + L::B_OFF);
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
+                for (int k = 0; k < 4; ++k) {
                     umma_f16(tmem, ad + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, (i | k) != 0);
+                    if (SPLIT) {
+                        const uint64_t al = umma_desc_sw128(sa + L::A_BYTES);
+                        umma_f16(tmem, al + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, 1u);
+                    }
+                }
                 umma_commit(&empty[s]);
             }
             umma_commit(tfull);
@@ -229,12 +262,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         __half * dst = which == 0 ? a.q : which == 1 ? a.k : a.v;
                         dst += (((size_t) b * a.NH + head) * a.S_pad + a.s_off + t) * 64;
 #pragma unroll
-                        for (int q = 0; q < 64; q += 8) {
-                            __align__(16) __half h[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(v[q + e]);
-                            *(uint4 *) (dst + q) = *(const uint4 *) h;
-                        }
+                        for (int q = 0; q < 64; q += 8) store8_split(dst + q, a.out_lo, v + q);
                     }
                 }
             } else {
@@ -253,14 +281,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
                     } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU) {
                         __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+                        if (EPI == EPI_F16_SILU) {
 #pragma unroll
-                        for (int q = 0; q < 32; q += 8) {
-                            __align__(16) __half h[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e)
-                                h[e] = __float2half_rn(EPI == EPI_F16_SILU ? silu_f(v[q + e]) : v[q + e]);
-                            *(uint4 *) (o + q) = *(const uint4 *) h;
+                            for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
                         }
+#pragma unroll
+                        for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, v + q);
                     } else if constexpr (EPI == EPI_GATE) {
                         float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
                         const float * g = a.mod + (long long) b * a.mod_bs + (a.mod_per_row ? (long long) t * a.mod_ld : 0) +

@@ -50,30 +50,37 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 }
 } // namespace
 
+// q, k, v and the output are split operands (hi + lo f16 halves, lo at +qkv_lo / +out_lo*):
+// S = qh·kh + qh·kl + ql·kh and O = P·vh + P·vl, so the only rounding left is P in f16.
+constexpr int ATTN_SMEM = 10 * 64 * 128;   // Q hi/lo + 2 x (K hi/lo) + 2 x (V hi/lo)
+
 __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
-    __shared__ __align__(128) uint8_t sQ[64 * 128];
-    __shared__ __align__(128) uint8_t sK[2][64 * 128];
-    __shared__ __align__(128) uint8_t sV[2][64 * 128];
+    extern __shared__ __align__(128) uint8_t sm[];
+    uint8_t * sQ = sm;                       // [hi | lo]
+    uint8_t * sK = sm + 2 * 8192;            // [buf][hi | lo]
+    uint8_t * sV = sm + 6 * 8192;            // [buf][hi | lo]
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t head = ((size_t) b * a.NH + h) * (size_t) a.S_pad * 64;
     const __half * Qg = a.q + head + (size_t) qt * 64 * 64;
     const __half * Kg = a.k + head;
     const __half * Vg = a.v + head;
+    const long long lo = a.qkv_lo;
     auto load_tile = [&](uint8_t * dst, const __half * src) {
         for (int i = tid; i < 512; i += 128) {
             const int r = i >> 3, c = i & 7;
             cp_async16(dst + swz(r, c), src + r * 64 + c * 8);
         }
     };
-    load_tile(sQ, Qg);
-    load_tile(sK[0], Kg);
-    load_tile(sV[0], Vg);
+    auto load_pair = [&](uint8_t * dst, const __half * src) { load_tile(dst, src); load_tile(dst + 8192, src + lo); };
+    load_pair(sQ, Qg);
+    load_pair(sK, Kg);
+    load_pair(sV, Vg);
     cp_commit();
 
     const int nkt = (a.S + 63) >> 6;
     const int mat = lane >> 3, mrow = lane & 7;
-    uint32_t qf[4][4];
+    uint32_t qf[4][4], ql[4][4];
     float o[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
@@ -81,8 +88,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
 
     for (int j = 0; j < nkt; ++j) {
         if (j + 1 < nkt) {
-            load_tile(sK[(j + 1) & 1], Kg + (size_t) (j + 1) * 64 * 64);
-            load_tile(sV[(j + 1) & 1], Vg + (size_t) (j + 1) * 64 * 64);
+            load_pair(sK + ((j + 1) & 1) * 16384, Kg + (size_t) (j + 1) * 64 * 64);
+            load_pair(sV + ((j + 1) & 1) * 16384, Vg + (size_t) (j + 1) * 64 * 64);
         }
         cp_commit();
         cp_wait1();
@@ -92,9 +99,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
             for (int kk = 0; kk < 4; ++kk) {
                 const int row = warp * 16 + (mat & 1) * 8 + mrow, ch = 2 * kk + (mat >> 1);
                 ldsm_x4(smem_u32(sQ) + swz(row, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+                ldsm_x4(smem_u32(sQ + 8192) + swz(row, ch), ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3]);
             }
         }
-        const uint32_t kb = smem_u32(sK[j & 1]), vb = smem_u32(sV[j & 1]);
+        const uint32_t kb = smem_u32(sK + (j & 1) * 16384), vb = smem_u32(sV + (j & 1) * 16384);
         float s[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
@@ -102,11 +110,16 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
         for (int kk = 0; kk < 4; ++kk) {
 #pragma unroll
             for (int p = 0; p < 4; ++p) {
-                uint32_t r0, r1, r2, r3;
+                uint32_t r0, r1, r2, r3, e0, e1, e2, e3;
                 const int key = 16 * p + (mat >> 1) * 8 + mrow, ch = 2 * kk + (mat & 1);
                 ldsm_x4(kb + swz(key, ch), r0, r1, r2, r3);
+                ldsm_x4(kb + 8192 + swz(key, ch), e0, e1, e2, e3);
                 mma16816(s[2 * p], qf[kk], r0, r1);
                 mma16816(s[2 * p + 1], qf[kk], r2, r3);
+                mma16816(s[2 * p], ql[kk], r0, r1);
+                mma16816(s[2 * p + 1], ql[kk], r2, r3);
+                mma16816(s[2 * p], qf[kk], e0, e1);
+                mma16816(s[2 * p + 1], qf[kk], e2, e3);
             }
         }
         // scale, mask keys >= S, online softmax (base 2)
@@ -143,7 +156,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
         l1 = l1 * al1 + ps1;
 #pragma unroll
         for (int dt = 0; dt < 8; ++dt) { o[dt][0] *= al0; o[dt][1] *= al0; o[dt][2] *= al1; o[dt][3] *= al1; }
-        // O += P V
+        // O += P (vh + vl)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
             uint32_t pa[4];
@@ -153,11 +166,14 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
             pa[3] = pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                uint32_t r0, r1, r2, r3;
+                uint32_t r0, r1, r2, r3, e0, e1, e2, e3;
                 const int key = 16 * kk + (mat & 1) * 8 + mrow, ch = 2 * q + (mat >> 1);
                 ldsm_x4_t(vb + swz(key, ch), r0, r1, r2, r3);
+                ldsm_x4_t(vb + 8192 + swz(key, ch), e0, e1, e2, e3);
                 mma16816(o[2 * q], pa, r0, r1);
                 mma16816(o[2 * q + 1], pa, r2, r3);
+                mma16816(o[2 * q], pa, e0, e1);
+                mma16816(o[2 * q + 1], pa, e2, e3);
             }
         }
         __syncthreads();
@@ -173,21 +189,30 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
         const int s_row = qt * 64 + warp * 16 + (lane >> 2) + half * 8;
         if (s_row >= a.S) continue;
         __half * dst;
-        if (s_row < a.n0) dst = a.out0 + ((size_t) b * a.n0 + s_row) * a.H;
-        else if (s_row < a.n0 + a.n1) dst = a.out1 + ((size_t) b * a.n1 + (s_row - a.n0)) * a.H;
-        else dst = a.out2 + ((size_t) b * a.n2 + (s_row - a.n0 - a.n1)) * a.H;
+        long long olo;
+        if (s_row < a.n0) { dst = a.out0 + ((size_t) b * a.n0 + s_row) * a.H; olo = a.out_lo0; }
+        else if (s_row < a.n0 + a.n1) { dst = a.out1 + ((size_t) b * a.n1 + (s_row - a.n0)) * a.H; olo = a.out_lo1; }
+        else { dst = a.out2 + ((size_t) b * a.n2 + (s_row - a.n0 - a.n1)) * a.H; olo = a.out_lo2; }
         dst += h * 64 + 2 * (lane & 3);
         const float inv = half ? i1 : i0;
 #pragma unroll
-        for (int dt = 0; dt < 8; ++dt)
-            *(__half2 *) (dst + dt * 8) = __floats2half2_rn(o[dt][2 * half] * inv, o[dt][2 * half + 1] * inv);
+        for (int dt = 0; dt < 8; ++dt) {
+            const float v0 = o[dt][2 * half] * inv, v1 = o[dt][2 * half + 1] * inv;
+            const __half2 hv = __floats2half2_rn(v0, v1);
+            *(__half2 *) (dst + dt * 8) = hv;
+            if (olo) *(__half2 *) (dst + dt * 8 + olo) = __floats2half2_rn(v0 - __low2float(hv), v1 - __high2float(hv));
+        }
     }
 }
 
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s) {
     dim3 grid((a.S + 63) / 64, a.NH, a.B);
-    attn_kernel<<<grid, 128, 0, s>>>(a);
+    attn_kernel<<<grid, 128, ATTN_SMEM, s>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t configure_attention() {
+    return cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATTN_SMEM);
 }
 
 // =============================================================================== adaLN
@@ -222,12 +247,19 @@ __global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
     for (int i = 0; i < NV; ++i) {
         const int c = (i * 32 + lane) * 4;
         const float4 sh = *(const float4 *) (m + c), sc = *(const float4 *) (m + a.H + c);
-        __align__(8) __half hv[4];
-        hv[0] = __float2half_rn((v[i].x - mean) * inv * (1.0f + sc.x) + sh.x);
-        hv[1] = __float2half_rn((v[i].y - mean) * inv * (1.0f + sc.y) + sh.y);
-        hv[2] = __float2half_rn((v[i].z - mean) * inv * (1.0f + sc.z) + sh.z);
-        hv[3] = __float2half_rn((v[i].w - mean) * inv * (1.0f + sc.w) + sh.w);
+        float y[4];
+        y[0] = (v[i].x - mean) * inv * (1.0f + sc.x) + sh.x;
+        y[1] = (v[i].y - mean) * inv * (1.0f + sc.y) + sh.y;
+        y[2] = (v[i].z - mean) * inv * (1.0f + sc.z) + sh.z;
+        y[3] = (v[i].w - mean) * inv * (1.0f + sc.w) + sh.w;
+        __align__(8) __half hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            hv[e] = __float2half_rn(y[e]);
+            lv[e] = __float2half_rn(y[e] - __half2float(hv[e]));
+        }
         *(uint2 *) (o + c) = *(const uint2 *) hv;
+        if (a.out_lo) *(uint2 *) (o + a.out_lo + c) = *(const uint2 *) lv;
     }
 }
 
@@ -315,7 +347,10 @@ __global__ void cond_kernel(const CondArgs a) {
             const int t = (int) (bt % a.T), b = (int) (bt / a.T);
             const float gc = a.gcmlp[(long long) b * a.H + c] + a.te[c];
             const float e = a.sync_gather[(long long) t * a.H + c] + gc;           // dit_fwd.cpp:135
-            a.extc16[r] = __float2half_rn(silu_d(e));                              // dit_fwd.cpp:136-137
+            const float es = silu_d(e);                                            // dit_fwd.cpp:136-137
+            const __half hi = __float2half_rn(es);
+            a.extc16[r] = hi;
+            a.extc16[r + a.extc_lo] = __float2half_rn(es - __half2float(hi));
             if (a.tap_extc) a.tap_extc[r] = e;
         } else if (i < nC) {
             const long long r = i - nB;                                            // dit_fwd.cpp:166
@@ -325,7 +360,10 @@ __global__ void cond_kernel(const CondArgs a) {
             a.text_s[r] = a.text_pp[r];
         } else {
             const long long r = i - nD;
-            a.x16[r] = __float2half_rn(a.x[r % ((long long) a.T * a.L)]);
+            const float xv = a.x[r % ((long long) a.T * a.L)];
+            const __half hi = __float2half_rn(xv);
+            a.x16[r] = hi;
+            a.x16[r + a.x_lo] = __float2half_rn(xv - __half2float(hi));
         }
     }
 }

@@ -12,10 +12,11 @@ namespace tsn {
 
 // ---- GEMM / implicit conv (gemm.cu) ----
 struct GemmLaunch {
-    CUtensorMap ta, tb;
+    CUtensorMap ta, ta2, tb;      // A (hi), A lo half (split operands only), weights
     GemmArgs args;
     dim3 grid;
-    int bn = 0, epi = 0, stages = 0, ab_bf16 = 0;
+    int bn = 0, epi = 0, ab_bf16 = 0;
+    bool split = false;
     size_t smem = 0;
 };
 // Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] 16-bit activation buffer.
@@ -25,8 +26,8 @@ bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t ro
 bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16);
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
 cudaError_t configure_gemm_kernels();
-size_t gemm_smem_bytes(int bn, int stages);
-int gemm_stages(int bn);
+size_t gemm_smem_bytes(int bn, bool split);
+int gemm_stages(int bn, bool split);
 
 // ---- attention (kernels.cu) ----
 struct AttnArgs {
@@ -36,7 +37,10 @@ struct AttnArgs {
     // output streams: joint row s < n0 -> out0 row s; s < n0+n1 -> out1; else out2
     __half * out0; __half * out1; __half * out2;             // [B][n_i][H]
     int n0, n1, n2, H;
+    long long qkv_lo;                                        // element offset of the lo halves of q, k, v
+    long long out_lo0, out_lo1, out_lo2;                     // ... and of each output (0: hi only)
 };
+cudaError_t configure_attention();
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s);
 
 // ---- adaLN LayerNorm + modulation -> f16 GEMM operand ----
@@ -46,6 +50,7 @@ struct AdaLnArgs {
     __half * out; long long out_bs;         // [B][rows][H] f16
     int B, rows, H;
     float eps;
+    long long out_lo;                       // element offset of the lo half (0: hi only)
 };
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s);
 
@@ -75,6 +80,7 @@ struct CondArgs {
     float * tap_gc;              // [B][H]     global_c before silu (nullable)
     float * tap_extc;            // [B][T][H]  extended_c before silu (nullable)
     int B, T, C, TS, H, L;
+    long long extc_lo, x_lo;     // element offsets of the lo halves of extc16 and x16
 };
 cudaError_t launch_cond(const CondArgs & a, cudaStream_t s);
 

@@ -329,20 +329,20 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
     ALLOC(modc, NJ * B * 6 * H * 4);
     ALLOC(modt, NJ * B * 6 * H * 4);
     ALLOC(flow, B * T * L * 4);
-    ALLOC(x16, B * T * L * 2);
-    ALLOC(extc16, B * T * H * 2);
-    ALLOC(xn_l, B * T * H * 2);
-    ALLOC(xn_c, B * C * H * 2);
-    ALLOC(xn_t, B * TS * H * 2);
-    ALLOC(att_l, B * T * H * 2);
-    ALLOC(att_c, B * C * H * 2);
-    ALLOC(att_t, B * TS * H * 2);
+    ALLOC(x16, 2 * B * T * L * 2);   // hi | lo
+    ALLOC(extc16, 2 * B * T * H * 2);   // hi | lo
+    ALLOC(xn_l, 2 * B * T * H * 2);   // hi | lo
+    ALLOC(xn_c, 2 * B * C * H * 2);   // hi | lo
+    ALLOC(xn_t, 2 * B * TS * H * 2);   // hi | lo
+    ALLOC(att_l, 2 * B * T * H * 2);   // hi | lo
+    ALLOC(att_c, 2 * B * C * H * 2);   // hi | lo
+    ALLOC(att_t, 2 * B * TS * H * 2);   // hi | lo
     ALLOC(h_l, B * T * F * 2);
     ALLOC(h_c, B * C * F * 2);
     ALLOC(h_t, B * TS * F * 2);
-    ALLOC(q, B * g.NH * S_pad * 64 * 2);
-    ALLOC(k, B * g.NH * S_pad * 64 * 2);
-    ALLOC(v, B * g.NH * S_pad * 64 * 2);
+    ALLOC(q, 2 * B * g.NH * S_pad * 64 * 2);   // hi | lo
+    ALLOC(k, 2 * B * g.NH * S_pad * 64 * 2);   // hi | lo
+    ALLOC(v, 2 * B * g.NH * S_pad * 64 * 2);   // hi | lo
     ALLOC(rope_l, T * 32 * sizeof(float2));
     ALLOC(rope_c, C * 32 * sizeof(float2));
     ALLOC(temb_tab, (size_t) max_steps * H * 4);
@@ -405,8 +405,11 @@ struct Plan {
 
     // Pick the tile width and split-K factor with a small cost model (per K-block time of one
     // CTA, waves over 148 SMs, split-K partial traffic), then encode both TMA views.
-    int gemm(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, int epi, GemmLaunch & g) {
+    // A is a split operand (hi at A, lo half right after it) unless `plain`.
+    int gemm(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, int epi, GemmLaunch & g,
+             bool plain = false) {
         const int B = m.B;
+        const bool split = !plain;
         const int bt = B >= 2 ? 64 : 128, bb = 128 / bt;
         const int mtt = (rows + bt - 1) / bt, mtb = (B + bb - 1) / bb;
         const int N = W.N, kb = W.taps * K_in / 64;
@@ -417,7 +420,8 @@ struct Plan {
             if (N % bn) continue;
             if (epi == EPI_SWIGLU && bn % 128) continue;
             if (epi == EPI_QKV && bn % 64) continue;
-            const double kcost = bn == 256 ? 0.37 : bn == 128 ? 0.24 : 0.18;
+            const double kcost = split ? (bn == 256 ? 0.74 : bn == 128 ? 0.40 : 0.30)
+                                       : (bn == 256 ? 0.37 : bn == 128 ? 0.24 : 0.18);
             const int tiles = mtt * mtb * (N / bn);
             for (int s = 1; s <= 16 && s <= kb; ++s) {
                 const int kbps = (kb + s - 1) / s;
@@ -434,11 +438,13 @@ struct Plan {
         g = GemmLaunch{};
         g.bn = bn_best;
         g.epi = epi;
-        g.stages = gemm_stages(bn_best);
-        g.smem = gemm_smem_bytes(bn_best, g.stages);
+        g.split = split;
+        g.smem = gemm_smem_bytes(bn_best, split);
         g.ab_bf16 = m.bf16;
         g.grid = dim3(N / bn_best, mtt * mtb, s_best);
+        const __half * Alo = (const __half *) A + (size_t) B * rows * K_in;
         if (!make_act_map(&g.ta, A, K_in, rows, B, bt, bb, m.bf16) ||
+            (split && !make_act_map(&g.ta2, Alo, K_in, rows, B, bt, bb, m.bf16)) ||
             !make_w_map(&g.tb, W.w, (uint64_t) W.taps * K_in, N, bn_best, m.bf16))
             return fail(TSN_ERR_CUDA, std::string(name) + ": tensor map encode failed");
         GemmArgs & a = g.args;
@@ -457,26 +463,29 @@ struct Plan {
     }
     static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
 
-    int out_f32(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * out, int ldo) {
+    int out_f32(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * out, int ldo,
+                bool plain = false) {
         GemmLaunch g;
-        int rc = gemm(name, A, K_in, rows, W, pad, EPI_F32, g);
+        int rc = gemm(name, A, K_in, rows, W, pad, EPI_F32, g, plain);
         if (rc) return rc;
         g.args.out = out; g.args.ldo = ldo; g.args.out_bs = (long long) rows * ldo;
         push(name, g, fl(m.B, rows, W));
         return TSN_OK;
     }
-    int out_f16(const char * name, int epi, const void * A, int K_in, int rows, const Lin & W, int pad, __half * out, int ldo) {
+    // out_lo: write the output as a split operand (lo half at out + out_lo) for a split consumer
+    int out_f16(const char * name, int epi, const void * A, int K_in, int rows, const Lin & W, int pad, __half * out, int ldo,
+                long long out_lo = 0) {
         GemmLaunch g;
         int rc = gemm(name, A, K_in, rows, W, pad, epi, g);
         if (rc) return rc;
-        g.args.out = out; g.args.ldo = ldo; g.args.out_bs = (long long) rows * ldo;
+        g.args.out = out; g.args.ldo = ldo; g.args.out_bs = (long long) rows * ldo; g.args.out_lo = out_lo;
         push(name, g, fl(m.B, rows, W));
         return TSN_OK;
     }
     int gate(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * res,
-             const float * mod, int per_row, long long mod_ld, long long mod_bs, int gate_idx) {
+             const float * mod, int per_row, long long mod_ld, long long mod_bs, int gate_idx, bool plain = false) {
         GemmLaunch g;
-        int rc = gemm(name, A, K_in, rows, W, pad, EPI_GATE, g);
+        int rc = gemm(name, A, K_in, rows, W, pad, EPI_GATE, g, plain);
         if (rc) return rc;
         g.args.out = res; g.args.ldo = m.g.H; g.args.out_bs = (long long) rows * m.g.H;
         g.args.mod = mod; g.args.mod_per_row = per_row; g.args.mod_ld = mod_ld; g.args.mod_bs = mod_bs;
@@ -491,18 +500,21 @@ struct Plan {
         GemmArgs & a = g.args;
         a.qn = b.qn; a.kn = b.kn; a.rope = rope; a.H = m.g.H; a.s_off = s_off; a.S_pad = m.S_pad; a.NH = m.g.NH;
         a.q = m.q; a.k = m.k; a.v = m.v;
+        a.out_lo = (long long) m.B * m.g.NH * m.S_pad * 64;
         push(name, g, fl(m.B, rows, b.qkv));
         return TSN_OK;
     }
     void adaln(const char * name, const float * x, int rows, const float * mod, int per_row, long long mod_ld,
                long long mod_bs, int base, __half * out) {
         AdaLnArgs a{x, (long long) rows * m.g.H, mod, mod_bs, mod_ld, per_row, base, out, (long long) rows * m.g.H,
-                    m.B, rows, (int) m.g.H, 1e-5f};
+                    m.B, rows, (int) m.g.H, 1e-5f, (long long) m.B * rows * m.g.H};
         ops.push_back(Op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name});
     }
     void attention(int S, int n0, int n1, int n2) {
+        const long long H = m.g.H;
         AttnArgs a{m.q, m.k, m.v, m.B, (int) m.g.NH, S, m.S_pad, 0.125f * 1.4426950408889634f,
-                   m.att_l, m.att_c, m.att_t, n0, n1, n2, (int) m.g.H};
+                   m.att_l, m.att_c, m.att_t, n0, n1, n2, (int) m.g.H,
+                   (long long) m.B * m.g.NH * m.S_pad * 64, m.B * m.T * H, m.B * m.C * H, m.B * m.TS * H};
         const double flops = 4.0 * m.B * (double) S * S * m.g.H;
         ops.push_back(Op{[a](cudaStream_t s) { return launch_attention(a, s); }, 1, flops, "attention"});
     }
@@ -514,7 +526,7 @@ struct Plan {
         if (rc) return rc;
         adaln("adaln_ffn", x, rows, mod, per_row, mod_ld, mod_bs, 3 * H, xn);
         if ((rc = out_f16("ffn_w13", EPI_SWIGLU, xn, H, rows, b.w13, pad, h, F))) return rc;
-        return gate("ffn_w2", h, F, rows, b.w2, pad, x, mod, per_row, mod_ld, mod_bs, 5);
+        return gate("ffn_w2", h, F, rows, b.w2, pad, x, mod, per_row, mod_ld, mod_bs, 5, true);
     }
     void tap(const std::string & name, const void * src, size_t bytes,
              std::function<void(const std::vector<uint8_t> &, int, std::vector<float> &)> cvt) {
@@ -566,7 +578,8 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb, 1, H, bfl, s); }, 2, 0, "t_embed.0"});
     ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb + 1, 1, H, bfl, s); }, 2, 0, "t_embed.2"});
     CondArgs ca{te, gcmlp, sync_gather, clip_pp, text_pp, x, gc_silu, extc16, clip_s, text_s, x16,
-                tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L};
+                tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L,
+                (long long) B * T * H, (long long) B * T * L};
     ops.push_back(Op{[ca](cudaStream_t s) { return launch_cond(ca, s); }, 2, 0, "cond"});
     ops.push_back(Op{[jb, nmj, H, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, bfl, s); }, 2, 0, "adaln_gemv"});
     if (tp) {
@@ -578,9 +591,9 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         p.tap("extended_c", tap_extc, (size_t) B * sTH * 4, cvt_f32_arm(sTH));
     }
     // audio_input_proj: conv k3 + silu, convmlp                   src/dit_fwd.cpp:143-149
-    if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H))) return rc;
+    if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H, (long long) B * T * H))) return rc;
     if ((rc = p.out_f16("audio_in.w13", EPI_SWIGLU, xn_l, H, T, ain13, 1, h_l, F))) return rc;
-    if ((rc = p.out_f32("audio_in.w2", h_l, F, T, ain2, 1, lat, H))) return rc;
+    if ((rc = p.out_f32("audio_in.w2", h_l, F, T, ain2, 1, lat, H, true))) return rc;
     if (tp) p.tap("x_in", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
     // joint blocks                                                src/dit_fwd.cpp:180-257
     for (int i = 0; i < NJ; ++i) {

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libtsn.so")
@@ -139,11 +140,14 @@ class Device:
         h = C.c_void_p()
         check(lib().tsn_device_create(ordinal, C.byref(h)))
         self.h = h
+        self._models = weakref.WeakSet()   # models must be freed before their device
         if stream is not None:
             check(lib().tsn_device_set_stream(self.h, C.c_void_p(stream)))
 
     def close(self):
         if self.h:
+            for m in list(self._models):
+                m.close()
             lib().tsn_device_destroy(self.h)
             self.h = None
 
@@ -203,15 +207,16 @@ class Dit:
             g = synthetic or geom()
             check(lib().tsn_dit_load_synthetic(dev.h, C.byref(g), seed, compute, C.byref(h)))
         self.h = h
+        dev._models.add(self)
         g = Geom()
         check(lib().tsn_dit_get_geom(self.h, C.byref(g)))
         self.geom = g
         self.T = self.C = self.TS = self.arms = 0
 
     def close(self):
-        if self.h:
+        if self.h and self.dev.h:
             lib().tsn_dit_free(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:
