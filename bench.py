@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--profile-ops", action="store_true", help="print one line per launch of an eager step to stderr")
     return ap.parse_args()
 
 
@@ -291,6 +292,8 @@ def run_tsn(a):
 
     prof = m.profile_step()
     kps = m.kernels_per_step()
+    if a.profile_ops and rank == 0:
+        print(m.profile_ops(), file=sys.stderr, flush=True)
     times = torch.tensor([ms, e2e_ms or 0.0], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)

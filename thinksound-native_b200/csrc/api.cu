@@ -413,6 +413,33 @@ int tsn_dit_profile_step(tsn_dit * m, double * out5) {
     return TSN_OK;
 }
 
+int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap) {
+    M_BEGIN NEED_PREPARED
+    const std::vector<Op> & ops = M.ops_fwd;
+    std::vector<cudaEvent_t> ev(ops.size() + 1);
+    for (auto & e : ev) CKR(cudaEventCreate(&e));
+    cudaStream_t s = M.dev->stream;
+    CKR(cudaEventRecord(ev[0], s));
+    for (size_t i = 0; i < ops.size(); ++i) {
+        cudaError_t e = ops[i].fn(s);
+        if (e != cudaSuccess) return fail(TSN_ERR_CUDA, "launch " + ops[i].name + ": " + cudaGetErrorString(e));
+        CKR(cudaEventRecord(ev[i + 1], s));
+    }
+    TRY(M.dev->sync());
+    std::string rep;
+    char line[320];
+    for (size_t i = 0; i < ops.size(); ++i) {
+        float ms = 0;
+        CKR(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+        const double tf = ops[i].flops > 0 && ms > 0 ? ops[i].flops / (ms * 1e-3) / 1e12 : 0.0;
+        snprintf(line, sizeof line, "%4zu %-14s %8.4f ms %8.1f TF/s  %s\n", i, ops[i].name.c_str(), ms, tf, ops[i].desc.c_str());
+        rep += line;
+    }
+    for (auto & e : ev) cudaEventDestroy(e);
+    if (out && cap) { std::strncpy(out, rep.c_str(), cap - 1); out[cap - 1] = 0; }
+    return TSN_OK;
+}
+
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep) {
     if (!path || !g) return fail(TSN_ERR_ARG, "null argument");
     DitGeom dg;

@@ -459,7 +459,10 @@ struct Plan {
         return TSN_OK;
     }
     void push(const char * name, const GemmLaunch & g, double flops) {
-        ops.push_back(Op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name});
+        char d[160];
+        snprintf(d, sizeof d, "bn=%d split=%d ksplit=%d grid=%ux%ux%u kb=%d smem=%zu", g.bn, (int) g.split, g.args.splits,
+                 g.grid.x, g.grid.y, g.grid.z, g.args.k_blocks, g.smem);
+        ops.push_back(Op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name, d});
     }
     static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
 

@@ -54,6 +54,7 @@ struct Op {
     int kind = 2;          // 0 tensor-core GEMM, 1 attention, 2 other
     double flops = 0.0;
     std::string name;
+    std::string desc;      // launch configuration, for profiles
 };
 
 struct TapBuf {

@@ -93,6 +93,7 @@ _SIGS = [
     ("tsn_dit_step_host", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float, C.c_float]),
     ("tsn_dit_kernels_per_step", C.c_int, [C.c_void_p]),
     ("tsn_dit_profile_step", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
+    ("tsn_dit_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_gguf_write_synthetic", C.c_int, [C.c_char_p, C.POINTER(Geom), C.c_uint64, C.c_int]),
 ]
 
@@ -277,6 +278,12 @@ class Dit:
         check(lib().tsn_dit_profile_step(self.h, out))
         return {"gemm_ms": out[0], "attn_ms": out[1], "other_ms": out[2], "gemm_flops": out[3],
                 "gemm_launches": int(out[4])}
+
+
+    def profile_ops(self) -> str:
+        buf = C.create_string_buffer(1 << 20)
+        check(lib().tsn_dit_profile_ops(self.h, buf, len(buf)))
+        return buf.value.decode()
 
 
 def write_synthetic_gguf(path: str, g: Geom, seed: int = 4242, with_prep: bool = False):
