@@ -77,6 +77,18 @@ double tsn_last_gpu_ms(tsn_device * dev);
  * f32 (wf16=0), leading dimensions in elements (0 = dense). */
 int tsn_gemm(tsn_device * dev, int wf16, const void * W, const void * X, void * Y, const void * bias,
              uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy);
+/* No counterpart in the reference. The same product as tsn_gemm with f16 weights, for callers
+ * that must not allocate device memory once running: an audio host's real-time render thread
+ * (cudaMalloc can take a device-wide lock and synchronise the GPU mid-callback) or a process
+ * whose device memory another framework's pool allocator divided up front. tsn_gemm grows a
+ * cudaMalloc'd scratch buffer for its split f16 copy of X; this entry point uses a fixed 8 MiB
+ * device array inside the library instead and calls no allocator. Limits: K and N multiples of
+ * 64, and 4*M*K bytes (plus 2*N*K when ldw != K) at most 8 MiB, else TSN_ERR_ARG. The first call
+ * on each device looks up the array's device address; make that first call before any stream
+ * capture begins. Every call on a device shares the one array: calls that overlap on the GPU
+ * (other streams, other threads) race on it, so serialise them. */
+int tsn_gemm_noalloc(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias,
+                     uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy);
 /* Runtime::gemv (src/net.h:25-26). */
 int tsn_gemv(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias,
              uint32_t N, uint32_t K, uint32_t ldw, int wf16);

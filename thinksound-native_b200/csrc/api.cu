@@ -10,7 +10,11 @@
 
 using namespace tsn;
 
-namespace tsn { const std::string & last_error(); }
+namespace tsn {
+const std::string & last_error();
+int gemm_noalloc(DeviceCtx & c, const void * W, const void * X, void * Y, const void * bias, uint32_t M, uint32_t N,
+                 uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy);
+}
 
 struct tsn_device { DeviceCtx ctx; };
 struct tsn_dit { Model m; };
@@ -156,6 +160,11 @@ int tsn_gemm(tsn_device * dev, int wf16, const void * W, const void * X, void * 
              uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy) {
     RT_BEGIN
     return compat_gemm(c, wf16, W, X, Y, bias, M, N, K, ldx ? ldx : K, ldw ? ldw : K, ldy ? ldy : N);
+}
+int tsn_gemm_noalloc(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias,
+                     uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy) {
+    RT_BEGIN
+    return gemm_noalloc(c, W, X, Y, bias, M, N, K, ldx ? ldx : K, ldw ? ldw : K, ldy ? ldy : N);
 }
 int tsn_gemv(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias, uint32_t N, uint32_t K,
              uint32_t ldw, int wf16) {

@@ -62,6 +62,8 @@ _SIGS = [
     ("tsn_last_gpu_ms", C.c_double, [C.c_void_p]),
     ("tsn_gemm", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                            C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+    ("tsn_gemm_noalloc", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
     ("tsn_gemv", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
                            C.c_uint32, C.c_uint32, C.c_int]),
     ("tsn_conv", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -183,6 +185,10 @@ class Device:
     # --- net.h Runtime
     def gemm(self, wf16, W, X, Y, bias, M, N, K, ldx=0, ldw=0, ldy=0):
         check(lib().tsn_gemm(self.h, int(wf16), _p(W), _p(X), _p(Y), _p(bias), M, N, K, ldx, ldw, ldy))
+
+    def gemm_noalloc(self, W, X, Y, bias, M, N, K, ldx=0, ldw=0, ldy=0):
+        """tsn_gemm (f16 weights) without any device allocation: scratch is a fixed 8 MiB array."""
+        check(lib().tsn_gemm_noalloc(self.h, _p(W), _p(X), _p(Y), _p(bias), M, N, K, ldx, ldw, ldy))
 
     def gemv(self, W, X, Y, bias, N, K, ldw=0, wf16=True):
         check(lib().tsn_gemv(self.h, _p(W), _p(X), _p(Y), _p(bias), N, K, ldw, int(wf16)))
