@@ -2,6 +2,7 @@
 // tensor-map encoders (driver entry point fetched through the runtime, no -lcuda needed).
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
 
 #include "kernels.h"
@@ -107,8 +108,71 @@ cudaError_t configure_gemm_kernels() {
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
     KernelFn fn = kernel_for(g.bn, g.epi, g.split);
     if (!fn) return cudaErrorInvalidValue;
-    fn<<<g.grid, 192, g.smem, s>>>(g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
-    return cudaGetLastError();
+    if (g.args.splits <= 1) {
+        fn<<<g.grid, 192, g.smem, s>>>(g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
+        return cudaGetLastError();
+    }
+    // split-K: the K slices of one output tile form a cluster along grid.z
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = g.grid;
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = g.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned) g.args.splits;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fn, g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
+}
+
+int cluster_capacity_uncached(int bn, int epi, bool split, int cluster);
+
+// How many CTAs of this configuration can run at once when grouped in clusters of `cluster`.
+int gemm_cluster_capacity(int bn, int epi, bool split, int cluster) {
+    static std::mutex mu;
+    static std::map<int, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int key = ((dev * 512 + bn) * 8 + epi) * 64 + (split ? 32 : 0) + cluster;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    const int cap = cluster_capacity_uncached(bn, epi, split, cluster);
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = cap;
+    return cap;
+}
+
+int cluster_capacity_uncached(int bn, int epi, bool split, int cluster) {
+    KernelFn fn = kernel_for(bn, epi, split);
+    if (!fn) return 0;
+    if (cluster <= 1) {
+        int per_sm = 0, sms = 0, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 192, gemm_smem_bytes(bn, split)) != cudaSuccess)
+            return 0;
+        return per_sm * sms;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1, 1, (unsigned) cluster);
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = gemm_smem_bytes(bn, split);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned) cluster;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n * cluster;
 }
 
 } // namespace tsn

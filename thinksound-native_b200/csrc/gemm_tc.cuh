@@ -16,8 +16,10 @@
 //   warp 4      TMA producer: A box + B box per 64-wide K block into a STAGES-deep smem ring
 //   warp 5      TMEM allocation + single-thread tcgen05.mma issue (M=128, N=BN, K=16 x 4)
 //   warps 0-3   epilogue: tcgen05.ld rows from TMEM, fused op, global stores
-// Split-K (grid.z) writes f32 partials to a workspace; the last CTA of a tile (arrival counter)
-// sums them in split order 0..S-1 and runs the epilogue, so results are deterministic.
+// Split-K (grid.z = S) runs the S K-slices of a tile as one thread-block cluster: each CTA stages
+// its f32 partial in its own shared memory, a cluster barrier publishes them, and CTA q reduces the
+// q-th 1/S share of the tile by reading all S partials over distributed shared memory, in the fixed
+// order 0..S-1 (deterministic), then applies the epilogue to that share. No global scratch.
 //
 // Split operands (SPLIT=true). The reference keeps activations in f32; one f16 rounding of every
 // GEMM input costs ~2.8e-4 relative error per site and ~1.8e-3 on the 21-block flow. A split
@@ -43,8 +45,6 @@ enum GemmEpi : int {
 
 struct GemmArgs {
     int rows, B, bt, bb, m_tiles_t, N, k_blocks, ic_blocks, pad, splits, kb_per_split;
-    float * ws;              // split-K partials
-    int * counters;          // split-K arrival counters, one per output tile, self-resetting
     int * err;               // device error word
     const float * bias;      // [N] or null
     void * out;              // EPI_F32/F16*/SWIGLU output, EPI_GATE residual (f32)
@@ -87,6 +87,104 @@ __device__ __forceinline__ void store8_split(__half * o, long long lo, const flo
     }
 }
 
+// Columns one epilogue call handles: one 32-column chunk; a whole 64-column head for the qkv
+// epilogue (RMSNorm + RoPE need it); a [64 w1 | 64 w3] group for SwiGLU.
+template <int EPI> struct EpiUnit { static constexpr int U = EPI == EPI_QKV ? 64 : EPI == EPI_SWIGLU ? 128 : 32; };
+
+// Epilogue for tile row r, columns [u*U, (u+1)*U) of the tile. load32(c, v) returns the 32
+// accumulated values of columns [c, c+32) of row r (from TMEM, or summed over the cluster's
+// partials). In the TMEM path every lane must call load32 (warp-collective tcgen05.ld), so the
+// validity test only guards the stores.
+template <int EPI, typename Load>
+__device__ __forceinline__ void epi_unit(const GemmArgs & a, int r, int u, int n0, int t0, int b0, bool ok, Load && load32) {
+    constexpr int U = EpiUnit<EPI>::U;
+    const int b = b0 + r / a.bt, t = t0 + r % a.bt;
+    const bool valid = ok && t < a.rows && b < a.B;
+    const int c0 = u * U;
+    if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int j = 0; j < 64; j += 32) {
+            float va[32], vb[32];
+            load32(c0 + j, va);
+            load32(c0 + 64 + j, vb);
+            if (valid) {
+                const long long nout = (long long) (n0 + c0) / 2 + j;
+                __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + nout;
+#pragma unroll
+                for (int q = 0; q < 32; q += 8) {
+                    __align__(16) __half h[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(va[q + e]) * vb[q + e]);
+                    *(uint4 *) (o + q) = *(const uint4 *) h;
+                }
+            }
+        }
+    } else if constexpr (EPI == EPI_QKV) {
+        float v[64];
+        load32(c0, v);
+        load32(c0 + 32, v + 32);
+        if (!valid) return;
+        const int n = n0 + c0, which = n / a.H, head = (n % a.H) >> 6;
+#pragma unroll
+        for (int e = 0; e < 64; ++e) v[e] += a.bias[n + e];
+        if (which < 2) {
+            const float * g = which == 0 ? a.qn : a.kn;
+            float ss = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
+            const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+#pragma unroll
+            for (int e = 0; e < 64; ++e) v[e] = v[e] * inv * g[e];
+            if (a.rope) {
+                const float2 * cs = a.rope + (size_t) t * 32;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const float2 w = cs[j];
+                    const float x0 = v[2 * j], x1 = v[2 * j + 1];
+                    v[2 * j] = x0 * w.x - x1 * w.y;
+                    v[2 * j + 1] = x0 * w.y + x1 * w.x;
+                }
+            }
+        }
+        __half * dst = which == 0 ? a.q : which == 1 ? a.k : a.v;
+        dst += (((size_t) b * a.NH + head) * a.S_pad + a.s_off + t) * 64;
+#pragma unroll
+        for (int q = 0; q < 64; q += 8) store8_split(dst + q, a.out_lo, v + q);
+    } else {
+        float v[32];
+        load32(c0, v);
+        if (!valid) return;
+        const int n = n0 + c0;
+        if (a.bias) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] += a.bias[n + e];
+        }
+        if constexpr (EPI == EPI_F32) {
+            float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+        } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU) {
+            __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+            if (EPI == EPI_F16_SILU) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
+            }
+#pragma unroll
+            for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, v + q);
+        } else if constexpr (EPI == EPI_GATE) {
+            float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+            const float * g = a.mod + (long long) b * a.mod_bs + (a.mod_per_row ? (long long) t * a.mod_ld : 0) + a.gate_off + n;
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) {
+                float4 x = *(float4 *) (o + q);
+                const float4 gg = *(const float4 *) (g + q);
+                x.x += v[q] * gg.x; x.y += v[q + 1] * gg.y; x.z += v[q + 2] * gg.z; x.w += v[q + 3] * gg.w;
+                *(float4 *) (o + q) = x;
+            }
+        }
+    }
+}
+
 template <int BN, int EPI, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
@@ -99,7 +197,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t * tfull = empty + STAGES;
     uint32_t * tslot = (uint32_t *) (tfull + 1);
     volatile int * abort_flag = (volatile int *) (tslot + 1);
-    volatile int * last_flag = abort_flag + 1;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = blockIdx.y % a.m_tiles_t, mb = blockIdx.y / a.m_tiles_t;
@@ -112,7 +209,6 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(tfull, 1);
         *abort_flag = 0;
-        *last_flag = 0;
         fence_mbar_init();
     }
     if (warp == 4 && lane == 0) {
@@ -163,150 +259,65 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             umma_commit(tfull);
         }
     } else {
-        // ------------------------------------------------------------------ epilogue
+        // ------------------------------------------------------------------ epilogue, part 1
         const bool ok = mbar_wait(tfull, 0, abort_flag, a.err, DEV_TIMEOUT_TMEM) && !*abort_flag;
         tc_fence_after();
         const int r = warp * 32 + lane;
-        const int b = b0 + r / a.bt, t = t0 + r % a.bt;
-        const bool valid = ok && t < a.rows && b < a.B;
         const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
-        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-        const int S = a.splits;
-        bool reduce = false;
-        if (S > 1) {
-            // partial -> workspace [tile][split][BN/4][128] float4
-            float4 * wp = (float4 *) a.ws + ((size_t) tile * S + blockIdx.z) * (BN / 4) * 128;
+        if (a.splits == 1) {
+            auto load_tmem = [&](int c, float * v) { tmem_ld32(trow + c, v); };
+#pragma unroll 1
+            for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, r, u, n0, t0, b0, ok, load_tmem);
+        } else {
+            // stage this CTA's partial in its own shared memory as [BN/4][128] float4 (the stage ring
+            // is free: every TMA load was consumed and every MMA has completed)
+            float4 * part = (float4 *) smem;
             for (int c = 0; c < BN; c += 32) {
                 float v[32];
                 tmem_ld32(trow + c, v);
-                if (ok) {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        __stcg(&wp[(size_t) (c / 4 + j) * 128 + r], make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-                }
+                for (int j = 0; j < 8; ++j)
+                    part[(c / 4 + j) * 128 + r] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             }
-            __threadfence();
-            epi_bar();
-            if (r == 0) {
-                const int prev = atomicAdd(&a.counters[tile], 1);
-                *last_flag = (prev == S - 1);
-            }
-            epi_bar();
-            reduce = *last_flag != 0;
-            if (!reduce) goto teardown;
-            __threadfence();
         }
-        {
-            const float4 * wbase = (const float4 *) a.ws + (size_t) tile * S * (BN / 4) * 128;
-            // 32 accumulated columns starting at column c of the tile
-            auto load32 = [&](int c, float * v) {
-                if (!reduce) { tmem_ld32(trow + c, v); return; }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    float4 s4 = __ldcg(&wbase[(size_t) (c / 4 + j) * 128 + r]);
-                    for (int sp = 1; sp < S; ++sp) {
-                        const float4 p4 = __ldcg(&wbase[((size_t) sp * (BN / 4) + c / 4 + j) * 128 + r]);
-                        s4.x += p4.x; s4.y += p4.y; s4.z += p4.z; s4.w += p4.w;
-                    }
-                    v[4 * j] = s4.x; v[4 * j + 1] = s4.y; v[4 * j + 2] = s4.z; v[4 * j + 3] = s4.w;
-                }
-            };
-            if constexpr (EPI == EPI_SWIGLU) {
-                static_assert(BN % 128 == 0, "swiglu tiles hold whole [64 a | 64 b] groups");
-                for (int g = 0; g < BN; g += 128) {
-                    for (int j = 0; j < 64; j += 32) {
-                        float va[32], vb[32];
-                        load32(g + j, va);
-                        load32(g + 64 + j, vb);
-                        if (valid) {
-                            const long long nout = (long long) (n0 + g) / 2 + j;
-                            __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + nout;
-#pragma unroll
-                            for (int q = 0; q < 32; q += 8) {
-                                __align__(16) __half h[8];
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(va[q + e]) * vb[q + e]);
-                                *(uint4 *) (o + q) = *(const uint4 *) h;
-                            }
-                        }
-                    }
-                }
-            } else if constexpr (EPI == EPI_QKV) {
-                for (int c = 0; c < BN; c += 64) {
-                    float v[64];
-                    load32(c, v);
-                    load32(c + 32, v + 32);
-                    if (valid) {
-                        const int n = n0 + c, which = n / a.H, head = (n % a.H) >> 6;
-#pragma unroll
-                        for (int e = 0; e < 64; ++e) v[e] += a.bias[n + e];
-                        if (which < 2) {
-                            const float * g = which == 0 ? a.qn : a.kn;
-                            float ss = 0.0f;
-#pragma unroll
-                            for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
-                            const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
-#pragma unroll
-                            for (int e = 0; e < 64; ++e) v[e] = v[e] * inv * g[e];
-                            if (a.rope) {
-                                const float2 * cs = a.rope + (size_t) t * 32;
-#pragma unroll
-                                for (int j = 0; j < 32; ++j) {
-                                    const float2 w = cs[j];
-                                    const float x0 = v[2 * j], x1 = v[2 * j + 1];
-                                    v[2 * j] = x0 * w.x - x1 * w.y;
-                                    v[2 * j + 1] = x0 * w.y + x1 * w.x;
-                                }
-                            }
-                        }
-                        __half * dst = which == 0 ? a.q : which == 1 ? a.k : a.v;
-                        dst += (((size_t) b * a.NH + head) * a.S_pad + a.s_off + t) * 64;
-#pragma unroll
-                        for (int q = 0; q < 64; q += 8) store8_split(dst + q, a.out_lo, v + q);
-                    }
-                }
-            } else {
-                for (int c = 0; c < BN; c += 32) {
-                    float v[32];
-                    load32(c, v);
-                    if (!valid) continue;
-                    const int n = n0 + c;
-                    if (a.bias) {
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) v[e] += a.bias[n + e];
-                    }
-                    if constexpr (EPI == EPI_F32) {
-                        float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
-#pragma unroll
-                        for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-                    } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU) {
-                        __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
-                        if (EPI == EPI_F16_SILU) {
-#pragma unroll
-                            for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
-                        }
-#pragma unroll
-                        for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, v + q);
-                    } else if constexpr (EPI == EPI_GATE) {
-                        float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
-                        const float * g = a.mod + (long long) b * a.mod_bs + (a.mod_per_row ? (long long) t * a.mod_ld : 0) +
-                                          a.gate_off + n;
-#pragma unroll
-                        for (int q = 0; q < 32; q += 4) {
-                            float4 x = *(float4 *) (o + q);
-                            const float4 gg = *(const float4 *) (g + q);
-                            x.x += v[q] * gg.x; x.y += v[q + 1] * gg.y; x.z += v[q + 2] * gg.z; x.w += v[q + 3] * gg.w;
-                            *(float4 *) (o + q) = x;
-                        }
-                    }
-                }
-            }
-            if (reduce && r == 0) a.counters[tile] = 0;
-        }
-    teardown:;
     }
     tc_fence_before();
     __syncthreads();
+    if (a.splits > 1) {
+        // ---------------------------------------------------------- epilogue, part 2 (cluster)
+        cluster_sync_all();
+        if (warp < 4 && !*abort_flag) {
+            const int S = a.splits;
+            const uint32_t q = cluster_rank();
+            const uint32_t local = smem_u32(smem);
+            uint32_t peer[8];
+#pragma unroll
+            for (int sp = 0; sp < 8; ++sp) peer[sp] = sp < S ? dsmem_map(local, (uint32_t) sp) : 0u;
+            constexpr int U = EpiUnit<EPI>::U;
+            const int items = (BN / U) * 128;
+            const int lo = (int) ((long long) items * q / S), hi = (int) ((long long) items * (q + 1) / S);
+            for (int it = lo + (int) threadIdx.x; it < hi; it += 128) {
+                const int rr = it & 127, u = it >> 7;
+                auto load_dsmem = [&](int c, float * v) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t off = (uint32_t) (((c / 4 + j) * 128 + rr) * 16);
+                        float4 p[8];
+#pragma unroll
+                        for (int sp = 0; sp < 8; ++sp)
+                            if (sp < S) p[sp] = dsmem_ld4(peer[sp] + off);
+                        float4 acc = p[0];
+#pragma unroll
+                        for (int sp = 1; sp < 8; ++sp)
+                            if (sp < S) { acc.x += p[sp].x; acc.y += p[sp].y; acc.z += p[sp].z; acc.w += p[sp].w; }
+                        v[4 * j] = acc.x; v[4 * j + 1] = acc.y; v[4 * j + 2] = acc.z; v[4 * j + 3] = acc.w;
+                    }
+                };
+                epi_unit<EPI>(a, rr, u, n0, t0, b0, true, load_dsmem);
+            }
+        }
+        cluster_sync_all();   // peers have finished reading this CTA's shared memory
+    }
     if (warp == 5) {
         tc_fence_after();
         tmem_dealloc(tmem, BN);

@@ -348,11 +348,6 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
     ALLOC(temb_tab, (size_t) max_steps * H * 4);
     ALLOC(dt_tab, (size_t) max_steps * 4);
     ALLOC(step, 64);
-    ws_bytes = (size_t) 48 << 20;
-    ALLOC(ws, ws_bytes);
-    n_counters = 1 << 16;
-    counters_used = 0;
-    ALLOC(counters, (size_t) n_counters * 4);
     ALLOC(tap_gc, B * H * 4);
     ALLOC(tap_extc, B * T * H * 4);
     n_mod_jobs = 2 * (int) NJ;
@@ -403,9 +398,9 @@ struct Plan {
     Model & m;
     std::vector<Op> & ops;
 
-    // Pick the tile width and split-K factor with a small cost model (per K-block time of one
-    // CTA, waves over 148 SMs, split-K partial traffic), then encode both TMA views.
-    // A is a split operand (hi at A, lo half right after it) unless `plain`.
+    // Pick the tile width and split-K (cluster) factor with a small cost model: per-K-block time
+    // of one CTA, waves over the CTAs that fit at once (clusters need their S SMs in one GPC), and
+    // the cluster reduction; then encode the TMA views.
     int gemm(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, int epi, GemmLaunch & g,
              bool plain = false) {
         const int B = m.B;
@@ -419,22 +414,20 @@ struct Plan {
         for (int bn : {256, 128, 64}) {
             if (N % bn) continue;
             if (epi == EPI_SWIGLU && bn % 128) continue;
-            if (epi == EPI_QKV && bn % 64) continue;
             const double kcost = split ? (bn == 256 ? 0.74 : bn == 128 ? 0.40 : 0.30)
                                        : (bn == 256 ? 0.37 : bn == 128 ? 0.24 : 0.18);
             const int tiles = mtt * mtb * (N / bn);
-            for (int s = 1; s <= 16 && s <= kb; ++s) {
+            for (int s = 1; s <= 8 && s <= kb; ++s) {
                 const int kbps = (kb + s - 1) / s;
                 if ((kb + kbps - 1) / kbps != s) continue;
-                if (s > 1 && (size_t) tiles * s * bn * 128 * 4 > m.ws_bytes) continue;
-                if (s > 1 && m.counters_used + tiles > m.n_counters) continue;
-                const int ctas = tiles * s, waves = (ctas + 147) / 148;
-                const double cost = waves * (kbps * kcost + 2.0 + (s > 1 ? (s + 1) * bn * 512.0 / 135e3 : 0.0));
+                const int cap = gemm_cluster_capacity(bn, epi, split, s);
+                if (cap <= 0) continue;
+                const int ctas = tiles * s, waves = (ctas + cap - 1) / cap;
+                const double cost = waves * (kbps * kcost + 1.5 + (s > 1 ? 1.5 : 0.0));
                 if (cost < best - 1e-9) { best = cost; bn_best = bn; s_best = s; }
             }
         }
         if (!bn_best) return fail(TSN_ERR_ARG, std::string(name) + ": no tile fits N=" + std::to_string(N));
-        const int tiles = mtt * mtb * (N / bn_best);
         g = GemmLaunch{};
         g.bn = bn_best;
         g.epi = epi;
@@ -451,9 +444,6 @@ struct Plan {
         a.rows = rows; a.B = B; a.bt = bt; a.bb = bb; a.m_tiles_t = mtt; a.N = N;
         a.k_blocks = kb; a.ic_blocks = K_in / 64; a.pad = pad;
         a.splits = s_best; a.kb_per_split = (kb + s_best - 1) / s_best;
-        a.ws = m.ws;
-        a.counters = m.counters + m.counters_used;
-        if (s_best > 1) m.counters_used += tiles;
         a.err = m.dev->d_err;
         a.bias = W.b;
         return TSN_OK;
@@ -568,7 +558,6 @@ auto cvt_f16_arm(size_t per_arm) {
 
 int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     ops.clear();
-    if (mode != 2) counters_used = 0;
     Plan p{*this, ops};
     const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim, NJ = (int) g.n_joint();
     const bool tp = mode == 2;

@@ -86,10 +86,6 @@ struct Model {
     float * temb_tab = nullptr, * dt_tab = nullptr;
     int * step = nullptr;
     int max_steps = 1024;
-    float * ws = nullptr;
-    size_t ws_bytes = 0;
-    int * counters = nullptr;
-    int n_counters = 0, counters_used = 0;
     GemvJob * jobs = nullptr;
     int n_mod_jobs = 0;
     float * tap_gc = nullptr, * tap_extc = nullptr;
