@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--profile-ops", action="store_true", help="print one line per launch of an eager step to stderr")
+    ap.add_argument("--no-autotune", action="store_true", help="keep the static tile cost model")
     return ap.parse_args()
 
 
@@ -247,6 +248,12 @@ def run_tsn(a):
     f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
     m.set_conditioning(f(a.C, a.H), f(a.T, a.H), f(2, a.TS, a.H), f(2, a.H))
     m.set_x(f(a.T, 64))
+    tuned = None
+    if not a.no_autotune:
+        rep = m.autotune()
+        tuned = True
+        if a.profile_ops and rank == 0:
+            print(rep, file=sys.stderr, flush=True)
     total = a.warmup + a.steps
     m.schedule(min(total, 1024), a.cfg)
 
@@ -318,7 +325,8 @@ def run_tsn(a):
             "metric": METRIC, "value": world * a.steps / (ms * 1e-3), "unit": "steps/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 (split hi+lo activations), f32 accumulate", "data": "synthetic",
-            "config": dict(workload(a), parallelism=f"dp{world} (one generation per GPU, no data-path collective)"),
+            "config": dict(workload(a), parallelism=f"dp{world} (one generation per GPU, no data-path collective)",
+                           gemm_tiles="autotuned per shape at load" if tuned else "static cost model"),
             "roofline": {"bound": "tensor", "achieved": g_tf, "peak": tf_sus, "unit": "TFLOP/s",
                          "frac": g_tf / tf_sus, "traffic": None,
                          "kernel": "gemm_tc_kernel (tcgen05 GEMM / implicit conv), all launches of one step",

@@ -168,6 +168,12 @@ int tsn_dit_profile_step(tsn_dit * m, double * out5);
  * written into out (NUL-terminated, truncated to cap). */
 int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap);
 
+/* Time every valid tile configuration (tile width, cluster split-K factor) of each distinct GEMM
+ * shape of the prepared forward on this device and keep the fastest (the default is a static cost
+ * model). Results stay bit-identical between calls of this model; two processes that tune
+ * differently may differ in the last bits. Writes one line per shape into report. */
+int tsn_dit_autotune(tsn_dit * m, char * report, size_t cap);
+
 /* ------------------------------------------------------------------ fixtures */
 /* Write the seeded synthetic DiT GGUF (with_prep adds the conditioning-prep tensors). Host only. */
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep);

@@ -449,6 +449,14 @@ int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap) {
     return TSN_OK;
 }
 
+int tsn_dit_autotune(tsn_dit * m, char * report, size_t cap) {
+    M_BEGIN NEED_PREPARED
+    std::string rep;
+    TRY(M.autotune(rep));
+    if (report && cap) { std::strncpy(report, rep.c_str(), cap - 1); report[cap - 1] = 0; }
+    return TSN_OK;
+}
+
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep) {
     if (!path || !g) return fail(TSN_ERR_ARG, "null argument");
     DitGeom dg;

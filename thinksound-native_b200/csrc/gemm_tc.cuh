@@ -174,12 +174,19 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, int r, int u, int n
         } else if constexpr (EPI == EPI_GATE) {
             float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
             const float * g = a.mod + (long long) b * a.mod_bs + (a.mod_per_row ? (long long) t * a.mod_ld : 0) + a.gate_off + n;
+            // all 16 loads first, then the stores: interleaving them serialises one L2 round trip per
+            // 4 columns (the compiler cannot move a load of g above a store to o)
+            float4 xr[8], gr[8];
 #pragma unroll
-            for (int q = 0; q < 32; q += 4) {
-                float4 x = *(float4 *) (o + q);
-                const float4 gg = *(const float4 *) (g + q);
-                x.x += v[q] * gg.x; x.y += v[q + 1] * gg.y; x.z += v[q + 2] * gg.z; x.w += v[q + 3] * gg.w;
-                *(float4 *) (o + q) = x;
+            for (int q = 0; q < 8; ++q) {
+                xr[q] = __ldcg((const float4 *) (o + 4 * q));
+                gr[q] = __ldg((const float4 *) (g + 4 * q));
+            }
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                xr[q].x += v[4 * q] * gr[q].x; xr[q].y += v[4 * q + 1] * gr[q].y;
+                xr[q].z += v[4 * q + 2] * gr[q].z; xr[q].w += v[4 * q + 3] * gr[q].w;
+                *(float4 *) (o + 4 * q) = xr[q];
             }
         }
     }

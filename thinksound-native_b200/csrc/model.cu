@@ -397,6 +397,7 @@ namespace {
 struct Plan {
     Model & m;
     std::vector<Op> & ops;
+    std::string last_shape;
 
     // Pick the tile width and split-K (cluster) factor with a small cost model: per-K-block time
     // of one CTA, waves over the CTAs that fit at once (clusters need their S SMs in one GPC), and
@@ -428,6 +429,11 @@ struct Plan {
             }
         }
         if (!bn_best) return fail(TSN_ERR_ARG, std::string(name) + ": no tile fits N=" + std::to_string(N));
+        auto fo = m.gemm_force.find(m.gemm_seq);
+        if (fo != m.gemm_force.end()) { bn_best = fo->second.first; s_best = fo->second.second; }
+        char key[128];
+        snprintf(key, sizeof key, "%d:%d:%d:%d:%d:%d", rows, N, K_in, W.taps, epi, (int) split);
+        last_shape = key;
         g = GemmLaunch{};
         g.bn = bn_best;
         g.epi = epi;
@@ -452,7 +458,10 @@ struct Plan {
         char d[160];
         snprintf(d, sizeof d, "bn=%d split=%d ksplit=%d grid=%ux%ux%u kb=%d smem=%zu", g.bn, (int) g.split, g.args.splits,
                  g.grid.x, g.grid.y, g.grid.z, g.args.k_blocks, g.smem);
-        ops.push_back(Op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name, d});
+        Op op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name, d};
+        op.gemm_id = m.gemm_seq++;
+        op.shape = last_shape;
+        ops.push_back(op);
     }
     static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
 
@@ -558,6 +567,7 @@ auto cvt_f16_arm(size_t per_arm) {
 
 int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     ops.clear();
+    gemm_seq = 0;
     Plan p{*this, ops};
     const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim, NJ = (int) g.n_joint();
     const bool tp = mode == 2;
@@ -667,6 +677,67 @@ int Model::run_ops(const std::vector<Op> & ops) {
         cudaError_t e = o.fn(dev->stream);
         if (e != cudaSuccess) return fail(TSN_ERR_CUDA, "launch " + o.name + ": " + cudaGetErrorString(e));
     }
+    return TSN_OK;
+}
+
+// Time every valid (tile width, splits) candidate of each distinct GEMM shape of the forward with
+// CUDA events and keep the fastest for every GEMM of that shape. Writes one line per shape.
+int Model::autotune(std::string & report) {
+    std::map<std::string, std::vector<int>> ids;          // shape -> gemm ids
+    std::map<std::string, size_t> first;                  // shape -> op index of its first GEMM
+    for (size_t i = 0; i < ops_fwd.size(); ++i) {
+        const Op & o = ops_fwd[i];
+        if (o.kind != 0) continue;
+        if (!ids.count(o.shape)) first[o.shape] = i;
+        ids[o.shape].push_back(o.gemm_id);
+    }
+    cudaEvent_t e0, e1;
+    CKR(cudaEventCreate(&e0));
+    CKR(cudaEventCreate(&e1));
+    std::map<int, std::pair<int, int>> best_cfg;
+    char line[256];
+    for (auto & [shape, list] : ids) {
+        const size_t oi = first[shape];
+        const int gid = ops_fwd[oi].gemm_id;
+        double best = 1e30;
+        std::pair<int, int> bc{0, 0};
+        std::string tried;
+        for (int bn : {256, 128, 64})
+            for (int sp = 1; sp <= 8; ++sp) {
+                gemm_force.clear();
+                gemm_force[gid] = {bn, sp};
+                std::vector<Op> tmp;
+                if (build_ops(tmp, 0, 0.0f) != TSN_OK) { clear_error(); continue; }
+                const Op & o = tmp[oi];
+                if (o.desc.find("bn=" + std::to_string(bn) + " ") == std::string::npos) continue;
+                if (o.desc.find("ksplit=" + std::to_string(sp) + " ") == std::string::npos) continue;
+                bool okk = true;
+                for (int w = 0; w < 2 && okk; ++w) okk = o.fn(dev->stream) == cudaSuccess;
+                if (!okk) { cudaGetLastError(); continue; }
+                CKR(cudaEventRecord(e0, dev->stream));
+                for (int r = 0; r < 5; ++r) o.fn(dev->stream);
+                CKR(cudaEventRecord(e1, dev->stream));
+                if (dev->sync() != TSN_OK) { gemm_force.clear(); return TSN_ERR_CUDA; }
+                float ms = 0;
+                CKR(cudaEventElapsedTime(&ms, e0, e1));
+                ms /= 5;
+                snprintf(line, sizeof line, " %d/%d:%.1f", bn, sp, ms * 1e3);
+                tried += line;
+                if (ms < best) { best = ms; bc = {bn, sp}; }
+            }
+        for (int id : list) best_cfg[id] = bc;
+        snprintf(line, sizeof line, "%-16s %-22s best bn=%d splits=%d %.1f us x%zu |", ops_fwd[oi].name.c_str(), shape.c_str(),
+                 bc.first, bc.second, best * 1e3, list.size());
+        report += line + tried + "\n";
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    gemm_force = best_cfg;
+    int rc = build_ops(ops_fwd, 0, 0.0f);
+    if (rc) return rc;
+    rc = capture(ops_fwd, &gx_fwd);
+    if (rc) return rc;
+    if (gx_step) { cudaGraphExecDestroy(gx_step); gx_step = nullptr; }   // recaptured with the new configs
     return TSN_OK;
 }
 

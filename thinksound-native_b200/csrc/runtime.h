@@ -55,6 +55,8 @@ struct Op {
     double flops = 0.0;
     std::string name;
     std::string desc;      // launch configuration, for profiles
+    int gemm_id = -1;      // GEMM sequence number within the forward (kind 0)
+    std::string shape;     // GEMM shape key: ops with equal keys have the same candidate configs
 };
 
 struct TapBuf {
@@ -91,6 +93,9 @@ struct Model {
     float * tap_gc = nullptr, * tap_extc = nullptr;
     std::map<std::string, TapBuf> taps;
 
+    // GEMM configuration overrides by GEMM sequence number in the forward: (tile width, splits)
+    std::map<int, std::pair<int, int>> gemm_force;
+    int gemm_seq = 0;
     std::vector<Op> ops_fwd, ops_step;
     cudaGraphExec_t gx_fwd = nullptr, gx_step = nullptr;
     float step_cfg = 0.0f;
@@ -102,6 +107,7 @@ struct Model {
     int build_ops(std::vector<Op> & ops, int mode, float cfg);   // mode 0 forward, 1 step, 2 taps
     int run_ops(const std::vector<Op> & ops);
     int capture(const std::vector<Op> & ops, cudaGraphExec_t * out);
+    int autotune(std::string & report);
     int set_time(float t, float dt);
     void temb_host(float t, float * out) const;
     void release_activations();

@@ -96,6 +96,7 @@ _SIGS = [
     ("tsn_dit_kernels_per_step", C.c_int, [C.c_void_p]),
     ("tsn_dit_profile_step", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
     ("tsn_dit_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    ("tsn_dit_autotune", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_gguf_write_synthetic", C.c_int, [C.c_char_p, C.POINTER(Geom), C.c_uint64, C.c_int]),
 ]
 
@@ -285,6 +286,11 @@ class Dit:
         return {"gemm_ms": out[0], "attn_ms": out[1], "other_ms": out[2], "gemm_flops": out[3],
                 "gemm_launches": int(out[4])}
 
+
+    def autotune(self) -> str:
+        buf = C.create_string_buffer(1 << 20)
+        check(lib().tsn_dit_autotune(self.h, buf, len(buf)))
+        return buf.value.decode()
 
     def profile_ops(self) -> str:
         buf = C.create_string_buffer(1 << 20)
