@@ -2,6 +2,7 @@
 // tensor-map encoders (driver entry point fetched through the runtime, no -lcuda needed).
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <map>
 #include <mutex>
 
@@ -105,27 +106,17 @@ cudaError_t configure_gemm_kernels() {
     return cudaSuccess;
 }
 
+bool pdl_enabled() {
+    static const bool on = std::getenv("TSN_NO_PDL") == nullptr;
+    return on;
+}
+
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
     KernelFn fn = kernel_for(g.bn, g.epi, g.split);
     if (!fn) return cudaErrorInvalidValue;
-    if (g.args.splits <= 1) {
-        fn<<<g.grid, 192, g.smem, s>>>(g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
-        return cudaGetLastError();
-    }
     // split-K: the K slices of one output tile form a cluster along grid.z
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = g.grid;
-    cfg.blockDim = dim3(192, 1, 1);
-    cfg.dynamicSmemBytes = g.smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = (unsigned) g.args.splits;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, fn, g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
+    return launch_ex(fn, g.grid, dim3(192), g.smem, s, g.args.splits > 1 ? (unsigned) g.args.splits : 1u,
+                     g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
 }
 
 int cluster_capacity_uncached(int bn, int epi, bool split, int cluster);

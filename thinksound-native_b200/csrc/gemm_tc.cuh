@@ -218,6 +218,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         *abort_flag = 0;
         fence_mbar_init();
     }
+    if (threadIdx.x == 0) pdl_trigger();
     if (warp == 4 && lane == 0) {
         tma_prefetch(&tmA);
         if (SPLIT) tma_prefetch(&tmA2);
@@ -231,6 +232,15 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
     if (warp == 4) {
         if (lane == 0) {
+            // weights do not depend on the upstream kernel: start the first stages' weight loads,
+            // then wait for upstream outputs before loading activations
+            const int pre = nk < STAGES ? nk : STAGES;
+            for (int i = 0; i < pre; ++i) {
+                uint8_t * sa = smem + i * L::STAGE;
+                mbar_expect_tx(&full[i], L::STAGE);
+                tma_load_2d(sa + L::B_OFF, &tmB, &full[i], (kb_begin + i) * 64, n0);
+            }
+            pdl_wait();
             for (int i = 0; i < nk; ++i) {
                 const int s = i % STAGES;
                 if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_EMPTY))
@@ -238,10 +248,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 const int kb = kb_begin + i;
                 const int tap = kb / a.ic_blocks, ic0 = (kb % a.ic_blocks) * 64;
                 uint8_t * sa = smem + s * L::STAGE;
-                mbar_expect_tx(&full[s], L::STAGE);
+                if (i >= pre) {
+                    mbar_expect_tx(&full[s], L::STAGE);
+                    tma_load_2d(sa + L::B_OFF, &tmB, &full[s], kb * 64, n0);
+                }
                 tma_load_3d(sa, &tmA, &full[s], ic0, t0 + tap - a.pad, b0);
                 if (SPLIT) tma_load_3d(sa + L::A_BYTES, &tmA2, &full[s], ic0, t0 + tap - a.pad, b0);
-                tma_load_2d(sa + L::B_OFF, &tmB, &full[s], kb * 64, n0);
             }
         }
     } else if (warp == 5) {
@@ -267,6 +279,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
     } else {
         // ------------------------------------------------------------------ epilogue, part 1
+        pdl_wait();
         const bool ok = mbar_wait(tfull, 0, abort_flag, a.err, DEV_TIMEOUT_TMEM) && !*abort_flag;
         tc_fence_after();
         const int r = warp * 32 + lane;

@@ -55,6 +55,8 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 constexpr int ATTN_SMEM = 10 * 64 * 128;   // Q hi/lo + 2 x (K hi/lo) + 2 x (V hi/lo)
 
 __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t * sQ = sm;                       // [hi | lo]
     uint8_t * sK = sm + 2 * 8192;            // [buf][hi | lo]
@@ -206,9 +208,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
 }
 
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s) {
-    dim3 grid((a.S + 63) / 64, a.NH, a.B);
-    attn_kernel<<<grid, 128, ATTN_SMEM, s>>>(a);
-    return cudaGetLastError();
+    return launch_ex(attn_kernel, dim3((a.S + 63) / 64, a.NH, a.B), dim3(128), ATTN_SMEM, s, 1u, a);
 }
 
 cudaError_t configure_attention() {
@@ -218,6 +218,8 @@ cudaError_t configure_attention() {
 // =============================================================================== adaLN
 template <int NV>
 __global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= a.B * a.rows) return;
     const int b = gw / a.rows, t = gw % a.rows;
@@ -267,15 +269,14 @@ cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s) {
     const int nrows = a.B * a.rows;
     const dim3 grid((nrows + 7) / 8);
     switch (a.H / 128) {
-        case 1: adaln_kernel<1><<<grid, 256, 0, s>>>(a); break;
-        case 2: adaln_kernel<2><<<grid, 256, 0, s>>>(a); break;
-        case 4: adaln_kernel<4><<<grid, 256, 0, s>>>(a); break;
-        case 8: adaln_kernel<8><<<grid, 256, 0, s>>>(a); break;
-        case 12: adaln_kernel<12><<<grid, 256, 0, s>>>(a); break;
-        case 16: adaln_kernel<16><<<grid, 256, 0, s>>>(a); break;
+        case 1: return launch_ex(adaln_kernel<1>, grid, dim3(256), 0, s, 1u, a);
+        case 2: return launch_ex(adaln_kernel<2>, grid, dim3(256), 0, s, 1u, a);
+        case 4: return launch_ex(adaln_kernel<4>, grid, dim3(256), 0, s, 1u, a);
+        case 8: return launch_ex(adaln_kernel<8>, grid, dim3(256), 0, s, 1u, a);
+        case 12: return launch_ex(adaln_kernel<12>, grid, dim3(256), 0, s, 1u, a);
+        case 16: return launch_ex(adaln_kernel<16>, grid, dim3(256), 0, s, 1u, a);
         default: return cudaErrorInvalidValue;
     }
-    return cudaGetLastError();
 }
 
 // =============================================================================== GEMV
@@ -287,6 +288,8 @@ __device__ __forceinline__ void cvt8(uint4 w, int bf16, float * f) {
 }
 
 __global__ void __launch_bounds__(256) gemv_kernel(const GemvJob * jobs, int ab_bf16) {
+    pdl_trigger();
+    pdl_wait();
     const GemvJob j = jobs[blockIdx.y];
     const int n = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (n >= j.N) return;
@@ -320,15 +323,15 @@ __global__ void __launch_bounds__(256) gemv_kernel(const GemvJob * jobs, int ab_
 }
 
 cudaError_t launch_gemv(const GemvJob * jobs_dev, int njobs, int max_n, int ab_bf16, cudaStream_t s) {
-    dim3 grid((max_n + 7) / 8, njobs);
-    gemv_kernel<<<grid, 256, 0, s>>>(jobs_dev, ab_bf16);
-    return cudaGetLastError();
+    return launch_ex(gemv_kernel, dim3((max_n + 7) / 8, njobs), dim3(256), 0, s, 1u, jobs_dev, ab_bf16);
 }
 
 // =============================================================================== conditioning
 __device__ __forceinline__ float silu_d(float v) { return v / (1.0f + expf(-v)); }
 
 __global__ void cond_kernel(const CondArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const long long nA = (long long) a.B * a.H;
     const long long nB = nA + (long long) a.B * a.T * a.H;
     const long long nC = nB + (long long) a.B * a.C * a.H;
@@ -369,13 +372,14 @@ __global__ void cond_kernel(const CondArgs a) {
 }
 
 cudaError_t launch_cond(const CondArgs & a, cudaStream_t s) {
-    cond_kernel<<<592, 256, 0, s>>>(a);
-    return cudaGetLastError();
+    return launch_ex(cond_kernel, dim3(592), dim3(256), 0, s, 1u, a);
 }
 
 // =============================================================================== sampler
 __global__ void cfg_euler_kernel(const float * flow2, float * x, int n, float cfg, const float * dt_table,
                                  const int * step, float dt_const) {
+    pdl_trigger();
+    pdl_wait();
     const float dt = dt_table ? dt_table[*step] : dt_const;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float fc = flow2[i], fu = flow2[n + i];
@@ -383,16 +387,18 @@ __global__ void cfg_euler_kernel(const float * flow2, float * x, int n, float cf
         x[i] = __fadd_rn(x[i], __fmul_rn(dt, v));
     }
 }
-__global__ void step_advance_kernel(int * step) { *step += 1; }
+__global__ void step_advance_kernel(int * step) {
+    pdl_trigger();
+    pdl_wait();
+    *step += 1;
+}
 
 cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, float cfg, const float * dt_table,
                              const int * step, float dt_const, cudaStream_t s) {
-    cfg_euler_kernel<<<(n + 255) / 256, 256, 0, s>>>(flow2, x, n, cfg, dt_table, step, dt_const);
-    return cudaGetLastError();
+    return launch_ex(cfg_euler_kernel, dim3((n + 255) / 256), dim3(256), 0, s, 1u, flow2, x, n, cfg, dt_table, step, dt_const);
 }
 cudaError_t launch_step_advance(int * step, cudaStream_t s) {
-    step_advance_kernel<<<1, 1, 0, s>>>(step);
-    return cudaGetLastError();
+    return launch_ex(step_advance_kernel, dim3(1), dim3(1), 0, s, 1u, step);
 }
 
 // =============================================================================== weights

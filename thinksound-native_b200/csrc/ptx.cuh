@@ -146,6 +146,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float * v) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Kernels are launched with programmatic stream serialisation: the next kernel may start while
+// this one runs. pdl_wait() blocks until every upstream grid has completed and its writes are
+// visible; every thread calls it before its first read of upstream outputs or its first global
+// write. pdl_trigger() lets the downstream grid begin launching (it still waits in pdl_wait).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---------------------------------------------------------------- thread-block clusters
 __device__ __forceinline__ uint32_t cluster_rank() {
     uint32_t r;
