@@ -217,10 +217,10 @@ cudaError_t configure_attention() {
 
 // =============================================================================== adaLN
 template <int NV>
-__global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
+__global__ void __launch_bounds__(64) adaln_kernel(const AdaLnArgs a) {
     pdl_trigger();
     pdl_wait();
-    const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * 2 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= a.B * a.rows) return;
     const int b = gw / a.rows, t = gw % a.rows;
     const float * xr = a.x + (long long) b * a.x_bs + (long long) t * a.H;
@@ -267,14 +267,14 @@ __global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
 
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s) {
     const int nrows = a.B * a.rows;
-    const dim3 grid((nrows + 7) / 8);
+    const dim3 grid((nrows + 1) / 2);   // two rows (warps) per block: enough blocks to cover the SMs
     switch (a.H / 128) {
-        case 1: return launch_ex(adaln_kernel<1>, grid, dim3(256), 0, s, 1u, a);
-        case 2: return launch_ex(adaln_kernel<2>, grid, dim3(256), 0, s, 1u, a);
-        case 4: return launch_ex(adaln_kernel<4>, grid, dim3(256), 0, s, 1u, a);
-        case 8: return launch_ex(adaln_kernel<8>, grid, dim3(256), 0, s, 1u, a);
-        case 12: return launch_ex(adaln_kernel<12>, grid, dim3(256), 0, s, 1u, a);
-        case 16: return launch_ex(adaln_kernel<16>, grid, dim3(256), 0, s, 1u, a);
+        case 1: return launch_ex(adaln_kernel<1>, grid, dim3(64), 0, s, 1u, a);
+        case 2: return launch_ex(adaln_kernel<2>, grid, dim3(64), 0, s, 1u, a);
+        case 4: return launch_ex(adaln_kernel<4>, grid, dim3(64), 0, s, 1u, a);
+        case 8: return launch_ex(adaln_kernel<8>, grid, dim3(64), 0, s, 1u, a);
+        case 12: return launch_ex(adaln_kernel<12>, grid, dim3(64), 0, s, 1u, a);
+        case 16: return launch_ex(adaln_kernel<16>, grid, dim3(64), 0, s, 1u, a);
         default: return cudaErrorInvalidValue;
     }
 }
