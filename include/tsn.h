@@ -168,6 +168,11 @@ int tsn_dit_profile_step(tsn_dit * m, double * out5);
  * written into out (NUL-terminated, truncated to cap). */
 int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap);
 
+/* Run the forward up to GEMM launch `op` (index in tsn_dit_profile_ops) and that GEMM once more
+ * with per-CTA phase timestamps (globaltimer ns): entry, setup done, first stage landed,
+ * accumulator complete, epilogue done, exit — 6 per CTA into out (max_ctas CTAs). */
+int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_ctas, int * n_ctas);
+
 /* Time every valid tile configuration (tile width, cluster split-K factor) of each distinct GEMM
  * shape of the prepared forward on this device and keep the fastest (the default is a static cost
  * model). Results stay bit-identical between calls of this model; two processes that tune

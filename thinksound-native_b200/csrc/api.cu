@@ -457,6 +457,23 @@ int tsn_dit_autotune(tsn_dit * m, char * report, size_t cap) {
     return TSN_OK;
 }
 
+int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_ctas, int * n_ctas) {
+    M_BEGIN NEED_PREPARED
+    if (op < 0 || op >= (int) M.ops_fwd.size() || !M.ops_fwd[op].traced) return fail(TSN_ERR_ARG, "op is not a GEMM");
+    const Op & o = M.ops_fwd[op];
+    const size_t n = (size_t) o.ctas * TRACE_SLOTS;
+    unsigned long long * d = nullptr;
+    CKR(cudaMalloc(&d, n * 8));
+    CKR(cudaMemsetAsync(d, 0, n * 8, M.dev->stream));
+    for (size_t i = 0; i < M.ops_fwd.size() && (int) i < op; ++i) M.ops_fwd[i].fn(M.dev->stream);   // inputs of op
+    cudaError_t e = o.traced(M.dev->stream, d);
+    int rc = e == cudaSuccess ? M.dev->sync() : fail(TSN_ERR_CUDA, cudaGetErrorString(e));
+    if (!rc && out) CKR(cudaMemcpy(out, d, std::min(n, max_ctas * TRACE_SLOTS) * 8, cudaMemcpyDeviceToHost));
+    cudaFree(d);
+    if (n_ctas) *n_ctas = o.ctas;
+    return rc;
+}
+
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep) {
     if (!path || !g) return fail(TSN_ERR_ARG, "null argument");
     DitGeom dg;

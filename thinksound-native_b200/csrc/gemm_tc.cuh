@@ -58,7 +58,12 @@ struct GemmArgs {
     int H, s_off, S_pad, NH;
     __half * q; __half * k; __half * v;   // [B][NH][S_pad][64]
     long long out_lo;                     // element offset of the lo half of a split f16 output (0: none)
+    unsigned long long * trace;           // optional per-CTA phase timestamps (tsn_dit_trace_op), else null
 };
+
+// phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),
+// accumulator complete (epilogue), epilogue done, exit
+constexpr int TRACE_SLOTS = 6;
 
 template <int BN, int STAGES, bool SPLIT>
 struct GemmSmem {
@@ -68,10 +73,22 @@ struct GemmSmem {
     static constexpr int B_OFF = NA * A_BYTES;
     static constexpr int STAGE = NA * A_BYTES + B_BYTES;
     static constexpr int BAR_OFF = STAGES * STAGE;
-    static constexpr int TOTAL = BAR_OFF + 256 + 1024;   // + barriers + alignment slack
+    static constexpr int CONST_OFF = BAR_OFF + 256;       // epilogue constants: bias slice, q/k gains
+    static constexpr int TOTAL = CONST_OFF + 2048 + 1024; // + alignment slack
 };
 
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + expf(-v)); }
+// SiLU with the fast exponential and division (relative error ~1e-7, far below the f16 operand
+// rounding every downstream GEMM sees)
+__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+
+__device__ __forceinline__ void prefetch_l1(const void * p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
+// Per-tile epilogue constants staged in shared memory before the accumulator is ready.
+struct EpiConst {
+    const float * bias;   // bias[n0 .. n0+BN) in shared memory, or null
+    const float * qn;     // q RMSNorm gains (64), shared memory
+    const float * kn;     // k RMSNorm gains (64), shared memory
+};
 
 // store 8 f32 values as f16 at o, and their rounding residuals at o + lo (when lo != 0)
 __device__ __forceinline__ void store8_split(__half * o, long long lo, const float * v) {
@@ -96,7 +113,8 @@ template <int EPI> struct EpiUnit { static constexpr int U = EPI == EPI_QKV ? 64
 // partials). In the TMEM path every lane must call load32 (warp-collective tcgen05.ld), so the
 // validity test only guards the stores.
 template <int EPI, typename Load>
-__device__ __forceinline__ void epi_unit(const GemmArgs & a, int r, int u, int n0, int t0, int b0, bool ok, Load && load32) {
+__device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec, int r, int u, int n0, int t0, int b0, bool ok,
+                                         Load && load32) {
     constexpr int U = EpiUnit<EPI>::U;
     const int b = b0 + r / a.bt, t = t0 + r % a.bt;
     const bool valid = ok && t < a.rows && b < a.B;
@@ -126,9 +144,9 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, int r, int u, int n
         if (!valid) return;
         const int n = n0 + c0, which = n / a.H, head = (n % a.H) >> 6;
 #pragma unroll
-        for (int e = 0; e < 64; ++e) v[e] += a.bias[n + e];
+        for (int e = 0; e < 64; ++e) v[e] += ec.bias[c0 + e];
         if (which < 2) {
-            const float * g = which == 0 ? a.qn : a.kn;
+            const float * g = which == 0 ? ec.qn : ec.kn;
             float ss = 0.0f;
 #pragma unroll
             for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
@@ -155,9 +173,9 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, int r, int u, int n
         load32(c0, v);
         if (!valid) return;
         const int n = n0 + c0;
-        if (a.bias) {
+        if (ec.bias) {
 #pragma unroll
-            for (int e = 0; e < 32; ++e) v[e] += a.bias[n + e];
+            for (int e = 0; e < 32; ++e) v[e] += ec.bias[c0 + e];
         }
         if constexpr (EPI == EPI_F32) {
             float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
@@ -204,8 +222,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     uint64_t * tfull = empty + STAGES;
     uint32_t * tslot = (uint32_t *) (tfull + 1);
     volatile int * abort_flag = (volatile int *) (tslot + 1);
+    float * cbias = (float *) (smem + L::CONST_OFF);      // BN floats
+    float * cqn = cbias + 256, * ckn = cqn + 64;           // 64 + 64 floats
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    unsigned long long * tr = a.trace ? a.trace + (size_t) cta * TRACE_SLOTS : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
     const int mt = blockIdx.y % a.m_tiles_t, mb = blockIdx.y / a.m_tiles_t;
     const int t0 = mt * a.bt, b0 = mb * a.bb, n0 = blockIdx.x * BN;
     const int kb_begin = blockIdx.z * a.kb_per_split;
@@ -229,6 +252,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    if (tr && threadIdx.x == 0) tr[1] = global_ns();
 
     if (warp == 4) {
         if (lane == 0) {
@@ -262,6 +286,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int i = 0; i < nk; ++i) {
                 const int s = i % STAGES;
                 if (!mbar_wait(&full[s], (i / STAGES) & 1, abort_flag, a.err, DEV_TIMEOUT_FULL)) break;
+                if (tr && i == 0) tr[2] = global_ns();
                 tc_fence_after();
                 const uint8_t * sa = smem + s * L::STAGE;
                 const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + L::B_OFF);
@@ -280,14 +305,27 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     } else {
         // ------------------------------------------------------------------ epilogue, part 1
         pdl_wait();
+        {   // stage the tile's constants while the mainloop runs; warm L1 with this row's RoPE entries
+            const int tid = threadIdx.x;
+            if (a.bias)
+                for (int i = tid; i < BN; i += 128) cbias[i] = a.bias[n0 + i];
+            if (EPI == EPI_QKV && tid < 64) { cqn[tid] = a.qn[tid]; ckn[tid] = a.kn[tid]; }
+            if (EPI == EPI_QKV && a.rope) {
+                const int t = t0 + tid % a.bt;
+                if (t < a.rows) { prefetch_l1(a.rope + (size_t) t * 32); prefetch_l1(a.rope + (size_t) t * 32 + 16); }
+            }
+            epi_bar();
+        }
+        const EpiConst ec{a.bias ? cbias : nullptr, cqn, ckn};
         const bool ok = mbar_wait(tfull, 0, abort_flag, a.err, DEV_TIMEOUT_TMEM) && !*abort_flag;
         tc_fence_after();
         const int r = warp * 32 + lane;
+        if (tr && r == 0) tr[3] = global_ns();
         const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
         if (a.splits == 1) {
             auto load_tmem = [&](int c, float * v) { tmem_ld32(trow + c, v); };
 #pragma unroll 1
-            for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, r, u, n0, t0, b0, ok, load_tmem);
+            for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, ec, r, u, n0, t0, b0, ok, load_tmem);
         } else {
             // stage this CTA's partial in its own shared memory as [BN/4][128] float4 (the stage ring
             // is free: every TMA load was consumed and every MMA has completed)
@@ -303,10 +341,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     tc_fence_before();
     __syncthreads();
+    if (tr && threadIdx.x == 0) tr[4] = global_ns();
     if (a.splits > 1) {
         // ---------------------------------------------------------- epilogue, part 2 (cluster)
         cluster_sync_all();
         if (warp < 4 && !*abort_flag) {
+            const EpiConst ec2{a.bias ? cbias : nullptr, cqn, ckn};
             const int S = a.splits;
             const uint32_t q = cluster_rank();
             const uint32_t local = smem_u32(smem);
@@ -333,7 +373,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         v[4 * j] = acc.x; v[4 * j + 1] = acc.y; v[4 * j + 2] = acc.z; v[4 * j + 3] = acc.w;
                     }
                 };
-                epi_unit<EPI>(a, rr, u, n0, t0, b0, true, load_dsmem);
+                epi_unit<EPI>(a, ec2, rr, u, n0, t0, b0, true, load_dsmem);
             }
         }
         cluster_sync_all();   // peers have finished reading this CTA's shared memory
@@ -342,6 +382,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         tc_fence_after();
         tmem_dealloc(tmem, BN);
     }
+    if (tr && threadIdx.x == 0) tr[5] = global_ns();
     if (*abort_flag && threadIdx.x == 0) {
         // let TMA copies that were issued but never consumed land before the CTA's smem is reused
         const uint64_t t1 = global_ns();

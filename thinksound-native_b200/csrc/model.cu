@@ -125,25 +125,26 @@ struct Loader {
         return TSN_OK;
     }
     // kind: 0 linear [N,K_in], 1 conv [OC=N][IC=K_in][taps], 2 qkv linear (rows de-interleaved)
-    int weight(const std::string & name, int kind, int N, int K_in, int taps, uint16_t ** dst) {
+    // placed: *dst already points into a reserved region (no arena take)
+    int weight(const std::string & name, int kind, int N, int K_in, int taps, uint16_t ** dst, bool placed = false) {
         const GgufTensorInfo * t;
         const uint64_t lin[2] = {(uint64_t) K_in, (uint64_t) N};
         const uint64_t cnv[3] = {(uint64_t) taps, (uint64_t) K_in, (uint64_t) N};
         int rc = kind == 1 ? find(name, 3, cnv, &t) : find(name, 2, lin, &t);
         if (rc) return rc;
-        *dst = (uint16_t *) take((size_t) N * K_in * taps * 2);
+        if (!placed) *dst = (uint16_t *) take((size_t) N * K_in * taps * 2);
         if (dry) return TSN_OK;
         if ((rc = src.stage(*t, stA, s))) return rc;
         CKR(launch_prep_weight(*dst, stA, nullptr, (int) t->type, m.bf16, N, K_in, kind == 1 ? taps : 1,
                                kind == 2 ? 1 : 0, (int) m.g.H, s));
         return TSN_OK;
     }
-    int vec(const std::string & name, int n, int mode, float ** dst) {
+    int vec(const std::string & name, int n, int mode, float ** dst, bool placed = false) {
         const GgufTensorInfo * t;
         const uint64_t ne[1] = {(uint64_t) n};
         int rc = find(name, 1, ne, &t);
         if (rc) return rc;
-        *dst = (float *) take((size_t) n * 4);
+        if (!placed) *dst = (float *) take((size_t) n * 4);
         if (dry) return TSN_OK;
         if ((rc = src.stage(*t, stA, s))) return rc;
         CKR(launch_prep_vec(*dst, stA, (int) t->type, n, mode, (int) m.g.H, s));
@@ -171,10 +172,21 @@ struct Loader {
         CKR(launch_prep_weight(L.w, stA, stB, (int) t1->type, m.bf16, 2 * F, K_in, L.taps, 2, 0, s));
         return TSN_OK;
     }
-    int block(const std::string & bp, int chunks, bool post, bool conv, Blk & b) {
+    // latent modulation of block k (or the final layer) into column range mod_off[k] of mod_all
+    int placed_mod(const std::string & p, int k, int N, Lin & L) {
+        const int H = (int) m.g.H;
+        L.N = N; L.K_in = H; L.taps = 1;
+        if (!dry) { L.w = m.mod_all.w + (size_t) m.mod_off[k] * H; L.b = m.mod_all.b + m.mod_off[k]; }
+        int rc = weight(p + ".weight", 0, N, H, 1, &L.w, true);
+        if (!rc) rc = vec(p + ".bias", N, 0, &L.b, true);
+        return rc;
+    }
+    // latent: mod_slot >= 0 places the adaLN weights in mod_all
+    int block(const std::string & bp, int chunks, bool post, bool conv, Blk & b, int mod_slot = -1) {
         const int H = (int) m.g.H, F = (int) m.g.F;
         b.chunks = chunks; b.post = post; b.conv = conv;
-        int rc = linear(bp + ".adaLN_modulation.1", 0, chunks * H, H, 1, true, b.ada);
+        int rc = mod_slot >= 0 ? placed_mod(bp + ".adaLN_modulation.1", mod_slot, chunks * H, b.ada)
+                               : linear(bp + ".adaLN_modulation.1", 0, chunks * H, H, 1, true, b.ada);
         if (!rc) rc = linear(bp + ".attn.qkv", 2, 3 * H, H, 1, true, b.qkv);
         if (!rc) rc = vec(bp + ".attn.q_norm.weight", (int) m.g.hd(), 0, &b.qn);
         if (!rc) rc = vec(bp + ".attn.k_norm.weight", (int) m.g.hd(), 0, &b.kn);
@@ -187,23 +199,30 @@ struct Loader {
     int all() {
         const DitGeom & g = m.g;
         const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim;
+        const int nj = (int) g.n_joint();
+        // contiguous region for every latent modulation matrix and bias
+        const int nmod = nj + (int) g.fused_depth;
+        m.mod_off.resize(nmod + 1);
+        for (int k = 0; k <= nmod; ++k) m.mod_off[k] = k * 6 * H;
+        m.mod_all.N = nmod * 6 * H + 2 * H; m.mod_all.K_in = H; m.mod_all.taps = 1;
+        m.mod_all.w = (uint16_t *) take((size_t) m.mod_all.N * H * 2);
+        m.mod_all.b = (float *) take((size_t) m.mod_all.N * 4);
         int rc = linear("t_embed.mlp.0", 0, H, H, 1, true, m.te0);
         if (!rc) rc = linear("t_embed.mlp.2", 0, H, H, 1, true, m.te2);
         if (!rc) rc = linear("audio_input_proj.0", 1, H, L, 3, true, m.ain0);
         if (!rc) rc = w13("audio_input_proj.2", true, F, H, m.ain13);
         if (!rc) rc = linear("audio_input_proj.2.w2", 1, H, F, 3, false, m.ain2);
-        const int nj = (int) g.n_joint();
         m.jl.resize(nj); m.jc.resize(nj); m.jt.resize(nj); m.fb.resize(g.fused_depth);
         for (int i = 0; !rc && i < nj; ++i) {
             const bool pre_only = i == nj - 1;
             const std::string jb = "joint_blocks." + std::to_string(i);
-            rc = block(jb + ".latent_block", 6, true, true, m.jl[i]);
+            rc = block(jb + ".latent_block", 6, true, true, m.jl[i], i);
             if (!rc) rc = block(jb + ".clip_block", pre_only ? 2 : 6, !pre_only, true, m.jc[i]);
             if (!rc) rc = block(jb + ".text_block", pre_only ? 2 : 6, !pre_only, false, m.jt[i]);
         }
         for (uint32_t i = 0; !rc && i < g.fused_depth; ++i)
-            rc = block("fused_blocks." + std::to_string(i), 6, true, true, m.fb[i]);
-        if (!rc) rc = linear("final_layer.adaLN_modulation.1", 0, 2 * H, H, 1, true, m.fada);
+            rc = block("fused_blocks." + std::to_string(i), 6, true, true, m.fb[i], nj + (int) i);
+        if (!rc) rc = placed_mod("final_layer.adaLN_modulation.1", nmod, 2 * H, m.fada);
         if (!rc) rc = linear("final_layer.conv", 1, L, H, 7, true, m.fconv);
         return rc;
     }
@@ -324,8 +343,7 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
     ALLOC(lat, B * T * H * 4);
     ALLOC(clip_s, B * C * H * 4);
     ALLOC(text_s, B * TS * H * 4);
-    ALLOC(modl, B * T * 6 * H * 4);
-    ALLOC(modf, B * T * 2 * H * 4);
+    ALLOC(modl, B * T * (size_t) mod_all.N * 4);
     ALLOC(modc, NJ * B * 6 * H * 4);
     ALLOC(modt, NJ * B * 6 * H * 4);
     ALLOC(flow, B * T * L * 4);
@@ -461,6 +479,12 @@ struct Plan {
         Op op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name, d};
         op.gemm_id = m.gemm_seq++;
         op.shape = last_shape;
+        op.traced = [g](cudaStream_t s, unsigned long long * tr) {
+            GemmLaunch t = g;
+            t.args.trace = tr;
+            return launch_gemm(t, s);
+        };
+        op.ctas = (int) (g.grid.x * g.grid.y * g.grid.z);
         ops.push_back(op);
     }
     static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
@@ -530,6 +554,23 @@ struct Plan {
         if ((rc = out_f16("ffn_w13", EPI_SWIGLU, xn, H, rows, b.w13, pad, h, F))) return rc;
         return gate("ffn_w2", h, F, rows, b.w2, pad, x, mod, per_row, mod_ld, mod_bs, 5, true);
     }
+    // strided source: `rows` rows of `width` bytes, `pitch` bytes apart, gathered densely
+    void tap2d(const std::string & name, const void * src, size_t width, size_t pitch, size_t rows,
+               std::function<void(const std::vector<uint8_t> &, int, std::vector<float> &)> cvt) {
+        const size_t bytes = width * rows;
+        TapBuf & tb = m.taps[name];
+        if (!tb.dev || tb.bytes != bytes) {
+            if (tb.dev) cudaFree(tb.dev);
+            cudaMalloc(&tb.dev, bytes);
+            tb.bytes = bytes;
+        }
+        tb.convert = std::move(cvt);
+        void * dst = tb.dev;
+        ops.push_back(Op{[dst, src, width, pitch, rows](cudaStream_t s) {
+                             return cudaMemcpy2DAsync(dst, width, src, pitch, width, rows, cudaMemcpyDeviceToDevice, s);
+                         },
+                         2, 0.0, "tap:" + name});
+    }
     void tap(const std::string & name, const void * src, size_t bytes,
              std::function<void(const std::vector<uint8_t> &, int, std::vector<float> &)> cvt) {
         TapBuf & tb = m.taps[name];
@@ -571,7 +612,8 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     Plan p{*this, ops};
     const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim, NJ = (int) g.n_joint();
     const bool tp = mode == 2;
-    const long long lat_mod_bs = (long long) T * 6 * H;
+    const long long NA = mod_all.N;                 // latent modulation row stride
+    const long long lat_mod_bs = (long long) T * NA;
     int rc;
     // t-embedding MLP and conditioning                           src/dit_fwd.cpp:111-140
     GemvJob * jb = jobs;
@@ -592,6 +634,9 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         p.tap("global_c", tap_gc, (size_t) B * sH * 4, cvt_f32_arm(sH));
         p.tap("extended_c", tap_extc, (size_t) B * sTH * 4, cvt_f32_arm(sTH));
     }
+    // every latent adaLN modulation of the step in one GEMM (they depend only on extc_silu):
+    // joint blocks, fused blocks and the final layer      src/dit_fwd.cpp:186-189, 271-274, 288-291
+    if ((rc = p.out_f32("latent_adaln_all", extc16, H, T, mod_all, 0, modl, (int) NA))) return rc;
     // audio_input_proj: conv k3 + silu, convmlp                   src/dit_fwd.cpp:143-149
     if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H, (long long) B * T * H))) return rc;
     if ((rc = p.out_f16("audio_in.w13", EPI_SWIGLU, xn_l, H, T, ain13, 1, h_l, F))) return rc;
@@ -601,8 +646,8 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     for (int i = 0; i < NJ; ++i) {
         const bool pre_only = i == NJ - 1;
         float * mc = modc + (size_t) i * B * 6 * H, * mt = modt + (size_t) i * B * 6 * H;
-        if ((rc = p.out_f32("latent_adaln", extc16, H, T, jl[i].ada, 0, modl, 6 * H))) return rc;
-        p.adaln("adaln_attn", lat, T, modl, 1, 6 * H, lat_mod_bs, 0, xn_l);
+        const float * ml = modl + mod_off[i];
+        p.adaln("adaln_attn", lat, T, ml, 1, NA, lat_mod_bs, 0, xn_l);
         if ((rc = p.qkv("qkv_lat", xn_l, T, jl[i], 0, rope_l))) return rc;
         p.adaln("adaln_attn", clip_s, C, mc, 0, 0, 6 * H, 0, xn_c);
         if ((rc = p.qkv("qkv_clip", xn_c, C, jc[i], T, rope_c))) return rc;
@@ -626,7 +671,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
             }
         }
         p.attention(S, T, C, TS);
-        if ((rc = p.post(jl[i], lat, att_l, xn_l, h_l, T, modl, 1, 6 * H, lat_mod_bs))) return rc;
+        if ((rc = p.post(jl[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs))) return rc;
         if (!pre_only) {
             if ((rc = p.post(jc[i], clip_s, att_c, xn_c, h_c, C, mc, 0, 0, 6 * H))) return rc;
             if ((rc = p.post(jt[i], text_s, att_t, xn_t, h_t, TS, mt, 0, 0, 6 * H))) return rc;
@@ -644,19 +689,19 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     if (tp) p.tap("after_joint", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
     // fused blocks                                                src/dit_fwd.cpp:268-279
     for (size_t i = 0; i < fb.size(); ++i) {
-        if ((rc = p.out_f32("latent_adaln", extc16, H, T, fb[i].ada, 0, modl, 6 * H))) return rc;
-        p.adaln("adaln_attn", lat, T, modl, 1, 6 * H, lat_mod_bs, 0, xn_l);
+        const float * ml = modl + mod_off[NJ + i];
+        p.adaln("adaln_attn", lat, T, ml, 1, NA, lat_mod_bs, 0, xn_l);
         if ((rc = p.qkv("qkv_lat", xn_l, T, fb[i], 0, rope_l))) return rc;
         p.attention(T, T, 0, 0);
-        if ((rc = p.post(fb[i], lat, att_l, xn_l, h_l, T, modl, 1, 6 * H, lat_mod_bs))) return rc;
+        if ((rc = p.post(fb[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs))) return rc;
     }
     if (tp) p.tap("after_fused", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
     // final layer                                                 src/dit_fwd.cpp:287-303
-    if ((rc = p.out_f32("final_adaln", extc16, H, T, fada, 0, modf, 2 * H))) return rc;
-    p.adaln("adaln_final", lat, T, modf, 1, 2 * H, (long long) T * 2 * H, 0, xn_l);
+    const float * mf = modl + mod_off.back();
+    p.adaln("adaln_final", lat, T, mf, 1, NA, lat_mod_bs, 0, xn_l);
     if (tp) {
         p.tap("final_fx", xn_l, (size_t) B * T * H * 2, cvt_f16_arm((size_t) T * H));
-        p.tap("final_mod", modf, (size_t) B * T * 2 * H * 4, cvt_f32_arm((size_t) T * 2 * H));
+        p.tap2d("final_mod", mf, (size_t) 2 * H * 4, (size_t) NA * 4, (size_t) B * T, cvt_f32_arm((size_t) T * 2 * H));
     }
     if ((rc = p.out_f32("final_conv", xn_l, H, T, fconv, 3, flow, L))) return rc;
     if (tp) p.tap("flow", flow, (size_t) B * T * L * 4, cvt_f32_arm((size_t) T * L));

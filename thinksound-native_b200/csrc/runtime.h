@@ -57,6 +57,8 @@ struct Op {
     std::string desc;      // launch configuration, for profiles
     int gemm_id = -1;      // GEMM sequence number within the forward (kind 0)
     std::string shape;     // GEMM shape key: ops with equal keys have the same candidate configs
+    std::function<cudaError_t(cudaStream_t, unsigned long long *)> traced;   // GEMMs: launch with phase trace
+    int ctas = 0;
 };
 
 struct TapBuf {
@@ -70,6 +72,10 @@ struct Model {
     DitGeom g;
     int bf16 = 0;
     Lin te0, te2, ain0, ain13, ain2, fada, fconv;
+    // every latent adaLN modulation weight (joint blocks, fused blocks, final layer) in one
+    // contiguous [N_all][H] matrix, so one GEMM per step computes all of them
+    Lin mod_all;
+    std::vector<int> mod_off;   // column offset of each block's 6H chunk (joint then fused), final last
     std::vector<Blk> jl, jc, jt, fb;
     void * arena = nullptr;
     size_t arena_bytes = 0, arena_used = 0;
@@ -80,7 +86,7 @@ struct Model {
     std::vector<void *> act;
     float * x = nullptr, * clip_pp = nullptr, * sync_gather = nullptr, * text_pp = nullptr, * gcmlp = nullptr;
     float * te_h = nullptr, * te = nullptr, * gc_silu = nullptr, * lat = nullptr, * clip_s = nullptr, * text_s = nullptr;
-    float * modl = nullptr, * modf = nullptr, * modc = nullptr, * modt = nullptr, * flow = nullptr;
+    float * modl = nullptr, * modc = nullptr, * modt = nullptr, * flow = nullptr;   // modl: [B][T][N_all]
     __half * x16 = nullptr, * extc16 = nullptr, * xn_l = nullptr, * xn_c = nullptr, * xn_t = nullptr;
     __half * att_l = nullptr, * att_c = nullptr, * att_t = nullptr, * h_l = nullptr, * h_c = nullptr, * h_t = nullptr;
     __half * q = nullptr, * k = nullptr, * v = nullptr;

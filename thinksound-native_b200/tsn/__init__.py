@@ -96,6 +96,7 @@ _SIGS = [
     ("tsn_dit_kernels_per_step", C.c_int, [C.c_void_p]),
     ("tsn_dit_profile_step", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
     ("tsn_dit_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    ("tsn_dit_trace_op", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
     ("tsn_dit_autotune", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_gguf_write_synthetic", C.c_int, [C.c_char_p, C.POINTER(Geom), C.c_uint64, C.c_int]),
 ]
@@ -286,6 +287,14 @@ class Dit:
         return {"gemm_ms": out[0], "attn_ms": out[1], "other_ms": out[2], "gemm_flops": out[3],
                 "gemm_launches": int(out[4])}
 
+
+    def trace_op(self, op: int):
+        """Per-CTA phase timestamps (ns) of GEMM launch `op`: array [ctas, 6]."""
+        import numpy as np
+        n = C.c_int()
+        out = np.zeros((4096, 6), np.uint64)
+        check(lib().tsn_dit_trace_op(self.h, op, out.ctypes.data, 4096, C.byref(n)))
+        return out[:min(n.value, 4096)]
 
     def autotune(self) -> str:
         buf = C.create_string_buffer(1 << 20)
