@@ -55,8 +55,17 @@ constexpr int stages_for(int bn, bool split) {
 }
 int gemm_stages(int bn, bool split) { return stages_for(bn, split); }
 
+// Dynamic shared memory of one configuration: the kernel's own layout constant (single source).
 size_t gemm_smem_bytes(int bn, bool split) {
-    return (size_t) stages_for(bn, split) * ((split ? 2 : 1) * 128 * 128 + bn * 128) + 256 + 1024;
+    switch (bn * 2 + (split ? 1 : 0)) {
+        case 64 * 2: return GemmSmem<64, stages_for(64, false), false>::TOTAL;
+        case 64 * 2 + 1: return GemmSmem<64, stages_for(64, true), true>::TOTAL;
+        case 128 * 2: return GemmSmem<128, stages_for(128, false), false>::TOTAL;
+        case 128 * 2 + 1: return GemmSmem<128, stages_for(128, true), true>::TOTAL;
+        case 256 * 2: return GemmSmem<256, stages_for(256, false), false>::TOTAL;
+        case 256 * 2 + 1: return GemmSmem<256, stages_for(256, true), true>::TOTAL;
+    }
+    return 0;
 }
 
 namespace {
