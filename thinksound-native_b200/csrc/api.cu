@@ -290,7 +290,7 @@ int tsn_dit_forward_taps(tsn_dit * m, float t, float * flow_out) {
     std::vector<Op> ops;
     TRY(M.build_ops(ops, 2, 0.0f));
     TRY(M.set_time(t, 0.0f));
-    TRY(M.run_ops(ops));
+    TRY(M.run_ops(ops, true));
     if (flow_out)
         CKR(cudaMemcpyAsync(flow_out, M.flow, (size_t) M.B * M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
     return M.dev->sync();
@@ -393,7 +393,9 @@ int tsn_dit_step_host(tsn_dit * m, const float * x_in, float * x_out, float t, f
 
 int tsn_dit_kernels_per_step(tsn_dit * m) {
     if (!m || !m->m.prepared) return 0;
-    return (int) m->m.ops_fwd.size() + 2;
+    int n = 0;
+    for (const Op & o : m->m.ops_fwd) n += o.evkind == 0;
+    return n + 2;
 }
 
 int tsn_dit_profile_step(tsn_dit * m, double * out5) {

@@ -297,6 +297,10 @@ int load_model(Model & m, const std::string * path, const DitGeom * sg, uint64_t
 
 // ------------------------------------------------------------------------------ activations
 void Model::release_activations() {
+    for (int i = 0; i < 2; ++i)
+        if (side[i]) { cudaStreamSynchronize(side[i]); cudaStreamDestroy(side[i]); side[i] = nullptr; }
+    for (cudaEvent_t e : events) cudaEventDestroy(e);
+    events.clear();
     if (gx_fwd) { cudaGraphExecDestroy(gx_fwd); gx_fwd = nullptr; }
     if (gx_step) { cudaGraphExecDestroy(gx_step); gx_step = nullptr; }
     for (void * p : act) cudaFree(p);
@@ -416,6 +420,21 @@ struct Plan {
     Model & m;
     std::vector<Op> & ops;
     std::string last_shape;
+    int cur = 0;              // stream the next ops go to
+    void add(Op o) { o.stream = cur; ops.push_back(std::move(o)); }
+    int record() {
+        Op o{[](cudaStream_t) { return cudaSuccess; }, 2, 0.0, "record"};
+        o.evkind = 1;
+        o.ev = m.n_events++;
+        add(o);
+        return o.ev;
+    }
+    void wait(int ev) {
+        Op o{[](cudaStream_t) { return cudaSuccess; }, 2, 0.0, "wait"};
+        o.evkind = 2;
+        o.ev = ev;
+        add(o);
+    }
 
     // Pick the tile width and split-K (cluster) factor with a small cost model: per-K-block time
     // of one CTA, waves over the CTAs that fit at once (clusters need their S SMs in one GPC), and
@@ -485,7 +504,7 @@ struct Plan {
             return launch_gemm(t, s);
         };
         op.ctas = (int) (g.grid.x * g.grid.y * g.grid.z);
-        ops.push_back(op);
+        add(op);
     }
     static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
 
@@ -534,7 +553,7 @@ struct Plan {
                long long mod_bs, int base, __half * out) {
         AdaLnArgs a{x, (long long) rows * m.g.H, mod, mod_bs, mod_ld, per_row, base, out, (long long) rows * m.g.H,
                     m.B, rows, (int) m.g.H, 1e-5f, (long long) m.B * rows * m.g.H};
-        ops.push_back(Op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name});
+        add(Op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name});
     }
     void attention(int S, int n0, int n1, int n2) {
         const long long H = m.g.H;
@@ -542,7 +561,7 @@ struct Plan {
                    m.att_l, m.att_c, m.att_t, n0, n1, n2, (int) m.g.H,
                    (long long) m.B * m.g.NH * m.S_pad * 64, m.B * m.T * H, m.B * m.C * H, m.B * m.TS * H};
         const double flops = 4.0 * m.B * (double) S * S * m.g.H;
-        ops.push_back(Op{[a](cudaStream_t s) { return launch_attention(a, s); }, 1, flops, "attention"});
+        add(Op{[a](cudaStream_t s) { return launch_attention(a, s); }, 1, flops, "attention"});
     }
     // post_attn (src/dit_fwd.cpp:51-81) for one stream, all arms
     int post(const Blk & b, float * x, const __half * att, __half * xn, __half * h, int rows, const float * mod,
@@ -566,7 +585,7 @@ struct Plan {
         }
         tb.convert = std::move(cvt);
         void * dst = tb.dev;
-        ops.push_back(Op{[dst, src, width, pitch, rows](cudaStream_t s) {
+        add(Op{[dst, src, width, pitch, rows](cudaStream_t s) {
                              return cudaMemcpy2DAsync(dst, width, src, pitch, width, rows, cudaMemcpyDeviceToDevice, s);
                          },
                          2, 0.0, "tap:" + name});
@@ -581,7 +600,7 @@ struct Plan {
         }
         tb.convert = std::move(cvt);
         void * dst = tb.dev;
-        ops.push_back(Op{[dst, src, bytes](cudaStream_t s) { return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s); },
+        add(Op{[dst, src, bytes](cudaStream_t s) { return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, s); },
                          2, 0.0, "tap:" + name});
     }
 };
@@ -609,6 +628,7 @@ auto cvt_f16_arm(size_t per_arm) {
 int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     ops.clear();
     gemm_seq = 0;
+    n_events = 0;
     Plan p{*this, ops};
     const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim, NJ = (int) g.n_joint();
     const bool tp = mode == 2;
@@ -643,16 +663,31 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     if ((rc = p.out_f32("audio_in.w2", h_l, F, T, ain2, 1, lat, H, true))) return rc;
     if (tp) p.tap("x_in", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
     // joint blocks                                                src/dit_fwd.cpp:180-257
+    // The latent, clip and text streams of a joint block meet only at attention: the clip and text
+    // chains run on their own CUDA streams (1, 2) and join the latent stream (0) through events.
+    {
+        const int e0 = p.record();            // clip_s/text_s restarted, clip/text modulations ready
+        p.cur = 1; p.wait(e0);
+        p.cur = 2; p.wait(e0);
+        p.cur = 0;
+    }
     for (int i = 0; i < NJ; ++i) {
         const bool pre_only = i == NJ - 1;
         float * mc = modc + (size_t) i * B * 6 * H, * mt = modt + (size_t) i * B * 6 * H;
         const float * ml = modl + mod_off[i];
         p.adaln("adaln_attn", lat, T, ml, 1, NA, lat_mod_bs, 0, xn_l);
         if ((rc = p.qkv("qkv_lat", xn_l, T, jl[i], 0, rope_l))) return rc;
+        p.cur = 1;
         p.adaln("adaln_attn", clip_s, C, mc, 0, 0, 6 * H, 0, xn_c);
         if ((rc = p.qkv("qkv_clip", xn_c, C, jc[i], T, rope_c))) return rc;
+        const int ec = p.record();
+        p.cur = 2;
         p.adaln("adaln_attn", text_s, TS, mt, 0, 0, 6 * H, 0, xn_t);
         if ((rc = p.qkv("qkv_text", xn_t, TS, jt[i], T + C, nullptr))) return rc;
+        const int et = p.record();
+        p.cur = 0;
+        p.wait(ec);
+        p.wait(et);
         if (tp && i == 0) {
             p.tap("text_xn", xn_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
             const int NH = (int) g.NH, Sp = S_pad, S_ = S;
@@ -671,10 +706,16 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
             }
         }
         p.attention(S, T, C, TS);
+        const int ea = p.record();
         if ((rc = p.post(jl[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs))) return rc;
         if (!pre_only) {
+            p.cur = 1;
+            p.wait(ea);
             if ((rc = p.post(jc[i], clip_s, att_c, xn_c, h_c, C, mc, 0, 0, 6 * H))) return rc;
+            p.cur = 2;
+            p.wait(ea);
             if ((rc = p.post(jt[i], text_s, att_t, xn_t, h_t, TS, mt, 0, 0, 6 * H))) return rc;
+            p.cur = 0;
         }
         if (tp && i == 0) {
             // a0_out is the concatenation [lat | clip | text] of these three (tsn_dit_tap joins them)
@@ -685,6 +726,15 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
             p.tap("jb0_clip", clip_s, (size_t) B * C * H * 4, cvt_f32_arm((size_t) C * H));
             p.tap("jb0_text", text_s, (size_t) B * TS * H * 4, cvt_f32_arm((size_t) TS * H));
         }
+    }
+    {   // join the clip and text streams back into the latent stream
+        p.cur = 1;
+        const int ecl = p.record();
+        p.cur = 2;
+        const int etl = p.record();
+        p.cur = 0;
+        p.wait(ecl);
+        p.wait(etl);
     }
     if (tp) p.tap("after_joint", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
     // fused blocks                                                src/dit_fwd.cpp:268-279
@@ -717,9 +767,29 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     return TSN_OK;
 }
 
-int Model::run_ops(const std::vector<Op> & ops) {
+int Model::ensure_streams() {
+    for (int i = 0; i < 2; ++i)
+        if (!side[i]) CKR(cudaStreamCreateWithFlags(&side[i], cudaStreamNonBlocking));
+    while ((int) events.size() < n_events) {
+        cudaEvent_t e;
+        CKR(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        events.push_back(e);
+    }
+    return TSN_OK;
+}
+
+int Model::run_ops(const std::vector<Op> & ops, bool serial) {
+    if (!serial) {
+        int rc = ensure_streams();
+        if (rc) return rc;
+    }
     for (const Op & o : ops) {
-        cudaError_t e = o.fn(dev->stream);
+        if (o.evkind && serial) continue;
+        cudaStream_t st = serial || o.stream == 0 ? dev->stream : side[o.stream - 1];
+        cudaError_t e;
+        if (o.evkind == 1) e = cudaEventRecord(events[o.ev], st);
+        else if (o.evkind == 2) e = cudaStreamWaitEvent(st, events[o.ev], 0);
+        else e = o.fn(st);
         if (e != cudaSuccess) return fail(TSN_ERR_CUDA, "launch " + o.name + ": " + cudaGetErrorString(e));
     }
     return TSN_OK;
@@ -789,6 +859,8 @@ int Model::autotune(std::string & report) {
 int Model::capture(const std::vector<Op> & ops, cudaGraphExec_t * out) {
     if (*out) { cudaGraphExecDestroy(*out); *out = nullptr; }
     cudaGraph_t graph = nullptr;
+    int rs = ensure_streams();
+    if (rs) return rs;
     CKR(cudaStreamBeginCapture(dev->stream, cudaStreamCaptureModeThreadLocal));
     int rc = run_ops(ops);
     cudaError_t e = cudaStreamEndCapture(dev->stream, &graph);

@@ -59,6 +59,9 @@ struct Op {
     std::string shape;     // GEMM shape key: ops with equal keys have the same candidate configs
     std::function<cudaError_t(cudaStream_t, unsigned long long *)> traced;   // GEMMs: launch with phase trace
     int ctas = 0;
+    int stream = 0;        // 0 latent (the device stream), 1 clip, 2 text
+    int evkind = 0;        // 0 kernel/copy, 1 record event `ev` on `stream`, 2 make `stream` wait on `ev`
+    int ev = -1;
 };
 
 struct TapBuf {
@@ -111,7 +114,13 @@ struct Model {
     void * arena_take(size_t bytes);
     int prepare(int T, int C, int TS, int B);
     int build_ops(std::vector<Op> & ops, int mode, float cfg);   // mode 0 forward, 1 step, 2 taps
-    int run_ops(const std::vector<Op> & ops);
+    // serial: every op on the device stream in list order (taps, profiles); otherwise the clip and
+    // text streams run on their own CUDA streams, joined by events
+    int run_ops(const std::vector<Op> & ops, bool serial = false);
+    int ensure_streams();
+    cudaStream_t side[2] = {nullptr, nullptr};
+    std::vector<cudaEvent_t> events;
+    int n_events = 0;
     int capture(const std::vector<Op> & ops, cudaGraphExec_t * out);
     int autotune(std::string & report);
     int set_time(float t, float dt);
