@@ -51,7 +51,7 @@ bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint
 
 // Pipeline depth: as many stages as fit in ~192 KB of shared memory.
 constexpr int stages_for(int bn, bool split) {
-    return split ? (bn == 256 ? 3 : bn == 128 ? 4 : 5) : (bn == 256 ? 4 : bn == 128 ? 6 : 8);
+    return split ? (bn >= 192 ? 3 : bn == 128 ? 4 : 5) : (bn == 256 ? 4 : bn == 192 ? 5 : bn == 128 ? 6 : 8);
 }
 int gemm_stages(int bn, bool split) { return stages_for(bn, split); }
 
@@ -62,6 +62,8 @@ size_t gemm_smem_bytes(int bn, bool split) {
         case 64 * 2 + 1: return GemmSmem<64, stages_for(64, true), true>::TOTAL;
         case 128 * 2: return GemmSmem<128, stages_for(128, false), false>::TOTAL;
         case 128 * 2 + 1: return GemmSmem<128, stages_for(128, true), true>::TOTAL;
+        case 192 * 2: return GemmSmem<192, stages_for(192, false), false>::TOTAL;
+        case 192 * 2 + 1: return GemmSmem<192, stages_for(192, true), true>::TOTAL;
         case 256 * 2: return GemmSmem<256, stages_for(256, false), false>::TOTAL;
         case 256 * 2 + 1: return GemmSmem<256, stages_for(256, true), true>::TOTAL;
     }
@@ -84,7 +86,7 @@ KernelFn pick_epi(int epi) {
         case EPI_F32: return pick<BN, EPI_F32, SPLIT>();
         case EPI_F16: return pick<BN, EPI_F16, SPLIT>();
         case EPI_F16_SILU: return pick<BN, EPI_F16_SILU, SPLIT>();
-        case EPI_SWIGLU: if constexpr (BN % 128 == 0) return pick<BN, EPI_SWIGLU, SPLIT>(); else return nullptr;
+        case EPI_SWIGLU: return pick<BN, EPI_SWIGLU, SPLIT>();
         case EPI_GATE: return pick<BN, EPI_GATE, SPLIT>();
         case EPI_QKV: return pick<BN, EPI_QKV, SPLIT>();
     }
@@ -95,6 +97,7 @@ KernelFn kernel_for(int bn, int epi, bool split) {
     switch (bn) {
         case 64: return split ? pick_epi<64, true>(epi) : pick_epi<64, false>(epi);
         case 128: return split ? pick_epi<128, true>(epi) : pick_epi<128, false>(epi);
+        case 192: return split ? pick_epi<192, true>(epi) : pick_epi<192, false>(epi);
         case 256: return split ? pick_epi<256, true>(epi) : pick_epi<256, false>(epi);
     }
     return nullptr;
@@ -104,7 +107,7 @@ KernelFn kernel_for(int bn, int epi, bool split) {
 // Set the dynamic shared-memory limit of every instantiation once, outside any stream capture.
 cudaError_t configure_gemm_kernels() {
     for (int split = 0; split < 2; ++split)
-        for (int bn : {64, 128, 256})
+        for (int bn : {64, 128, 192, 256})
             for (int epi = 0; epi < 6; ++epi) {
                 KernelFn fn = kernel_for(bn, epi, split != 0);
                 if (!fn) continue;

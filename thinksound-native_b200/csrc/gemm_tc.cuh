@@ -38,7 +38,7 @@ enum GemmEpi : int {
     EPI_F32 = 0,       // out f32 = acc (+bias)
     EPI_F16 = 1,       // out f16 = acc (+bias)
     EPI_F16_SILU = 2,  // out f16 = silu(acc + bias)
-    EPI_SWIGLU = 3,    // columns in groups of 128 = [64 w1 | 64 w3] -> out f16 = silu(a)*b
+    EPI_SWIGLU = 3,    // columns in groups of 64 = [32 w1 | 32 w3] -> out f16 = silu(a)*b
     EPI_GATE = 4,      // res f32 += (acc + bias) * mod[row][gate_off + n]
     EPI_QKV = 5,       // bias, per-head RMSNorm(q,k), RoPE(q,k), f16 head-major q/k/v
 };
@@ -105,8 +105,11 @@ __device__ __forceinline__ void store8_split(__half * o, long long lo, const flo
 }
 
 // Columns one epilogue call handles: one 32-column chunk; a whole 64-column head for the qkv
-// epilogue (RMSNorm + RoPE need it); a [64 w1 | 64 w3] group for SwiGLU.
-template <int EPI> struct EpiUnit { static constexpr int U = EPI == EPI_QKV ? 64 : EPI == EPI_SWIGLU ? 128 : 32; };
+// epilogue (RMSNorm + RoPE need it); a [32 w1 | 32 w3] group for SwiGLU.
+template <int EPI> struct EpiUnit { static constexpr int U = EPI == EPI_QKV ? 64 : EPI == EPI_SWIGLU ? 64 : 32; };
+
+// TMEM columns for a BN-wide f32 accumulator (allocations are powers of two, at least 32)
+template <int BN> struct TmemCols { static constexpr int N = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256; };
 
 // Epilogue for tile row r, columns [u*U, (u+1)*U) of the tile. load32(c, v) returns the 32
 // accumulated values of columns [c, c+32) of row r (from TMEM, or summed over the cluster's
@@ -117,14 +120,15 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
                                          Load && load32) {
     constexpr int U = EpiUnit<EPI>::U;
     const int b = b0 + r / a.bt, t = t0 + r % a.bt;
-    const bool valid = ok && t < a.rows && b < a.B;
     const int c0 = u * U;
+    // a tile may overhang N (tile widths that do not divide N): whole units beyond N are skipped
+    const bool valid = ok && t < a.rows && b < a.B && n0 + c0 < a.N;
     if constexpr (EPI == EPI_SWIGLU) {
-#pragma unroll 1
-        for (int j = 0; j < 64; j += 32) {
+        {
+            const int j = 0;
             float va[32], vb[32];
-            load32(c0 + j, va);
-            load32(c0 + 64 + j, vb);
+            load32(c0, va);
+            load32(c0 + 32, vb);
             if (valid) {
                 const long long nout = (long long) (n0 + c0) / 2 + j;
                 __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + nout;
@@ -247,7 +251,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (SPLIT) tma_prefetch(&tmA2);
         tma_prefetch(&tmB);
     }
-    if (warp == 5) tmem_alloc(tslot, BN);
+    if (warp == 5) tmem_alloc(tslot, TmemCols<BN>::N);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -308,7 +312,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         {   // stage the tile's constants while the mainloop runs; warm L1 with this row's RoPE entries
             const int tid = threadIdx.x;
             if (a.bias)
-                for (int i = tid; i < BN; i += 128) cbias[i] = a.bias[n0 + i];
+                for (int i = tid; i < BN && n0 + i < a.N; i += 128) cbias[i] = a.bias[n0 + i];
             if (EPI == EPI_QKV && tid < 64) { cqn[tid] = a.qn[tid]; ckn[tid] = a.kn[tid]; }
             if (EPI == EPI_QKV && a.rope) {
                 const int t = t0 + tid % a.bt;
@@ -380,7 +384,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     if (warp == 5) {
         tc_fence_after();
-        tmem_dealloc(tmem, BN);
+        tmem_dealloc(tmem, TmemCols<BN>::N);
     }
     if (tr && threadIdx.x == 0) tr[5] = global_ns();
     if (*abort_flag && threadIdx.x == 0) {

@@ -156,7 +156,7 @@ struct Loader {
         if (!rc && bias) rc = vec(p + ".bias", N, kind == 2 ? 1 : 0, &L.b);
         return rc;
     }
-    // w1 and w3 interleaved in [64 w1 rows | 64 w3 rows] groups -> one [2F][taps*K_in] matrix
+    // w1 and w3 interleaved in [32 w1 rows | 32 w3 rows] groups -> one [2F][taps*K_in] matrix
     int w13(const std::string & p, bool conv, int F, int K_in, Lin & L) {
         L.N = 2 * F; L.K_in = K_in; L.taps = conv ? 3 : 1;
         const GgufTensorInfo * t1, * t3;
@@ -449,12 +449,13 @@ struct Plan {
         if (K_in % 64 || kb < 1) return fail(TSN_ERR_ARG, std::string(name) + ": K not a multiple of 64");
         double best = 1e30;
         int bn_best = 0, s_best = 1;
-        for (int bn : {256, 128, 64}) {
-            if (N % bn) continue;
-            if (epi == EPI_SWIGLU && bn % 128) continue;
-            const double kcost = split ? (bn == 256 ? 0.74 : bn == 128 ? 0.40 : 0.30)
-                                       : (bn == 256 ? 0.37 : bn == 128 ? 0.24 : 0.18);
-            const int tiles = mtt * mtb * (N / bn);
+        // tile widths that do not divide N leave the last column tile partly empty (its TMA rows
+        // beyond N read zeros and its epilogue skips those columns)
+        for (int bn : {256, 192, 128, 64}) {
+            if (N % bn && (bn != 192 || N < 192)) continue;
+            const double kcost = split ? (bn == 256 ? 0.74 : bn == 192 ? 0.57 : bn == 128 ? 0.40 : 0.30)
+                                       : (bn == 256 ? 0.37 : bn == 192 ? 0.30 : bn == 128 ? 0.24 : 0.18);
+            const int tiles = mtt * mtb * ((N + bn - 1) / bn);
             for (int s = 1; s <= 8 && s <= kb; ++s) {
                 const int kbps = (kb + s - 1) / s;
                 if ((kb + kbps - 1) / kbps != s) continue;
@@ -477,7 +478,7 @@ struct Plan {
         g.split = split;
         g.smem = gemm_smem_bytes(bn_best, split);
         g.ab_bf16 = m.bf16;
-        g.grid = dim3(N / bn_best, mtt * mtb, s_best);
+        g.grid = dim3((N + bn_best - 1) / bn_best, mtt * mtb, s_best);
         const __half * Alo = (const __half *) A + (size_t) B * rows * K_in;
         if (!make_act_map(&g.ta, A, K_in, rows, B, bt, bb, m.bf16) ||
             (split && !make_act_map(&g.ta2, Alo, K_in, rows, B, bt, bb, m.bf16)) ||
@@ -817,7 +818,7 @@ int Model::autotune(std::string & report) {
         double best = 1e30;
         std::pair<int, int> bc{0, 0};
         std::string tried;
-        for (int bn : {256, 128, 64})
+        for (int bn : {256, 192, 128, 64})
             for (int sp = 1; sp <= 8; ++sp) {
                 gemm_force.clear();
                 gemm_force[gid] = {bn, sp};
