@@ -170,8 +170,16 @@ int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap);
 
 /* Run the forward up to GEMM launch `op` (index in tsn_dit_profile_ops) and that GEMM once more
  * with per-CTA phase timestamps (globaltimer ns): entry, setup done, first stage landed,
- * accumulator complete, epilogue done, exit — 6 per CTA into out (max_ctas CTAs). */
+ * accumulator complete, epilogue done, exit, first cluster barrier passed, cluster reduction
+ * done (the last two 0 without split-K) — 8 per CTA into out (max_ctas CTAs). */
 int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_ctas, int * n_ctas);
+
+/* Run one forward eagerly on the graph's streams with every GEMM, adaLN and attention launch
+ * stamping its CTAs (globaltimer ns). Per stamped launch, 5 doubles into out (max_rows rows): op
+ * index (as in tsn_dit_profile_ops), earliest CTA entry, earliest start of work (GEMM: first operand
+ * stage landed; others: upstream wait passed), latest exit, median exit — in ns from the earliest
+ * entry. n_rows receives the number of stamped launches. */
+int tsn_dit_timeline(tsn_dit * m, double * out, size_t max_rows, int * n_rows);
 
 /* Time every valid tile configuration (tile width, cluster split-K factor) of each distinct GEMM
  * shape of the prepared forward on this device and keep the fastest (the default is a static cost

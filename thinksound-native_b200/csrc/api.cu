@@ -461,7 +461,8 @@ int tsn_dit_autotune(tsn_dit * m, char * report, size_t cap) {
 
 int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_ctas, int * n_ctas) {
     M_BEGIN NEED_PREPARED
-    if (op < 0 || op >= (int) M.ops_fwd.size() || !M.ops_fwd[op].traced) return fail(TSN_ERR_ARG, "op is not a GEMM");
+    if (op < 0 || op >= (int) M.ops_fwd.size() || M.ops_fwd[op].kind != 0 || !M.ops_fwd[op].traced)
+        return fail(TSN_ERR_ARG, "op is not a GEMM");
     const Op & o = M.ops_fwd[op];
     const size_t n = (size_t) o.ctas * TRACE_SLOTS;
     unsigned long long * d = nullptr;
@@ -474,6 +475,16 @@ int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_c
     cudaFree(d);
     if (n_ctas) *n_ctas = o.ctas;
     return rc;
+}
+
+int tsn_dit_timeline(tsn_dit * m, double * out, size_t max_rows, int * n_rows) {
+    M_BEGIN NEED_PREPARED
+    std::vector<double> rows;
+    TRY(M.timeline(rows));
+    const size_t n = rows.size() / 5;
+    if (out) std::memcpy(out, rows.data(), std::min(n, max_rows) * 5 * sizeof(double));
+    if (n_rows) *n_rows = (int) n;
+    return TSN_OK;
 }
 
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep) {

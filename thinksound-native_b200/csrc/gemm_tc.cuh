@@ -62,8 +62,9 @@ struct GemmArgs {
 };
 
 // phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),
-// accumulator complete (epilogue), epilogue done, exit
-constexpr int TRACE_SLOTS = 6;
+// accumulator complete (epilogue), epilogue done, exit, and for split-K clusters: first cluster
+// barrier passed, cluster reduction done (0 otherwise)
+constexpr int TRACE_SLOTS = 8;
 
 template <int BN, int STAGES, bool SPLIT>
 struct GemmSmem {
@@ -349,6 +350,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (a.splits > 1) {
         // ---------------------------------------------------------- epilogue, part 2 (cluster)
         cluster_sync_all();
+        if (tr && threadIdx.x == 0) tr[6] = global_ns();
         if (warp < 4 && !*abort_flag) {
             const EpiConst ec2{a.bias ? cbias : nullptr, cqn, ckn};
             const int S = a.splits;
@@ -380,6 +382,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 epi_unit<EPI>(a, ec2, rr, u, n0, t0, b0, true, load_dsmem);
             }
         }
+        if (tr && threadIdx.x == 0) tr[7] = global_ns();
         cluster_sync_all();   // peers have finished reading this CTA's shared memory
     }
     if (warp == 5) {

@@ -55,8 +55,11 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 constexpr int ATTN_SMEM = 10 * 64 * 128;   // Q hi/lo + 2 x (K hi/lo) + 2 x (V hi/lo)
 
 __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+    unsigned long long * tr = a.trace ? a.trace + 3 * ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
     pdl_trigger();
     pdl_wait();
+    if (tr && threadIdx.x == 0) tr[1] = global_ns();
     extern __shared__ __align__(128) uint8_t sm[];
     uint8_t * sQ = sm;                       // [hi | lo]
     uint8_t * sK = sm + 2 * 8192;            // [buf][hi | lo]
@@ -205,6 +208,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
             if (olo) *(__half2 *) (dst + dt * 8 + olo) = __floats2half2_rn(v0 - __low2float(hv), v1 - __high2float(hv));
         }
     }
+    if (tr) {
+        __syncthreads();
+        if (threadIdx.x == 0) tr[2] = global_ns();
+    }
 }
 
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s) {
@@ -218,19 +225,28 @@ cudaError_t configure_attention() {
 // =============================================================================== adaLN
 template <int NV>
 __global__ void __launch_bounds__(64) adaln_kernel(const AdaLnArgs a) {
+    unsigned long long * tr = a.trace ? a.trace + 3 * blockIdx.x : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
     pdl_trigger();
     pdl_wait();
+    if (tr && threadIdx.x == 0) tr[1] = global_ns();
     const int gw = blockIdx.x * 2 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (gw >= a.B * a.rows) return;
     const int b = gw / a.rows, t = gw % a.rows;
     const float * xr = a.x + (long long) b * a.x_bs + (long long) t * a.H;
-    float4 v[NV];
-    float sum = 0.0f;
+    const float * m = a.mod + (long long) b * a.mod_bs + (a.per_row ? (long long) t * a.mod_ld : 0) + a.base;
+    // every load of the row (x, shift, scale) is issued before the reductions: one memory round trip
+    float4 v[NV], sh[NV], sc[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-        v[i] = *(const float4 *) (xr + (i * 32 + lane) * 4);
-        sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        const int c = (i * 32 + lane) * 4;
+        v[i] = *(const float4 *) (xr + c);
+        sh[i] = __ldg((const float4 *) (m + c));
+        sc[i] = __ldg((const float4 *) (m + a.H + c));
     }
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
     for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
     const float mean = sum / (float) a.H;
@@ -243,17 +259,15 @@ __global__ void __launch_bounds__(64) adaln_kernel(const AdaLnArgs a) {
 #pragma unroll
     for (int off = 16; off; off >>= 1) var += __shfl_xor_sync(0xffffffffu, var, off);
     const float inv = 1.0f / sqrtf(var / (float) a.H + a.eps);
-    const float * m = a.mod + (long long) b * a.mod_bs + (a.per_row ? (long long) t * a.mod_ld : 0) + a.base;
     __half * o = a.out + (long long) b * a.out_bs + (long long) t * a.H;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         const int c = (i * 32 + lane) * 4;
-        const float4 sh = *(const float4 *) (m + c), sc = *(const float4 *) (m + a.H + c);
         float y[4];
-        y[0] = (v[i].x - mean) * inv * (1.0f + sc.x) + sh.x;
-        y[1] = (v[i].y - mean) * inv * (1.0f + sc.y) + sh.y;
-        y[2] = (v[i].z - mean) * inv * (1.0f + sc.z) + sh.z;
-        y[3] = (v[i].w - mean) * inv * (1.0f + sc.w) + sh.w;
+        y[0] = (v[i].x - mean) * inv * (1.0f + sc[i].x) + sh[i].x;
+        y[1] = (v[i].y - mean) * inv * (1.0f + sc[i].y) + sh[i].y;
+        y[2] = (v[i].z - mean) * inv * (1.0f + sc[i].z) + sh[i].z;
+        y[3] = (v[i].w - mean) * inv * (1.0f + sc[i].w) + sh[i].w;
         __align__(8) __half hv[4], lv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -263,6 +277,7 @@ __global__ void __launch_bounds__(64) adaln_kernel(const AdaLnArgs a) {
         *(uint2 *) (o + c) = *(const uint2 *) hv;
         if (a.out_lo) *(uint2 *) (o + a.out_lo + c) = *(const uint2 *) lv;
     }
+    if (tr && lane == 0) atomicMax(&tr[2], global_ns());
 }
 
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s) {

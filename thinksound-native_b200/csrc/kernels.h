@@ -72,6 +72,7 @@ struct AttnArgs {
     int n0, n1, n2, H;
     long long qkv_lo;                                        // element offset of the lo halves of q, k, v
     long long out_lo0, out_lo1, out_lo2;                     // ... and of each output (0: hi only)
+    unsigned long long * trace;                              // optional per-CTA stamps (entry, upstream done, exit)
 };
 cudaError_t configure_attention();
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s);
@@ -84,6 +85,7 @@ struct AdaLnArgs {
     int B, rows, H;
     float eps;
     long long out_lo;                       // element offset of the lo half (0: hi only)
+    unsigned long long * trace;             // optional per-CTA stamps (entry, upstream done, exit)
 };
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s);
 

@@ -554,7 +554,15 @@ struct Plan {
                long long mod_bs, int base, __half * out) {
         AdaLnArgs a{x, (long long) rows * m.g.H, mod, mod_bs, mod_ld, per_row, base, out, (long long) rows * m.g.H,
                     m.B, rows, (int) m.g.H, 1e-5f, (long long) m.B * rows * m.g.H};
-        add(Op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name});
+        Op op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name};
+        op.traced = [a](cudaStream_t s, unsigned long long * tr) {
+            AdaLnArgs t = a;
+            t.trace = tr;
+            return launch_adaln(t, s);
+        };
+        op.ctas = (m.B * rows + 1) / 2;
+        op.trace_slots = 3;
+        add(op);
     }
     void attention(int S, int n0, int n1, int n2) {
         const long long H = m.g.H;
@@ -562,7 +570,15 @@ struct Plan {
                    m.att_l, m.att_c, m.att_t, n0, n1, n2, (int) m.g.H,
                    (long long) m.B * m.g.NH * m.S_pad * 64, m.B * m.T * H, m.B * m.C * H, m.B * m.TS * H};
         const double flops = 4.0 * m.B * (double) S * S * m.g.H;
-        add(Op{[a](cudaStream_t s) { return launch_attention(a, s); }, 1, flops, "attention"});
+        Op op{[a](cudaStream_t s) { return launch_attention(a, s); }, 1, flops, "attention"};
+        op.traced = [a](cudaStream_t s, unsigned long long * tr) {
+            AttnArgs t = a;
+            t.trace = tr;
+            return launch_attention(t, s);
+        };
+        op.ctas = ((S + 63) / 64) * (int) m.g.NH * m.B;
+        op.trace_slots = 3;
+        add(op);
     }
     // post_attn (src/dit_fwd.cpp:51-81) for one stream, all arms
     int post(const Blk & b, float * x, const __half * att, __half * xn, __half * h, int rows, const float * mod,
@@ -792,6 +808,62 @@ int Model::run_ops(const std::vector<Op> & ops, bool serial) {
         else if (o.evkind == 2) e = cudaStreamWaitEvent(st, events[o.ev], 0);
         else e = o.fn(st);
         if (e != cudaSuccess) return fail(TSN_ERR_CUDA, "launch " + o.name + ": " + cudaGetErrorString(e));
+    }
+    return TSN_OK;
+}
+
+// One eager forward on the graph's streams with every traceable launch stamping its CTAs
+// (globaltimer ns). Per traced op: index, earliest CTA entry, earliest start of work (GEMM: first
+// operand stage landed; others: upstream wait passed), latest exit, median exit — relative to the
+// earliest entry of the forward.
+int Model::timeline(std::vector<double> & rows) {
+    std::vector<size_t> off(ops_fwd.size(), 0);
+    size_t total = 0;
+    for (size_t i = 0; i < ops_fwd.size(); ++i)
+        if (ops_fwd[i].traced) { off[i] = total; total += (size_t) ops_fwd[i].ctas * ops_fwd[i].trace_slots; }
+    int rc = ensure_streams();
+    if (rc) return rc;
+    unsigned long long * d = nullptr;
+    CKR(cudaMalloc(&d, std::max<size_t>(total, 1) * 8));
+    std::vector<unsigned long long> h(total);
+    rc = TSN_OK;
+    cudaError_t e = cudaMemsetAsync(d, 0, total * 8, dev->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(dev->stream);
+    for (size_t i = 0; i < ops_fwd.size() && e == cudaSuccess; ++i) {
+        const Op & o = ops_fwd[i];
+        cudaStream_t st = o.stream == 0 ? dev->stream : side[o.stream - 1];
+        if (o.evkind == 1) e = cudaEventRecord(events[o.ev], st);
+        else if (o.evkind == 2) e = cudaStreamWaitEvent(st, events[o.ev], 0);
+        else e = o.traced ? o.traced(st, d + off[i]) : o.fn(st);
+    }
+    if (e != cudaSuccess) rc = fail(TSN_ERR_CUDA, std::string("timeline: ") + cudaGetErrorString(e));
+    if (!rc) rc = dev->sync();
+    if (!rc && total) {
+        e = cudaMemcpy(h.data(), d, total * 8, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = fail(TSN_ERR_CUDA, std::string("timeline copy: ") + cudaGetErrorString(e));
+    }
+    cudaFree(d);
+    if (rc) return rc;
+    unsigned long long t_min = ~0ull;
+    for (unsigned long long v : h)
+        if (v) t_min = std::min(t_min, v);
+    for (size_t i = 0; i < ops_fwd.size(); ++i) {
+        const Op & o = ops_fwd[i];
+        if (!o.traced) continue;
+        const int sl = o.trace_slots, work = o.kind == 0 ? 2 : 1, end = o.kind == 0 ? 5 : 2;
+        unsigned long long a0 = ~0ull, w0 = ~0ull, e1 = 0;
+        std::vector<unsigned long long> ends;
+        for (int c = 0; c < o.ctas; ++c) {
+            const unsigned long long * s = &h[off[i] + (size_t) c * sl];
+            if (s[0]) a0 = std::min(a0, s[0]);
+            if (s[work]) w0 = std::min(w0, s[work]);
+            if (s[end]) { e1 = std::max(e1, s[end]); ends.push_back(s[end]); }
+        }
+        if (ends.empty() || a0 == ~0ull) continue;
+        std::nth_element(ends.begin(), ends.begin() + ends.size() / 2, ends.end());
+        const double rel = (double) t_min;
+        rows.insert(rows.end(), {(double) i, (double) a0 - rel, w0 == ~0ull ? -1.0 : (double) w0 - rel, (double) e1 - rel,
+                                 (double) ends[ends.size() / 2] - rel});
     }
     return TSN_OK;
 }

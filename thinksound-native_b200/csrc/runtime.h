@@ -57,8 +57,9 @@ struct Op {
     std::string desc;      // launch configuration, for profiles
     int gemm_id = -1;      // GEMM sequence number within the forward (kind 0)
     std::string shape;     // GEMM shape key: ops with equal keys have the same candidate configs
-    std::function<cudaError_t(cudaStream_t, unsigned long long *)> traced;   // GEMMs: launch with phase trace
+    std::function<cudaError_t(cudaStream_t, unsigned long long *)> traced;   // launch with per-CTA stamps
     int ctas = 0;
+    int trace_slots = TRACE_SLOTS;   // stamps per CTA of `traced` (GEMMs: TRACE_SLOTS; others: 3)
     int stream = 0;        // 0 latent (the device stream), 1 clip, 2 text
     int evkind = 0;        // 0 kernel/copy, 1 record event `ev` on `stream`, 2 make `stream` wait on `ev`
     int ev = -1;
@@ -123,6 +124,7 @@ struct Model {
     int n_events = 0;
     int capture(const std::vector<Op> & ops, cudaGraphExec_t * out);
     int autotune(std::string & report);
+    int timeline(std::vector<double> & rows);
     int set_time(float t, float dt);
     void temb_host(float t, float * out) const;
     void release_activations();

@@ -97,6 +97,7 @@ _SIGS = [
     ("tsn_dit_profile_step", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
     ("tsn_dit_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_dit_trace_op", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
+    ("tsn_dit_timeline", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
     ("tsn_dit_autotune", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_gguf_write_synthetic", C.c_int, [C.c_char_p, C.POINTER(Geom), C.c_uint64, C.c_int]),
 ]
@@ -289,12 +290,21 @@ class Dit:
 
 
     def trace_op(self, op: int):
-        """Per-CTA phase timestamps (ns) of GEMM launch `op`: array [ctas, 6]."""
+        """Per-CTA phase timestamps (ns) of GEMM launch `op`: array [ctas, 8]."""
         import numpy as np
         n = C.c_int()
-        out = np.zeros((4096, 6), np.uint64)
+        out = np.zeros((4096, 8), np.uint64)
         check(lib().tsn_dit_trace_op(self.h, op, out.ctypes.data, 4096, C.byref(n)))
         return out[:min(n.value, 4096)]
+
+    def timeline(self):
+        """One eager forward with every GEMM, adaLN and attention launch stamped: array [launches, 5]
+        of (op index, first entry, first work, last exit, median exit), ns from the forward's start."""
+        import numpy as np
+        n = C.c_int()
+        out = np.zeros((8192, 5), np.float64)
+        check(lib().tsn_dit_timeline(self.h, out.ctypes.data, 8192, C.byref(n)))
+        return out[:min(n.value, 8192)]
 
     def autotune(self) -> str:
         buf = C.create_string_buffer(1 << 20)
