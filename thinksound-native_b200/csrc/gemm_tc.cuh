@@ -59,6 +59,7 @@ struct GemmArgs {
     __half * q; __half * k; __half * v;   // [B][NH][S_pad][64]
     long long out_lo;                     // element offset of the lo half of a split f16 output (0: none)
     unsigned long long * trace;           // optional per-CTA phase timestamps (tsn_dit_trace_op), else null
+    long long part_stride;                // EPI_F32 split-K without a cluster: K slice z writes out + z*part_stride
 };
 
 // phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),
@@ -183,7 +184,7 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             for (int e = 0; e < 32; ++e) v[e] += ec.bias[c0 + e];
         }
         if constexpr (EPI == EPI_F32) {
-            float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+            float * o = (float *) a.out + blockIdx.z * a.part_stride + (long long) b * a.out_bs + (long long) t * a.ldo + n;
 #pragma unroll
             for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU) {

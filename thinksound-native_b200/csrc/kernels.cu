@@ -4,8 +4,10 @@
 //                    (shaders/gemm_attn.metal:96-202). Flash-style online softmax over 64-key
 //                    tiles, f16 tensor-core QK^T and PV (mma.sync m16n8k16, f32 accumulate);
 //                    the [NH,S,S] f32 probability tensor of the reference never exists.
-//   adaln_kernel     adaln_ln (shaders/ops_conv.metal:127-144), one warp per row, writing the
-//                    f16 A operand of the next GEMM directly.
+//   adaln_kernel     adaln_ln (shaders/ops_conv.metal:127-144), one block per row, writing the
+//                    f16 A operand of the next GEMM directly; first applies the gated residual
+//                    update of the GEMM before it (gate_add, ops_conv.metal:146-154) from that
+//                    GEMM's split-K partial sums.
 //   gemv_kernel      batched gemv_h (shaders/gemm_attn.metal:48-64): warp per output row, 16-B
 //                    weight loads, every CFG arm from one weight read.
 //   cond_kernel      the per-forward conditioning adds and SiLUs (src/dit_fwd.cpp:131-140) and
@@ -224,31 +226,73 @@ cudaError_t configure_attention() {
 
 // =============================================================================== adaLN
 template <int NV>
-__global__ void __launch_bounds__(64) adaln_kernel(const AdaLnArgs a) {
+__global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
+    // one row per block; thread i owns float4 chunks i, i + TPR, ... of the row
     unsigned long long * tr = a.trace ? a.trace + 3 * blockIdx.x : nullptr;
     if (tr && threadIdx.x == 0) tr[0] = global_ns();
     pdl_trigger();
     pdl_wait();
     if (tr && threadIdx.x == 0) tr[1] = global_ns();
-    const int gw = blockIdx.x * 2 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (gw >= a.B * a.rows) return;
-    const int b = gw / a.rows, t = gw % a.rows;
-    const float * xr = a.x + (long long) b * a.x_bs + (long long) t * a.H;
+    const int row = blockIdx.x;
+    if (row >= a.B * a.rows) return;
+    const int b = row / a.rows, t = row % a.rows;
+    const int tid = threadIdx.x, TPR = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = TPR >> 5;
+    float * xr = a.x + (long long) b * a.x_bs + (long long) t * a.H;
     const float * m = a.mod + (long long) b * a.mod_bs + (a.per_row ? (long long) t * a.mod_ld : 0) + a.base;
-    // every load of the row (x, shift, scale) is issued before the reductions: one memory round trip
+    // every load of the row is issued before any arithmetic: one memory round trip
     float4 v[NV], sh[NV], sc[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-        const int c = (i * 32 + lane) * 4;
+        const int c = (i * TPR + tid) * 4;
         v[i] = *(const float4 *) (xr + c);
-        sh[i] = __ldg((const float4 *) (m + c));
-        sc[i] = __ldg((const float4 *) (m + a.H + c));
+        if (a.out) {
+            sh[i] = __ldg((const float4 *) (m + c));
+            sc[i] = __ldg((const float4 *) (m + a.H + c));
+        }
     }
+    if (a.part) {
+        const float * g = a.gmod + (long long) b * a.gmod_bs + (a.gper_row ? (long long) t * a.gmod_ld : 0) + a.goff;
+        const float * p = a.part + (long long) b * a.x_bs + (long long) t * a.H;
+        float4 acc[NV], pz[NV][7], gg[NV], bb[NV];
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const int c = (i * TPR + tid) * 4;
+            acc[i] = __ldcg((const float4 *) (p + c));
+#pragma unroll
+            for (int z = 1; z < 8; ++z)
+                if (z < a.nsplit) pz[i][z - 1] = __ldcg((const float4 *) (p + z * a.part_stride + c));
+            gg[i] = __ldg((const float4 *) (g + c));
+            bb[i] = a.pbias ? __ldg((const float4 *) (a.pbias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+#pragma unroll
+            for (int z = 1; z < 8; ++z)
+                if (z < a.nsplit) {
+                    acc[i].x += pz[i][z - 1].x; acc[i].y += pz[i][z - 1].y;
+                    acc[i].z += pz[i][z - 1].z; acc[i].w += pz[i][z - 1].w;
+                }
+            v[i].x = __fmaf_rn(acc[i].x + bb[i].x, gg[i].x, v[i].x);
+            v[i].y = __fmaf_rn(acc[i].y + bb[i].y, gg[i].y, v[i].y);
+            v[i].z = __fmaf_rn(acc[i].z + bb[i].z, gg[i].z, v[i].z);
+            v[i].w = __fmaf_rn(acc[i].w + bb[i].w, gg[i].w, v[i].w);
+            *(float4 *) (xr + (i * TPR + tid) * 4) = v[i];
+        }
+    }
+    if (!a.out) {
+        if (tr) { __syncthreads(); if (tid == 0) tr[2] = global_ns(); }
+        return;
+    }
+    __shared__ float red[2][32];
     float sum = 0.0f;
 #pragma unroll
     for (int i = 0; i < NV; ++i) sum += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
     for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) red[0][warp] = sum;
+    __syncthreads();
+    sum = 0.0f;
+    for (int w = 0; w < nw; ++w) sum += red[0][w];
     const float mean = sum / (float) a.H;
     float var = 0.0f;
 #pragma unroll
@@ -258,11 +302,15 @@ __global__ void __launch_bounds__(64) adaln_kernel(const AdaLnArgs a) {
     }
 #pragma unroll
     for (int off = 16; off; off >>= 1) var += __shfl_xor_sync(0xffffffffu, var, off);
+    if (lane == 0) red[1][warp] = var;
+    __syncthreads();
+    var = 0.0f;
+    for (int w = 0; w < nw; ++w) var += red[1][w];
     const float inv = 1.0f / sqrtf(var / (float) a.H + a.eps);
     __half * o = a.out + (long long) b * a.out_bs + (long long) t * a.H;
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-        const int c = (i * 32 + lane) * 4;
+        const int c = (i * TPR + tid) * 4;
         float y[4];
         y[0] = (v[i].x - mean) * inv * (1.0f + sc[i].x) + sh[i].x;
         y[1] = (v[i].y - mean) * inv * (1.0f + sc[i].y) + sh[i].y;
@@ -277,19 +325,26 @@ __global__ void __launch_bounds__(64) adaln_kernel(const AdaLnArgs a) {
         *(uint2 *) (o + c) = *(const uint2 *) hv;
         if (a.out_lo) *(uint2 *) (o + a.out_lo + c) = *(const uint2 *) lv;
     }
-    if (tr && lane == 0) atomicMax(&tr[2], global_ns());
+    if (tr) { __syncthreads(); if (tid == 0) tr[2] = global_ns(); }
+}
+
+int adaln_threads(int H) {
+    if (H % 128) return 0;
+    for (int nv : {1, 2, 4}) {
+        const int tpr = H / 4 / nv;
+        if (H % (4 * nv) == 0 && tpr % 32 == 0 && tpr <= 256) return tpr;
+    }
+    return 0;
 }
 
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s) {
-    const int nrows = a.B * a.rows;
-    const dim3 grid((nrows + 1) / 2);   // two rows (warps) per block: enough blocks to cover the SMs
-    switch (a.H / 128) {
-        case 1: return launch_ex(adaln_kernel<1>, grid, dim3(64), 0, s, 1u, a);
-        case 2: return launch_ex(adaln_kernel<2>, grid, dim3(64), 0, s, 1u, a);
-        case 4: return launch_ex(adaln_kernel<4>, grid, dim3(64), 0, s, 1u, a);
-        case 8: return launch_ex(adaln_kernel<8>, grid, dim3(64), 0, s, 1u, a);
-        case 12: return launch_ex(adaln_kernel<12>, grid, dim3(64), 0, s, 1u, a);
-        case 16: return launch_ex(adaln_kernel<16>, grid, dim3(64), 0, s, 1u, a);
+    const int tpr = adaln_threads(a.H);
+    if (!tpr || (a.part && (a.nsplit < 1 || a.nsplit > 8))) return cudaErrorInvalidValue;
+    const dim3 grid(a.B * a.rows);
+    switch (a.H / 4 / tpr) {
+        case 1: return launch_ex(adaln_kernel<1>, grid, dim3(tpr), 0, s, 1u, a);
+        case 2: return launch_ex(adaln_kernel<2>, grid, dim3(tpr), 0, s, 1u, a);
+        case 4: return launch_ex(adaln_kernel<4>, grid, dim3(tpr), 0, s, 1u, a);
         default: return cudaErrorInvalidValue;
     }
 }

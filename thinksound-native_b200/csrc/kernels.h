@@ -79,15 +79,21 @@ cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s);
 
 // ---- adaLN LayerNorm + modulation -> f16 GEMM operand ----
 struct AdaLnArgs {
-    const float * x; long long x_bs;        // [B][rows][H] f32
-    const float * mod; long long mod_bs, mod_ld; int per_row, base;
-    __half * out; long long out_bs;         // [B][rows][H] f16
+    float * x; long long x_bs;              // [B][rows][H] f32 residual stream
+    const float * mod; long long mod_bs, mod_ld; int per_row, base;   // shift at base, scale at base + H
+    __half * out; long long out_bs;         // [B][rows][H] f16, or null: apply the pending update only
     int B, rows, H;
     float eps;
     long long out_lo;                       // element offset of the lo half (0: hi only)
     unsigned long long * trace;             // optional per-CTA stamps (entry, upstream done, exit)
+    // Pending gated residual update of the GEMM before (gate_add, shaders/ops_conv.metal:146-154),
+    // applied to x first and written back: x += gate * (part[0] + ... + part[nsplit-1] + pbias).
+    const float * part; long long part_stride; int nsplit;   // part[z][B][rows][H]; null: none
+    const float * pbias;                                     // [H]
+    const float * gmod; long long gmod_bs, gmod_ld; int gper_row, goff;   // gate rows, like mod
 };
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s);
+int adaln_threads(int H);   // threads per row (one row per block), 0 when H is unsupported
 
 // ---- batched GEMV y[b][n] = act(W[n,:]·x[b,:] + bias[n]) ----
 struct GemvJob {

@@ -359,6 +359,9 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
     ALLOC(att_l, 2 * B * T * H * 2);   // hi | lo
     ALLOC(att_c, 2 * B * C * H * 2);   // hi | lo
     ALLOC(att_t, 2 * B * TS * H * 2);   // hi | lo
+    ALLOC(part_l, 8 * B * T * H * 4);   // split-K partial sums of the gated GEMMs, up to 8 K slices
+    ALLOC(part_c, 8 * B * C * H * 4);
+    ALLOC(part_t, 8 * B * TS * H * 4);
     ALLOC(h_l, B * T * F * 2);
     ALLOC(h_c, B * C * F * 2);
     ALLOC(h_t, B * TS * F * 2);
@@ -416,11 +419,19 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
 
 // ------------------------------------------------------------------------------ planning
 namespace {
+// a gated residual update that a GEMM left for the next adaLN of the same residual stream
+struct Pending {
+    const float * part; long long stride; int nsplit;
+    const float * bias;
+    const float * gmod; long long gmod_ld, gmod_bs; int gper_row, goff;
+};
+
 struct Plan {
     Model & m;
     std::vector<Op> & ops;
     std::string last_shape;
     int cur = 0;              // stream the next ops go to
+    std::map<const float *, Pending> pend;   // residual stream -> its pending update
     void add(Op o) { o.stream = cur; ops.push_back(std::move(o)); }
     int record() {
         Op o{[](cudaStream_t) { return cudaSuccess; }, 2, 0.0, "record"};
@@ -436,11 +447,12 @@ struct Plan {
         add(o);
     }
 
-    // Pick the tile width and split-K (cluster) factor with a small cost model: per-K-block time
-    // of one CTA, waves over the CTAs that fit at once (clusters need their S SMs in one GPC), and
-    // the cluster reduction; then encode the TMA views.
+    // Pick the tile width and split-K factor with a small cost model: per-K-block time of one CTA,
+    // waves over the CTAs that fit at once (clusters need their S SMs in one GPC), and the split-K
+    // reduction; then encode the TMA views. With `partial`, the S K-slices are independent CTAs that
+    // write S partial tiles (the consumer adds them), so no cluster is formed.
     int gemm(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, int epi, GemmLaunch & g,
-             bool plain = false) {
+             bool plain = false, bool partial = false) {
         const int B = m.B;
         const bool split = !plain;
         const int bt = B >= 2 ? 64 : 128, bb = 128 / bt;
@@ -457,18 +469,22 @@ struct Plan {
                                        : (bn == 256 ? 0.37 : bn == 192 ? 0.30 : bn == 128 ? 0.24 : 0.18);
             const int tiles = mtt * mtb * ((N + bn - 1) / bn);
             for (int s = 1; s <= 8 && s <= kb; ++s) {
+                if (!splits_valid(kb, s)) continue;
                 const int kbps = (kb + s - 1) / s;
-                if ((kb + kbps - 1) / kbps != s) continue;
-                const int cap = gemm_cluster_capacity(bn, epi, split, s);
+                const int cap = partial ? gemm_cluster_capacity(bn, epi, split, 1) : gemm_cluster_capacity(bn, epi, split, s);
                 if (cap <= 0) continue;
                 const int ctas = tiles * s, waves = (ctas + cap - 1) / cap;
-                const double cost = waves * (kbps * kcost + 1.5 + (s > 1 ? 1.5 : 0.0));
+                const double cost = waves * (kbps * kcost + 1.5) + (s > 1 ? (partial ? 0.3 * s : 1.5 * waves) : 0.0);
                 if (cost < best - 1e-9) { best = cost; bn_best = bn; s_best = s; }
             }
         }
         if (!bn_best) return fail(TSN_ERR_ARG, std::string(name) + ": no tile fits N=" + std::to_string(N));
         auto fo = m.gemm_force.find(m.gemm_seq);
-        if (fo != m.gemm_force.end()) { bn_best = fo->second.first; s_best = fo->second.second; }
+        if (fo != m.gemm_force.end() && splits_valid(kb, fo->second.second) &&
+            (fo->second.first == 192 || N % fo->second.first == 0)) {
+            bn_best = fo->second.first;
+            s_best = fo->second.second;
+        }
         char key[128];
         snprintf(key, sizeof key, "%d:%d:%d:%d:%d:%d", rows, N, K_in, W.taps, epi, (int) split);
         last_shape = key;
@@ -487,15 +503,21 @@ struct Plan {
         GemmArgs & a = g.args;
         a.rows = rows; a.B = B; a.bt = bt; a.bb = bb; a.m_tiles_t = mtt; a.N = N;
         a.k_blocks = kb; a.ic_blocks = K_in / 64; a.pad = pad;
-        a.splits = s_best; a.kb_per_split = (kb + s_best - 1) / s_best;
+        a.splits = partial ? 1 : s_best; a.kb_per_split = (kb + s_best - 1) / s_best;
         a.err = m.dev->d_err;
         a.bias = W.b;
         return TSN_OK;
     }
+    // every one of the s K-slices gets at least one 64-wide K block
+    static bool splits_valid(int kb, int s) {
+        if (s < 1 || s > 8 || s > kb) return false;
+        const int kbps = (kb + s - 1) / s;
+        return (kb + kbps - 1) / kbps == s;
+    }
     void push(const char * name, const GemmLaunch & g, double flops) {
         char d[160];
-        snprintf(d, sizeof d, "bn=%d split=%d ksplit=%d grid=%ux%ux%u kb=%d smem=%zu", g.bn, (int) g.split, g.args.splits,
-                 g.grid.x, g.grid.y, g.grid.z, g.args.k_blocks, g.smem);
+        snprintf(d, sizeof d, "bn=%d split=%d ksplit=%u%s grid=%ux%ux%u kb=%d smem=%zu", g.bn, (int) g.split, g.grid.z,
+                 g.args.part_stride ? " partial" : "", g.grid.x, g.grid.y, g.grid.z, g.args.k_blocks, g.smem);
         Op op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name, d};
         op.gemm_id = m.gemm_seq++;
         op.shape = last_shape;
@@ -528,16 +550,28 @@ struct Plan {
         push(name, g, fl(m.B, rows, W));
         return TSN_OK;
     }
+    // res += gate * (A.W^T + bias) (linear1/ffn.w2 + gate_add, src/dit_fwd.cpp:61-79): the GEMM
+    // writes its split-K partial sums into the stream's workspace, and the next adaLN of `res`
+    // (or resolve()) adds them, applies bias and gate, and updates res in place.
     int gate(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * res,
              const float * mod, int per_row, long long mod_ld, long long mod_bs, int gate_idx, bool plain = false) {
         GemmLaunch g;
-        int rc = gemm(name, A, K_in, rows, W, pad, EPI_GATE, g, plain);
+        int rc = gemm(name, A, K_in, rows, W, pad, EPI_F32, g, plain, true);
         if (rc) return rc;
-        g.args.out = res; g.args.ldo = m.g.H; g.args.out_bs = (long long) rows * m.g.H;
-        g.args.mod = mod; g.args.mod_per_row = per_row; g.args.mod_ld = mod_ld; g.args.mod_bs = mod_bs;
-        g.args.gate_off = gate_idx * (int) m.g.H;
+        float * ws = res == m.lat ? m.part_l : res == m.clip_s ? m.part_c : m.part_t;
+        const long long H = m.g.H;
+        g.args.out = ws; g.args.ldo = H; g.args.out_bs = (long long) rows * H;
+        g.args.part_stride = (long long) m.B * rows * H;
+        g.args.bias = nullptr;
         push(name, g, fl(m.B, rows, W));
+        Pending & pd = pend[res];
+        pd = Pending{ws, g.args.part_stride, (int) g.grid.z, W.b, mod, per_row ? mod_ld : 0, mod_bs, per_row,
+                     gate_idx * (int) H};
         return TSN_OK;
+    }
+    // apply a pending gated update to x without normalising (taps read x between blocks)
+    void resolve(float * x, int rows) {
+        if (pend.count(x)) adaln("gate_resolve", x, rows, nullptr, 0, 0, 0, 0, nullptr);
     }
     int qkv(const char * name, const __half * A, int rows, const Blk & b, int s_off, const float2 * rope) {
         GemmLaunch g;
@@ -550,17 +584,24 @@ struct Plan {
         push(name, g, fl(m.B, rows, b.qkv));
         return TSN_OK;
     }
-    void adaln(const char * name, const float * x, int rows, const float * mod, int per_row, long long mod_ld,
+    void adaln(const char * name, float * x, int rows, const float * mod, int per_row, long long mod_ld,
                long long mod_bs, int base, __half * out) {
         AdaLnArgs a{x, (long long) rows * m.g.H, mod, mod_bs, mod_ld, per_row, base, out, (long long) rows * m.g.H,
                     m.B, rows, (int) m.g.H, 1e-5f, (long long) m.B * rows * m.g.H};
+        auto it = pend.find(x);
+        if (it != pend.end()) {
+            const Pending & pd = it->second;
+            a.part = pd.part; a.part_stride = pd.stride; a.nsplit = pd.nsplit; a.pbias = pd.bias;
+            a.gmod = pd.gmod; a.gmod_ld = pd.gmod_ld; a.gmod_bs = pd.gmod_bs; a.gper_row = pd.gper_row; a.goff = pd.goff;
+            pend.erase(it);
+        }
         Op op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name};
         op.traced = [a](cudaStream_t s, unsigned long long * tr) {
             AdaLnArgs t = a;
             t.trace = tr;
             return launch_adaln(t, s);
         };
-        op.ctas = (m.B * rows + 1) / 2;
+        op.ctas = m.B * rows;
         op.trace_slots = 3;
         add(op);
     }
@@ -739,7 +780,20 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
             p.tap("a0_out_l", att_l, (size_t) B * T * H * 2, cvt_f16_arm((size_t) T * H));
             p.tap("a0_out_c", att_c, (size_t) B * C * H * 2, cvt_f16_arm((size_t) C * H));
             p.tap("a0_out_t", att_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
+            p.resolve(lat, T);
             p.tap("jb0_lat", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+            if (!pre_only) {
+                // the clip/text posts ran on their own streams: join them before reading their results
+                p.cur = 1;
+                const int e1 = p.record();
+                p.cur = 2;
+                const int e2 = p.record();
+                p.cur = 0;
+                p.wait(e1);
+                p.wait(e2);
+            }
+            p.resolve(clip_s, C);
+            p.resolve(text_s, TS);
             p.tap("jb0_clip", clip_s, (size_t) B * C * H * 4, cvt_f32_arm((size_t) C * H));
             p.tap("jb0_text", text_s, (size_t) B * TS * H * 4, cvt_f32_arm((size_t) TS * H));
         }
@@ -753,7 +807,10 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         p.wait(ecl);
         p.wait(etl);
     }
-    if (tp) p.tap("after_joint", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    if (tp) {
+        p.resolve(lat, T);
+        p.tap("after_joint", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    }
     // fused blocks                                                src/dit_fwd.cpp:268-279
     for (size_t i = 0; i < fb.size(); ++i) {
         const float * ml = modl + mod_off[NJ + i];
@@ -762,7 +819,10 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         p.attention(T, T, 0, 0);
         if ((rc = p.post(fb[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs))) return rc;
     }
-    if (tp) p.tap("after_fused", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    if (tp) {
+        p.resolve(lat, T);
+        p.tap("after_fused", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    }
     // final layer                                                 src/dit_fwd.cpp:287-303
     const float * mf = modl + mod_off.back();
     p.adaln("adaln_final", lat, T, mf, 1, NA, lat_mod_bs, 0, xn_l);
