@@ -49,9 +49,9 @@ bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Pipeline depth: as many stages as fit in ~192 KB of shared memory.
+// Pipeline depth: as many stages as fit in the 227 KB of shared memory a CTA may use.
 constexpr int stages_for(int bn, bool split) {
-    return split ? (bn >= 192 ? 3 : bn == 128 ? 4 : 5) : (bn == 256 ? 4 : bn == 192 ? 5 : bn == 128 ? 6 : 8);
+    return split ? (bn == 256 ? 3 : bn == 192 ? 4 : bn == 128 ? 4 : 5) : (bn == 256 ? 4 : bn == 192 ? 5 : bn == 128 ? 6 : 8);
 }
 int gemm_stages(int bn, bool split) { return stages_for(bn, split); }
 

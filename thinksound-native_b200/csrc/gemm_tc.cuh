@@ -76,7 +76,7 @@ struct GemmSmem {
     static constexpr int STAGE = NA * A_BYTES + B_BYTES;
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int CONST_OFF = BAR_OFF + 256;       // epilogue constants: bias slice, q/k gains
-    static constexpr int TOTAL = CONST_OFF + 2048 + 1024; // + alignment slack
+    static constexpr int TOTAL = CONST_OFF + (256 + 64 + 64) * 4 + 1024;   // + alignment slack
 };
 
 // SiLU with the fast exponential and division (relative error ~1e-7, far below the f16 operand
