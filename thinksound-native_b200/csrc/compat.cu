@@ -342,7 +342,7 @@ int compat_gemm(DeviceCtx & c, int wf16, const void * W, const void * X, void * 
     }
     const int bn = N % 256 == 0 ? 256 : N % 128 == 0 ? 128 : 64;
     GemmLaunch g{};
-    g.bn = bn; g.epi = EPI_F32; g.split = true; g.smem = gemm_smem_bytes(bn, true); g.ab_bf16 = 0;
+    g.bn = bn; g.epi = EPI_F32; g.split = true; g.smem = gemm_smem_bytes(bn, true, EPI_F32); g.ab_bf16 = 0;
     g.grid = dim3(N / bn, (M + 127) / 128, 1);
     if (!make_act_map(&g.ta, xa, K, M, 1, 128, 1, 0) || !make_act_map(&g.ta2, xa + (size_t) M * K, K, M, 1, 128, 1, 0) ||
         !make_w_map(&g.tb, wd, K, N, bn, 0))

@@ -49,23 +49,37 @@ bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Pipeline depth: as many stages as fit in the 227 KB of shared memory a CTA may use.
-constexpr int stages_for(int bn, bool split) {
-    return split ? (bn == 256 ? 3 : bn == 192 ? 4 : bn == 128 ? 4 : 5) : (bn == 256 ? 4 : bn == 192 ? 5 : bn == 128 ? 6 : 8);
+// Pipeline depth: as many stages as fit in the 227 KB of shared memory a CTA may use (the qkv
+// epilogue also stages RoPE rows, which costs the 192-wide split tile one stage).
+constexpr int stages_for(int bn, bool split, int epi) {
+    return split ? (bn == 256 ? 3 : bn == 192 ? (epi == EPI_QKV ? 3 : 4) : bn == 128 ? 4 : 5)
+                 : (bn == 256 ? 4 : bn == 192 ? 5 : bn == 128 ? 6 : 8);
 }
-int gemm_stages(int bn, bool split) { return stages_for(bn, split); }
+int gemm_stages(int bn, bool split, int epi) { return stages_for(bn, split, epi); }
+
+namespace {
+template <int BN, bool SPLIT, int EPI>
+constexpr int smem_total() { return GemmSmem<BN, stages_for(BN, SPLIT, EPI), SPLIT, EPI>::TOTAL; }
+template <int BN, bool SPLIT>
+size_t smem_of(int epi) {
+    switch (epi) {
+        case EPI_F32: return smem_total<BN, SPLIT, EPI_F32>();
+        case EPI_F16: return smem_total<BN, SPLIT, EPI_F16>();
+        case EPI_F16_SILU: return smem_total<BN, SPLIT, EPI_F16_SILU>();
+        case EPI_SWIGLU: return smem_total<BN, SPLIT, EPI_SWIGLU>();
+        case EPI_QKV: return smem_total<BN, SPLIT, EPI_QKV>();
+    }
+    return 0;
+}
+} // namespace
 
 // Dynamic shared memory of one configuration: the kernel's own layout constant (single source).
-size_t gemm_smem_bytes(int bn, bool split) {
-    switch (bn * 2 + (split ? 1 : 0)) {
-        case 64 * 2: return GemmSmem<64, stages_for(64, false), false>::TOTAL;
-        case 64 * 2 + 1: return GemmSmem<64, stages_for(64, true), true>::TOTAL;
-        case 128 * 2: return GemmSmem<128, stages_for(128, false), false>::TOTAL;
-        case 128 * 2 + 1: return GemmSmem<128, stages_for(128, true), true>::TOTAL;
-        case 192 * 2: return GemmSmem<192, stages_for(192, false), false>::TOTAL;
-        case 192 * 2 + 1: return GemmSmem<192, stages_for(192, true), true>::TOTAL;
-        case 256 * 2: return GemmSmem<256, stages_for(256, false), false>::TOTAL;
-        case 256 * 2 + 1: return GemmSmem<256, stages_for(256, true), true>::TOTAL;
+size_t gemm_smem_bytes(int bn, bool split, int epi) {
+    switch (bn) {
+        case 64: return split ? smem_of<64, true>(epi) : smem_of<64, false>(epi);
+        case 128: return split ? smem_of<128, true>(epi) : smem_of<128, false>(epi);
+        case 192: return split ? smem_of<192, true>(epi) : smem_of<192, false>(epi);
+        case 256: return split ? smem_of<256, true>(epi) : smem_of<256, false>(epi);
     }
     return 0;
 }
@@ -75,8 +89,8 @@ using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs, int);
 
 template <int BN, int EPI, bool SPLIT>
 KernelFn pick() {
-    constexpr int ST = stages_for(BN, SPLIT);
-    static_assert(GemmSmem<BN, ST, SPLIT>::TOTAL <= 232448, "smem budget");
+    constexpr int ST = stages_for(BN, SPLIT, EPI);
+    static_assert(GemmSmem<BN, ST, SPLIT, EPI>::TOTAL <= 232448, "smem budget");
     return (KernelFn) gemm_tc_kernel<BN, EPI, ST, SPLIT>;
 }
 
@@ -87,7 +101,6 @@ KernelFn pick_epi(int epi) {
         case EPI_F16: return pick<BN, EPI_F16, SPLIT>();
         case EPI_F16_SILU: return pick<BN, EPI_F16_SILU, SPLIT>();
         case EPI_SWIGLU: return pick<BN, EPI_SWIGLU, SPLIT>();
-        case EPI_GATE: return pick<BN, EPI_GATE, SPLIT>();
         case EPI_QKV: return pick<BN, EPI_QKV, SPLIT>();
     }
     return nullptr;
@@ -112,7 +125,7 @@ cudaError_t configure_gemm_kernels() {
                 KernelFn fn = kernel_for(bn, epi, split != 0);
                 if (!fn) continue;
                 cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                     (int) gemm_smem_bytes(bn, split != 0));
+                                                     (int) gemm_smem_bytes(bn, split != 0, epi));
                 if (e != cudaSuccess) return e;
             }
     return cudaSuccess;
@@ -158,14 +171,14 @@ int cluster_capacity_uncached(int bn, int epi, bool split, int cluster) {
         int per_sm = 0, sms = 0, dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 192, gemm_smem_bytes(bn, split)) != cudaSuccess)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 192, gemm_smem_bytes(bn, split, epi)) != cudaSuccess)
             return 0;
         return per_sm * sms;
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(1, 1, (unsigned) cluster);
     cfg.blockDim = dim3(192, 1, 1);
-    cfg.dynamicSmemBytes = gemm_smem_bytes(bn, split);
+    cfg.dynamicSmemBytes = gemm_smem_bytes(bn, split, epi);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 1;

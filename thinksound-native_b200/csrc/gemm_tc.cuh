@@ -39,7 +39,6 @@ enum GemmEpi : int {
     EPI_F16 = 1,       // out f16 = acc (+bias)
     EPI_F16_SILU = 2,  // out f16 = silu(acc + bias)
     EPI_SWIGLU = 3,    // columns in groups of 64 = [32 w1 | 32 w3] -> out f16 = silu(a)*b
-    EPI_GATE = 4,      // res f32 += (acc + bias) * mod[row][gate_off + n]
     EPI_QKV = 5,       // bias, per-head RMSNorm(q,k), RoPE(q,k), f16 head-major q/k/v
 };
 
@@ -47,11 +46,8 @@ struct GemmArgs {
     int rows, B, bt, bb, m_tiles_t, N, k_blocks, ic_blocks, pad, splits, kb_per_split;
     int * err;               // device error word
     const float * bias;      // [N] or null
-    void * out;              // EPI_F32/F16*/SWIGLU output, EPI_GATE residual (f32)
+    void * out;              // EPI_F32/F16*/SWIGLU output
     long long ldo, out_bs;   // row stride and batch stride of out (elements)
-    const float * mod;       // EPI_GATE modulation rows
-    long long mod_ld, mod_bs;  // row stride; per-batch stride (per-row mods: rows*mod_ld)
-    int mod_per_row, gate_off;
     // EPI_QKV
     const float * qn; const float * kn;   // per-head RMSNorm gains [64]
     const float2 * rope;                  // [rows][32] (cos, sin) or null (text stream)
@@ -67,7 +63,11 @@ struct GemmArgs {
 // barrier passed, cluster reduction done (0 otherwise)
 constexpr int TRACE_SLOTS = 8;
 
-template <int BN, int STAGES, bool SPLIT>
+// RoPE rows staged for the qkv epilogue: 64 time rows of 32 (cos, sin) pairs, rows padded to 17
+// float4 so that threads reading consecutive rows hit different banks
+constexpr int ROPE_ROWS = 64, ROPE_STRIDE4 = 17;
+
+template <int BN, int STAGES, bool SPLIT, int EPI>
 struct GemmSmem {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int NA = SPLIT ? 2 : 1;
@@ -76,20 +76,23 @@ struct GemmSmem {
     static constexpr int STAGE = NA * A_BYTES + B_BYTES;
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int CONST_OFF = BAR_OFF + 256;       // epilogue constants: bias slice, q/k gains
-    static constexpr int TOTAL = CONST_OFF + (256 + 64 + 64) * 4 + 1024;   // + alignment slack
+    static constexpr int ROPE_OFF = CONST_OFF + (256 + 64 + 64) * 4;
+    static constexpr int ROPE_BYTES = EPI == 5 ? ROPE_ROWS * ROPE_STRIDE4 * 16 : 0;   // EPI_QKV only
+    static constexpr int TOTAL = ROPE_OFF + ROPE_BYTES + 1024;   // + alignment slack
 };
 
 // SiLU with the fast exponential and division (relative error ~1e-7, far below the f16 operand
 // rounding every downstream GEMM sees)
 __device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
 
-__device__ __forceinline__ void prefetch_l1(const void * p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
 
 // Per-tile epilogue constants staged in shared memory before the accumulator is ready.
 struct EpiConst {
     const float * bias;   // bias[n0 .. n0+BN) in shared memory, or null
     const float * qn;     // q RMSNorm gains (64), shared memory
     const float * kn;     // k RMSNorm gains (64), shared memory
+    const float4 * rope;  // RoPE rows t0 .. t0+ROPE_ROWS-1 in shared memory (qkv with RoPE), or null
+    int t0;
 };
 
 // store 8 f32 values as f16 at o, and their rounding residuals at o + lo (when lo != 0)
@@ -160,13 +163,19 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
 #pragma unroll
             for (int e = 0; e < 64; ++e) v[e] = v[e] * inv * g[e];
             if (a.rope) {
-                const float2 * cs = a.rope + (size_t) t * 32;
+                // this row's (cos, sin) pairs, two per float4: staged rows when the tile's time rows
+                // fit the staged table, else straight from the global table
+                const float4 * cs = t - ec.t0 < ROPE_ROWS ? ec.rope + (t - ec.t0) * ROPE_STRIDE4
+                                                          : (const float4 *) (a.rope + (size_t) t * 32);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const float2 w = cs[j];
-                    const float x0 = v[2 * j], x1 = v[2 * j + 1];
-                    v[2 * j] = x0 * w.x - x1 * w.y;
-                    v[2 * j + 1] = x0 * w.y + x1 * w.x;
+                for (int j = 0; j < 16; ++j) {
+                    const float4 w = cs[j];
+                    float x0 = v[4 * j], x1 = v[4 * j + 1];
+                    v[4 * j] = x0 * w.x - x1 * w.y;
+                    v[4 * j + 1] = x0 * w.y + x1 * w.x;
+                    x0 = v[4 * j + 2]; x1 = v[4 * j + 3];
+                    v[4 * j + 2] = x0 * w.z - x1 * w.w;
+                    v[4 * j + 3] = x0 * w.w + x1 * w.z;
                 }
             }
         }
@@ -195,23 +204,6 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             }
 #pragma unroll
             for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, v + q);
-        } else if constexpr (EPI == EPI_GATE) {
-            float * o = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
-            const float * g = a.mod + (long long) b * a.mod_bs + (a.mod_per_row ? (long long) t * a.mod_ld : 0) + a.gate_off + n;
-            // all 16 loads first, then the stores: interleaving them serialises one L2 round trip per
-            // 4 columns (the compiler cannot move a load of g above a store to o)
-            float4 xr[8], gr[8];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                xr[q] = __ldcg((const float4 *) (o + 4 * q));
-                gr[q] = __ldg((const float4 *) (g + 4 * q));
-            }
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-                xr[q].x += v[4 * q] * gr[q].x; xr[q].y += v[4 * q + 1] * gr[q].y;
-                xr[q].z += v[4 * q + 2] * gr[q].z; xr[q].w += v[4 * q + 3] * gr[q].w;
-                *(float4 *) (o + 4 * q) = xr[q];
-            }
         }
     }
 }
@@ -220,7 +212,7 @@ template <int BN, int EPI, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                const __grid_constant__ CUtensorMap tmB, const GemmArgs a, const int ab_bf16) {
-    using L = GemmSmem<BN, STAGES, SPLIT>;
+    using L = GemmSmem<BN, STAGES, SPLIT, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
@@ -230,6 +222,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     volatile int * abort_flag = (volatile int *) (tslot + 1);
     float * cbias = (float *) (smem + L::CONST_OFF);      // BN floats
     float * cqn = cbias + 256, * ckn = cqn + 64;           // 64 + 64 floats
+    float4 * crope = (float4 *) (smem + L::ROPE_OFF);      // qkv: ROPE_ROWS x ROPE_STRIDE4
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
@@ -316,13 +309,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (a.bias)
                 for (int i = tid; i < BN && n0 + i < a.N; i += 128) cbias[i] = a.bias[n0 + i];
             if (EPI == EPI_QKV && tid < 64) { cqn[tid] = a.qn[tid]; ckn[tid] = a.kn[tid]; }
-            if (EPI == EPI_QKV && a.rope) {
-                const int t = t0 + tid % a.bt;
-                if (t < a.rows) { prefetch_l1(a.rope + (size_t) t * 32); prefetch_l1(a.rope + (size_t) t * 32 + 16); }
-            }
+            if (EPI == EPI_QKV && a.rope)
+                for (int i = tid; i < ROPE_ROWS * 16; i += 128) {
+                    const int rr = i >> 4, c4 = i & 15;
+                    if (t0 + rr < a.rows) crope[rr * ROPE_STRIDE4 + c4] = __ldg((const float4 *) (a.rope + (size_t) (t0 + rr) * 32) + c4);
+                }
             epi_bar();
         }
-        const EpiConst ec{a.bias ? cbias : nullptr, cqn, ckn};
+        const EpiConst ec{a.bias ? cbias : nullptr, cqn, ckn, crope, t0};
         const bool ok = mbar_wait(tfull, 0, abort_flag, a.err, DEV_TIMEOUT_TMEM) && !*abort_flag;
         tc_fence_after();
         const int r = warp * 32 + lane;
@@ -353,7 +347,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         cluster_sync_all();
         if (tr && threadIdx.x == 0) tr[6] = global_ns();
         if (warp < 4 && !*abort_flag) {
-            const EpiConst ec2{a.bias ? cbias : nullptr, cqn, ckn};
+            const EpiConst ec2{a.bias ? cbias : nullptr, cqn, ckn, crope, t0};
             const int S = a.splits;
             const uint32_t q = cluster_rank();
             const uint32_t local = smem_u32(smem);

@@ -59,8 +59,8 @@ bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
 cudaError_t configure_gemm_kernels();
 int gemm_cluster_capacity(int bn, int epi, bool split, int cluster);
-size_t gemm_smem_bytes(int bn, bool split);
-int gemm_stages(int bn, bool split);
+size_t gemm_smem_bytes(int bn, bool split, int epi);
+int gemm_stages(int bn, bool split, int epi);
 
 // ---- attention (kernels.cu) ----
 struct AttnArgs {

@@ -492,7 +492,7 @@ struct Plan {
         g.bn = bn_best;
         g.epi = epi;
         g.split = split;
-        g.smem = gemm_smem_bytes(bn_best, split);
+        g.smem = gemm_smem_bytes(bn_best, split, epi);
         g.ab_bf16 = m.bf16;
         g.grid = dim3((N + bn_best - 1) / bn_best, mtt * mtb, s_best);
         const __half * Alo = (const __half *) A + (size_t) B * rows * K_in;
