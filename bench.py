@@ -10,6 +10,8 @@ F=4096) with seeded synthetic weights N(0,0.02) generated on the device.
 Multi-GPU (torchrun, one process per GPU): every rank samples its own generation (data-parallel
 generations) with no cross-GPU traffic in the timed region; value is the
 steps of all ranks divided by the slowest rank's device time (weak scaling).
+With --cfg-split, ranks 2k and 2k+1 share one generation instead: each runs one CFG arm and the
+pair all-gathers the two flows every step (BASELINE config 3 on 2 GPUs; a latency mode).
 
 --impl reference times the reference's own CPU implementation of the path (the reference's
 src/dit_fwd.cpp built over the scalar kernel transliteration in oracle/_ref; the oracle port when
@@ -50,6 +52,7 @@ def parse():
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--profile-ops", action="store_true", help="print one line per launch of an eager step to stderr")
     ap.add_argument("--no-autotune", action="store_true", help="keep the static tile cost model")
+    ap.add_argument("--cfg-split", action="store_true", help="one CFG arm per rank, pairs of ranks per generation")
     return ap.parse_args()
 
 
@@ -352,10 +355,85 @@ def run_tsn(a):
         dist.destroy_process_group()
 
 
+def run_cfg_split(a):
+    """Pairs of ranks sample one generation each, one CFG arm per rank (tsn.cfg_split)."""
+    import datetime
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import tsn
+    from tsn import cfg_split
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2 or world % 2:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "error": "--cfg-split needs an even number of ranks"}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    pairs = [dist.new_group([2 * k, 2 * k + 1]) for k in range(world // 2)]
+    group, arm = pairs[rank // 2], rank % 2
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dev = tsn.Device(local, stream=stream.cuda_stream)
+        m = tsn.Dit(dev, synthetic=tsn.geom(**geom_kwargs(a)), seed=a.seed)
+        m.prepare(a.T, a.C, a.TS, 1)
+        rng = np.random.default_rng(a.seed + 1000 * (rank // 2))     # one generation per pair
+        f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
+        clip, sync, text, gc, x0 = f(a.C, a.H), f(a.T, a.H), f(2, a.TS, a.H), f(2, a.H), f(a.T, 64)
+        m.set_conditioning(clip, sync, text[arm], gc[arm])
+        m.set_x(x0)
+        if not a.no_autotune:
+            m.autotune()
+        sampler = cfg_split.CfgSplitSampler(m, dev, a.T, group=group)
+        x = torch.from_numpy(x0).cuda()
+        sampler.sample(x, a.warmup, a.cfg)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        sampler.sample(x, a.steps, a.cfg)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        times = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        ms = float(times[0])
+        finite = bool(torch.isfinite(x).all())
+        if rank == 0:
+            flops, wbytes = step_flops_bytes(a)
+            hbm, _, tf_sus, src = peaks()
+            compute_ms = flops / 2 / (tf_sus * 1e12) * 1e3     # each GPU does one arm
+            hbm_ms = wbytes / (hbm * 1e9) * 1e3                 # ... but streams every weight
+            step_ms = ms / a.steps
+            print(json.dumps({
+                "metric": METRIC, "value": (world // 2) * a.steps / (ms * 1e-3), "unit": "steps/s", "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f16 (split hi+lo activations), f32 accumulate",
+                "data": "synthetic",
+                "config": dict(workload(a), parallelism=f"cfg-split x{world // 2} (one CFG arm per GPU, NCCL all-gather "
+                                                        f"of the flow every step)"),
+                "step_roofline": {"compute_ms": compute_ms, "hbm_ms": hbm_ms, "roofline_ms": max(compute_ms, hbm_ms),
+                                  "frac": max(compute_ms, hbm_ms) / step_ms,
+                                  "peaks": f"{src}: {tf_sus} TFLOP/s sustained bf16, {hbm} GB/s"},
+                "x_finite": finite}), flush=True)
+        m.close()
+        dev.close()
+    for g in pairs:
+        dist.destroy_process_group(g)
+    dist.destroy_process_group()
+
+
 def main():
     a = parse()
     if a.impl == "reference":
         run_reference(a)
+    elif a.cfg_split:
+        run_cfg_split(a)
     else:
         run_tsn(a)
 
