@@ -164,8 +164,8 @@ int tsn_dit_kernels_per_step(tsn_dit * m);
  * each launch: out[0] tensor-core GEMM ms, out[1] attention ms, out[2] other ms, out[3] GEMM
  * FLOPs, out[4] GEMM launches. */
 int tsn_dit_profile_step(tsn_dit * m, double * out5);
-/* The same eager forward with one line per launch (name, device ms, TFLOP/s, tile configuration)
- * written into out (NUL-terminated, truncated to cap). */
+/* The same eager forward with one line per launch (name, device ms, TFLOP/s, tile configuration,
+ * algorithmic FLOPs) written into out (NUL-terminated, truncated to cap). */
 int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap);
 
 /* Run the forward up to GEMM launch `op` (index in tsn_dit_profile_ops) and that GEMM once more

@@ -443,7 +443,8 @@ int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap) {
         float ms = 0;
         CKR(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
         const double tf = ops[i].flops > 0 && ms > 0 ? ops[i].flops / (ms * 1e-3) / 1e12 : 0.0;
-        snprintf(line, sizeof line, "%4zu %-14s %8.4f ms %8.1f TF/s  %s\n", i, ops[i].name.c_str(), ms, tf, ops[i].desc.c_str());
+        snprintf(line, sizeof line, "%4zu %-14s %8.4f ms %8.1f TF/s  %s%sflops=%.0f\n", i, ops[i].name.c_str(), ms, tf,
+                 ops[i].desc.c_str(), ops[i].desc.empty() ? "" : " ", ops[i].flops);
         rep += line;
     }
     for (auto & e : ev) cudaEventDestroy(e);
