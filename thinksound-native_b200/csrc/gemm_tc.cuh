@@ -56,6 +56,7 @@ struct GemmArgs {
     long long out_lo;                     // element offset of the lo half of a split f16 output (0: none)
     unsigned long long * trace;           // optional per-CTA phase timestamps (tsn_dit_trace_op), else null
     long long part_stride;                // EPI_F32 split-K without a cluster: K slice z writes out + z*part_stride
+    int m_fast;                           // grid.x walks the M tiles and grid.y the N tiles (else the reverse)
 };
 
 // phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),
@@ -228,8 +229,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     unsigned long long * tr = a.trace ? a.trace + (size_t) cta * TRACE_SLOTS : nullptr;
     if (tr && threadIdx.x == 0) tr[0] = global_ns();
-    const int mt = blockIdx.y % a.m_tiles_t, mb = blockIdx.y / a.m_tiles_t;
-    const int t0 = mt * a.bt, b0 = mb * a.bb, n0 = blockIdx.x * BN;
+    // with m_fast the CTAs that share a weight tile are launched next to each other, so a weight
+    // matrix larger than L2 is streamed from HBM once rather than once per M tile
+    const int mi = a.m_fast ? blockIdx.x : blockIdx.y, ni = a.m_fast ? blockIdx.y : blockIdx.x;
+    const int mt = mi % a.m_tiles_t, mb = mi / a.m_tiles_t;
+    const int t0 = mt * a.bt, b0 = mb * a.bb, n0 = ni * BN;
     const int kb_begin = blockIdx.z * a.kb_per_split;
     const int kb_end = min(a.k_blocks, kb_begin + a.kb_per_split);
     const int nk = kb_end - kb_begin;

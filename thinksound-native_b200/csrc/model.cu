@@ -494,7 +494,8 @@ struct Plan {
         g.split = split;
         g.smem = gemm_smem_bytes(bn_best, split, epi);
         g.ab_bf16 = m.bf16;
-        g.grid = dim3((N + bn_best - 1) / bn_best, mtt * mtb, s_best);
+        g.args.m_fast = 1;
+        g.grid = dim3(mtt * mtb, (N + bn_best - 1) / bn_best, s_best);
         const __half * Alo = (const __half *) A + (size_t) B * rows * K_in;
         if (!make_act_map(&g.ta, A, K_in, rows, B, bt, bb, m.bf16) ||
             (split && !make_act_map(&g.ta2, Alo, K_in, rows, B, bt, bb, m.bf16)) ||
