@@ -84,8 +84,32 @@ size_t gemm_smem_bytes(int bn, bool split, int epi) {
     return 0;
 }
 
+constexpr int persist_stages(int bn) { return bn == 256 ? 3 : 4; }
+size_t gemm_persistent_smem_bytes(int bn) {
+    switch (bn) {
+        case 128: return PersistSmem<128, persist_stages(128)>::TOTAL;
+        case 192: return PersistSmem<192, persist_stages(192)>::TOTAL;
+        case 256: return PersistSmem<256, persist_stages(256)>::TOTAL;
+    }
+    return 0;
+}
+
 namespace {
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs, int);
+
+template <int BN>
+KernelFn pick_persistent() {
+    static_assert(PersistSmem<BN, persist_stages(BN)>::TOTAL <= 232448, "smem budget");
+    return (KernelFn) gemm_tc_persistent<BN, persist_stages(BN)>;
+}
+KernelFn persistent_for(int bn) {
+    switch (bn) {
+        case 128: return pick_persistent<128>();
+        case 192: return pick_persistent<192>();
+        case 256: return pick_persistent<256>();
+    }
+    return nullptr;
+}
 
 template <int BN, int EPI, bool SPLIT>
 KernelFn pick() {
@@ -128,6 +152,11 @@ cudaError_t configure_gemm_kernels() {
                                                      (int) gemm_smem_bytes(bn, split != 0, epi));
                 if (e != cudaSuccess) return e;
             }
+    for (int bn : {128, 192, 256}) {
+        cudaError_t e = cudaFuncSetAttribute((const void *) persistent_for(bn), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int) gemm_persistent_smem_bytes(bn));
+        if (e != cudaSuccess) return e;
+    }
     return cudaSuccess;
 }
 
@@ -137,6 +166,11 @@ bool pdl_enabled() {
 }
 
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
+    if (g.persistent) {
+        KernelFn fn = persistent_for(g.bn);
+        if (!fn || g.epi != EPI_F32 || !g.split || g.args.splits != 1) return cudaErrorInvalidValue;
+        return launch_ex(fn, g.grid, dim3(192), g.smem, s, 1u, g.ta, g.ta2, g.tb, g.args, g.ab_bf16);
+    }
     KernelFn fn = kernel_for(g.bn, g.epi, g.split);
     if (!fn) return cudaErrorInvalidValue;
     // split-K: the K slices of one output tile form a cluster along grid.z

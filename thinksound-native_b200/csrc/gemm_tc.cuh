@@ -115,7 +115,9 @@ __device__ __forceinline__ void store8_split(__half * o, long long lo, const flo
 template <int EPI> struct EpiUnit { static constexpr int U = EPI == EPI_QKV ? 64 : EPI == EPI_SWIGLU ? 64 : 32; };
 
 // TMEM columns for a BN-wide f32 accumulator (allocations are powers of two, at least 32)
-template <int BN> struct TmemCols { static constexpr int N = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256; };
+template <int BN> struct TmemCols {
+    static constexpr int N = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : BN <= 256 ? 256 : 512;
+};
 
 // Epilogue for tile row r, columns [u*U, (u+1)*U) of the tile. load32(c, v) returns the 32
 // accumulated values of columns [c, c+32) of row r (from TMEM, or summed over the cluster's
@@ -391,6 +393,170 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (tr && threadIdx.x == 0) tr[5] = global_ns();
     if (*abort_flag && threadIdx.x == 0) {
         // let TMA copies that were issued but never consumed land before the CTA's smem is reused
+        const uint64_t t1 = global_ns();
+        while (global_ns() - t1 < 20000ull) {}
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// Persistent variant for GEMMs with many more tiles than SMs (the step's latent modulation GEMM,
+// 376 x 131072 x 1024: 2049 tiles). One CTA per SM walks the tiles blockIdx.x, +gridDim.x, ...
+// (M tiles fastest, so the CTAs sharing a weight tile run together); the operand ring runs on
+// across tile boundaries, and two TMEM accumulators let the epilogue of tile i (f32 + bias) overlap
+// the mainloop of tile i+1. Split f16 A operand, f32 output.
+template <int BN, int STAGES>
+struct PersistSmem {
+    static constexpr int A_BYTES = 128 * 128;
+    static constexpr int B_OFF = 2 * A_BYTES;
+    static constexpr int STAGE = 2 * A_BYTES + BN * 128;
+    static constexpr int BAR_OFF = STAGES * STAGE;
+    static constexpr int TOTAL = BAR_OFF + 256 + 1024;   // barriers, TMEM slot, abort flag + alignment slack
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+                   const __grid_constant__ CUtensorMap tmB, const GemmArgs a, const int ab_bf16) {
+    using L = PersistSmem<BN, STAGES>;
+    constexpr int ACC = 256;   // TMEM column offset of the second accumulator
+    static_assert(BN <= ACC, "two accumulators must fit TMEM");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
+    uint64_t * empty = full + STAGES;
+    uint64_t * afull = empty + STAGES;       // [2] accumulator ready for the epilogue
+    uint64_t * aempty = afull + 2;           // [2] accumulator drained (4 arrivals: one per epilogue warp)
+    uint32_t * tslot = (uint32_t *) (aempty + 2);
+    volatile int * abort_flag = (volatile int *) (tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long * tr = a.trace ? a.trace + (size_t) blockIdx.x * TRACE_SLOTS : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
+    const int MT = a.m_tiles_t * ((a.B + a.bb - 1) / a.bb), NT = (a.N + BN - 1) / BN;
+    const int tiles = MT * NT, nk = a.k_blocks;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&afull[b], 1); mbar_init(&aempty[b], 4); }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (threadIdx.x == 0) pdl_trigger();
+    if (warp == 4 && lane == 0) { tma_prefetch(&tmA); tma_prefetch(&tmA2); tma_prefetch(&tmB); }
+    if (warp == 5) tmem_alloc(tslot, 2 * ACC);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    auto tile_coords = [&](int tile, int & t0, int & b0, int & n0) {
+        const int mi = tile % MT, ni = tile / MT;
+        t0 = (mi % a.m_tiles_t) * a.bt;
+        b0 = (mi / a.m_tiles_t) * a.bb;
+        n0 = ni * BN;
+    };
+
+    if (warp == 4) {
+        if (lane == 0) {
+            // the first tile's weight stages do not depend on the upstream kernel
+            int t0, b0, n0;
+            tile_coords(blockIdx.x, t0, b0, n0);
+            const int pre = blockIdx.x < tiles ? (nk < STAGES ? nk : STAGES) : 0;
+            for (int i = 0; i < pre; ++i) {
+                mbar_expect_tx(&full[i], L::STAGE);
+                tma_load_2d(smem + i * L::STAGE + L::B_OFF, &tmB, &full[i], i * 64, n0);
+            }
+            pdl_wait();
+            int g = 0;   // k blocks issued by this CTA so far (ring position)
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x) {
+                tile_coords(tile, t0, b0, n0);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (g >= STAGES && !mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_EMPTY)) {
+                        stop = true;
+                        break;
+                    }
+                    uint8_t * sa = smem + s * L::STAGE;
+                    if (g >= pre) {
+                        mbar_expect_tx(&full[s], L::STAGE);
+                        tma_load_2d(sa + L::B_OFF, &tmB, &full[s], kb * 64, n0);
+                    }
+                    tma_load_3d(sa, &tmA, &full[s], kb * 64, t0, b0);
+                    tma_load_3d(sa + L::A_BYTES, &tmA2, &full[s], kb * 64, t0, b0);
+                }
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(BN, ab_bf16);
+            int g = 0, i = 0;
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x, ++i) {
+                const int buf = i & 1;
+                if (i >= 2 && !mbar_wait(&aempty[buf], ((i >> 1) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_TMEM)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t) (buf * ACC);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (!mbar_wait(&full[s], (g / STAGES) & 1, abort_flag, a.err, DEV_TIMEOUT_FULL)) { stop = true; break; }
+                    if (tr && g == 0) tr[2] = global_ns();
+                    tc_fence_after();
+                    const uint8_t * sa = smem + s * L::STAGE;
+                    const uint64_t ad = umma_desc_sw128(sa), al = umma_desc_sw128(sa + L::A_BYTES),
+                                   bd = umma_desc_sw128(sa + L::B_OFF);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        umma_f16(d, ad + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, (kb | k) != 0);
+                        umma_f16(d, al + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, 1u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (!stop) umma_commit(&afull[buf]);
+            }
+        }
+    } else {
+        pdl_wait();
+        const int r = warp * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        int i = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+            const int buf = i & 1;
+            if (!mbar_wait(&afull[buf], (i >> 1) & 1, abort_flag, a.err, DEV_TIMEOUT_TMEM)) break;
+            tc_fence_after();
+            int t0, b0, n0;
+            tile_coords(tile, t0, b0, n0);
+            const int b = b0 + r / a.bt, t = t0 + r % a.bt;
+            const bool valid = t < a.rows && b < a.B;
+            float * orow = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo;
+#pragma unroll 1
+            for (int c = 0; c < BN; c += 32) {
+                float v[32];
+                tmem_ld32(trow + (uint32_t) (buf * ACC + c), v);
+                const int n = n0 + c;
+                if (!valid || n >= a.N) continue;
+                if (a.bias) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 4) {
+                        const float4 bb = __ldg((const float4 *) (a.bias + n + e));
+                        v[e] += bb.x; v[e + 1] += bb.y; v[e + 2] += bb.z; v[e + 3] += bb.w;
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 32; q += 4) *(float4 *) (orow + n + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+            }
+            // this warp is done reading accumulator `buf`
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&aempty[buf])) : "memory");
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * ACC);
+    }
+    if (tr && threadIdx.x == 0) tr[5] = global_ns();
+    if (*abort_flag && threadIdx.x == 0) {
         const uint64_t t1 = global_ns();
         while (global_ns() - t1 < 20000ull) {}
     }

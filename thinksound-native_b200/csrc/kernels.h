@@ -49,6 +49,7 @@ struct GemmLaunch {
     dim3 grid;
     int bn = 0, epi = 0, ab_bf16 = 0;
     bool split = false;
+    bool persistent = false;      // gemm_tc_persistent (f32 out, split A, one CTA per SM over many tiles)
     size_t smem = 0;
 };
 // Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] 16-bit activation buffer.
@@ -60,6 +61,7 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
 cudaError_t configure_gemm_kernels();
 int gemm_cluster_capacity(int bn, int epi, bool split, int cluster);
 size_t gemm_smem_bytes(int bn, bool split, int epi);
+size_t gemm_persistent_smem_bytes(int bn);   // 0: no persistent kernel for this tile width
 int gemm_stages(int bn, bool split, int epi);
 
 // ---- attention (kernels.cu) ----

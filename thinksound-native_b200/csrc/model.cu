@@ -518,7 +518,8 @@ struct Plan {
     void push(const char * name, const GemmLaunch & g, double flops) {
         char d[160];
         snprintf(d, sizeof d, "bn=%d split=%d ksplit=%u%s grid=%ux%ux%u kb=%d smem=%zu", g.bn, (int) g.split, g.grid.z,
-                 g.args.part_stride ? " partial" : "", g.grid.x, g.grid.y, g.grid.z, g.args.k_blocks, g.smem);
+                 g.args.part_stride ? " partial" : g.persistent ? " persistent" : "", g.grid.x, g.grid.y, g.grid.z,
+                 g.args.k_blocks, g.smem);
         Op op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name, d};
         op.gemm_id = m.gemm_seq++;
         op.shape = last_shape;
@@ -538,6 +539,16 @@ struct Plan {
         int rc = gemm(name, A, K_in, rows, W, pad, EPI_F32, g, plain);
         if (rc) return rc;
         g.args.out = out; g.args.ldo = ldo; g.args.out_bs = (long long) rows * ldo;
+        // many waves of tiles without split-K: one persistent CTA per SM overlaps each tile's
+        // epilogue with the next tile's mainloop
+        const int tiles = (int) (g.grid.x * g.grid.y);
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m.dev->ordinal);
+        if (g.split && g.grid.z == 1 && tiles > 2 * sms && gemm_persistent_smem_bytes(g.bn)) {
+            g.persistent = true;
+            g.smem = gemm_persistent_smem_bytes(g.bn);
+            g.grid = dim3((unsigned) std::min(tiles, sms), 1, 1);
+        }
         push(name, g, fl(m.B, rows, W));
         return TSN_OK;
     }
