@@ -53,7 +53,13 @@ def parse():
     ap.add_argument("--profile-ops", action="store_true", help="print one line per launch of an eager step to stderr")
     ap.add_argument("--no-autotune", action="store_true", help="keep the static tile cost model")
     ap.add_argument("--cfg-split", action="store_true", help="one CFG arm per rank, pairs of ranks per generation")
+    ap.add_argument("--long", action="store_true", help="BASELINE config 4 geometry: 30 s audio (T=704, clip 240, text 77)")
     return ap.parse_args()
+
+
+def apply_long(a):
+    if a.long:
+        a.T, a.C, a.TS = 704, 240, 77
 
 
 def geom_kwargs(a):
@@ -61,8 +67,10 @@ def geom_kwargs(a):
 
 
 def workload(a):
-    return {"workload": f"config2/3: {a.depth}-block MMDiT CFG Euler step ({a.depth - a.fused} joint + {a.fused} fused), "
-                        f"8 s audio geometry, cond+uncond batched",
+    geo = "30 s audio geometry (config 4)" if (a.T, a.C) == (704, 240) else "8 s audio geometry" if a.T == 188 else \
+        f"T={a.T} geometry"
+    return {"workload": f"config{'4' if (a.T, a.C) == (704, 240) else '2/3'}: {a.depth}-block MMDiT CFG Euler step "
+                        f"({a.depth - a.fused} joint + {a.fused} fused), {geo}, cond+uncond batched",
             "T": a.T, "clip_S": a.C, "text_S": a.TS, "H": a.H, "heads": a.H // 64, "F": a.F, "cfg": a.cfg,
             "weights": "synthetic BF16 N(0,0.02) -> f16 operands (reference weight conversion)",
             "l2": "inputs larger than L2: every step streams ~3.1 GB of weights from HBM (L2 126 MB)"}
@@ -469,6 +477,7 @@ def run_cfg_split(a):
 
 def main():
     a = parse()
+    apply_long(a)
     if a.impl == "reference":
         run_reference(a)
     elif a.cfg_split:

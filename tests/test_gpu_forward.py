@@ -139,6 +139,15 @@ def test_wide_forward_taps_vs_oracle(dev, wide_gguf):
     check_taps(m, O.Oracle(wide_gguf), inp, T, C, TS, 0.5)
 
 
+def test_wide_long_context_taps_vs_oracle(dev, wide_gguf):
+    """BASELINE config 4 geometry (30 s: 704 latent rows, 240 clip rows, 77 text rows; joint
+    S = 1021, not a multiple of the 64-row attention tiles), real widths, 2 joint + 1 fused block."""
+    T, C, TS = 704, 240, 77
+    inp = make_inputs(T, C, TS, WIDE["H"], seed=SEED + 3)
+    m = gpu_model(dev, wide_gguf, inp, T, C, TS)
+    check_taps(m, O.Oracle(wide_gguf), inp, T, C, TS, 0.75)
+
+
 def test_single_arm_matches_batched(dev, tiny_gguf):
     """arms=1 (one CFG arm per GPU) gives the same flow as the arms=2 batch."""
     T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
