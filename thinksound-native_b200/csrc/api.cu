@@ -52,6 +52,7 @@ int tsn_device_create(int ordinal, tsn_device ** out) {
     CKR(cudaEventCreate(&d->ctx.ev1));
     CKR(configure_gemm_kernels());
     CKR(configure_attention());
+    CKR(configure_attention_tc());
     *out = d.release();
     return TSN_OK;
 }

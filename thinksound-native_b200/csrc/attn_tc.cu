@@ -1,0 +1,270 @@
+// attn_tc.cu — joint / latent attention on the tcgen05 tensor cores (sm_100a).
+//
+// Replaces attn_qk + softmax_rows + attn_pav (shaders/gemm_attn.metal:96-202) for the DiT path:
+// O = softmax(Q·K^T / 8) · V per (arm, head), head dim 64, no mask, over the joint sequence. The
+// [NH, S, S] f32 probability tensor of the reference never exists.
+//
+// One CTA per (128 query rows, head, arm), 192 threads, two CTAs per SM:
+//   warp 4      TMA: the Q tile (hi and lo halves) once, then K and V 64-key tiles into a
+//               2-stage ring
+//   warp 5      one thread issues the UMMAs: S_j = Qh·Kh^T + Qh·Kl^T + Ql·Kh^T (M 128, N 64,
+//               K 64) into TMEM columns [0, 64), one key tile ahead of the softmax, and
+//               O_j = P_j·Vh + P_j·Vl (M 128, N 64, K 64; V read MN-major) into columns [64, 128)
+//   warps 0-3   one query row per thread: base-2 online softmax in f32 on the row of S_j read
+//               from TMEM, P_j rounded to f16 into a swizzled shared-memory tile (the A operand
+//               of the PV product), running O and row sum in registers, O / l written as the
+//               split f16 attention output of the row's stream.
+// The arithmetic matches attn_kernel (same split products, P in f16, sums of the f32 p).
+// Every mbarrier wait is bounded (ptx.cuh): a stalled pipeline ends the kernel with an error code.
+#include "kernels.h"
+
+namespace tsn {
+
+namespace {
+
+// 2^x by the hardware approximation (relative error ~2^-22, far below the f16 rounding of P)
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+constexpr int Q_BYTES = 128 * 128;              // one half (hi or lo) of the 128 x 64 f16 Q tile
+constexpr int KV_BYTES = 64 * 128;              // one half of a 64 x 64 f16 K or V tile
+constexpr int OFF_Q = 0;                        // Q hi | Q lo
+constexpr int OFF_K = 2 * Q_BYTES;              // [stage][hi | lo]
+constexpr int OFF_V = OFF_K + 4 * KV_BYTES;     // [stage][hi | lo]
+constexpr int OFF_P = OFF_V + 4 * KV_BYTES;     // 128 x 64 f16 probabilities
+constexpr int OFF_BAR = OFF_P + Q_BYTES;
+constexpr int SMEM_TOTAL = OFF_BAR + 256;       // the dynamic window starts 1024-aligned (checked)
+
+__global__ void __launch_bounds__(192, 2)
+attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+               const __grid_constant__ CUtensorMap tv, const AttnArgs a, int * err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long * tr = a.trace ? a.trace + 3 * ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
+    if (smem_u32(smem) & 1023) {   // the swizzled tiles need 1024-byte alignment
+        if (threadIdx.x == 0 && err) atomicCAS(err, 0, DEV_BAD_ARGS);
+        return;
+    }
+    uint64_t * bar = (uint64_t *) (smem + OFF_BAR);
+    uint64_t * q_full = bar;          // Q landed
+    uint64_t * kv_full = bar + 1;     // [2] K and V tile landed
+    uint64_t * kv_empty = bar + 3;    // [2] K and V tile consumed (after PV)
+    uint64_t * s_full = bar + 5;      // S_j in TMEM
+    uint64_t * s_free = bar + 6;      // S_j read by the softmax warps (4 arrivals)
+    uint64_t * p_full = bar + 7;      // P_j in shared memory (4 arrivals)
+    uint64_t * pv_done = bar + 8;     // O_j in TMEM, P buffer free
+    uint32_t * tslot = (uint32_t *) (bar + 9);
+    volatile int * abort_flag = (volatile int *) (tslot + 1);
+
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int head_row = (b * a.NH + h) * a.S_pad;   // first row of this (arm, head) in the q/k/v views
+    const int nkt = (a.S + 63) >> 6;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        mbar_init(p_full, 4);
+        mbar_init(pv_done, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (threadIdx.x == 0) pdl_trigger();
+    if (warp == 4 && lane == 0) { tma_prefetch(&tq); tma_prefetch(&tk); tma_prefetch(&tv); }
+    if (warp == 5) tmem_alloc(tslot, 128);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;          // S at columns [0, 64), O_j at [64, 128)
+
+    if (warp == 4) {
+        if (lane == 0) {
+            pdl_wait();
+            mbar_expect_tx(q_full, 2 * Q_BYTES);
+            tma_load_3d(smem + OFF_Q, &tq, q_full, 0, head_row + qt * 128, 0);
+            tma_load_3d(smem + OFF_Q + Q_BYTES, &tq, q_full, 0, head_row + qt * 128, 1);
+            for (int j = 0; j < nkt; ++j) {
+                const int s = j & 1;
+                if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, abort_flag, err, DEV_TIMEOUT_EMPTY)) break;
+                uint8_t * k = smem + OFF_K + s * 2 * KV_BYTES, * v = smem + OFF_V + s * 2 * KV_BYTES;
+                mbar_expect_tx(&kv_full[s], 4 * KV_BYTES);
+                tma_load_3d(k, &tk, &kv_full[s], 0, head_row + j * 64, 0);
+                tma_load_3d(k + KV_BYTES, &tk, &kv_full[s], 0, head_row + j * 64, 1);
+                tma_load_3d(v, &tv, &kv_full[s], 0, head_row + j * 64, 0);
+                tma_load_3d(v + KV_BYTES, &tv, &kv_full[s], 0, head_row + j * 64, 1);
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t id_s = umma_idesc_f16(64, 0), id_pv = umma_idesc_f16(64, 0, 1);
+            const uint64_t qh = umma_desc_sw128(smem + OFF_Q), ql = umma_desc_sw128(smem + OFF_Q + Q_BYTES);
+            const uint64_t pd = umma_desc_sw128(smem + OFF_P);
+            bool ok = mbar_wait(q_full, 0, abort_flag, err, DEV_TIMEOUT_FULL);
+            auto issue_s = [&](int j) {   // S_j = Qh Kh^T + Qh Kl^T + Ql Kh^T
+                const int s = j & 1;
+                if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) return false;
+                if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) return false;
+                if (tr && j == 0) tr[1] = global_ns();
+                tc_fence_after();
+                const uint8_t * k = smem + OFF_K + s * 2 * KV_BYTES;
+                const uint64_t kh = umma_desc_sw128(k), kl = umma_desc_sw128(k + KV_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t o = (uint64_t) (2 * kk);
+                    umma_f16(tmem, qh + o, kh + o, id_s, kk != 0);
+                    umma_f16(tmem, qh + o, kl + o, id_s, 1u);
+                    umma_f16(tmem, ql + o, kh + o, id_s, 1u);
+                }
+                umma_commit(s_full);
+                return true;
+            };
+            if (ok) ok = issue_s(0);
+            for (int j = 0; j < nkt && ok; ++j) {
+                if (j + 1 < nkt && !issue_s(j + 1)) break;
+                // O_j = P_j (Vh + Vl)
+                if (!mbar_wait(p_full, j & 1, abort_flag, err, DEV_TIMEOUT_FULL)) break;
+                tc_fence_after();
+                const uint8_t * v = smem + OFF_V + (j & 1) * 2 * KV_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t vh = umma_desc_sw128_mn(v + kk * 2048), vl = umma_desc_sw128_mn(v + KV_BYTES + kk * 2048);
+                    umma_f16(tmem + 64, pd + (uint64_t) (2 * kk), vh, id_pv, kk != 0);
+                    umma_f16(tmem + 64, pd + (uint64_t) (2 * kk), vl, id_pv, 1u);
+                }
+                umma_commit(pv_done);
+                umma_commit(&kv_empty[j & 1]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ softmax warps
+        pdl_wait();
+        const int r = warp * 32 + lane;                          // query row within the tile
+        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        uint8_t * prow = smem + OFF_P + r * 128;                 // this row of the swizzled P tile
+        float o[64];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) o[i] = 0.0f;
+        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        bool ok = true;
+        for (int j = 0; j < nkt; ++j) {
+            if (!mbar_wait(s_full, j & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) { ok = false; break; }
+            tc_fence_after();
+            float p[64];
+            tmem_ld32(trow, p);
+            tmem_ld32(trow + 32, p + 32);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);                  // the MMA may overwrite S now
+            // online softmax in base 2 on the scaled logits (scale > 0: max first, scale once);
+            // keys >= S exist only in the last tile
+            if (j * 64 + 64 > a.S) {
+#pragma unroll
+                for (int e = 0; e < 64; ++e)
+                    if (j * 64 + e >= a.S) p[e] = -INFINITY;
+            }
+            float mx = p[0];
+#pragma unroll
+            for (int e = 1; e < 64; ++e) mx = fmaxf(mx, p[e]);
+            const float mn = fmaxf(m, mx * a.scale_log2);
+            const float alpha = ex2(m - mn);
+            m = mn;
+            float ps = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 64; ++e) {
+                p[e] = ex2(fmaf(p[e], a.scale_log2, -mn));
+                ps += p[e];
+            }
+            l = l * alpha + ps;
+            // PV_{j-1} done: the P buffer is free and O_{j-1} is in TMEM
+            if (j >= 1) {
+                if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) { ok = false; break; }
+                tc_fence_after();
+            }
+            // P_j as f16 into the swizzled tile: 16-byte chunk c of row r at chunk c ^ (r & 7)
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                __align__(16) __half hv[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(p[8 * c + e]);
+                *(uint4 *) (prow + ((c ^ (r & 7)) << 4)) = *(const uint4 *) hv;
+            }
+            // fold O_{j-1} = O_{j-2} * alpha_{j-1} + P_{j-1} V_{j-1} before PV_j may overwrite it
+            if (j >= 1) {
+#pragma unroll
+                for (int c = 0; c < 64; c += 32) {
+                    float ot[32];
+                    tmem_ld32(trow + 64 + c, ot);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[c + e] = o[c + e] * alpha_prev + ot[e];
+                }
+            }
+            alpha_prev = alpha;
+            fence_proxy_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+        }
+        if (ok && mbar_wait(pv_done, (nkt - 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) {
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 64; c += 32) {
+                float ot[32];
+                tmem_ld32(trow + 64 + c, ot);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o[c + e] = o[c + e] * alpha_prev + ot[e];
+            }
+            const int s_row = qt * 128 + r;
+            if (s_row < a.S) {
+                __half * dst;
+                long long olo;
+                if (s_row < a.n0) { dst = a.out0 + ((size_t) b * a.n0 + s_row) * a.H; olo = a.out_lo0; }
+                else if (s_row < a.n0 + a.n1) { dst = a.out1 + ((size_t) b * a.n1 + (s_row - a.n0)) * a.H; olo = a.out_lo1; }
+                else { dst = a.out2 + ((size_t) b * a.n2 + (s_row - a.n0 - a.n1)) * a.H; olo = a.out_lo2; }
+                dst += h * 64;
+                const float inv = 1.0f / l;
+#pragma unroll
+                for (int c = 0; c < 64; c += 8) {
+                    __align__(16) __half hv[8], lv[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float v = o[c + e] * inv;
+                        hv[e] = __float2half_rn(v);
+                        lv[e] = __float2half_rn(v - __half2float(hv[e]));
+                    }
+                    *(uint4 *) (dst + c) = *(const uint4 *) hv;
+                    if (olo) *(uint4 *) (dst + olo + c) = *(const uint4 *) lv;
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 128);
+    }
+    if (tr && threadIdx.x == 0) tr[2] = global_ns();
+    if (*abort_flag && threadIdx.x == 0) {
+        // let TMA copies that were issued but never consumed land before the CTA's smem is reused
+        const uint64_t t1 = global_ns();
+        while (global_ns() - t1 < 20000ull) {}
+    }
+}
+
+} // namespace
+
+cudaError_t configure_attention_tc() {
+    return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL);
+}
+
+cudaError_t launch_attention_tc(const AttnMaps & m, const AttnArgs & a, cudaStream_t s) {
+    return launch_ex(attn_tc_kernel, dim3((a.S + 127) / 128, a.NH, a.B), dim3(192), SMEM_TOTAL, s, 1u, m.q, m.k, m.v, a,
+                     a.err);
+}
+
+} // namespace tsn

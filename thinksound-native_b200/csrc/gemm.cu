@@ -38,6 +38,17 @@ bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t ro
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows) {
+    if (!encoder() || ((uintptr_t) base & 15) || box_rows > 256) return false;
+    const cuuint64_t dims[3] = {64, rows, 2};
+    const cuuint64_t strides[2] = {128, rows * 128};
+    const cuuint32_t box[3] = {64, box_rows, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void *) base, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16) {
     if (!encoder() || ((uintptr_t) base & 15) || (K % 64) || bn > 256) return false;
     const cuuint64_t dims[2] = {K, N};

@@ -55,6 +55,9 @@ struct GemmLaunch {
 // Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] 16-bit activation buffer.
 bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t rows, uint64_t B,
                   uint32_t bt, uint32_t bb, int bf16);
+// Encode a 3-D TMA view {64, rows, 2} of a head-major [hi|lo][rows][64] f16 q/k/v buffer with a
+// {64, box_rows, 1} box (rows = B * NH * S_pad).
+bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows);
 // Encode a 2-D TMA view {K, N} of an [N][K] 16-bit weight matrix with a {64, bn} box.
 bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16);
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
@@ -75,9 +78,14 @@ struct AttnArgs {
     long long qkv_lo;                                        // element offset of the lo halves of q, k, v
     long long out_lo0, out_lo1, out_lo2;                     // ... and of each output (0: hi only)
     unsigned long long * trace;                              // optional per-CTA stamps (entry, upstream done, exit)
+    int * err;                                               // device error word (attn_tc_kernel)
 };
 cudaError_t configure_attention();
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s);
+// tcgen05 attention (attn_tc.cu): q/k/v read through TMA views made by make_head_map
+struct AttnMaps { CUtensorMap q, k, v; };
+cudaError_t configure_attention_tc();
+cudaError_t launch_attention_tc(const AttnMaps & m, const AttnArgs & a, cudaStream_t s);
 
 // ---- adaLN LayerNorm + modulation -> f16 GEMM operand ----
 struct AdaLnArgs {

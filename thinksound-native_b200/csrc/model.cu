@@ -617,21 +617,34 @@ struct Plan {
         op.trace_slots = 3;
         add(op);
     }
-    void attention(int S, int n0, int n1, int n2) {
+    int attention(int S, int n0, int n1, int n2) {
         const long long H = m.g.H;
         AttnArgs a{m.q, m.k, m.v, m.B, (int) m.g.NH, S, m.S_pad, 0.125f * 1.4426950408889634f,
                    m.att_l, m.att_c, m.att_t, n0, n1, n2, (int) m.g.H,
                    (long long) m.B * m.g.NH * m.S_pad * 64, m.B * m.T * H, m.B * m.C * H, m.B * m.TS * H};
+        a.err = m.dev->d_err;
         const double flops = 4.0 * m.B * (double) S * S * m.g.H;
-        Op op{[a](cudaStream_t s) { return launch_attention(a, s); }, 1, flops, "attention"};
-        op.traced = [a](cudaStream_t s, unsigned long long * tr) {
+        // Long sequences run on the tcgen05 kernel (attn_tc.cu, 128 query rows per CTA, TMA views of
+        // q/k/v [hi|lo][B*NH*S_pad][64]); below 256 rows its 128-row tiles leave most SMs idle and
+        // the 64-row mma.sync kernel (attn_kernel) is faster (measured: S 188: 9.2 vs 9.7 us;
+        // S 329: 16.2 vs 12.2 us; S 1021: 77.6 vs 34.0 us).
+        const uint64_t rows = (uint64_t) m.B * m.g.NH * m.S_pad;
+        AttnMaps mp{};
+        const bool tc = S >= 256;
+        if (tc && !(make_head_map(&mp.q, m.q, rows, 128) && make_head_map(&mp.k, m.k, rows, 64) &&
+                    make_head_map(&mp.v, m.v, rows, 64)))
+            return fail(TSN_ERR_CUDA, "attention: tensor map encode failed");
+        Op op{[a, mp, tc](cudaStream_t s) { return tc ? launch_attention_tc(mp, a, s) : launch_attention(a, s); }, 1, flops,
+              "attention"};
+        op.traced = [a, mp, tc](cudaStream_t s, unsigned long long * tr) {
             AttnArgs t = a;
             t.trace = tr;
-            return launch_attention(t, s);
+            return tc ? launch_attention_tc(mp, t, s) : launch_attention(t, s);
         };
-        op.ctas = ((S + 63) / 64) * (int) m.g.NH * m.B;
+        op.ctas = tc ? ((S + 127) / 128) * (int) m.g.NH * m.B : ((S + 63) / 64) * (int) m.g.NH * m.B;
         op.trace_slots = 3;
         add(op);
+        return TSN_OK;
     }
     // post_attn (src/dit_fwd.cpp:51-81) for one stream, all arms
     int post(const Blk & b, float * x, const __half * att, __half * xn, __half * h, int rows, const float * mod,
@@ -775,7 +788,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
                       });
             }
         }
-        p.attention(S, T, C, TS);
+        if ((rc = p.attention(S, T, C, TS))) return rc;
         const int ea = p.record();
         if ((rc = p.post(jl[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs))) return rc;
         if (!pre_only) {
@@ -828,7 +841,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         const float * ml = modl + mod_off[NJ + i];
         p.adaln("adaln_attn", lat, T, ml, 1, NA, lat_mod_bs, 0, xn_l);
         if ((rc = p.qkv("qkv_lat", xn_l, T, fb[i], 0, rope_l))) return rc;
-        p.attention(T, T, 0, 0);
+        if ((rc = p.attention(T, T, 0, 0))) return rc;
         if ((rc = p.post(fb[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs))) return rc;
     }
     if (tp) {

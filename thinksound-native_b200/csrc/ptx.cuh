@@ -120,13 +120,36 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void * smem_tile) {
     return d;
 }
 
+// Same, MN-major (the N index contiguous in 128-byte rows, one row per K index), for an operand whose
+// N extent is one 64-element swizzle atom: 8-row groups along K are 1024 B apart (SBO); a K step of
+// 16 advances the start address by 2048 B.
+__device__ __forceinline__ uint64_t umma_desc_sw128_mn(const void * smem_tile) {
+    const uint32_t a = smem_u32(smem_tile);
+    uint64_t d = 0;
+    d |= (uint64_t) ((a & 0x3FFFFu) >> 4);          // start address
+    d |= (uint64_t) 1u << 16;                        // LBO (one atom along N: unused)
+    d |= (uint64_t) (1024u >> 4) << 32;              // SBO = 1024 B between 8-row groups along K
+    d |= (uint64_t) 1u << 46;                        // descriptor version (sm100)
+    d |= (uint64_t) 2u << 61;                        // SWIZZLE_128B
+    return d;
+}
+
 // Instruction descriptor, kind::f16: f32 accumulate, A/B both f16 (ab_bf16=0) or both bf16 (1),
-// both K-major, M=128, N=n.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int n, int ab_bf16) {
+// A K-major, B K-major (b_mn = 0) or MN-major (1), M=128, N=n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n, int ab_bf16, int b_mn = 0) {
     return (1u << 4)                                   // D format f32
          | ((uint32_t) ab_bf16 << 7) | ((uint32_t) ab_bf16 << 10)
+         | ((uint32_t) b_mn << 16)                     // B major-ness
          | ((uint32_t) (n >> 3) << 17)
          | ((uint32_t) (128 >> 4) << 24);
+}
+
+// make this thread's generic-proxy shared-memory writes visible to the async proxy (tcgen05.mma)
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// plain arrive on a CTA-local mbarrier
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 // 32 lanes x 32 consecutive f32 columns from TMEM into registers (one row per thread).
