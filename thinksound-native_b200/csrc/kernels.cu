@@ -253,13 +253,13 @@ __global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
     if (a.part) {
         const float * g = a.gmod + (long long) b * a.gmod_bs + (a.gper_row ? (long long) t * a.gmod_ld : 0) + a.goff;
         const float * p = a.part + (long long) b * a.x_bs + (long long) t * a.H;
-        float4 acc[NV], pz[NV][7], gg[NV], bb[NV];
+        float4 acc[NV], pz[NV][MAX_PARTS - 1], gg[NV], bb[NV];
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
             const int c = (i * TPR + tid) * 4;
             acc[i] = __ldcg((const float4 *) (p + c));
 #pragma unroll
-            for (int z = 1; z < 8; ++z)
+            for (int z = 1; z < MAX_PARTS; ++z)
                 if (z < a.nsplit) pz[i][z - 1] = __ldcg((const float4 *) (p + z * a.part_stride + c));
             gg[i] = __ldg((const float4 *) (g + c));
             bb[i] = a.pbias ? __ldg((const float4 *) (a.pbias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -267,7 +267,7 @@ __global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
 #pragma unroll
         for (int i = 0; i < NV; ++i) {
 #pragma unroll
-            for (int z = 1; z < 8; ++z)
+            for (int z = 1; z < MAX_PARTS; ++z)
                 if (z < a.nsplit) {
                     acc[i].x += pz[i][z - 1].x; acc[i].y += pz[i][z - 1].y;
                     acc[i].z += pz[i][z - 1].z; acc[i].w += pz[i][z - 1].w;
@@ -339,7 +339,7 @@ int adaln_threads(int H) {
 
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s) {
     const int tpr = adaln_threads(a.H);
-    if (!tpr || (a.part && (a.nsplit < 1 || a.nsplit > 8))) return cudaErrorInvalidValue;
+    if (!tpr || (a.part && (a.nsplit < 1 || a.nsplit > MAX_PARTS))) return cudaErrorInvalidValue;
     const dim3 grid(a.B * a.rows);
     switch (a.H / 4 / tpr) {
         case 1: return launch_ex(adaln_kernel<1>, grid, dim3(tpr), 0, s, 1u, a);

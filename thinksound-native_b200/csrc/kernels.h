@@ -88,6 +88,7 @@ cudaError_t configure_attention_tc();
 cudaError_t launch_attention_tc(const AttnMaps & m, const AttnArgs & a, cudaStream_t s);
 
 // ---- adaLN LayerNorm + modulation -> f16 GEMM operand ----
+constexpr int MAX_PARTS = 12;   // most split-K partial tiles a gated GEMM leaves for the next adaLN
 struct AdaLnArgs {
     float * x; long long x_bs;              // [B][rows][H] f32 residual stream
     const float * mod; long long mod_bs, mod_ld; int per_row, base;   // shift at base, scale at base + H

@@ -359,9 +359,9 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
     ALLOC(att_l, 2 * B * T * H * 2);   // hi | lo
     ALLOC(att_c, 2 * B * C * H * 2);   // hi | lo
     ALLOC(att_t, 2 * B * TS * H * 2);   // hi | lo
-    ALLOC(part_l, 8 * B * T * H * 4);   // split-K partial sums of the gated GEMMs, up to 8 K slices
-    ALLOC(part_c, 8 * B * C * H * 4);
-    ALLOC(part_t, 8 * B * TS * H * 4);
+    ALLOC(part_l, MAX_PARTS * B * T * H * 4);   // split-K partial sums of the gated GEMMs
+    ALLOC(part_c, MAX_PARTS * B * C * H * 4);
+    ALLOC(part_t, MAX_PARTS * B * TS * H * 4);
     ALLOC(h_l, B * T * F * 2);
     ALLOC(h_c, B * C * F * 2);
     ALLOC(h_t, B * TS * F * 2);
@@ -461,6 +461,7 @@ struct Plan {
         if (K_in % 64 || kb < 1) return fail(TSN_ERR_ARG, std::string(name) + ": K not a multiple of 64");
         double best = 1e30;
         int bn_best = 0, s_best = 1;
+        const int smax = partial ? MAX_PARTS : 8;   // clusters hold at most 8 CTAs portably
         // tile widths that do not divide N leave the last column tile partly empty (its TMA rows
         // beyond N read zeros and its epilogue skips those columns)
         for (int bn : {256, 192, 128, 64}) {
@@ -468,8 +469,9 @@ struct Plan {
             const double kcost = split ? (bn == 256 ? 0.74 : bn == 192 ? 0.57 : bn == 128 ? 0.40 : 0.30)
                                        : (bn == 256 ? 0.37 : bn == 192 ? 0.30 : bn == 128 ? 0.24 : 0.18);
             const int tiles = mtt * mtb * ((N + bn - 1) / bn);
+            // the cost model searches up to 8 K slices; the autotuner also times up to MAX_PARTS
             for (int s = 1; s <= 8 && s <= kb; ++s) {
-                if (!splits_valid(kb, s)) continue;
+                if (!splits_valid(kb, s, smax)) continue;
                 const int kbps = (kb + s - 1) / s;
                 const int cap = partial ? gemm_cluster_capacity(bn, epi, split, 1) : gemm_cluster_capacity(bn, epi, split, s);
                 if (cap <= 0) continue;
@@ -480,7 +482,7 @@ struct Plan {
         }
         if (!bn_best) return fail(TSN_ERR_ARG, std::string(name) + ": no tile fits N=" + std::to_string(N));
         auto fo = m.gemm_force.find(m.gemm_seq);
-        if (fo != m.gemm_force.end() && splits_valid(kb, fo->second.second) &&
+        if (fo != m.gemm_force.end() && splits_valid(kb, fo->second.second, smax) &&
             (fo->second.first == 192 || N % fo->second.first == 0)) {
             bn_best = fo->second.first;
             s_best = fo->second.second;
@@ -510,8 +512,8 @@ struct Plan {
         return TSN_OK;
     }
     // every one of the s K-slices gets at least one 64-wide K block
-    static bool splits_valid(int kb, int s) {
-        if (s < 1 || s > 8 || s > kb) return false;
+    static bool splits_valid(int kb, int s, int smax) {
+        if (s < 1 || s > smax || s > kb) return false;
         const int kbps = (kb + s - 1) / s;
         return (kb + kbps - 1) / kbps == s;
     }
@@ -976,7 +978,7 @@ int Model::autotune(std::string & report) {
         std::pair<int, int> bc{0, 0};
         std::string tried;
         for (int bn : {256, 192, 128, 64})
-            for (int sp = 1; sp <= 8; ++sp) {
+            for (int sp = 1; sp <= MAX_PARTS; ++sp) {
                 gemm_force.clear();
                 gemm_force[gid] = {bn, sp};
                 std::vector<Op> tmp;

@@ -93,7 +93,7 @@ struct Model {
     float * modl = nullptr, * modc = nullptr, * modt = nullptr, * flow = nullptr;   // modl: [B][T][N_all]
     __half * x16 = nullptr, * extc16 = nullptr, * xn_l = nullptr, * xn_c = nullptr, * xn_t = nullptr;
     __half * att_l = nullptr, * att_c = nullptr, * att_t = nullptr, * h_l = nullptr, * h_c = nullptr, * h_t = nullptr;
-    float * part_l = nullptr, * part_c = nullptr, * part_t = nullptr;   // [8][B][rows][H] split-K partials
+    float * part_l = nullptr, * part_c = nullptr, * part_t = nullptr;   // [MAX_PARTS][B][rows][H] split-K partials
     __half * q = nullptr, * k = nullptr, * v = nullptr;
     float2 * rope_l = nullptr, * rope_c = nullptr;
     float * temb_tab = nullptr, * dt_tab = nullptr;
