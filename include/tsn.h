@@ -136,6 +136,20 @@ int tsn_dit_prepare(tsn_dit * m, uint32_t T, uint32_t clip_S, uint32_t text_S, u
 int tsn_dit_set_conditioning(tsn_dit * m, const float * clip_pp, const float * sync_gather,
                              const float * text_pp, const float * gcmlp);
 /* Latent x [T,64] (any-pointer in / out). */
+/* Read back the model's conditioning buffers (the layouts of tsn_dit_set_conditioning); any
+ * pointer may be null to skip that buffer. */
+int tsn_dit_get_conditioning(tsn_dit * m, float * clip_pp, float * sync_gather, float * text_pp, float * gcmlp);
+/* DitModel::prep_conditioning (src/dit.cpp:55-135) on the GPU for the prepared geometry:
+ * clip_f [C][1024] (C = the prepared clip rows) and sync_f [sync_S][768] f32, host or device
+ * pointers. Writes the model's clip_pp and sync_gather and keeps clip_fc for the text arms.
+ * Needs the once-per-generation conditioning weights in the model's source (loaded on first use)
+ * and H = 1024. */
+int tsn_dit_prep_conditioning(tsn_dit * m, const float * clip_f, const float * sync_f, int sync_S);
+/* DitModel::prep_text_arm (src/dit.cpp:137-192) for CFG arm `arm` (< the prepared arms):
+ * text_cat [TS][2048] and gtext [1024] f32 -> the model's text_pp[arm] and gcmlp[arm].
+ * After tsn_dit_prep_conditioning; together they replace tsn_dit_set_conditioning. */
+int tsn_dit_prep_text_arm(tsn_dit * m, int arm, const float * text_cat, const float * gtext);
+
 int tsn_dit_set_x(tsn_dit * m, const float * x);
 int tsn_dit_get_x(tsn_dit * m, float * x_out);
 

@@ -41,6 +41,7 @@ class Oracle:
         L.oracle_forward.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, C.c_float, _F, _F, _F, _F, _F, C.c_int]
         L.oracle_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, C.c_float, C.c_float, C.c_float,
                                   _F, _F, _F, _F, _F, _F, _F, _F]
+        L.oracle_prep.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int] + [_F] * 12
         L.oracle_tap.restype = C.c_longlong
         L.oracle_tap.argtypes = [C.c_void_p, C.c_char_p, _F, C.c_longlong]
         self.h = L.oracle_load(gguf.encode())
@@ -80,6 +81,22 @@ class Oracle:
         a = [np.ascontiguousarray(v, dtype=np.float32) for v in (clip_pp, sync_gather, tp_c, gc_c, tp_u, gc_u)]
         self.L.oracle_step(self.h, T, C_, TS, _f(x), t, cfg, dt, *[_f(v) for v in a], _f(fc), _f(fu))
         return x, fc, fu
+
+    def prep(self, T, C_, TS, sync_S, clip_f, sync_f, text_cat_c, gtext_c, text_cat_u, gtext_u):
+        """prep_conditioning + prep_text_arm (src/dit.cpp:55-192) for both arms; needs H = 1024.
+        Returns a dict of PREP_OUT arrays."""
+        H = self.H
+        out = {"clip_pp": np.zeros((C_, H), np.float32), "sync_gather": np.zeros((T, H), np.float32),
+               "text_pp_cond": np.zeros((TS, H), np.float32), "gcmlp_cond": np.zeros(H, np.float32),
+               "text_pp_unc": np.zeros((TS, H), np.float32), "gcmlp_unc": np.zeros(H, np.float32)}
+        a = [np.ascontiguousarray(v, dtype=np.float32) for v in (clip_f, sync_f, text_cat_c, gtext_c, text_cat_u, gtext_u)]
+        rc = self.L.oracle_prep(self.h, T, C_, TS, sync_S, *[_f(v) for v in a], *[_f(out[k]) for k in PREP_OUT])
+        if rc != 0:
+            raise RuntimeError("oracle_prep needs a model with H = 1024")
+        return out
+
+
+PREP_OUT = ("clip_pp", "sync_gather", "text_pp_cond", "gcmlp_cond", "text_pp_unc", "gcmlp_unc")
 
 
 def have_ref() -> bool:

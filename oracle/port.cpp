@@ -444,9 +444,106 @@ struct Fwd {
     }
 };
 
+// ------------------------------------------------------------------------------------------
+// Per-generation conditioning: DitModel::prep_conditioning (src/dit.cpp:55-135) and
+// DitModel::prep_text_arm (src/dit.cpp:137-192), with convmlp / mlp of src/dit.cpp:14-27.
+// ------------------------------------------------------------------------------------------
+struct Prep {
+    Model & m;
+    Rt rt;
+    std::vector<float> h1, h3;
+    std::vector<float> clip_fc;                                   // DitModel::clip_fc_host
+
+    explicit Prep(Model & model) : m(model) {}
+
+    // convmlp (src/dit.cpp:14-20): conv k3 w1, w3 -> swiglu -> conv k3 w2; y may alias x
+    void convmlp(const std::string & pre, const float * x, float * y, uint32_t T, uint32_t C) {
+        const uint32_t F = m.H_ffn;
+        h1.assign((size_t) T * F, 0.0f);
+        h3.assign((size_t) T * F, 0.0f);
+        rt.conv(m.W(pre + ".w1.weight"), nullptr, x, h1.data(), T, C, F, 3, 1, 1);
+        rt.conv(m.W(pre + ".w3.weight"), nullptr, x, h3.data(), T, C, F, 3, 1, 1);
+        rt.swiglu(h1.data(), h3.data(), h1.data(), (size_t) T * F);
+        rt.conv(m.W(pre + ".w2.weight"), nullptr, h1.data(), y, T, F, C, 3, 1, 1);
+    }
+    // mlp (src/dit.cpp:21-27)
+    void mlp(const std::string & pre, const float * x, float * y, uint32_t rows, uint32_t C) {
+        const uint32_t F = m.H_ffn;
+        h1.assign((size_t) rows * F, 0.0f);
+        h3.assign((size_t) rows * F, 0.0f);
+        rt.gemm(m.W(pre + ".w1.weight"), x, h1.data(), nullptr, rows, F, C);
+        rt.gemm(m.W(pre + ".w3.weight"), x, h3.data(), nullptr, rows, F, C);
+        rt.swiglu(h1.data(), h3.data(), h1.data(), (size_t) rows * F);
+        rt.gemm(m.W(pre + ".w2.weight"), h1.data(), y, nullptr, rows, C, F);
+    }
+    // src/dit.cpp:91-133
+    void conditioning(uint32_t T, uint32_t clip_S, uint32_t sync_S, const float * clip_f, const float * sync_f,
+                      float * clip_pp, float * sync_gather) {
+        const uint32_t H = m.H;
+        // sync: + sync_pos_emb per 8-frame segment (host f32), conv k7, silu, convmlp, gather to T
+        auto pit = m.file.tensors.find("sync_pos_emb");
+        const std::vector<float> spe = pit == m.file.tensors.end() ? std::vector<float>() : to_f32(pit->second);
+        std::vector<float> sbuf(sync_f, sync_f + (size_t) sync_S * 768);
+        for (uint32_t s = 0; s < sync_S && !spe.empty(); ++s)
+            for (int c = 0; c < 768; ++c) sbuf[(size_t) s * 768 + c] += spe[(size_t) (s % 8) * 768 + c];
+        std::vector<float> smid((size_t) sync_S * H, 0.0f);
+        rt.conv(m.W("sync_input_proj.0.weight"), (const float *) m.W("sync_input_proj.0.bias"), sbuf.data(), smid.data(),
+                sync_S, 768, H, 7, 3, 1);
+        rt.silu(smid.data(), (size_t) sync_S * H);
+        convmlp("sync_input_proj.2", smid.data(), smid.data(), sync_S, H);
+        for (uint32_t i = 0; i < T; ++i) {
+            const int32_t si = (int32_t) floorf(((float) i + 0.5f) * (float) sync_S / (float) T);
+            memcpy(sync_gather + (size_t) i * H, smid.data() + (size_t) si * H, (size_t) H * 4);
+        }
+        // clip: linear + silu + convmlp -> clip_pp
+        rt.gemm(m.W("clip_input_proj.0.weight"), clip_f, clip_pp, (const float *) m.W("clip_input_proj.0.bias"), clip_S, H,
+                1024);
+        rt.silu(clip_pp, (size_t) clip_S * H);
+        convmlp("clip_input_proj.2", clip_pp, clip_pp, clip_S, H);
+        // clip_fc = clip_cond_proj(mean over clip rows)
+        std::vector<float> cmean(H, 0.0f);
+        SH sh{clip_S, H};
+        mean_cols(clip_pp, cmean.data(), sh);
+        clip_fc.assign(H, 0.0f);
+        rt.gemv(m.W("clip_cond_proj.weight"), cmean.data(), clip_fc.data(), (const float *) m.W("clip_cond_proj.bias"), H,
+                1024, 1024);
+    }
+    // src/dit.cpp:137-192
+    void text_arm(uint32_t text_S, const float * text_cat, const float * gtext, float * text_pp, float * gcmlp) {
+        const uint32_t H = m.H, F = m.H_ffn;
+        rt.gemm(m.W("text_input_proj.0.weight"), text_cat, text_pp, (const float *) m.W("text_input_proj.0.bias"), text_S, H,
+                2048);
+        rt.silu(text_pp, (size_t) text_S * H);
+        std::vector<float> f1((size_t) text_S * F, 0.0f), f3((size_t) text_S * F, 0.0f);
+        rt.gemm(m.W("text_input_proj.2.w1.weight"), text_pp, f1.data(), nullptr, text_S, F, H);
+        rt.gemm(m.W("text_input_proj.2.w3.weight"), text_pp, f3.data(), nullptr, text_S, F, H);
+        rt.swiglu(f1.data(), f3.data(), f1.data(), (size_t) text_S * F);
+        rt.gemm(m.W("text_input_proj.2.w2.weight"), f1.data(), text_pp, nullptr, text_S, H, F);
+        std::vector<float> tfc(H, 0.0f);
+        rt.gemv(m.W("text_cond_proj.weight"), gtext, tfc.data(), (const float *) m.W("text_cond_proj.bias"), H, 1024, 1024);
+        for (uint32_t i = 0; i < H; ++i) tfc[i] += clip_fc[i];                 // host f32 add (dit.cpp:186-187)
+        mlp("global_cond_mlp", tfc.data(), gcmlp, 1, H);
+    }
+};
+
 } // namespace
 
 extern "C" {
+
+// prep_conditioning + prep_text_arm for both CFG arms (needs H = 1024: the clip and text cond
+// projections read 1024 inputs, src/dit.cpp:130-131, 181-182).
+int oracle_prep(void * h, int T, int C, int TS, int sync_S, const float * clip_f, const float * sync_f,
+                const float * text_cat_c, const float * gtext_c, const float * text_cat_u, const float * gtext_u,
+                float * clip_pp, float * sync_gather, float * text_pp_c, float * gcmlp_c, float * text_pp_u,
+                float * gcmlp_u) {
+    Model * m = (Model *) h;
+    if (m->H != 1024) return -1;
+    Prep p(*m);
+    p.conditioning((uint32_t) T, (uint32_t) C, (uint32_t) sync_S, clip_f, sync_f, clip_pp, sync_gather);
+    p.text_arm((uint32_t) TS, text_cat_c, gtext_c, text_pp_c, gcmlp_c);
+    p.text_arm((uint32_t) TS, text_cat_u, gtext_u, text_pp_u, gcmlp_u);
+    return 0;
+}
 
 void * oracle_load(const char * gguf_path) {
     auto * m = new Model();

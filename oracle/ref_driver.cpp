@@ -9,6 +9,11 @@
 //       cond, forward uncond, Runtime::cfg_euler. Writes x_out.bin; prints a JSON timing line.
 //   ts_ref_dit sample <gguf> <T> <C> <TS> <in_dir> <out_dir> <steps> <cfg>
 //       the Euler loop of src/pipeline.cpp:142-155 from the given x; writes x_final.bin.
+//   ts_ref_dit prep <gguf> <T> <C> <TS> <in_dir> <out_dir> <sync_S>
+//       DitModel::prep_conditioning (src/dit.cpp:55-135) on clip_f.bin [C,1024] and sync_f.bin
+//       [sync_S,768], then DitModel::prep_text_arm (src/dit.cpp:137-192) on text_cat_<arm>.bin
+//       [TS,2048] and gtext_<arm>.bin [1024] for arm = cond, unc; writes clip_pp.bin,
+//       sync_gather.bin, text_pp_<arm>.bin, gcmlp_<arm>.bin.
 //
 // Inputs in <in_dir> (f32, row-major): x.bin [T,64], clip_pp.bin [C,H], sync_gather.bin [T,H],
 // text_pp_cond.bin / text_pp_unc.bin [TS,H], gcmlp_cond.bin / gcmlp_unc.bin [H].
@@ -87,6 +92,27 @@ int main(int argc, char ** argv) {
     if (!rt.init("")) return 1;
     DitModel dit;
     if (!dit.load(rt, gguf)) { fprintf(stderr, "dit load failed\n"); return 1; }
+    if (mode == "prep") {
+        if (argc < 9) { fprintf(stderr, "prep needs <sync_S>\n"); return 2; }
+        const uint32_t sync_S = (uint32_t) atoi(argv[8]), H = dit.H;
+        dit.text_S = TS;
+        gpu::Buf clip_f = rt.dev.alloc((size_t) C * 1024 * 4), sync_f = rt.dev.alloc((size_t) sync_S * 768 * 4);
+        if (!read_into(in + "/clip_f.bin", clip_f, (size_t) C * 1024) ||
+            !read_into(in + "/sync_f.bin", sync_f, (size_t) sync_S * 768)) return 1;
+        if (!dit.prep_conditioning(rt, clip_f, sync_f, T, C, sync_S)) { fprintf(stderr, "prep failed\n"); return 1; }
+        write_from(out + "/clip_pp.bin", dit.clip_pp.p, (size_t) C * H);
+        write_from(out + "/sync_gather.bin", dit.sync_gather.p, (size_t) T * H);
+        for (const char * arm : {"cond", "unc"}) {
+            gpu::Buf tc = rt.dev.alloc((size_t) TS * 2048 * 4), gt = rt.dev.alloc(1024 * 4);
+            gpu::Buf tp = rt.dev.alloc((size_t) TS * H * 4), gc = rt.dev.alloc(H * 4);
+            if (!read_into(in + "/text_cat_" + arm + ".bin", tc, (size_t) TS * 2048) ||
+                !read_into(in + "/gtext_" + arm + ".bin", gt, 1024)) return 1;
+            dit.prep_text_arm(rt, tc, gt, tp, gc);
+            write_from(out + "/text_pp_" + std::string(arm) + ".bin", tp.p, (size_t) TS * H);
+            write_from(out + "/gcmlp_" + std::string(arm) + ".bin", gc.p, H);
+        }
+        return 0;
+    }
     dit.T = T; dit.clip_S = C; dit.text_S = TS; dit.sync_S = 0;
     if (!alloc_forward_buffers(rt, dit)) { fprintf(stderr, "alloc failed\n"); return 1; }
     const uint32_t H = dit.H, L = dit.latent_dim;

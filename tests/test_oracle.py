@@ -139,3 +139,38 @@ def test_synthetic_values_match_independent_restatement(tiny_gguf):
     got = read_tensor(tiny_gguf, "joint_blocks.0.latent_block.attn.q_norm.weight", 16)
     want = np.array([np.float32(1.0) + _normal(key, i) * np.float32(0.02) for i in range(16)], np.float32)
     assert np.array_equal(got, want)
+
+
+# prep_conditioning / prep_text_arm need the real hidden size (their cond projections read 1024
+# inputs); a 2-block model with real widths keeps the reference run short.
+PREP_GEOM = dict(H=1024, NH=16, F=4096, depth=2, fused_depth=1)
+PREP_SEQ = dict(T=24, C=8, TS=16, sync_S=32)
+
+
+def prep_inputs(seed=SEED + 11):
+    s = PREP_SEQ
+    rng = np.random.default_rng(seed)
+    f = lambda *d: rng.standard_normal(d, dtype=np.float32)  # noqa: E731
+    return {"clip_f": f(s["C"], 1024), "sync_f": f(s["sync_S"], 768), "text_cat_cond": f(s["TS"], 2048),
+            "gtext_cond": f(1024), "text_cat_unc": f(s["TS"], 2048), "gtext_unc": f(1024)}
+
+
+@pytest.fixture(scope="module")
+def prep_gguf(tmp_path_factory):
+    p = str(tmp_path_factory.mktemp("gguf_prep") / "prep.gguf")
+    tsn.write_synthetic_gguf(p, make_geom(**PREP_GEOM), SEED, with_prep=True)
+    return p
+
+
+@pytest.mark.skipif(not O.have_ref(), reason="reference build (oracle/_ref) absent")
+def test_port_matches_reference_build_prep(prep_gguf, tmp_path):
+    """The port's prep_conditioning + prep_text_arm equal the reference's own host code bit for bit."""
+    s = PREP_SEQ
+    inp = prep_inputs()
+    O.write_inputs(str(tmp_path / "in"), inp)
+    O.run_ref("prep", prep_gguf, s["T"], s["C"], s["TS"], str(tmp_path / "in"), str(tmp_path / "out"), s["sync_S"])
+    got = O.Oracle(prep_gguf).prep(s["T"], s["C"], s["TS"], s["sync_S"], inp["clip_f"], inp["sync_f"],
+                                   inp["text_cat_cond"], inp["gtext_cond"], inp["text_cat_unc"], inp["gtext_unc"])
+    for k in O.PREP_OUT:
+        ref = np.fromfile(str(tmp_path / "out" / f"{k}.bin"), np.float32)
+        assert np.array_equal(got[k].ravel(), ref), k

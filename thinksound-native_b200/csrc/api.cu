@@ -264,6 +264,29 @@ int tsn_dit_set_conditioning(tsn_dit * m, const float * clip_pp, const float * s
     return TSN_OK;
 }
 
+int tsn_dit_get_conditioning(tsn_dit * m, float * clip_pp, float * sync_gather, float * text_pp, float * gcmlp) {
+    M_BEGIN NEED_PREPARED
+    const size_t H = M.g.H;
+    cudaStream_t s = M.dev->stream;
+    if (clip_pp) CKR(cudaMemcpyAsync(clip_pp, M.clip_pp, (size_t) M.C * H * 4, cudaMemcpyDefault, s));
+    if (sync_gather) CKR(cudaMemcpyAsync(sync_gather, M.sync_gather, (size_t) M.T * H * 4, cudaMemcpyDefault, s));
+    if (text_pp) CKR(cudaMemcpyAsync(text_pp, M.text_pp, (size_t) M.B * M.TS * H * 4, cudaMemcpyDefault, s));
+    if (gcmlp) CKR(cudaMemcpyAsync(gcmlp, M.gcmlp, (size_t) M.B * H * 4, cudaMemcpyDefault, s));
+    return M.dev->sync();
+}
+
+int tsn_dit_prep_conditioning(tsn_dit * m, const float * clip_f, const float * sync_f, int sync_S) {
+    M_BEGIN NEED_PREPARED
+    if (!clip_f || !sync_f) return fail(TSN_ERR_ARG, "null argument");
+    return M.prep_conditioning(clip_f, sync_f, sync_S);
+}
+
+int tsn_dit_prep_text_arm(tsn_dit * m, int arm, const float * text_cat, const float * gtext) {
+    M_BEGIN NEED_PREPARED
+    if (!text_cat || !gtext) return fail(TSN_ERR_ARG, "null argument");
+    return M.prep_text_arm(arm, text_cat, gtext);
+}
+
 int tsn_dit_set_x(tsn_dit * m, const float * x) {
     M_BEGIN NEED_PREPARED
     CKR(cudaMemcpyAsync(M.x, x, (size_t) M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));

@@ -76,8 +76,8 @@ struct SynthSrc : Src {
     uint64_t seed = 0;
     std::map<std::string, TensorSpec> specs;
     std::map<std::string, GgufTensorInfo> infos;
-    SynthSrc(const DitGeom & g, uint64_t sd) : seed(sd) {
-        for (const TensorSpec & s : dit_schema(g, false)) {
+    SynthSrc(const DitGeom & g, uint64_t sd, bool with_prep = false) : seed(sd) {
+        for (const TensorSpec & s : dit_schema(g, with_prep)) {
             specs[s.name] = s;
             GgufTensorInfo t;
             t.name = s.name;
@@ -109,8 +109,11 @@ struct Loader {
     size_t need = 0;
 
     static size_t al(size_t b) { return (b + 255) & ~(size_t) 255; }
+    char * own = nullptr;     // non-null: place tensors in this buffer instead of the model arena
+    size_t own_used = 0;
     void * take(size_t bytes) {
         if (dry) { need += al(bytes); return nullptr; }
+        if (own) { void * p = own + own_used; own_used += al(bytes); return p; }
         return m.arena_take(bytes);
     }
     int find(const std::string & name, uint32_t dims, const uint64_t * ne, const GgufTensorInfo ** out) {
@@ -137,6 +140,32 @@ struct Loader {
         if ((rc = src.stage(*t, stA, s))) return rc;
         CKR(launch_prep_weight(*dst, stA, nullptr, (int) t->type, m.bf16, N, K_in, kind == 1 ? taps : 1,
                                kind == 2 ? 1 : 0, (int) m.g.H, s));
+        return TSN_OK;
+    }
+    // conv weight kept in the reference's [OC][IC][K] order (read as an [OC][IC*K] matrix)
+    int conv_ref(const std::string & p, int OC, int IC, int K, bool bias, Lin & L) {
+        const GgufTensorInfo * t;
+        const uint64_t cnv[3] = {(uint64_t) K, (uint64_t) IC, (uint64_t) OC};
+        int rc = find(p + ".weight", 3, cnv, &t);
+        if (rc) return rc;
+        L.N = OC; L.K_in = IC * K; L.taps = 1;
+        L.w = (uint16_t *) take((size_t) OC * IC * K * 2);
+        if (!dry) {
+            if ((rc = src.stage(*t, stA, s))) return rc;
+            CKR(launch_prep_weight(L.w, stA, nullptr, (int) t->type, m.bf16, OC, IC * K, 1, 0, (int) m.g.H, s));
+        }
+        return bias ? vec(p + ".bias", OC, 0, &L.b) : TSN_OK;
+    }
+    // 2-D f32 table [rows][cols] (sync_pos_emb)
+    int table(const std::string & name, int rows, int cols, float ** dst) {
+        const GgufTensorInfo * t;
+        const uint64_t ne[2] = {(uint64_t) cols, (uint64_t) rows};
+        int rc = find(name, 2, ne, &t);
+        if (rc) return rc;
+        *dst = (float *) take((size_t) rows * cols * 4);
+        if (dry) return TSN_OK;
+        if ((rc = src.stage(*t, stA, s))) return rc;
+        CKR(launch_prep_vec(*dst, stA, (int) t->type, (long long) rows * cols, 0, (int) m.g.H, s));
         return TSN_OK;
     }
     int vec(const std::string & name, int n, int mode, float ** dst, bool placed = false) {
@@ -196,6 +225,29 @@ struct Loader {
         if (!rc) rc = linear(bp + ".ffn.w2", conv ? 1 : 0, H, F, 3, false, b.w2);
         return rc;
     }
+    // DitModel::prep_conditioning / prep_text_arm weights (src/dit.cpp:91-192)
+    int prep(PrepW & w) {
+        const int H = (int) m.g.H, F = (int) m.g.F;
+        int rc = table("sync_pos_emb", 8, 768, &w.sync_pos);
+        if (!rc) rc = conv_ref("sync_input_proj.0", H, 768, 7, true, w.sync0);
+        if (!rc) rc = conv_ref("sync_input_proj.2.w1", F, H, 3, false, w.sync_w1);
+        if (!rc) rc = conv_ref("sync_input_proj.2.w3", F, H, 3, false, w.sync_w3);
+        if (!rc) rc = conv_ref("sync_input_proj.2.w2", H, F, 3, false, w.sync_w2);
+        if (!rc) rc = linear("clip_input_proj.0", 0, H, 1024, 1, true, w.clip0);
+        if (!rc) rc = conv_ref("clip_input_proj.2.w1", F, H, 3, false, w.clip_w1);
+        if (!rc) rc = conv_ref("clip_input_proj.2.w3", F, H, 3, false, w.clip_w3);
+        if (!rc) rc = conv_ref("clip_input_proj.2.w2", H, F, 3, false, w.clip_w2);
+        if (!rc) rc = linear("clip_cond_proj", 0, H, 1024, 1, true, w.clip_cond);
+        if (!rc) rc = linear("text_input_proj.0", 0, H, 2048, 1, true, w.text0);
+        if (!rc) rc = linear("text_input_proj.2.w1", 0, F, H, 1, false, w.text_w1);
+        if (!rc) rc = linear("text_input_proj.2.w3", 0, F, H, 1, false, w.text_w3);
+        if (!rc) rc = linear("text_input_proj.2.w2", 0, H, F, 1, false, w.text_w2);
+        if (!rc) rc = linear("text_cond_proj", 0, H, 1024, 1, true, w.text_cond);
+        if (!rc) rc = linear("global_cond_mlp.w1", 0, F, H, 1, false, w.g_w1);
+        if (!rc) rc = linear("global_cond_mlp.w3", 0, F, H, 1, false, w.g_w3);
+        if (!rc) rc = linear("global_cond_mlp.w2", 0, H, F, 1, false, w.g_w2);
+        return rc;
+    }
     int all() {
         const DitGeom & g = m.g;
         const int H = (int) g.H, F = (int) g.F, L = (int) g.latent_dim;
@@ -243,6 +295,8 @@ Model::~Model() {
     if (dev) dev->activate();
     release_activations();
     if (arena) cudaFree(arena);
+    if (prep_arena) cudaFree(prep_arena);
+    if (clip_fc) cudaFree(clip_fc);
 }
 
 void * Model::arena_take(size_t bytes) {
@@ -274,6 +328,8 @@ int load_model(Model & m, const std::string * path, const DitGeom * sg, uint64_t
         m.g = *sg;
         src = std::make_unique<SynthSrc>(*sg, seed);
     }
+    m.src_path = path ? *path : std::string();
+    m.src_seed = seed;
     int rc = check_geom(m.g);
     if (rc) return rc;
     Loader dry{m, *src, m.dev->stream};
@@ -292,6 +348,38 @@ int load_model(Model & m, const std::string * path, const DitGeom * sg, uint64_t
     cudaFree(ld.stB);
     if (rc) return rc;
     if (se != cudaSuccess) return fail(TSN_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(se));
+    return TSN_OK;
+}
+
+int load_prep(Model & m) {
+    if (m.prep_loaded) return TSN_OK;
+    std::unique_ptr<Src> src;
+    if (!m.src_path.empty()) {
+        auto fs = std::make_unique<FileSrc>();
+        std::string err;
+        if (!fs->f.open(m.src_path, err)) return fail(TSN_ERR_IO, err);
+        src = std::move(fs);
+    } else {
+        src = std::make_unique<SynthSrc>(m.g, m.src_seed, true);
+    }
+    PrepW sizing;
+    Loader dry{m, *src, m.dev->stream};
+    dry.dry = true;
+    int rc = dry.prep(sizing);
+    if (rc) return rc;
+    CKR(cudaMalloc(&m.prep_arena, dry.need));
+    Loader ld{m, *src, m.dev->stream};
+    ld.own = (char *) m.prep_arena;
+    ld.st_bytes = dry.st_bytes;
+    CKR(cudaMalloc(&ld.stA, ld.st_bytes));
+    CKR(cudaMalloc(&ld.stB, ld.st_bytes));
+    rc = ld.prep(m.pw);
+    cudaError_t se = cudaStreamSynchronize(m.dev->stream);
+    cudaFree(ld.stA);
+    cudaFree(ld.stB);
+    if (rc) return rc;
+    if (se != cudaSuccess) return fail(TSN_ERR_CUDA, std::string("prep weight upload: ") + cudaGetErrorString(se));
+    m.prep_loaded = true;
     return TSN_OK;
 }
 

@@ -65,6 +65,17 @@ struct Op {
     int ev = -1;
 };
 
+// Once-per-generation conditioning weights (DitModel::prep_conditioning / prep_text_arm,
+// src/dit.cpp:55-192) in the reference's own layouts: linear [N][K], conv [OC][IC][K] f16 (the
+// runtime face's im2col GEMM reads them as they are), biases and sync_pos_emb f32.
+struct PrepW {
+    float * sync_pos = nullptr;                         // [8][768]
+    Lin sync0, sync_w1, sync_w3, sync_w2;               // conv k7 768->H; convmlp k3
+    Lin clip0, clip_w1, clip_w3, clip_w2, clip_cond;    // linear 1024->H; convmlp k3; cond proj
+    Lin text0, text_w1, text_w3, text_w2, text_cond;    // linear 2048->H; linear SwiGLU MLP; cond proj
+    Lin g_w1, g_w3, g_w2;                               // global_cond_mlp
+};
+
 struct TapBuf {
     void * dev = nullptr;
     size_t bytes = 0;
@@ -83,6 +94,16 @@ struct Model {
     std::vector<Blk> jl, jc, jt, fb;
     void * arena = nullptr;
     size_t arena_bytes = 0, arena_used = 0;
+    // the weights' source, for the once-per-generation conditioning weights loaded on first use
+    std::string src_path;             // GGUF path, or empty for the synthetic generator
+    uint64_t src_seed = 0;
+    PrepW pw;
+    void * prep_arena = nullptr;
+    bool prep_loaded = false;
+    float * clip_fc = nullptr;        // [H] clip_cond_proj(mean clip_pp) of the current generation
+    bool clip_fc_valid = false;
+    int prep_conditioning(const float * clip_f, const float * sync_f, int sync_S);
+    int prep_text_arm(int arm, const float * text_cat, const float * gtext);
 
     // geometry (tsn_dit_prepare)
     bool prepared = false;
@@ -132,5 +153,6 @@ struct Model {
 };
 
 int load_model(Model & m, const std::string * gguf_path, const DitGeom * synth_geom, uint64_t seed, std::string & err);
+int load_prep(Model & m);   // loads PrepW from the model's source on first use
 
 } // namespace tsn

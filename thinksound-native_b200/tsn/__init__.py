@@ -96,6 +96,9 @@ _SIGS = [
     ("tsn_dit_kernels_per_step", C.c_int, [C.c_void_p]),
     ("tsn_dit_profile_step", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
     ("tsn_dit_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    ("tsn_dit_get_conditioning", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("tsn_dit_prep_conditioning", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]),
+    ("tsn_dit_prep_text_arm", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     ("tsn_dit_trace_op", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
     ("tsn_dit_timeline", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
     ("tsn_dit_autotune", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
@@ -243,6 +246,17 @@ class Dit:
 
     def set_conditioning(self, clip_pp, sync_gather, text_pp, gcmlp):
         check(lib().tsn_dit_set_conditioning(self.h, _p(clip_pp), _p(sync_gather), _p(text_pp), _p(gcmlp)))
+
+    def get_conditioning(self, clip_pp=None, sync_gather=None, text_pp=None, gcmlp=None):
+        check(lib().tsn_dit_get_conditioning(self.h, _p(clip_pp), _p(sync_gather), _p(text_pp), _p(gcmlp)))
+
+    def prep_conditioning(self, clip_f, sync_f, sync_S: int):
+        """prep_conditioning on the GPU: clip_f [C, 1024], sync_f [sync_S, 768] f32."""
+        check(lib().tsn_dit_prep_conditioning(self.h, _p(clip_f), _p(sync_f), sync_S))
+
+    def prep_text_arm(self, arm: int, text_cat, gtext):
+        """prep_text_arm on the GPU for CFG arm `arm`: text_cat [TS, 2048], gtext [1024] f32."""
+        check(lib().tsn_dit_prep_text_arm(self.h, arm, _p(text_cat), _p(gtext)))
 
     def set_x(self, x):
         check(lib().tsn_dit_set_x(self.h, _p(x)))
