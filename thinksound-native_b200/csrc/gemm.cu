@@ -6,6 +6,7 @@
 #include <map>
 #include <mutex>
 
+#include "gemm_2sm.cuh"
 #include "kernels.h"
 
 namespace tsn {
@@ -36,6 +37,17 @@ bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t ro
     return g_encode(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void *) base,
                     dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_act_map_rows(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t rows, uint64_t B, uint32_t box_rows) {
+    if (!encoder() || ((uintptr_t) base & 15) || (K_in % 64) || box_rows == 0 || box_rows > 256) return false;
+    const cuuint64_t dims[3] = {K_in, rows, B};
+    const cuuint64_t strides[2] = {K_in * 2, rows * K_in * 2};
+    const cuuint32_t box[3] = {64, box_rows, 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void *) base, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows) {
@@ -105,6 +117,47 @@ size_t gemm_persistent_smem_bytes(int bn) {
     return 0;
 }
 
+constexpr int stages2(int nt, bool split) {
+    return split ? (nt == 256 ? 4 : nt == 192 ? 5 : nt == 128 ? 6 : 8) : (nt == 256 ? 6 : nt == 192 ? 7 : 8);
+}
+size_t gemm2_smem_bytes(int nt, bool split) {
+    switch (nt * 2 + (split ? 1 : 0)) {
+        case 64 * 2: return Gemm2Smem<64, stages2(64, false), false>::TOTAL;
+        case 64 * 2 + 1: return Gemm2Smem<64, stages2(64, true), true>::TOTAL;
+        case 128 * 2: return Gemm2Smem<128, stages2(128, false), false>::TOTAL;
+        case 128 * 2 + 1: return Gemm2Smem<128, stages2(128, true), true>::TOTAL;
+        case 192 * 2: return Gemm2Smem<192, stages2(192, false), false>::TOTAL;
+        case 192 * 2 + 1: return Gemm2Smem<192, stages2(192, true), true>::TOTAL;
+        case 256 * 2: return Gemm2Smem<256, stages2(256, false), false>::TOTAL;
+        case 256 * 2 + 1: return Gemm2Smem<256, stages2(256, true), true>::TOTAL;
+    }
+    return 0;
+}
+
+namespace {
+using Kernel2Fn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
+template <int NT, int EPI, bool SPLIT>
+Kernel2Fn pick2() {
+    static_assert(Gemm2Smem<NT, stages2(NT, SPLIT), SPLIT>::TOTAL <= 232448, "smem budget");
+    return (Kernel2Fn) gemm2_kernel<NT, EPI, stages2(NT, SPLIT), SPLIT>;
+}
+template <int NT>
+Kernel2Fn pick2_epi(int epi, bool split) {
+    if (epi == EPI_F32) return split ? pick2<NT, EPI_F32, true>() : pick2<NT, EPI_F32, false>();
+    if (epi == EPI_SWIGLU) return split ? pick2<NT, EPI_SWIGLU, true>() : pick2<NT, EPI_SWIGLU, false>();
+    return nullptr;
+}
+Kernel2Fn gemm2_for(int nt, int epi, bool split) {
+    switch (nt) {
+        case 64: return pick2_epi<64>(epi, split);
+        case 128: return pick2_epi<128>(epi, split);
+        case 192: return pick2_epi<192>(epi, split);
+        case 256: return pick2_epi<256>(epi, split);
+    }
+    return nullptr;
+}
+} // namespace
+
 namespace {
 using KernelFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs, int);
 
@@ -168,6 +221,14 @@ cudaError_t configure_gemm_kernels() {
                                              (int) gemm_persistent_smem_bytes(bn));
         if (e != cudaSuccess) return e;
     }
+    for (int nt : {64, 128, 192, 256})
+        for (int epi : {(int) EPI_F32, (int) EPI_SWIGLU})
+            for (int split = 0; split < 2; ++split) {
+                cudaError_t e = cudaFuncSetAttribute((const void *) gemm2_for(nt, epi, split != 0),
+                                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int) gemm2_smem_bytes(nt, split != 0));
+                if (e != cudaSuccess) return e;
+            }
     return cudaSuccess;
 }
 
@@ -177,6 +238,11 @@ bool pdl_enabled() {
 }
 
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
+    if (g.pair_nt) {
+        Kernel2Fn fn = gemm2_for(g.pair_nt, g.epi, g.split);
+        if (!fn || g.grid.x % 2) return cudaErrorInvalidValue;
+        return launch_cl(fn, g.grid, dim3(192), g.smem, s, dim3(2, 1, 1), g.tb, g.ta, g.ta2, g.args);
+    }
     if (g.persistent) {
         KernelFn fn = persistent_for(g.bn);
         if (!fn || g.epi != EPI_F32 || !g.split || g.args.splits != 1) return cudaErrorInvalidValue;
@@ -187,6 +253,41 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
     // split-K: the K slices of one output tile form a cluster along grid.z
     return launch_ex(fn, g.grid, dim3(192), g.smem, s, g.args.splits > 1 ? (unsigned) g.args.splits : 1u,
                      g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
+}
+
+// CTAs of the 2-SM kernel that can run at once (in pairs)
+int gemm2_capacity(int nt, int epi, bool split) {
+    static std::mutex mu;
+    static std::map<int, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int key = ((dev * 512 + nt) * 8 + epi) * 2 + (split ? 1 : 0);
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    Kernel2Fn fn = gemm2_for(nt, epi, split);
+    int cap = 0;
+    if (fn) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(2, 1, 1);
+        cfg.blockDim = dim3(192, 1, 1);
+        cfg.dynamicSmemBytes = gemm2_smem_bytes(nt, split);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, (const void *) fn, &cfg) == cudaSuccess) cap = 2 * clusters;
+        else cudaGetLastError();
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = cap;
+    return cap;
 }
 
 int cluster_capacity_uncached(int bn, int epi, bool split, int cluster);

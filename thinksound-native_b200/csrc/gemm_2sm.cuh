@@ -1,0 +1,198 @@
+// gemm_2sm.cuh — the CTA-pair (cta_group::2) tcgen05 GEMM with weights on the M side.
+//
+// Same product as gemm_tc.cuh, Y[token][n] = sum_k X[token][k] W[n][k], but computed as
+// D[n][token] = W · X^T so that the large output-feature dimension is the MMA's M and the few
+// tokens (2 CFG arms x 188 rows at 8 s) its N. Two CTAs on neighbouring SMs form a cluster pair:
+// each loads 128 weight rows (its half of M = 256) and half of the NT-token activation tile
+// (f16, split hi + lo or plain), and the pair leader issues tcgen05.mma.cta_group::2 over both CTAs' shared
+// memory into both CTAs' TMEM (split f16 activations: a hi and a lo UMMA per K step; plain f16 for
+// the FFN down-projection). Per SM and per MMA cycle this moves ~30 % fewer operand bytes than
+// the single-CTA kernel (which holds a whole weight tile per SM), so the same ring depth hides
+// more of the weight-tile latency. Each CTA's epilogue owns its 128 output features: lanes are
+// consecutive features, so every store instruction writes one token's contiguous feature run.
+//
+//   warp 4 (both CTAs)  TMA: weight rows and activation half-tile per 64-wide K block into a
+//                       STAGES-deep ring; the bytes of both CTAs are counted on the leader's barrier
+//   warp 5 (leader)     M=256 x N=NT x K=16 UMMAs (hi, then lo) into TMEM; commits release the
+//                       stage in both CTAs and finally signal both CTAs' epilogues
+//   warps 0-3           tcgen05.ld of the CTA's 128 feature rows x NT tokens; f32 (+bias, or
+//                       split-K partial tile) or SwiGLU f16 output
+// Split-K (grid.z) gives independent K slices, each writing its own partial tile (EPI_F32 with
+// part_stride); there is no in-kernel split-K reduction. No TMA load uses multicast.
+#pragma once
+#include "gemm_tc.cuh"
+
+namespace tsn {
+
+template <int NT, int STAGES, bool SPLIT>
+struct Gemm2Smem {
+    static constexpr int W_BYTES = 128 * 128;              // 128 weight rows x 64 K f16
+    static constexpr int X_BYTES = (NT / 2) * 128;         // this CTA's NT/2 tokens x 64 K f16, one half
+    static constexpr int X_OFF = W_BYTES;
+    static constexpr int STAGE = W_BYTES + (SPLIT ? 2 : 1) * X_BYTES;
+    static constexpr int BAR_OFF = STAGES * STAGE;
+    static constexpr int TOTAL = BAR_OFF + 256 + 1024;    // barriers, TMEM slot, abort flag + alignment slack
+    static_assert(X_BYTES % 1024 == 0, "activation half-tiles must stay 1024-byte aligned");
+};
+
+template <int NT, int EPI, int STAGES, bool SPLIT>
+__global__ void __launch_bounds__(192, 1)
+gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+             const __grid_constant__ CUtensorMap tmX2, const GemmArgs a) {
+    using L = Gemm2Smem<NT, STAGES, SPLIT>;
+    static_assert(EPI == EPI_F32 || EPI == EPI_SWIGLU, "2-SM epilogues: f32 / partial f32, SwiGLU");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);    // used on the leader only
+    uint64_t * empty = full + STAGES;
+    uint64_t * tfull = empty + STAGES;
+    uint32_t * tslot = (uint32_t *) (tfull + 1);
+    volatile int * abort_flag = (volatile int *) (tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();                  // 0: pair leader
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    unsigned long long * tr = a.trace ? a.trace + (size_t) cta * TRACE_SLOTS : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
+    const int n0 = (blockIdx.x >> 1) * 256 + (int) rank * 128;      // this CTA's 128 weight rows
+    const int b = blockIdx.y / a.m_tiles_t, t0 = (blockIdx.y % a.m_tiles_t) * NT;   // the pair's token tile
+    const int tx = t0 + (int) rank * (NT / 2);             // this CTA's half of the tokens
+    const int kb_begin = blockIdx.z * a.kb_per_split;
+    const int kb_end = min(a.k_blocks, kb_begin + a.kb_per_split);
+    const int nk = kb_end - kb_begin;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(tfull, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (threadIdx.x == 0) pdl_trigger();
+    if (warp == 4 && lane == 0) {
+        tma_prefetch(&tmW);
+        tma_prefetch(&tmX);
+        if (SPLIT) tma_prefetch(&tmX2);
+    }
+    if (warp == 5) tmem_alloc2(tslot, TmemCols<NT>::N);
+    // both CTAs' barriers are initialised and their TMEM allocated before either side proceeds
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    if (tr && threadIdx.x == 0) tr[1] = global_ns();
+
+    if (warp == 4) {
+        if (lane == 0) {
+            uint32_t full_leader[STAGES];
+#pragma unroll
+            for (int s = 0; s < STAGES; ++s) full_leader[s] = dsmem_map(smem_u32(&full[s]), 0);
+            // weights do not depend on the upstream kernel: issue the first stages' weight rows now
+            const int pre = nk < STAGES ? nk : STAGES;
+            for (int i = 0; i < pre; ++i) {
+                if (rank == 0) mbar_expect_tx(&full[i], 2 * L::STAGE);
+                tma_load_2d_cg2(smem + i * L::STAGE, &tmW, full_leader[i], (kb_begin + i) * 64, n0);
+            }
+            pdl_wait();
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % STAGES;
+                if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_EMPTY))
+                    break;
+                const int kb = kb_begin + i;
+                const int tap = kb / a.ic_blocks, ic0 = (kb % a.ic_blocks) * 64;
+                uint8_t * st = smem + s * L::STAGE;
+                if (i >= pre) {
+                    if (rank == 0) mbar_expect_tx(&full[s], 2 * L::STAGE);
+                    tma_load_2d_cg2(st, &tmW, full_leader[s], kb * 64, n0);
+                }
+                tma_load_3d_cg2(st + L::X_OFF, &tmX, full_leader[s], ic0, tx + tap - a.pad, b);
+                if (SPLIT) tma_load_3d_cg2(st + L::X_OFF + L::X_BYTES, &tmX2, full_leader[s], ic0, tx + tap - a.pad, b);
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = umma_idesc_f16(NT, 0, 0, 256);
+            for (int i = 0; i < nk; ++i) {
+                const int s = i % STAGES;
+                if (!mbar_wait(&full[s], (i / STAGES) & 1, abort_flag, a.err, DEV_TIMEOUT_FULL)) break;
+                if (tr && i == 0) tr[2] = global_ns();
+                tc_fence_after();
+                const uint8_t * st = smem + s * L::STAGE;
+                const uint64_t wd = umma_desc_sw128(st), xh = umma_desc_sw128(st + L::X_OFF),
+                               xl = umma_desc_sw128(st + L::X_OFF + L::X_BYTES);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    umma2_f16(tmem, wd + (uint64_t) (2 * k), xh + (uint64_t) (2 * k), idesc, (i | k) != 0);
+                    if (SPLIT) umma2_f16(tmem, wd + (uint64_t) (2 * k), xl + (uint64_t) (2 * k), idesc, 1u);
+                }
+                umma2_commit_pair(&empty[s]);
+            }
+            umma2_commit_pair(tfull);
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        pdl_wait();
+        const bool ok = mbar_wait(tfull, 0, abort_flag, a.err, DEV_TIMEOUT_TMEM) && !*abort_flag;
+        tc_fence_after();
+        if (tr && threadIdx.x == 0) tr[3] = global_ns();
+        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        const int n = n0 + warp * 32 + lane;              // this thread's weight row
+        if constexpr (EPI == EPI_F32) {
+            const float bias = (a.bias && n < a.N) ? a.bias[n] : 0.0f;
+            float * ob = (float *) a.out + blockIdx.z * a.part_stride + (long long) b * a.out_bs + n;
+#pragma unroll 1
+            for (int c = 0; c < NT; c += 32) {
+                float v[32];
+                tmem_ld32(trow + c, v);
+                if (!ok || n >= a.N) continue;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int t = t0 + c + j;
+                    if (t < a.rows) ob[(long long) t * a.ldo] = v[j] + bias;
+                }
+            }
+        } else {
+            // SwiGLU: rows come in groups of 64 = [32 w1 | 32 w3], so warps (0,1) and (2,3) hold
+            // matching w1 and w3 rows for output features g*32 + lane, g = (n0 + 64*pair) / 64.
+            // Each warp puts its 32 x 32 block in shared memory (the operand ring is free: every
+            // MMA of the pair has completed) and the pair splits the 32 tokens of the chunk.
+            float * xb = (float *) smem + warp * 32 * 32;           // [token][lane]
+            const int pw = warp >> 1, odd = warp & 1;
+            const int f = ((n0 + 64 * pw) >> 6) * 32 + lane;        // output feature
+            __half * ob = (__half *) a.out + (long long) b * a.out_bs + f;
+            const bool fok = (n0 + 64 * pw) < a.N;
+#pragma unroll 1
+            for (int c = 0; c < NT; c += 32) {
+                float v[32];
+                tmem_ld32(trow + c, v);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) xb[j * 32 + lane] = v[j];
+                asm volatile("bar.sync %0, 64;" ::"r"(2 + pw) : "memory");
+                const float * w1 = (const float *) smem + (2 * pw) * 32 * 32;
+                const float * w3 = w1 + 32 * 32;
+                if (ok && fok) {
+#pragma unroll 4
+                    for (int j = odd * 16; j < odd * 16 + 16; ++j) {
+                        const int t = t0 + c + j;
+                        if (t < a.rows) ob[(long long) t * a.ldo] = __float2half_rn(silu_f(w1[j * 32 + lane]) * w3[j * 32 + lane]);
+                    }
+                }
+                asm volatile("bar.sync %0, 64;" ::"r"(2 + pw) : "memory");
+            }
+        }
+    }
+    // every thread of both CTAs: TMEM reads and peer shared-memory traffic are over before the
+    // pair releases its TMEM
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc2(tmem, TmemCols<NT>::N);
+    }
+    if (tr && threadIdx.x == 0) tr[5] = global_ns();
+    if (*abort_flag && threadIdx.x == 0) {
+        const uint64_t t1 = global_ns();
+        while (global_ns() - t1 < 20000ull) {}
+    }
+}
+
+} // namespace tsn

@@ -12,11 +12,11 @@
 namespace tsn {
 
 // Launch with programmatic stream serialisation (the kernel may start while its predecessor on
-// the stream runs; it calls pdl_wait() before touching upstream data) and an optional cluster
-// along z. Setting TSN_NO_PDL in the environment launches with plain stream order instead.
+// the stream runs; it calls pdl_wait() before touching upstream data) and an optional thread-block
+// cluster shape. Setting TSN_NO_PDL in the environment launches with plain stream order instead.
 bool pdl_enabled();
 template <typename... KArgs, typename... Args>
-cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, unsigned cluster_z,
+cudaError_t launch_cl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, dim3 cluster,
                       Args &&... args) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
@@ -30,16 +30,23 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
         attr[n].val.programmaticStreamSerializationAllowed = 1;
         ++n;
     }
-    if (cluster_z > 1) {
+    if (cluster.x * cluster.y * cluster.z > 1) {
         attr[n].id = cudaLaunchAttributeClusterDimension;
-        attr[n].val.clusterDim.x = 1;
-        attr[n].val.clusterDim.y = 1;
-        attr[n].val.clusterDim.z = cluster_z;
+        attr[n].val.clusterDim.x = cluster.x;
+        attr[n].val.clusterDim.y = cluster.y;
+        attr[n].val.clusterDim.z = cluster.z;
         ++n;
     }
     cfg.attrs = attr;
     cfg.numAttrs = n;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// cluster of cluster_z CTAs along z (the split-K clusters)
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, unsigned cluster_z,
+                      Args &&... args) {
+    return launch_cl(kernel, grid, block, smem, s, dim3(1, 1, cluster_z), std::forward<Args>(args)...);
 }
 
 // ---- GEMM / implicit conv (gemm.cu) ----
@@ -50,6 +57,7 @@ struct GemmLaunch {
     int bn = 0, epi = 0, ab_bf16 = 0;
     bool split = false;
     bool persistent = false;      // gemm_tc_persistent (f32 out, split A, one CTA per SM over many tiles)
+    int pair_nt = 0;              // > 0: gemm2_kernel (CTA pairs, weights on M) with NT-token tiles
     size_t smem = 0;
 };
 // Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] 16-bit activation buffer.
@@ -65,6 +73,11 @@ cudaError_t configure_gemm_kernels();
 int gemm_cluster_capacity(int bn, int epi, bool split, int cluster);
 size_t gemm_smem_bytes(int bn, bool split, int epi);
 size_t gemm_persistent_smem_bytes(int bn);   // 0: no persistent kernel for this tile width
+size_t gemm2_smem_bytes(int nt, bool split);   // 0: no 2-SM kernel for this token tile
+int gemm2_capacity(int nt, int epi, bool split);   // 2-SM CTAs that fit on the device at once
+// Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] f16 activation buffer with a
+// {64, box_rows, 1} box (the 2-SM GEMM's half token tile).
+bool make_act_map_rows(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t rows, uint64_t B, uint32_t box_rows);
 int gemm_stages(int bn, bool split, int epi);
 
 // ---- attention (kernels.cu) ----

@@ -568,16 +568,40 @@ struct Plan {
                 if (cost < best - 1e-9) { best = cost; bn_best = bn; s_best = s; }
             }
         }
+        // CTA-pair kernel (gemm_2sm.cuh): tile code 2000 + NT, weights on M in 256-row pairs, NT
+        // tokens of one arm; K slices only as partial tiles
+        const bool pair_ok = (epi == EPI_F32 || epi == EPI_SWIGLU) && !m.bf16;
+        if (pair_ok)
+            for (int nt : {192, 128, 64, 256}) {
+                const int tiles = m.B * ((rows + nt - 1) / nt) * ((N + 255) / 256);
+                // measured: the pair mainloop runs ~10 % faster per K block, but its epilogue is
+                // slower, so the cost model leaves the choice to the autotuner
+                const double kcost = (split ? 0.57 : 0.30) * nt / 192.0 * 1.2;
+                for (int s = 1; s <= (partial ? 8 : 1) && s <= kb; ++s) {
+                    if (!splits_valid(kb, s, smax)) continue;
+                    const int kbps = (kb + s - 1) / s;
+                    const int cap = gemm2_capacity(nt, epi, split);
+                    if (cap <= 0) continue;
+                    const int ctas = 2 * tiles * s, waves = (ctas + cap - 1) / cap;
+                    const double cost = waves * (kbps * kcost + 1.5) + (s > 1 ? 0.3 * s : 0.0);
+                    if (cost < best - 1e-9) { best = cost; bn_best = 2000 + nt; s_best = s; }
+                }
+            }
         if (!bn_best) return fail(TSN_ERR_ARG, std::string(name) + ": no tile fits N=" + std::to_string(N));
         auto fo = m.gemm_force.find(m.gemm_seq);
-        if (fo != m.gemm_force.end() && splits_valid(kb, fo->second.second, smax) &&
-            (fo->second.first == 192 || N % fo->second.first == 0)) {
-            bn_best = fo->second.first;
-            s_best = fo->second.second;
+        if (fo != m.gemm_force.end()) {
+            const int fb = fo->second.first, fs = fo->second.second;
+            const bool pair = fb > 2000;
+            if (pair ? (pair_ok && gemm2_smem_bytes(fb - 2000, split) && splits_valid(kb, fs, partial ? smax : 1))
+                     : (splits_valid(kb, fs, smax) && (fb == 192 || N % fb == 0))) {
+                bn_best = fb;
+                s_best = fs;
+            }
         }
         char key[128];
-        snprintf(key, sizeof key, "%d:%d:%d:%d:%d:%d", rows, N, K_in, W.taps, epi, (int) split);
+        snprintf(key, sizeof key, "%d:%d:%d:%d:%d:%d:%d", rows, N, K_in, W.taps, epi, (int) split, (int) partial);
         last_shape = key;
+        if (bn_best > 2000) return pair_gemm(name, A, K_in, rows, W, pad, epi, split, partial, bn_best - 2000, s_best, g);
         g = GemmLaunch{};
         g.bn = bn_best;
         g.epi = epi;
@@ -597,6 +621,34 @@ struct Plan {
         a.splits = partial ? 1 : s_best; a.kb_per_split = (kb + s_best - 1) / s_best;
         a.err = m.dev->d_err;
         a.bias = W.b;
+        return TSN_OK;
+    }
+    // the CTA-pair launch: grid (2 x weight-row pairs, arms x token tiles, K slices), cluster (2,1,1)
+    int pair_gemm(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, int epi, bool split,
+                  bool partial, int nt, int s, GemmLaunch & g) {
+        const int B = m.B, N = W.N, kb = W.taps * K_in / 64;
+        const int mtt = (rows + nt - 1) / nt;
+        g = GemmLaunch{};
+        g.bn = 2000 + nt;
+        g.pair_nt = nt;
+        g.epi = epi;
+        g.split = split;
+        g.smem = gemm2_smem_bytes(nt, split);
+        g.ab_bf16 = 0;
+        g.grid = dim3(2 * ((N + 255) / 256), B * mtt, s);
+        const __half * Alo = (const __half *) A + (size_t) B * rows * K_in;
+        if (!make_act_map_rows(&g.ta, A, K_in, rows, B, nt / 2) ||
+            (split && !make_act_map_rows(&g.ta2, Alo, K_in, rows, B, nt / 2)) ||
+            !make_w_map(&g.tb, W.w, (uint64_t) W.taps * K_in, N, 128, 0))
+            return fail(TSN_ERR_CUDA, std::string(name) + ": tensor map encode failed");
+        if (!split) g.ta2 = g.ta;
+        GemmArgs & a = g.args;
+        a.rows = rows; a.B = B; a.bt = nt; a.bb = 1; a.m_tiles_t = mtt; a.N = N;
+        a.k_blocks = kb; a.ic_blocks = K_in / 64; a.pad = pad;
+        a.splits = 1; a.kb_per_split = (kb + s - 1) / s;
+        a.err = m.dev->d_err;
+        a.bias = W.b;
+        (void) partial;
         return TSN_OK;
     }
     // every one of the s K-slices gets at least one 64-wide K block
@@ -634,7 +686,7 @@ struct Plan {
         const int tiles = (int) (g.grid.x * g.grid.y);
         int sms = 148;
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m.dev->ordinal);
-        if (g.split && g.grid.z == 1 && tiles > 2 * sms && gemm_persistent_smem_bytes(g.bn)) {
+        if (!g.pair_nt && g.split && g.grid.z == 1 && tiles > 2 * sms && gemm_persistent_smem_bytes(g.bn)) {
             g.persistent = true;
             g.smem = gemm_persistent_smem_bytes(g.bn);
             g.grid = dim3((unsigned) std::min(tiles, sms), 1, 1);
@@ -666,6 +718,7 @@ struct Plan {
         g.args.part_stride = (long long) m.B * rows * H;
         g.args.bias = nullptr;
         push(name, g, fl(m.B, rows, W));
+        ops.back().part_bytes = (double) g.args.part_stride * 4;
         Pending & pd = pend[res];
         pd = Pending{ws, g.args.part_stride, (int) g.grid.z, W.b, mod, per_row ? mod_ld : 0, mod_bs, per_row,
                      gate_idx * (int) H};
@@ -1065,7 +1118,7 @@ int Model::autotune(std::string & report) {
         double best = 1e30;
         std::pair<int, int> bc{0, 0};
         std::string tried;
-        for (int bn : {256, 192, 128, 64})
+        for (int bn : {256, 192, 128, 64, 2192, 2128, 2064, 2256})
             for (int sp = 1; sp <= MAX_PARTS; ++sp) {
                 gemm_force.clear();
                 gemm_force[gid] = {bn, sp};
@@ -1084,6 +1137,9 @@ int Model::autotune(std::string & report) {
                 float ms = 0;
                 CKR(cudaEventElapsedTime(&ms, e0, e1));
                 ms /= 5;
+                // a partial-tile GEMM's K slices are read again by the next adaLN: charge each slice's
+                // f32 tile at ~5 TB/s so that the choice covers the pair of kernels
+                if (o.desc.find(" partial") != std::string::npos) ms += (float) (o.part_bytes * sp / 5e9);
                 snprintf(line, sizeof line, " %d/%d:%.1f", bn, sp, ms * 1e3);
                 tried += line;
                 if (ms < best) { best = ms; bc = {bn, sp}; }

@@ -83,6 +83,21 @@ __device__ __forceinline__ void tma_load_3d(void * dst, const CUtensorMap * m, u
         : "memory");
 }
 
+// 2-SM (cta_group::2) loads: the data lands in this CTA's shared memory, the transaction bytes are
+// counted on `bar_cluster` (a shared::cluster address: the pair leader's barrier). No multicast.
+__device__ __forceinline__ void tma_load_2d_cg2(void * dst, const CUtensorMap * m, uint32_t bar_cluster, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(dst)), "l"((uint64_t) m), "r"(bar_cluster), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_cg2(void * dst, const CUtensorMap * m, uint32_t bar_cluster, int c0, int c1, int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(smem_u32(dst)), "l"((uint64_t) m), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t * slot, uint32_t ncols) {      // whole warp
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
@@ -102,6 +117,30 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
         ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
         : "memory");
 }
+// CTA-pair versions: TMEM allocation by the same warp of both CTAs; the MMA issued by the pair
+// leader with M = 256 (each CTA holds 128 rows of A and half of B's N); commits arrive on the
+// barrier at the same offset in both CTAs.
+__device__ __forceinline__ void tmem_alloc2(uint32_t * slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma2_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void umma2_commit_pair(uint64_t * bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+        ::"r"(smem_u32(bar)), "h"((uint16_t) 3)
+        : "memory");
+}
+
 // Arrive once on bar when every tcgen05 op issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t * bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -136,12 +175,12 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(const void * smem_tile) {
 
 // Instruction descriptor, kind::f16: f32 accumulate, A/B both f16 (ab_bf16=0) or both bf16 (1),
 // A K-major, B K-major (b_mn = 0) or MN-major (1), M=128, N=n.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int n, int ab_bf16, int b_mn = 0) {
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n, int ab_bf16, int b_mn = 0, int m = 128) {
     return (1u << 4)                                   // D format f32
          | ((uint32_t) ab_bf16 << 7) | ((uint32_t) ab_bf16 << 10)
          | ((uint32_t) b_mn << 16)                     // B major-ness
          | ((uint32_t) (n >> 3) << 17)
-         | ((uint32_t) (128 >> 4) << 24);
+         | ((uint32_t) (m >> 4) << 24);
 }
 
 // make this thread's generic-proxy shared-memory writes visible to the async proxy (tcgen05.mma)

@@ -60,6 +60,7 @@ struct Op {
     std::function<cudaError_t(cudaStream_t, unsigned long long *)> traced;   // launch with per-CTA stamps
     int ctas = 0;
     int trace_slots = TRACE_SLOTS;   // stamps per CTA of `traced` (GEMMs: TRACE_SLOTS; others: 3)
+    double part_bytes = 0.0;         // partial-tile GEMMs: bytes of one K slice's f32 tile
     int stream = 0;        // 0 latent (the device stream), 1 clip, 2 text
     int evkind = 0;        // 0 kernel/copy, 1 record event `ev` on `stream`, 2 make `stream` wait on `ev`
     int ev = -1;
