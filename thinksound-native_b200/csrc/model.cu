@@ -568,25 +568,11 @@ struct Plan {
                 if (cost < best - 1e-9) { best = cost; bn_best = bn; s_best = s; }
             }
         }
-        // CTA-pair kernel (gemm_2sm.cuh): tile code 2000 + NT, weights on M in 256-row pairs, NT
-        // tokens of one arm; K slices only as partial tiles
+        // CTA-pair kernel (gemm_2sm.cuh, tile code 2000 + NT: weights on M in 256-row pairs, NT
+        // tokens of one arm, K slices only as partial tiles) is chosen only by the autotuner: its
+        // mainloop runs ~10 % faster per K block but its epilogue is slower, so the static model
+        // does not rank it
         const bool pair_ok = (epi == EPI_F32 || epi == EPI_SWIGLU) && !m.bf16;
-        if (pair_ok)
-            for (int nt : {192, 128, 64, 256}) {
-                const int tiles = m.B * ((rows + nt - 1) / nt) * ((N + 255) / 256);
-                // measured: the pair mainloop runs ~10 % faster per K block, but its epilogue is
-                // slower, so the cost model leaves the choice to the autotuner
-                const double kcost = (split ? 0.57 : 0.30) * nt / 192.0 * 1.2;
-                for (int s = 1; s <= (partial ? 8 : 1) && s <= kb; ++s) {
-                    if (!splits_valid(kb, s, smax)) continue;
-                    const int kbps = (kb + s - 1) / s;
-                    const int cap = gemm2_capacity(nt, epi, split);
-                    if (cap <= 0) continue;
-                    const int ctas = 2 * tiles * s, waves = (ctas + cap - 1) / cap;
-                    const double cost = waves * (kbps * kcost + 1.5) + (s > 1 ? 0.3 * s : 0.0);
-                    if (cost < best - 1e-9) { best = cost; bn_best = 2000 + nt; s_best = s; }
-                }
-            }
         if (!bn_best) return fail(TSN_ERR_ARG, std::string(name) + ": no tile fits N=" + std::to_string(N));
         auto fo = m.gemm_force.find(m.gemm_seq);
         if (fo != m.gemm_force.end()) {
