@@ -126,16 +126,17 @@ int tsn_dit_get_geom(tsn_dit * m, tsn_dit_geom * out);
 size_t tsn_dit_weight_bytes(tsn_dit * m);
 
 /* Fix the sequence geometry and allocate every activation buffer (src/dit.cpp:63-88):
- * T latent rows, clip_S clip rows, text_S text rows; arms = 2 runs cond and uncond batched in one
- * forward (CFG), arms = 1 runs a single arm (the 2-GPU CFG split). */
+ * T latent rows, clip_S clip rows, text_S text rows. arms = 2 runs one generation's cond and uncond
+ * arms batched in one forward (CFG); arms = 2G (4, 6, 8) batches G independent generations, each
+ * with its two arms (cond at 2g, uncond at 2g + 1), all stepping on the same schedule; arms = 1
+ * runs a single arm (the 2-GPU CFG split). */
 int tsn_dit_prepare(tsn_dit * m, uint32_t T, uint32_t clip_S, uint32_t text_S, uint32_t arms);
 
 /* Per-generation conditioning, the outputs of DitModel::prep_conditioning / prep_text_arm
- * (src/dit.cpp:55-192): clip_pp [C,H], sync_gather [T,H] shared by the arms; text_pp [arms][TS,H]
- * and gcmlp [arms][H] per arm (cond first). Any-pointers; copied into the model. */
+ * (src/dit.cpp:55-192): clip_pp [G][C,H], sync_gather [G][T,H] shared by a generation's arms;
+ * text_pp [arms][TS,H] and gcmlp [arms][H] per arm (cond first). Any-pointers; copied in. */
 int tsn_dit_set_conditioning(tsn_dit * m, const float * clip_pp, const float * sync_gather,
                              const float * text_pp, const float * gcmlp);
-/* Latent x [T,64] (any-pointer in / out). */
 /* Read back the model's conditioning buffers (the layouts of tsn_dit_set_conditioning); any
  * pointer may be null to skip that buffer. */
 int tsn_dit_get_conditioning(tsn_dit * m, float * clip_pp, float * sync_gather, float * text_pp, float * gcmlp);
@@ -143,13 +144,14 @@ int tsn_dit_get_conditioning(tsn_dit * m, float * clip_pp, float * sync_gather, 
  * clip_f [C][1024] (C = the prepared clip rows) and sync_f [sync_S][768] f32, host or device
  * pointers. Writes the model's clip_pp and sync_gather and keeps clip_fc for the text arms.
  * Needs the once-per-generation conditioning weights in the model's source (loaded on first use)
- * and H = 1024. */
+ * and H = 1024; one generation (arms 1 or 2). */
 int tsn_dit_prep_conditioning(tsn_dit * m, const float * clip_f, const float * sync_f, int sync_S);
 /* DitModel::prep_text_arm (src/dit.cpp:137-192) for CFG arm `arm` (< the prepared arms):
  * text_cat [TS][2048] and gtext [1024] f32 -> the model's text_pp[arm] and gcmlp[arm].
  * After tsn_dit_prep_conditioning; together they replace tsn_dit_set_conditioning. */
 int tsn_dit_prep_text_arm(tsn_dit * m, int arm, const float * text_cat, const float * gtext);
 
+/* Latent x [G][T,64] (any-pointer in / out). */
 int tsn_dit_set_x(tsn_dit * m, const float * x);
 int tsn_dit_get_x(tsn_dit * m, float * x_out);
 

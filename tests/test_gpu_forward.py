@@ -181,3 +181,31 @@ def test_full_depth_forward_vs_oracle(dev, full_gguf):
     inp = make_inputs(T, C, TS, FULL["H"])
     m = gpu_model(dev, full_gguf, inp, T, C, TS)
     check_taps(m, O.Oracle(full_gguf), inp, T, C, TS, 0.5)
+
+
+def test_two_generations_batched_match_single(dev, tiny_gguf):
+    """arms = 4 (two generations, each with its cond and uncond arm) gives each generation's
+    single-generation flow and sampler step."""
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    gens = [make_inputs(T, C, TS, TINY["H"], seed=SEED + 20 + g) for g in range(2)]
+    m = tsn.Dit(dev, gguf=tiny_gguf)
+    m.prepare(T, C, TS, 4)
+    m.set_conditioning(np.stack([g["clip_pp"] for g in gens]), np.stack([g["sync_gather"] for g in gens]),
+                       np.stack([g[k] for g in gens for k in ("text_pp_cond", "text_pp_unc")]),
+                       np.stack([g[k] for g in gens for k in ("gcmlp_cond", "gcmlp_unc")]))
+    m.set_x(np.stack([g["x"] for g in gens]))
+    flow4 = np.zeros((4, T, 64), np.float32)
+    m.forward(0.5, flow4)
+    dt = float(np.float32(1.0 - 1.0 / 24) - np.float32(1.0))
+    m.step(1.0, 5.0, dt)
+    x4 = np.zeros((2, T, 64), np.float32)
+    m.get_x(x4)
+    for g, inp in enumerate(gens):
+        one = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+        flow2 = np.zeros((2, T, 64), np.float32)
+        one.forward(0.5, flow2)
+        assert rel_l2(flow4[2 * g:2 * g + 2], flow2) < 1e-5
+        one.step(1.0, 5.0, dt)
+        x1 = np.zeros((T, 64), np.float32)
+        one.get_x(x1)
+        assert rel_l2(x4[g] - inp["x"], x1 - inp["x"]) < 1e-5

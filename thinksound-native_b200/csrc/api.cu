@@ -256,8 +256,8 @@ int tsn_dit_set_conditioning(tsn_dit * m, const float * clip_pp, const float * s
     M_BEGIN NEED_PREPARED
     const size_t H = M.g.H;
     cudaStream_t s = M.dev->stream;
-    CKR(cudaMemcpyAsync(M.clip_pp, clip_pp, (size_t) M.C * H * 4, cudaMemcpyDefault, s));
-    CKR(cudaMemcpyAsync(M.sync_gather, sync_gather, (size_t) M.T * H * 4, cudaMemcpyDefault, s));
+    CKR(cudaMemcpyAsync(M.clip_pp, clip_pp, (size_t) M.G * M.C * H * 4, cudaMemcpyDefault, s));
+    CKR(cudaMemcpyAsync(M.sync_gather, sync_gather, (size_t) M.G * M.T * H * 4, cudaMemcpyDefault, s));
     CKR(cudaMemcpyAsync(M.text_pp, text_pp, (size_t) M.B * M.TS * H * 4, cudaMemcpyDefault, s));
     CKR(cudaMemcpyAsync(M.gcmlp, gcmlp, (size_t) M.B * H * 4, cudaMemcpyDefault, s));
     CKR(cudaStreamSynchronize(s));
@@ -268,8 +268,8 @@ int tsn_dit_get_conditioning(tsn_dit * m, float * clip_pp, float * sync_gather, 
     M_BEGIN NEED_PREPARED
     const size_t H = M.g.H;
     cudaStream_t s = M.dev->stream;
-    if (clip_pp) CKR(cudaMemcpyAsync(clip_pp, M.clip_pp, (size_t) M.C * H * 4, cudaMemcpyDefault, s));
-    if (sync_gather) CKR(cudaMemcpyAsync(sync_gather, M.sync_gather, (size_t) M.T * H * 4, cudaMemcpyDefault, s));
+    if (clip_pp) CKR(cudaMemcpyAsync(clip_pp, M.clip_pp, (size_t) M.G * M.C * H * 4, cudaMemcpyDefault, s));
+    if (sync_gather) CKR(cudaMemcpyAsync(sync_gather, M.sync_gather, (size_t) M.G * M.T * H * 4, cudaMemcpyDefault, s));
     if (text_pp) CKR(cudaMemcpyAsync(text_pp, M.text_pp, (size_t) M.B * M.TS * H * 4, cudaMemcpyDefault, s));
     if (gcmlp) CKR(cudaMemcpyAsync(gcmlp, M.gcmlp, (size_t) M.B * H * 4, cudaMemcpyDefault, s));
     return M.dev->sync();
@@ -289,14 +289,14 @@ int tsn_dit_prep_text_arm(tsn_dit * m, int arm, const float * text_cat, const fl
 
 int tsn_dit_set_x(tsn_dit * m, const float * x) {
     M_BEGIN NEED_PREPARED
-    CKR(cudaMemcpyAsync(M.x, x, (size_t) M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
+    CKR(cudaMemcpyAsync(M.x, x, (size_t) M.G * M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
     CKR(cudaStreamSynchronize(M.dev->stream));
     return TSN_OK;
 }
 
 int tsn_dit_get_x(tsn_dit * m, float * x) {
     M_BEGIN NEED_PREPARED
-    CKR(cudaMemcpyAsync(x, M.x, (size_t) M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
+    CKR(cudaMemcpyAsync(x, M.x, (size_t) M.G * M.T * M.g.latent_dim * 4, cudaMemcpyDefault, M.dev->stream));
     return M.dev->sync();
 }
 
@@ -358,7 +358,7 @@ static int ensure_step_graph(Model & M, float cfg) {
 
 int tsn_dit_step(tsn_dit * m, float t, float cfg, float dt) {
     M_BEGIN NEED_PREPARED
-    if (M.B != 2) return fail(TSN_ERR_STATE, "tsn_dit_step needs arms = 2");
+    if (M.A != 2) return fail(TSN_ERR_STATE, "tsn_dit_step needs both CFG arms (arms = 2 per generation)");
     TRY(ensure_step_graph(M, cfg));
     TRY(M.set_time(t, dt));
     CKR(cudaGraphLaunch(M.gx_step, M.dev->stream));
@@ -367,7 +367,7 @@ int tsn_dit_step(tsn_dit * m, float t, float cfg, float dt) {
 
 int tsn_dit_schedule(tsn_dit * m, int steps, float cfg) {
     M_BEGIN NEED_PREPARED
-    if (M.B != 2) return fail(TSN_ERR_STATE, "the sampler needs arms = 2");
+    if (M.A != 2) return fail(TSN_ERR_STATE, "the sampler needs both CFG arms (arms = 2 per generation)");
     if (steps < 1 || steps > M.max_steps) return fail(TSN_ERR_ARG, "steps out of range");
     TRY(ensure_step_graph(M, cfg));
     // src/pipeline.cpp:142-145
@@ -400,9 +400,9 @@ int tsn_dit_sample(tsn_dit * m, int steps, float cfg) {
 
 int tsn_dit_step_host(tsn_dit * m, const float * x_in, float * x_out, float t, float cfg, float dt) {
     M_BEGIN NEED_PREPARED
-    if (M.B != 2) return fail(TSN_ERR_STATE, "tsn_dit_step_host needs arms = 2");
+    if (M.A != 2) return fail(TSN_ERR_STATE, "tsn_dit_step_host needs both CFG arms (arms = 2 per generation)");
     TRY(ensure_step_graph(M, cfg));
-    const size_t bytes = (size_t) M.T * M.g.latent_dim * 4;
+    const size_t bytes = (size_t) M.G * M.T * M.g.latent_dim * 4;
     std::vector<float> tb(M.g.H);
     M.temb_host(t, tb.data());
     cudaStream_t s = M.dev->stream;

@@ -419,7 +419,7 @@ __global__ void cond_kernel(const CondArgs a) {
             const long long bt = r / a.H;
             const int t = (int) (bt % a.T), b = (int) (bt / a.T);
             const float gc = a.gcmlp[(long long) b * a.H + c] + a.te[c];
-            const float e = a.sync_gather[(long long) t * a.H + c] + gc;           // dit_fwd.cpp:135
+            const float e = a.sync_gather[((long long) (b / a.A) * a.T + t) * a.H + c] + gc;   // dit_fwd.cpp:135
             const float es = silu_d(e);                                            // dit_fwd.cpp:136-137
             const __half hi = __float2half_rn(es);
             a.extc16[r] = hi;
@@ -427,13 +427,15 @@ __global__ void cond_kernel(const CondArgs a) {
             if (a.tap_extc) a.tap_extc[r] = e;
         } else if (i < nC) {
             const long long r = i - nB;                                            // dit_fwd.cpp:166
-            a.clip_s[r] = a.clip_pp[r % ((long long) a.C * a.H)];
+            const long long per = (long long) a.C * a.H;
+            a.clip_s[r] = a.clip_pp[(r / per / a.A) * per + r % per];
         } else if (i < nD) {
             const long long r = i - nC;                                            // dit_fwd.cpp:167
             a.text_s[r] = a.text_pp[r];
         } else {
             const long long r = i - nD;
-            const float xv = a.x[r % ((long long) a.T * a.L)];
+            const long long per = (long long) a.T * a.L;
+            const float xv = a.x[(r / per / a.A) * per + r % per];
             const __half hi = __float2half_rn(xv);
             a.x16[r] = hi;
             a.x16[r + a.x_lo] = __float2half_rn(xv - __half2float(hi));
@@ -446,13 +448,14 @@ cudaError_t launch_cond(const CondArgs & a, cudaStream_t s) {
 }
 
 // =============================================================================== sampler
-__global__ void cfg_euler_kernel(const float * flow2, float * x, int n, float cfg, const float * dt_table,
+__global__ void cfg_euler_kernel(const float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
                                  const int * step, float dt_const) {
     pdl_trigger();
     pdl_wait();
     const float dt = dt_table ? dt_table[*step] : dt_const;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        const float fc = flow2[i], fu = flow2[n + i];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * gens; i += gridDim.x * blockDim.x) {
+        const int g = i / n, j = i % n;
+        const float fc = flow2[(2LL * g) * n + j], fu = flow2[(2LL * g + 1) * n + j];
         const float v = __fadd_rn(fu, __fmul_rn(__fsub_rn(fc, fu), cfg));
         x[i] = __fadd_rn(x[i], __fmul_rn(dt, v));
     }
@@ -463,9 +466,10 @@ __global__ void step_advance_kernel(int * step) {
     *step += 1;
 }
 
-cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, float cfg, const float * dt_table,
+cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
                              const int * step, float dt_const, cudaStream_t s) {
-    return launch_ex(cfg_euler_kernel, dim3((n + 255) / 256), dim3(256), 0, s, 1u, flow2, x, n, cfg, dt_table, step, dt_const);
+    return launch_ex(cfg_euler_kernel, dim3((n * gens + 255) / 256), dim3(256), 0, s, 1u, flow2, x, n, gens, cfg, dt_table,
+                     step, dt_const);
 }
 cudaError_t launch_step_advance(int * step, cudaStream_t s) {
     return launch_ex(step_advance_kernel, dim3(1), dim3(1), 0, s, 1u, step);

@@ -130,13 +130,15 @@ struct GemvJob {
 cudaError_t launch_gemv(const GemvJob * jobs_dev, int njobs, int max_n, int ab_bf16, cudaStream_t s);
 
 // ---- per-forward conditioning prologue (src/dit_fwd.cpp:131-140, 166-167) ----
+// B batch rows = G generations x A CFG arms (A = 2, or 1 for a single-arm model); the per-
+// generation inputs (sync_gather, clip_pp, x) are indexed by generation b / A.
 struct CondArgs {
     const float * te;            // [H]  t_embed output
     const float * gcmlp;         // [B][H]
-    const float * sync_gather;   // [T][H]
-    const float * clip_pp;       // [C][H]
+    const float * sync_gather;   // [G][T][H]
+    const float * clip_pp;       // [G][C][H]
     const float * text_pp;       // [B][TS][H]
-    const float * x;             // [T][L]
+    const float * x;             // [G][T][L]
     float * gc_silu;             // [B][H]
     __half * extc16;             // [B][T][H]  silu(sync_gather + gcmlp + te)
     float * clip_s;              // [B][C][H]
@@ -146,11 +148,13 @@ struct CondArgs {
     float * tap_extc;            // [B][T][H]  extended_c before silu (nullable)
     int B, T, C, TS, H, L;
     long long extc_lo, x_lo;     // element offsets of the lo halves of extc16 and x16
+    int A;                       // CFG arms per generation
 };
 cudaError_t launch_cond(const CondArgs & a, cudaStream_t s);
 
 // ---- x += dt * (fu + cfg * (fc - fu)) (src/pipeline.cpp:148, shaders/ops_conv.metal:194-201) ----
-cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, float cfg, const float * dt_table,
+// x[g] += dt (fu + cfg (fc - fu)) for g < gens, with fc = flow[2g], fu = flow[2g + 1], n floats each
+cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
                              const int * step, float dt_const, cudaStream_t s);
 cudaError_t launch_step_advance(int * step, cudaStream_t s);
 

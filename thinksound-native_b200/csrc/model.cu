@@ -411,9 +411,12 @@ void Model::temb_host(float t, float * out) const {
 }
 
 int Model::prepare(int T_, int C_, int TS_, int B_) {
-    if (T_ < 1 || C_ < 1 || TS_ < 1 || (B_ != 1 && B_ != 2)) return fail(TSN_ERR_ARG, "bad geometry for prepare");
+    if (T_ < 1 || C_ < 1 || TS_ < 1 || B_ < 1 || B_ > 8 || (B_ > 1 && B_ % 2))
+        return fail(TSN_ERR_ARG, "bad geometry for prepare (arms: 1, or 2 per generation up to 8)");
     release_activations();
     T = T_; C = C_; TS = TS_; B = B_;
+    A = B == 1 ? 1 : 2;
+    G = B / A;
     S = T + C + TS;
     S_pad = (S + 63) / 64 * 64;
     const size_t H = g.H, F = g.F, L = g.latent_dim, NJ = g.n_joint();
@@ -424,9 +427,9 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
         return TSN_OK;
     };
 #define ALLOC(ptr, bytes) do { int rc_ = al((bytes), (void **) &(ptr)); if (rc_) return rc_; } while (0)
-    ALLOC(x, T * L * 4);
-    ALLOC(clip_pp, C * H * 4);
-    ALLOC(sync_gather, T * H * 4);
+    ALLOC(x, G * T * L * 4);                 // per generation
+    ALLOC(clip_pp, G * C * H * 4);
+    ALLOC(sync_gather, G * T * H * 4);
     ALLOC(text_pp, B * TS * H * 4);
     ALLOC(gcmlp, B * H * 4);
     ALLOC(te_h, H * 4);
@@ -855,7 +858,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb + 1, 1, H, bfl, s); }, 2, 0, "t_embed.2"});
     CondArgs ca{te, gcmlp, sync_gather, clip_pp, text_pp, x, gc_silu, extc16, clip_s, text_s, x16,
                 tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L,
-                (long long) B * T * H, (long long) B * T * L};
+                (long long) B * T * H, (long long) B * T * L, A};
     ops.push_back(Op{[ca](cudaStream_t s) { return launch_cond(ca, s); }, 2, 0, "cond"});
     ops.push_back(Op{[jb, nmj, H, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, bfl, s); }, 2, 0, "adaln_gemv"});
     if (tp) {
@@ -990,8 +993,10 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         float * fl = flow, * xx = x;
         const float * dtt = dt_tab;
         int * st = step;
-        const int n = T * L;
-        ops.push_back(Op{[fl, xx, n, cfg, dtt, st](cudaStream_t s) { return launch_cfg_euler(fl, xx, n, cfg, dtt, st, 0.0f, s); },
+        const int n = T * L, gens = G;
+        ops.push_back(Op{[fl, xx, n, gens, cfg, dtt, st](cudaStream_t s) {
+                             return launch_cfg_euler(fl, xx, n, gens, cfg, dtt, st, 0.0f, s);
+                         },
                          2, 0, "cfg_euler"});
         ops.push_back(Op{[st](cudaStream_t s) { return launch_step_advance(st, s); }, 2, 0, "step_advance"});
     }

@@ -82,6 +82,7 @@ int mlp(DeviceCtx & c, const Lin & w1, const Lin & w3, const Lin & w2, const flo
 
 int Model::prep_conditioning(const float * clip_f, const float * sync_f, int sync_S) {
     if (g.H != 1024) return fail(TSN_ERR_UNSUPPORTED, "prep_conditioning needs H = 1024 (its cond projections read 1024 inputs)");
+    if (G != 1) return fail(TSN_ERR_UNSUPPORTED, "prep_conditioning serves models prepared for one generation");
     if (sync_S < 1) return fail(TSN_ERR_ARG, "sync_S must be positive");
     RT(load_prep(*this));
     DeviceCtx & c = *dev;

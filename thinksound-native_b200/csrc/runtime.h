@@ -109,6 +109,8 @@ struct Model {
     // geometry (tsn_dit_prepare)
     bool prepared = false;
     int T = 0, C = 0, TS = 0, B = 0, S = 0, S_pad = 0;
+    int A = 2, G = 1;     // B = G generations x A CFG arms (A = 1: one arm of a CFG split)
+
     std::vector<void *> act;
     float * x = nullptr, * clip_pp = nullptr, * sync_gather = nullptr, * text_pp = nullptr, * gcmlp = nullptr;
     float * te_h = nullptr, * te = nullptr, * gc_silu = nullptr, * lat = nullptr, * clip_s = nullptr, * text_s = nullptr;
