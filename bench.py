@@ -12,6 +12,9 @@ generations) with no cross-GPU traffic in the timed region; v
 steps of all ranks divided by the slowest rank's device time (weak scaling).
 With --cfg-split, ranks 2k and 2k+1 share one generation instead: each runs one CFG arm and the
 pair all-gathers the two flows every step (BASELINE config 3 on 2 GPUs; a latency mode).
+With --config5, the ranks share BASELINE config 5: 64 independent 24-step generations (seeds
+0..63, contiguous seed ranges per rank), --gens-per-forward of them batched in each forward, and
+one gather of the final latents to rank 0; the line reports generations/s.
 
 --impl reference times the reference's own CPU implementation of the path (the reference's
 src/dit_fwd.cpp built over the scalar kernel transliteration in oracle/_ref; the oracle port when
@@ -54,6 +57,9 @@ def parse():
     ap.add_argument("--no-autotune", action="store_true", help="keep the static tile cost model")
     ap.add_argument("--cfg-split", action="store_true", help="one CFG arm per rank, pairs of ranks per generation")
     ap.add_argument("--long", action="store_true", help="BASELINE config 4 geometry: 30 s audio (T=704, clip 240, text 77)")
+    ap.add_argument("--config5", action="store_true", help="64 generations x 24 steps, data-parallel, final gather")
+    ap.add_argument("--gens-per-forward", type=int, default=4, help="config 5: generations batched per forward (1-4)")
+    ap.add_argument("--generations", type=int, default=64)
     return ap.parse_args()
 
 
@@ -475,6 +481,94 @@ def run_cfg_split(a):
     dist.destroy_process_group()
 
 
+def run_config5(a):
+    """`generations` independent 24-step generations split over the ranks as
+    contiguous seed ranges, G = --gens-per-forward of them sampled together (arms = 2G); the final
+    latents are gathered to rank 0 once at the end."""
+    import datetime
+
+    import numpy as np
+    import torch
+
+    import tsn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    G = max(1, min(4, a.gens_per_forward))
+    per_rank = (a.generations + world - 1) // world
+    mine = list(range(rank * per_rank, min(a.generations, (rank + 1) * per_rank)))
+    steps = 24
+    stream = torch.cuda.Stream()
+    dev = tsn.Device(local, stream=stream.cuda_stream)
+    m = tsn.Dit(dev, synthetic=tsn.geom(**geom_kwargs(a)), seed=a.seed)
+    m.prepare(a.T, a.C, a.TS, 2 * G)
+
+    def inputs(gens):
+        xs, cps, sgs, tps, gcs = [], [], [], [], []
+        for g in gens:
+            rng = np.random.default_rng(g)                     # per-generation seed (config 5: seeds 0..63)
+            f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
+            cps.append(f(a.C, a.H)); sgs.append(f(a.T, a.H)); tps.append(f(2, a.TS, a.H)); gcs.append(f(2, a.H))
+            xs.append(f(a.T, 64))
+        return (np.stack(cps), np.stack(sgs), np.concatenate(tps), np.concatenate(gcs), np.stack(xs))
+
+    def run_batch(gens):
+        cp, sg, tp, gc, x = inputs(gens + [gens[-1]] * (G - len(gens)))   # a short last batch repeats
+        m.set_conditioning(cp, sg, tp, gc)
+        m.set_x(x)
+        m.schedule(steps, a.cfg)
+        m.run_steps(steps)
+        out = np.zeros((G, a.T, 64), np.float32)
+        m.get_x(out)
+        return out[:len(gens)]
+
+    with torch.cuda.stream(stream):
+        m.set_conditioning(*inputs(list(range(G)))[:4])
+        m.set_x(inputs(list(range(G)))[4])
+        if not a.no_autotune:
+            m.autotune()
+        run_batch(list(range(G)))                               # warm-up
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        finals = [run_batch(mine[i:i + G]) for i in range(0, len(mine), G)]
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        x_all = np.concatenate(finals) if finals else np.zeros((0, a.T, 64), np.float32)
+        times = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        if dist:
+            dist.all_reduce(times, op=dist.ReduceOp.MAX)
+            # the only cross-GPU traffic: the final latents to rank 0
+            buf = torch.zeros(per_rank, a.T, 64, dtype=torch.float32, device="cuda")
+            buf[:len(mine)] = torch.from_numpy(x_all).cuda()
+            gathered = [torch.empty_like(buf) for _ in range(world)] if rank == 0 else None
+            dist.gather(buf, gathered, dst=0)
+        ms = float(times[0])
+        finite = bool(np.isfinite(x_all).all())
+        if rank == 0:
+            gen_s = a.generations / (ms * 1e-3)
+            print(json.dumps({
+                "metric": "config 5: independent 8 s generations/s (24-step CFG-5 sampler), data-parallel",
+                "value": gen_s, "unit": "generations/s", "n_gpus": world, "generations": a.generations,
+                "gens_per_forward": G, "steps_per_generation": steps, "seconds": ms * 1e-3,
+                "cfg_steps_per_s": gen_s * steps, "higher_is_better": True, "scaling": "strong",
+                "data": "synthetic", "config": dict(workload(a), parallelism=f"dp{world}, {G} generation(s) per forward"),
+                "x_finite": finite}), flush=True)
+    m.close()
+    dev.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     a = parse()
     apply_long(a)
@@ -482,6 +576,8 @@ def main():
         run_reference(a)
     elif a.cfg_split:
         run_cfg_split(a)
+    elif a.config5:
+        run_config5(a)
     else:
         run_tsn(a)
 
