@@ -203,7 +203,31 @@ KernelFn kernel_for(int bn, int epi, bool split) {
     }
     return nullptr;
 }
+using GroupFn = void (*)(GroupMaps, GroupArgs, int);
+template <int BN, int EPI, bool SPLIT>
+GroupFn pick_group() {
+    return (GroupFn) gemm_tc_group<BN, EPI, stages_for(BN, SPLIT, EPI), SPLIT>;
+}
+// the grouped instantiations the joint blocks use: qkv, swiglu (split operands), f32 (both)
+template <int BN>
+GroupFn group_epi(int epi, bool split) {
+    if (epi == EPI_QKV && split) return pick_group<BN, EPI_QKV, true>();
+    if (epi == EPI_SWIGLU && split) return pick_group<BN, EPI_SWIGLU, true>();
+    if (epi == EPI_F32) return split ? pick_group<BN, EPI_F32, true>() : pick_group<BN, EPI_F32, false>();
+    return nullptr;
+}
+GroupFn group_for(int bn, int epi, bool split) {
+    switch (bn) {
+        case 64: return group_epi<64>(epi, split);
+        case 128: return group_epi<128>(epi, split);
+        case 192: return group_epi<192>(epi, split);
+        case 256: return group_epi<256>(epi, split);
+    }
+    return nullptr;
+}
 } // namespace
+
+bool gemm_group_supported(int bn, int epi, bool split) { return group_for(bn, epi, split) != nullptr; }
 
 // Set the dynamic shared-memory limit of every instantiation once, outside any stream capture.
 cudaError_t configure_gemm_kernels() {
@@ -211,6 +235,15 @@ cudaError_t configure_gemm_kernels() {
         for (int bn : {64, 128, 192, 256})
             for (int epi = 0; epi < 6; ++epi) {
                 KernelFn fn = kernel_for(bn, epi, split != 0);
+                if (!fn) continue;
+                cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                     (int) gemm_smem_bytes(bn, split != 0, epi));
+                if (e != cudaSuccess) return e;
+            }
+    for (int split = 0; split < 2; ++split)
+        for (int bn : {64, 128, 192, 256})
+            for (int epi = 0; epi < 6; ++epi) {
+                GroupFn fn = group_for(bn, epi, split != 0);
                 if (!fn) continue;
                 cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      (int) gemm_smem_bytes(bn, split != 0, epi));
@@ -253,6 +286,22 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
     // split-K: the K slices of one output tile form a cluster along grid.z
     return launch_ex(fn, g.grid, dim3(192), g.smem, s, g.args.splits > 1 ? (unsigned) g.args.splits : 1u,
                      g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
+}
+
+cudaError_t launch_gemm_group(const GroupLaunch & g, cudaStream_t s) {
+    GroupFn fn = group_for(g.bn, g.epi, g.split);
+    const int n = g.args.n;
+    if (!fn || n < 1 || n > MAX_GROUP || g.cluster < 1 || g.cluster > 8) return cudaErrorInvalidValue;
+    for (int q = 0; q < n; ++q) {
+        const int begin = q ? g.args.cta_end[q - 1] : 0;
+        if (g.args.cta_end[q] <= begin || g.args.slices[q] < 1 || g.args.m_tiles[q] < 1) return cudaErrorInvalidValue;
+        // clusters never straddle two problems, and a cluster is exactly one tile's K slices
+        if (g.cluster > 1 && (begin % g.cluster || g.args.slices[q] != g.cluster || g.args.p[q].splits != g.cluster))
+            return cudaErrorInvalidValue;
+        if (g.cluster == 1 && g.args.p[q].splits != 1) return cudaErrorInvalidValue;
+    }
+    return launch_cl(fn, dim3((unsigned) g.args.cta_end[n - 1]), dim3(192), g.smem, s, dim3((unsigned) g.cluster, 1, 1),
+                     g.maps, g.args, g.ab_bf16);
 }
 
 // CTAs of the 2-SM kernel that can run at once (in pairs)

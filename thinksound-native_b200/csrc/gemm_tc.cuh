@@ -124,8 +124,8 @@ template <int BN> struct TmemCols {
 // partials). In the TMEM path every lane must call load32 (warp-collective tcgen05.ld), so the
 // validity test only guards the stores.
 template <int EPI, typename Load>
-__device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec, int r, int u, int n0, int t0, int b0, bool ok,
-                                         Load && load32) {
+__device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec, int r, int u, int n0, int t0, int b0, int z,
+                                         bool ok, Load && load32) {
     constexpr int U = EpiUnit<EPI>::U;
     const int b = b0 + r / a.bt, t = t0 + r % a.bt;
     const int c0 = u * U;
@@ -196,7 +196,7 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             for (int e = 0; e < 32; ++e) v[e] += ec.bias[c0 + e];
         }
         if constexpr (EPI == EPI_F32) {
-            float * o = (float *) a.out + blockIdx.z * a.part_stride + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+            float * o = (float *) a.out + z * a.part_stride + (long long) b * a.out_bs + (long long) t * a.ldo + n;
 #pragma unroll
             for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
         } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU) {
@@ -211,10 +211,12 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
     }
 }
 
+// One output tile (M tile mi, N tile ni, K slice z) computed by the whole CTA; `cta` indexes the
+// trace rows. The tensor maps are kernel parameters (grid constants).
 template <int BN, int EPI, int STAGES, bool SPLIT>
-__global__ void __launch_bounds__(192, 1)
-gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
-               const __grid_constant__ CUtensorMap tmB, const GemmArgs a, const int ab_bf16) {
+__device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtensorMap * tmA2, const CUtensorMap * tmB,
+                                          const GemmArgs & a, const int ab_bf16, const int mi, const int ni, const int z,
+                                          const int cta) {
     using L = GemmSmem<BN, STAGES, SPLIT, EPI>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
@@ -228,15 +230,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     float4 * crope = (float4 *) (smem + L::ROPE_OFF);      // qkv: ROPE_ROWS x ROPE_STRIDE4
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     unsigned long long * tr = a.trace ? a.trace + (size_t) cta * TRACE_SLOTS : nullptr;
     if (tr && threadIdx.x == 0) tr[0] = global_ns();
-    // with m_fast the CTAs that share a weight tile are launched next to each other, so a weight
-    // matrix larger than L2 is streamed from HBM once rather than once per M tile
-    const int mi = a.m_fast ? blockIdx.x : blockIdx.y, ni = a.m_fast ? blockIdx.y : blockIdx.x;
     const int mt = mi % a.m_tiles_t, mb = mi / a.m_tiles_t;
     const int t0 = mt * a.bt, b0 = mb * a.bb, n0 = ni * BN;
-    const int kb_begin = blockIdx.z * a.kb_per_split;
+    const int kb_begin = z * a.kb_per_split;
     const int kb_end = min(a.k_blocks, kb_begin + a.kb_per_split);
     const int nk = kb_end - kb_begin;
 
@@ -248,9 +246,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     if (threadIdx.x == 0) pdl_trigger();
     if (warp == 4 && lane == 0) {
-        tma_prefetch(&tmA);
-        if (SPLIT) tma_prefetch(&tmA2);
-        tma_prefetch(&tmB);
+        tma_prefetch(tmA);
+        if (SPLIT) tma_prefetch(tmA2);
+        tma_prefetch(tmB);
     }
     if (warp == 5) tmem_alloc(tslot, TmemCols<BN>::N);
     tc_fence_before();
@@ -267,7 +265,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             for (int i = 0; i < pre; ++i) {
                 uint8_t * sa = smem + i * L::STAGE;
                 mbar_expect_tx(&full[i], L::STAGE);
-                tma_load_2d(sa + L::B_OFF, &tmB, &full[i], (kb_begin + i) * 64, n0);
+                tma_load_2d(sa + L::B_OFF, tmB, &full[i], (kb_begin + i) * 64, n0);
             }
             pdl_wait();
             for (int i = 0; i < nk; ++i) {
@@ -279,10 +277,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 uint8_t * sa = smem + s * L::STAGE;
                 if (i >= pre) {
                     mbar_expect_tx(&full[s], L::STAGE);
-                    tma_load_2d(sa + L::B_OFF, &tmB, &full[s], kb * 64, n0);
+                    tma_load_2d(sa + L::B_OFF, tmB, &full[s], kb * 64, n0);
                 }
-                tma_load_3d(sa, &tmA, &full[s], ic0, t0 + tap - a.pad, b0);
-                if (SPLIT) tma_load_3d(sa + L::A_BYTES, &tmA2, &full[s], ic0, t0 + tap - a.pad, b0);
+                tma_load_3d(sa, tmA, &full[s], ic0, t0 + tap - a.pad, b0);
+                if (SPLIT) tma_load_3d(sa + L::A_BYTES, tmA2, &full[s], ic0, t0 + tap - a.pad, b0);
             }
         }
     } else if (warp == 5) {
@@ -331,7 +329,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (a.splits == 1) {
             auto load_tmem = [&](int c, float * v) { tmem_ld32(trow + c, v); };
 #pragma unroll 1
-            for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, ec, r, u, n0, t0, b0, ok, load_tmem);
+            for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, ec, r, u, n0, t0, b0, z, ok, load_tmem);
         } else {
             // stage this CTA's partial in its own shared memory as [BN/4][128] float4 (the stage ring
             // is free: every TMA load was consumed and every MMA has completed)
@@ -380,7 +378,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         v[4 * j] = acc.x; v[4 * j + 1] = acc.y; v[4 * j + 2] = acc.z; v[4 * j + 3] = acc.w;
                     }
                 };
-                epi_unit<EPI>(a, ec2, rr, u, n0, t0, b0, true, load_dsmem);
+                epi_unit<EPI>(a, ec2, rr, u, n0, t0, b0, z, true, load_dsmem);
             }
         }
         if (tr && threadIdx.x == 0) tr[7] = global_ns();
@@ -396,6 +394,50 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint64_t t1 = global_ns();
         while (global_ns() - t1 < 20000ull) {}
     }
+}
+
+template <int BN, int EPI, int STAGES, bool SPLIT>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ GemmArgs a, const int ab_bf16) {
+    // with m_fast the CTAs that share a weight tile are launched next to each other, so a weight
+    // matrix larger than L2 is streamed from HBM once rather than once per M tile
+    const int mi = a.m_fast ? blockIdx.x : blockIdx.y, ni = a.m_fast ? blockIdx.y : blockIdx.x;
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    gemm_tile<BN, EPI, STAGES, SPLIT>(&tmA, &tmA2, &tmB, a, ab_bf16, mi, ni, (int) blockIdx.z, cta);
+}
+
+// ------------------------------------------------------------------------------------------
+// Grouped launch: up to MAX_GROUP independent GEMMs with one tile shape and epilogue kind (the
+// latent, clip and text streams of a joint block run the same projection with their own weights,
+// rows and outputs). grid.x is the concatenation of the problems' CTAs, problem q owning
+// [cta_end[q-1], cta_end[q]); inside a problem consecutive CTAs are the K slices of one tile and
+// tiles go M tile fastest. The slices either form a cluster along x (in-cluster split-K reduction:
+// every problem then has `slices` equal to the cluster size and starts on a cluster boundary) or
+// are independent partial tiles (EPI_F32 with part_stride, any slice count per problem). One
+// launch fills the SMs with all three streams' tiles where three launches would contend for them.
+constexpr int MAX_GROUP = 3;
+struct GroupMaps {
+    CUtensorMap a[MAX_GROUP], a2[MAX_GROUP], b[MAX_GROUP];
+};
+struct GroupArgs {
+    GemmArgs p[MAX_GROUP];
+    int n;                     // problems in the group
+    int cta_end[MAX_GROUP];    // exclusive end of each problem's CTA range in grid.x
+    int slices[MAX_GROUP];     // K slices per tile
+    int m_tiles[MAX_GROUP];    // M tiles per problem
+};
+
+template <int BN, int EPI, int STAGES, bool SPLIT>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_group(const __grid_constant__ GroupMaps maps, const __grid_constant__ GroupArgs g, const int ab_bf16) {
+    const int x = (int) blockIdx.x;
+    int q = 0;
+    while (q + 1 < g.n && x >= g.cta_end[q]) ++q;
+    const int l = x - (q ? g.cta_end[q - 1] : 0);
+    const int S = g.slices[q], z = l % S, tile = l / S;
+    const int mi = tile % g.m_tiles[q], ni = tile / g.m_tiles[q];
+    gemm_tile<BN, EPI, STAGES, SPLIT>(&maps.a[q], &maps.a2[q], &maps.b[q], g.p[q], ab_bf16, mi, ni, z, x);
 }
 
 // ------------------------------------------------------------------------------------------

@@ -225,15 +225,9 @@ cudaError_t configure_attention() {
 }
 
 // =============================================================================== adaLN
+// one row per block; thread i owns float4 chunks i, i + TPR, ... of the row
 template <int NV>
-__global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
-    // one row per block; thread i owns float4 chunks i, i + TPR, ... of the row
-    unsigned long long * tr = a.trace ? a.trace + 3 * blockIdx.x : nullptr;
-    if (tr && threadIdx.x == 0) tr[0] = global_ns();
-    pdl_trigger();
-    pdl_wait();
-    if (tr && threadIdx.x == 0) tr[1] = global_ns();
-    const int row = blockIdx.x;
+__device__ __forceinline__ void adaln_row(const AdaLnArgs & a, const int row, unsigned long long * tr) {
     if (row >= a.B * a.rows) return;
     const int b = row / a.rows, t = row % a.rows;
     const int tid = threadIdx.x, TPR = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = TPR >> 5;
@@ -328,6 +322,32 @@ __global__ void __launch_bounds__(256) adaln_kernel(const AdaLnArgs a) {
     if (tr) { __syncthreads(); if (tid == 0) tr[2] = global_ns(); }
 }
 
+template <int NV>
+__global__ void __launch_bounds__(256) adaln_kernel(const __grid_constant__ AdaLnArgs a) {
+    unsigned long long * tr = a.trace ? a.trace + 3 * blockIdx.x : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
+    pdl_trigger();
+    pdl_wait();
+    if (tr && threadIdx.x == 0) tr[1] = global_ns();
+    adaln_row<NV>(a, (int) blockIdx.x, tr);
+}
+
+// the adaLNs of several residual streams in one launch: block x serves stream q's row
+// x - end[q-1] (the joint blocks' latent, clip and text streams step together)
+template <int NV>
+__global__ void __launch_bounds__(256) adaln_group_kernel(const __grid_constant__ AdaLnGroup g) {
+    const int x = (int) blockIdx.x;
+    int q = 0;
+    while (q + 1 < g.n && x >= g.end[q]) ++q;
+    const AdaLnArgs & a = g.p[q];
+    unsigned long long * tr = a.trace ? a.trace + 3 * x : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
+    pdl_trigger();
+    pdl_wait();
+    if (tr && threadIdx.x == 0) tr[1] = global_ns();
+    adaln_row<NV>(a, x - (q ? g.end[q - 1] : 0), tr);
+}
+
 int adaln_threads(int H) {
     if (H % 128) return 0;
     for (int nv : {1, 2, 4}) {
@@ -345,6 +365,24 @@ cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s) {
         case 1: return launch_ex(adaln_kernel<1>, grid, dim3(tpr), 0, s, 1u, a);
         case 2: return launch_ex(adaln_kernel<2>, grid, dim3(tpr), 0, s, 1u, a);
         case 4: return launch_ex(adaln_kernel<4>, grid, dim3(tpr), 0, s, 1u, a);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_adaln_group(const AdaLnGroup & g, cudaStream_t s) {
+    if (g.n < 1 || g.n > MAX_GROUP) return cudaErrorInvalidValue;
+    const int H = g.p[0].H, tpr = adaln_threads(H);
+    if (!tpr) return cudaErrorInvalidValue;
+    for (int q = 0; q < g.n; ++q) {
+        const AdaLnArgs & a = g.p[q];
+        if (a.H != H || (a.part && (a.nsplit < 1 || a.nsplit > MAX_PARTS))) return cudaErrorInvalidValue;
+        if (g.end[q] - (q ? g.end[q - 1] : 0) != a.B * a.rows) return cudaErrorInvalidValue;
+    }
+    const dim3 grid((unsigned) g.end[g.n - 1]);
+    switch (H / 4 / tpr) {
+        case 1: return launch_ex(adaln_group_kernel<1>, grid, dim3(tpr), 0, s, 1u, g);
+        case 2: return launch_ex(adaln_group_kernel<2>, grid, dim3(tpr), 0, s, 1u, g);
+        case 4: return launch_ex(adaln_group_kernel<4>, grid, dim3(tpr), 0, s, 1u, g);
         default: return cudaErrorInvalidValue;
     }
 }

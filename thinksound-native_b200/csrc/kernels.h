@@ -69,8 +69,20 @@ bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t b
 // Encode a 2-D TMA view {K, N} of an [N][K] 16-bit weight matrix with a {64, bn} box.
 bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16);
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
+// A grouped launch of up to MAX_GROUP GEMMs sharing tile width, epilogue and operand split
+// (gemm_tc_group): grid.x = args.cta_end[args.n - 1] CTAs, clusters of `cluster` along x.
+struct GroupLaunch {
+    GroupMaps maps;
+    GroupArgs args;
+    int bn = 0, epi = 0, ab_bf16 = 0;
+    bool split = false;
+    int cluster = 1;
+    size_t smem = 0;
+};
+cudaError_t launch_gemm_group(const GroupLaunch & g, cudaStream_t s);
 cudaError_t configure_gemm_kernels();
 int gemm_cluster_capacity(int bn, int epi, bool split, int cluster);
+bool gemm_group_supported(int bn, int epi, bool split);   // a grouped instantiation exists
 size_t gemm_smem_bytes(int bn, bool split, int epi);
 size_t gemm_persistent_smem_bytes(int bn);   // 0: no persistent kernel for this tile width
 size_t gemm2_smem_bytes(int nt, bool split);   // 0: no 2-SM kernel for this token tile
@@ -117,6 +129,13 @@ struct AdaLnArgs {
     const float * gmod; long long gmod_bs, gmod_ld; int gper_row, goff;   // gate rows, like mod
 };
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s);
+// several streams' adaLNs (same H) in one launch; stream q owns blocks [end[q-1], end[q])
+struct AdaLnGroup {
+    AdaLnArgs p[MAX_GROUP];
+    int n;
+    int end[MAX_GROUP];
+};
+cudaError_t launch_adaln_group(const AdaLnGroup & g, cudaStream_t s);
 int adaln_threads(int H);   // threads per row (one row per block), 0 when H is unsupported
 
 // ---- batched GEMV y[b][n] = act(W[n,:]·x[b,:] + bias[n]) ----

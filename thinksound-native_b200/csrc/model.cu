@@ -543,7 +543,7 @@ struct Plan {
     // reduction; then encode the TMA views. With `partial`, the S K-slices are independent CTAs that
     // write S partial tiles (the consumer adds them), so no cluster is formed.
     int gemm(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, int epi, GemmLaunch & g,
-             bool plain = false, bool partial = false) {
+             bool plain = false, bool partial = false, int force_bn = 0, int force_s = 0) {
         const int B = m.B;
         const bool split = !plain;
         const int bt = B >= 2 ? 64 : 128, bb = 128 / bt;
@@ -586,6 +586,12 @@ struct Plan {
                 bn_best = fb;
                 s_best = fs;
             }
+        }
+        if (force_bn) {   // a member of a grouped launch: the group fixed the tile and the K slices
+            if (!(splits_valid(kb, force_s, smax) && (N % force_bn == 0 || (force_bn == 192 && N >= 192))))
+                return fail(TSN_ERR_ARG, std::string(name) + ": group configuration does not fit");
+            bn_best = force_bn;
+            s_best = force_s;
         }
         char key[128];
         snprintf(key, sizeof key, "%d:%d:%d:%d:%d:%d:%d", rows, N, K_in, W.taps, epi, (int) split, (int) partial);
@@ -713,6 +719,226 @@ struct Plan {
                      gate_idx * (int) H};
         return TSN_OK;
     }
+    // ---------------------------------------------------------------- grouped launches
+    // The latent, clip and text streams of a joint block run the same projections with their own
+    // weights and rows. Launched separately they contend for the SMs (each launch is sized as if it
+    // had the GPU to itself); a grouped launch hands the block scheduler all three streams' tiles.
+    struct GItem { const void * A; int K_in, rows; const Lin * W; int pad; };
+    struct Strm {             // one residual stream of a joint block
+        const Blk * b; float * x; const __half * att; __half * xn; __half * h; int rows;
+        const float * mod; int per_row; long long mod_ld, mod_bs;
+    };
+
+    // Choose one tile width and K slicing for all members and plan each member with it. Without
+    // `partial` every member is cut into s K slices reduced inside a cluster of s CTAs; with it the
+    // member with the most K blocks is cut into s slices and every other one into slices of about the
+    // same depth, each slice an independent partial tile.
+    int group_plan(const char * name, const std::vector<GItem> & it, int epi, bool plain, bool partial,
+                   std::vector<GemmLaunch> & gl, std::vector<int> & zs, int & s_out, std::string & shape) {
+        const bool split = !plain;
+        const int B = m.B, bt = B >= 2 ? 64 : 128, bb = 128 / bt, mtb = (B + bb - 1) / bb;
+        const int smax = partial ? MAX_PARTS : 8;
+        int kbmax = 0;
+        for (const GItem & x : it) kbmax = std::max(kbmax, x.W->taps * x.K_in / 64);
+        auto slices_of = [&](int kb, int s) {
+            if (!partial) return s;
+            const int depth = (kbmax + s - 1) / s;
+            return (kb + depth - 1) / depth;
+        };
+        auto fits = [&](int bn, int s) {
+            if (bn <= 0 || bn > 256 || !gemm_group_supported(bn, epi, split) || s < 1 || s > smax) return false;
+            for (const GItem & x : it) {
+                const int kb = x.W->taps * x.K_in / 64, N = x.W->N;
+                if (x.K_in % 64 || !(N % bn == 0 || (bn == 192 && N >= 192))) return false;
+                if (!splits_valid(kb, slices_of(kb, s), smax)) return false;
+            }
+            return true;
+        };
+        int bn = 0, s = 1;
+        auto fo = m.gemm_force.find(m.gemm_seq);
+        if (fo != m.gemm_force.end() && fits(fo->second.first, fo->second.second)) {
+            bn = fo->second.first;
+            s = fo->second.second;
+        } else {
+            // static model: the CTAs' total work spread over the CTAs that fit at once, plus the
+            // longest CTA (the tail); same per-K-block costs as the single-GEMM model
+            double best = 1e30;
+            for (int cb : {256, 192, 128, 64})
+                for (int cs = 1; cs <= smax; ++cs) {
+                    if (!fits(cb, cs)) continue;
+                    const int cap = gemm_cluster_capacity(cb, epi, split, partial ? 1 : cs);
+                    if (cap <= 0) continue;
+                    const double kcost = split ? (cb == 256 ? 0.74 : cb == 192 ? 0.57 : cb == 128 ? 0.40 : 0.30)
+                                               : (cb == 256 ? 0.37 : cb == 192 ? 0.30 : cb == 128 ? 0.24 : 0.18);
+                    double work = 0.0, longest = 0.0;
+                    for (const GItem & x : it) {
+                        const int kb = x.W->taps * x.K_in / 64, z = slices_of(kb, cs), kbps = (kb + z - 1) / z;
+                        const int tiles = ((x.rows + bt - 1) / bt) * mtb * ((x.W->N + cb - 1) / cb);
+                        const double w = kbps * kcost + 1.5 + (z > 1 ? (partial ? 0.3 : 1.5) : 0.0);
+                        work += (double) tiles * z * w;
+                        longest = std::max(longest, w);
+                    }
+                    const double cost = work / cap + longest;
+                    if (cost < best - 1e-9) { best = cost; bn = cb; s = cs; }
+                }
+        }
+        if (!bn) return fail(TSN_ERR_ARG, std::string(name) + ": no group configuration fits");
+        gl.assign(it.size(), GemmLaunch{});
+        zs.assign(it.size(), 0);
+        shape = "group";
+        for (size_t q = 0; q < it.size(); ++q) {
+            const GItem & x = it[q];
+            zs[q] = slices_of(x.W->taps * x.K_in / 64, s);
+            int rc = gemm(name, x.A, x.K_in, x.rows, *x.W, x.pad, epi, gl[q], plain, partial, bn, zs[q]);
+            if (rc) return rc;
+            if (gl[q].pair_nt || gl[q].persistent) return fail(TSN_ERR_ARG, std::string(name) + ": group member not plain");
+            shape += "|" + last_shape;
+        }
+        s_out = s;
+        return TSN_OK;
+    }
+    // one grouped launch of planned members; members with the deepest CTAs first, so that the
+    // block scheduler starts the long CTAs before the short ones fill in behind them
+    void push_group(const char * name, const std::vector<GemmLaunch> & gl, const std::vector<int> & zs, bool partial, int s,
+                    double flops, const std::string & shape) {
+        std::vector<int> ord(gl.size());
+        for (size_t q = 0; q < ord.size(); ++q) ord[q] = (int) q;
+        std::stable_sort(ord.begin(), ord.end(),
+                         [&](int x, int y) { return gl[x].args.kb_per_split > gl[y].args.kb_per_split; });
+        GroupLaunch G;
+        G.bn = gl[0].bn; G.epi = gl[0].epi; G.split = gl[0].split; G.ab_bf16 = gl[0].ab_bf16; G.smem = gl[0].smem;
+        G.cluster = partial ? 1 : s;
+        int end = 0, n = 0;
+        std::string kbs;
+        for (int q : ord) {
+            const GemmLaunch & g = gl[q];
+            G.maps.a[n] = g.ta;
+            G.maps.a2[n] = g.split ? g.ta2 : g.ta;
+            G.maps.b[n] = g.tb;
+            G.args.p[n] = g.args;
+            G.args.slices[n] = zs[q];
+            G.args.m_tiles[n] = (int) g.grid.x;
+            end += (int) (g.grid.x * g.grid.y) * zs[q];
+            G.args.cta_end[n] = end;
+            kbs += (n ? "/" : "") + std::to_string(g.args.k_blocks) + "x" + std::to_string(zs[q]);
+            ++n;
+        }
+        G.args.n = n;
+        char d[200];
+        snprintf(d, sizeof d, "bn=%d split=%d ksplit=%d %s group=%d ctas=%d kb=%s smem=%zu", G.bn, (int) G.split, s,
+                 partial ? "partial" : "cluster", n, end, kbs.c_str(), G.smem);
+        Op op{[G](cudaStream_t st) { return launch_gemm_group(G, st); }, 0, flops, name, d};
+        op.gemm_id = m.gemm_seq++;
+        op.shape = shape;
+        op.traced = [G](cudaStream_t st, unsigned long long * tr) {
+            GroupLaunch t = G;
+            for (int q = 0; q < t.args.n; ++q) t.args.p[q].trace = tr;
+            return launch_gemm_group(t, st);
+        };
+        op.ctas = end;
+        double pb = 0.0;
+        if (partial)
+            for (int q : ord) pb += (double) gl[q].args.part_stride * 4 * zs[q];
+        op.part_bytes = pb / s;   // the autotuner charges part_bytes x s
+        add(op);
+    }
+    // a gated residual update (linear1 / ffn.w2) of every stream, partial tiles left for the next adaLN
+    int gate_group(const char * name, const std::vector<Strm> & st, bool w2, int gate_idx) {
+        std::vector<GItem> it;
+        const int H = (int) m.g.H, F = (int) m.g.F;
+        double flops = 0.0;
+        for (const Strm & x : st) {
+            const Lin & W = w2 ? x.b->w2 : x.b->l1;
+            it.push_back(GItem{w2 ? (const void *) x.h : (const void *) x.att, w2 ? F : H, x.rows, &W, x.b->conv ? 1 : 0});
+            flops += fl(m.B, x.rows, W);
+        }
+        std::vector<GemmLaunch> gl;
+        std::vector<int> zs;
+        int s = 1;
+        std::string shape;
+        int rc = group_plan(name, it, EPI_F32, w2, true, gl, zs, s, shape);
+        if (rc) return rc;
+        for (size_t q = 0; q < st.size(); ++q) {
+            const Strm & x = st[q];
+            float * ws = x.x == m.lat ? m.part_l : x.x == m.clip_s ? m.part_c : m.part_t;
+            GemmArgs & a = gl[q].args;
+            a.out = ws; a.ldo = H; a.out_bs = (long long) x.rows * H;
+            a.part_stride = (long long) m.B * x.rows * H;
+            a.bias = nullptr;
+            const Lin & W = w2 ? x.b->w2 : x.b->l1;
+            pend[x.x] = Pending{ws, a.part_stride, zs[q], W.b, x.mod, x.per_row ? x.mod_ld : 0, x.mod_bs, x.per_row,
+                                gate_idx * H};
+        }
+        push_group(name, gl, zs, true, s, flops, shape);
+        return TSN_OK;
+    }
+    void adaln_group(const char * name, const std::vector<Strm> & st, int base, bool to_xn) {
+        AdaLnGroup G{};
+        int end = 0;
+        for (size_t q = 0; q < st.size(); ++q) {
+            const Strm & x = st[q];
+            G.p[q] = adaln_args(x.x, x.rows, x.mod, x.per_row, x.mod_ld, x.mod_bs, base, to_xn ? x.xn : nullptr);
+            end += m.B * x.rows;
+            G.end[q] = end;
+        }
+        G.n = (int) st.size();
+        Op op{[G](cudaStream_t s) { return launch_adaln_group(G, s); }, 2, 0.0, name};
+        op.traced = [G](cudaStream_t s, unsigned long long * tr) {
+            AdaLnGroup t = G;
+            for (int q = 0; q < t.n; ++q) t.p[q].trace = tr;
+            return launch_adaln_group(t, s);
+        };
+        op.ctas = end;
+        op.trace_slots = 3;
+        add(op);
+    }
+    // fused qkv projection of every stream (joint rows at s_off[q] of the attention sequence)
+    int qkv_group(const char * name, const std::vector<Strm> & st, const int * s_off, const float2 * const * rope) {
+        std::vector<GItem> it;
+        double flops = 0.0;
+        for (const Strm & x : st) {
+            it.push_back(GItem{x.xn, (int) m.g.H, x.rows, &x.b->qkv, 0});
+            flops += fl(m.B, x.rows, x.b->qkv);
+        }
+        std::vector<GemmLaunch> gl;
+        std::vector<int> zs;
+        int s = 1;
+        std::string shape;
+        int rc = group_plan(name, it, EPI_QKV, false, false, gl, zs, s, shape);
+        if (rc) return rc;
+        for (size_t q = 0; q < st.size(); ++q) {
+            GemmArgs & a = gl[q].args;
+            a.qn = st[q].b->qn; a.kn = st[q].b->kn; a.rope = rope[q]; a.H = m.g.H; a.s_off = s_off[q];
+            a.S_pad = m.S_pad; a.NH = m.g.NH; a.q = m.q; a.k = m.k; a.v = m.v;
+            a.out_lo = (long long) m.B * m.g.NH * m.S_pad * 64;
+        }
+        push_group(name, gl, zs, false, s, flops, shape);
+        return TSN_OK;
+    }
+    // post_attn (src/dit_fwd.cpp:51-81) of every stream, one grouped launch per phase
+    int post_group(const std::vector<Strm> & st) {
+        const int F = (int) m.g.F;
+        int rc = gate_group("linear1", st, false, 2);
+        if (rc) return rc;
+        adaln_group("adaln_ffn", st, 3 * (int) m.g.H, true);
+        std::vector<GItem> it;
+        double flops = 0.0;
+        for (const Strm & x : st) {
+            it.push_back(GItem{x.xn, (int) m.g.H, x.rows, &x.b->w13, x.b->conv ? 1 : 0});
+            flops += fl(m.B, x.rows, x.b->w13);
+        }
+        std::vector<GemmLaunch> gl;
+        std::vector<int> zs;
+        int s = 1;
+        std::string shape;
+        if ((rc = group_plan("ffn_w13", it, EPI_SWIGLU, false, false, gl, zs, s, shape))) return rc;
+        for (size_t q = 0; q < st.size(); ++q) {
+            GemmArgs & a = gl[q].args;
+            a.out = st[q].h; a.ldo = F; a.out_bs = (long long) st[q].rows * F;
+        }
+        push_group("ffn_w13", gl, zs, false, s, flops, shape);
+        return gate_group("ffn_w2", st, true, 5);
+    }
     // apply a pending gated update to x without normalising (taps read x between blocks)
     void resolve(float * x, int rows) {
         if (pend.count(x)) adaln("gate_resolve", x, rows, nullptr, 0, 0, 0, 0, nullptr);
@@ -728,8 +954,9 @@ struct Plan {
         push(name, g, fl(m.B, rows, b.qkv));
         return TSN_OK;
     }
-    void adaln(const char * name, float * x, int rows, const float * mod, int per_row, long long mod_ld,
-               long long mod_bs, int base, __half * out) {
+    // adaLN arguments for residual stream x, taking over its pending gated update
+    AdaLnArgs adaln_args(float * x, int rows, const float * mod, int per_row, long long mod_ld, long long mod_bs, int base,
+                         __half * out) {
         AdaLnArgs a{x, (long long) rows * m.g.H, mod, mod_bs, mod_ld, per_row, base, out, (long long) rows * m.g.H,
                     m.B, rows, (int) m.g.H, 1e-5f, (long long) m.B * rows * m.g.H};
         auto it = pend.find(x);
@@ -739,6 +966,11 @@ struct Plan {
             a.gmod = pd.gmod; a.gmod_ld = pd.gmod_ld; a.gmod_bs = pd.gmod_bs; a.gper_row = pd.gper_row; a.goff = pd.goff;
             pend.erase(it);
         }
+        return a;
+    }
+    void adaln(const char * name, float * x, int rows, const float * mod, int per_row, long long mod_ld,
+               long long mod_bs, int base, __half * out) {
+        const AdaLnArgs a = adaln_args(x, rows, mod, per_row, mod_ld, mod_bs, base, out);
         Op op{[a](cudaStream_t s) { return launch_adaln(a, s); }, 2, 0.0, name};
         op.traced = [a](cudaStream_t s, unsigned long long * tr) {
             AdaLnArgs t = a;
@@ -880,7 +1112,34 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // joint blocks                                                src/dit_fwd.cpp:180-257
     // The latent, clip and text streams of a joint block meet only at attention: the clip and text
     // chains run on their own CUDA streams (1, 2) and join the latent stream (0) through events.
-    {
+    // With grouped launches (the default) the three streams instead step together on one stream:
+    // each phase of the block is one launch over all three streams' rows (TSN_NO_GROUP=1 selects
+    // the three-stream schedule, for comparison).
+    const bool grouped = std::getenv("TSN_NO_GROUP") == nullptr;
+    // taps of the first joint block: its text operand and q/k/v, then its attention outputs
+    auto tap_qkv = [&](Plan & p) {
+        p.tap("text_xn", xn_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
+        const int NH = (int) g.NH, Sp = S_pad, S_ = S;
+        for (const char * nm : {"a0_q", "a0_k", "a0_v"}) {
+            const __half * src = nm[3] == 'q' ? q : nm[3] == 'k' ? k : v;
+            p.tap(nm, src, (size_t) B * NH * Sp * 64 * 2,
+                  [NH, Sp, S_, H](const std::vector<uint8_t> & raw, int arm, std::vector<float> & out) {
+                      const uint16_t * hh = (const uint16_t *) raw.data();
+                      out.resize((size_t) S_ * H);
+                      for (int s = 0; s < S_; ++s)
+                          for (int h = 0; h < NH; ++h)
+                              for (int d = 0; d < 64; ++d)
+                                  out[(size_t) s * H + h * 64 + d] = h2f_host(hh[(((size_t) arm * NH + h) * Sp + s) * 64 + d]);
+                  });
+        }
+    };
+    auto tap_a0_out = [&](Plan & p) {
+        // a0_out is the concatenation [lat | clip | text] of these three (tsn_dit_tap joins them)
+        p.tap("a0_out_l", att_l, (size_t) B * T * H * 2, cvt_f16_arm((size_t) T * H));
+        p.tap("a0_out_c", att_c, (size_t) B * C * H * 2, cvt_f16_arm((size_t) C * H));
+        p.tap("a0_out_t", att_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
+    };
+    if (!grouped) {
         const int e0 = p.record();            // clip_s/text_s restarted, clip/text modulations ready
         p.cur = 1; p.wait(e0);
         p.cur = 2; p.wait(e0);
@@ -890,6 +1149,31 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         const bool pre_only = i == NJ - 1;
         float * mc = modc + (size_t) i * B * 6 * H, * mt = modt + (size_t) i * B * 6 * H;
         const float * ml = modl + mod_off[i];
+        if (grouped) {
+            const std::vector<Plan::Strm> st{
+                {&jl[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs},
+                {&jc[i], clip_s, att_c, xn_c, h_c, C, mc, 0, 0, 6LL * H},
+                {&jt[i], text_s, att_t, xn_t, h_t, TS, mt, 0, 0, 6LL * H}};
+            p.adaln_group("adaln_attn", st, 0, true);
+            const int s_off[3] = {0, T, T + C};
+            const float2 * const rp[3] = {rope_l, rope_c, nullptr};
+            if ((rc = p.qkv_group("qkv", st, s_off, rp))) return rc;
+            if (tp && i == 0) tap_qkv(p);
+            if ((rc = p.attention(S, T, C, TS))) return rc;
+            if (pre_only) rc = p.post(jl[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs);
+            else rc = p.post_group(st);
+            if (rc) return rc;
+            if (tp && i == 0) {
+                tap_a0_out(p);
+                p.resolve(lat, T);
+                p.tap("jb0_lat", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+                p.resolve(clip_s, C);
+                p.resolve(text_s, TS);
+                p.tap("jb0_clip", clip_s, (size_t) B * C * H * 4, cvt_f32_arm((size_t) C * H));
+                p.tap("jb0_text", text_s, (size_t) B * TS * H * 4, cvt_f32_arm((size_t) TS * H));
+            }
+            continue;
+        }
         p.adaln("adaln_attn", lat, T, ml, 1, NA, lat_mod_bs, 0, xn_l);
         if ((rc = p.qkv("qkv_lat", xn_l, T, jl[i], 0, rope_l))) return rc;
         p.cur = 1;
@@ -903,23 +1187,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         p.cur = 0;
         p.wait(ec);
         p.wait(et);
-        if (tp && i == 0) {
-            p.tap("text_xn", xn_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
-            const int NH = (int) g.NH, Sp = S_pad, S_ = S;
-            for (const char * nm : {"a0_q", "a0_k", "a0_v"}) {
-                const __half * src = nm[3] == 'q' ? q : nm[3] == 'k' ? k : v;
-                p.tap(nm, src, (size_t) B * NH * Sp * 64 * 2,
-                      [NH, Sp, S_, H](const std::vector<uint8_t> & raw, int arm, std::vector<float> & out) {
-                          const uint16_t * hh = (const uint16_t *) raw.data();
-                          out.resize((size_t) S_ * H);
-                          for (int s = 0; s < S_; ++s)
-                              for (int h = 0; h < NH; ++h)
-                                  for (int d = 0; d < 64; ++d)
-                                      out[(size_t) s * H + h * 64 + d] =
-                                          h2f_host(hh[(((size_t) arm * NH + h) * Sp + s) * 64 + d]);
-                      });
-            }
-        }
+        if (tp && i == 0) tap_qkv(p);
         if ((rc = p.attention(S, T, C, TS))) return rc;
         const int ea = p.record();
         if ((rc = p.post(jl[i], lat, att_l, xn_l, h_l, T, ml, 1, NA, lat_mod_bs))) return rc;
@@ -933,10 +1201,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
             p.cur = 0;
         }
         if (tp && i == 0) {
-            // a0_out is the concatenation [lat | clip | text] of these three (tsn_dit_tap joins them)
-            p.tap("a0_out_l", att_l, (size_t) B * T * H * 2, cvt_f16_arm((size_t) T * H));
-            p.tap("a0_out_c", att_c, (size_t) B * C * H * 2, cvt_f16_arm((size_t) C * H));
-            p.tap("a0_out_t", att_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
+            tap_a0_out(p);
             p.resolve(lat, T);
             p.tap("jb0_lat", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
             if (!pre_only) {
@@ -955,7 +1220,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
             p.tap("jb0_text", text_s, (size_t) B * TS * H * 4, cvt_f32_arm((size_t) TS * H));
         }
     }
-    {   // join the clip and text streams back into the latent stream
+    if (!grouped) {   // join the clip and text streams back into the latent stream
         p.cur = 1;
         const int ecl = p.record();
         p.cur = 2;
