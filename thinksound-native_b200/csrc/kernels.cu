@@ -14,6 +14,7 @@
 //                    the stream restarts (src/dit_fwd.cpp:166-167) in one pass.
 //   cfg_euler_kernel cfg_euler (shaders/ops_conv.metal:194-201) reading dt from the schedule.
 //   prep_* / synth   load-time weight conversion and synthetic weight generation.
+#include <algorithm>
 #include <cstdint>
 
 #include "../../include/tsn_synth.h"
@@ -54,62 +55,82 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
 
 // q, k, v and the output are split operands (hi + lo f16 halves, lo at +qkv_lo / +out_lo*):
 // S = qh·kh + qh·kl + ql·kh and O = P·vh + P·vl, so the only rounding left is P in f16.
-constexpr int ATTN_SMEM = 10 * 64 * 128;   // Q hi/lo + 2 x (K hi/lo) + 2 x (V hi/lo)
+//
+// One CTA per 64 query rows of one head; KG key groups of 4 warps each. Warp (r, g) owns query
+// rows 16r..16r+15 and the key tiles g, g + KG, g + 2 KG, ... (64 keys each), streamed through its
+// group's own double-buffered ring; the KG partial softmax states (row max, row sum, unnormalised
+// O) are merged in group order 0..KG-1, so the result does not depend on timing. Splitting the keys
+// shortens each warp's serial chain of mma.sync by KG (the CTAs of an 8 s forward are too few to
+// fill the SMs, so the chain length is the kernel's duration).
+constexpr int ATTN_Q_BYTES = 2 * 8192;              // Q hi | lo
+constexpr int ATTN_RING_BYTES = 4 * 16384;          // per group: 2 buffers x (K hi/lo + V hi/lo)
+constexpr int attn_smem(int kg) { return ATTN_Q_BYTES + kg * ATTN_RING_BYTES; }
 
-__global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
+template <int KG>
+__global__ void __launch_bounds__(128 * KG, 1) attn_kernel(const AttnArgs a) {
     unsigned long long * tr = a.trace ? a.trace + 3 * ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
     if (tr && threadIdx.x == 0) tr[0] = global_ns();
     pdl_trigger();
     pdl_wait();
     if (tr && threadIdx.x == 0) tr[1] = global_ns();
     extern __shared__ __align__(128) uint8_t sm[];
-    uint8_t * sQ = sm;                       // [hi | lo]
-    uint8_t * sK = sm + 2 * 8192;            // [buf][hi | lo]
-    uint8_t * sV = sm + 6 * 8192;            // [buf][hi | lo]
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rw = warp & 3, g = warp >> 2, gt = tid & 127;   // row warp, key group, thread in group
+    uint8_t * sQ = sm;                                         // [hi | lo]
+    uint8_t * sK = sm + ATTN_Q_BYTES + g * ATTN_RING_BYTES;    // [buf][hi | lo]
+    uint8_t * sV = sK + 2 * 16384;                             // [buf][hi | lo]
     const size_t head = ((size_t) b * a.NH + h) * (size_t) a.S_pad * 64;
     const __half * Qg = a.q + head + (size_t) qt * 64 * 64;
     const __half * Kg = a.k + head;
     const __half * Vg = a.v + head;
     const long long lo = a.qkv_lo;
-    auto load_tile = [&](uint8_t * dst, const __half * src) {
-        for (int i = tid; i < 512; i += 128) {
+    auto load_tile = [&](uint8_t * dst, const __half * src, int t0, int nthr) {
+        for (int i = t0; i < 512; i += nthr) {
             const int r = i >> 3, c = i & 7;
             cp_async16(dst + swz(r, c), src + r * 64 + c * 8);
         }
     };
-    auto load_pair = [&](uint8_t * dst, const __half * src) { load_tile(dst, src); load_tile(dst + 8192, src + lo); };
-    load_pair(sQ, Qg);
-    load_pair(sK, Kg);
-    load_pair(sV, Vg);
-    cp_commit();
-
     const int nkt = (a.S + 63) >> 6;
+    // Q by the whole CTA, each group's first key tile by the group
+    load_tile(sQ, Qg, tid, 128 * KG);
+    load_tile(sQ + 8192, Qg + lo, tid, 128 * KG);
+    if (g < nkt) {
+        const size_t o0 = (size_t) g * 64 * 64;
+        load_tile(sK, Kg + o0, gt, 128); load_tile(sK + 8192, Kg + o0 + lo, gt, 128);
+        load_tile(sV, Vg + o0, gt, 128); load_tile(sV + 8192, Vg + o0 + lo, gt, 128);
+    }
+    cp_commit();
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+
     const int mat = lane >> 3, mrow = lane & 7;
     uint32_t qf[4][4], ql[4][4];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+        const int row = rw * 16 + (mat & 1) * 8 + mrow, ch = 2 * kk + (mat >> 1);
+        ldsm_x4(smem_u32(sQ) + swz(row, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+        ldsm_x4(smem_u32(sQ + 8192) + swz(row, ch), ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3]);
+    }
     float o[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
 
-    for (int j = 0; j < nkt; ++j) {
-        if (j + 1 < nkt) {
-            load_pair(sK + ((j + 1) & 1) * 16384, Kg + (size_t) (j + 1) * 64 * 64);
-            load_pair(sV + ((j + 1) & 1) * 16384, Vg + (size_t) (j + 1) * 64 * 64);
+    for (int it = 0;; ++it) {
+        const int j = g + it * KG;
+        if (j >= nkt) break;
+        const int jn = j + KG;
+        if (jn < nkt) {
+            const size_t on = (size_t) jn * 64 * 64;
+            uint8_t * kd = sK + ((it + 1) & 1) * 16384, * vd = sV + ((it + 1) & 1) * 16384;
+            load_tile(kd, Kg + on, gt, 128); load_tile(kd + 8192, Kg + on + lo, gt, 128);
+            load_tile(vd, Vg + on, gt, 128); load_tile(vd + 8192, Vg + on + lo, gt, 128);
         }
         cp_commit();
         cp_wait1();
-        __syncthreads();
-        if (j == 0) {
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-                const int row = warp * 16 + (mat & 1) * 8 + mrow, ch = 2 * kk + (mat >> 1);
-                ldsm_x4(smem_u32(sQ) + swz(row, ch), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
-                ldsm_x4(smem_u32(sQ + 8192) + swz(row, ch), ql[kk][0], ql[kk][1], ql[kk][2], ql[kk][3]);
-            }
-        }
-        const uint32_t kb = smem_u32(sK + (j & 1) * 16384), vb = smem_u32(sV + (j & 1) * 16384);
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory");   // this group's tile j has landed
+        const uint32_t kb = smem_u32(sK + (it & 1) * 16384), vb = smem_u32(sV + (it & 1) * 16384);
         float s[8][4];
 #pragma unroll
         for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
@@ -183,7 +204,39 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
                 mma16816(o[2 * q + 1], pa, e2, e3);
             }
         }
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + g) : "memory");   // buffer (it & 1) is free again
+    }
+    if (KG > 1) {
+        // merge the key groups' partial states into group 0, in group order; the rings are free
         __syncthreads();
+        float * st = (float *) (sm + ATTN_Q_BYTES);   // [KG - 1][4 warps][32 lanes][36]
+        if (g > 0) {
+            float * d = st + (((g - 1) * 4 + rw) * 32 + lane) * 36;
+#pragma unroll
+            for (int dt = 0; dt < 8; ++dt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) d[dt * 4 + e] = o[dt][e];
+            d[32] = m0; d[33] = m1; d[34] = l0; d[35] = l1;
+        }
+        __syncthreads();
+        if (g > 0) return;
+#pragma unroll
+        for (int q = 1; q < KG; ++q) {
+            const float * d = st + (((q - 1) * 4 + rw) * 32 + lane) * 36;
+            const float mq0 = d[32], mq1 = d[33];
+            const float M0 = fmaxf(m0, mq0), M1 = fmaxf(m1, mq1);
+            const float a0 = exp2f(m0 - M0), a1 = exp2f(m1 - M1), b0 = exp2f(mq0 - M0), b1 = exp2f(mq1 - M1);
+#pragma unroll
+            for (int dt = 0; dt < 8; ++dt) {
+                o[dt][0] = o[dt][0] * a0 + d[dt * 4 + 0] * b0;
+                o[dt][1] = o[dt][1] * a0 + d[dt * 4 + 1] * b0;
+                o[dt][2] = o[dt][2] * a1 + d[dt * 4 + 2] * b1;
+                o[dt][3] = o[dt][3] * a1 + d[dt * 4 + 3] * b1;
+            }
+            l0 = l0 * a0 + d[34] * b0;
+            l1 = l1 * a1 + d[35] * b1;
+            m0 = M0; m1 = M1;
+        }
     }
 #pragma unroll
     for (int off = 1; off <= 2; off <<= 1) {
@@ -193,7 +246,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
     const float i0 = 1.0f / l0, i1 = 1.0f / l1;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-        const int s_row = qt * 64 + warp * 16 + (lane >> 2) + half * 8;
+        const int s_row = qt * 64 + rw * 16 + (lane >> 2) + half * 8;
         if (s_row >= a.S) continue;
         __half * dst;
         long long olo;
@@ -211,17 +264,28 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnArgs a) {
         }
     }
     if (tr) {
-        __syncthreads();
+        asm volatile("bar.sync 1, 128;" ::: "memory");   // group 0's warps (the only ones left)
         if (threadIdx.x == 0) tr[2] = global_ns();
     }
 }
 
+// key groups for a sequence of S keys: up to 3, never more than there are 64-key tiles
+int attn_key_groups(int S) { return std::min(3, std::max(1, (S + 63) / 64)); }
+
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s) {
-    return launch_ex(attn_kernel, dim3((a.S + 63) / 64, a.NH, a.B), dim3(128), ATTN_SMEM, s, 1u, a);
+    const dim3 grid((a.S + 63) / 64, a.NH, a.B);
+    switch (attn_key_groups(a.S)) {
+        case 1: return launch_ex(attn_kernel<1>, grid, dim3(128), attn_smem(1), s, 1u, a);
+        case 2: return launch_ex(attn_kernel<2>, grid, dim3(256), attn_smem(2), s, 1u, a);
+        default: return launch_ex(attn_kernel<3>, grid, dim3(384), attn_smem(3), s, 1u, a);
+    }
 }
 
 cudaError_t configure_attention() {
-    return cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATTN_SMEM);
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem(1));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem(2));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, attn_smem(3));
+    return e;
 }
 
 // =============================================================================== adaLN

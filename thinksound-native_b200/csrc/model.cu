@@ -1092,7 +1092,14 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
                 tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L,
                 (long long) B * T * H, (long long) B * T * L, A};
     ops.push_back(Op{[ca](cudaStream_t s) { return launch_cond(ca, s); }, 2, 0, "cond"});
-    ops.push_back(Op{[jb, nmj, H, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, bfl, s); }, 2, 0, "adaln_gemv"});
+    // the clip/text modulations of every joint block (HBM-bound GEMVs) run on a side stream beside
+    // the latent modulation GEMM and the audio input projection; the joint blocks wait for them
+    const int e_cond = p.record();
+    p.cur = 1;
+    p.wait(e_cond);
+    p.add(Op{[jb, nmj, H, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, bfl, s); }, 2, 0, "adaln_gemv"});
+    const int e_gemv = p.record();
+    p.cur = 0;
     if (tp) {
         const size_t sH = (size_t) H, sTH = (size_t) T * H;
         p.tap("t_emb", te, sH * 4, [sH](const std::vector<uint8_t> & raw, int, std::vector<float> & out) {
@@ -1116,6 +1123,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // each phase of the block is one launch over all three streams' rows (TSN_NO_GROUP=1 selects
     // the three-stream schedule, for comparison).
     const bool grouped = std::getenv("TSN_NO_GROUP") == nullptr;
+    p.wait(e_gemv);
     // taps of the first joint block: its text operand and q/k/v, then its attention outputs
     auto tap_qkv = [&](Plan & p) {
         p.tap("text_xn", xn_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
