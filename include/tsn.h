@@ -184,10 +184,11 @@ int tsn_dit_profile_step(tsn_dit * m, double * out5);
  * algorithmic FLOPs) written into out (NUL-terminated, truncated to cap). */
 int tsn_dit_profile_ops(tsn_dit * m, char * out, size_t cap);
 
-/* Run the forward up to GEMM launch `op` (index in tsn_dit_profile_ops) and that GEMM once more
+/* Run the forward up to stamped launch `op` (index in tsn_dit_profile_ops) and that launch once more
  * with per-CTA phase timestamps (globaltimer ns): entry, setup done, first stage landed,
  * accumulator complete, epilogue done, exit, first cluster barrier passed, cluster reduction
- * done (the last two 0 without split-K) — 8 per CTA into out (max_ctas CTAs). */
+ * done (the last two 0 without split-K) — 8 per CTA into out (max_ctas CTAs). adaLN and
+ * attention launches stamp entry, upstream wait passed and exit in the first 3 of the 8. */
 int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_ctas, int * n_ctas);
 
 /* Run one forward eagerly on the graph's streams with every GEMM, adaLN and attention launch

@@ -486,17 +486,23 @@ int tsn_dit_autotune(tsn_dit * m, char * report, size_t cap) {
 
 int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_ctas, int * n_ctas) {
     M_BEGIN NEED_PREPARED
-    if (op < 0 || op >= (int) M.ops_fwd.size() || M.ops_fwd[op].kind != 0 || !M.ops_fwd[op].traced)
-        return fail(TSN_ERR_ARG, "op is not a GEMM");
+    if (op < 0 || op >= (int) M.ops_fwd.size() || !M.ops_fwd[op].traced)
+        return fail(TSN_ERR_ARG, "op is not a stamped launch");
     const Op & o = M.ops_fwd[op];
-    const size_t n = (size_t) o.ctas * TRACE_SLOTS;
+    const size_t slots = (size_t) o.trace_slots, n = (size_t) o.ctas * slots;
     unsigned long long * d = nullptr;
     CKR(cudaMalloc(&d, n * 8));
     CKR(cudaMemsetAsync(d, 0, n * 8, M.dev->stream));
     for (size_t i = 0; i < M.ops_fwd.size() && (int) i < op; ++i) M.ops_fwd[i].fn(M.dev->stream);   // inputs of op
     cudaError_t e = o.traced(M.dev->stream, d);
     int rc = e == cudaSuccess ? M.dev->sync() : fail(TSN_ERR_CUDA, cudaGetErrorString(e));
-    if (!rc && out) CKR(cudaMemcpy(out, d, std::min(n, max_ctas * TRACE_SLOTS) * 8, cudaMemcpyDeviceToHost));
+    if (!rc && out) {
+        std::vector<unsigned long long> h(n);
+        CKR(cudaMemcpy(h.data(), d, n * 8, cudaMemcpyDeviceToHost));
+        const size_t rows = std::min((size_t) o.ctas, max_ctas);
+        for (size_t r = 0; r < rows; ++r)
+            for (size_t k = 0; k < (size_t) TRACE_SLOTS; ++k) out[r * TRACE_SLOTS + k] = k < slots ? h[r * slots + k] : 0;
+    }
     cudaFree(d);
     if (n_ctas) *n_ctas = o.ctas;
     return rc;

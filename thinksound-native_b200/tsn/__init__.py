@@ -304,7 +304,7 @@ class Dit:
 
 
     def trace_op(self, op: int):
-        """Per-CTA phase timestamps (ns) of GEMM launch `op`: array [ctas, 8]."""
+        """Per-CTA phase timestamps (ns) of stamped launch `op` (GEMM: 8 phases; adaLN, attention: 3): array [ctas, 8]."""
         import numpy as np
         n = C.c_int()
         out = np.zeros((4096, 8), np.uint64)
