@@ -204,6 +204,17 @@ int tsn_dit_timeline(tsn_dit * m, double * out, size_t max_rows, int * n_rows);
  * differently may differ in the last bits. Writes one line per shape into report. */
 int tsn_dit_autotune(tsn_dit * m, char * report, size_t cap);
 
+/* The tile of every GEMM launch of the planned forward, 3 ints each into out (max_gemms entries):
+ * GEMM index, tile width (2000 + NT for the CTA-pair kernel with NT-token tiles) and K slices (the
+ * cluster size, or the partial-tile count of the deepest member of a grouped launch). n_gemms
+ * receives the count. Saving this table after tsn_dit_autotune and passing it to
+ * tsn_dit_set_tiles later reproduces the tuned forward without re-timing. */
+int tsn_dit_get_tiles(tsn_dit * m, int * out, int max_gemms, int * n_gemms);
+
+/* Pin GEMM tiles (n triples as tsn_dit_get_tiles writes them) and re-plan the forward; GEMMs not
+ * listed, and entries that do not fit their GEMM, fall back to the static cost model. */
+int tsn_dit_set_tiles(tsn_dit * m, const int * tiles, int n);
+
 /* ------------------------------------------------------------------ fixtures */
 /* Write the seeded synthetic DiT GGUF (with_prep adds the conditioning-prep tensors). Host only. */
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep);

@@ -87,6 +87,33 @@ def test_graph_replay_deterministic_and_equal_to_eager(dev, tiny_gguf):
     assert np.array_equal(a, c), "graph replay differs from eager launch"
 
 
+def test_tile_table_round_trip(dev, tiny_gguf):
+    """Tiles read after autotuning and pinned on a fresh model reproduce the tuned forward bit for bit;
+    pinning a different valid tile changes the plan but stays within the parity gate."""
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    m.autotune()
+    tiles = m.tiles()
+    assert tiles.shape[1] == 3 and len(tiles) > 0
+    a = np.zeros((2, T, 64), np.float32)
+    m.forward(0.25, a)
+    m2 = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    m2.set_tiles(tiles)
+    assert np.array_equal(m2.tiles(), tiles)
+    b = np.zeros_like(a)
+    m2.forward(0.25, b)
+    assert np.array_equal(a, b), "pinned tiles do not reproduce the tuned forward"
+    # one GEMM on the narrowest tile without split-K: a valid different plan, same result within the gate
+    t3 = tiles.copy()
+    t3[0, 1:] = (64, 1)
+    m2.set_tiles(t3)
+    assert m2.tiles()[0, 1] == 64
+    c = np.zeros_like(a)
+    m2.forward(0.25, c)
+    assert rel_l2(c, a) < 1e-5
+
+
 def test_synthetic_device_weights_equal_file(dev, tiny_gguf):
     T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
     inp = make_inputs(T, C, TS, TINY["H"])

@@ -484,6 +484,26 @@ int tsn_dit_autotune(tsn_dit * m, char * report, size_t cap) {
     return TSN_OK;
 }
 
+int tsn_dit_get_tiles(tsn_dit * m, int * out, int max_gemms, int * n_gemms) {
+    M_BEGIN NEED_PREPARED
+    int n = 0;
+    for (const Op & o : M.ops_fwd) {
+        if (o.kind != 0 || o.gemm_id < 0) continue;
+        if (out && n < max_gemms) { out[3 * n] = o.gemm_id; out[3 * n + 1] = o.tile_bn; out[3 * n + 2] = o.tile_s; }
+        ++n;
+    }
+    if (n_gemms) *n_gemms = n;
+    return TSN_OK;
+}
+
+int tsn_dit_set_tiles(tsn_dit * m, const int * tiles, int n) {
+    M_BEGIN NEED_PREPARED
+    if (n < 0 || (n > 0 && !tiles)) return fail(TSN_ERR_ARG, "null tile table");
+    std::map<int, std::pair<int, int>> t;
+    for (int i = 0; i < n; ++i) t[tiles[3 * i]] = {tiles[3 * i + 1], tiles[3 * i + 2]};
+    return M.set_tiles(t);
+}
+
 int tsn_dit_trace_op(tsn_dit * m, int op, unsigned long long * out, size_t max_ctas, int * n_ctas) {
     M_BEGIN NEED_PREPARED
     if (op < 0 || op >= (int) M.ops_fwd.size() || !M.ops_fwd[op].traced)

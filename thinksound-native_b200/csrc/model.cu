@@ -659,6 +659,8 @@ struct Plan {
                  g.args.k_blocks, g.smem);
         Op op{[g](cudaStream_t s) { return launch_gemm(g, s); }, 0, flops, name, d};
         op.gemm_id = m.gemm_seq++;
+        op.tile_bn = g.bn;
+        op.tile_s = (int) g.grid.z;
         op.shape = last_shape;
         op.traced = [g](cudaStream_t s, unsigned long long * tr) {
             GemmLaunch t = g;
@@ -829,6 +831,8 @@ struct Plan {
                  partial ? "partial" : "cluster", n, end, kbs.c_str(), G.smem);
         Op op{[G](cudaStream_t st) { return launch_gemm_group(G, st); }, 0, flops, name, d};
         op.gemm_id = m.gemm_seq++;
+        op.tile_bn = G.bn;
+        op.tile_s = s;
         op.shape = shape;
         op.traced = [G](cudaStream_t st, unsigned long long * tr) {
             GroupLaunch t = G;
@@ -1421,6 +1425,16 @@ int Model::autotune(std::string & report) {
     rc = capture(ops_fwd, &gx_fwd);
     if (rc) return rc;
     if (gx_step) { cudaGraphExecDestroy(gx_step); gx_step = nullptr; }   // recaptured with the new configs
+    return TSN_OK;
+}
+
+int Model::set_tiles(const std::map<int, std::pair<int, int>> & tiles) {
+    gemm_force = tiles;
+    int rc = build_ops(ops_fwd, 0, 0.0f);
+    if (rc) return rc;
+    rc = capture(ops_fwd, &gx_fwd);
+    if (rc) return rc;
+    if (gx_step) { cudaGraphExecDestroy(gx_step); gx_step = nullptr; }   // recaptured with the new tiles
     return TSN_OK;
 }
 

@@ -56,6 +56,7 @@ struct Op {
     std::string name;
     std::string desc;      // launch configuration, for profiles
     int gemm_id = -1;      // GEMM sequence number within the forward (kind 0)
+    int tile_bn = 0, tile_s = 0;   // the GEMM's tile: width (2000 + NT: CTA pair) and K slices / cluster size
     std::string shape;     // GEMM shape key: ops with equal keys have the same candidate configs
     std::function<cudaError_t(cudaStream_t, unsigned long long *)> traced;   // launch with per-CTA stamps
     int ctas = 0;
@@ -149,6 +150,7 @@ struct Model {
     int n_events = 0;
     int capture(const std::vector<Op> & ops, cudaGraphExec_t * out);
     int autotune(std::string & report);
+    int set_tiles(const std::map<int, std::pair<int, int>> & tiles);   // pin tiles, re-plan, re-capture
     int timeline(std::vector<double> & rows);
     int set_time(float t, float dt);
     void temb_host(float t, float * out) const;

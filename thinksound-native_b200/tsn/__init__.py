@@ -102,6 +102,8 @@ _SIGS = [
     ("tsn_dit_trace_op", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
     ("tsn_dit_timeline", C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]),
     ("tsn_dit_autotune", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    ("tsn_dit_get_tiles", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
+    ("tsn_dit_set_tiles", C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     ("tsn_gguf_write_synthetic", C.c_int, [C.c_char_p, C.POINTER(Geom), C.c_uint64, C.c_int]),
 ]
 
@@ -324,6 +326,21 @@ class Dit:
         buf = C.create_string_buffer(1 << 20)
         check(lib().tsn_dit_autotune(self.h, buf, len(buf)))
         return buf.value.decode()
+
+    def tiles(self):
+        """Tile of every GEMM launch: int32 array [gemms, 3] of (GEMM index, tile width, K slices)."""
+        import numpy as np
+        n = C.c_int()
+        check(lib().tsn_dit_get_tiles(self.h, None, 0, C.byref(n)))
+        out = np.zeros((max(n.value, 1), 3), np.int32)
+        check(lib().tsn_dit_get_tiles(self.h, out.ctypes.data, n.value, C.byref(n)))
+        return out[:n.value]
+
+    def set_tiles(self, tiles) -> None:
+        """Pin GEMM tiles (rows as `tiles()` returns them) and re-plan the forward."""
+        import numpy as np
+        t = np.ascontiguousarray(np.asarray(tiles, np.int32).reshape(-1, 3))
+        check(lib().tsn_dit_set_tiles(self.h, t.ctypes.data, len(t)))
 
     def profile_ops(self) -> str:
         buf = C.create_string_buffer(1 << 20)
