@@ -107,7 +107,7 @@ size_t gemm_smem_bytes(int bn, bool split, int epi) {
     return 0;
 }
 
-constexpr int persist_stages(int bn) { return bn == 256 ? 3 : 4; }
+constexpr int persist_stages(int bn) { return bn == 128 ? 4 : 3; }
 size_t gemm_persistent_smem_bytes(int bn) {
     switch (bn) {
         case 128: return PersistSmem<128, persist_stages(128)>::TOTAL;

@@ -452,7 +452,8 @@ struct PersistSmem {
     static constexpr int B_OFF = 2 * A_BYTES;
     static constexpr int STAGE = 2 * A_BYTES + BN * 128;
     static constexpr int BAR_OFF = STAGES * STAGE;
-    static constexpr int TOTAL = BAR_OFF + 256 + 1024;   // barriers, TMEM slot, abort flag + alignment slack
+    static constexpr int XPOSE_OFF = BAR_OFF + 256;      // per epilogue warp: 32 rows x 33 floats (padded)
+    static constexpr int TOTAL = XPOSE_OFF + 4 * 32 * 33 * 4 + 1024;   // + alignment slack
 };
 
 template <int BN, int STAGES>
@@ -566,24 +567,33 @@ gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc_fence_after();
             int t0, b0, n0;
             tile_coords(tile, t0, b0, n0);
-            const int b = b0 + r / a.bt, t = t0 + r % a.bt;
-            const bool valid = t < a.rows && b < a.B;
-            float * orow = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo;
+            // The output rows are far apart (the modulation GEMM's rows are 512 KB long): each
+            // 32 x 32 chunk goes through this warp's padded smem block so that every store
+            // instruction writes four whole 128-byte row segments.
+            float * tb = (float *) (smem + L::XPOSE_OFF) + warp * (32 * 33);
 #pragma unroll 1
             for (int c = 0; c < BN; c += 32) {
                 float v[32];
                 tmem_ld32(trow + (uint32_t) (buf * ACC + c), v);
                 const int n = n0 + c;
-                if (!valid || n >= a.N) continue;
-                if (a.bias) {
+                if (n >= a.N) continue;                      // the same for the whole warp
 #pragma unroll
-                    for (int e = 0; e < 32; e += 4) {
-                        const float4 bb = __ldg((const float4 *) (a.bias + n + e));
-                        v[e] += bb.x; v[e + 1] += bb.y; v[e + 2] += bb.z; v[e + 3] += bb.w;
-                    }
+                for (int j = 0; j < 32; ++j) tb[lane * 33 + j] = v[j];
+                __syncwarp();
+                // store i: rows 4i .. 4i+3 of the block, 8 lanes per row, one float4 each
+                const int cq = (lane & 7) * 4, col = n + cq;
+                const bool col_ok = col < a.N;
+                float4 bl = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (a.bias && col_ok) bl = __ldg((const float4 *) (a.bias + col));
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int rr = 4 * i + (lane >> 3), row = warp * 32 + rr, b = b0 + row / a.bt, t = t0 + row % a.bt;
+                    const float * src = tb + rr * 33 + cq;
+                    if (col_ok && t < a.rows && b < a.B)
+                        *(float4 *) ((float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + col) =
+                            make_float4(src[0] + bl.x, src[1] + bl.y, src[2] + bl.z, src[3] + bl.w);
                 }
-#pragma unroll
-                for (int q = 0; q < 32; q += 4) *(float4 *) (orow + n + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+                __syncwarp();
             }
             // this warp is done reading accumulator `buf`
             tc_fence_before();
