@@ -5,16 +5,20 @@
 // [NH, S, S] f32 probability tensor of the reference never exists.
 //
 // One CTA per (128 query rows, head, arm), 192 threads, two CTAs per SM:
-//   warp 4      TMA: the Q tile (hi and lo halves) once, then K and V 64-key tiles into a
-//               2-stage ring
+//   warp 4      TMA: the Q tile (hi and lo halves) once, then K (lane 0) and V (lane 1) 64-key
+//               tiles into 2-stage rings; a K stage is free once its S product is done, a V stage
+//               once its PV product is
 //   warp 5      one thread issues the UMMAs: S_j = Qh·Kh^T + Qh·Kl^T + Ql·Kh^T (M 128, N 64,
-//               K 64) into TMEM columns [0, 64), one key tile ahead of the softmax, and
-//               O_j = P_j·Vh + P_j·Vl (M 128, N 64, K 64; V read MN-major) into columns [64, 128)
+//               K 64) into TMEM, one key tile ahead of the softmax, and O_j = P_j·Vh + P_j·Vl
+//               (M 128, N 64, K 64; P read from TMEM, V MN-major from shared memory)
 //   warps 0-3   one query row per thread: base-2 online softmax in f32 on the row of S_j read
-//               from TMEM, P_j rounded to f16 into a swizzled shared-memory tile (the A operand
-//               of the PV product), running O and row sum in registers, O / l written as the
-//               split f16 attention output of the row's stream.
-// The arithmetic matches attn_kernel (same split products, P in f16, sums of the f32 p).
+//               from TMEM, P_j rounded to f16 and stored back into TMEM (the A operand of the PV
+//               product), running O and row sum in registers, O / l written as the split f16
+//               attention output of the row's stream.
+// P and O_j are double-buffered in TMEM, so the softmax of tile j waits only for the PV product
+// of tile j - 2: it overlaps the PV product of tile j - 1 instead of following it. O_j is folded
+// into the register O two tiles later with the scale factors of both tiles. The arithmetic matches
+// attn_kernel (same split products, P in f16, sums of the f32 p).
 // Every mbarrier wait is bounded (ptx.cuh): a stalled pipeline ends the kernel with an error code.
 #include "kernels.h"
 
@@ -34,9 +38,47 @@ constexpr int KV_BYTES = 64 * 128;              // one half of a 64 x 64 f16 K o
 constexpr int OFF_Q = 0;                        // Q hi | Q lo
 constexpr int OFF_K = 2 * Q_BYTES;              // [stage][hi | lo]
 constexpr int OFF_V = OFF_K + 4 * KV_BYTES;     // [stage][hi | lo]
-constexpr int OFF_P = OFF_V + 4 * KV_BYTES;     // 128 x 64 f16 probabilities
-constexpr int OFF_BAR = OFF_P + Q_BYTES;
+constexpr int OFF_BAR = OFF_V + 4 * KV_BYTES;
 constexpr int SMEM_TOTAL = OFF_BAR + 256;       // the dynamic window starts 1024-aligned (checked)
+
+// TMEM columns (256 allocated): S_j, O in two buffers, P (two f16 per column) in two buffers
+constexpr uint32_t TM_S = 0, TM_O = 64, TM_P = 192;
+
+// the split f16 attention output of joint row s_row (o unnormalised, l its row sum), into the
+// output of the row's stream
+__device__ __forceinline__ void store_row(const AttnArgs & a, int b, int h, int s_row, const float * o, float l) {
+    if (s_row >= a.S) return;
+    __half * dst;
+    long long olo;
+    if (s_row < a.n0) { dst = a.out0 + ((size_t) b * a.n0 + s_row) * a.H; olo = a.out_lo0; }
+    else if (s_row < a.n0 + a.n1) { dst = a.out1 + ((size_t) b * a.n1 + (s_row - a.n0)) * a.H; olo = a.out_lo1; }
+    else { dst = a.out2 + ((size_t) b * a.n2 + (s_row - a.n0 - a.n1)) * a.H; olo = a.out_lo2; }
+    dst += h * 64;
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int c = 0; c < 64; c += 8) {
+        __align__(16) __half hv[8], lv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float v = o[c + e] * inv;
+            hv[e] = __float2half_rn(v);
+            lv[e] = __float2half_rn(v - __half2float(hv[e]));
+        }
+        *(uint4 *) (dst + c) = *(const uint4 *) hv;
+        if (olo) *(uint4 *) (dst + olo + c) = *(const uint4 *) lv;
+    }
+}
+
+// o = o * alpha + (this row's 64 columns of the O buffer at TMEM address t)
+__device__ __forceinline__ void fold_o(float * o, float alpha, uint32_t t) {
+#pragma unroll
+    for (int c = 0; c < 64; c += 32) {
+        float ot[32];
+        tmem_ld32(t + c, ot);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) o[c + e] = o[c + e] * alpha + ot[e];
+    }
+}
 
 __global__ void __launch_bounds__(192, 2)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -51,13 +93,15 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     }
     uint64_t * bar = (uint64_t *) (smem + OFF_BAR);
     uint64_t * q_full = bar;          // Q landed
-    uint64_t * kv_full = bar + 1;     // [2] K and V tile landed
-    uint64_t * kv_empty = bar + 3;    // [2] K and V tile consumed (after PV)
-    uint64_t * s_full = bar + 5;      // S_j in TMEM
-    uint64_t * s_free = bar + 6;      // S_j read by the softmax warps (4 arrivals)
-    uint64_t * p_full = bar + 7;      // P_j in shared memory (4 arrivals)
-    uint64_t * pv_done = bar + 8;     // O_j in TMEM, P buffer free
-    uint32_t * tslot = (uint32_t *) (bar + 9);
+    uint64_t * k_full = bar + 1;      // [2] K tile landed
+    uint64_t * k_empty = bar + 3;     // [2] K tile consumed (after S)
+    uint64_t * v_full = bar + 5;      // [2] V tile landed
+    uint64_t * v_empty = bar + 7;     // [2] V tile consumed (after PV)
+    uint64_t * s_full = bar + 9;      // S_j in TMEM
+    uint64_t * s_free = bar + 10;     // S_j read by the softmax warps (4 arrivals)
+    uint64_t * p_full = bar + 11;     // [2] P_j in TMEM buffer j & 1 (4 arrivals)
+    uint64_t * pv_done = bar + 13;    // [2] O_j in TMEM buffer j & 1
+    uint32_t * tslot = (uint32_t *) (bar + 15);
     volatile int * abort_flag = (volatile int *) (tslot + 1);
 
     const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -66,48 +110,53 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < 2; ++s) { mbar_init(&kv_full[s], 1); mbar_init(&kv_empty[s], 1); }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&k_full[s], 1); mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1); mbar_init(&v_empty[s], 1);
+            mbar_init(&p_full[s], 4); mbar_init(&pv_done[s], 1);
+        }
         mbar_init(s_full, 1);
         mbar_init(s_free, 4);
-        mbar_init(p_full, 4);
-        mbar_init(pv_done, 1);
         *abort_flag = 0;
         fence_mbar_init();
     }
     if (threadIdx.x == 0) pdl_trigger();
     if (warp == 4 && lane == 0) { tma_prefetch(&tq); tma_prefetch(&tk); tma_prefetch(&tv); }
-    if (warp == 5) tmem_alloc(tslot, 128);
+    if (warp == 5) tmem_alloc(tslot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tslot;          // S at columns [0, 64), O_j at [64, 128)
+    const uint32_t tmem = *tslot;
 
     if (warp == 4) {
-        if (lane == 0) {
+        if (lane < 2) {
             pdl_wait();
-            mbar_expect_tx(q_full, 2 * Q_BYTES);
-            tma_load_3d(smem + OFF_Q, &tq, q_full, 0, head_row + qt * 128, 0);
-            tma_load_3d(smem + OFF_Q + Q_BYTES, &tq, q_full, 0, head_row + qt * 128, 1);
+            if (lane == 0) {
+                mbar_expect_tx(q_full, 2 * Q_BYTES);
+                tma_load_3d(smem + OFF_Q, &tq, q_full, 0, head_row + qt * 128, 0);
+                tma_load_3d(smem + OFF_Q + Q_BYTES, &tq, q_full, 0, head_row + qt * 128, 1);
+            }
+            // lane 0 streams K, lane 1 streams V
+            const CUtensorMap * tm = lane == 0 ? &tk : &tv;
+            uint64_t * full = lane == 0 ? k_full : v_full, * empty = lane == 0 ? k_empty : v_empty;
+            uint8_t * ring = smem + (lane == 0 ? OFF_K : OFF_V);
             for (int j = 0; j < nkt; ++j) {
                 const int s = j & 1;
-                if (j >= 2 && !mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, abort_flag, err, DEV_TIMEOUT_EMPTY)) break;
-                uint8_t * k = smem + OFF_K + s * 2 * KV_BYTES, * v = smem + OFF_V + s * 2 * KV_BYTES;
-                mbar_expect_tx(&kv_full[s], 4 * KV_BYTES);
-                tma_load_3d(k, &tk, &kv_full[s], 0, head_row + j * 64, 0);
-                tma_load_3d(k + KV_BYTES, &tk, &kv_full[s], 0, head_row + j * 64, 1);
-                tma_load_3d(v, &tv, &kv_full[s], 0, head_row + j * 64, 0);
-                tma_load_3d(v + KV_BYTES, &tv, &kv_full[s], 0, head_row + j * 64, 1);
+                if (j >= 2 && !mbar_wait(&empty[s], ((j >> 1) - 1) & 1, abort_flag, err, DEV_TIMEOUT_EMPTY)) break;
+                uint8_t * t = ring + s * 2 * KV_BYTES;
+                mbar_expect_tx(&full[s], 2 * KV_BYTES);
+                tma_load_3d(t, tm, &full[s], 0, head_row + j * 64, 0);
+                tma_load_3d(t + KV_BYTES, tm, &full[s], 0, head_row + j * 64, 1);
             }
         }
     } else if (warp == 5) {
         if (lane == 0) {
             const uint32_t id_s = umma_idesc_f16(64, 0), id_pv = umma_idesc_f16(64, 0, 1);
             const uint64_t qh = umma_desc_sw128(smem + OFF_Q), ql = umma_desc_sw128(smem + OFF_Q + Q_BYTES);
-            const uint64_t pd = umma_desc_sw128(smem + OFF_P);
             bool ok = mbar_wait(q_full, 0, abort_flag, err, DEV_TIMEOUT_FULL);
             auto issue_s = [&](int j) {   // S_j = Qh Kh^T + Qh Kl^T + Ql Kh^T
                 const int s = j & 1;
-                if (!mbar_wait(&kv_full[s], (j >> 1) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) return false;
+                if (!mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) return false;
                 if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) return false;
                 if (tr && j == 0) tr[1] = global_ns();
                 tc_fence_after();
@@ -116,28 +165,32 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t o = (uint64_t) (2 * kk);
-                    umma_f16(tmem, qh + o, kh + o, id_s, kk != 0);
-                    umma_f16(tmem, qh + o, kl + o, id_s, 1u);
-                    umma_f16(tmem, ql + o, kh + o, id_s, 1u);
+                    umma_f16(tmem + TM_S, qh + o, kh + o, id_s, kk != 0);
+                    umma_f16(tmem + TM_S, qh + o, kl + o, id_s, 1u);
+                    umma_f16(tmem + TM_S, ql + o, kh + o, id_s, 1u);
                 }
                 umma_commit(s_full);
+                umma_commit(&k_empty[s]);
                 return true;
             };
             if (ok) ok = issue_s(0);
             for (int j = 0; j < nkt && ok; ++j) {
                 if (j + 1 < nkt && !issue_s(j + 1)) break;
-                // O_j = P_j (Vh + Vl)
-                if (!mbar_wait(p_full, j & 1, abort_flag, err, DEV_TIMEOUT_FULL)) break;
+                // O_j = P_j (Vh + Vl) into O buffer j & 1, P_j from TMEM buffer j & 1
+                const int pb = j & 1;
+                if (!mbar_wait(&p_full[pb], (j >> 1) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) break;
+                if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) break;
                 tc_fence_after();
                 const uint8_t * v = smem + OFF_V + (j & 1) * 2 * KV_BYTES;
+                const uint32_t d = tmem + TM_O + 64 * pb, p = tmem + TM_P + 32 * pb;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t vh = umma_desc_sw128_mn(v + kk * 2048), vl = umma_desc_sw128_mn(v + KV_BYTES + kk * 2048);
-                    umma_f16(tmem + 64, pd + (uint64_t) (2 * kk), vh, id_pv, kk != 0);
-                    umma_f16(tmem + 64, pd + (uint64_t) (2 * kk), vl, id_pv, 1u);
+                    umma_f16_ts(d, p + 8 * kk, vh, id_pv, kk != 0);
+                    umma_f16_ts(d, p + 8 * kk, vl, id_pv, 1u);
                 }
-                umma_commit(pv_done);
-                umma_commit(&kv_empty[j & 1]);
+                umma_commit(&pv_done[pb]);
+                umma_commit(&v_empty[j & 1]);
             }
         }
     } else {
@@ -145,18 +198,19 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
         pdl_wait();
         const int r = warp * 32 + lane;                          // query row within the tile
         const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
-        uint8_t * prow = smem + OFF_P + r * 128;                 // this row of the swizzled P tile
         float o[64];
 #pragma unroll
         for (int i = 0; i < 64; ++i) o[i] = 0.0f;
-        float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
+        // m: running row max; a1, a2: the scale factors of tiles j - 1 and j - 2
+        // (alpha_i = 2^(m_{i-1} - m_i)); O_{j-2} is folded at tile j with a2
+        float m = -INFINITY, l = 0.0f, a1 = 1.0f, a2 = 1.0f;
         bool ok = true;
         for (int j = 0; j < nkt; ++j) {
             if (!mbar_wait(s_full, j & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) { ok = false; break; }
             tc_fence_after();
             float p[64];
-            tmem_ld32(trow, p);
-            tmem_ld32(trow + 32, p + 32);
+            tmem_ld32(trow + TM_S, p);
+            tmem_ld32(trow + TM_S + 32, p + 32);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(s_free);                  // the MMA may overwrite S now
@@ -167,86 +221,58 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
                 for (int e = 0; e < 64; ++e)
                     if (j * 64 + e >= a.S) p[e] = -INFINITY;
             }
-            float mx = p[0];
+            // max and sum as four interleaved chains (one warp per SM sub-partition: the
+            // softmax is latency-bound, not issue-bound)
+            float mq[4] = {p[0], p[1], p[2], p[3]};
 #pragma unroll
-            for (int e = 1; e < 64; ++e) mx = fmaxf(mx, p[e]);
+            for (int e = 4; e < 64; ++e) mq[e & 3] = fmaxf(mq[e & 3], p[e]);
+            const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
             const float mn = fmaxf(m, mx * a.scale_log2);
             const float alpha = ex2(m - mn);
             m = mn;
-            float ps = 0.0f;
+            float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
             for (int e = 0; e < 64; ++e) {
                 p[e] = ex2(fmaf(p[e], a.scale_log2, -mn));
-                ps += p[e];
+                sq[e & 3] += p[e];
             }
-            l = l * alpha + ps;
-            // PV_{j-1} done: the P buffer is free and O_{j-1} is in TMEM
-            if (j >= 1) {
-                if (!mbar_wait(pv_done, (j - 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) { ok = false; break; }
+            l = l * alpha + ((sq[0] + sq[1]) + (sq[2] + sq[3]));
+            // buffer j & 1 is free once the PV product of tile j - 2 is done: fold O_{j-2}
+            const int pb = j & 1;
+            if (j >= 2) {
+                if (!mbar_wait(&pv_done[pb], ((j - 2) >> 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) { ok = false; break; }
                 tc_fence_after();
+                fold_o(o, a2, trow + TM_O + 64 * pb);
             }
-            // P_j as f16 into the swizzled tile: 16-byte chunk c of row r at chunk c ^ (r & 7)
+            // P_j as f16 pairs into TMEM buffer pb (column c holds elements 2c, 2c + 1)
+            uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                __align__(16) __half hv[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) hv[e] = __float2half_rn(p[8 * c + e]);
-                *(uint4 *) (prow + ((c ^ (r & 7)) << 4)) = *(const uint4 *) hv;
+            for (int c = 0; c < 32; ++c) {
+                const __half2 hv = __floats2half2_rn(p[2 * c], p[2 * c + 1]);
+                pk[c] = *(const uint32_t *) &hv;
             }
-            // fold O_{j-1} = O_{j-2} * alpha_{j-1} + P_{j-1} V_{j-1} before PV_j may overwrite it
-            if (j >= 1) {
-#pragma unroll
-                for (int c = 0; c < 64; c += 32) {
-                    float ot[32];
-                    tmem_ld32(trow + 64 + c, ot);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o[c + e] = o[c + e] * alpha_prev + ot[e];
-                }
-            }
-            alpha_prev = alpha;
-            fence_proxy_async_smem();
+            tmem_st32(trow + TM_P + 32 * pb, pk);
+            tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[pb]);
+            a2 = a1;
+            a1 = alpha;
         }
-        if (ok && mbar_wait(pv_done, (nkt - 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) {
+        // fold the last two tiles' O (tile nkt - 2 with its scale, then tile nkt - 1)
+        for (int j = nkt >= 2 ? nkt - 2 : 0; ok && j < nkt; ++j) {
+            const int pb = j & 1;
+            if (!mbar_wait(&pv_done[pb], (j >> 1) & 1, abort_flag, err, DEV_TIMEOUT_TMEM)) { ok = false; break; }
             tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 64; c += 32) {
-                float ot[32];
-                tmem_ld32(trow + 64 + c, ot);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) o[c + e] = o[c + e] * alpha_prev + ot[e];
-            }
-            const int s_row = qt * 128 + r;
-            if (s_row < a.S) {
-                __half * dst;
-                long long olo;
-                if (s_row < a.n0) { dst = a.out0 + ((size_t) b * a.n0 + s_row) * a.H; olo = a.out_lo0; }
-                else if (s_row < a.n0 + a.n1) { dst = a.out1 + ((size_t) b * a.n1 + (s_row - a.n0)) * a.H; olo = a.out_lo1; }
-                else { dst = a.out2 + ((size_t) b * a.n2 + (s_row - a.n0 - a.n1)) * a.H; olo = a.out_lo2; }
-                dst += h * 64;
-                const float inv = 1.0f / l;
-#pragma unroll
-                for (int c = 0; c < 64; c += 8) {
-                    __align__(16) __half hv[8], lv[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float v = o[c + e] * inv;
-                        hv[e] = __float2half_rn(v);
-                        lv[e] = __float2half_rn(v - __half2float(hv[e]));
-                    }
-                    *(uint4 *) (dst + c) = *(const uint4 *) hv;
-                    if (olo) *(uint4 *) (dst + olo + c) = *(const uint4 *) lv;
-                }
-            }
+            fold_o(o, j == nkt - 1 ? a1 : a2, trow + TM_O + 64 * pb);
         }
+        if (ok) store_row(a, b, h, qt * 128 + r, o, l);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 5) {
         tc_fence_after();
-        tmem_dealloc(tmem, 128);
+        tmem_dealloc(tmem, 256);
     }
     if (tr && threadIdx.x == 0) tr[2] = global_ns();
     if (*abort_flag && threadIdx.x == 0) {

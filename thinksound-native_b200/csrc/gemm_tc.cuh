@@ -558,7 +558,6 @@ gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constan
         }
     } else {
         pdl_wait();
-        const int r = warp * 32 + lane;
         const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
         int i = 0;
         for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
