@@ -135,20 +135,31 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
         tc_fence_after();
         if (tr && threadIdx.x == 0) tr[3] = global_ns();
         const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
-        const int n = n0 + warp * 32 + lane;              // this thread's weight row
         if constexpr (EPI == EPI_F32) {
-            const float bias = (a.bias && n < a.N) ? a.bias[n] : 0.0f;
-            float * ob = (float *) a.out + blockIdx.z * a.part_stride + (long long) b * a.out_bs + n;
+            // this warp's 32 features x 32 tokens per chunk go through a padded smem block (the
+            // operand ring is free: every MMA of the pair has completed), so that each store
+            // instruction writes four tokens' 128-byte runs of 32 consecutive features
+            float * tb = (float *) smem + warp * (32 * 33);
+            const int f0 = n0 + warp * 32, cq = (lane & 7) * 4;   // the warp's first feature; lane's 4
+            float4 bl = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (a.bias && f0 + cq < a.N) bl = *(const float4 *) (a.bias + f0 + cq);
+            float * ob = (float *) a.out + blockIdx.z * a.part_stride + (long long) b * a.out_bs + f0 + cq;
 #pragma unroll 1
             for (int c = 0; c < NT; c += 32) {
                 float v[32];
                 tmem_ld32(trow + c, v);
-                if (!ok || n >= a.N) continue;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = t0 + c + j;
-                    if (t < a.rows) ob[(long long) t * a.ldo] = v[j] + bias;
+                for (int j = 0; j < 32; ++j) tb[lane * 33 + j] = v[j];   // [feature][token]
+                __syncwarp();
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int tk = 4 * i + (lane >> 3), t = t0 + c + tk;   // token of this store
+                    if (ok && f0 + cq < a.N && t < a.rows)
+                        *(float4 *) (ob + (long long) t * a.ldo) =
+                            make_float4(tb[cq * 33 + tk] + bl.x, tb[(cq + 1) * 33 + tk] + bl.y,
+                                        tb[(cq + 2) * 33 + tk] + bl.z, tb[(cq + 3) * 33 + tk] + bl.w);
                 }
+                __syncwarp();
             }
         } else {
             // SwiGLU: rows come in groups of 64 = [32 w1 | 32 w3], so warps (0,1) and (2,3) hold
