@@ -218,6 +218,11 @@ int tsn_dit_set_tiles(tsn_dit * m, const int * tiles, int n);
 /* ------------------------------------------------------------------ fixtures */
 /* Write the seeded synthetic DiT GGUF (with_prep adds the conditioning-prep tensors). Host only. */
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep);
+/* Write the seeded synthetic VAE decoder GGUF (f32 tensors: conv k7 latent_dim -> 16 channels,
+ * five upsampling blocks at strides 8, 8, 4, 4, 2 with widths 8, 4, 2, 1, 1 x channels, final conv
+ * to out_channels; tensor names of src/vae.cpp). Host only. */
+int tsn_gguf_write_synthetic_vae(const char * path, uint32_t latent_dim, uint32_t channels, uint32_t out_channels,
+                                 uint64_t seed);
 
 #ifdef __cplusplus
 }

@@ -138,3 +138,68 @@ def parse_json_line(s: str) -> dict:
         if line.startswith("{"):
             return json.loads(line)
     raise ValueError("no JSON line in output")
+
+
+# ---------------------------------------------------------------- VAE decoder (src/vae.cpp)
+VAE_STRIDES = (8, 8, 4, 4, 2)
+VAE_DILS = (1, 3, 9)
+
+
+def ref_vae(gguf: str, latent: np.ndarray, threads=None, reps=1, workdir=None):
+    """VaeModel::decode of the reference build (src/vae.cpp:17-86) on latent [T, 64].
+    Returns (audio [T_audio, 2] f32, timing JSON)."""
+    import tempfile
+    d = workdir or tempfile.mkdtemp(prefix="tsn_vae_")
+    write_inputs(d, {"latent": latent})
+    out = run_ref("vae", gguf, latent.shape[0], 0, 0, d, d, reps, threads=threads)
+    js = parse_json_line(out)
+    audio = np.fromfile(os.path.join(d, "audio.bin"), np.float32).reshape(-1, 2)
+    return audio, js
+
+
+def _conv1d_np(x, w, b, stride=1, pad=0, dil=1, convt=False, OL=None):
+    """conv1d as the reference's im2col + GEMM (shaders/ops_conv.metal:262-283): x [T, IC],
+    w [OC, IC, K]; with convt the input is zero-stuffed by `stride` and convolved at stride 1."""
+    T, IC = x.shape
+    OC, _, K = w.shape
+    OL = T if OL is None else OL
+    t = np.arange(OL)[:, None]
+    k = np.arange(K)[None, :]
+    if convt:
+        ui = t - pad + k
+        ok = (ui >= 0) & (ui % stride == 0)
+        ti = ui // stride
+    else:
+        ti = t * stride - pad + k * dil
+        ok = np.ones_like(ti, dtype=bool)
+    ok = ok & (ti >= 0) & (ti < T)
+    col = np.where(ok[:, :, None], x[np.clip(ti, 0, T - 1)], 0.0)   # [OL, K, IC]
+    y = np.einsum("tki,oik->to", col, w, optimize=True)
+    return y + b if b is not None else y
+
+
+def _snake_np(x, alpha, beta):
+    """snake_ (shaders/ops_conv.metal:204-213): x + sin(x e^alpha)^2 e^-beta, per channel."""
+    s = np.sin(x * np.exp(alpha))
+    return x + s * s * np.exp(-beta)
+
+
+def vae_decode_np(W, latent):
+    """Float64 restatement of VaeModel::decode (src/vae.cpp:17-86) for small cases.
+    W(name) returns a tensor as numpy: conv weights [OC, IC, K], vectors [n]."""
+    x = _conv1d_np(latent.astype(np.float64), W("decoder.layers.0.weight"), W("decoder.layers.0.bias"), pad=3)
+    for n, st in enumerate(VAE_STRIDES):
+        bp = f"decoder.layers.{n + 1}"
+        h = _snake_np(x, W(bp + ".layers.0.alpha"), W(bp + ".layers.0.beta"))
+        w = W(bp + ".layers.1.weight")
+        K = w.shape[2]
+        x = _conv1d_np(h, w, W(bp + ".layers.1.bias"), stride=st, pad=K - 1 - st // 2, convt=True, OL=h.shape[0] * st)
+        for r, dl in enumerate(VAE_DILS):
+            rp = f"{bp}.layers.{r + 2}"
+            h = _snake_np(x, W(rp + ".layers.0.alpha"), W(rp + ".layers.0.beta"))
+            g = _conv1d_np(h, W(rp + ".layers.1.weight"), W(rp + ".layers.1.bias"), pad=3 * dl, dil=dl)
+            h = _snake_np(g, W(rp + ".layers.2.alpha"), W(rp + ".layers.2.beta"))
+            x = x + _conv1d_np(h, W(rp + ".layers.3.weight"), W(rp + ".layers.3.bias"))
+    h = _snake_np(x, W("decoder.layers.6.alpha"), W("decoder.layers.6.beta"))
+    return _conv1d_np(h, W("decoder.layers.7.weight"), None, pad=3)
+

@@ -14,6 +14,9 @@
 //       [sync_S,768], then DitModel::prep_text_arm (src/dit.cpp:137-192) on text_cat_<arm>.bin
 //       [TS,2048] and gtext_<arm>.bin [1024] for arm = cond, unc; writes clip_pp.bin,
 //       sync_gather.bin, text_pp_<arm>.bin, gcmlp_<arm>.bin.
+//   ts_ref_dit vae <vae_gguf> <T> 0 0 <in_dir> <out_dir> [reps]
+//       VaeModel::decode (src/vae.cpp:17-86) of latent.bin [T,64]; writes audio.bin
+//       [T_audio,2] (interleaved stereo) and prints a JSON timing line.
 //
 // Inputs in <in_dir> (f32, row-major): x.bin [T,64], clip_pp.bin [C,H], sync_gather.bin [T,H],
 // text_pp_cond.bin / text_pp_unc.bin [TS,H], gcmlp_cond.bin / gcmlp_unc.bin [H].
@@ -90,6 +93,33 @@ int main(int argc, char ** argv) {
 
     Runtime rt;
     if (!rt.init("")) return 1;
+    if (mode == "vae") {
+        VaeModel vae;
+        if (!vae.load(rt, gguf)) { fprintf(stderr, "vae load failed\n"); return 1; }
+        std::vector<float> lat((size_t) T * 64);
+        {
+            FILE * f = fopen((in + "/latent.bin").c_str(), "rb");
+            if (!f || fread(lat.data(), 4, lat.size(), f) != lat.size()) { fprintf(stderr, "missing latent.bin\n"); return 1; }
+            fclose(f);
+        }
+        const int reps = argc > 8 ? atoi(argv[8]) : 1;
+        int threads = 1;
+#ifdef _OPENMP
+        threads = omp_get_max_threads();
+#endif
+        std::vector<float> audio;
+        uint32_t Ta = 0;
+        printf("{\"mode\": \"vae\", \"threads\": %d, \"seconds\": [", threads);
+        for (int r = 0; r < reps; ++r) {
+            const auto t0 = std::chrono::steady_clock::now();
+            audio = vae.decode(rt, lat.data(), T, Ta);
+            const double sec = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+            printf("%s%.6f", r ? ", " : "", sec);
+        }
+        printf("], \"T_audio\": %u}\n", Ta);
+        write_from(out + "/audio.bin", audio.data(), audio.size());
+        return 0;
+    }
     DitModel dit;
     if (!dit.load(rt, gguf)) { fprintf(stderr, "dit load failed\n"); return 1; }
     if (mode == "prep") {

@@ -548,4 +548,14 @@ int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t
     return TSN_OK;
 }
 
+int tsn_gguf_write_synthetic_vae(const char * path, uint32_t latent_dim, uint32_t channels, uint32_t out_channels,
+                                 uint64_t seed) {
+    if (!path || latent_dim == 0 || channels == 0 || out_channels == 0) return fail(TSN_ERR_ARG, "bad VAE geometry");
+    VaeGeom v;
+    v.latent_dim = latent_dim; v.channels = channels; v.out_channels = out_channels;
+    std::string err;
+    if (!write_synthetic_vae_gguf(path, v, seed, err)) return fail(TSN_ERR_IO, err);
+    return TSN_OK;
+}
+
 } // extern "C"

@@ -1,6 +1,8 @@
 // dit_schema.cpp — tensor inventory of the MMDiT (see dit_schema.h for the reference citations).
 #include "dit_schema.h"
 
+#include <cmath>
+
 #include "../../include/tsn_synth.h"
 
 namespace tsn {
@@ -97,6 +99,44 @@ std::vector<TensorSpec> dit_schema(const DitGeom & g, bool with_prep) {
         b.f32mat("empty_t5_feat", 2048, 77, 1.0f);
     }
     return b.v;
+}
+
+std::vector<TensorSpec> vae_schema(const VaeGeom & v) {
+    std::vector<TensorSpec> out;
+    auto conv = [&](const std::string & n, uint64_t K, uint64_t IC, uint64_t OC, float scale) {
+        TensorSpec t; t.name = n; t.n_dims = 3; t.ne[0] = K; t.ne[1] = IC; t.ne[2] = OC; t.type = GG_F32; t.scale = scale;
+        out.push_back(t);
+    };
+    auto vec = [&](const std::string & n, uint64_t len, float scale) {
+        TensorSpec t; t.name = n; t.n_dims = 1; t.ne[0] = len; t.type = GG_F32; t.scale = scale;
+        out.push_back(t);
+    };
+    auto snake = [&](const std::string & p, uint64_t C) { vec(p + ".alpha", C, 0.1f); vec(p + ".beta", C, 0.1f); };
+    auto fan = [](uint64_t n) { return 1.0f / std::sqrt((float) n); };
+    const uint64_t L = v.latent_dim;
+    uint64_t c = vae_width(v, 0);
+    conv("decoder.layers.0.weight", 7, L, c, fan(7 * L));                   // src/vae.cpp:59
+    vec("decoder.layers.0.bias", c, 0.02f);
+    for (int n = 0; n < 5; ++n) {                                            // src/vae.cpp:61-78
+        const std::string bp = "decoder.layers." + std::to_string(n + 1);
+        const uint64_t s = VAE_STRIDES[n], o = vae_width(v, n + 1);
+        snake(bp + ".layers.0", c);
+        conv(bp + ".layers.1.weight", 2 * s, c, o, fan(2 * c));             // 2 taps meet each output
+        vec(bp + ".layers.1.bias", o, 0.02f);
+        for (int r = 0; r < 3; ++r) {
+            const std::string rp = bp + ".layers." + std::to_string(r + 2);
+            snake(rp + ".layers.0", o);
+            conv(rp + ".layers.1.weight", 7, o, o, 0.5f * fan(7 * o));
+            vec(rp + ".layers.1.bias", o, 0.02f);
+            snake(rp + ".layers.2", o);
+            conv(rp + ".layers.3.weight", 1, o, o, 0.5f * fan(o));
+            vec(rp + ".layers.3.bias", o, 0.02f);
+        }
+        c = o;
+    }
+    snake("decoder.layers.6", c);                                            // src/vae.cpp:80-81
+    conv("decoder.layers.7.weight", 7, c, v.out_channels, fan(7 * c));
+    return out;
 }
 
 } // namespace tsn

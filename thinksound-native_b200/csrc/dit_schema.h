@@ -35,4 +35,21 @@ struct TensorSpec {
 // global_cond_mlp, empty features) that DitModel::prep_* and the pipeline read.
 std::vector<TensorSpec> dit_schema(const DitGeom & g, bool with_prep);
 
+// The VAE decoder (VaeModel::decode, src/vae.cpp:17-86): conv k7 latent -> 16C, five upsampling
+// blocks (snake, transposed conv with kernel 2s at the strides below, three residual units with
+// dilations 1, 3, 9), final snake and conv k7 C -> out_channels without bias. Widths follow the
+// block order 16C, 8C, 4C, 2C, C, C. All tensors f32 (the reference keeps VAE weights in f32,
+// src/vae.cpp:12-13); transposed-conv weights are stored converted, as the stride-1 conv kernel
+// the reference applies to the zero-stuffed input.
+struct VaeGeom {
+    uint32_t latent_dim = 64, channels = 128, out_channels = 2;
+};
+constexpr uint32_t VAE_STRIDES[5] = {8, 8, 4, 4, 2};
+constexpr uint32_t VAE_DILS[3] = {1, 3, 9};
+inline uint32_t vae_width(const VaeGeom & v, int i) {   // channels after conv0 (i = 0) and block i
+    static const uint32_t mult[6] = {16, 8, 4, 2, 1, 1};
+    return v.channels * mult[i];
+}
+std::vector<TensorSpec> vae_schema(const VaeGeom & v);
+
 } // namespace tsn

@@ -140,37 +140,36 @@ void synth_fill_host(const TensorSpec & s, uint64_t seed, void * dst) {
     for (auto & x : th) x.join();
 }
 
-bool write_synthetic_gguf(const std::string & path, const DitGeom & g, uint64_t seed, bool with_prep,
-                          std::string & err) {
+namespace {
+struct KvU32 { std::string k; uint32_t v; };
+struct KvF32 { std::string k; float v; };
+// GGUF v3 file: the given scalar KV pairs plus architecture and seed, then every tensor of specs
+// filled by synth_fill_host (bit-identical to the device fill)
+bool write_gguf(const std::string & path, const std::vector<TensorSpec> & specs, const std::vector<KvU32> & u32s,
+                const std::vector<KvF32> & f32s, const std::string & arch, uint64_t seed, std::string & err) {
     FILE * f = fopen(path.c_str(), "wb");
     if (!f) { err = "cannot create " + path; return false; }
     auto w = [&](const void * p, size_t n) { fwrite(p, 1, n, f); };
     auto w32 = [&](uint32_t v) { w(&v, 4); };
     auto w64 = [&](uint64_t v) { w(&v, 8); };
     auto ws = [&](const std::string & s) { w64(s.size()); w(s.data(), s.size()); };
-    const std::vector<TensorSpec> specs = dit_schema(g, with_prep);
     const uint64_t align = 32;
-    struct KvU { const char * k; uint32_t v; };
-    const KvU u32s[] = {{"general.alignment", (uint32_t) align}, {"dit.hidden_dim", g.H}, {"dit.num_heads", g.NH},
-                        {"dit.depth", g.depth}, {"dit.fused_depth", g.fused_depth}, {"dit.latent_dim", g.latent_dim}};
     w32(0x46554747u);            // "GGUF"
     w32(3);
     w64(specs.size());
-    w64(6 + 2 + 2);
-    for (const KvU & kv : u32s) { ws(kv.k); w32(4); w32(kv.v); }
-    ws("dit.rope_theta"); w32(6); { float v = g.rope_theta; w(&v, 4); }
-    ws("dit.t_embed_max_period"); w32(6); { float v = g.t_max_period; w(&v, 4); }
-    ws("general.architecture"); w32(8); ws("thinksound-dit-synthetic");
+    w64(1 + u32s.size() + f32s.size() + 2);
+    ws("general.alignment"); w32(4); w32((uint32_t) align);
+    for (const KvU32 & kv : u32s) { ws(kv.k); w32(4); w32(kv.v); }
+    for (const KvF32 & kv : f32s) { ws(kv.k); w32(6); w(&kv.v, 4); }
+    ws("general.architecture"); w32(8); ws(arch);
     ws("tsn.synthetic.seed"); w32(10); w64(seed);
     uint64_t off = 0;
-    std::vector<uint64_t> offs;
     for (const TensorSpec & s : specs) {
         ws(s.name);
         w32(s.n_dims);
         for (uint32_t d = 0; d < s.n_dims; ++d) w64(s.ne[d]);
         w32(s.type);
         w64(off);
-        offs.push_back(off);
         off += (s.nelem() * type_size(s.type) + align - 1) & ~(align - 1);
     }
     long pos = ftell(f);
@@ -190,6 +189,22 @@ bool write_synthetic_gguf(const std::string & path, const DitGeom & g, uint64_t 
     fclose(f);
     if (!ok) err = "write error on " + path;
     return ok;
+}
+} // namespace
+
+bool write_synthetic_gguf(const std::string & path, const DitGeom & g, uint64_t seed, bool with_prep,
+                          std::string & err) {
+    return write_gguf(path, dit_schema(g, with_prep),
+                      {{"dit.hidden_dim", g.H}, {"dit.num_heads", g.NH}, {"dit.depth", g.depth},
+                       {"dit.fused_depth", g.fused_depth}, {"dit.latent_dim", g.latent_dim}},
+                      {{"dit.rope_theta", g.rope_theta}, {"dit.t_embed_max_period", g.t_max_period}},
+                      "thinksound-dit-synthetic", seed, err);
+}
+
+bool write_synthetic_vae_gguf(const std::string & path, const VaeGeom & v, uint64_t seed, std::string & err) {
+    return write_gguf(path, vae_schema(v),
+                      {{"vae.latent_dim", v.latent_dim}, {"vae.channels", v.channels}, {"vae.out_channels", v.out_channels}},
+                      {}, "thinksound-vae-synthetic", seed, err);
 }
 
 } // namespace tsn

@@ -46,6 +46,8 @@ private:
 // Write the seeded synthetic DiT fixture (values from include/tsn_synth.h) as GGUF v3.
 bool write_synthetic_gguf(const std::string & path, const DitGeom & g, uint64_t seed, bool with_prep,
                           std::string & err);
+// The seeded synthetic VAE decoder fixture (f32 tensors of vae_schema).
+bool write_synthetic_vae_gguf(const std::string & path, const VaeGeom & v, uint64_t seed, std::string & err);
 
 // Fill dst with the synthetic values of one tensor (F32 values or BF16 bits by spec.type).
 void synth_fill_host(const TensorSpec & spec, uint64_t seed, void * dst);

@@ -105,6 +105,7 @@ _SIGS = [
     ("tsn_dit_get_tiles", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.POINTER(C.c_int)]),
     ("tsn_dit_set_tiles", C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
     ("tsn_gguf_write_synthetic", C.c_int, [C.c_char_p, C.POINTER(Geom), C.c_uint64, C.c_int]),
+    ("tsn_gguf_write_synthetic_vae", C.c_int, [C.c_char_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64]),
 ]
 
 EXPORTED = [s[0] for s in _SIGS]
@@ -346,6 +347,12 @@ class Dit:
         buf = C.create_string_buffer(1 << 20)
         check(lib().tsn_dit_profile_ops(self.h, buf, len(buf)))
         return buf.value.decode()
+
+
+def write_synthetic_vae_gguf(path: str, channels: int = 128, latent_dim: int = 64, out_channels: int = 2,
+                             seed: int = 4242):
+    """Seeded synthetic VAE decoder GGUF (f32; the tensor names src/vae.cpp reads)."""
+    check(lib().tsn_gguf_write_synthetic_vae(path.encode(), latent_dim, channels, out_channels, seed))
 
 
 def write_synthetic_gguf(path: str, g: Geom, seed: int = 4242, with_prep: bool = False):
