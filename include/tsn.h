@@ -215,6 +215,25 @@ int tsn_dit_get_tiles(tsn_dit * m, int * out, int max_gemms, int * n_gemms);
  * listed, and entries that do not fit their GEMM, fall back to the static cost model. */
 int tsn_dit_set_tiles(tsn_dit * m, const int * tiles, int n);
 
+/* ------------------------------------------------------------------ VAE decoder */
+/* VaeModel::decode (src/vae.cpp:17-86) on the GPU: latent [T, latent_dim] f32 -> interleaved audio
+ * [T * 2048, out_channels] f32. The f32 weights are held as f16 hi + lo halves (split-weight
+ * tcgen05 GEMMs); transposed convs run as polyphase stride-1 convs. */
+typedef struct tsn_vae tsn_vae;
+/* Load from a VAE GGUF (the tensor names of src/vae.cpp; f32, f16 or bf16 values). */
+int tsn_vae_load(tsn_device * dev, const char * gguf_path, tsn_vae ** out);
+/* The seeded synthetic VAE (the values tsn_gguf_write_synthetic_vae writes), generated in memory. */
+int tsn_vae_load_synthetic(tsn_device * dev, uint32_t latent_dim, uint32_t channels, uint32_t out_channels, uint64_t seed,
+                           tsn_vae ** out);
+/* Decode latent [T, latent_dim] into audio [T_audio, out_channels] (host or device pointers;
+ * audio_cap in floats). The first decode of a length plans and captures its graph. */
+int tsn_vae_decode(tsn_vae * v, const float * latent, uint32_t T, float * audio, size_t audio_cap, uint32_t * T_audio);
+/* Device time of the last decode (ms, graph only) and the algorithmic FLOPs (2·M·N·K over every
+ * conv) of the prepared length. */
+double tsn_vae_last_ms(tsn_vae * v);
+double tsn_vae_flops(tsn_vae * v);
+int tsn_vae_free(tsn_vae * v);
+
 /* ------------------------------------------------------------------ fixtures */
 /* Write the seeded synthetic DiT GGUF (with_prep adds the conditioning-prep tensors). Host only. */
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep);

@@ -7,7 +7,10 @@ tiny_forward.npz  one DitModel::forward (src/dit_fwd.cpp:104-304) of the cond ar
                   synthetic DiT (H=256, 4 heads, F=512, 2 joint + 1 fused block; T=24, C=8, TS=16,
                   t=0.5) with every tap the reference dumps, plus the SHA-256 of the weight file.
 tiny_sample.npz   4 Euler steps of the sampler loop (src/pipeline.cpp:142-155), CFG 5.0.
-The weights are regenerated bit-exactly by tsn.write_synthetic_gguf (seed 4242).
+small_vae.npz     VaeModel::decode (src/vae.cpp:17-86) of a seeded latent [3, 64] on the synthetic
+                  VAE with 64 base channels (widths 1024 ... 64), audio [6144, 2].
+The weights are regenerated bit-exactly by tsn.write_synthetic_gguf / write_synthetic_vae_gguf
+(seed 4242). `python tests/golden/make_golden.py vae` writes only the VAE fixture.
 """
 import hashlib
 import os
@@ -24,7 +27,31 @@ import oracle as O  # noqa: E402
 import tsn  # noqa: E402
 
 
+VAE_CH, VAE_T = 64, 3
+
+
+def vae_latent():
+    return np.random.default_rng(SEED).standard_normal((VAE_T, 64)).astype(np.float32)
+
+
+def make_vae(d):
+    gguf = os.path.join(d, "vae.gguf")
+    tsn.write_synthetic_vae_gguf(gguf, channels=VAE_CH, seed=SEED)
+    sha = hashlib.sha256(open(gguf, "rb").read()).hexdigest()
+    lat = vae_latent()
+    audio, _ = O.ref_vae(gguf, lat, workdir=os.path.join(d, "vae"))
+    np.savez_compressed(os.path.join(HERE, "small_vae.npz"), latent=lat, audio=audio, channels=VAE_CH,
+                        gguf_sha256=sha)
+
+
 def main():
+    if not O.have_ref():
+        raise SystemExit("oracle/_ref/ts_ref_dit not built (needs the reference tree)")
+    if sys.argv[1:] == ["vae"]:
+        with tempfile.TemporaryDirectory() as d:
+            make_vae(d)
+        print("wrote small_vae.npz")
+        return
     if not O.have_ref():
         raise SystemExit("oracle/_ref/ts_ref_dit not built (needs the reference tree)")
     T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
@@ -47,6 +74,7 @@ def main():
         out = {f"in_{k}": v for k, v in inp.items()}
         out.update(T=T, C=C, TS=TS, steps=steps, cfg=np.float32(cfg), x_final=xf, gguf_sha256=sha)
         np.savez_compressed(os.path.join(HERE, "tiny_sample.npz"), **out)
+        make_vae(d)
     print("wrote", os.listdir(HERE))
 
 

@@ -174,3 +174,44 @@ def test_port_matches_reference_build_prep(prep_gguf, tmp_path):
     for k in O.PREP_OUT:
         ref = np.fromfile(str(tmp_path / "out" / f"{k}.bin"), np.float32)
         assert np.array_equal(got[k].ravel(), ref), k
+
+
+# ---------------------------------------------------------------- VAE decoder
+def _vae_weights(path):
+    import gguf_read
+    b, kv, tensors, data = gguf_read.read_header(path)
+
+    def W(name):
+        ne, ty, off = tensors[name]
+        a = np.frombuffer(b, np.float32, int(np.prod(ne)), data + off).astype(np.float64)
+        return a.reshape(ne[::-1]) if len(ne) > 1 else a
+    return W
+
+
+@pytest.fixture(scope="module")
+def vae_gguf(tmp_path_factory):
+    p = str(tmp_path_factory.mktemp("vae") / "vae.gguf")
+    tsn.write_synthetic_vae_gguf(p, channels=64, seed=SEED)
+    yield p
+    os.unlink(p)
+
+
+def test_vae_synthetic_gguf_bytes_pinned(vae_gguf):
+    g = np.load(os.path.join(GOLDEN, "small_vae.npz"))
+    assert hashlib.sha256(open(vae_gguf, "rb").read()).hexdigest() == str(g["gguf_sha256"])
+
+
+def test_vae_restatement_reproduces_golden(vae_gguf):
+    """The float64 restatement of VaeModel::decode matches the reference's own decode (golden)."""
+    g = np.load(os.path.join(GOLDEN, "small_vae.npz"))
+    audio = O.vae_decode_np(_vae_weights(vae_gguf), g["latent"])
+    assert audio.shape == g["audio"].shape
+    assert rel_l2(audio, g["audio"]) < 1e-5
+
+
+@needs_ref
+def test_vae_reference_build_matches_restatement(vae_gguf, tmp_path):
+    lat = np.random.default_rng(7).standard_normal((2, 64)).astype(np.float32)
+    audio, js = O.ref_vae(vae_gguf, lat, workdir=str(tmp_path))
+    assert js["T_audio"] == 2 * 2048
+    assert rel_l2(O.vae_decode_np(_vae_weights(vae_gguf), lat), audio) < 1e-5

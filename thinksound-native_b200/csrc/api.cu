@@ -16,7 +16,6 @@ int gemm_noalloc(DeviceCtx & c, const void * W, const void * X, void * Y, const 
                  uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy);
 }
 
-struct tsn_device { DeviceCtx ctx; };
 struct tsn_dit { Model m; };
 
 #define CKR(expr)                                                                                   \

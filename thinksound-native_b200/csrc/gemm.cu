@@ -229,6 +229,80 @@ GroupFn group_for(int bn, int epi, bool split) {
 
 bool gemm_group_supported(int bn, int epi, bool split) { return group_for(bn, epi, split) != nullptr; }
 
+// ---- split activations x split weights (gemm_ws_kernel): the VAE decoder ----
+namespace {
+constexpr int stages_ws(int bn) { return bn == 256 ? 2 : bn == 128 ? 3 : 4; }
+using KernelWsFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
+template <int BN, int EPI>
+KernelWsFn pick_ws() {
+    static_assert(GemmSmem<BN, stages_ws(BN), true, EPI, true>::TOTAL <= 232448, "smem budget");
+    return (KernelWsFn) gemm_ws_kernel<BN, EPI, stages_ws(BN)>;
+}
+template <int BN>
+KernelWsFn ws_epi(int epi) {
+    if (epi == EPI_F32) return pick_ws<BN, EPI_F32>();
+    if (epi == EPI_F16_SNAKE) return pick_ws<BN, EPI_F16_SNAKE>();
+    return nullptr;
+}
+KernelWsFn ws_for(int bn, int epi) {
+    switch (bn) {
+        case 64: return ws_epi<64>(epi);
+        case 128: return ws_epi<128>(epi);
+        case 256: return ws_epi<256>(epi);
+    }
+    return nullptr;
+}
+} // namespace
+
+size_t gemm_ws_smem_bytes(int bn, int epi) {
+    switch (bn * 8 + epi) {
+        case 64 * 8 + EPI_F32: return GemmSmem<64, stages_ws(64), true, EPI_F32, true>::TOTAL;
+        case 64 * 8 + EPI_F16_SNAKE: return GemmSmem<64, stages_ws(64), true, EPI_F16_SNAKE, true>::TOTAL;
+        case 128 * 8 + EPI_F32: return GemmSmem<128, stages_ws(128), true, EPI_F32, true>::TOTAL;
+        case 128 * 8 + EPI_F16_SNAKE: return GemmSmem<128, stages_ws(128), true, EPI_F16_SNAKE, true>::TOTAL;
+        case 256 * 8 + EPI_F32: return GemmSmem<256, stages_ws(256), true, EPI_F32, true>::TOTAL;
+        case 256 * 8 + EPI_F16_SNAKE: return GemmSmem<256, stages_ws(256), true, EPI_F16_SNAKE, true>::TOTAL;
+    }
+    return 0;
+}
+
+// CTAs of the split-weight kernel that fit at once in clusters of `cluster` along z
+int gemm_ws_capacity(int bn, int epi, int cluster) {
+    KernelWsFn fn = ws_for(bn, epi);
+    if (!fn) return 0;
+    if (cluster <= 1) {
+        int per_sm = 0, sms = 0, d = 0;
+        cudaGetDevice(&d);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, 192, gemm_ws_smem_bytes(bn, epi)) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        return per_sm * sms;
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(1, 1, (unsigned) std::max(cluster, 1));
+    cfg.blockDim = dim3(192, 1, 1);
+    cfg.dynamicSmemBytes = gemm_ws_smem_bytes(bn, epi);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = (unsigned) std::max(cluster, 1);
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n * std::max(cluster, 1);
+}
+
+cudaError_t launch_gemm_ws(const GemmLaunch & g, cudaStream_t s) {
+    KernelWsFn fn = ws_for(g.bn, g.epi);
+    if (!fn || !g.split) return cudaErrorInvalidValue;
+    return launch_ex(fn, g.grid, dim3(192), g.smem, s, g.args.splits > 1 ? (unsigned) g.args.splits : 1u, g.ta, g.ta2,
+                     g.tb, g.tb2, g.args);
+}
+
 // Set the dynamic shared-memory limit of every instantiation once, outside any stream capture.
 cudaError_t configure_gemm_kernels() {
     for (int split = 0; split < 2; ++split)
@@ -249,6 +323,12 @@ cudaError_t configure_gemm_kernels() {
                                                      (int) gemm_smem_bytes(bn, split != 0, epi));
                 if (e != cudaSuccess) return e;
             }
+    for (int bn : {64, 128, 256})
+        for (int epi : {(int) EPI_F32, (int) EPI_F16_SNAKE}) {
+            cudaError_t e = cudaFuncSetAttribute((const void *) ws_for(bn, epi), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int) gemm_ws_smem_bytes(bn, epi));
+            if (e != cudaSuccess) return e;
+        }
     for (int bn : {128, 192, 256}) {
         cudaError_t e = cudaFuncSetAttribute((const void *) persistent_for(bn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int) gemm_persistent_smem_bytes(bn));

@@ -104,8 +104,9 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
                     if (rank == 0) mbar_expect_tx(&full[s], 2 * L::STAGE);
                     tma_load_2d_cg2(st, &tmW, full_leader[s], kb * 64, n0);
                 }
-                tma_load_3d_cg2(st + L::X_OFF, &tmX, full_leader[s], ic0, tx + tap - a.pad, b);
-                if (SPLIT) tma_load_3d_cg2(st + L::X_OFF + L::X_BYTES, &tmX2, full_leader[s], ic0, tx + tap - a.pad, b);
+                const int row = tx + tap * (a.dil > 1 ? a.dil : 1) - a.pad;
+                tma_load_3d_cg2(st + L::X_OFF, &tmX, full_leader[s], ic0, row, b);
+                if (SPLIT) tma_load_3d_cg2(st + L::X_OFF + L::X_BYTES, &tmX2, full_leader[s], ic0, row, b);
             }
         }
     } else if (warp == 5) {

@@ -40,6 +40,7 @@ enum GemmEpi : int {
     EPI_F16_SILU = 2,  // out f16 = silu(acc + bias)
     EPI_SWIGLU = 3,    // columns in groups of 64 = [32 w1 | 32 w3] -> out f16 = silu(a)*b
     EPI_QKV = 5,       // bias, per-head RMSNorm(q,k), RoPE(q,k), f16 head-major q/k/v
+    EPI_F16_SNAKE = 6, // out split f16 = snake(acc + bias) with per-column e^alpha, e^-beta (VAE)
 };
 
 struct GemmArgs {
@@ -57,6 +58,8 @@ struct GemmArgs {
     unsigned long long * trace;           // optional per-CTA phase timestamps (tsn_dit_trace_op), else null
     long long part_stride;                // EPI_F32 split-K without a cluster: K slice z writes out + z*part_stride
     int m_fast;                           // grid.x walks the M tiles and grid.y the N tiles (else the reverse)
+    int dil;                              // conv tap dilation: tap k reads row t + k*dil - pad (0 or 1: none)
+    const float * snake_a; const float * snake_b;   // EPI_F16_SNAKE: [N] e^alpha, e^-beta
 };
 
 // phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),
@@ -68,16 +71,19 @@ constexpr int TRACE_SLOTS = 8;
 // float4 so that threads reading consecutive rows hit different banks
 constexpr int ROPE_ROWS = 64, ROPE_STRIDE4 = 17;
 
-template <int BN, int STAGES, bool SPLIT, int EPI>
+template <int BN, int STAGES, bool SPLIT, int EPI, bool WS = false>
 struct GemmSmem {
     static constexpr int A_BYTES = 128 * 128;
     static constexpr int NA = SPLIT ? 2 : 1;
     static constexpr int B_BYTES = BN * 128;
     static constexpr int B_OFF = NA * A_BYTES;
-    static constexpr int STAGE = NA * A_BYTES + B_BYTES;
+    static constexpr int B2_OFF = B_OFF + B_BYTES;        // WS: the weights' lo half
+    static constexpr int STAGE = NA * A_BYTES + (WS ? 2 : 1) * B_BYTES;
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int CONST_OFF = BAR_OFF + 256;       // epilogue constants: bias slice, q/k gains
-    static constexpr int ROPE_OFF = CONST_OFF + (256 + 64 + 64) * 4;
+    // bias (256) + q/k gains (64 + 64), or bias + snake e^alpha, e^-beta (256 each)
+    static constexpr int CONST_BYTES = (EPI == 6 ? 3 * 256 : 256 + 64 + 64) * 4;
+    static constexpr int ROPE_OFF = CONST_OFF + CONST_BYTES;
     static constexpr int ROPE_BYTES = EPI == 5 ? ROPE_ROWS * ROPE_STRIDE4 * 16 : 0;   // EPI_QKV only
     static constexpr int TOTAL = ROPE_OFF + ROPE_BYTES + 1024;   // + alignment slack
 };
@@ -90,8 +96,8 @@ __device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + _
 // Per-tile epilogue constants staged in shared memory before the accumulator is ready.
 struct EpiConst {
     const float * bias;   // bias[n0 .. n0+BN) in shared memory, or null
-    const float * qn;     // q RMSNorm gains (64), shared memory
-    const float * kn;     // k RMSNorm gains (64), shared memory
+    const float * qn;     // q RMSNorm gains (64), shared memory; EPI_F16_SNAKE: e^alpha[n0 ..]
+    const float * kn;     // k RMSNorm gains (64), shared memory; EPI_F16_SNAKE: e^-beta[n0 ..]
     const float4 * rope;  // RoPE rows t0 .. t0+ROPE_ROWS-1 in shared memory (qkv with RoPE), or null
     int t0;
 };
@@ -199,11 +205,18 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             float * o = (float *) a.out + z * a.part_stride + (long long) b * a.out_bs + (long long) t * a.ldo + n;
 #pragma unroll
             for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-        } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU) {
+        } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU || EPI == EPI_F16_SNAKE) {
             __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
             if (EPI == EPI_F16_SILU) {
 #pragma unroll
                 for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
+            }
+            if (EPI == EPI_F16_SNAKE) {   // snake_ (shaders/ops_conv.metal:204-213) on acc + bias
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const float sv = sinf(v[e] * ec.qn[c0 + e]);
+                    v[e] = v[e] + sv * sv * ec.kn[c0 + e];
+                }
             }
 #pragma unroll
             for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, v + q);
@@ -213,11 +226,14 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
 
 // One output tile (M tile mi, N tile ni, K slice z) computed by the whole CTA; `cta` indexes the
 // trace rows. The tensor maps are kernel parameters (grid constants).
-template <int BN, int EPI, int STAGES, bool SPLIT>
+// WS: the weights are split too (W = W_hi + W_lo, tmB2 the lo half; the VAE's f32 weights): each
+// K step issues A_hi·W_hi + A_lo·W_hi + A_hi·W_lo.
+template <int BN, int EPI, int STAGES, bool SPLIT, bool WS = false>
 __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtensorMap * tmA2, const CUtensorMap * tmB,
                                           const GemmArgs & a, const int ab_bf16, const int mi, const int ni, const int z,
-                                          const int cta) {
-    using L = GemmSmem<BN, STAGES, SPLIT, EPI>;
+                                          const int cta, const CUtensorMap * tmB2 = nullptr) {
+    using L = GemmSmem<BN, STAGES, SPLIT, EPI, WS>;
+    static_assert(!WS || SPLIT, "split weights go with a split A operand");
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
@@ -226,7 +242,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
     uint32_t * tslot = (uint32_t *) (tfull + 1);
     volatile int * abort_flag = (volatile int *) (tslot + 1);
     float * cbias = (float *) (smem + L::CONST_OFF);      // BN floats
-    float * cqn = cbias + 256, * ckn = cqn + 64;           // 64 + 64 floats
+    float * cqn = cbias + 256, * ckn = cqn + (EPI == EPI_F16_SNAKE ? 256 : 64);   // q/k gains, or snake e^a, e^-b
     float4 * crope = (float4 *) (smem + L::ROPE_OFF);      // qkv: ROPE_ROWS x ROPE_STRIDE4
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -266,6 +282,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
                 uint8_t * sa = smem + i * L::STAGE;
                 mbar_expect_tx(&full[i], L::STAGE);
                 tma_load_2d(sa + L::B_OFF, tmB, &full[i], (kb_begin + i) * 64, n0);
+                if (WS) tma_load_2d(sa + L::B2_OFF, tmB2, &full[i], (kb_begin + i) * 64, n0);
             }
             pdl_wait();
             for (int i = 0; i < nk; ++i) {
@@ -278,9 +295,11 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
                 if (i >= pre) {
                     mbar_expect_tx(&full[s], L::STAGE);
                     tma_load_2d(sa + L::B_OFF, tmB, &full[s], kb * 64, n0);
+                    if (WS) tma_load_2d(sa + L::B2_OFF, tmB2, &full[s], kb * 64, n0);
                 }
-                tma_load_3d(sa, tmA, &full[s], ic0, t0 + tap - a.pad, b0);
-                if (SPLIT) tma_load_3d(sa + L::A_BYTES, tmA2, &full[s], ic0, t0 + tap - a.pad, b0);
+                const int row = t0 + tap * (a.dil > 1 ? a.dil : 1) - a.pad;
+                tma_load_3d(sa, tmA, &full[s], ic0, row, b0);
+                if (SPLIT) tma_load_3d(sa + L::A_BYTES, tmA2, &full[s], ic0, row, b0);
             }
         }
     } else if (warp == 5) {
@@ -300,6 +319,10 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
                         const uint64_t al = umma_desc_sw128(sa + L::A_BYTES);
                         umma_f16(tmem, al + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, 1u);
                     }
+                    if (WS) {
+                        const uint64_t b2 = umma_desc_sw128(sa + L::B2_OFF);
+                        umma_f16(tmem, ad + (uint64_t) (2 * k), b2 + (uint64_t) (2 * k), idesc, 1u);
+                    }
                 }
                 umma_commit(&empty[s]);
             }
@@ -313,6 +336,8 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
             if (a.bias)
                 for (int i = tid; i < BN && n0 + i < a.N; i += 128) cbias[i] = a.bias[n0 + i];
             if (EPI == EPI_QKV && tid < 64) { cqn[tid] = a.qn[tid]; ckn[tid] = a.kn[tid]; }
+            if (EPI == EPI_F16_SNAKE)
+                for (int i = tid; i < BN && n0 + i < a.N; i += 128) { cqn[i] = a.snake_a[n0 + i]; ckn[i] = a.snake_b[n0 + i]; }
             if (EPI == EPI_QKV && a.rope)
                 for (int i = tid; i < ROPE_ROWS * 16; i += 128) {
                     const int rr = i >> 4, c4 = i & 15;
@@ -405,6 +430,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int mi = a.m_fast ? blockIdx.x : blockIdx.y, ni = a.m_fast ? blockIdx.y : blockIdx.x;
     const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     gemm_tile<BN, EPI, STAGES, SPLIT>(&tmA, &tmA2, &tmB, a, ab_bf16, mi, ni, (int) blockIdx.z, cta);
+}
+
+// Split activations and split weights (the VAE decoder's f32 weights as W_hi + W_lo f16): grid
+// as gemm_tc_kernel, tmB2 the weights' lo half.
+template <int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+gemm_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB2,
+               const __grid_constant__ GemmArgs a) {
+    const int mi = a.m_fast ? blockIdx.x : blockIdx.y, ni = a.m_fast ? blockIdx.y : blockIdx.x;
+    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    gemm_tile<BN, EPI, STAGES, true, true>(&tmA, &tmA2, &tmB, a, 0, mi, ni, (int) blockIdx.z, cta, &tmB2);
 }
 
 // ------------------------------------------------------------------------------------------

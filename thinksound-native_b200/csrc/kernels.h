@@ -51,7 +51,7 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 
 // ---- GEMM / implicit conv (gemm.cu) ----
 struct GemmLaunch {
-    CUtensorMap ta, ta2, tb;      // A (hi), A lo half (split operands only), weights
+    CUtensorMap ta, ta2, tb, tb2; // A (hi), A lo half (split operands only), weights, weights' lo half (WS)
     GemmArgs args;
     dim3 grid;
     int bn = 0, epi = 0, ab_bf16 = 0;
@@ -69,6 +69,10 @@ bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t b
 // Encode a 2-D TMA view {K, N} of an [N][K] 16-bit weight matrix with a {64, bn} box.
 bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16);
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
+// split activations x split weights (gemm_ws_kernel; EPI_F32 or EPI_F16_SNAKE; bn 64, 128, 256)
+cudaError_t launch_gemm_ws(const GemmLaunch & g, cudaStream_t s);
+size_t gemm_ws_smem_bytes(int bn, int epi);
+int gemm_ws_capacity(int bn, int epi, int cluster);
 // A grouped launch of up to MAX_GROUP GEMMs sharing tile width, epilogue and operand split
 // (gemm_tc_group): grid.x = args.cta_end[args.n - 1] CTAs, clusters of `cluster` along x.
 struct GroupLaunch {

@@ -161,3 +161,5 @@ int load_model(Model & m, const std::string * gguf_path, const DitGeom * synth_g
 int load_prep(Model & m);   // loads PrepW from the model's source on first use
 
 } // namespace tsn
+
+struct tsn_device { tsn::DeviceCtx ctx; };   // the C ABI's device handle (include/tsn.h)

@@ -79,6 +79,13 @@ _SIGS = [
     ("tsn_dit_load", C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.POINTER(C.c_void_p)]),
     ("tsn_dit_load_synthetic", C.c_int, [C.c_void_p, C.POINTER(Geom), C.c_uint64, C.c_int, C.POINTER(C.c_void_p)]),
     ("tsn_dit_free", C.c_int, [C.c_void_p]),
+    ("tsn_vae_load", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
+    ("tsn_vae_load_synthetic", C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64,
+                                         C.POINTER(C.c_void_p)]),
+    ("tsn_vae_decode", C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_size_t, C.POINTER(C.c_uint32)]),
+    ("tsn_vae_last_ms", C.c_double, [C.c_void_p]),
+    ("tsn_vae_flops", C.c_double, [C.c_void_p]),
+    ("tsn_vae_free", C.c_int, [C.c_void_p]),
     ("tsn_dit_get_geom", C.c_int, [C.c_void_p, C.POINTER(Geom)]),
     ("tsn_dit_weight_bytes", C.c_size_t, [C.c_void_p]),
     ("tsn_dit_prepare", C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
@@ -208,6 +215,49 @@ class Device:
 
     def cfg_euler(self, fc, fu, x, n, cfg, dt):
         check(lib().tsn_cfg_euler(self.h, _p(fc), _p(fu), _p(x), n, cfg, dt))
+
+
+class Vae:
+    """tn::VaeModel's decoder on the device: latent [T, 64] -> audio [T * 2048, out_channels]."""
+
+    def __init__(self, dev: Device, gguf: str | None = None, channels: int = 128, latent_dim: int = 64,
+                 out_channels: int = 2, seed: int = 4242):
+        self.dev = dev
+        h = C.c_void_p()
+        if gguf is not None:
+            check(lib().tsn_vae_load(dev.h, gguf.encode(), C.byref(h)))
+        else:
+            check(lib().tsn_vae_load_synthetic(dev.h, latent_dim, channels, out_channels, seed, C.byref(h)))
+        self.h = h
+        self.out_channels = out_channels
+        dev._models.add(self)
+
+    def decode(self, latent):
+        """Host latent [T, latent_dim] f32 -> host audio [T_audio, out_channels] f32."""
+        import numpy as np
+        lat = np.ascontiguousarray(latent, np.float32)
+        T = lat.shape[0]
+        out = np.zeros((T * 2048, self.out_channels), np.float32)
+        ta = C.c_uint32()
+        check(lib().tsn_vae_decode(self.h, lat.ctypes.data, T, out.ctypes.data, out.size, C.byref(ta)))
+        return out[:ta.value]
+
+    def last_ms(self) -> float:
+        return lib().tsn_vae_last_ms(self.h)
+
+    def flops(self) -> float:
+        return lib().tsn_vae_flops(self.h)
+
+    def close(self):
+        if self.h and self.dev.h:
+            lib().tsn_vae_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 class Dit:
