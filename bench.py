@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--config5", action="store_true", help="64 generations x 24 steps, data-parallel, final gather")
     ap.add_argument("--gens-per-forward", type=int, default=4, help="config 5: generations batched per forward (1-4)")
     ap.add_argument("--generations", type=int, default=64)
+    ap.add_argument("--vae", action="store_true",
+                    help="the VAE decoder after the sampler (src/vae.cpp): decode T latent frames, synthetic f32 weights")
+    ap.add_argument("--vae-channels", type=int, default=128)
     return ap.parse_args()
 
 
@@ -569,10 +572,76 @@ def run_config5(a):
         dist.destroy_process_group()
 
 
+def run_vae(a):
+    """The VAE decode of one 8 s latent [T, 64] -> stereo audio [T * 2048, 2] (the step after the
+    sampler, src/vae.cpp:17-86): device time of the decode graph, end-to-end time through
+    tsn_vae_decode with host buffers, the split-weight GEMMs' algorithmic rate, and the reference's
+    own decode (oracle/_ref over the scalar kernels) on a bounded sample of latent frames."""
+    import time
+
+    import numpy as np
+
+    import tsn
+
+    dev = tsn.Device(0)
+    v = tsn.Vae(dev, channels=a.vae_channels, seed=a.seed)
+    lat = np.random.default_rng(a.seed).standard_normal((a.T, 64)).astype(np.float32)
+    for _ in range(max(a.warmup, 3)):
+        v.decode(lat)
+    dev_ms, wall = [], []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        v.decode(lat)
+        wall.append(time.perf_counter() - t0)
+        dev_ms.append(v.last_ms())
+    ms = max(dev_ms)
+    flops = v.flops()
+    _, peak, _, peak_src = peaks()
+    line = {
+        "metric": "VAE decodes/s of one 8 s latent (T=188 -> 385024 stereo samples)",
+        "value": 1000.0 / ms, "unit": "decodes/s", "n_gpus": 1, "steps": a.steps, "warmup": max(a.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 split activations x f16 split weights (f32 weights as hi+lo), f32 accumulate",
+        "data": "synthetic",
+        "config": {"workload": "VAE decoder (src/vae.cpp): conv k7 64->16C, 5 upsampling blocks (strides 8,8,4,4,2, "
+                               "3 residual units each), snake, conv k7 C->2", "T": a.T, "channels": a.vae_channels,
+                   "weights": "synthetic f32 (seed %d)" % a.seed},
+        "roofline": {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                     "frac": flops / (ms * 1e-3) / 1e12 / peak, "algorithmic_flops_per_step": flops,
+                     "peak_source": f"{peak_src} bf16_tflops (burst)",
+                     "note": "2·M·N·K over every conv; each K step issues three split products"},
+        "e2e": {"value": 1.0 / max(wall), "unit": "decodes/s", "h2d_bytes_per_step": lat.nbytes,
+                "d2h_bytes_per_step": a.T * 2048 * 2 * 4},
+        "gpu_launches": None,
+    }
+    if not a.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        if O.have_ref():
+            frames = 2
+            _, js = O.ref_vae(write_vae_fixture(a), lat[:frames])
+            sec = min(js["seconds"]) * a.T / frames
+            line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "decodes/s", "cores": js["threads"], "kind": "reference",
+                                    "sample": f"the reference's decode of {frames} latent frames, scaled to {a.T}"}
+    print(json.dumps(line), flush=True)
+
+
+def write_vae_fixture(a):
+    import tempfile
+
+    import tsn
+    p = os.path.join(tempfile.gettempdir(), f"tsn_bench_vae_{a.vae_channels}_{a.seed}.gguf")
+    if not os.path.exists(p):
+        tsn.write_synthetic_vae_gguf(p, channels=a.vae_channels, seed=a.seed)
+    return p
+
+
 def main():
     a = parse()
     apply_long(a)
-    if a.impl == "reference":
+    if a.vae:
+        run_vae(a)
+    elif a.impl == "reference":
         run_reference(a)
     elif a.cfg_split:
         run_cfg_split(a)

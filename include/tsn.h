@@ -231,6 +231,8 @@ int tsn_vae_decode(tsn_vae * v, const float * latent, uint32_t T, float * audio,
 /* Device time of the last decode (ms, graph only) and the algorithmic FLOPs (2·M·N·K over every
  * conv) of the prepared length. */
 double tsn_vae_last_ms(tsn_vae * v);
+/* The last decoded length once more, launch by launch, one line per launch (name, device ms). */
+int tsn_vae_profile_ops(tsn_vae * v, char * out, size_t cap);
 double tsn_vae_flops(tsn_vae * v);
 int tsn_vae_free(tsn_vae * v);
 

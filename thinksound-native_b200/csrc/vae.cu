@@ -388,6 +388,28 @@ struct VaeModel {
         return TSN_OK;
     }
 
+    // the prepared decode eagerly, one line per launch: index, name, device ms
+    int profile(std::string & rep) {
+        if (!T) return fail(TSN_ERR_STATE, "decode once before profiling");
+        std::vector<cudaEvent_t> ev(ops.size() + 1);
+        for (auto & e : ev) VCK(cudaEventCreate(&e));
+        VCK(cudaEventRecord(ev[0], dev->stream));
+        for (size_t i = 0; i < ops.size(); ++i) {
+            VCK(ops[i](dev->stream));
+            VCK(cudaEventRecord(ev[i + 1], dev->stream));
+        }
+        int rc = dev->sync();
+        char line[160];
+        for (size_t i = 0; !rc && i < ops.size(); ++i) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            snprintf(line, sizeof line, "%4zu %-16s %8.4f ms\n", i, op_names[i].c_str(), ms);
+            rep += line;
+        }
+        for (auto & e : ev) cudaEventDestroy(e);
+        return rc;
+    }
+
     long long audio_len(int T_) const {
         long long t = T_;
         for (int n = 0; n < 5; ++n) t *= VAE_STRIDES[n];
@@ -463,6 +485,15 @@ int tsn_vae_decode(tsn_vae * v, const float * latent, uint32_t T, float * audio,
 }
 
 double tsn_vae_last_ms(tsn_vae * v) { return v ? v->m.last_ms : 0.0; }
+
+int tsn_vae_profile_ops(tsn_vae * v, char * out, size_t cap) {
+    if (!v) return fail(TSN_ERR_ARG, "null argument");
+    VRT(v->m.dev->activate());
+    std::string rep;
+    VRT(v->m.profile(rep));
+    if (out && cap) { std::strncpy(out, rep.c_str(), cap - 1); out[cap - 1] = 0; }
+    return TSN_OK;
+}
 double tsn_vae_flops(tsn_vae * v) { return v ? v->m.flops : 0.0; }
 
 int tsn_vae_free(tsn_vae * v) {

@@ -84,6 +84,7 @@ _SIGS = [
                                          C.POINTER(C.c_void_p)]),
     ("tsn_vae_decode", C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_size_t, C.POINTER(C.c_uint32)]),
     ("tsn_vae_last_ms", C.c_double, [C.c_void_p]),
+    ("tsn_vae_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_vae_flops", C.c_double, [C.c_void_p]),
     ("tsn_vae_free", C.c_int, [C.c_void_p]),
     ("tsn_dit_get_geom", C.c_int, [C.c_void_p, C.POINTER(Geom)]),
@@ -247,6 +248,11 @@ class Vae:
 
     def flops(self) -> float:
         return lib().tsn_vae_flops(self.h)
+
+    def profile_ops(self) -> str:
+        buf = C.create_string_buffer(1 << 18)
+        check(lib().tsn_vae_profile_ops(self.h, buf, len(buf)))
+        return buf.value.decode()
 
     def close(self):
         if self.h and self.dev.h:
