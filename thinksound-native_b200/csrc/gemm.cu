@@ -240,8 +240,12 @@ KernelWsFn pick_ws() {
 }
 template <int BN>
 KernelWsFn ws_epi(int epi) {
-    if (epi == EPI_F32) return pick_ws<BN, EPI_F32>();
-    if (epi == EPI_F16_SNAKE) return pick_ws<BN, EPI_F16_SNAKE>();
+    switch (epi) {
+        case EPI_F32: return pick_ws<BN, EPI_F32>();
+        case EPI_F16_SNAKE: return pick_ws<BN, EPI_F16_SNAKE>();
+        case EPI_RESID_SNAKE: return pick_ws<BN, EPI_RESID_SNAKE>();
+        case EPI_F32_SNAKE2: return pick_ws<BN, EPI_F32_SNAKE2>();
+    }
     return nullptr;
 }
 KernelWsFn ws_for(int bn, int epi) {
@@ -254,14 +258,69 @@ KernelWsFn ws_for(int bn, int epi) {
 }
 } // namespace
 
+namespace {
+template <int BN>
+size_t ws_smem_of(int epi) {
+    switch (epi) {
+        case EPI_F32: return GemmSmem<BN, stages_ws(BN), true, EPI_F32, true>::TOTAL;
+        case EPI_F16_SNAKE: return GemmSmem<BN, stages_ws(BN), true, EPI_F16_SNAKE, true>::TOTAL;
+        case EPI_RESID_SNAKE: return GemmSmem<BN, stages_ws(BN), true, EPI_RESID_SNAKE, true>::TOTAL;
+        case EPI_F32_SNAKE2: return GemmSmem<BN, stages_ws(BN), true, EPI_F32_SNAKE2, true>::TOTAL;
+    }
+    return 0;
+}
+} // namespace
+
 size_t gemm_ws_smem_bytes(int bn, int epi) {
-    switch (bn * 8 + epi) {
-        case 64 * 8 + EPI_F32: return GemmSmem<64, stages_ws(64), true, EPI_F32, true>::TOTAL;
-        case 64 * 8 + EPI_F16_SNAKE: return GemmSmem<64, stages_ws(64), true, EPI_F16_SNAKE, true>::TOTAL;
-        case 128 * 8 + EPI_F32: return GemmSmem<128, stages_ws(128), true, EPI_F32, true>::TOTAL;
-        case 128 * 8 + EPI_F16_SNAKE: return GemmSmem<128, stages_ws(128), true, EPI_F16_SNAKE, true>::TOTAL;
-        case 256 * 8 + EPI_F32: return GemmSmem<256, stages_ws(256), true, EPI_F32, true>::TOTAL;
-        case 256 * 8 + EPI_F16_SNAKE: return GemmSmem<256, stages_ws(256), true, EPI_F16_SNAKE, true>::TOTAL;
+    switch (bn) {
+        case 64: return ws_smem_of<64>(epi);
+        case 128: return ws_smem_of<128>(epi);
+        case 256: return ws_smem_of<256>(epi);
+    }
+    return 0;
+}
+
+namespace {
+template <int BN, int EPI>
+KernelWsFn pick_wsp() {
+    static_assert(PersistWsSmem<BN, stages_ws(BN), EPI>::TOTAL <= 232448, "smem budget");
+    return (KernelWsFn) gemm_ws_persistent<BN, EPI, stages_ws(BN)>;
+}
+template <int BN>
+KernelWsFn wsp_epi(int epi) {
+    switch (epi) {
+        case EPI_F32: return pick_wsp<BN, EPI_F32>();
+        case EPI_F16_SNAKE: return pick_wsp<BN, EPI_F16_SNAKE>();
+        case EPI_RESID_SNAKE: return pick_wsp<BN, EPI_RESID_SNAKE>();
+        case EPI_F32_SNAKE2: return pick_wsp<BN, EPI_F32_SNAKE2>();
+    }
+    return nullptr;
+}
+KernelWsFn wsp_for(int bn, int epi) {
+    switch (bn) {
+        case 64: return wsp_epi<64>(epi);
+        case 128: return wsp_epi<128>(epi);
+        case 256: return wsp_epi<256>(epi);
+    }
+    return nullptr;
+}
+template <int BN>
+size_t wsp_smem_of(int epi) {
+    switch (epi) {
+        case EPI_F32: return PersistWsSmem<BN, stages_ws(BN), EPI_F32>::TOTAL;
+        case EPI_F16_SNAKE: return PersistWsSmem<BN, stages_ws(BN), EPI_F16_SNAKE>::TOTAL;
+        case EPI_RESID_SNAKE: return PersistWsSmem<BN, stages_ws(BN), EPI_RESID_SNAKE>::TOTAL;
+        case EPI_F32_SNAKE2: return PersistWsSmem<BN, stages_ws(BN), EPI_F32_SNAKE2>::TOTAL;
+    }
+    return 0;
+}
+} // namespace
+
+size_t gemm_ws_persistent_smem_bytes(int bn, int epi) {
+    switch (bn) {
+        case 64: return wsp_smem_of<64>(epi);
+        case 128: return wsp_smem_of<128>(epi);
+        case 256: return wsp_smem_of<256>(epi);
     }
     return 0;
 }
@@ -297,6 +356,11 @@ int gemm_ws_capacity(int bn, int epi, int cluster) {
 }
 
 cudaError_t launch_gemm_ws(const GemmLaunch & g, cudaStream_t s) {
+    if (g.persistent) {
+        KernelWsFn fn = wsp_for(g.bn, g.epi);
+        if (!fn || !g.split || g.args.splits != 1) return cudaErrorInvalidValue;
+        return launch_ex(fn, g.grid, dim3(192), g.smem, s, 1u, g.ta, g.ta2, g.tb, g.tb2, g.args);
+    }
     KernelWsFn fn = ws_for(g.bn, g.epi);
     if (!fn || !g.split) return cudaErrorInvalidValue;
     return launch_ex(fn, g.grid, dim3(192), g.smem, s, g.args.splits > 1 ? (unsigned) g.args.splits : 1u, g.ta, g.ta2,
@@ -324,9 +388,12 @@ cudaError_t configure_gemm_kernels() {
                 if (e != cudaSuccess) return e;
             }
     for (int bn : {64, 128, 256})
-        for (int epi : {(int) EPI_F32, (int) EPI_F16_SNAKE}) {
+        for (int epi : {(int) EPI_F32, (int) EPI_F16_SNAKE, (int) EPI_RESID_SNAKE, (int) EPI_F32_SNAKE2}) {
             cudaError_t e = cudaFuncSetAttribute((const void *) ws_for(bn, epi), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int) gemm_ws_smem_bytes(bn, epi));
+            if (e == cudaSuccess)
+                e = cudaFuncSetAttribute((const void *) wsp_for(bn, epi), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int) gemm_ws_persistent_smem_bytes(bn, epi));
             if (e != cudaSuccess) return e;
         }
     for (int bn : {128, 192, 256}) {

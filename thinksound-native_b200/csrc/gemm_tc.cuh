@@ -40,8 +40,12 @@ enum GemmEpi : int {
     EPI_F16_SILU = 2,  // out f16 = silu(acc + bias)
     EPI_SWIGLU = 3,    // columns in groups of 64 = [32 w1 | 32 w3] -> out f16 = silu(a)*b
     EPI_QKV = 5,       // bias, per-head RMSNorm(q,k), RoPE(q,k), f16 head-major q/k/v
-    EPI_F16_SNAKE = 6, // out split f16 = snake(acc + bias) with per-column e^alpha, e^-beta (VAE)
+    EPI_F16_SNAKE = 6, // out split f16 = snake(acc + bias) with per-column e^alpha, e^-beta (VAE;
+                       // hardware __sinf: a few 1e-6 absolute, far below the f16 rounding of the output)
+    EPI_RESID_SNAKE = 7,   // out f32 += acc + bias (residual, in place); out2 split f16 = snake(out)
+    EPI_F32_SNAKE2 = 8,    // out f32 = acc + bias; out2 split f16 = snake(out)
 };
+constexpr bool epi_snake(int epi) { return epi == EPI_F16_SNAKE || epi == EPI_RESID_SNAKE || epi == EPI_F32_SNAKE2; }
 
 struct GemmArgs {
     int rows, B, bt, bb, m_tiles_t, N, k_blocks, ic_blocks, pad, splits, kb_per_split;
@@ -59,7 +63,8 @@ struct GemmArgs {
     long long part_stride;                // EPI_F32 split-K without a cluster: K slice z writes out + z*part_stride
     int m_fast;                           // grid.x walks the M tiles and grid.y the N tiles (else the reverse)
     int dil;                              // conv tap dilation: tap k reads row t + k*dil - pad (0 or 1: none)
-    const float * snake_a; const float * snake_b;   // EPI_F16_SNAKE: [N] e^alpha, e^-beta
+    const float * snake_a; const float * snake_b;   // snake epilogues: [N] e^alpha, e^-beta
+    void * out2; long long ldo2, out2_lo;           // EPI_RESID_SNAKE / EPI_F32_SNAKE2: split f16 [rows][ldo2] (B = 1)
 };
 
 // phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),
@@ -82,7 +87,7 @@ struct GemmSmem {
     static constexpr int BAR_OFF = STAGES * STAGE;
     static constexpr int CONST_OFF = BAR_OFF + 256;       // epilogue constants: bias slice, q/k gains
     // bias (256) + q/k gains (64 + 64), or bias + snake e^alpha, e^-beta (256 each)
-    static constexpr int CONST_BYTES = (EPI == 6 ? 3 * 256 : 256 + 64 + 64) * 4;
+    static constexpr int CONST_BYTES = (EPI >= 6 && EPI <= 8 ? 3 * 256 : 256 + 64 + 64) * 4;
     static constexpr int ROPE_OFF = CONST_OFF + CONST_BYTES;
     static constexpr int ROPE_BYTES = EPI == 5 ? ROPE_ROWS * ROPE_STRIDE4 * 16 : 0;   // EPI_QKV only
     static constexpr int TOTAL = ROPE_OFF + ROPE_BYTES + 1024;   // + alignment slack
@@ -214,12 +219,31 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             if (EPI == EPI_F16_SNAKE) {   // snake_ (shaders/ops_conv.metal:204-213) on acc + bias
 #pragma unroll
                 for (int e = 0; e < 32; ++e) {
-                    const float sv = sinf(v[e] * ec.qn[c0 + e]);
+                    const float sv = __sinf(v[e] * ec.qn[c0 + e]);
                     v[e] = v[e] + sv * sv * ec.kn[c0 + e];
                 }
             }
 #pragma unroll
             for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, v + q);
+        } else if constexpr (EPI == EPI_RESID_SNAKE || EPI == EPI_F32_SNAKE2) {
+            float * xo = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
+            if (EPI == EPI_RESID_SNAKE) {   // the residual add of src/vae.cpp:75
+#pragma unroll
+                for (int q = 0; q < 32; q += 4) {
+                    const float4 r = *(const float4 *) (xo + q);
+                    v[q] += r.x; v[q + 1] += r.y; v[q + 2] += r.z; v[q + 3] += r.w;
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) *(float4 *) (xo + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {   // snake_ (shaders/ops_conv.metal:204-213) of the new value
+                const float sv = __sinf(v[e] * ec.qn[c0 + e]);
+                v[e] = v[e] + sv * sv * ec.kn[c0 + e];
+            }
+            __half * ho = (__half *) a.out2 + (long long) t * a.ldo2 + n;
+#pragma unroll
+            for (int q = 0; q < 32; q += 8) store8_split(ho + q, a.out2_lo, v + q);
         }
     }
 }
@@ -242,7 +266,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
     uint32_t * tslot = (uint32_t *) (tfull + 1);
     volatile int * abort_flag = (volatile int *) (tslot + 1);
     float * cbias = (float *) (smem + L::CONST_OFF);      // BN floats
-    float * cqn = cbias + 256, * ckn = cqn + (EPI == EPI_F16_SNAKE ? 256 : 64);   // q/k gains, or snake e^a, e^-b
+    float * cqn = cbias + 256, * ckn = cqn + (epi_snake(EPI) ? 256 : 64);   // q/k gains, or snake e^a, e^-b
     float4 * crope = (float4 *) (smem + L::ROPE_OFF);      // qkv: ROPE_ROWS x ROPE_STRIDE4
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -336,7 +360,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
             if (a.bias)
                 for (int i = tid; i < BN && n0 + i < a.N; i += 128) cbias[i] = a.bias[n0 + i];
             if (EPI == EPI_QKV && tid < 64) { cqn[tid] = a.qn[tid]; ckn[tid] = a.kn[tid]; }
-            if (EPI == EPI_F16_SNAKE)
+            if (epi_snake(EPI))
                 for (int i = tid; i < BN && n0 + i < a.N; i += 128) { cqn[i] = a.snake_a[n0 + i]; ckn[i] = a.snake_b[n0 + i]; }
             if (EPI == EPI_QKV && a.rope)
                 for (int i = tid; i < ROPE_ROWS * 16; i += 128) {
@@ -635,6 +659,228 @@ gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constan
             tc_fence_before();
             __syncwarp();
             if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&aempty[buf])) : "memory");
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * ACC);
+    }
+    if (tr && threadIdx.x == 0) tr[5] = global_ns();
+    if (*abort_flag && threadIdx.x == 0) {
+        const uint64_t t1 = global_ns();
+        while (global_ns() - t1 < 20000ull) {}
+    }
+}
+
+
+// ------------------------------------------------------------------------------------------
+// Persistent split-activation x split-weight GEMM / implicit conv (the VAE decoder's convs, up to
+// 3008 tiles per launch): one CTA per SM walks the tiles blockIdx.x, +gridDim.x, ... (M tiles
+// fastest); the operand ring runs on across tiles and two TMEM accumulators let the epilogue of
+// tile i (any epi_unit epilogue, constants read from global memory) overlap the mainloop of tile
+// i + 1. Conv taps and dilation as in gemm_tile; no split-K (a.splits must be 1).
+template <int BN, int STAGES, int EPI>
+struct PersistWsSmem {
+    using S = GemmSmem<BN, STAGES, true, EPI, true>;
+    static constexpr int STAGE = S::STAGE, A_BYTES = S::A_BYTES, B_OFF = S::B_OFF, B2_OFF = S::B2_OFF;
+    static constexpr int BAR_OFF = STAGES * STAGE;
+    static constexpr int XPOSE_OFF = BAR_OFF + 256;      // per epilogue warp: 32 x 33 floats (padded)
+    static constexpr int TOTAL = XPOSE_OFF + 4 * 32 * 33 * 4 + 1024;   // + alignment slack
+};
+
+template <int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+gemm_ws_persistent(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+                   const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmB2,
+                   const __grid_constant__ GemmArgs a) {
+    using L = PersistWsSmem<BN, STAGES, EPI>;
+    constexpr uint32_t ACC = BN <= 128 ? 128 : 256;   // TMEM column offset of the second accumulator
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
+    uint64_t * empty = full + STAGES;
+    uint64_t * afull = empty + STAGES;       // [2] accumulator ready for the epilogue
+    uint64_t * aempty = afull + 2;           // [2] accumulator drained (4 arrivals: one per epilogue warp)
+    uint32_t * tslot = (uint32_t *) (aempty + 2);
+    volatile int * abort_flag = (volatile int *) (tslot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long * tr = a.trace ? a.trace + (size_t) blockIdx.x * TRACE_SLOTS : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
+    const int MT = a.m_tiles_t * ((a.B + a.bb - 1) / a.bb), NT = (a.N + BN - 1) / BN;
+    const int tiles = MT * NT, nk = a.k_blocks, dil = a.dil > 1 ? a.dil : 1;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&afull[b], 1); mbar_init(&aempty[b], 4); }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (threadIdx.x == 0) pdl_trigger();
+    if (warp == 4 && lane == 0) { tma_prefetch(&tmA); tma_prefetch(&tmA2); tma_prefetch(&tmB); tma_prefetch(&tmB2); }
+    if (warp == 5) tmem_alloc(tslot, 2 * ACC);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    auto tile_coords = [&](int tile, int & t0, int & b0, int & n0) {
+        const int mi = tile % MT, ni = tile / MT;
+        t0 = (mi % a.m_tiles_t) * a.bt;
+        b0 = (mi / a.m_tiles_t) * a.bb;
+        n0 = ni * BN;
+    };
+
+    if (warp == 4) {
+        if (lane == 0) {
+            // the first tile's weight stages do not depend on the upstream kernel
+            int t0, b0, n0;
+            tile_coords(blockIdx.x, t0, b0, n0);
+            const int pre = blockIdx.x < tiles ? (nk < STAGES ? nk : STAGES) : 0;
+            for (int i = 0; i < pre; ++i) {
+                mbar_expect_tx(&full[i], L::STAGE);
+                tma_load_2d(smem + i * L::STAGE + L::B_OFF, &tmB, &full[i], i * 64, n0);
+                tma_load_2d(smem + i * L::STAGE + L::B2_OFF, &tmB2, &full[i], i * 64, n0);
+            }
+            pdl_wait();
+            int g = 0;   // k blocks issued by this CTA so far (ring position)
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x) {
+                tile_coords(tile, t0, b0, n0);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (g >= STAGES && !mbar_wait(&empty[s], ((g / STAGES) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_EMPTY)) {
+                        stop = true;
+                        break;
+                    }
+                    uint8_t * sa = smem + s * L::STAGE;
+                    if (g >= pre) {
+                        mbar_expect_tx(&full[s], L::STAGE);
+                        tma_load_2d(sa + L::B_OFF, &tmB, &full[s], kb * 64, n0);
+                        tma_load_2d(sa + L::B2_OFF, &tmB2, &full[s], kb * 64, n0);
+                    }
+                    const int tap = kb / a.ic_blocks, ic0 = (kb % a.ic_blocks) * 64;
+                    const int row = t0 + tap * dil - a.pad;
+                    tma_load_3d(sa, &tmA, &full[s], ic0, row, b0);
+                    tma_load_3d(sa + L::A_BYTES, &tmA2, &full[s], ic0, row, b0);
+                }
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(BN, 0);
+            int g = 0, i = 0;
+            bool stop = false;
+            for (int tile = blockIdx.x; tile < tiles && !stop; tile += gridDim.x, ++i) {
+                const int buf = i & 1;
+                if (i >= 2 && !mbar_wait(&aempty[buf], ((i >> 1) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_TMEM)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t) (buf * ACC);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % STAGES;
+                    if (!mbar_wait(&full[s], (g / STAGES) & 1, abort_flag, a.err, DEV_TIMEOUT_FULL)) { stop = true; break; }
+                    if (tr && g == 0) tr[2] = global_ns();
+                    tc_fence_after();
+                    const uint8_t * sa = smem + s * L::STAGE;
+                    const uint64_t ad = umma_desc_sw128(sa), al = umma_desc_sw128(sa + L::A_BYTES),
+                                   bd = umma_desc_sw128(sa + L::B_OFF), b2 = umma_desc_sw128(sa + L::B2_OFF);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        umma_f16(d, ad + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, (kb | k) != 0);
+                        umma_f16(d, al + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, 1u);
+                        umma_f16(d, ad + (uint64_t) (2 * k), b2 + (uint64_t) (2 * k), idesc, 1u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (!stop) umma_commit(&afull[buf]);
+            }
+        }
+    } else {
+        pdl_wait();
+        const int r = warp * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        int i = 0;
+        for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+            const int buf = i & 1;
+            if (!mbar_wait(&afull[buf], (i >> 1) & 1, abort_flag, a.err, DEV_TIMEOUT_TMEM)) break;
+            tc_fence_after();
+            int t0, b0, n0;
+            tile_coords(tile, t0, b0, n0);
+            // the tile's constants straight from global memory (L1/L2-resident across tiles)
+            const EpiConst ec{a.bias ? a.bias + n0 : nullptr, a.snake_a ? a.snake_a + n0 : nullptr,
+                              a.snake_b ? a.snake_b + n0 : nullptr, nullptr, t0};
+            if constexpr (EPI == EPI_F32 || EPI == EPI_RESID_SNAKE || EPI == EPI_F32_SNAKE2) {
+                // rows are 512 B or more apart: each 32 x 32 chunk goes through this warp's padded
+                // smem block, so every access instruction covers four whole 128-byte row segments
+                // (the residual read, the f32 write and the split f16 write)
+                float * tb = (float *) (smem + L::XPOSE_OFF) + warp * (32 * 33);
+                const int cq = (lane & 7) * 4;
+#pragma unroll 1
+                for (int c = 0; c < BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(trow + (uint32_t) (buf * ACC + c), v);
+                    if (n0 + c >= a.N) continue;                  // the same for the whole warp
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) tb[lane * 33 + j] = v[j];
+                    __syncwarp();
+                    const int col = n0 + c + cq;
+                    const bool col_ok = col < a.N;
+                    float bl[4] = {0.f, 0.f, 0.f, 0.f}, ea[4] = {0.f, 0.f, 0.f, 0.f}, eb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (col_ok && ec.bias) bl[e] = __ldg(ec.bias + c + cq + e);
+                        if (EPI != EPI_F32 && col_ok) { ea[e] = __ldg(ec.qn + c + cq + e); eb[e] = __ldg(ec.kn + c + cq + e); }
+                    }
+                    // the chunk's residual rows are read before any arithmetic: one memory round trip
+                    float4 xr[8];
+                    if (EPI == EPI_RESID_SNAKE) {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int row = warp * 32 + 4 * i + (lane >> 3);
+                            const int b = b0 + row / a.bt, t = t0 + row % a.bt;
+                            xr[i] = col_ok && t < a.rows && b < a.B
+                                        ? *(const float4 *) ((const float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + col)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int rr = 4 * i + (lane >> 3), row = warp * 32 + rr;
+                        const int b = b0 + row / a.bt, t = t0 + row % a.bt;
+                        if (!col_ok || t >= a.rows || b >= a.B) continue;
+                        float y[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) y[e] = tb[rr * 33 + cq + e] + bl[e];
+                        float * xo = (float *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + col;
+                        if (EPI == EPI_RESID_SNAKE) {   // the residual add of src/vae.cpp:75
+                            y[0] += xr[i].x; y[1] += xr[i].y; y[2] += xr[i].z; y[3] += xr[i].w;
+                        }
+                        *(float4 *) xo = make_float4(y[0], y[1], y[2], y[3]);
+                        if constexpr (EPI != EPI_F32) {
+                            __align__(8) __half hv[4], lv[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float sv = __sinf(y[e] * ea[e]);       // snake_, ops_conv.metal:204-213
+                                const float z = y[e] + sv * sv * eb[e];
+                                hv[e] = __float2half_rn(z);
+                                lv[e] = __float2half_rn(z - __half2float(hv[e]));
+                            }
+                            __half * ho = (__half *) a.out2 + (long long) t * a.ldo2 + col;
+                            *(uint2 *) ho = *(const uint2 *) hv;
+                            *(uint2 *) (ho + a.out2_lo) = *(const uint2 *) lv;
+                        }
+                    }
+                    __syncwarp();
+                }
+            } else {
+                auto load_tmem = [&](int c, float * v) { tmem_ld32(trow + (uint32_t) (buf * ACC + c), v); };
+#pragma unroll 1
+                for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, ec, r, u, n0, t0, b0, 0, true, load_tmem);
+            }
+            // this warp is done reading accumulator `buf`
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&aempty[buf]);
         }
     }
     tc_fence_before();

@@ -72,6 +72,7 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);
 // split activations x split weights (gemm_ws_kernel; EPI_F32 or EPI_F16_SNAKE; bn 64, 128, 256)
 cudaError_t launch_gemm_ws(const GemmLaunch & g, cudaStream_t s);
 size_t gemm_ws_smem_bytes(int bn, int epi);
+size_t gemm_ws_persistent_smem_bytes(int bn, int epi);   // GemmLaunch::persistent with the split-weight kernel
 int gemm_ws_capacity(int bn, int epi, int cluster);
 // A grouped launch of up to MAX_GROUP GEMMs sharing tile width, epilogue and operand split
 // (gemm_tc_group): grid.x = args.cta_end[args.n - 1] CTAs, clusters of `cluster` along x.

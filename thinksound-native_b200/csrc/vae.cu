@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(256) vae_snake_kernel(const float * x, const f
             const int c = (int) ((i * 4) % C);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float s = sinf(y[e] * ea[c + e]);
+                const float s = __sinf(y[e] * ea[c + e]);
                 y[e] = y[e] + s * s * eb[c + e];
             }
         }
@@ -133,8 +133,8 @@ struct VaeModel {
     // per latent length
     int T = 0;
     size_t max_elems = 0;
-    float * lat = nullptr, * x = nullptr, * gb = nullptr, * audio = nullptr;
-    __half * lat16 = nullptr, * h = nullptr, * h2 = nullptr;
+    float * lat = nullptr, * x = nullptr, * audio = nullptr;
+    __half * lat16 = nullptr, * hA = nullptr, * hB = nullptr, * hC = nullptr;   // split operands, rotated
     std::vector<void *> bufs;
     std::vector<std::function<cudaError_t(cudaStream_t)>> ops;
     std::vector<std::string> op_names;
@@ -275,7 +275,8 @@ struct VaeModel {
     // one phase of a conv as a split-weight GEMM over `rows` input rows of the split operand A
     // ([rows][IC] hi, then lo): tile width and K slices by the cost model of the DiT planner
     int conv_op(const std::string & name, const VConv & cv, int ph, const __half * A, int rows, void * out, long long ldo,
-                int epi, const VSnake * snake, long long out_lo) {
+                int epi, const VSnake * snake, long long out_lo, void * out2 = nullptr, long long ldo2 = 0,
+                long long out2_lo = 0) {
         const int kb = cv.taps * cv.IC / 64, mtt = (rows + 127) / 128;
         double best = 1e30;
         int bn = 0, sp = 1;
@@ -310,8 +311,19 @@ struct VaeModel {
         a.err = dev->d_err;
         a.bias = cv.b;
         a.out = out; a.ldo = ldo; a.out_bs = 0; a.out_lo = out_lo;
+        a.out2 = out2; a.ldo2 = ldo2; a.out2_lo = out2_lo;
         a.m_fast = 1;
         if (snake) { a.snake_a = snake->ea; a.snake_b = snake->eb; }
+        // many waves of tiles: one persistent CTA per SM overlaps each tile's epilogue (the fused
+        // residual and snake passes) with the next tile's mainloop
+        const int tiles = mtt * (cv.Npad / bn);
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev->ordinal);
+        if (sp == 1 && tiles > 2 * sms) {
+            gl.persistent = true;
+            gl.smem = gemm_ws_persistent_smem_bytes(bn, epi);
+            gl.grid = dim3((unsigned) std::min(tiles, sms), 1, 1);
+        }
         ops.push_back([gl](cudaStream_t s) { return launch_gemm_ws(gl, s); });
         op_names.push_back(name);
         flops += 2.0 * rows * (double) cv.OC * cv.taps * cv.IC;
@@ -343,34 +355,35 @@ struct VaeModel {
         VRT(dalloc(&lat, (size_t) T_ * conv0.IC * 4, bufs));
         VRT(dalloc(&lat16, (size_t) T_ * conv0.IC * 2 * 2, bufs));
         VRT(dalloc(&x, max_elems * 4, bufs));
-        VRT(dalloc(&gb, max_elems * 4, bufs));
-        VRT(dalloc(&h, max_elems * 2 * 2, bufs));
-        VRT(dalloc(&h2, max_elems * 2 * 2, bufs));
+        VRT(dalloc(&hA, max_elems * 2 * 2, bufs));
+        VRT(dalloc(&hB, max_elems * 2 * 2, bufs));
+        VRT(dalloc(&hC, max_elems * 2 * 2, bufs));
         VRT(dalloc(&audio, (size_t) Ta * 32 * 4, bufs));
-        // VaeModel::decode, src/vae.cpp:57-81
+        // VaeModel::decode, src/vae.cpp:57-81. Every snake except the latent split is a GEMM
+        // epilogue: conv0 writes the first block's snake; each transposed conv writes x and the
+        // first unit's snake; each unit's dilated conv applies its inner snake, and its k1 conv adds
+        // the residual into x and writes the snake that follows (the next unit's, the next
+        // block's, or the final one). hC feeds transposed convs and the final conv, hA dilated
+        // convs, hB k1 convs, so no launch reads the buffer it writes.
         snake_op(lat, nullptr, nullptr, nullptr, lat16, T_, conv0.IC);
-        VRT(conv_op("conv0", conv0, 0, lat16, T_, x, conv0.OC, EPI_F32, nullptr, 0));
+        VRT(conv_op("conv0", conv0, 0, lat16, T_, hC, conv0.OC, EPI_F16_SNAKE, &s_in[0], (long long) T_ * conv0.OC));
         long long rows = T_;
         for (int n = 0; n < 5; ++n) {
-            const int s = (int) VAE_STRIDES[n], Cin = convT[n].IC, C = convT[n].OC;
-            // snake of the block input (the previous block's last residual add folded in)
-            snake_op(x, n ? gb : nullptr, nullptr, &s_in[n], h, rows, Cin);
+            const int s = (int) VAE_STRIDES[n], C = convT[n].OC;
+            const long long out_rows = rows * s;
             for (int ph = 0; ph < s; ++ph)
-                VRT(conv_op("convT" + std::to_string(n), convT[n], ph, h, (int) rows, x + (size_t) ph * C, (long long) s * C,
-                            EPI_F32, nullptr, 0));
-            rows *= s;
+                VRT(conv_op("convT" + std::to_string(n), convT[n], ph, hC, (int) rows, x + (size_t) ph * C, (long long) s * C,
+                            EPI_F32_SNAKE2, &s_a[n][0], 0, hA + (size_t) ph * C, (long long) s * C, out_rows * C));
+            rows = out_rows;
             for (int r = 0; r < 3; ++r) {
-                // x += g of the previous unit, then its snake; the dilated conv's epilogue applies the
-                // second snake; the k1 conv leaves g for the next add
-                snake_op(x, r ? gb : nullptr, r ? x : nullptr, &s_a[n][r], h, rows, C);
-                VRT(conv_op("res" + std::to_string(n) + std::to_string(r) + ".conv7", c7[n][r], 0, h, (int) rows, h2, C,
-                            EPI_F16_SNAKE, &s_b[n][r], rows * C));
-                VRT(conv_op("res" + std::to_string(n) + std::to_string(r) + ".conv1", c1[n][r], 0, h2, (int) rows, gb, C,
-                            EPI_F32, nullptr, 0));
+                const std::string nm = "res" + std::to_string(n) + std::to_string(r);
+                const VSnake * next = r < 2 ? &s_a[n][r + 1] : n < 4 ? &s_in[n + 1] : &s_fin;
+                __half * hn = r < 2 ? hA : hC;
+                VRT(conv_op(nm + ".conv7", c7[n][r], 0, hA, (int) rows, hB, C, EPI_F16_SNAKE, &s_b[n][r], rows * C));
+                VRT(conv_op(nm + ".conv1", c1[n][r], 0, hB, (int) rows, x, C, EPI_RESID_SNAKE, next, 0, hn, C, rows * C));
             }
         }
-        snake_op(x, gb, nullptr, &s_fin, h, rows, fin.IC);
-        VRT(conv_op("final", fin, 0, h, (int) rows, audio, 32, EPI_F32, nullptr, 0));
+        VRT(conv_op("final", fin, 0, hC, (int) rows, audio, 32, EPI_F32, nullptr, 0));
         T = T_;
         // capture
         cudaGraph_t graph = nullptr;
