@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--vae", action="store_true",
                     help="the VAE decoder after the sampler (src/vae.cpp): decode T latent frames, synthetic f32 weights")
     ap.add_argument("--vae-channels", type=int, default=128)
+    ap.add_argument("--encoders", action="store_true",
+                    help="the text encoders before the sampler (src/t5.cpp, src/clip.cpp) at full size, synthetic weights")
+    ap.add_argument("--encoder-layers", type=int, default=24)
     return ap.parse_args()
 
 
@@ -626,6 +629,83 @@ def run_vae(a):
     print(json.dumps(line), flush=True)
 
 
+def run_encoders(a):
+    """The two text encoders at full size (T5 v1.1 XL: d_model 2048, d_ff 5120, 32 heads, Q8_0 file;
+    MetaCLIP text: hidden 1024, 16 heads, f32 file; 24 layers each, 77 tokens): device time of each
+    encode graph, end-to-end time through tsn_encoder_encode with host buffers, the weight-streaming
+    rate against HBM, and the reference's own encodes (oracle/_ref over the scalar kernels). One
+    JSON line per encoder."""
+    import tempfile
+    import time
+
+    import numpy as np
+
+    import tsn
+
+    def t5_ids(seed, n):     # n ids, EOS (1), pad (0): the T5 tokenizer's layout
+        ids = np.zeros(77, np.int32)
+        ids[:n] = np.random.default_rng(seed).integers(2, 32000, n)
+        ids[n] = 1
+        return ids
+
+    def clip_ids(seed, n):   # BOS, n ids, EOS padding: the CLIP tokenizer's layout
+        ids = np.full(77, 49407, np.int32)
+        ids[0] = 49406
+        ids[1:1 + n] = np.random.default_rng(seed).integers(1, 49000, n)
+        return ids
+
+    hbm, _, _, peak_src = peaks()
+    dev = tsn.Device(0)
+    L = a.encoder_layers
+    for kind in ("t5", "clip"):
+        path = os.path.join(tempfile.gettempdir(), f"tsn_bench_{kind}_{L}_{a.seed}.gguf")
+        if not os.path.exists(path):
+            if kind == "t5":
+                tsn.write_synthetic_t5_gguf(path, d_model=2048, d_ff=5120, layers=L, heads=32, seed=a.seed)
+            else:
+                tsn.write_synthetic_clip_gguf(path, hidden=1024, layers=L, heads=16, seed=a.seed)
+        e = tsn.TextEncoder(dev, kind, path)
+        ids = t5_ids(a.seed, 40) if kind == "t5" else clip_ids(a.seed, 30)
+        for _ in range(max(a.warmup, 3)):
+            e.encode(ids)
+        dev_ms, wall = [], []
+        for _ in range(a.steps):
+            t0 = time.perf_counter()
+            e.encode(ids)
+            wall.append(time.perf_counter() - t0)
+            dev_ms.append(e.last_ms())
+        ms = max(dev_ms)
+        wb = e.weight_bytes()
+        line = {
+            "metric": f"{kind} encodes/s (77 tokens)", "value": 1000.0 / ms, "unit": "encodes/s", "n_gpus": 1,
+            "steps": a.steps, "warmup": max(a.warmup, 3), "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 split activations x " + ("f16 weights (Q8_0 file)" if kind == "t5" else "f16 split weights (f32 file)")
+                     + ", f32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": "T5Model::encode (src/t5.cpp)" if kind == "t5" else "ClipModel::encode (src/clip.cpp)",
+                       "width": e.width, "layers": e.layers, "tokens": e.ctx, "weights": "synthetic (seed %d)" % a.seed},
+            "roofline": {"bound": "hbm", "achieved": wb / (ms * 1e-3) / 1e9, "peak": hbm, "unit": "GB/s",
+                         "frac": wb / (ms * 1e-3) / 1e9 / hbm, "traffic": None,
+                         "algorithmic_bytes_per_step": wb, "peak_source": f"{peak_src} hbm_gbs",
+                         "note": "weights streamed once per encode (2 B per f16 weight, 4 B per split f32 weight); "
+                                 "77-row activations are negligible", "tflops": e.flops() / (ms * 1e-3) / 1e12},
+            "e2e": {"value": 1.0 / max(wall), "unit": "encodes/s", "h2d_bytes_per_step": ids.nbytes,
+                    "d2h_bytes_per_step": e.ctx * e.width * 4 + (e.width * 4 if kind == "clip" else 0)},
+            "gpu_launches": None,
+        }
+        if not a.no_cpu_baseline:
+            sys.path.insert(0, os.path.join(ROOT, "oracle"))
+            import oracle as O
+            if O.have_ref():
+                _, _, js = O.ref_encoder(kind, path, ids)
+                sec = min(js["seconds"])
+                line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "encodes/s", "cores": js["threads"],
+                                        "kind": "reference", "sample": "one full encode of the reference build"}
+        e.close()
+        print(json.dumps(line), flush=True)
+
+
 def write_vae_fixture(a):
     import tempfile
 
@@ -641,6 +721,8 @@ def main():
     apply_long(a)
     if a.vae:
         run_vae(a)
+    elif a.encoders:
+        run_encoders(a)
     elif a.impl == "reference":
         run_reference(a)
     elif a.cfg_split:

@@ -236,6 +236,33 @@ int tsn_vae_profile_ops(tsn_vae * v, char * out, size_t cap);
 double tsn_vae_flops(tsn_vae * v);
 int tsn_vae_free(tsn_vae * v);
 
+/* ------------------------------------------------------------------ text encoders */
+/* T5Model (src/t5.cpp, src/models.h:40-52) and ClipModel (src/clip.cpp, src/models.h:24-38) on the
+ * GPU, one handle type for both. Loading follows WeightSet::load with keep_f32 (src/net.mm:126-173):
+ * f32 tensors stay f32 (split-weight GEMMs), others (the T5 file's Q8_0) become f16 by the
+ * reference's rounding rule. Returns TSN_ERR_UNSUPPORTED unless the head size is 64. */
+typedef struct tsn_encoder tsn_encoder;
+/* Replaces T5Model::load (src/t5.cpp:22-59): KV keys t5.* with the reference's defaults. */
+int tsn_t5_load(tsn_device * dev, const char * gguf_path, tsn_encoder ** out);
+/* Replaces ClipModel::load (src/clip.cpp:6-28): KV keys clip.*. */
+int tsn_clip_load(tsn_device * dev, const char * gguf_path, tsn_encoder ** out);
+/* Width (d_model / hidden), context (77) and layer count. */
+int tsn_encoder_info(tsn_encoder * e, uint32_t * width, uint32_t * ctx, uint32_t * layers);
+/* Replaces T5Model::encode (src/t5.cpp:84-131) and ClipModel::encode (src/clip.cpp:30-101): n_ids
+ * must equal ctx (ids already padded, as the tokenizers return them); every id must lie inside the
+ * vocabulary (TSN_ERR_ARG otherwise; the reference would read past its table). per_token [ctx, width]
+ * f32; pooled [width] (CLIP's text_proj of the EOT row; ignored for T5, may be null). Host or device
+ * pointers. One CUDA graph per encoder. */
+int tsn_encoder_encode(tsn_encoder * e, const int32_t * ids, uint32_t n_ids, float * per_token, size_t per_token_cap,
+                       float * pooled, size_t pooled_cap);
+/* Device time of the last encode (ms), its algorithmic FLOPs and the weight bytes it streams. */
+double tsn_encoder_last_ms(tsn_encoder * e);
+double tsn_encoder_flops(tsn_encoder * e);
+double tsn_encoder_weight_bytes(tsn_encoder * e);
+/* The encode's launches once more eagerly, one line per launch (name, device ms). */
+int tsn_encoder_profile_ops(tsn_encoder * e, char * out, size_t cap);
+int tsn_encoder_free(tsn_encoder * e);
+
 /* ------------------------------------------------------------------ fixtures */
 /* Write the seeded synthetic DiT GGUF (with_prep adds the conditioning-prep tensors). Host only. */
 int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t seed, int with_prep);
@@ -244,6 +271,13 @@ int tsn_gguf_write_synthetic(const char * path, const tsn_dit_geom * g, uint64_t
  * to out_channels; tensor names of src/vae.cpp). Host only. */
 int tsn_gguf_write_synthetic_vae(const char * path, uint32_t latent_dim, uint32_t channels, uint32_t out_channels,
                                  uint64_t seed);
+/* Write the seeded synthetic T5 encoder GGUF (Q8_0 matrices and embedding, f32 norms and relative
+ * bias; tensor names and KV keys of src/t5.cpp; vocabulary 32128). Host only. */
+int tsn_gguf_write_synthetic_t5(const char * path, uint32_t d_model, uint32_t d_ff, uint32_t layers, uint32_t heads,
+                                uint64_t seed);
+/* Write the seeded synthetic MetaCLIP text encoder GGUF (f32; names and keys of src/clip.cpp;
+ * vocabulary 49408, context 77). Host only. */
+int tsn_gguf_write_synthetic_clip(const char * path, uint32_t hidden, uint32_t layers, uint32_t heads, uint64_t seed);
 
 #ifdef __cplusplus
 }

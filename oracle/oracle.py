@@ -203,3 +203,114 @@ def vae_decode_np(W, latent):
     h = _snake_np(x, W("decoder.layers.6.alpha"), W("decoder.layers.6.beta"))
     return _conv1d_np(h, W("decoder.layers.7.weight"), None, pad=3)
 
+
+
+# ------------------------------------------------ text encoders (src/t5.cpp, src/clip.cpp)
+def ref_encoder(kind: str, gguf: str, ids: np.ndarray, threads=None, reps=1, workdir=None):
+    """T5Model::encode (kind "t5", src/t5.cpp:84-131) or ClipModel::encode ("clip",
+    src/clip.cpp:30-101) of the reference build on 77 int32 ids. Returns (per_token [77, width],
+    pooled [width] or None, timing JSON)."""
+    import tempfile
+    d = workdir or tempfile.mkdtemp(prefix="tsn_enc_")
+    os.makedirs(d, exist_ok=True)
+    np.ascontiguousarray(ids, np.int32).tofile(os.path.join(d, "ids.bin"))
+    js = parse_json_line(run_ref(kind, gguf, 0, 0, 0, d, d, reps, threads=threads))
+    if kind == "t5":
+        return np.fromfile(os.path.join(d, "out.bin"), np.float32).reshape(77, -1), None, js
+    pt = np.fromfile(os.path.join(d, "per_token.bin"), np.float32)
+    g = np.fromfile(os.path.join(d, "global.bin"), np.float32)
+    return pt.reshape(-1, g.size), g, js
+
+
+def t5_bucket(rel: int, num_buckets: int, max_dist: int) -> int:
+    """T5's bidirectional relative-position bucket (src/t5.cpp:7-20)."""
+    ret = 0
+    num_buckets //= 2
+    if rel > 0:
+        ret += num_buckets
+    n = abs(rel)
+    max_exact = num_buckets // 2
+    if n < max_exact:
+        return ret + n
+    v = max_exact + int(np.log(n / max_exact) / np.log(max_dist / max_exact) * (num_buckets - max_exact))
+    return ret + min(v, num_buckets - 1)
+
+
+def _softmax_rows(s):
+    m = s.max(axis=-1, keepdims=True)
+    e = np.exp(s - m)
+    return e / e.sum(axis=-1, keepdims=True)
+
+
+def _heads_attention(q, k, v, nh, scale, bias):
+    """softmax(scale q kᵀ + bias) v per head (attn_qk / softmax_rows / attn_pav,
+    shaders/gemm_attn.metal:96-202); bias [nh, n, n] with -inf for masked keys."""
+    n, d = q.shape
+    hd = d // nh
+    out = np.zeros_like(q)
+    for h in range(nh):
+        sl = slice(h * hd, (h + 1) * hd)
+        s = scale * (q[:, sl] @ k[:, sl].T) + bias[h]
+        out[:, sl] = _softmax_rows(s) @ v[:, sl]
+    return out
+
+
+def t5_encode_np(W, kv: dict, ids: np.ndarray) -> np.ndarray:
+    """Float64 restatement of T5Model::encode (src/t5.cpp:84-131). W(name) gives a tensor as the
+    reference's device holds it (matrices [N, K], vectors [n]), W(name, host=True) the to_f32 values
+    of its host copies (the embedding table); kv the GGUF's t5.* keys."""
+    d, nh, L = kv["t5.d_model"], kv["t5.n_heads"], kv["t5.n_layers"]
+    nb, md = kv.get("t5.rel_buckets", 32), kv.get("t5.rel_max_dist", 128)
+    eps = kv.get("t5.eps", 1e-6)
+    n = ids.size
+    x = W("tok_emb", host=True).reshape(-1, d)[ids].astype(np.float64)   # host gather of to_f32 values
+    rb = W("rel_bias").reshape(nb, nh)
+    bk = np.array([[t5_bucket(k - q, nb, md) for k in range(n)] for q in range(n)])
+    bias = np.transpose(rb[bk], (2, 0, 1)).copy()             # [nh, q, k]
+    bias[:, :, ids == 0] = -np.inf                           # pad keys (pad_on)
+
+    def rms(v, w):
+        return v / np.sqrt((v * v).mean(axis=1, keepdims=True) + eps) * w
+
+    def gelu_tanh(a):
+        arg = 0.7978845608 * (a + 0.044715 * a ** 3)
+        return 0.5 * a * (1.0 + np.tanh(np.clip(arg, -10.0, 10.0)))
+
+    for l in range(L):
+        bp = f"blk.{l}"
+        r = rms(x, W(bp + ".attn_norm"))
+        q, k, v = r @ W(bp + ".q").T, r @ W(bp + ".k").T, r @ W(bp + ".v").T
+        x = x + _heads_attention(q, k, v, nh, 1.0, bias) @ W(bp + ".o").T
+        r = rms(x, W(bp + ".ffn_norm"))
+        x = x + (gelu_tanh(r @ W(bp + ".wi_0").T) * (r @ W(bp + ".wi_1").T)) @ W(bp + ".wo").T
+    return rms(x, W("out_norm"))
+
+
+def clip_encode_np(W, kv: dict, ids: np.ndarray):
+    """Float64 restatement of ClipModel::encode (src/clip.cpp:30-101): (per_token [n, H], pooled [H])."""
+    H, nh, L = kv["clip.hidden"], kv["clip.heads"], kv["clip.layers"]
+    n = ids.size
+    x = W("tok_emb", host=True).reshape(-1, H)[ids] + W("pos_emb", host=True).reshape(-1, H)[:n]
+    eot = int(np.argmax(ids))                                 # first position of the largest id
+    q_i, k_i = np.meshgrid(np.arange(n), np.arange(n), indexing="ij")
+    bias = np.where((k_i <= q_i) & (k_i <= eot), 0.0, -np.inf)[None].repeat(nh, axis=0)
+
+    def ln(v, w, b):
+        m = v.mean(axis=1, keepdims=True)
+        var = ((v - m) ** 2).mean(axis=1, keepdims=True)
+        return (v - m) / np.sqrt(var + 1e-5) * w + b
+
+    for l in range(L):
+        bp = f"blk.{l}"
+        r = ln(x, W(bp + ".ln1.w"), W(bp + ".ln1.b"))
+        q = r @ W(bp + ".q.w").T + W(bp + ".q.b")
+        k = r @ W(bp + ".k.w").T + W(bp + ".k.b")
+        v = r @ W(bp + ".v.w").T + W(bp + ".v.b")
+        a = _heads_attention(q, k, v, nh, 1.0 / np.sqrt(H // nh), bias)
+        x = x + a @ W(bp + ".out.w").T + W(bp + ".out.b")
+        r = ln(x, W(bp + ".ln2.w"), W(bp + ".ln2.b"))
+        hdn = r @ W(bp + ".fc1.w").T + W(bp + ".fc1.b")
+        hdn = hdn / (1.0 + np.exp(-1.702 * hdn))
+        x = x + hdn @ W(bp + ".fc2.w").T + W(bp + ".fc2.b")
+    pt = ln(x, W("out_ln.w"), W("out_ln.b"))
+    return pt, W("text_proj").reshape(H, H) @ pt[eot]

@@ -17,6 +17,11 @@
 //   ts_ref_dit vae <vae_gguf> <T> 0 0 <in_dir> <out_dir> [reps]
 //       VaeModel::decode (src/vae.cpp:17-86) of latent.bin [T,64]; writes audio.bin
 //       [T_audio,2] (interleaved stereo) and prints a JSON timing line.
+//   ts_ref_dit t5 <t5_gguf> 0 0 0 <in_dir> <out_dir> [reps]
+//       T5Model::encode (src/t5.cpp:84-131) of ids.bin (int32 [77]); writes out.bin [77,d_model].
+//   ts_ref_dit clip <clip_gguf> 0 0 0 <in_dir> <out_dir> [reps]
+//       ClipModel::encode (src/clip.cpp:30-101) of ids.bin (int32 [77]); writes per_token.bin
+//       [77,H] and global.bin [H].
 //
 // Inputs in <in_dir> (f32, row-major): x.bin [T,64], clip_pp.bin [C,H], sync_gather.bin [T,H],
 // text_pp_cond.bin / text_pp_unc.bin [TS,H], gcmlp_cond.bin / gcmlp_unc.bin [H].
@@ -118,6 +123,48 @@ int main(int argc, char ** argv) {
         }
         printf("], \"T_audio\": %u}\n", Ta);
         write_from(out + "/audio.bin", audio.data(), audio.size());
+        return 0;
+    }
+    if (mode == "t5" || mode == "clip") {
+        std::vector<int32_t> ids(77);
+        {
+            FILE * f = fopen((in + "/ids.bin").c_str(), "rb");
+            if (!f || fread(ids.data(), 4, ids.size(), f) != ids.size()) { fprintf(stderr, "missing ids.bin\n"); return 1; }
+            fclose(f);
+        }
+        const int reps = argc > 8 ? atoi(argv[8]) : 1;
+        int threads = 1;
+#ifdef _OPENMP
+        threads = omp_get_max_threads();
+#endif
+        std::vector<double> secs;
+        if (mode == "t5") {
+            T5Model t5;
+            if (!t5.load(rt, gguf)) { fprintf(stderr, "t5 load failed\n"); return 1; }
+            gpu::Buf o = rt.dev.alloc((size_t) 77 * t5.d_model * 4);
+            for (int r = 0; r < reps; ++r) {
+                const auto t0 = std::chrono::steady_clock::now();
+                t5.encode(rt, ids, o);
+                rt.dev.commit();
+                secs.push_back(std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+            }
+            write_from(out + "/out.bin", o.p, (size_t) 77 * t5.d_model);
+        } else {
+            ClipModel clip;
+            if (!clip.load(rt, gguf)) { fprintf(stderr, "clip load failed\n"); return 1; }
+            gpu::Buf pt = rt.dev.alloc((size_t) clip.ctx * clip.H * 4), gl = rt.dev.alloc((size_t) clip.H * 4);
+            for (int r = 0; r < reps; ++r) {
+                const auto t0 = std::chrono::steady_clock::now();
+                clip.encode(rt, ids, pt, gl);
+                rt.dev.commit();
+                secs.push_back(std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+            }
+            write_from(out + "/per_token.bin", pt.p, (size_t) clip.ctx * clip.H);
+            write_from(out + "/global.bin", gl.p, clip.H);
+        }
+        printf("{\"mode\": \"%s\", \"threads\": %d, \"seconds\": [", mode.c_str(), threads);
+        for (size_t i = 0; i < secs.size(); ++i) printf("%s%.6f", i ? ", " : "", secs[i]);
+        printf("]}\n");
         return 0;
     }
     DitModel dit;

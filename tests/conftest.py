@@ -28,6 +28,27 @@ WIDE_SEQ = dict(T=188, C=64, TS=77)
 SEED = 4242
 
 
+# Text encoder fixtures (tests/golden/small_t5.npz, small_clip.npz).
+T5_SMALL = dict(d_model=256, d_ff=512, layers=2, heads=4)
+CLIP_SMALL = dict(hidden=256, layers=2, heads=4)
+
+
+def t5_ids(seed, n_tok=31):
+    """n_tok seeded token ids, EOS (1), pad (0) to 77: the T5 tokenizer's layout."""
+    ids = np.zeros(77, np.int32)
+    ids[:n_tok] = np.random.default_rng(seed).integers(2, 32000, n_tok)
+    ids[n_tok] = 1
+    return ids
+
+
+def clip_ids(seed, n_tok=20):
+    """BOS (49406), n_tok seeded ids, EOS (49407) padding to 77: the CLIP tokenizer's layout."""
+    ids = np.full(77, 49407, np.int32)
+    ids[0] = 49406
+    ids[1:1 + n_tok] = np.random.default_rng(seed).integers(1, 49000, n_tok)
+    return ids
+
+
 def make_geom(H, NH, F, depth, fused_depth):
     return tsn.geom(H=H, NH=NH, F=F, depth=depth, fused_depth=fused_depth)
 

@@ -9,8 +9,14 @@ tiny_forward.npz  one DitModel::forward (src/dit_fwd.cpp:104-304) of the cond ar
 tiny_sample.npz   4 Euler steps of the sampler loop (src/pipeline.cpp:142-155), CFG 5.0.
 small_vae.npz     VaeModel::decode (src/vae.cpp:17-86) of a seeded latent [3, 64] on the synthetic
                   VAE with 64 base channels (widths 1024 ... 64), audio [6144, 2].
-The weights are regenerated bit-exactly by tsn.write_synthetic_gguf / write_synthetic_vae_gguf
-(seed 4242). `python tests/golden/make_golden.py vae` writes only the VAE fixture.
+small_t5.npz      T5Model::encode (src/t5.cpp:84-131) of seeded ids (31 tokens + EOS, then pad) on
+                  the synthetic Q8_0 T5 (d_model 256, d_ff 512, 2 layers, 4 heads): out [77, 256].
+small_clip.npz    ClipModel::encode (src/clip.cpp:30-101) of seeded ids (BOS, 20 tokens, EOS padded)
+                  on the synthetic f32 MetaCLIP text model (hidden 256, 2 layers, 4 heads):
+                  per_token [77, 256], pooled [256].
+The weights are regenerated bit-exactly by tsn.write_synthetic_gguf / write_synthetic_vae_gguf /
+write_synthetic_t5_gguf / write_synthetic_clip_gguf (seed 4242). `python tests/golden/make_golden.py
+vae` (or `encoders`) writes only those fixtures.
 """
 import hashlib
 import os
@@ -21,7 +27,7 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
-from conftest import SEED, TINY, TINY_SEQ, make_geom, make_inputs  # noqa: E402
+from conftest import CLIP_SMALL, SEED, T5_SMALL, TINY, TINY_SEQ, clip_ids, make_geom, make_inputs, t5_ids  # noqa: E402
 
 import oracle as O  # noqa: E402
 import tsn  # noqa: E402
@@ -44,9 +50,30 @@ def make_vae(d):
                         gguf_sha256=sha)
 
 
+def make_encoders(d):
+    g = os.path.join(d, "t5.gguf")
+    tsn.write_synthetic_t5_gguf(g, seed=SEED, **T5_SMALL)
+    sha = hashlib.sha256(open(g, "rb").read()).hexdigest()
+    ids = t5_ids(SEED)
+    out, _, _ = O.ref_encoder("t5", g, ids, workdir=os.path.join(d, "t5"))
+    np.savez_compressed(os.path.join(HERE, "small_t5.npz"), ids=ids, out=out, gguf_sha256=sha, **T5_SMALL)
+    g = os.path.join(d, "clip.gguf")
+    tsn.write_synthetic_clip_gguf(g, seed=SEED, **CLIP_SMALL)
+    sha = hashlib.sha256(open(g, "rb").read()).hexdigest()
+    ids = clip_ids(SEED)
+    pt, pooled, _ = O.ref_encoder("clip", g, ids, workdir=os.path.join(d, "clip"))
+    np.savez_compressed(os.path.join(HERE, "small_clip.npz"), ids=ids, per_token=pt, pooled=pooled, gguf_sha256=sha,
+                        **CLIP_SMALL)
+
+
 def main():
     if not O.have_ref():
         raise SystemExit("oracle/_ref/ts_ref_dit not built (needs the reference tree)")
+    if sys.argv[1:] == ["encoders"]:
+        with tempfile.TemporaryDirectory() as d:
+            make_encoders(d)
+        print("wrote small_t5.npz, small_clip.npz")
+        return
     if sys.argv[1:] == ["vae"]:
         with tempfile.TemporaryDirectory() as d:
             make_vae(d)
@@ -75,6 +102,7 @@ def main():
         out.update(T=T, C=C, TS=TS, steps=steps, cfg=np.float32(cfg), x_final=xf, gguf_sha256=sha)
         np.savez_compressed(os.path.join(HERE, "tiny_sample.npz"), **out)
         make_vae(d)
+        make_encoders(d)
     print("wrote", os.listdir(HERE))
 
 

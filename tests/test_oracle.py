@@ -13,8 +13,9 @@ import os
 import numpy as np
 import pytest
 
+import gguf_read
 import oracle as O
-from conftest import SEED, TINY, TINY_SEQ, make_geom, make_inputs, rel_l2
+from conftest import CLIP_SMALL, SEED, T5_SMALL, TINY, TINY_SEQ, clip_ids, make_geom, make_inputs, rel_l2, t5_ids
 
 import tsn
 
@@ -215,3 +216,83 @@ def test_vae_reference_build_matches_restatement(vae_gguf, tmp_path):
     audio, js = O.ref_vae(vae_gguf, lat, workdir=str(tmp_path))
     assert js["T_audio"] == 2 * 2048
     assert rel_l2(O.vae_decode_np(_vae_weights(vae_gguf), lat), audio) < 1e-5
+
+
+# ---------------------------------------------------------------- text encoders
+
+
+@pytest.fixture(scope="module")
+def t5_gguf(tmp_path_factory):
+    p = str(tmp_path_factory.mktemp("t5") / "t5.gguf")
+    tsn.write_synthetic_t5_gguf(p, seed=SEED, **T5_SMALL)
+    yield p
+    os.unlink(p)
+
+
+@pytest.fixture(scope="module")
+def clip_gguf(tmp_path_factory):
+    p = str(tmp_path_factory.mktemp("clip") / "clip.gguf")
+    tsn.write_synthetic_clip_gguf(p, seed=SEED, **CLIP_SMALL)
+    yield p
+    os.unlink(p)
+
+
+def test_t5_bucket_known_values():
+    """src/t5.cpp:7-20 at 32 buckets, max distance 128: exact below 8, logarithmic to 127, clamped."""
+    b = lambda r: O.t5_bucket(r, 32, 128)  # noqa: E731
+    assert [b(0), b(1), b(-1), b(7), b(-7)] == [0, 17, 1, 23, 7]
+    assert b(8) == 24 and b(-8) == 8
+    assert b(200) == 31 and b(-200) == 15 and b(127) == 31
+
+
+def test_encoder_synthetic_gguf_bytes_pinned(t5_gguf, clip_gguf):
+    for path, name in ((t5_gguf, "small_t5.npz"), (clip_gguf, "small_clip.npz")):
+        g = np.load(os.path.join(GOLDEN, name))
+        assert hashlib.sha256(open(path, "rb").read()).hexdigest() == str(g["gguf_sha256"])
+
+
+def test_q8_0_blocks_follow_the_synthetic_values(t5_gguf):
+    """The writer's Q8_0 blocks decode (to_f32, src/gguf.cpp:216-228) to the seeded normal values
+    within half a quantisation step, and every block's largest value maps to +-127."""
+    b, kv, tensors, data = gguf_read.read_header(t5_gguf)
+    v, ty = gguf_read.tensor_f32(b, tensors, data, "blk.0.q")
+    assert ty == 8
+    blk = np.frombuffer(b, np.uint8, v.size // 32 * 34, data + tensors["blk.0.q"][2]).reshape(-1, 34)
+    q = blk[:, 2:].view(np.int8)
+    assert np.all(np.abs(q).max(axis=1) == 127)
+    assert np.all(np.abs(v) <= 127 * gguf_read._f16_flush(blk[:, :2].copy().view(np.uint16)[:, 0]).max() * 1.001)
+
+
+def test_t5_restatement_reproduces_golden(t5_gguf):
+    g = np.load(os.path.join(GOLDEN, "small_t5.npz"))
+    W, kv = gguf_read.device_weights(t5_gguf)
+    assert rel_l2(O.t5_encode_np(W, kv, g["ids"]), g["out"]) < 1e-5
+
+
+def test_clip_restatement_reproduces_golden(clip_gguf):
+    g = np.load(os.path.join(GOLDEN, "small_clip.npz"))
+    W, kv = gguf_read.device_weights(clip_gguf)
+    pt, pooled = O.clip_encode_np(W, kv, g["ids"])
+    assert rel_l2(pt, g["per_token"]) < 1e-5
+    assert rel_l2(pooled, g["pooled"]) < 1e-5
+
+
+@needs_ref
+@pytest.mark.parametrize("n_tok", [1, 76])
+def test_t5_reference_build_matches_restatement(t5_gguf, tmp_path, n_tok):
+    """Edge cases of the pad mask: a single token + EOS (75 pad keys), and no padding at all."""
+    ids = t5_ids(SEED + n_tok, n_tok)
+    out, _, _ = O.ref_encoder("t5", t5_gguf, ids, workdir=str(tmp_path))
+    W, kv = gguf_read.device_weights(t5_gguf)
+    assert rel_l2(O.t5_encode_np(W, kv, ids), out) < 1e-5
+
+
+@needs_ref
+@pytest.mark.parametrize("n_tok", [0, 75])
+def test_clip_reference_build_matches_restatement(clip_gguf, tmp_path, n_tok):
+    """EOT at position 1 (empty caption) and at the last position (a full context)."""
+    ids = clip_ids(SEED + n_tok, n_tok)
+    pt, pooled, _ = O.ref_encoder("clip", clip_gguf, ids, workdir=str(tmp_path))
+    W, kv = gguf_read.device_weights(clip_gguf)
+    p2, g2 = O.clip_encode_np(W, kv, ids)
+    assert rel_l2(p2, pt) < 1e-5 and rel_l2(g2, pooled) < 1e-5

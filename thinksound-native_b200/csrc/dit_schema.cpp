@@ -139,4 +139,59 @@ std::vector<TensorSpec> vae_schema(const VaeGeom & v) {
     return out;
 }
 
+namespace {
+TensorSpec spec(const std::string & n, uint64_t ne0, uint64_t ne1, uint32_t type, int init, float scale) {
+    TensorSpec t; t.name = n; t.n_dims = ne1 ? 2 : 1; t.ne[0] = ne0; t.ne[1] = ne1 ? ne1 : 1;
+    t.type = type; t.init = init; t.scale = scale;
+    return t;
+}
+float fan_in(uint64_t n) { return 1.0f / std::sqrt((float) n); }
+} // namespace
+
+// Scales give unit-variance projections of unit-RMS inputs, so attention is neither uniform nor
+// one-hot at any width; norm gains 1 + 0.1 N(0,1).
+std::vector<TensorSpec> t5_schema(const T5Geom & g) {
+    std::vector<TensorSpec> v;
+    const uint64_t d = g.d_model, f = g.d_ff;
+    v.push_back(spec("tok_emb", d, T5_VOCAB, GG_Q8_0, TSN_INIT_NORMAL, 1.0f));            // src/t5.cpp:55
+    for (uint32_t l = 0; l < g.layers; ++l) {                                             // src/t5.cpp:104-127
+        const std::string bp = "blk." + std::to_string(l);
+        v.push_back(spec(bp + ".attn_norm", d, 0, GG_F32, TSN_INIT_ONE_PLUS, 0.1f));
+        for (const char * m : {".q", ".k", ".v", ".o"}) v.push_back(spec(bp + m, d, d, GG_Q8_0, TSN_INIT_NORMAL, fan_in(d)));
+        v.push_back(spec(bp + ".ffn_norm", d, 0, GG_F32, TSN_INIT_ONE_PLUS, 0.1f));
+        v.push_back(spec(bp + ".wi_0", d, f, GG_Q8_0, TSN_INIT_NORMAL, fan_in(d)));
+        v.push_back(spec(bp + ".wi_1", d, f, GG_Q8_0, TSN_INIT_NORMAL, fan_in(d)));
+        v.push_back(spec(bp + ".wo", f, d, GG_Q8_0, TSN_INIT_NORMAL, fan_in(f)));
+    }
+    v.push_back(spec("out_norm", d, 0, GG_F32, TSN_INIT_ONE_PLUS, 0.1f));                 // src/t5.cpp:129
+    v.push_back(spec("rel_bias", g.heads, g.rel_buckets, GG_F32, TSN_INIT_NORMAL, 1.0f));  // src/t5.cpp:74
+    return v;
+}
+
+std::vector<TensorSpec> clip_schema(const ClipGeom & g) {
+    std::vector<TensorSpec> v;
+    const uint64_t H = g.hidden;
+    v.push_back(spec("tok_emb", H, CLIP_VOCAB, GG_F32, TSN_INIT_NORMAL, 0.5f));          // src/clip.cpp:25-26
+    v.push_back(spec("pos_emb", H, g.ctx, GG_F32, TSN_INIT_NORMAL, 0.1f));
+    for (uint32_t l = 0; l < g.layers; ++l) {                                             // src/clip.cpp:50-94
+        const std::string bp = "blk." + std::to_string(l);
+        auto ln = [&](const std::string & n) {
+            v.push_back(spec(bp + n + ".w", H, 0, GG_F32, TSN_INIT_ONE_PLUS, 0.1f));
+            v.push_back(spec(bp + n + ".b", H, 0, GG_F32, TSN_INIT_NORMAL, 0.02f));
+        };
+        auto lin = [&](const std::string & n, uint64_t in, uint64_t out) {
+            v.push_back(spec(bp + n + ".w", in, out, GG_F32, TSN_INIT_NORMAL, fan_in(in)));
+            v.push_back(spec(bp + n + ".b", out, 0, GG_F32, TSN_INIT_NORMAL, 0.02f));
+        };
+        ln(".ln1");
+        lin(".q", H, H); lin(".k", H, H); lin(".v", H, H); lin(".out", H, H);
+        ln(".ln2");
+        lin(".fc1", H, 4 * H); lin(".fc2", 4 * H, H);
+    }
+    v.push_back(spec("out_ln.w", H, 0, GG_F32, TSN_INIT_ONE_PLUS, 0.1f));                // src/clip.cpp:117-120
+    v.push_back(spec("out_ln.b", H, 0, GG_F32, TSN_INIT_NORMAL, 0.02f));
+    v.push_back(spec("text_proj", H, H, GG_F32, TSN_INIT_NORMAL, fan_in(H)));
+    return v;
+}
+
 } // namespace tsn

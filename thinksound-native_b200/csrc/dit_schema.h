@@ -19,7 +19,7 @@ struct DitGeom {
     uint32_t hd() const { return H / NH; }
 };
 
-enum : uint32_t { GG_F32 = 0, GG_F16 = 1, GG_BF16 = 30 };
+enum : uint32_t { GG_F32 = 0, GG_F16 = 1, GG_Q8_0 = 8, GG_BF16 = 30 };
 
 struct TensorSpec {
     std::string name;
@@ -51,5 +51,25 @@ inline uint32_t vae_width(const VaeGeom & v, int i) {   // channels after conv0 
     return v.channels * mult[i];
 }
 std::vector<TensorSpec> vae_schema(const VaeGeom & v);
+
+// The T5 v1.1 text encoder (T5Model, src/t5.cpp:22-131): token embedding [32128, d_model], per
+// layer RMSNorm gains, q/k/v/o [d,d], gated-GELU FFN wi_0/wi_1 [d_ff,d] and wo [d,d_ff], the
+// relative-position bias table [n_bucket][NH] and the final RMSNorm. The reference's file is
+// Q8_0 ("t5-q8.gguf", src/pipeline.cpp:62): matrices and the embedding are Q8_0 here too, norm
+// gains and the bias table f32 (the bias is read as f32 by attn_qk, shaders/gemm_attn.metal:133-136).
+struct T5Geom {
+    uint32_t d_model = 2048, d_ff = 5120, layers = 24, heads = 32, rel_buckets = 32, rel_max_dist = 128;
+};
+constexpr uint32_t T5_VOCAB = 32128, T5_CTX = 77;
+std::vector<TensorSpec> t5_schema(const T5Geom & g);
+
+// The MetaCLIP text encoder (ClipModel, src/clip.cpp:6-123): token [49408, H] and position
+// [ctx, H] embeddings, per layer LayerNorms, biased q/k/v/out [H,H], fc1 [4H,H], fc2 [H,4H], the
+// final LayerNorm and the pooled projection text_proj [H,H]. All f32 ("metaclip-text-f32.gguf").
+struct ClipGeom {
+    uint32_t hidden = 1024, layers = 24, heads = 16, ctx = 77;
+};
+constexpr uint32_t CLIP_VOCAB = 49408;
+std::vector<TensorSpec> clip_schema(const ClipGeom & g);
 
 } // namespace tsn

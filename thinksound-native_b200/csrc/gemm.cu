@@ -91,6 +91,7 @@ size_t smem_of(int epi) {
         case EPI_F16_SILU: return smem_total<BN, SPLIT, EPI_F16_SILU>();
         case EPI_SWIGLU: return smem_total<BN, SPLIT, EPI_SWIGLU>();
         case EPI_QKV: return smem_total<BN, SPLIT, EPI_QKV>();
+        case EPI_GEGLU: return smem_total<BN, SPLIT, EPI_GEGLU>();
     }
     return 0;
 }
@@ -190,6 +191,7 @@ KernelFn pick_epi(int epi) {
         case EPI_F16_SILU: return pick<BN, EPI_F16_SILU, SPLIT>();
         case EPI_SWIGLU: return pick<BN, EPI_SWIGLU, SPLIT>();
         case EPI_QKV: return pick<BN, EPI_QKV, SPLIT>();
+        case EPI_GEGLU: return pick<BN, EPI_GEGLU, SPLIT>();
     }
     return nullptr;
 }
@@ -245,6 +247,8 @@ KernelWsFn ws_epi(int epi) {
         case EPI_F16_SNAKE: return pick_ws<BN, EPI_F16_SNAKE>();
         case EPI_RESID_SNAKE: return pick_ws<BN, EPI_RESID_SNAKE>();
         case EPI_F32_SNAKE2: return pick_ws<BN, EPI_F32_SNAKE2>();
+        case EPI_QKV: return pick_ws<BN, EPI_QKV>();
+        case EPI_F16_GELUQ: return pick_ws<BN, EPI_F16_GELUQ>();
     }
     return nullptr;
 }
@@ -266,6 +270,8 @@ size_t ws_smem_of(int epi) {
         case EPI_F16_SNAKE: return GemmSmem<BN, stages_ws(BN), true, EPI_F16_SNAKE, true>::TOTAL;
         case EPI_RESID_SNAKE: return GemmSmem<BN, stages_ws(BN), true, EPI_RESID_SNAKE, true>::TOTAL;
         case EPI_F32_SNAKE2: return GemmSmem<BN, stages_ws(BN), true, EPI_F32_SNAKE2, true>::TOTAL;
+        case EPI_QKV: return GemmSmem<BN, stages_ws(BN), true, EPI_QKV, true>::TOTAL;
+        case EPI_F16_GELUQ: return GemmSmem<BN, stages_ws(BN), true, EPI_F16_GELUQ, true>::TOTAL;
     }
     return 0;
 }
@@ -371,7 +377,7 @@ cudaError_t launch_gemm_ws(const GemmLaunch & g, cudaStream_t s) {
 cudaError_t configure_gemm_kernels() {
     for (int split = 0; split < 2; ++split)
         for (int bn : {64, 128, 192, 256})
-            for (int epi = 0; epi < 6; ++epi) {
+            for (int epi = 0; epi <= EPI_F16_GELUQ; ++epi) {
                 KernelFn fn = kernel_for(bn, epi, split != 0);
                 if (!fn) continue;
                 cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -388,10 +394,11 @@ cudaError_t configure_gemm_kernels() {
                 if (e != cudaSuccess) return e;
             }
     for (int bn : {64, 128, 256})
-        for (int epi : {(int) EPI_F32, (int) EPI_F16_SNAKE, (int) EPI_RESID_SNAKE, (int) EPI_F32_SNAKE2}) {
+        for (int epi : {(int) EPI_F32, (int) EPI_F16_SNAKE, (int) EPI_RESID_SNAKE, (int) EPI_F32_SNAKE2, (int) EPI_QKV,
+                        (int) EPI_F16_GELUQ}) {
             cudaError_t e = cudaFuncSetAttribute((const void *) ws_for(bn, epi), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int) gemm_ws_smem_bytes(bn, epi));
-            if (e == cudaSuccess)
+            if (e == cudaSuccess && wsp_for(bn, epi))
                 e = cudaFuncSetAttribute((const void *) wsp_for(bn, epi), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int) gemm_ws_persistent_smem_bytes(bn, epi));
             if (e != cudaSuccess) return e;

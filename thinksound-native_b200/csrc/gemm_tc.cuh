@@ -44,6 +44,8 @@ enum GemmEpi : int {
                        // hardware __sinf: a few 1e-6 absolute, far below the f16 rounding of the output)
     EPI_RESID_SNAKE = 7,   // out f32 += acc + bias (residual, in place); out2 split f16 = snake(out)
     EPI_F32_SNAKE2 = 8,    // out f32 = acc + bias; out2 split f16 = snake(out)
+    EPI_GEGLU = 9,     // columns in groups of 64 = [32 wi_0 | 32 wi_1] -> out split f16 = gelu_tanh(a)*b (T5 FFN)
+    EPI_F16_GELUQ = 10,    // out split f16 = gelu_quick(acc + bias) (CLIP MLP)
 };
 constexpr bool epi_snake(int epi) { return epi == EPI_F16_SNAKE || epi == EPI_RESID_SNAKE || epi == EPI_F32_SNAKE2; }
 
@@ -123,7 +125,17 @@ __device__ __forceinline__ void store8_split(__half * o, long long lo, const flo
 
 // Columns one epilogue call handles: one 32-column chunk; a whole 64-column head for the qkv
 // epilogue (RMSNorm + RoPE need it); a [32 w1 | 32 w3] group for SwiGLU.
-template <int EPI> struct EpiUnit { static constexpr int U = EPI == EPI_QKV ? 64 : EPI == EPI_SWIGLU ? 64 : 32; };
+template <int EPI> struct EpiUnit {
+    static constexpr int U = EPI == EPI_QKV || EPI == EPI_SWIGLU || EPI == EPI_GEGLU ? 64 : 32;
+};
+
+// geglu_ (shaders/ops_conv.metal:15-24): tanh-approximated GELU of a, argument clamped to +-10
+__device__ __forceinline__ float gelu_tanh_f(float v) {
+    const float arg = 0.7978845608f * (v + 0.044715f * v * v * v);
+    return 0.5f * v * (1.0f + tanhf(fminf(fmaxf(arg, -10.0f), 10.0f)));
+}
+// gelu_quick_ (shaders/ops_conv.metal:25-29)
+__device__ __forceinline__ float gelu_quick_f(float v) { return v / (1.0f + expf(-1.702f * v)); }
 
 // TMEM columns for a BN-wide f32 accumulator (allocations are powers of two, at least 32)
 template <int BN> struct TmemCols {
@@ -142,7 +154,18 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
     const int c0 = u * U;
     // a tile may overhang N (tile widths that do not divide N): whole units beyond N are skipped
     const bool valid = ok && t < a.rows && b < a.B && n0 + c0 < a.N;
-    if constexpr (EPI == EPI_SWIGLU) {
+    if constexpr (EPI == EPI_GEGLU) {
+        float va[32], vb[32];
+        load32(c0, va);
+        load32(c0 + 32, vb);
+        if (valid) {
+            __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + (n0 + c0) / 2;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) va[e] = gelu_tanh_f(va[e]) * vb[e];
+#pragma unroll
+            for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, va + q);
+        }
+    } else if constexpr (EPI == EPI_SWIGLU) {
         {
             const int j = 0;
             float va[32], vb[32];
@@ -166,16 +189,20 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
         load32(c0 + 32, v + 32);
         if (!valid) return;
         const int n = n0 + c0, which = n / a.H, head = (n % a.H) >> 6;
+        if (ec.bias) {
 #pragma unroll
-        for (int e = 0; e < 64; ++e) v[e] += ec.bias[c0 + e];
+            for (int e = 0; e < 64; ++e) v[e] += ec.bias[c0 + e];
+        }
         if (which < 2) {
-            const float * g = which == 0 ? ec.qn : ec.kn;
-            float ss = 0.0f;
+            if (a.qn) {   // per-head RMSNorm (the DiT; the text encoders have none)
+                const float * g = which == 0 ? ec.qn : ec.kn;
+                float ss = 0.0f;
 #pragma unroll
-            for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
-            const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
+                for (int e = 0; e < 64; ++e) ss += v[e] * v[e];
+                const float inv = 1.0f / sqrtf(ss / 64.0f + 1e-6f);
 #pragma unroll
-            for (int e = 0; e < 64; ++e) v[e] = v[e] * inv * g[e];
+                for (int e = 0; e < 64; ++e) v[e] = v[e] * inv * g[e];
+            }
             if (a.rope) {
                 // this row's (cos, sin) pairs, two per float4: staged rows when the tile's time rows
                 // fit the staged table, else straight from the global table
@@ -210,11 +237,15 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             float * o = (float *) a.out + z * a.part_stride + (long long) b * a.out_bs + (long long) t * a.ldo + n;
 #pragma unroll
             for (int q = 0; q < 32; q += 4) *(float4 *) (o + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-        } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU || EPI == EPI_F16_SNAKE) {
+        } else if constexpr (EPI == EPI_F16 || EPI == EPI_F16_SILU || EPI == EPI_F16_SNAKE || EPI == EPI_F16_GELUQ) {
             __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + n;
             if (EPI == EPI_F16_SILU) {
 #pragma unroll
                 for (int e = 0; e < 32; ++e) v[e] = silu_f(v[e]);
+            }
+            if (EPI == EPI_F16_GELUQ) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) v[e] = gelu_quick_f(v[e]);
             }
             if (EPI == EPI_F16_SNAKE) {   // snake_ (shaders/ops_conv.metal:204-213) on acc + bias
 #pragma unroll
@@ -359,7 +390,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
             const int tid = threadIdx.x;
             if (a.bias)
                 for (int i = tid; i < BN && n0 + i < a.N; i += 128) cbias[i] = a.bias[n0 + i];
-            if (EPI == EPI_QKV && tid < 64) { cqn[tid] = a.qn[tid]; ckn[tid] = a.kn[tid]; }
+            if (EPI == EPI_QKV && a.qn && tid < 64) { cqn[tid] = a.qn[tid]; ckn[tid] = a.kn[tid]; }
             if (epi_snake(EPI))
                 for (int i = tid; i < BN && n0 + i < a.N; i += 128) { cqn[i] = a.snake_a[n0 + i]; ckn[i] = a.snake_b[n0 + i]; }
             if (EPI == EPI_QKV && a.rope)

@@ -2,6 +2,7 @@
 #include "gguf_io.h"
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <fcntl.h>
@@ -19,6 +20,12 @@ Gguf::~Gguf() {
 }
 
 static uint64_t type_size(uint32_t t) { return t == GG_F32 ? 4 : (t == GG_F16 || t == GG_BF16) ? 2 : 0; }
+// bytes of a tensor's data: plain types, or Q8_0 blocks of 32 values (f16 scale + 32 int8), the
+// only quantised type the reference reads (src/gguf.cpp:46,216-228); 0 for any other type
+static uint64_t tensor_bytes(uint32_t t, uint64_t nelem) {
+    if (t == GG_Q8_0) return nelem % 32 ? 0 : nelem / 32 * 34;
+    return nelem * type_size(t);
+}
 
 bool Gguf::open(const std::string & path, std::string & err) {
     int fd = ::open(path.c_str(), O_RDONLY);
@@ -96,14 +103,14 @@ bool Gguf::open(const std::string & path, std::string & err) {
         for (uint32_t d = 0; d < t.n_dims; ++d) t.ne[d] = u64();
         t.type = u32();
         t.offset = u64();
-        t.nbytes = t.nelem() * type_size(t.type);
+        t.nbytes = tensor_bytes(t.type, t.nelem());
         tensors_[t.name] = t;
     }
     if (bad) { err = "truncated GGUF tensor table"; return false; }
     const uint64_t hdr = (uint64_t) (p - (const uint8_t *) map_);
     const uint64_t data_start = (hdr + align - 1) & ~(align - 1);
     for (auto & [name, t] : tensors_) {
-        if (type_size(t.type) == 0) continue;   // quantised types are not part of the DiT file
+        if (t.nbytes == 0) continue;   // types the reference cannot read either
         if (data_start + t.offset + t.nbytes > len_) { err = "tensor " + name + " runs past end of file"; return false; }
         t.data = (const uint8_t *) map_ + data_start + t.offset;
     }
@@ -126,6 +133,27 @@ void synth_fill_host(const TensorSpec & s, uint64_t seed, void * dst) {
     const unsigned nth = std::max(1u, std::min(16u, std::thread::hardware_concurrency()));
     auto work = [&](unsigned t) {
         const uint64_t lo = n * t / nth, hi = n * (t + 1) / nth;
+        if (s.type == GG_Q8_0) {
+            // ggml's Q8_0 quantiser: per block of 32, d = max|x| / 127, q = round(x / d)
+            uint8_t * o = (uint8_t *) dst;
+            const uint64_t nb = n / 32, b0 = nb * t / nth, b1 = nb * (t + 1) / nth;
+            for (uint64_t bk = b0; bk < b1; ++bk) {
+                float x[32], amax = 0.0f;
+                for (int k = 0; k < 32; ++k) {
+                    x[k] = tsn_init_value(key, bk * 32 + k, s.init, s.scale);
+                    amax = std::max(amax, std::fabs(x[k]));
+                }
+                const float d = amax / 127.0f, id = d != 0.0f ? 1.0f / d : 0.0f;
+                const uint16_t d16 = tsn_ref_f32_to_f16(d);
+                uint8_t * blk = o + bk * 34;
+                std::memcpy(blk, &d16, 2);
+                for (int k = 0; k < 32; ++k) {
+                    const long q = std::lrint(x[k] * id);
+                    blk[2 + k] = (uint8_t) (int8_t) std::max(-127L, std::min(127L, q));
+                }
+            }
+            return;
+        }
         if (s.type == GG_F32) {
             float * o = (float *) dst;
             for (uint64_t i = lo; i < hi; ++i) o[i] = tsn_init_value(key, i, s.init, s.scale);
@@ -170,7 +198,7 @@ bool write_gguf(const std::string & path, const std::vector<TensorSpec> & specs,
         for (uint32_t d = 0; d < s.n_dims; ++d) w64(s.ne[d]);
         w32(s.type);
         w64(off);
-        off += (s.nelem() * type_size(s.type) + align - 1) & ~(align - 1);
+        off += (tensor_bytes(s.type, s.nelem()) + align - 1) & ~(align - 1);
     }
     long pos = ftell(f);
     const uint64_t pad = ((uint64_t) pos + align - 1) / align * align - (uint64_t) pos;
@@ -178,7 +206,7 @@ bool write_gguf(const std::string & path, const std::vector<TensorSpec> & specs,
     w(zeros, (size_t) pad);
     std::vector<uint8_t> buf;
     for (const TensorSpec & s : specs) {
-        const uint64_t nb = s.nelem() * type_size(s.type);
+        const uint64_t nb = tensor_bytes(s.type, s.nelem());
         buf.resize((size_t) nb);
         synth_fill_host(s, seed, buf.data());
         w(buf.data(), (size_t) nb);
@@ -205,6 +233,20 @@ bool write_synthetic_vae_gguf(const std::string & path, const VaeGeom & v, uint6
     return write_gguf(path, vae_schema(v),
                       {{"vae.latent_dim", v.latent_dim}, {"vae.channels", v.channels}, {"vae.out_channels", v.out_channels}},
                       {}, "thinksound-vae-synthetic", seed, err);
+}
+
+// KV keys of T5Model::load (src/t5.cpp:22-33) and ClipModel::load (src/clip.cpp:6-12)
+bool write_synthetic_t5_gguf(const std::string & path, const T5Geom & g, uint64_t seed, std::string & err) {
+    return write_gguf(path, t5_schema(g),
+                      {{"t5.d_model", g.d_model}, {"t5.d_ff", g.d_ff}, {"t5.n_layers", g.layers}, {"t5.n_heads", g.heads},
+                       {"t5.d_kv", g.d_model / g.heads}, {"t5.rel_buckets", g.rel_buckets}, {"t5.rel_max_dist", g.rel_max_dist}},
+                      {{"t5.eps", 1e-6f}}, "t5-synthetic", seed, err);
+}
+
+bool write_synthetic_clip_gguf(const std::string & path, const ClipGeom & g, uint64_t seed, std::string & err) {
+    return write_gguf(path, clip_schema(g),
+                      {{"clip.hidden", g.hidden}, {"clip.layers", g.layers}, {"clip.heads", g.heads}, {"clip.ctx", g.ctx}},
+                      {}, "metaclip-text-synthetic", seed, err);
 }
 
 } // namespace tsn

@@ -48,8 +48,11 @@ bool write_synthetic_gguf(const std::string & path, const DitGeom & g, uint64_t 
                           std::string & err);
 // The seeded synthetic VAE decoder fixture (f32 tensors of vae_schema).
 bool write_synthetic_vae_gguf(const std::string & path, const VaeGeom & v, uint64_t seed, std::string & err);
+// The seeded synthetic text encoders (t5_schema: Q8_0 matrices; clip_schema: f32).
+bool write_synthetic_t5_gguf(const std::string & path, const T5Geom & g, uint64_t seed, std::string & err);
+bool write_synthetic_clip_gguf(const std::string & path, const ClipGeom & g, uint64_t seed, std::string & err);
 
-// Fill dst with the synthetic values of one tensor (F32 values or BF16 bits by spec.type).
+// Fill dst with the synthetic values of one tensor (F32 values, BF16 bits or Q8_0 blocks by spec.type).
 void synth_fill_host(const TensorSpec & spec, uint64_t seed, void * dst);
 
 } // namespace tsn

@@ -150,16 +150,25 @@ __global__ void __launch_bounds__(128 * KG, 1) attn_kernel(const AttnArgs a) {
                 mma16816(s[2 * p + 1], qf[kk], e2, e3);
             }
         }
-        // scale, mask keys >= S, online softmax (base 2)
+        // scale, mask keys >= S, add the logit bias, online softmax (base 2)
         float mx0 = -INFINITY, mx1 = -INFINITY;
+        const float * lb0 = nullptr, * lb1 = nullptr;
+        if (a.lbias) {   // rows past S read row S-1 (their results are never stored)
+            const int r0 = min(qt * 64 + rw * 16 + (lane >> 2), a.S - 1), r1 = min(qt * 64 + rw * 16 + (lane >> 2) + 8, a.S - 1);
+            const float * lb = a.lbias + ((size_t) b * a.NH + h) * (size_t) a.S * a.S_pad;
+            lb0 = lb + (size_t) r0 * a.S_pad;
+            lb1 = lb + (size_t) r1 * a.S_pad;
+        }
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
             const int key = j * 64 + nt * 8 + 2 * (lane & 3);
+            float2 bb0 = make_float2(0.0f, 0.0f), bb1 = bb0;
+            if (lb0) { bb0 = *(const float2 *) (lb0 + key); bb1 = *(const float2 *) (lb1 + key); }
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 const bool ok = key + e < a.S;
-                s[nt][e] = ok ? s[nt][e] * a.scale_log2 : -INFINITY;
-                s[nt][2 + e] = ok ? s[nt][2 + e] * a.scale_log2 : -INFINITY;
+                s[nt][e] = ok ? s[nt][e] * a.scale_log2 + (e ? bb0.y : bb0.x) : -INFINITY;
+                s[nt][2 + e] = ok ? s[nt][2 + e] * a.scale_log2 + (e ? bb1.y : bb1.x) : -INFINITY;
                 mx0 = fmaxf(mx0, s[nt][e]);
                 mx1 = fmaxf(mx1, s[nt][2 + e]);
             }
@@ -169,14 +178,16 @@ __global__ void __launch_bounds__(128 * KG, 1) attn_kernel(const AttnArgs a) {
             mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
             mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
         }
+        // a row whose keys so far are all masked keeps max -inf: exponents then use 0 as reference
         const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+        const float rf0 = mn0 == -INFINITY ? 0.0f : mn0, rf1 = mn1 == -INFINITY ? 0.0f : mn1;
+        const float al0 = exp2f(m0 - rf0), al1 = exp2f(m1 - rf1);
         m0 = mn0; m1 = mn1;
         float ps0 = 0.0f, ps1 = 0.0f;
 #pragma unroll
         for (int nt = 0; nt < 8; ++nt) {
-            s[nt][0] = exp2f(s[nt][0] - mn0); s[nt][1] = exp2f(s[nt][1] - mn0);
-            s[nt][2] = exp2f(s[nt][2] - mn1); s[nt][3] = exp2f(s[nt][3] - mn1);
+            s[nt][0] = exp2f(s[nt][0] - rf0); s[nt][1] = exp2f(s[nt][1] - rf0);
+            s[nt][2] = exp2f(s[nt][2] - rf1); s[nt][3] = exp2f(s[nt][3] - rf1);
             ps0 += s[nt][0] + s[nt][1];
             ps1 += s[nt][2] + s[nt][3];
         }
@@ -225,7 +236,8 @@ __global__ void __launch_bounds__(128 * KG, 1) attn_kernel(const AttnArgs a) {
             const float * d = st + (((q - 1) * 4 + rw) * 32 + lane) * 36;
             const float mq0 = d[32], mq1 = d[33];
             const float M0 = fmaxf(m0, mq0), M1 = fmaxf(m1, mq1);
-            const float a0 = exp2f(m0 - M0), a1 = exp2f(m1 - M1), b0 = exp2f(mq0 - M0), b1 = exp2f(mq1 - M1);
+            const float R0 = M0 == -INFINITY ? 0.0f : M0, R1 = M1 == -INFINITY ? 0.0f : M1;
+            const float a0 = exp2f(m0 - R0), a1 = exp2f(m1 - R1), b0 = exp2f(mq0 - R0), b1 = exp2f(mq1 - R1);
 #pragma unroll
             for (int dt = 0; dt < 8; ++dt) {
                 o[dt][0] = o[dt][0] * a0 + d[dt * 4 + 0] * b0;

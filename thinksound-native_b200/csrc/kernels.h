@@ -109,6 +109,10 @@ struct AttnArgs {
     long long out_lo0, out_lo1, out_lo2;                     // ... and of each output (0: hi only)
     unsigned long long * trace;                              // optional per-CTA stamps (entry, upstream done, exit)
     int * err;                                               // device error word (attn_tc_kernel)
+    // optional additive logit bias in log2 units, [B][NH][S][S_pad] (key fastest; -inf masks a key):
+    // the text encoders' T5 relative-position bias and pad mask, or CLIP's causal + EOT mask
+    // (attn_kernel only)
+    const float * lbias;
 };
 cudaError_t configure_attention();
 cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s);

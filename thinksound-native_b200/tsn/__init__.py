@@ -87,6 +87,17 @@ _SIGS = [
     ("tsn_vae_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_vae_flops", C.c_double, [C.c_void_p]),
     ("tsn_vae_free", C.c_int, [C.c_void_p]),
+    ("tsn_t5_load", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
+    ("tsn_clip_load", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
+    ("tsn_encoder_info", C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_uint32), C.POINTER(C.c_uint32)]),
+    ("tsn_encoder_encode", C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]),
+    ("tsn_encoder_last_ms", C.c_double, [C.c_void_p]),
+    ("tsn_encoder_flops", C.c_double, [C.c_void_p]),
+    ("tsn_encoder_weight_bytes", C.c_double, [C.c_void_p]),
+    ("tsn_encoder_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    ("tsn_encoder_free", C.c_int, [C.c_void_p]),
+    ("tsn_gguf_write_synthetic_t5", C.c_int, [C.c_char_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64]),
+    ("tsn_gguf_write_synthetic_clip", C.c_int, [C.c_char_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint64]),
     ("tsn_dit_get_geom", C.c_int, [C.c_void_p, C.POINTER(Geom)]),
     ("tsn_dit_weight_bytes", C.c_size_t, [C.c_void_p]),
     ("tsn_dit_prepare", C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
@@ -403,6 +414,71 @@ class Dit:
         buf = C.create_string_buffer(1 << 20)
         check(lib().tsn_dit_profile_ops(self.h, buf, len(buf)))
         return buf.value.decode()
+
+
+class TextEncoder:
+    """tn::T5Model (kind "t5") or tn::ClipModel (kind "clip") on the device: 77 token ids ->
+    per-token features [77, width] (and CLIP's pooled projection [width])."""
+
+    def __init__(self, dev: Device, kind: str, gguf: str):
+        if kind not in ("t5", "clip"):
+            raise ValueError("kind must be 't5' or 'clip'")
+        self.dev = dev
+        self.kind = kind
+        h = C.c_void_p()
+        load = lib().tsn_t5_load if kind == "t5" else lib().tsn_clip_load
+        check(load(dev.h, gguf.encode(), C.byref(h)))
+        self.h = h
+        w, n, layers = C.c_uint32(), C.c_uint32(), C.c_uint32()
+        check(lib().tsn_encoder_info(h, C.byref(w), C.byref(n), C.byref(layers)))
+        self.width, self.ctx, self.layers = w.value, n.value, layers.value
+        dev._models.add(self)
+
+    def encode(self, ids):
+        """Host int32 ids [ctx] -> per_token [ctx, width] f32 (t5), or (per_token, pooled [width]) (clip)."""
+        import numpy as np
+        ids = np.ascontiguousarray(ids, np.int32)
+        out = np.zeros((self.ctx, self.width), np.float32)
+        pooled = np.zeros(self.width, np.float32)
+        check(lib().tsn_encoder_encode(self.h, ids.ctypes.data, ids.size, out.ctypes.data, out.size,
+                                       pooled.ctypes.data, pooled.size))
+        return out if self.kind == "t5" else (out, pooled)
+
+    def last_ms(self) -> float:
+        return lib().tsn_encoder_last_ms(self.h)
+
+    def flops(self) -> float:
+        return lib().tsn_encoder_flops(self.h)
+
+    def weight_bytes(self) -> float:
+        return lib().tsn_encoder_weight_bytes(self.h)
+
+    def profile_ops(self) -> str:
+        buf = C.create_string_buffer(1 << 18)
+        check(lib().tsn_encoder_profile_ops(self.h, buf, len(buf)))
+        return buf.value.decode()
+
+    def close(self):
+        if self.h and self.dev.h:
+            lib().tsn_encoder_free(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def write_synthetic_t5_gguf(path: str, d_model: int = 2048, d_ff: int = 5120, layers: int = 24, heads: int = 32,
+                            seed: int = 4242):
+    """The seeded synthetic T5 encoder GGUF (Q8_0 matrices; tensor names of src/t5.cpp)."""
+    check(lib().tsn_gguf_write_synthetic_t5(path.encode(), d_model, d_ff, layers, heads, seed))
+
+
+def write_synthetic_clip_gguf(path: str, hidden: int = 1024, layers: int = 24, heads: int = 16, seed: int = 4242):
+    """The seeded synthetic MetaCLIP text encoder GGUF (f32; tensor names of src/clip.cpp)."""
+    check(lib().tsn_gguf_write_synthetic_clip(path.encode(), hidden, layers, heads, seed))
 
 
 def write_synthetic_vae_gguf(path: str, channels: int = 128, latent_dim: int = 64, out_channels: int = 2,
