@@ -676,6 +676,8 @@ def run_encoders(a):
             dev_ms.append(e.last_ms())
         ms = max(dev_ms)
         wb = e.weight_bytes()
+        if a.profile_ops:
+            print(e.profile_ops(), file=sys.stderr, flush=True)
         line = {
             "metric": f"{kind} encodes/s (77 tokens)", "value": 1000.0 / ms, "unit": "encodes/s", "n_gpus": 1,
             "steps": a.steps, "warmup": max(a.warmup, 3), "ms_per_step": ms, "higher_is_better": True,

@@ -29,8 +29,8 @@ def dev():
     d.close()
 
 
-def _gguf(tmp_path_factory, kind, **geom):
-    p = str(tmp_path_factory.mktemp(kind) / f"{kind}.gguf")
+def _gguf(tmp_path_factory, kind, tag=None, **geom):
+    p = str(tmp_path_factory.mktemp(tag or kind) / f"{kind}.gguf")
     (tsn.write_synthetic_t5_gguf if kind == "t5" else tsn.write_synthetic_clip_gguf)(p, seed=SEED, **geom)
     return p
 
@@ -93,13 +93,13 @@ def test_clip_eot_edges(dev, clip_small, n_tok):
 def test_wide_geometries(dev, tmp_path_factory):
     """Widths of the real models (T5 d_model 1024 with 16 heads, d_ff 2816; CLIP hidden 512) over
     two layers: many weight tiles per GEMM and K-sliced partial tiles."""
-    p = _gguf(tmp_path_factory, "t5w", d_model=1024, d_ff=2816, layers=2, heads=16)
+    p = _gguf(tmp_path_factory, "t5", "t5w", d_model=1024, d_ff=2816, layers=2, heads=16)
     ids = t5_ids(SEED + 5, 40)
     out = tsn.TextEncoder(dev, "t5", p).encode(ids)
     W, kv = gguf_read.device_weights(p)
     assert rel_l2(out, O.t5_encode_np(W, kv, ids)) < TOL
     os.unlink(p)
-    p = _gguf(tmp_path_factory, "clipw", hidden=512, layers=2, heads=8)
+    p = _gguf(tmp_path_factory, "clip", "clipw", hidden=512, layers=2, heads=8)
     ids = clip_ids(SEED + 6, 30)
     pt, pooled = tsn.TextEncoder(dev, "clip", p).encode(ids)
     W, kv = gguf_read.device_weights(p)
