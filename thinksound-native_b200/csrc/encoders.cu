@@ -26,6 +26,7 @@
 #include <cmath>
 #include <cstring>
 #include <functional>
+#include <map>
 #include <memory>
 #include <thread>
 #include <vector>
@@ -490,31 +491,45 @@ struct EncModel {
         return prepare();
     }
 
-    // One projection over the n token rows of the split operand A ([n][K] hi, then lo): tile width
-    // and K slices by the split-operand cost model (the weights are read once; a few CTAs per SM
-    // keep them streaming). partial: independent K slices write partial tiles into `part`.
-    int gemm_op(const std::string & name, const ELin & W, const __half * A, int epi, bool partial,
-                const std::function<void(GemmArgs &)> & outs) {
+    // One projection over the n token rows of the split operand A ([n][K] hi, then lo). Tile width
+    // and K slices: timed at load over every valid configuration (once per GEMM role: qkv, o, up,
+    // down share their shapes across layers), or the split-operand cost model with autotune off.
+    // partial: independent K slices write partial tiles into `part`.
+    std::map<std::string, std::pair<int, int>> tiles;   // role -> (tile width, K slices)
+    bool autotune = true;
+
+    std::vector<std::pair<int, int>> candidates(const ELin & W, int epi, bool partial) const {
+        std::vector<std::pair<int, int>> c;
         const int kb = W.K / 64;
-        double best = 1e30;
-        int bn = 0, sp = 1;
         for (int cb : {256, 128, 64}) {
             if (W.N % cb) continue;
-            const double kcost = W.split ? (cb == 256 ? 1.1 : cb == 128 ? 0.6 : 0.45) : (cb == 256 ? 0.74 : cb == 128 ? 0.40 : 0.30);
-            const int tiles = W.N / cb, smax = partial ? MAX_PARTS : 8;
-            for (int s = 1; s <= smax && s <= kb; ++s) {
+            for (int s = 1; s <= (partial ? MAX_PARTS : 8) && s <= kb; ++s) {
                 const int kbps = (kb + s - 1) / s;
                 if ((kb + kbps - 1) / kbps != s) continue;
                 const int cl = partial ? 1 : s;
-                const int cap = W.split ? gemm_ws_capacity(cb, epi, cl) : gemm_cluster_capacity(cb, epi, true, cl);
-                if (cap <= 0) continue;
-                const int waves = (tiles * s + cap - 1) / cap;
-                const double cost = waves * (kbps * kcost + 1.5) + (s > 1 ? (partial ? 0.3 * s : 1.5 * waves) : 0.0);
-                if (cost < best - 1e-9) { best = cost; bn = cb; sp = s; }
+                if ((W.split ? gemm_ws_capacity(cb, epi, cl) : gemm_cluster_capacity(cb, epi, true, cl)) > 0) c.push_back({cb, s});
             }
         }
-        if (!bn) return fail(TSN_ERR_ARG, name + ": no tile fits");
-        GemmLaunch gl{};
+        return c;
+    }
+    std::pair<int, int> cost_model(const ELin & W, int epi, bool partial) const {
+        const int kb = W.K / 64;
+        double best = 1e30;
+        std::pair<int, int> r{0, 1};
+        for (auto [cb, s] : candidates(W, epi, partial)) {
+            const double kcost = W.split ? (cb == 256 ? 1.1 : cb == 128 ? 0.6 : 0.45) : (cb == 256 ? 0.74 : cb == 128 ? 0.40 : 0.30);
+            const int kbps = (kb + s - 1) / s, cl = partial ? 1 : s;
+            const int cap = W.split ? gemm_ws_capacity(cb, epi, cl) : gemm_cluster_capacity(cb, epi, true, cl);
+            const int waves = (W.N / cb * s + cap - 1) / cap;
+            const double cost = waves * (kbps * kcost + 1.5) + (s > 1 ? (partial ? 0.3 * s : 1.5 * waves) : 0.0);
+            if (cost < best - 1e-9) { best = cost; r = {cb, s}; }
+        }
+        return r;
+    }
+    int build_gemm(const std::string & name, const ELin & W, const __half * A, int epi, bool partial, int bn, int sp,
+                   const std::function<void(GemmArgs &)> & outs, GemmLaunch & gl) {
+        const int kb = W.K / 64;
+        gl = GemmLaunch{};
         gl.bn = bn; gl.epi = epi; gl.split = true; gl.ab_bf16 = 0;
         gl.smem = W.split ? gemm_ws_smem_bytes(bn, epi) : gemm_smem_bytes(bn, true, epi);
         gl.grid = dim3(1, W.N / bn, sp);
@@ -530,10 +545,49 @@ struct EncModel {
         a.m_fast = 1;
         if (partial) { a.out = part; a.ldo = d; a.out_bs = 0; a.part_stride = (long long) n * d; }
         outs(a);
+        return TSN_OK;
+    }
+    static cudaError_t run_gemm(const GemmLaunch & gl, bool ws, cudaStream_t s) {
+        return ws ? launch_gemm_ws(gl, s) : launch_gemm(gl, s);
+    }
+    // mean device time of `reps` back-to-back launches (after warm-up), microseconds
+    int time_gemm(const GemmLaunch & gl, bool ws, double & us) {
+        for (int i = 0; i < 3; ++i) ECK(run_gemm(gl, ws, dev->stream));
+        ECK(cudaEventRecord(e0, dev->stream));
+        const int reps = 10;
+        for (int i = 0; i < reps; ++i) ECK(run_gemm(gl, ws, dev->stream));
+        ECK(cudaEventRecord(e1, dev->stream));
+        ERT(dev->sync());
+        float ms = 0;
+        ECK(cudaEventElapsedTime(&ms, e0, e1));
+        us = 1000.0 * ms / reps;
+        return TSN_OK;
+    }
+    int gemm_op(const std::string & name, const ELin & W, const __half * A, int epi, bool partial,
+                const std::function<void(GemmArgs &)> & outs) {
+        const std::string role = name.substr(name.rfind('.') + 1);
+        GemmLaunch gl;
+        auto it = tiles.find(role);
+        if (it == tiles.end()) {
+            std::pair<int, int> pick = cost_model(W, epi, partial);
+            if (!pick.first) return fail(TSN_ERR_ARG, name + ": no tile fits");
+            if (autotune) {
+                double best = 1e30;
+                for (auto c : candidates(W, epi, partial)) {
+                    double us = 0;
+                    ERT(build_gemm(name, W, A, epi, partial, c.first, c.second, outs, gl));
+                    ERT(time_gemm(gl, W.split, us));
+                    if (us < best) { best = us; pick = c; }
+                }
+            }
+            it = tiles.emplace(role, pick).first;
+        }
+        const int bn = it->second.first, sp = it->second.second;
+        ERT(build_gemm(name, W, A, epi, partial, bn, sp, outs, gl));
         last_splits = sp;
-        if (W.split) ops.push_back([gl](cudaStream_t s) { return launch_gemm_ws(gl, s); });
-        else ops.push_back([gl](cudaStream_t s) { return launch_gemm(gl, s); });
-        op_names.push_back(name);
+        const bool ws = W.split;
+        ops.push_back([gl, ws](cudaStream_t s) { return run_gemm(gl, ws, s); });
+        op_names.push_back(name + "[" + std::to_string(bn) + "x" + std::to_string(sp) + "]");
         flops += 2.0 * n * (double) W.N * W.K;
         return TSN_OK;
     }
