@@ -615,7 +615,7 @@ def run_vae(a):
                      "note": "2·M·N·K over every conv; each K step issues three split products"},
         "e2e": {"value": 1.0 / max(wall), "unit": "decodes/s", "h2d_bytes_per_step": lat.nbytes,
                 "d2h_bytes_per_step": a.T * 2048 * 2 * 4},
-        "gpu_launches": None,
+        "gpu_launches": v.launches() * a.steps,
     }
     if not a.no_cpu_baseline:
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -694,7 +694,7 @@ def run_encoders(a):
                                  "77-row activations are negligible", "tflops": e.flops() / (ms * 1e-3) / 1e12},
             "e2e": {"value": 1.0 / max(wall), "unit": "encodes/s", "h2d_bytes_per_step": ids.nbytes,
                     "d2h_bytes_per_step": e.ctx * e.width * 4 + (e.width * 4 if kind == "clip" else 0)},
-            "gpu_launches": None,
+            "gpu_launches": e.launches() * a.steps,
         }
         if not a.no_cpu_baseline:
             sys.path.insert(0, os.path.join(ROOT, "oracle"))

@@ -234,6 +234,8 @@ double tsn_vae_last_ms(tsn_vae * v);
 /* The last decoded length once more, launch by launch, one line per launch (name, device ms). */
 int tsn_vae_profile_ops(tsn_vae * v, char * out, size_t cap);
 double tsn_vae_flops(tsn_vae * v);
+/* Kernel launches in one decode graph of the prepared length. */
+int tsn_vae_launches(tsn_vae * v);
 int tsn_vae_free(tsn_vae * v);
 
 /* ------------------------------------------------------------------ text encoders */
@@ -258,6 +260,8 @@ int tsn_encoder_encode(tsn_encoder * e, const int32_t * ids, uint32_t n_ids, flo
 /* Device time of the last encode (ms), its algorithmic FLOPs and the weight bytes it streams. */
 double tsn_encoder_last_ms(tsn_encoder * e);
 double tsn_encoder_flops(tsn_encoder * e);
+/* Kernel launches in one encode graph. */
+int tsn_encoder_launches(tsn_encoder * e);
 double tsn_encoder_weight_bytes(tsn_encoder * e);
 /* The encode's launches once more eagerly, one line per launch (name, device ms). */
 int tsn_encoder_profile_ops(tsn_encoder * e, char * out, size_t cap);

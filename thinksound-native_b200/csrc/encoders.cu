@@ -778,6 +778,7 @@ int tsn_encoder_encode(tsn_encoder * e, const int32_t * ids, uint32_t n_ids, flo
 
 double tsn_encoder_last_ms(tsn_encoder * e) { return e ? e->m.last_ms : 0.0; }
 double tsn_encoder_flops(tsn_encoder * e) { return e ? e->m.flops : 0.0; }
+int tsn_encoder_launches(tsn_encoder * e) { return e ? (int) e->m.ops.size() : 0; }
 double tsn_encoder_weight_bytes(tsn_encoder * e) { return e ? e->m.wbytes : 0.0; }
 
 int tsn_encoder_profile_ops(tsn_encoder * e, char * out, size_t cap) {

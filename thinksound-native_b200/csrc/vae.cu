@@ -508,6 +508,7 @@ int tsn_vae_profile_ops(tsn_vae * v, char * out, size_t cap) {
     return TSN_OK;
 }
 double tsn_vae_flops(tsn_vae * v) { return v ? v->m.flops : 0.0; }
+int tsn_vae_launches(tsn_vae * v) { return v ? (int) v->m.ops.size() : 0; }
 
 int tsn_vae_free(tsn_vae * v) {
     if (v) { if (v->m.dev) cudaStreamSynchronize(v->m.dev->stream); delete v; }

@@ -86,6 +86,7 @@ _SIGS = [
     ("tsn_vae_last_ms", C.c_double, [C.c_void_p]),
     ("tsn_vae_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_vae_flops", C.c_double, [C.c_void_p]),
+    ("tsn_vae_launches", C.c_int, [C.c_void_p]),
     ("tsn_vae_free", C.c_int, [C.c_void_p]),
     ("tsn_t5_load", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
     ("tsn_clip_load", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
@@ -93,6 +94,7 @@ _SIGS = [
     ("tsn_encoder_encode", C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t]),
     ("tsn_encoder_last_ms", C.c_double, [C.c_void_p]),
     ("tsn_encoder_flops", C.c_double, [C.c_void_p]),
+    ("tsn_encoder_launches", C.c_int, [C.c_void_p]),
     ("tsn_encoder_weight_bytes", C.c_double, [C.c_void_p]),
     ("tsn_encoder_profile_ops", C.c_int, [C.c_void_p, C.c_char_p, C.c_size_t]),
     ("tsn_encoder_free", C.c_int, [C.c_void_p]),
@@ -259,6 +261,10 @@ class Vae:
 
     def flops(self) -> float:
         return lib().tsn_vae_flops(self.h)
+
+    def launches(self) -> int:
+        """Kernel launches in one decode graph of the last decoded length."""
+        return lib().tsn_vae_launches(self.h)
 
     def profile_ops(self) -> str:
         buf = C.create_string_buffer(1 << 18)
@@ -449,6 +455,10 @@ class TextEncoder:
 
     def flops(self) -> float:
         return lib().tsn_encoder_flops(self.h)
+
+    def launches(self) -> int:
+        """Kernel launches in one encode graph."""
+        return lib().tsn_encoder_launches(self.h)
 
     def weight_bytes(self) -> float:
         return lib().tsn_encoder_weight_bytes(self.h)
