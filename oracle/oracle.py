@@ -5,6 +5,8 @@ module. It wraps:
   * lib/liboracle.so  — the CPU restatement of the reference's DiT path (port.cpp + kernels.cpp)
   * _ref/ts_ref_dit   — the reference's own host code (src/dit.cpp, src/dit_fwd.cpp, src/net.mm,
                         src/gguf.cpp) built over a CPU Device; present only where it was built.
+  * _ref/ts_ref_dit_tsn — the same host code and driver over the GPU through the library's drop-in
+                        device (integration/gpu_tsn.cpp): the tests check the boundary with it.
 """
 from __future__ import annotations
 
@@ -18,6 +20,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "lib", "liboracle.so")
 REF_BIN = os.path.join(HERE, "_ref", "ts_ref_dit")
+REF_TSN_BIN = os.path.join(HERE, "_ref", "ts_ref_dit_tsn")
 
 TAPS = ["t_emb", "global_c", "extended_c", "x_in", "text_xn", "a0_q", "a0_k", "a0_v", "a0_out",
         "jb0_lat", "jb0_clip", "jb0_text", "after_joint", "after_fused", "final_fx", "final_mod", "flow"]
@@ -110,13 +113,13 @@ def write_inputs(d: str, inputs: dict):
 
 
 def run_ref(mode: str, gguf: str, T: int, C_: int, TS: int, in_dir: str, out_dir: str, *args, threads=None,
-            timeout=3600):
-    """Run the reference-built driver; returns its stdout (JSON for step/sample)."""
+            timeout=3600, binary=None):
+    """Run the reference-built driver (binary: REF_TSN_BIN for its GPU build); returns its stdout."""
     os.makedirs(out_dir, exist_ok=True)
     env = dict(os.environ)
     if threads:
         env["OMP_NUM_THREADS"] = str(threads)
-    cmd = [REF_BIN, mode, gguf, str(T), str(C_), str(TS), in_dir, out_dir] + [str(a) for a in args]
+    cmd = [binary or REF_BIN, mode, gguf, str(T), str(C_), str(TS), in_dir, out_dir] + [str(a) for a in args]
     r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=timeout)
     if r.returncode != 0:
         raise RuntimeError(f"ts_ref_dit failed ({r.returncode}): {r.stderr[-2000:]}")
@@ -145,13 +148,13 @@ VAE_STRIDES = (8, 8, 4, 4, 2)
 VAE_DILS = (1, 3, 9)
 
 
-def ref_vae(gguf: str, latent: np.ndarray, threads=None, reps=1, workdir=None):
+def ref_vae(gguf: str, latent: np.ndarray, threads=None, reps=1, workdir=None, binary=None):
     """VaeModel::decode of the reference build (src/vae.cpp:17-86) on latent [T, 64].
     Returns (audio [T_audio, 2] f32, timing JSON)."""
     import tempfile
     d = workdir or tempfile.mkdtemp(prefix="tsn_vae_")
     write_inputs(d, {"latent": latent})
-    out = run_ref("vae", gguf, latent.shape[0], 0, 0, d, d, reps, threads=threads)
+    out = run_ref("vae", gguf, latent.shape[0], 0, 0, d, d, reps, threads=threads, binary=binary)
     js = parse_json_line(out)
     audio = np.fromfile(os.path.join(d, "audio.bin"), np.float32).reshape(-1, 2)
     return audio, js
@@ -206,7 +209,7 @@ def vae_decode_np(W, latent):
 
 
 # ------------------------------------------------ text encoders (src/t5.cpp, src/clip.cpp)
-def ref_encoder(kind: str, gguf: str, ids: np.ndarray, threads=None, reps=1, workdir=None):
+def ref_encoder(kind: str, gguf: str, ids: np.ndarray, threads=None, reps=1, workdir=None, binary=None):
     """T5Model::encode (kind "t5", src/t5.cpp:84-131) or ClipModel::encode ("clip",
     src/clip.cpp:30-101) of the reference build on 77 int32 ids. Returns (per_token [77, width],
     pooled [width] or None, timing JSON)."""
@@ -214,7 +217,7 @@ def ref_encoder(kind: str, gguf: str, ids: np.ndarray, threads=None, reps=1, wor
     d = workdir or tempfile.mkdtemp(prefix="tsn_enc_")
     os.makedirs(d, exist_ok=True)
     np.ascontiguousarray(ids, np.int32).tofile(os.path.join(d, "ids.bin"))
-    js = parse_json_line(run_ref(kind, gguf, 0, 0, 0, d, d, reps, threads=threads))
+    js = parse_json_line(run_ref(kind, gguf, 0, 0, 0, d, d, reps, threads=threads, binary=binary))
     if kind == "t5":
         return np.fromfile(os.path.join(d, "out.bin"), np.float32).reshape(77, -1), None, js
     pt = np.fromfile(os.path.join(d, "per_token.bin"), np.float32)
