@@ -533,11 +533,13 @@ struct EncModel {
         gl.bn = bn; gl.epi = epi; gl.split = true; gl.ab_bf16 = 0;
         gl.smem = W.split ? gemm_ws_smem_bytes(bn, epi) : gemm_smem_bytes(bn, true, epi);
         gl.grid = dim3(1, W.N / bn, sp);
-        if (!make_act_map(&gl.ta, A, W.K, n, 1, 128, 1, 0) || !make_act_map(&gl.ta2, A + (size_t) n * W.K, W.K, n, 1, 128, 1, 0) ||
+        // the 77 token rows as an 80-row activation box: rows 80..127 of each A tile are never loaded
+        const int ar = (n + 15) / 16 * 16;
+        if (!make_act_map(&gl.ta, A, W.K, n, 1, ar, 1, 0) || !make_act_map(&gl.ta2, A + (size_t) n * W.K, W.K, n, 1, ar, 1, 0) ||
             !make_w_map(&gl.tb, W.w, W.K, W.N, bn, 0) || (W.split && !make_w_map(&gl.tb2, W.lo(), W.K, W.N, bn, 0)))
             return fail(TSN_ERR_CUDA, name + ": tensor map encode failed");
         GemmArgs & a = gl.args;
-        a.rows = n; a.B = 1; a.bt = 128; a.bb = 1; a.m_tiles_t = 1; a.N = W.N;
+        a.rows = n; a.B = 1; a.bt = ar; a.bb = 1; a.m_tiles_t = 1; a.N = W.N; a.a_rows = ar;
         a.k_blocks = kb; a.ic_blocks = kb; a.pad = 0;
         a.splits = partial ? 1 : sp; a.kb_per_split = (kb + sp - 1) / sp;
         a.err = dev->d_err;

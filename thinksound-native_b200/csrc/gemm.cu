@@ -29,7 +29,7 @@ bool encoder() {
 
 bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t rows, uint64_t B,
                   uint32_t bt, uint32_t bb, int bf16) {
-    if (!encoder() || ((uintptr_t) base & 15) || (K_in % 64) || bt * bb != 128) return false;
+    if (!encoder() || ((uintptr_t) base & 15) || (K_in % 64) || bt * bb > 128 || (bt * bb) % 8) return false;
     const cuuint64_t dims[3] = {K_in, rows, B};
     const cuuint64_t strides[2] = {K_in * 2, rows * K_in * 2};
     const cuuint32_t box[3] = {64, bt, bb};

@@ -67,6 +67,8 @@ struct GemmArgs {
     int dil;                              // conv tap dilation: tap k reads row t + k*dil - pad (0 or 1: none)
     const float * snake_a; const float * snake_b;   // snake epilogues: [N] e^alpha, e^-beta
     void * out2; long long ldo2, out2_lo;           // EPI_RESID_SNAKE / EPI_F32_SNAKE2: split f16 [rows][ldo2] (B = 1)
+    int a_rows;                                     // rows per activation tile the A views load (0: 128; tile kernel,
+                                                    // bt * bb = a_rows): rows past it hold stale data, never stored
 };
 
 // phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),
@@ -330,12 +332,15 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
 
     if (warp == 4) {
         if (lane == 0) {
+            // bytes per stage: activation tiles of a_rows rows leave the rest of the 128-row tile
+            // unwritten (rows the epilogue never stores)
+            const uint32_t stage_tx = L::STAGE - (a.a_rows ? (uint32_t) (128 - a.a_rows) * 128u * (SPLIT ? 2u : 1u) : 0u);
             // weights do not depend on the upstream kernel: start the first stages' weight loads,
             // then wait for upstream outputs before loading activations
             const int pre = nk < STAGES ? nk : STAGES;
             for (int i = 0; i < pre; ++i) {
                 uint8_t * sa = smem + i * L::STAGE;
-                mbar_expect_tx(&full[i], L::STAGE);
+                mbar_expect_tx(&full[i], stage_tx);
                 tma_load_2d(sa + L::B_OFF, tmB, &full[i], (kb_begin + i) * 64, n0);
                 if (WS) tma_load_2d(sa + L::B2_OFF, tmB2, &full[i], (kb_begin + i) * 64, n0);
             }
@@ -348,7 +353,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
                 const int tap = kb / a.ic_blocks, ic0 = (kb % a.ic_blocks) * 64;
                 uint8_t * sa = smem + s * L::STAGE;
                 if (i >= pre) {
-                    mbar_expect_tx(&full[s], L::STAGE);
+                    mbar_expect_tx(&full[s], stage_tx);
                     tma_load_2d(sa + L::B_OFF, tmB, &full[s], kb * 64, n0);
                     if (WS) tma_load_2d(sa + L::B2_OFF, tmB2, &full[s], kb * 64, n0);
                 }

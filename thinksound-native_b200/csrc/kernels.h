@@ -60,7 +60,8 @@ struct GemmLaunch {
     int pair_nt = 0;              // > 0: gemm2_kernel (CTA pairs, weights on M) with NT-token tiles
     size_t smem = 0;
 };
-// Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] 16-bit activation buffer.
+// Encode a 3-D TMA view {K_in, rows, B} of a [B][rows][K_in] 16-bit activation buffer with a
+// {64, bt, bb} box; bt * bb = 128, or fewer (a multiple of 8) with GemmArgs::a_rows = bt * bb.
 bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t rows, uint64_t B,
                   uint32_t bt, uint32_t bb, int bf16);
 // Encode a 3-D TMA view {64, rows, 2} of a head-major [hi|lo][rows][64] f16 q/k/v buffer with a
