@@ -210,29 +210,42 @@ def test_full_depth_forward_vs_oracle(dev, full_gguf):
     check_taps(m, O.Oracle(full_gguf), inp, T, C, TS, 0.5)
 
 
-def test_two_generations_batched_match_single(dev, tiny_gguf):
-    """arms = 4 (two generations, each with its cond and uncond arm) gives each generation's
-    single-generation flow and sampler step."""
+@pytest.mark.parametrize("G", [2, 4])
+def test_generations_batched_match_single(dev, tiny_gguf, G):
+    """arms = 2G (G generations, each with its cond and uncond arm; G = 4 is bench.py --config5's
+    batch) gives each generation its own flow and sampler step. At G = 2 the GEMMs get the same
+    tiles as one generation, so the sums, and the results, are those of the single-generation
+    model (to 1e-5). At G = 4 (192 latent rows) the tile plan differs, the f32 sums run in another
+    order, and an occasional f16 rounding of the FFN down-projection input flips: each generation
+    is checked against the CPU oracle instead (flow within the 1e-3 gate), and against the single-
+    generation model within the same gate."""
     T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
-    gens = [make_inputs(T, C, TS, TINY["H"], seed=SEED + 20 + g) for g in range(2)]
+    gens = [make_inputs(T, C, TS, TINY["H"], seed=SEED + 20 + g) for g in range(G)]
     m = tsn.Dit(dev, gguf=tiny_gguf)
-    m.prepare(T, C, TS, 4)
+    m.prepare(T, C, TS, 2 * G)
     m.set_conditioning(np.stack([g["clip_pp"] for g in gens]), np.stack([g["sync_gather"] for g in gens]),
                        np.stack([g[k] for g in gens for k in ("text_pp_cond", "text_pp_unc")]),
                        np.stack([g[k] for g in gens for k in ("gcmlp_cond", "gcmlp_unc")]))
     m.set_x(np.stack([g["x"] for g in gens]))
-    flow4 = np.zeros((4, T, 64), np.float32)
-    m.forward(0.5, flow4)
+    flowG = np.zeros((2 * G, T, 64), np.float32)
+    m.forward(0.5, flowG)
     dt = float(np.float32(1.0 - 1.0 / 24) - np.float32(1.0))
     m.step(1.0, 5.0, dt)
-    x4 = np.zeros((2, T, 64), np.float32)
-    m.get_x(x4)
+    xG = np.zeros((G, T, 64), np.float32)
+    m.get_x(xG)
+    tol = 1e-5 if G == 2 else FLOW_TOL
+    orc = O.Oracle(tiny_gguf) if G > 2 else None
     for g, inp in enumerate(gens):
         one = gpu_model(dev, tiny_gguf, inp, T, C, TS)
         flow2 = np.zeros((2, T, 64), np.float32)
         one.forward(0.5, flow2)
-        assert rel_l2(flow4[2 * g:2 * g + 2], flow2) < 1e-5
+        assert rel_l2(flowG[2 * g:2 * g + 2], flow2) < tol
+        if orc is not None:
+            for arm, sfx in ((0, "cond"), (1, "unc")):
+                ref = orc.forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"], inp[f"text_pp_{sfx}"],
+                                  inp[f"gcmlp_{sfx}"])
+                assert rel_l2(flowG[2 * g + arm], ref) < FLOW_TOL, (g, arm)
         one.step(1.0, 5.0, dt)
         x1 = np.zeros((T, 64), np.float32)
         one.get_x(x1)
-        assert rel_l2(x4[g] - inp["x"], x1 - inp["x"]) < 1e-5
+        assert rel_l2(xG[g] - inp["x"], x1 - inp["x"]) < tol

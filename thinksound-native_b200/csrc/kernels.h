@@ -156,7 +156,8 @@ struct GemvJob {
     float * y; long long y_bs;
     int N, K, nb, act;                             // act: 0 none, 1 silu
 };
-cudaError_t launch_gemv(const GemvJob * jobs_dev, int njobs, int max_n, int ab_bf16, cudaStream_t s);
+// nb: arms of the jobs (1..8, every job's nb <= it); max_n even
+cudaError_t launch_gemv(const GemvJob * jobs_dev, int njobs, int max_n, int nb, int ab_bf16, cudaStream_t s);
 
 // ---- per-forward conditioning prologue (src/dit_fwd.cpp:131-140, 166-167) ----
 // B batch rows = G generations x A CFG arms (A = 2, or 1 for a single-arm model); the per-

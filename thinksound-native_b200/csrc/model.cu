@@ -1089,21 +1089,18 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // t-embedding MLP and conditioning                           src/dit_fwd.cpp:111-140
     GemvJob * jb = jobs;
     const int nmj = n_mod_jobs;
-    const int bfl = bf16;
-    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb, 1, H, bfl, s); }, 2, 0, "t_embed.0"});
-    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb + 1, 1, H, bfl, s); }, 2, 0, "t_embed.2"});
+    const int bfl = bf16, nbm = B;
+    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb, 1, H, 1, bfl, s); }, 2, 0, "t_embed.0"});
+    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb + 1, 1, H, 1, bfl, s); }, 2, 0, "t_embed.2"});
     CondArgs ca{te, gcmlp, sync_gather, clip_pp, text_pp, x, gc_silu, extc16, clip_s, text_s, x16,
                 tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L,
                 (long long) B * T * H, (long long) B * T * L, A};
     ops.push_back(Op{[ca](cudaStream_t s) { return launch_cond(ca, s); }, 2, 0, "cond"});
-    // the clip/text modulations of every joint block (HBM-bound GEMVs) run on a side stream beside
-    // the latent modulation GEMM and the audio input projection; the joint blocks wait for them
-    const int e_cond = p.record();
-    p.cur = 1;
-    p.wait(e_cond);
-    p.add(Op{[jb, nmj, H, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, bfl, s); }, 2, 0, "adaln_gemv"});
-    const int e_gemv = p.record();
-    p.cur = 0;
+    // the clip/text modulations of every joint block (HBM-bound GEMVs, ~160 MB of weights at the
+    // 8 s geometry) in one launch with the GPU to itself: beside the modulation GEMM they starved
+    // for L2-to-SM bandwidth and held SMs that the next GEMM's CTAs needed
+    p.add(Op{[jb, nmj, H, nbm, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, nbm, bfl, s); }, 2, 0,
+             "adaln_gemv"});
     if (tp) {
         const size_t sH = (size_t) H, sTH = (size_t) T * H;
         p.tap("t_emb", te, sH * 4, [sH](const std::vector<uint8_t> & raw, int, std::vector<float> & out) {
@@ -1127,7 +1124,6 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // each phase of the block is one launch over all three streams' rows (TSN_NO_GROUP=1 selects
     // the three-stream schedule, for comparison).
     const bool grouped = std::getenv("TSN_NO_GROUP") == nullptr;
-    p.wait(e_gemv);
     // taps of the first joint block: its text operand and q/k/v, then its attention outputs
     auto tap_qkv = [&](Plan & p) {
         p.tap("text_xn", xn_t, (size_t) B * TS * H * 2, cvt_f16_arm((size_t) TS * H));
