@@ -114,6 +114,36 @@ def test_tile_table_round_trip(dev, tiny_gguf):
     assert rel_l2(c, a) < 1e-5
 
 
+def test_pair_kernel_tiles_vs_oracle(dev, tiny_gguf, monkeypatch):
+    """The CTA-pair GEMM (tile code 2000 + NT, only ever picked by the autotuner) pinned on every
+    GEMM it can serve, without and with K slices: the flow stays within the gate of the CPU oracle,
+    and its f32 output through the TMA store view equals the per-lane store epilogue bit for bit."""
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    orc = O.Oracle(tiny_gguf)
+    refs = [orc.forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"], inp[f"text_pp_{sfx}"],
+                        inp[f"gcmlp_{sfx}"]) for sfx in ("cond", "unc")]
+    for slices in (1, 2):
+        flows = []
+        for tma in (True, False):
+            if tma:
+                monkeypatch.delenv("TSN_NO_TMA_OUT", raising=False)
+            else:
+                monkeypatch.setenv("TSN_NO_TMA_OUT", "1")
+            m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+            t = m.tiles().copy()
+            t[:, 1], t[:, 2] = 2064, slices
+            m.set_tiles(t)
+            assert (m.tiles()[:, 1] == 2064).any(), "no GEMM took the pair tile"
+            flow = np.zeros((2, T, 64), np.float32)
+            m.forward(0.5, flow)
+            for arm in (0, 1):
+                assert rel_l2(flow[arm], refs[arm]) < FLOW_TOL, (slices, tma, arm)
+            flows.append(flow)
+        assert np.array_equal(flows[0], flows[1]), f"TMA-store and per-lane epilogues differ (K slices {slices})"
+    monkeypatch.delenv("TSN_NO_TMA_OUT", raising=False)
+
+
 def test_synthetic_device_weights_equal_file(dev, tiny_gguf):
     T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
     inp = make_inputs(T, C, TS, TINY["H"])

@@ -72,6 +72,19 @@ bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool make_out_map_f32(CUtensorMap * m, void * base, uint64_t N, uint64_t rows, uint64_t B, uint64_t Z, uint64_t ldo,
+                      uint64_t out_bs, uint64_t z_stride) {
+    if (!encoder() || ((uintptr_t) base & 15) || ldo < N || (ldo * 4) % 16 || (out_bs * 4) % 16 || (z_stride * 4) % 16 ||
+        !N || !rows || !B || !Z)
+        return false;
+    const cuuint64_t dims[4] = {N, rows, B, Z};
+    const cuuint64_t strides[3] = {ldo * 4, out_bs * 4, z_stride * 4};
+    const cuuint32_t box[4] = {32, 32, 1, 1};
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, base, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Pipeline depth: as many stages as fit in the 227 KB of shared memory a CTA may use (the qkv
 // epilogue also stages RoPE rows, which costs the 192-wide split tile one stage).
 constexpr int stages_for(int bn, bool split, int epi) {
@@ -136,7 +149,7 @@ size_t gemm2_smem_bytes(int nt, bool split) {
 }
 
 namespace {
-using Kernel2Fn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
+using Kernel2Fn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs);
 template <int NT, int EPI, bool SPLIT>
 Kernel2Fn pick2() {
     static_assert(Gemm2Smem<NT, stages2(NT, SPLIT), SPLIT>::TOTAL <= 232448, "smem budget");
@@ -428,7 +441,8 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
     if (g.pair_nt) {
         Kernel2Fn fn = gemm2_for(g.pair_nt, g.epi, g.split);
         if (!fn || g.grid.x % 2) return cudaErrorInvalidValue;
-        return launch_cl(fn, g.grid, dim3(192), g.smem, s, dim3(2, 1, 1), g.tb, g.ta, g.ta2, g.args);
+        return launch_cl(fn, g.grid, dim3(192), g.smem, s, dim3(2, 1, 1), g.tb, g.ta, g.ta2, g.args.tma_out ? g.to : g.tb,
+                         g.args);
     }
     if (g.persistent) {
         KernelFn fn = persistent_for(g.bn);

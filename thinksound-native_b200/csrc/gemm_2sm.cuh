@@ -38,7 +38,7 @@ struct Gemm2Smem {
 template <int NT, int EPI, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
 gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
-             const __grid_constant__ CUtensorMap tmX2, const GemmArgs a) {
+             const __grid_constant__ CUtensorMap tmX2, const __grid_constant__ CUtensorMap tmY, const GemmArgs a) {
     using L = Gemm2Smem<NT, STAGES, SPLIT>;
     static_assert(EPI == EPI_F32 || EPI == EPI_SWIGLU, "2-SM epilogues: f32 / partial f32, SwiGLU");
     extern __shared__ uint8_t smem_raw[];
@@ -137,6 +137,35 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
         if (tr && threadIdx.x == 0) tr[3] = global_ns();
         const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
         if constexpr (EPI == EPI_F32) {
+          static_assert(NT / 32 * 4096 * 4 <= STAGES * L::STAGE, "TMA output boxes must fit in the operand ring");
+          if (a.tma_out) {
+            // each 32-token chunk of this warp's 32 features goes to its own 4 KB box in shared memory
+            // (the operand ring is free: every MMA of the pair has completed) as [token][feature],
+            // 128-byte rows in the 128-byte swizzle (16-byte chunk j of row t at chunk j ^ (t & 7);
+            // a store instruction writes one token's 32 features, one per bank), then one TMA store
+            // writes the box; the stores drain while the next chunks are read from TMEM
+            const int f0 = n0 + warp * 32;
+            const float bl = a.bias && f0 + lane < a.N ? a.bias[f0 + lane] : 0.0f;
+            uint8_t * boxes = smem + warp * (NT / 32) * 4096;
+            const uint32_t chunk = (uint32_t) (lane >> 2), word = (uint32_t) (lane & 3) * 4;
+#pragma unroll 1
+            for (int c = 0; c < NT; c += 32) {
+                float v[32];
+                tmem_ld32(trow + c, v);
+                uint8_t * box = boxes + (c / 32) * 4096;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    *(float *) (box + j * 128 + ((chunk ^ (uint32_t) (j & 7)) << 4) + word) = v[j] + bl;
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0 && ok && f0 < a.N && t0 + c < a.rows) tma_store_4d(&tmY, box, f0, t0 + c, b, (int) blockIdx.z);
+            }
+            if (lane == 0) {
+                bulk_commit();
+                bulk_wait_read0();
+            }
+            __syncwarp();
+          } else {
             // this warp's 32 features x 32 tokens per chunk go through a padded smem block (the
             // operand ring is free: every MMA of the pair has completed), so that each store
             // instruction writes four tokens' 128-byte runs of 32 consecutive features
@@ -162,6 +191,7 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
                 }
                 __syncwarp();
             }
+          }
         } else {
             // SwiGLU: rows come in groups of 64 = [32 w1 | 32 w3], so warps (0,1) and (2,3) hold
             // matching w1 and w3 rows for output features g*32 + lane, g = (n0 + 64*pair) / 64.

@@ -69,6 +69,8 @@ struct GemmArgs {
     void * out2; long long ldo2, out2_lo;           // EPI_RESID_SNAKE / EPI_F32_SNAKE2: split f16 [rows][ldo2] (B = 1)
     int a_rows;                                     // rows per activation tile the A views load (0: 128; tile kernel,
                                                     // bt * bb = a_rows): rows past it hold stale data, never stored
+    int tma_out;                                    // EPI_F32 of the CTA-pair kernel: store through the output
+                                                    // tensor map (4-D {N, rows, B, K slice}, 32 x 32 f32 boxes)
 };
 
 // phase stamps per CTA when tracing: entry, setup done, first stage landed (MMA issuer),

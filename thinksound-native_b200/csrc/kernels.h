@@ -52,6 +52,7 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 // ---- GEMM / implicit conv (gemm.cu) ----
 struct GemmLaunch {
     CUtensorMap ta, ta2, tb, tb2; // A (hi), A lo half (split operands only), weights, weights' lo half (WS)
+    CUtensorMap to;               // f32 output view of the CTA-pair kernel when GemmArgs::tma_out
     GemmArgs args;
     dim3 grid;
     int bn = 0, epi = 0, ab_bf16 = 0;
@@ -67,6 +68,10 @@ bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t ro
 // Encode a 3-D TMA view {64, rows, 2} of a head-major [hi|lo][rows][64] f16 q/k/v buffer with a
 // {64, box_rows, 1} box (rows = B * NH * S_pad).
 bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows);
+// Encode a 4-D TMA view {N, rows, B, Z} of an f32 output out[z][b][t][n] (strides ldo, out_bs and
+// z_stride elements) with {32, 32, 1, 1} boxes of 128-byte rows in the 128-byte swizzle.
+bool make_out_map_f32(CUtensorMap * m, void * base, uint64_t N, uint64_t rows, uint64_t B, uint64_t Z, uint64_t ldo,
+                      uint64_t out_bs, uint64_t z_stride);
 // Encode a 2-D TMA view {K, N} of an [N][K] 16-bit weight matrix with a {64, bn} box.
 bool make_w_map(CUtensorMap * m, const void * base, uint64_t K, uint64_t N, uint32_t bn, int bf16);
 cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s);

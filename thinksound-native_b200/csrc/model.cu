@@ -671,6 +671,18 @@ struct Plan {
         add(op);
     }
     static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
+    // f32 output of the CTA-pair kernel through a TMA view (whole 128-byte rows per box; the
+    // per-lane stores of the staged epilogue remain behind TSN_NO_TMA_OUT=1, for comparison)
+    int bind_tma_out(const char * name, GemmLaunch & g, int rows) {
+        if (!g.pair_nt || g.epi != EPI_F32 || std::getenv("TSN_NO_TMA_OUT")) return TSN_OK;
+        GemmArgs & a = g.args;
+        const long long zs = a.part_stride ? a.part_stride : (long long) m.B * a.out_bs;
+        if (!make_out_map_f32(&g.to, a.out, (uint64_t) a.N, (uint64_t) rows, (uint64_t) m.B, g.grid.z, (uint64_t) a.ldo,
+                              (uint64_t) a.out_bs, (uint64_t) zs))
+            return fail(TSN_ERR_CUDA, std::string(name) + ": output tensor map encode failed");
+        a.tma_out = 1;
+        return TSN_OK;
+    }
 
     int out_f32(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * out, int ldo,
                 bool plain = false) {
@@ -688,6 +700,7 @@ struct Plan {
             g.smem = gemm_persistent_smem_bytes(g.bn);
             g.grid = dim3((unsigned) std::min(tiles, sms), 1, 1);
         }
+        if ((rc = bind_tma_out(name, g, rows))) return rc;
         push(name, g, fl(m.B, rows, W));
         return TSN_OK;
     }
@@ -714,6 +727,7 @@ struct Plan {
         g.args.out = ws; g.args.ldo = H; g.args.out_bs = (long long) rows * H;
         g.args.part_stride = (long long) m.B * rows * H;
         g.args.bias = nullptr;
+        if ((rc = bind_tma_out(name, g, rows))) return rc;
         push(name, g, fl(m.B, rows, W));
         ops.back().part_bytes = (double) g.args.part_stride * 4;
         Pending & pd = pend[res];

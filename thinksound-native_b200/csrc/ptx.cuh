@@ -83,6 +83,18 @@ __device__ __forceinline__ void tma_load_3d(void * dst, const CUtensorMap * m, u
         : "memory");
 }
 
+// TMA tensor store of a shared-memory box into a 4-D view, as one bulk async-group of this thread.
+// The box must have been written and made visible to the async proxy (fence_proxy_async_smem)
+// first; bulk_wait_read0() returns once every committed store has finished reading shared memory
+// (the writes reach global memory by the grid's completion).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap * m, const void * src, int c0, int c1, int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];"
+                 ::"l"((uint64_t) m), "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // 2-SM (cta_group::2) loads: the data lands in this CTA's shared memory, the transaction bytes are
 // counted on `bar_cluster` (a shared::cluster address: the pair leader's barrier). No multicast.
 __device__ __forceinline__ void tma_load_2d_cg2(void * dst, const CUtensorMap * m, uint32_t bar_cluster, int c0, int c1) {
