@@ -189,15 +189,17 @@ KernelFn persistent_for(int bn) {
     return nullptr;
 }
 
+using TileFn = void (*)(CUtensorMap, CUtensorMap, CUtensorMap, CUtensorMap, GemmArgs, int);
+
 template <int BN, int EPI, bool SPLIT>
-KernelFn pick() {
+TileFn pick() {
     constexpr int ST = stages_for(BN, SPLIT, EPI);
     static_assert(GemmSmem<BN, ST, SPLIT, EPI>::TOTAL <= 232448, "smem budget");
-    return (KernelFn) gemm_tc_kernel<BN, EPI, ST, SPLIT>;
+    return (TileFn) gemm_tc_kernel<BN, EPI, ST, SPLIT>;
 }
 
 template <int BN, bool SPLIT>
-KernelFn pick_epi(int epi) {
+TileFn pick_epi(int epi) {
     switch (epi) {
         case EPI_F32: return pick<BN, EPI_F32, SPLIT>();
         case EPI_F16: return pick<BN, EPI_F16, SPLIT>();
@@ -209,7 +211,7 @@ KernelFn pick_epi(int epi) {
     return nullptr;
 }
 
-KernelFn kernel_for(int bn, int epi, bool split) {
+TileFn kernel_for(int bn, int epi, bool split) {
     switch (bn) {
         case 64: return split ? pick_epi<64, true>(epi) : pick_epi<64, false>(epi);
         case 128: return split ? pick_epi<128, true>(epi) : pick_epi<128, false>(epi);
@@ -391,7 +393,7 @@ cudaError_t configure_gemm_kernels() {
     for (int split = 0; split < 2; ++split)
         for (int bn : {64, 128, 192, 256})
             for (int epi = 0; epi <= EPI_F16_GELUQ; ++epi) {
-                KernelFn fn = kernel_for(bn, epi, split != 0);
+                TileFn fn = kernel_for(bn, epi, split != 0);
                 if (!fn) continue;
                 cudaError_t e = cudaFuncSetAttribute((const void *) fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      (int) gemm_smem_bytes(bn, split != 0, epi));
@@ -449,11 +451,11 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
         if (!fn || g.epi != EPI_F32 || !g.split || g.args.splits != 1) return cudaErrorInvalidValue;
         return launch_ex(fn, g.grid, dim3(192), g.smem, s, 1u, g.ta, g.ta2, g.tb, g.args, g.ab_bf16);
     }
-    KernelFn fn = kernel_for(g.bn, g.epi, g.split);
+    TileFn fn = kernel_for(g.bn, g.epi, g.split);
     if (!fn) return cudaErrorInvalidValue;
     // split-K: the K slices of one output tile form a cluster along grid.z
     return launch_ex(fn, g.grid, dim3(192), g.smem, s, g.args.splits > 1 ? (unsigned) g.args.splits : 1u,
-                     g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args, g.ab_bf16);
+                     g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args.tma_out ? g.to : g.tb, g.args, g.ab_bf16);
 }
 
 cudaError_t launch_gemm_group(const GroupLaunch & g, cudaStream_t s) {
@@ -528,7 +530,7 @@ int gemm_cluster_capacity(int bn, int epi, bool split, int cluster) {
 }
 
 int cluster_capacity_uncached(int bn, int epi, bool split, int cluster) {
-    KernelFn fn = kernel_for(bn, epi, split);
+    TileFn fn = kernel_for(bn, epi, split);
     if (!fn) return 0;
     if (cluster <= 1) {
         int per_sm = 0, sms = 0, dev = 0;

@@ -69,7 +69,7 @@ struct GemmArgs {
     void * out2; long long ldo2, out2_lo;           // EPI_RESID_SNAKE / EPI_F32_SNAKE2: split f16 [rows][ldo2] (B = 1)
     int a_rows;                                     // rows per activation tile the A views load (0: 128; tile kernel,
                                                     // bt * bb = a_rows): rows past it hold stale data, never stored
-    int tma_out;                                    // EPI_F32 of the CTA-pair kernel: store through the output
+    int tma_out;                                    // EPI_F32 without a split-K cluster: store through the output
                                                     // tensor map (4-D {N, rows, B, K slice}, 32 x 32 f32 boxes)
 };
 
@@ -290,7 +290,8 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
 template <int BN, int EPI, int STAGES, bool SPLIT, bool WS = false>
 __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtensorMap * tmA2, const CUtensorMap * tmB,
                                           const GemmArgs & a, const int ab_bf16, const int mi, const int ni, const int z,
-                                          const int cta, const CUtensorMap * tmB2 = nullptr) {
+                                          const int cta, const CUtensorMap * tmB2 = nullptr,
+                                          const CUtensorMap * tmO = nullptr) {
     using L = GemmSmem<BN, STAGES, SPLIT, EPI, WS>;
     static_assert(!WS || SPLIT, "split weights go with a split A operand");
     extern __shared__ uint8_t smem_raw[];
@@ -413,7 +414,45 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
         const int r = warp * 32 + lane;
         if (tr && r == 0) tr[3] = global_ns();
         const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
-        if (a.splits == 1) {
+        bool tma_done = false;
+        if constexpr (EPI == EPI_F32) {
+            if (a.splits == 1 && a.tma_out && tmO) {
+                static_assert(BN / 32 * 4096 * 4 <= STAGES * L::STAGE, "TMA output boxes must fit in the operand ring");
+                // each 32-column unit of the warp's 32 rows goes to its own 4 KB box in shared memory
+                // (the operand ring is free: every TMA load was consumed and every MMA has completed),
+                // a thread's row as 128 bytes in the 128-byte swizzle (16-byte chunk j at j ^ (row & 7)),
+                // then one TMA store writes the box and drains while the next unit is read from TMEM.
+                // The warp's rows are consecutive times of one arm: the host binds the view only when
+                // bt is a multiple of 32.
+                const int rw = warp * 32, bw = b0 + rw / a.bt, tw = t0 + rw % a.bt;
+                uint8_t * boxes = smem + warp * (BN / 32) * 4096;
+#pragma unroll 1
+                for (int u = 0; u < BN / 32; ++u) {
+                    float v[32];
+                    tmem_ld32(trow + u * 32, v);
+                    if (ec.bias) {
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] += ec.bias[u * 32 + e];
+                    }
+                    uint8_t * row = boxes + u * 4096 + lane * 128;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        *(float4 *) (row + ((q ^ (lane & 7)) << 4)) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && ok && tw < a.rows && bw < a.B && n0 + u * 32 < a.N)
+                        tma_store_4d(tmO, boxes + u * 4096, n0 + u * 32, tw, bw, z);
+                }
+                if (lane == 0) {
+                    bulk_commit();
+                    bulk_wait_read0();
+                }
+                __syncwarp();
+                tma_done = true;
+            }
+        }
+        if (tma_done) {
+        } else if (a.splits == 1) {
             auto load_tmem = [&](int c, float * v) { tmem_ld32(trow + c, v); };
 #pragma unroll 1
             for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, ec, r, u, n0, t0, b0, z, ok, load_tmem);
@@ -486,12 +525,13 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
 template <int BN, int EPI, int STAGES, bool SPLIT>
 __global__ void __launch_bounds__(192, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
-               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ GemmArgs a, const int ab_bf16) {
+               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmO,
+               const __grid_constant__ GemmArgs a, const int ab_bf16) {
     // with m_fast the CTAs that share a weight tile are launched next to each other, so a weight
     // matrix larger than L2 is streamed from HBM once rather than once per M tile
     const int mi = a.m_fast ? blockIdx.x : blockIdx.y, ni = a.m_fast ? blockIdx.y : blockIdx.x;
     const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
-    gemm_tile<BN, EPI, STAGES, SPLIT>(&tmA, &tmA2, &tmB, a, ab_bf16, mi, ni, (int) blockIdx.z, cta);
+    gemm_tile<BN, EPI, STAGES, SPLIT>(&tmA, &tmA2, &tmB, a, ab_bf16, mi, ni, (int) blockIdx.z, cta, nullptr, &tmO);
 }
 
 // Split activations and split weights (the VAE decoder's f32 weights as W_hi + W_lo f16): grid
@@ -518,6 +558,7 @@ gemm_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 constexpr int MAX_GROUP = 3;
 struct GroupMaps {
     CUtensorMap a[MAX_GROUP], a2[MAX_GROUP], b[MAX_GROUP];
+    CUtensorMap o[MAX_GROUP];    // f32 output views of members with GemmArgs::tma_out
 };
 struct GroupArgs {
     GemmArgs p[MAX_GROUP];
@@ -536,7 +577,7 @@ gemm_tc_group(const __grid_constant__ GroupMaps maps, const __grid_constant__ Gr
     const int l = x - (q ? g.cta_end[q - 1] : 0);
     const int S = g.slices[q], z = l % S, tile = l / S;
     const int mi = tile % g.m_tiles[q], ni = tile / g.m_tiles[q];
-    gemm_tile<BN, EPI, STAGES, SPLIT>(&maps.a[q], &maps.a2[q], &maps.b[q], g.p[q], ab_bf16, mi, ni, z, x);
+    gemm_tile<BN, EPI, STAGES, SPLIT>(&maps.a[q], &maps.a2[q], &maps.b[q], g.p[q], ab_bf16, mi, ni, z, x, nullptr, &maps.o[q]);
 }
 
 // ------------------------------------------------------------------------------------------

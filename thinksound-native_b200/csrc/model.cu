@@ -671,11 +671,14 @@ struct Plan {
         add(op);
     }
     static double fl(int B, int rows, const Lin & W) { return 2.0 * B * rows * (double) W.N * W.K_in * W.taps; }
-    // f32 output of the CTA-pair kernel through a TMA view (whole 128-byte rows per box; the
-    // per-lane stores of the staged epilogue remain behind TSN_NO_TMA_OUT=1, for comparison)
+    // f32 output (tile kernel without a split-K cluster, or the CTA-pair kernel) through a TMA view:
+    // whole 128-byte rows per box (the per-lane store epilogues remain behind TSN_NO_TMA_OUT=1,
+    // for comparison)
     int bind_tma_out(const char * name, GemmLaunch & g, int rows) {
-        if (!g.pair_nt || g.epi != EPI_F32 || std::getenv("TSN_NO_TMA_OUT")) return TSN_OK;
         GemmArgs & a = g.args;
+        if (g.epi != EPI_F32 || g.persistent || std::getenv("TSN_NO_TMA_OUT")) return TSN_OK;
+        // the tile kernel: a warp's 32 rows must be consecutive times of one arm, and no cluster
+        if (!g.pair_nt && (a.splits != 1 || a.bt % 32)) return TSN_OK;
         const long long zs = a.part_stride ? a.part_stride : (long long) m.B * a.out_bs;
         if (!make_out_map_f32(&g.to, a.out, (uint64_t) a.N, (uint64_t) rows, (uint64_t) m.B, g.grid.z, (uint64_t) a.ldo,
                               (uint64_t) a.out_bs, (uint64_t) zs))
@@ -826,12 +829,20 @@ struct Plan {
         G.cluster = partial ? 1 : s;
         int end = 0, n = 0;
         std::string kbs;
+        const bool tma_out = G.epi == EPI_F32 && G.cluster == 1 && !std::getenv("TSN_NO_TMA_OUT");
         for (int q : ord) {
             const GemmLaunch & g = gl[q];
             G.maps.a[n] = g.ta;
             G.maps.a2[n] = g.split ? g.ta2 : g.ta;
             G.maps.b[n] = g.tb;
             G.args.p[n] = g.args;
+            G.args.p[n].tma_out = 0;
+            const GemmArgs & ga = g.args;
+            if (tma_out && ga.bt % 32 == 0 &&
+                make_out_map_f32(&G.maps.o[n], ga.out, (uint64_t) ga.N, (uint64_t) ga.rows, (uint64_t) ga.B, (uint64_t) zs[q],
+                                 (uint64_t) ga.ldo, (uint64_t) ga.out_bs,
+                                 (uint64_t) (ga.part_stride ? ga.part_stride : (long long) ga.B * ga.out_bs)))
+                G.args.p[n].tma_out = 1;
             G.args.slices[n] = zs[q];
             G.args.m_tiles[n] = (int) g.grid.x;
             end += (int) (g.grid.x * g.grid.y) * zs[q];
