@@ -8,9 +8,9 @@
 //                    f16 A operand of the next GEMM directly; first applies the gated residual
 //                    update of the GEMM before it (gate_add, ops_conv.metal:146-154) from that
 //                    GEMM's split-K partial sums.
-//   gemv_kernel      batched gemv_h (shaders/gemm_attn.metal:48-64): each warp two rows per pass
-//                    with all their 16-B weight loads in flight, every CFG arm (up to 8) from one
-//                    weight read.
+//   gemv_kernel      batched gemv_h (shaders/gemm_attn.metal:48-64): two blocks per SM walk the
+//                    rows, each warp two rows per pass with the next pass's 16-B weight loads in
+//                    flight while it sums, every CFG arm (up to 8) from one weight read.
 //   cond_kernel      the per-forward conditioning adds and SiLUs (src/dit_fwd.cpp:131-140) and
 //                    the stream restarts (src/dit_fwd.cpp:166-167) in one pass.
 //   cfg_euler_kernel cfg_euler (shaders/ops_conv.metal:194-201) reading dt from the schedule.
@@ -472,91 +472,134 @@ __device__ __forceinline__ void cvt8(uint4 w, int bf16, float * f) {
         f[e] = bf16 ? __uint_as_float((uint32_t) h[e] << 16) : __half2float(__ushort_as_half(h[e]));
 }
 
-// Each warp takes R consecutive rows of one job per pass and loads all of their 16-byte weight
-// chunks (R x GEMV_CHUNKS per lane, K up to 1024 per pass) before using any, the first pass before
-// the wait on the upstream kernel (weights do not depend on it). The grid covers every row (a
-// grid-stride loop only guards oversized launches). A lane sums its chunks in k order, and a warp
-// adds the 32 lane sums in a fixed butterfly, so a row's result does not depend on the grid or on R.
-// The launch is HBM-bound only when it has the GPU to itself: beside a tcgen05 GEMM, whose tile
-// loads already fill each SM's share of the L2 fabric, its loads starve (and slow the GEMM), so
-// the forward runs it in line, not on a side stream.
+// A grid of up to two 8-warp blocks per SM walks the (job, row) slots; each warp takes R
+// consecutive rows of one job per pass and keeps two passes of weights in registers: while it
+// sums pass p it already has every 16-byte weight load of pass p + 1 in flight (R x GEMV_CHUNKS
+// per lane, K <= 256 x GEMV_CHUNKS), so each warp always has ~8 KB of HBM reads outstanding. The
+// jobs travel as a kernel parameter, so no dependent global load precedes the first weight loads,
+// which are issued before the wait on the upstream kernel (weights do not depend on it). A lane
+// sums its chunks in k order and a warp adds the 32 lane sums in a fixed butterfly, so a row's
+// result does not depend on the grid or on R. The launch is HBM-bound only when it has the GPU to
+// itself: beside a tcgen05 GEMM, whose tile loads already fill each SM's share of the L2-to-SM
+// fabric, its loads starve (and slow the GEMM), so the forward runs it in line.
 constexpr int GEMV_CHUNKS = 4;
 
-template <int NB, int R>
-__global__ void __launch_bounds__(256) gemv_kernel(const GemvJob * jobs, int njobs, int max_n, int ab_bf16) {
-    pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    // slots s = q * max_n + n; max_n is a multiple of R, so a warp's R rows share one job
-    const long long slots = (long long) njobs * max_n;
-    const long long stride = (long long) gridDim.x * 8 * R;
-    bool waited = false;
-    for (long long s0 = ((long long) blockIdx.x * 8 + (threadIdx.x >> 5)) * R; s0 < slots; s0 += stride) {
-        const GemvJob & j = jobs[s0 / max_n];
-        const int n0 = (int) (s0 % max_n), K = j.K;
-        if (n0 >= j.N) continue;
-        const int rows = min(R, j.N - n0);
-        const uint16_t * w = (const uint16_t *) j.W + (size_t) n0 * K;
-        float acc[R][NB];
+template <int R>
+struct GemvPass {
+    uint4 w[R][GEMV_CHUNKS];
+};
+
+template <int R>
+__device__ __forceinline__ void gemv_issue(const GemvBatch & jb, long long s, long long slots, int max_n, int lane,
+                                           GemvPass<R> & p) {
+    const bool in = s < slots;
+    const GemvJob & j = jb.j[in ? (int) (s / max_n) : 0];
+    const int n0 = in ? (int) (s % max_n) : 0, K = j.K;
+    const int rows = in && n0 < j.N ? min(R, j.N - n0) : 0;
+    const uint16_t * w = (const uint16_t *) j.W + (size_t) n0 * K;
 #pragma unroll
-        for (int r = 0; r < R; ++r)
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int bb = 0; bb < NB; ++bb) acc[r][bb] = 0.0f;
-        for (int k0 = 0; k0 < K; k0 += 256 * GEMV_CHUNKS) {
-            uint4 wr[R][GEMV_CHUNKS];
-#pragma unroll
-            for (int r = 0; r < R; ++r)
-#pragma unroll
-                for (int c = 0; c < GEMV_CHUNKS; ++c) {
-                    const int k = k0 + c * 256 + lane * 8;
-                    wr[r][c] = r < rows && k < K ? __ldg((const uint4 *) (w + (size_t) r * K + k)) : make_uint4(0u, 0u, 0u, 0u);
-                }
-            if (!waited) { pdl_wait(); waited = true; }
-            const float * x = j.x + (j.x_step ? (long long) (*j.x_step) * j.x_step_stride : 0);
-#pragma unroll
-            for (int r = 0; r < R; ++r)
-#pragma unroll
-                for (int c = 0; c < GEMV_CHUNKS; ++c) {
-                    const int k = k0 + c * 256 + lane * 8;
-                    if (k >= K) break;
-                    float wf[8];
-                    cvt8(wr[r][c], ab_bf16, wf);
-#pragma unroll
-                    for (int bb = 0; bb < NB; ++bb) {
-                        if (bb >= j.nb) break;
-                        const float * xb = x + bb * j.x_bs + k;
-                        const float4 x0 = *(const float4 *) xb, x1 = *(const float4 *) (xb + 4);
-                        acc[r][bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
-                                      wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
-                    }
-                }
+        for (int c = 0; c < GEMV_CHUNKS; ++c) {
+            const int k = c * 256 + lane * 8;
+            p.w[r][c] = r < rows && k < K ? __ldg((const uint4 *) (w + (size_t) r * K + k)) : make_uint4(0u, 0u, 0u, 0u);
         }
+}
+
+template <int NB, int R>
+__device__ __forceinline__ void gemv_sum(const GemvBatch & jb, long long s, int max_n, int lane, int ab_bf16,
+                                         const GemvPass<R> & p) {
+    const GemvJob & j = jb.j[(int) (s / max_n)];
+    const int n0 = (int) (s % max_n), K = j.K;
+    if (n0 >= j.N) return;
+    const int rows = min(R, j.N - n0);
+    const float * x = j.x + (j.x_step ? (long long) (*j.x_step) * j.x_step_stride : 0);
+    float acc[R][NB];
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-            if (r >= rows) break;
+    for (int r = 0; r < R; ++r)
 #pragma unroll
-            for (int bb = 0; bb < NB; ++bb) {
-                if (bb >= j.nb) break;
-                float val = acc[r][bb];
+        for (int bb = 0; bb < NB; ++bb) acc[r][bb] = 0.0f;
+    // each x chunk is loaded once per pass and used for all R rows (a row still adds its chunks
+    // in k order)
 #pragma unroll
-                for (int off = 16; off; off >>= 1) val += __shfl_xor_sync(0xffffffffu, val, off);
-                if (lane == 0) {
-                    if (j.bias) val += j.bias[n0 + r];
-                    if (j.act == 1) val = val / (1.0f + expf(-val));
-                    j.y[bb * j.y_bs + n0 + r] = val;
-                }
+    for (int c = 0; c < GEMV_CHUNKS; ++c) {
+        const int k = c * 256 + lane * 8;
+        if (k >= K) break;
+#pragma unroll
+        for (int bb = 0; bb < NB; ++bb) {
+            if (bb >= j.nb) break;
+            const float * xb = x + bb * j.x_bs + k;
+            const float4 x0 = *(const float4 *) xb, x1 = *(const float4 *) (xb + 4);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                float wf[8];
+                cvt8(p.w[r][c], ab_bf16, wf);
+                acc[r][bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
+                              wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        if (r >= rows) break;
+#pragma unroll
+        for (int bb = 0; bb < NB; ++bb) {
+            if (bb >= j.nb) break;
+            float val = acc[r][bb];
+#pragma unroll
+            for (int off = 16; off; off >>= 1) val += __shfl_xor_sync(0xffffffffu, val, off);
+            if (lane == 0) {
+                if (j.bias) val += j.bias[n0 + r];
+                if (j.act == 1) val = val / (1.0f + expf(-val));
+                j.y[bb * j.y_bs + n0 + r] = val;
             }
         }
     }
 }
 
-cudaError_t launch_gemv(const GemvJob * jobs_dev, int njobs, int max_n, int nb, int ab_bf16, cudaStream_t s) {
-    if (njobs < 1 || max_n < 1 || max_n % 2 || nb < 1 || nb > 8) return cudaErrorInvalidValue;
+template <int NB, int R>
+__global__ void __launch_bounds__(256) gemv_kernel(const __grid_constant__ GemvBatch jb, int njobs, int max_n, int ab_bf16) {
+    pdl_trigger();
+    const int lane = threadIdx.x & 31;
+    // slots s = q * max_n + n; max_n is a multiple of R, so a warp's R rows share one job
     const long long slots = (long long) njobs * max_n;
-    const dim3 grid((unsigned) std::min<long long>((slots + 15) / 16, 1 << 20));   // 8 warps x R = 2 rows
-    if (nb == 1) return launch_ex(gemv_kernel<1, 2>, grid, dim3(256), 0, s, 1u, jobs_dev, njobs, max_n, ab_bf16);
-    if (nb == 2) return launch_ex(gemv_kernel<2, 2>, grid, dim3(256), 0, s, 1u, jobs_dev, njobs, max_n, ab_bf16);
-    if (nb <= 4) return launch_ex(gemv_kernel<4, 2>, grid, dim3(256), 0, s, 1u, jobs_dev, njobs, max_n, ab_bf16);
-    return launch_ex(gemv_kernel<8, 2>, grid, dim3(256), 0, s, 1u, jobs_dev, njobs, max_n, ab_bf16);
+    const long long stride = (long long) gridDim.x * 8 * R;
+    long long s = ((long long) blockIdx.x * 8 + (threadIdx.x >> 5)) * R;
+    GemvPass<R> pa, pb;
+    gemv_issue<R>(jb, s, slots, max_n, lane, pa);
+    pdl_wait();
+    for (;;) {   // two passes per trip, so each register set keeps a fixed name
+        if (s >= slots) break;
+        gemv_issue<R>(jb, s + stride, slots, max_n, lane, pb);
+        gemv_sum<NB, R>(jb, s, max_n, lane, ab_bf16, pa);
+        s += stride;
+        if (s >= slots) break;
+        gemv_issue<R>(jb, s + stride, slots, max_n, lane, pa);
+        gemv_sum<NB, R>(jb, s, max_n, lane, ab_bf16, pb);
+        s += stride;
+    }
+}
+
+cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, cudaStream_t s) {
+    if (njobs < 1 || max_n < 1 || max_n % 2 || nb < 1 || nb > 8 || sms < 1) return cudaErrorInvalidValue;
+    for (int q0 = 0; q0 < njobs; q0 += GEMV_MAX_JOBS) {
+        const int n = std::min(GEMV_MAX_JOBS, njobs - q0);
+        GemvBatch jb{};
+        for (int q = 0; q < n; ++q) {
+            jb.j[q] = jobs[q0 + q];
+            if (jb.j[q].K > 256 * GEMV_CHUNKS || jb.j[q].K % 8 || jb.j[q].nb > nb || jb.j[q].N > max_n)
+                return cudaErrorInvalidValue;
+        }
+        const long long slots = (long long) n * max_n;
+        const dim3 grid((unsigned) std::min<long long>((slots + 15) / 16, 2LL * sms));   // 8 warps x R = 2 rows
+        cudaError_t e;
+        if (nb == 1) e = launch_ex(gemv_kernel<1, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
+        else if (nb == 2) e = launch_ex(gemv_kernel<2, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
+        else if (nb <= 4) e = launch_ex(gemv_kernel<4, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
+        else e = launch_ex(gemv_kernel<8, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 // =============================================================================== conditioning

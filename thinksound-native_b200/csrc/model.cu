@@ -467,7 +467,6 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
     ALLOC(tap_gc, B * H * 4);
     ALLOC(tap_extc, B * T * H * 4);
     n_mod_jobs = 2 * (int) NJ;
-    ALLOC(jobs, (size_t) (2 + n_mod_jobs) * sizeof(GemvJob));
 #undef ALLOC
     // RoPE tables: rope_pairs (shaders/ops_conv.metal:156-169) with positions 0..rows-1
     // (src/dit_fwd.cpp:171-179); clip positions are scaled by T/C (src/dit_fwd.cpp:170).
@@ -491,7 +490,8 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
     // GEMV jobs: t_embed.mlp.0 (+silu) from the step's temb row, t_embed.mlp.2, then the clip and
     // text adaLN modulations of every joint block from silu(global_c) (src/dit_fwd.cpp:122-128, 195-207)
     {
-        std::vector<GemvJob> j(2 + n_mod_jobs);
+        std::vector<GemvJob> & j = jobs;
+        j.assign(2 + n_mod_jobs, GemvJob{});
         j[0] = GemvJob{te0.w, te0.b, temb_tab, 0, step, (long long) H, te_h, 0, (int) H, (int) H, 1, 1};
         j[1] = GemvJob{te2.w, te2.b, te_h, 0, nullptr, 0, te, 0, (int) H, (int) H, 1, 0};
         for (size_t i = 0; i < NJ; ++i) {
@@ -500,7 +500,6 @@ int Model::prepare(int T_, int C_, int TS_, int B_) {
             j[3 + 2 * i] = GemvJob{jt[i].ada.w, jt[i].ada.b, gc_silu, (long long) H, nullptr, 0,
                                    modt + i * B * 6 * H, (long long) (6 * H), jt[i].ada.N, (int) H, B, 0};
         }
-        CKR(cudaMemcpy(jobs, j.data(), j.size() * sizeof(GemvJob), cudaMemcpyHostToDevice));
     }
     prepared = true;
     int rc = build_ops(ops_fwd, 0, 0.0f);
@@ -1112,11 +1111,15 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     const long long lat_mod_bs = (long long) T * NA;
     int rc;
     // t-embedding MLP and conditioning                           src/dit_fwd.cpp:111-140
-    GemvJob * jb = jobs;
+    const std::vector<GemvJob> jb = jobs;
     const int nmj = n_mod_jobs;
+    int sms = 148;
+    CKR(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev->ordinal));
     const int bfl = bf16, nbm = B;
-    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb, 1, H, 1, bfl, s); }, 2, 0, "t_embed.0"});
-    ops.push_back(Op{[jb, H, bfl](cudaStream_t s) { return launch_gemv(jb + 1, 1, H, 1, bfl, s); }, 2, 0, "t_embed.2"});
+    ops.push_back(Op{[jb, H, sms, bfl](cudaStream_t s) { return launch_gemv(jb.data(), 1, H, 1, sms, bfl, s); }, 2, 0,
+                     "t_embed.0"});
+    ops.push_back(Op{[jb, H, sms, bfl](cudaStream_t s) { return launch_gemv(jb.data() + 1, 1, H, 1, sms, bfl, s); }, 2, 0,
+                     "t_embed.2"});
     CondArgs ca{te, gcmlp, sync_gather, clip_pp, text_pp, x, gc_silu, extc16, clip_s, text_s, x16,
                 tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L,
                 (long long) B * T * H, (long long) B * T * L, A};
@@ -1124,7 +1127,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // the clip/text modulations of every joint block (HBM-bound GEMVs, ~160 MB of weights at the
     // 8 s geometry) in one launch with the GPU to itself: beside the modulation GEMM they starved
     // for L2-to-SM bandwidth and held SMs that the next GEMM's CTAs needed
-    p.add(Op{[jb, nmj, H, nbm, bfl](cudaStream_t s) { return launch_gemv(jb + 2, nmj, 6 * H, nbm, bfl, s); }, 2, 0,
+    p.add(Op{[jb, nmj, H, nbm, sms, bfl](cudaStream_t s) { return launch_gemv(jb.data() + 2, nmj, 6 * H, nbm, sms, bfl, s); }, 2, 0,
              "adaln_gemv"});
     if (tp) {
         const size_t sH = (size_t) H, sTH = (size_t) T * H;

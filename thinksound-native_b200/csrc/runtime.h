@@ -124,7 +124,7 @@ struct Model {
     float * temb_tab = nullptr, * dt_tab = nullptr;
     int * step = nullptr;
     int max_steps = 1024;
-    GemvJob * jobs = nullptr;
+    std::vector<GemvJob> jobs;     // t-embed MLP, then the clip/text modulations of every joint block
     int n_mod_jobs = 0;
     float * tap_gc = nullptr, * tap_extc = nullptr;
     std::map<std::string, TapBuf> taps;
