@@ -8,9 +8,9 @@
 //                    f16 A operand of the next GEMM directly; first applies the gated residual
 //                    update of the GEMM before it (gate_add, ops_conv.metal:146-154) from that
 //                    GEMM's split-K partial sums.
-//   gemv_kernel      batched gemv_h (shaders/gemm_attn.metal:48-64): two blocks per SM walk the
-//                    rows, each warp two rows per pass with the next pass's 16-B weight loads in
-//                    flight while it sums, every CFG arm (up to 8) from one weight read.
+//   gemv_kernel      batched gemv_h (shaders/gemm_attn.metal:48-64): four-warp blocks walk the
+//                    rows, each warp two rows per pass staged by bulk copies into a two-stage
+//                    shared-memory ring, every CFG arm (up to 8) from one weight read.
 //   cond_kernel      the per-forward conditioning adds and SiLUs (src/dit_fwd.cpp:131-140) and
 //                    the stream restarts (src/dit_fwd.cpp:166-167) in one pass.
 //   cfg_euler_kernel cfg_euler (shaders/ops_conv.metal:194-201) reading dt from the schedule.
@@ -472,131 +472,149 @@ __device__ __forceinline__ void cvt8(uint4 w, int bf16, float * f) {
         f[e] = bf16 ? __uint_as_float((uint32_t) h[e] << 16) : __half2float(__ushort_as_half(h[e]));
 }
 
-// A grid of up to two 8-warp blocks per SM walks the (job, row) slots; each warp takes R
-// consecutive rows of one job per pass and keeps two passes of weights in registers: while it
-// sums pass p it already has every 16-byte weight load of pass p + 1 in flight (R x GEMV_CHUNKS
-// per lane, K <= 256 x GEMV_CHUNKS), so each warp always has ~8 KB of HBM reads outstanding. The
-// jobs travel as a kernel parameter, so no dependent global load precedes the first weight loads,
-// which are issued before the wait on the upstream kernel (weights do not depend on it). A lane
-// sums its chunks in k order and a warp adds the 32 lane sums in a fixed butterfly, so a row's
-// result does not depend on the grid or on R. The launch is HBM-bound only when it has the GPU to
-// itself: beside a tcgen05 GEMM, whose tile loads already fill each SM's share of the L2-to-SM
-// fabric, its loads starve (and slow the GEMM), so the forward runs it in line.
-constexpr int GEMV_CHUNKS = 4;
+// Blocks of four warps walk the (job, row) slots; each warp takes R = 2 consecutive rows of one
+// job per pass. Lane 0 brings a pass's weight rows (one contiguous 4 KB run at K = 1024) into the
+// warp's shared-memory stage with one bulk copy that completes on the stage's mbarrier; with
+// GEMV_STAGES stages per warp the next passes' copies are in flight while the warp sums the
+// current one from shared memory, and no registers hold weights in flight, so many warps fit on an
+// SM. The first copies are issued before the wait on the upstream kernel (weights do not depend
+// on it); the jobs travel as a kernel parameter. Each x chunk is loaded once per pass and used for
+// both rows. A lane sums its chunks in k order and a warp adds the 32 lane sums in a fixed
+// butterfly, so a row's result does not depend on the grid. Every wait is bounded (a timeout sets
+// the device error word). The launch is HBM-bound only when it has the GPU to itself: beside a
+// tcgen05 GEMM, whose tile loads already fill each SM's share of the L2-to-SM fabric, its loads
+// starve (and slow the GEMM), so the forward runs it in line.
+constexpr int GEMV_CHUNKS = 4;                          // K <= 256 x GEMV_CHUNKS
+constexpr int GEMV_R = 2, GEMV_WARPS = 4, GEMV_STAGES = 2;
+constexpr int GEMV_STAGE_BYTES = GEMV_R * 256 * GEMV_CHUNKS * 2;   // 4 KB
 
-template <int R>
-struct GemvPass {
-    uint4 w[R][GEMV_CHUNKS];
-};
-
-template <int R>
-__device__ __forceinline__ void gemv_issue(const GemvBatch & jb, long long s, long long slots, int max_n, int lane,
-                                           GemvPass<R> & p) {
-    const bool in = s < slots;
-    const GemvJob & j = jb.j[in ? (int) (s / max_n) : 0];
-    const int n0 = in ? (int) (s % max_n) : 0, K = j.K;
-    const int rows = in && n0 < j.N ? min(R, j.N - n0) : 0;
-    const uint16_t * w = (const uint16_t *) j.W + (size_t) n0 * K;
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int c = 0; c < GEMV_CHUNKS; ++c) {
-            const int k = c * 256 + lane * 8;
-            p.w[r][c] = r < rows && k < K ? __ldg((const uint4 *) (w + (size_t) r * K + k)) : make_uint4(0u, 0u, 0u, 0u);
-        }
+// slot s of the batch: its job, first row and row count (0: nothing to load)
+__device__ __forceinline__ int gemv_rows(const GemvBatch & jb, long long s, long long slots, int max_n, int & q, int & n0) {
+    if (s >= slots) return 0;
+    q = (int) (s / max_n);
+    n0 = (int) (s % max_n);
+    return n0 < jb.j[q].N ? min(GEMV_R, jb.j[q].N - n0) : 0;
 }
 
-template <int NB, int R>
-__device__ __forceinline__ void gemv_sum(const GemvBatch & jb, long long s, int max_n, int lane, int ab_bf16,
-                                         const GemvPass<R> & p) {
-    const GemvJob & j = jb.j[(int) (s / max_n)];
-    const int n0 = (int) (s % max_n), K = j.K;
-    if (n0 >= j.N) return;
-    const int rows = min(R, j.N - n0);
-    const float * x = j.x + (j.x_step ? (long long) (*j.x_step) * j.x_step_stride : 0);
-    float acc[R][NB];
-#pragma unroll
-    for (int r = 0; r < R; ++r)
-#pragma unroll
-        for (int bb = 0; bb < NB; ++bb) acc[r][bb] = 0.0f;
-    // each x chunk is loaded once per pass and used for all R rows (a row still adds its chunks
-    // in k order)
-#pragma unroll
-    for (int c = 0; c < GEMV_CHUNKS; ++c) {
-        const int k = c * 256 + lane * 8;
-        if (k >= K) break;
-#pragma unroll
-        for (int bb = 0; bb < NB; ++bb) {
-            if (bb >= j.nb) break;
-            const float * xb = x + bb * j.x_bs + k;
-            const float4 x0 = *(const float4 *) xb, x1 = *(const float4 *) (xb + 4);
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                float wf[8];
-                cvt8(p.w[r][c], ab_bf16, wf);
-                acc[r][bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
-                              wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
-            }
-        }
-    }
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        if (r >= rows) break;
-#pragma unroll
-        for (int bb = 0; bb < NB; ++bb) {
-            if (bb >= j.nb) break;
-            float val = acc[r][bb];
-#pragma unroll
-            for (int off = 16; off; off >>= 1) val += __shfl_xor_sync(0xffffffffu, val, off);
-            if (lane == 0) {
-                if (j.bias) val += j.bias[n0 + r];
-                if (j.act == 1) val = val / (1.0f + expf(-val));
-                j.y[bb * j.y_bs + n0 + r] = val;
-            }
-        }
-    }
-}
-
-template <int NB, int R>
-__global__ void __launch_bounds__(256) gemv_kernel(const __grid_constant__ GemvBatch jb, int njobs, int max_n, int ab_bf16) {
+template <int NB>
+__global__ void __launch_bounds__(128) gemv_kernel(const __grid_constant__ GemvBatch jb, int njobs, int max_n, int ab_bf16,
+                                                   int * err) {
+    __shared__ __align__(128) uint8_t wbuf[GEMV_WARPS][GEMV_STAGES][GEMV_STAGE_BYTES];
+    __shared__ __align__(8) uint64_t bars[GEMV_WARPS][GEMV_STAGES];
+    __shared__ int abort_word;
     pdl_trigger();
-    const int lane = threadIdx.x & 31;
-    // slots s = q * max_n + n; max_n is a multiple of R, so a warp's R rows share one job
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const long long slots = (long long) njobs * max_n;
-    const long long stride = (long long) gridDim.x * 8 * R;
-    long long s = ((long long) blockIdx.x * 8 + (threadIdx.x >> 5)) * R;
-    GemvPass<R> pa, pb;
-    gemv_issue<R>(jb, s, slots, max_n, lane, pa);
+    const long long stride = (long long) gridDim.x * GEMV_WARPS * GEMV_R;
+    const long long s0 = ((long long) blockIdx.x * GEMV_WARPS + w) * GEMV_R;
+    if (threadIdx.x == 0) abort_word = 0;
+    if (lane == 0) {
+        for (int st = 0; st < GEMV_STAGES; ++st) mbar_init(&bars[w][st], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    volatile int * abort_flag = &abort_word;
+    auto issue = [&](long long s, int st) {   // lane 0
+        int q = 0, n0 = 0;
+        const int rows = gemv_rows(jb, s, slots, max_n, q, n0);
+        if (!rows) return;
+        const uint32_t bytes = (uint32_t) rows * (uint32_t) jb.j[q].K * 2u;
+        mbar_expect_tx(&bars[w][st], bytes);
+        bulk_load(wbuf[w][st], (const uint16_t *) jb.j[q].W + (size_t) n0 * jb.j[q].K, bytes, &bars[w][st]);
+    };
+    if (lane == 0)
+        for (int st = 0; st < GEMV_STAGES; ++st) issue(s0 + st * stride, st);
     pdl_wait();
-    for (;;) {   // two passes per trip, so each register set keeps a fixed name
+    uint32_t phase = 0;   // bit st: parity of stage st's next completion
+    bool ok = true;
+    for (int i = 0;; ++i) {
+        const long long s = s0 + (long long) i * stride;
         if (s >= slots) break;
-        gemv_issue<R>(jb, s + stride, slots, max_n, lane, pb);
-        gemv_sum<NB, R>(jb, s, max_n, lane, ab_bf16, pa);
-        s += stride;
-        if (s >= slots) break;
-        gemv_issue<R>(jb, s + stride, slots, max_n, lane, pa);
-        gemv_sum<NB, R>(jb, s, max_n, lane, ab_bf16, pb);
-        s += stride;
+        const int st = i % GEMV_STAGES;
+        int q = 0, n0 = 0;
+        const int rows = gemv_rows(jb, s, slots, max_n, q, n0);
+        if (rows) {
+            if (!mbar_wait(&bars[w][st], (phase >> st) & 1u, abort_flag, err, DEV_TIMEOUT_FULL)) { ok = false; break; }
+            phase ^= 1u << st;
+            const GemvJob & j = jb.j[q];
+            const int K = j.K;
+            const float * x = j.x + (j.x_step ? (long long) (*j.x_step) * j.x_step_stride : 0);
+            const uint8_t * wb = wbuf[w][st];
+            float acc[GEMV_R][NB];
+#pragma unroll
+            for (int r = 0; r < GEMV_R; ++r)
+#pragma unroll
+                for (int bb = 0; bb < NB; ++bb) acc[r][bb] = 0.0f;
+#pragma unroll
+            for (int c = 0; c < GEMV_CHUNKS; ++c) {
+                const int k = c * 256 + lane * 8;
+                if (k >= K) break;
+                uint4 wr[GEMV_R];
+#pragma unroll
+                for (int r = 0; r < GEMV_R; ++r)
+                    wr[r] = r < rows ? *(const uint4 *) (wb + ((size_t) r * K + k) * 2) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int bb = 0; bb < NB; ++bb) {
+                    if (bb >= j.nb) break;
+                    const float * xb = x + bb * j.x_bs + k;
+                    const float4 x0 = *(const float4 *) xb, x1 = *(const float4 *) (xb + 4);
+#pragma unroll
+                    for (int r = 0; r < GEMV_R; ++r) {
+                        float wf[8];
+                        cvt8(wr[r], ab_bf16, wf);
+                        acc[r][bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
+                                      wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
+                    }
+                }
+            }
+            __syncwarp();   // every lane has read the stage before lane 0 refills it
+#pragma unroll
+            for (int r = 0; r < GEMV_R; ++r) {
+                if (r >= rows) break;
+#pragma unroll
+                for (int bb = 0; bb < NB; ++bb) {
+                    if (bb >= j.nb) break;
+                    float val = acc[r][bb];
+#pragma unroll
+                    for (int off = 16; off; off >>= 1) val += __shfl_xor_sync(0xffffffffu, val, off);
+                    if (lane == 0) {
+                        if (j.bias) val += j.bias[n0 + r];
+                        if (j.act == 1) val = val / (1.0f + expf(-val));
+                        j.y[bb * j.y_bs + n0 + r] = val;
+                    }
+                }
+            }
+        }
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            issue(s + GEMV_STAGES * stride, st);
+        }
+    }
+    if (!ok && lane == 0) {
+        // let copies that were issued but never waited for land before the block's smem is reused
+        const uint64_t t1 = global_ns();
+        while (global_ns() - t1 < 20000ull) {}
     }
 }
 
-cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, cudaStream_t s) {
-    if (njobs < 1 || max_n < 1 || max_n % 2 || nb < 1 || nb > 8 || sms < 1) return cudaErrorInvalidValue;
+cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s) {
+    if (njobs < 1 || max_n < 1 || max_n % GEMV_R || nb < 1 || nb > 8 || sms < 1) return cudaErrorInvalidValue;
     for (int q0 = 0; q0 < njobs; q0 += GEMV_MAX_JOBS) {
         const int n = std::min(GEMV_MAX_JOBS, njobs - q0);
         GemvBatch jb{};
         for (int q = 0; q < n; ++q) {
             jb.j[q] = jobs[q0 + q];
-            if (jb.j[q].K > 256 * GEMV_CHUNKS || jb.j[q].K % 8 || jb.j[q].nb > nb || jb.j[q].N > max_n)
+            if (jb.j[q].K > 256 * GEMV_CHUNKS || jb.j[q].K % 8 || jb.j[q].nb > nb || jb.j[q].N > max_n ||
+                ((uintptr_t) jb.j[q].W & 15))
                 return cudaErrorInvalidValue;
         }
-        const long long slots = (long long) n * max_n;
-        const dim3 grid((unsigned) std::min<long long>((slots + 15) / 16, 2LL * sms));   // 8 warps x R = 2 rows
+        const long long slots = (long long) n * max_n, per_block = GEMV_WARPS * GEMV_R;
+        const dim3 grid((unsigned) std::min<long long>((slots + per_block - 1) / per_block, 6LL * sms));
         cudaError_t e;
-        if (nb == 1) e = launch_ex(gemv_kernel<1, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
-        else if (nb == 2) e = launch_ex(gemv_kernel<2, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
-        else if (nb <= 4) e = launch_ex(gemv_kernel<4, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
-        else e = launch_ex(gemv_kernel<8, 2>, grid, dim3(256), 0, s, 1u, jb, n, max_n, ab_bf16);
+        if (nb == 1) e = launch_ex(gemv_kernel<1>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
+        else if (nb == 2) e = launch_ex(gemv_kernel<2>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
+        else if (nb <= 4) e = launch_ex(gemv_kernel<4>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
+        else e = launch_ex(gemv_kernel<8>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

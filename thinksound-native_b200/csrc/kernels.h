@@ -168,8 +168,9 @@ struct GemvBatch {
 };
 // jobs: host array (copied into the launch's parameters; more than GEMV_MAX_JOBS take several
 // launches); nb: arms of the jobs (1..8, every job's nb <= it); max_n even; every K <= 1024 and a
-// multiple of 8; sms: the device's SM count (the grid holds at most two blocks per SM)
-cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, cudaStream_t s);
+// multiple of 8, W 16-byte aligned; sms: the device's SM count (the grid holds at most six blocks
+// per SM); err: device error word for wait timeouts
+cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s);
 
 // ---- per-forward conditioning prologue (src/dit_fwd.cpp:131-140, 166-167) ----
 // B batch rows = G generations x A CFG arms (A = 2, or 1 for a single-arm model); the per-

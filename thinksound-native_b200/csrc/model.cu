@@ -1115,10 +1115,11 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     const int nmj = n_mod_jobs;
     int sms = 148;
     CKR(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev->ordinal));
+    int * derr = dev->d_err;
     const int bfl = bf16, nbm = B;
-    ops.push_back(Op{[jb, H, sms, bfl](cudaStream_t s) { return launch_gemv(jb.data(), 1, H, 1, sms, bfl, s); }, 2, 0,
+    ops.push_back(Op{[jb, H, sms, bfl, derr](cudaStream_t s) { return launch_gemv(jb.data(), 1, H, 1, sms, bfl, derr, s); }, 2, 0,
                      "t_embed.0"});
-    ops.push_back(Op{[jb, H, sms, bfl](cudaStream_t s) { return launch_gemv(jb.data() + 1, 1, H, 1, sms, bfl, s); }, 2, 0,
+    ops.push_back(Op{[jb, H, sms, bfl, derr](cudaStream_t s) { return launch_gemv(jb.data() + 1, 1, H, 1, sms, bfl, derr, s); }, 2, 0,
                      "t_embed.2"});
     CondArgs ca{te, gcmlp, sync_gather, clip_pp, text_pp, x, gc_silu, extc16, clip_s, text_s, x16,
                 tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L,
@@ -1127,7 +1128,7 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // the clip/text modulations of every joint block (HBM-bound GEMVs, ~160 MB of weights at the
     // 8 s geometry) in one launch with the GPU to itself: beside the modulation GEMM they starved
     // for L2-to-SM bandwidth and held SMs that the next GEMM's CTAs needed
-    p.add(Op{[jb, nmj, H, nbm, sms, bfl](cudaStream_t s) { return launch_gemv(jb.data() + 2, nmj, 6 * H, nbm, sms, bfl, s); }, 2, 0,
+    p.add(Op{[jb, nmj, H, nbm, sms, bfl, derr](cudaStream_t s) { return launch_gemv(jb.data() + 2, nmj, 6 * H, nbm, sms, bfl, derr, s); }, 2, 0,
              "adaln_gemv"});
     if (tp) {
         const size_t sH = (size_t) H, sTH = (size_t) T * H;

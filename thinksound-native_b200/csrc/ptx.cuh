@@ -95,6 +95,14 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap * m, const void *
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
+// Untiled bulk copy global -> this CTA's shared memory (16-byte aligned addresses, size a multiple
+// of 16), completing `bytes` transactions on `bar`.
+__device__ __forceinline__ void bulk_load(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"((uint64_t) src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // 2-SM (cta_group::2) loads: the data lands in this CTA's shared memory, the transaction bytes are
 // counted on `bar_cluster` (a shared::cluster address: the pair leader's barrier). No multicast.
 __device__ __forceinline__ void tma_load_2d_cg2(void * dst, const CUtensorMap * m, uint32_t bar_cluster, int c0, int c1) {
