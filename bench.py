@@ -54,7 +54,9 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--profile-ops", action="store_true", help="print one line per launch of an eager step to stderr")
-    ap.add_argument("--no-autotune", action="store_true", help="keep the static tile cost model")
+    ap.add_argument("--autotune", action="store_true",
+                    help="time every tile candidate at load instead of the library's built-in tile table (the tuned "
+                         "forward may then differ from other processes' in the last bits)")
     ap.add_argument("--cfg-split", action="store_true", help="one CFG arm per rank, pairs of ranks per generation")
     ap.add_argument("--long", action="store_true", help="BASELINE config 4 geometry: 30 s audio (T=704, clip 240, text 77)")
     ap.add_argument("--config5", action="store_true", help="64 generations x 24 steps, data-parallel, final gather")
@@ -213,11 +215,11 @@ def cpu_reference_steps(a, reps, threads):
 
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    import tsn
 
     tmp = tempfile.mkdtemp(prefix="tsn_cpu_")
     gguf = os.path.join(tmp, "dit.gguf")
-    tsn.write_synthetic_gguf(gguf, tsn.geom(**geom_kwargs(a)), a.seed)
+    # written by the oracle library: the CPU arms never load the GPU library
+    O.write_synthetic_gguf(gguf, seed=a.seed, **geom_kwargs(a))
     rng = np.random.default_rng(a.seed)
     f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
     inp = {"x": f(a.T, 64), "clip_pp": f(a.C, a.H), "sync_gather": f(a.T, a.H), "text_pp_cond": f(a.TS, a.H),
@@ -301,10 +303,11 @@ def run_tsn(a):
     f = lambda *s: rng.standard_normal(s, dtype=np.float32)  # noqa: E731
     m.set_conditioning(f(a.C, a.H), f(a.T, a.H), f(2, a.TS, a.H), f(2, a.H))
     m.set_x(f(a.T, 64))
-    tuned = None
-    if not a.no_autotune:
+    tiles_desc = "built-in B200 tile table (fixed per GEMM shape, cost model for unlisted shapes): the same bits " \
+                 "in every process"
+    if a.autotune:
         rep = m.autotune()
-        tuned = True
+        tiles_desc = "autotuned per shape at load"
         if a.profile_ops and rank == 0:
             print(rep, file=sys.stderr, flush=True)
     total = a.warmup + a.steps
@@ -382,8 +385,9 @@ def run_tsn(a):
             "metric": METRIC, "value": world * a.steps / (ms * 1e-3), "unit": "steps/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16 (split hi+lo activations), f32 accumulate", "data": "synthetic",
-            "config": dict(workload(a), parallelism=f"dp{world} (one generation per GPU, no data-path collective)",
-                           gemm_tiles="autotuned per shape at load" if tuned else "static cost model"),
+            "config": workload(a),
+            "parallelism": f"dp{world} (one generation per GPU, no data-path collective)",
+            "gemm_tiles": tiles_desc,
             # dominant kernel: the GEMM with the most device time per step, each launch timed with
             # CUDA events on its stream (eager per-op pass after the timed region), against the
             # burst bf16 peak (a kernel timed alone)
@@ -446,7 +450,7 @@ def run_cfg_split(a):
         clip, sync, text, gc, x0 = f(a.C, a.H), f(a.T, a.H), f(2, a.TS, a.H), f(2, a.H), f(a.T, 64)
         m.set_conditioning(clip, sync, text[arm], gc[arm])
         m.set_x(x0)
-        if not a.no_autotune:
+        if a.autotune:
             m.autotune()
         sampler = cfg_split.CfgSplitSampler(m, dev, a.T, group=group)
         x = torch.from_numpy(x0).cuda()
@@ -474,8 +478,8 @@ def run_cfg_split(a):
                 "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f16 (split hi+lo activations), f32 accumulate",
                 "data": "synthetic",
-                "config": dict(workload(a), parallelism=f"cfg-split x{world // 2} (one CFG arm per GPU, NCCL all-gather "
-                                                        f"of the flow every step)"),
+                "config": workload(a),
+                "parallelism": f"cfg-split x{world // 2} (one CFG arm per GPU, NCCL all-gather of the flow every step)",
                 "step_roofline": {"compute_ms": compute_ms, "hbm_ms": hbm_ms, "roofline_ms": max(compute_ms, hbm_ms),
                                   "frac": max(compute_ms, hbm_ms) / step_ms,
                                   "peaks": f"{src}: {tf_sus} TFLOP/s sustained bf16, {hbm} GB/s"},
@@ -537,7 +541,7 @@ def run_config5(a):
     with torch.cuda.stream(stream):
         m.set_conditioning(*inputs(list(range(G)))[:4])
         m.set_x(inputs(list(range(G)))[4])
-        if not a.no_autotune:
+        if a.autotune:
             m.autotune()
         run_batch(list(range(G)))                               # warm-up
         torch.cuda.synchronize()
@@ -567,7 +571,7 @@ def run_config5(a):
                 "value": gen_s, "unit": "generations/s", "n_gpus": world, "generations": a.generations,
                 "gens_per_forward": G, "steps_per_generation": steps, "seconds": ms * 1e-3,
                 "cfg_steps_per_s": gen_s * steps, "higher_is_better": True, "scaling": "strong",
-                "data": "synthetic", "config": dict(workload(a), parallelism=f"dp{world}, {G} generation(s) per forward"),
+                "data": "synthetic", "config": workload(a), "parallelism": f"dp{world}, {G} generation(s) per forward",
                 "x_finite": finite}), flush=True)
     m.close()
     dev.close()

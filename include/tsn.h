@@ -71,6 +71,11 @@ int tsn_commit(tsn_device * dev);
 uint32_t tsn_exec_width(tsn_device * dev, const char * kernel);
 /* Device::last_gpu_ms (src/gpu.h:41). */
 double tsn_last_gpu_ms(tsn_device * dev);
+/* No counterpart in the reference (a test hook for the failure path). Launches one block whose
+ * thread waits on an mbarrier that nothing ever arrives on, bounded by limit_us (100 us .. 1 s), the
+ * way every pipeline wait of this library is bounded. Expected result: TSN_ERR_TIMEOUT, with the
+ * device still usable afterwards. */
+int tsn_selftest_device_timeout(tsn_device * dev, uint32_t limit_us);
 
 /* ------------------------------------------------------------------ runtime face (src/net.h) */
 /* Runtime::gemm (src/net.h:23-24): Y[M,N] = X[M,K]·W[N,K]^T (+bias), X/Y f32, W f16 (wf16=1) or
@@ -85,8 +90,9 @@ int tsn_gemm(tsn_device * dev, int wf16, const void * W, const void * X, void * 
  * device array inside the library instead and calls no allocator. Limits: K and N multiples of
  * 64, and 4*M*K bytes (plus 2*N*K when ldw != K) at most 8 MiB, else TSN_ERR_ARG. The first call
  * on each device looks up the array's device address; make that first call before any stream
- * capture begins. Every call on a device shares the one array: calls that overlap on the GPU
- * (other streams, other threads) race on it, so serialise them. */
+ * capture begins; the looked-up address does not survive cudaDeviceReset of that device. Every
+ * call on a device shares the one array: calls that overlap on the GPU (other streams, other
+ * threads) race on it, so serialise them. */
 int tsn_gemm_noalloc(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias,
                      uint32_t M, uint32_t N, uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy);
 /* Runtime::gemv (src/net.h:25-26). */
@@ -118,6 +124,14 @@ typedef struct tsn_dit_geom {
  * HBM and convert them there (qkv rows de-interleaved, conv weights reordered to [OC][K][IC],
  * FFN w1/w3 interleaved). compute_type: TSN_COMPUTE_F16 or TSN_COMPUTE_BF16. */
 int tsn_dit_load(tsn_device * dev, const char * gguf_path, int compute_type, tsn_dit ** out);
+/* Host-only check of a DiT GGUF, no device needed: DitModel::load's geometry keys
+ * (src/dit.cpp:29-46) and every tensor the forward reads, present with its expected shape
+ * (WeightSet::need, src/net.mm:110-118). TSN_ERR_IO (unreadable), TSN_ERR_FORMAT (bad magic,
+ * version, truncated header or tensor table, tensor data past the end of the file;
+ * src/gguf.cpp:73-151), TSN_ERR_MISSING (a tensor absent or mis-shaped), TSN_ERR_ARG (geometry
+ * this build does not provide). tsn_dit_load fails with the same codes. geom and weight_bytes (the
+ * device bytes the weights take) may be null. */
+int tsn_dit_inspect(const char * gguf_path, tsn_dit_geom * geom, size_t * weight_bytes);
 /* Same model from the seeded synthetic fixture generated on the device: bit-identical to loading
  * the file tsn_gguf_write_synthetic writes for the same geometry and seed. */
 int tsn_dit_load_synthetic(tsn_device * dev, const tsn_dit_geom * g, uint64_t seed, int compute_type, tsn_dit ** out);

@@ -102,6 +102,19 @@ class Oracle:
 PREP_OUT = ("clip_pp", "sync_gather", "text_pp_cond", "gcmlp_cond", "text_pp_unc", "gcmlp_unc")
 
 
+def write_synthetic_gguf(path: str, H=1024, NH=16, F=4096, depth=21, fused_depth=14, latent_dim=64,
+                         rope_theta=10000.0, t_max_period=1.0, seed=4242, with_prep=False):
+    """The seeded synthetic DiT GGUF (byte-identical to tsn.write_synthetic_gguf), written by
+    liboracle.so so that a CPU-only process never loads the GPU library."""
+    L = C.CDLL(LIB)
+    L.oracle_write_synthetic_gguf.restype = C.c_int
+    L.oracle_write_synthetic_gguf.argtypes = [C.c_char_p] + [C.c_uint] * 6 + [C.c_float, C.c_float, C.c_ulonglong,
+                                                                              C.c_int]
+    if L.oracle_write_synthetic_gguf(path.encode(), H, NH, F, depth, fused_depth, latent_dim, rope_theta, t_max_period,
+                                     seed, int(with_prep)) != 0:
+        raise RuntimeError(f"could not write {path}")
+
+
 def have_ref() -> bool:
     return os.access(REF_BIN, os.X_OK)
 

@@ -7,8 +7,12 @@
 //   ts_ref_dit step <gguf> <T> <C> <TS> <in_dir> <out_dir> <t> <cfg> <dt> [reps]
 //       one CFG step exactly as the sampler loop runs it (src/pipeline.cpp:146-148): forward
 //       cond, forward uncond, Runtime::cfg_euler. Writes x_out.bin; prints a JSON timing line.
-//   ts_ref_dit sample <gguf> <T> <C> <TS> <in_dir> <out_dir> <steps> <cfg>
-//       the Euler loop of src/pipeline.cpp:142-155 from the given x; writes x_final.bin.
+//   ts_ref_dit sample <gguf> <T> <C> <TS> <in_dir> <out_dir> <steps> <cfg> [x0_seed] [dump_steps]
+//       the Euler loop of src/pipeline.cpp:142-155 from the given x; writes x_final.bin. With
+//       x0_seed >= 0 the initial latent is drawn as generate_wav draws it (src/pipeline.cpp:126-132:
+//       mt19937(seed), normal_distribution<float>, channel-major draws into [T,64]) instead of read
+//       from x.bin, and written to x0.bin. dump_steps (comma-separated step indices) writes, for
+//       each listed step s, its input x_s<s>.bin and the flows fc_s<s>.bin, fu_s<s>.bin.
 //   ts_ref_dit prep <gguf> <T> <C> <TS> <in_dir> <out_dir> <sync_S>
 //       DitModel::prep_conditioning (src/dit.cpp:55-135) on clip_f.bin [C,1024] and sync_f.bin
 //       [sync_S,768], then DitModel::prep_text_arm (src/dit.cpp:137-192) on text_cat_<arm>.bin
@@ -30,8 +34,10 @@
 // prep_conditioning does (src/dit.cpp:63-88).
 #include "models.h"
 
+#include <algorithm>
 #include <chrono>
 #include <cstdio>
+#include <random>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -251,13 +257,35 @@ int main(int argc, char ** argv) {
     if (mode == "sample") {
         const int steps = atoi(argv[8]);
         const float cfg = argc > 9 ? (float) atof(argv[9]) : 5.0f;
+        const long long x0_seed = argc > 10 ? atoll(argv[10]) : -1;
+        std::vector<int> dump;
+        if (argc > 11)
+            for (const char * p = argv[11]; *p;) {
+                dump.push_back(atoi(p));
+                while (*p && *p != ',') ++p;
+                if (*p == ',') ++p;
+            }
+        if (x0_seed >= 0) {                                                   // pipeline.cpp:126-132
+            std::mt19937 rng((uint32_t) x0_seed);
+            std::normal_distribution<float> nd(0, 1);
+            for (uint32_t c = 0; c < L; ++c)
+                for (uint32_t t = 0; t < T; ++t) ((float *) x.p)[(size_t) t * L + c] = nd(rng);
+            write_from(out + "/x0.bin", x.p, (size_t) T * L);
+        }
         auto t0 = std::chrono::steady_clock::now();
         for (int s = 0; s < steps; ++s) {                                     // pipeline.cpp:142-155
             float t_curr = 1.0f - (float) s / steps;
             float t_prev = 1.0f - (float) (s + 1) / steps;
             float dt = t_prev - t_curr;
+            const bool d = std::find(dump.begin(), dump.end(), s) != dump.end();
+            if (d) write_from(out + "/x_s" + std::to_string(s) + ".bin", x.p, (size_t) T * L);
             dit.forward(rt, x, t_curr, tp_c, gc_c, fc);
             dit.forward(rt, x, t_curr, tp_u, gc_u, fu);
+            if (d) {
+                rt.dev.commit();
+                write_from(out + "/fc_s" + std::to_string(s) + ".bin", fc.p, (size_t) T * L);
+                write_from(out + "/fu_s" + std::to_string(s) + ".bin", fu.p, (size_t) T * L);
+            }
             rt.cfg_euler(fc.p, fu.p, x.p, (size_t) T * L, cfg, dt);
         }
         rt.dev.commit();

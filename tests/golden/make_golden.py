@@ -11,6 +11,12 @@ small_vae.npz     VaeModel::decode (src/vae.cpp:17-86) of a seeded latent [3, 64
                   VAE with 64 base channels (widths 1024 ... 64), audio [6144, 2].
 small_t5.npz      T5Model::encode (src/t5.cpp:84-131) of seeded ids (31 tokens + EOS, then pad) on
                   the synthetic Q8_0 T5 (d_model 256, d_ff 512, 2 layers, 4 heads): out [77, 256].
+full_sample.npz   BASELINE config 3 at full size: the 24-step CFG-5 sampler (src/pipeline.cpp:126-155) of
+                  the 21-block model (H 1024, 16 heads, F 4096; T 188, clip 64, text 77), initial
+                  latent drawn as generate_wav draws it from mt19937(4242); the conditioning inputs
+                  are make_inputs(188, 64, 77, 1024) (seed 4242, stored as a SHA-256 only: the tests
+                  regenerate them). Holds x0, x_final and, for steps 0, 11 and 23, the step's input x
+                  and both arms' flows. `python tests/golden/make_golden.py full` writes only this.
 small_clip.npz    ClipModel::encode (src/clip.cpp:30-101) of seeded ids (BOS, 20 tokens, EOS padded)
                   on the synthetic f32 MetaCLIP text model (hidden 256, 2 layers, 4 heads):
                   per_token [77, 256], pooled [256].
@@ -66,9 +72,47 @@ def make_encoders(d):
                         **CLIP_SMALL)
 
 
+FULL = dict(H=1024, NH=16, F=4096, depth=21, fused_depth=14)
+FULL_SEQ = dict(T=188, C=64, TS=77)
+FULL_STEPS, FULL_CFG, FULL_DUMP = 24, 5.0, (0, 11, 23)
+
+
+def inputs_sha(inp):
+    h = hashlib.sha256()
+    for k in sorted(inp):
+        h.update(k.encode())
+        h.update(np.ascontiguousarray(inp[k], np.float32).tobytes())
+    return h.hexdigest()
+
+
+def make_full(d):
+    T, C, TS = FULL_SEQ["T"], FULL_SEQ["C"], FULL_SEQ["TS"]
+    gguf = os.path.join(d, "full.gguf")
+    tsn.write_synthetic_gguf(gguf, make_geom(**FULL), SEED)
+    inp = make_inputs(T, C, TS, FULL["H"])
+    O.write_inputs(os.path.join(d, "in"), inp)
+    od = os.path.join(d, "full")
+    out = O.run_ref("sample", gguf, T, C, TS, os.path.join(d, "in"), od, FULL_STEPS, FULL_CFG, SEED,
+                    ",".join(str(s) for s in FULL_DUMP), timeout=7200)
+    rd = lambda n: np.fromfile(os.path.join(od, n), np.float32).reshape(T, 64)  # noqa: E731
+    res = {"x0": rd("x0.bin"), "x_final": rd("x_final.bin")}
+    for s in FULL_DUMP:
+        res[f"x_s{s}"] = rd(f"x_s{s}.bin")
+        res[f"fc_s{s}"] = rd(f"fc_s{s}.bin")
+        res[f"fu_s{s}"] = rd(f"fu_s{s}.bin")
+    np.savez_compressed(os.path.join(HERE, "full_sample.npz"), **res, steps=FULL_STEPS, cfg=np.float32(FULL_CFG),
+                        dump_steps=np.array(FULL_DUMP), inputs_sha256=inputs_sha(inp), seconds=O.parse_json_line(out)["seconds"],
+                        **{k: v for k, v in FULL.items()}, **FULL_SEQ)
+
+
 def main():
     if not O.have_ref():
         raise SystemExit("oracle/_ref/ts_ref_dit not built (needs the reference tree)")
+    if sys.argv[1:] == ["full"]:
+        with tempfile.TemporaryDirectory() as d:
+            make_full(d)
+        print("wrote full_sample.npz")
+        return
     if sys.argv[1:] == ["encoders"]:
         with tempfile.TemporaryDirectory() as d:
             make_encoders(d)

@@ -1,8 +1,10 @@
 // api.cu — the C ABI of include/tsn.h over DeviceCtx / Model (runtime.h) and the named-kernel
 // compat layer (compat.cu).
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <memory>
+#include <unistd.h>
 
 #include "compat.h"
 #include "gguf_io.h"
@@ -62,7 +64,9 @@ int tsn_device_destroy(tsn_device * dev) {
     c.activate();
     cudaStreamSynchronize(c.stream);
     for (void * p : c.managed) cudaFree(p);
+    for (auto & r : c.host_regs) cudaHostUnregister((void *) r.first);
     if (c.scratch) cudaFree(c.scratch);
+    if (c.col) cudaFree(c.col);
     if (c.d_err) cudaFree(c.d_err);
     if (c.ev0) cudaEventDestroy(c.ev0);
     if (c.ev1) cudaEventDestroy(c.ev1);
@@ -96,16 +100,55 @@ int tsn_alloc(tsn_device * dev, size_t bytes, void ** out) {
     return TSN_OK;
 }
 
+// Device::wrap (src/gpu.mm:66-87). Managed/device memory is used as is; host memory is pinned in
+// place (no copy) page by page. Like the reference's registry lookup, a range inside memory an
+// earlier wrap registered resolves through that registration; a range that reaches past it
+// registers only the pages not yet registered (mapped host pages keep their host address on the
+// device, so the pieces need not be one registration). Registrations end with the device.
 int tsn_wrap(tsn_device * dev, const void * p, size_t bytes, void ** out) {
-    if (!dev || !out) return fail(TSN_ERR_ARG, "null argument");
-    // Managed/device memory is used as is; host memory is pinned in place (no copy).
-    cudaPointerAttributes a{};
-    if (cudaPointerGetAttributes(&a, p) == cudaSuccess && a.type != cudaMemoryTypeUnregistered) { *out = (void *) p; return TSN_OK; }
+    if (!dev || !out || !p) return fail(TSN_ERR_ARG, "null argument");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    DeviceCtx & c = dev->ctx;
+    TRY(c.activate());
+    const uintptr_t a = (uintptr_t) p, e = a + std::max<size_t>(bytes, 1);
+    auto covering = [&](uintptr_t x) {   // the registration holding address x, or end()
+        auto it = c.host_regs.upper_bound(x);
+        if (it == c.host_regs.begin()) return c.host_regs.end();
+        --it;
+        return x < it->first + it->second.bytes ? it : c.host_regs.end();
+    };
+    auto hit = covering(a);
+    if (hit != c.host_regs.end() && e <= hit->first + hit->second.bytes) {
+        *out = (char *) hit->second.dev + (a - hit->first);
+        return TSN_OK;
+    }
+    cudaPointerAttributes pa{};
+    if (hit == c.host_regs.end() && cudaPointerGetAttributes(&pa, p) == cudaSuccess &&
+        pa.type != cudaMemoryTypeUnregistered) {
+        *out = (void *) p;
+        return TSN_OK;
+    }
     cudaGetLastError();
-    CKR(cudaHostRegister((void *) p, bytes, cudaHostRegisterMapped));
-    void * d = nullptr;
-    CKR(cudaHostGetDevicePointer(&d, (void *) p, 0));
-    *out = d;
+    int same_addr = 0;
+    CKR(cudaDeviceGetAttribute(&same_addr, cudaDevAttrCanUseHostPointerForRegisteredMem, c.ordinal));
+    const uintptr_t page = (uintptr_t) sysconf(_SC_PAGESIZE), lo = a & ~(page - 1), hi = (e + page - 1) & ~(page - 1);
+    if (hit != c.host_regs.end() && !same_addr)
+        return fail(TSN_ERR_ARG, "wrap range extends a registered range and this device cannot use host addresses");
+    // register every run of pages in [lo, hi) that no earlier wrap holds
+    for (uintptr_t x = lo; x < hi;) {
+        auto r = covering(x);
+        if (r != c.host_regs.end()) { x = r->first + r->second.bytes; continue; }
+        auto next = c.host_regs.upper_bound(x);
+        const uintptr_t run_end = next == c.host_regs.end() ? hi : std::min<uintptr_t>(hi, next->first);
+        CKR(cudaHostRegister((void *) x, run_end - x, cudaHostRegisterMapped | cudaHostRegisterPortable));
+        void * d = nullptr;
+        CKR(cudaHostGetDevicePointer(&d, (void *) x, 0));
+        c.host_regs[x] = DeviceCtx::HostReg{run_end - x, d};
+        x = run_end;
+    }
+    if (same_addr) { *out = (void *) p; return TSN_OK; }
+    hit = covering(a);
+    *out = (char *) hit->second.dev + (a - hit->first);
     return TSN_OK;
 }
 
@@ -147,6 +190,17 @@ uint32_t tsn_exec_width(tsn_device * dev, const char * kernel) {
 }
 
 double tsn_last_gpu_ms(tsn_device * dev) { return dev ? dev->ctx.last_ms : 0.0; }
+
+int tsn_selftest_device_timeout(tsn_device * dev, uint32_t limit_us) {
+    if (!dev) return fail(TSN_ERR_ARG, "null device");
+    if (limit_us < 100 || limit_us > 1000000) return fail(TSN_ERR_ARG, "limit must lie in [100 us, 1 s]");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    DeviceCtx & c = dev->ctx;
+    TRY(c.activate());
+    TRY(c.sync());    // a timeout reported below is this call's own
+    CKR(launch_wait_selftest(c.d_err, 1000ull * limit_us, c.stream));
+    return c.sync();
+}
 
 // ------------------------------------------------------------------------------- runtime face
 #define RT_BEGIN                                                         \
@@ -218,6 +272,16 @@ int tsn_dit_load(tsn_device * dev, const char * path, int compute_type, tsn_dit 
     if (!path) return fail(TSN_ERR_ARG, "null path");
     std::string p(path);
     return new_model(dev, compute_type, out, &p, nullptr, 0);
+}
+
+int tsn_dit_inspect(const char * path, tsn_dit_geom * geom, size_t * weight_bytes) {
+    if (!path) return fail(TSN_ERR_ARG, "null path");
+    DitGeom g;
+    size_t wb = 0;
+    TRY(inspect_model(path, g, wb));
+    if (geom) *geom = tsn_dit_geom{g.H, g.NH, g.F, g.depth, g.fused_depth, g.latent_dim, g.rope_theta, g.t_max_period};
+    if (weight_bytes) *weight_bytes = wb;
+    return TSN_OK;
 }
 
 int tsn_dit_load_synthetic(tsn_device * dev, const tsn_dit_geom * g, uint64_t seed, int compute_type, tsn_dit ** out) {

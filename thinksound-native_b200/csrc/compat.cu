@@ -14,6 +14,7 @@
 // depends on them (gate_add covers every dispatched thread; row counts come from the grid).
 // Dense GEMMs whose shapes fit the tensor-core tiles (K, N multiples of 64) convert X to f16 and
 // run the tcgen05 kernel; other shapes use a CUDA-core tiled GEMM.
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -374,16 +375,28 @@ int compat_conv(DeviceCtx & c, int wf16, const void * W, const void * bias, cons
         k_conv1d<<<nblk((long long) OL * OC), 256, 0, c.stream>>>((const float *) x, W, wf16, (const float *) bias, (float *) y, p);
         return launched("conv1d");
     }
-    const size_t KC = (size_t) IC * K;
-    float * col = nullptr;
-    if (cudaMalloc(&col, (size_t) OL * KC * 4) != cudaSuccess) return fail(TSN_ERR_OOM, "im2col buffer");
-    IcP ip{T, OL, IC, K, stride, pad, dil, IC, convt ? 1u : 0u, 0};
-    k_im2col<<<nblk((long long) OL * KC), 256, 0, c.stream>>>((const float *) x, col, ip, (long long) OL * KC);
-    int rc = launched("im2col");
-    if (!rc) rc = compat_gemm(c, wf16, W, col, y, bias, OL, OC, (uint32_t) KC, (uint32_t) KC, (uint32_t) KC, OC);
-    cudaStreamSynchronize(c.stream);
-    cudaFree(col);
-    return rc;
+    // Runtime::conv's chunking (src/net.mm:36-47): output rows per chunk keep the col scratch at
+    // most 16 M floats; the col buffer persists on the device context (grown only when a larger
+    // chunk needs it, freed with the device), so a conv allocates nothing once the buffer is sized
+    const size_t KC = (size_t) IC * K, max_elems = (size_t) 16 << 20;
+    const uint32_t rows = (uint32_t) std::max<size_t>(1, std::min<size_t>(OL, max_elems / KC));
+    const size_t need = (size_t) rows * KC * 4;
+    if (c.col_bytes < need) {
+        if (c.col) { cudaStreamSynchronize(c.stream); cudaFree(c.col); c.col = nullptr; c.col_bytes = 0; }
+        if (cudaMalloc(&c.col, need) != cudaSuccess) return fail(TSN_ERR_OOM, "im2col buffer");
+        c.col_bytes = need;
+    }
+    float * col = (float *) c.col;
+    for (uint32_t t0 = 0; t0 < OL; t0 += rows) {
+        const uint32_t n = std::min(rows, OL - t0);
+        IcP ip{T, n, IC, K, stride, pad, dil, IC, convt ? 1u : 0u, t0};
+        k_im2col<<<nblk((long long) n * KC), 256, 0, c.stream>>>((const float *) x, col, ip, (long long) n * KC);
+        int rc = launched("im2col");
+        if (!rc) rc = compat_gemm(c, wf16, W, col, (float *) y + (size_t) t0 * OC, bias, n, OC, (uint32_t) KC, (uint32_t) KC,
+                                  (uint32_t) KC, OC);
+        if (rc) return rc;
+    }
+    return TSN_OK;
 }
 
 int compat_elementwise(DeviceCtx & c, const char * name, const void * a, const void * b, void * y, size_t n,

@@ -699,6 +699,28 @@ cudaError_t launch_step_advance(int * step, cudaStream_t s) {
     return launch_ex(step_advance_kernel, dim3(1), dim3(1), 0, s, 1u, step);
 }
 
+// A wait that can only end by its bound: the barrier expects one arrival that never comes, so
+// the phase-0 wait gives up after limit_ns, records the code the pipelines use for a load that
+// never landed, and the kernel returns normally.
+__global__ void wait_selftest_kernel(int * err, unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        const uint64_t t0 = global_ns();
+        while (!mbar_try_wait(&bar, 0)) {
+            if (global_ns() - t0 > limit_ns) {
+                atomicCAS(err, 0, DEV_TIMEOUT_FULL);
+                break;
+            }
+        }
+    }
+}
+cudaError_t launch_wait_selftest(int * err, unsigned long long limit_ns, cudaStream_t s) {
+    wait_selftest_kernel<<<1, 32, 0, s>>>(err, limit_ns);
+    return cudaGetLastError();
+}
+
 // =============================================================================== weights
 __device__ __forceinline__ float src_value(const void * src, int type, size_t i) {
     if (type == 30) return tsn_bf16_to_f32(((const uint16_t *) src)[i]);

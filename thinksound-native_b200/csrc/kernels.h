@@ -200,6 +200,9 @@ cudaError_t launch_cond(const CondArgs & a, cudaStream_t s);
 cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
                              const int * step, float dt_const, cudaStream_t s);
 cudaError_t launch_step_advance(int * step, cudaStream_t s);
+// failure-path self-test: one thread waits on an mbarrier that nothing arrives on, bounded by
+// limit_ns; records DEV_TIMEOUT_FULL in err when the bound runs out
+cudaError_t launch_wait_selftest(int * err, unsigned long long limit_ns, cudaStream_t s);
 
 // ---- weight preparation ----
 // dst[n][tap*IC + ic] = cvt(src[row(n)][ic][tap]) for conv sources ([OC][IC][K], K=taps) or

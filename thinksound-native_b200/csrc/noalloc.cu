@@ -35,7 +35,11 @@ __global__ void k_split_operand(const float * x, uint32_t M, uint32_t K, uint32_
 }
 
 std::mutex g_mu;
-void * g_addr[64] = {};   // device address of g_scratch, per device ordinal, looked up once
+// Device address of g_scratch, per device ordinal, looked up once. The cache belongs to the
+// device's primary context: after cudaDeviceReset on a device the module is loaded anew and the
+// cached address is stale, so a process that resets a device must not call tsn_gemm_noalloc on it
+// again.
+void * g_addr[64] = {};
 
 int scratch_address(int ordinal, void ** out) {
     if (ordinal < 0 || ordinal >= 64) return fail(TSN_ERR_ARG, "device ordinal out of range");

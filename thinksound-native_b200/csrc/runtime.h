@@ -28,9 +28,16 @@ struct DeviceCtx {
     bool pending = false;            // work issued since the last commit
     std::mutex mu;
     std::vector<void *> managed;     // tsn_alloc buffers (freed with the device)
+    // tsn_wrap registrations of host memory: page-aligned [base, base + bytes) -> device address
+    // (unregistered with the device)
+    struct HostReg { size_t bytes; void * dev; };
+    std::map<uintptr_t, HostReg> host_regs;
     // compat path scratch: f32 -> f16 operand staging, grown on demand
     void * scratch = nullptr;
     size_t scratch_bytes = 0;
+    // runtime-face conv: im2col scratch of one chunk of output rows (at most 16 M floats)
+    void * col = nullptr;
+    size_t col_bytes = 0;
     int activate();                  // cudaSetDevice(ordinal)
     int check_device_error();        // after a sync: TSN_ERR_TIMEOUT if a kernel gave up
     int sync();                      // stream sync + device error word
@@ -159,6 +166,8 @@ struct Model {
 
 int load_model(Model & m, const std::string * gguf_path, const DitGeom * synth_geom, uint64_t seed, std::string & err);
 int load_prep(Model & m);   // loads PrepW from the model's source on first use
+// Host-only check of a DiT GGUF: geometry and every tensor the forward reads (no device needed).
+int inspect_model(const std::string & path, DitGeom & g, size_t & weight_bytes);
 
 } // namespace tsn
 

@@ -60,6 +60,7 @@ _SIGS = [
     ("tsn_commit", C.c_int, [C.c_void_p]),
     ("tsn_exec_width", C.c_uint32, [C.c_void_p, C.c_char_p]),
     ("tsn_last_gpu_ms", C.c_double, [C.c_void_p]),
+    ("tsn_selftest_device_timeout", C.c_int, [C.c_void_p, C.c_uint32]),
     ("tsn_gemm", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                            C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
     ("tsn_gemm_noalloc", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -77,6 +78,7 @@ _SIGS = [
     ("tsn_cfg_euler", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_size_t, C.c_float, C.c_float]),
     ("tsn_mean_cols", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32, C.c_uint32]),
     ("tsn_dit_load", C.c_int, [C.c_void_p, C.c_char_p, C.c_int, C.POINTER(C.c_void_p)]),
+    ("tsn_dit_inspect", C.c_int, [C.c_char_p, C.POINTER(Geom), C.POINTER(C.c_size_t)]),
     ("tsn_dit_load_synthetic", C.c_int, [C.c_void_p, C.POINTER(Geom), C.c_uint64, C.c_int, C.POINTER(C.c_void_p)]),
     ("tsn_dit_free", C.c_int, [C.c_void_p]),
     ("tsn_vae_load", C.c_int, [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p)]),
@@ -211,6 +213,11 @@ class Device:
 
     def exec_width(self, kernel: str) -> int:
         return lib().tsn_exec_width(self.h, kernel.encode())
+
+    def selftest_timeout(self, limit_us: int = 1000):
+        """Run the bounded-wait self-test (a wait nothing completes); raises TsnError (TSN_ERR_TIMEOUT
+        expected) unless the wait somehow completed."""
+        check(lib().tsn_selftest_device_timeout(self.h, limit_us))
 
     # --- net.h Runtime
     def gemm(self, wf16, W, X, Y, bias, M, N, K, ldx=0, ldw=0, ldy=0):
@@ -495,6 +502,15 @@ def write_synthetic_vae_gguf(path: str, channels: int = 128, latent_dim: int = 6
                              seed: int = 4242):
     """Seeded synthetic VAE decoder GGUF (f32; the tensor names src/vae.cpp reads)."""
     check(lib().tsn_gguf_write_synthetic_vae(path.encode(), latent_dim, channels, out_channels, seed))
+
+
+def inspect(path: str):
+    """Host-only check of a DiT GGUF (tsn_dit_inspect): (geometry, device weight bytes); raises
+    TsnError with TSN_ERR_IO / FORMAT / MISSING / ARG. Needs no GPU."""
+    g = Geom()
+    nb = C.c_size_t()
+    check(lib().tsn_dit_inspect(path.encode(), C.byref(g), C.byref(nb)))
+    return g, nb.value
 
 
 def write_synthetic_gguf(path: str, g: Geom, seed: int = 4242, with_prep: bool = False):
