@@ -15,8 +15,11 @@ full_sample.npz   BASELINE config 3 at full size: the 24-step CFG-5 sampler (src
                   the 21-block model (H 1024, 16 heads, F 4096; T 188, clip 64, text 77), initial
                   latent drawn as generate_wav draws it from mt19937(4242); the conditioning inputs
                   are make_inputs(188, 64, 77, 1024) (seed 4242, stored as a SHA-256 only: the tests
-                  regenerate them). Holds x0, x_final and, for steps 0, 11 and 23, the step's input x
-                  and both arms' flows. `python tests/golden/make_golden.py full` writes only this.
+                  regenerate them). Holds x0, x_final and, for steps 0, 1, 11, 12 and 23, the step's
+                  input x and both arms' flows; and the trajectory's sensitivity: x_final of the
+                  reference's own run from x0 perturbed by relative SENS_EPS (the size of the per-step
+                  flow gate) Gaussian noise, as its rel-L2 distance from x_final.
+                  `python tests/golden/make_golden.py full` writes only this.
 small_clip.npz    ClipModel::encode (src/clip.cpp:30-101) of seeded ids (BOS, 20 tokens, EOS padded)
                   on the synthetic f32 MetaCLIP text model (hidden 256, 2 layers, 4 heads):
                   per_token [77, 256], pooled [256].
@@ -74,7 +77,8 @@ def make_encoders(d):
 
 FULL = dict(H=1024, NH=16, F=4096, depth=21, fused_depth=14)
 FULL_SEQ = dict(T=188, C=64, TS=77)
-FULL_STEPS, FULL_CFG, FULL_DUMP = 24, 5.0, (0, 11, 23)
+FULL_STEPS, FULL_CFG, FULL_DUMP = 24, 5.0, (0, 1, 11, 12, 23)
+SENS_EPS = 1e-3
 
 
 def inputs_sha(inp):
@@ -100,9 +104,20 @@ def make_full(d):
         res[f"x_s{s}"] = rd(f"x_s{s}.bin")
         res[f"fc_s{s}"] = rd(f"fc_s{s}.bin")
         res[f"fu_s{s}"] = rd(f"fu_s{s}.bin")
+    # sensitivity: the same sampler from x0 + SENS_EPS * rms(x0) * N(0, 1)
+    x0 = res["x0"]
+    pin = dict(inp)
+    noise = np.random.default_rng(1).standard_normal(x0.shape)
+    pin["x"] = (x0 + SENS_EPS * np.sqrt(np.mean(x0.astype(np.float64) ** 2)) * noise).astype(np.float32)
+    O.write_inputs(os.path.join(d, "pin"), pin)
+    pd = os.path.join(d, "pert")
+    O.run_ref("sample", gguf, T, C, TS, os.path.join(d, "pin"), pd, FULL_STEPS, FULL_CFG, -1, "", timeout=7200)
+    xp = np.fromfile(os.path.join(pd, "x_final.bin"), np.float32).reshape(T, 64).astype(np.float64)
+    xf = res["x_final"].astype(np.float64)
+    sens = float(np.linalg.norm(xp - xf) / np.linalg.norm(xf))
     np.savez_compressed(os.path.join(HERE, "full_sample.npz"), **res, steps=FULL_STEPS, cfg=np.float32(FULL_CFG),
                         dump_steps=np.array(FULL_DUMP), inputs_sha256=inputs_sha(inp), seconds=O.parse_json_line(out)["seconds"],
-                        **{k: v for k, v in FULL.items()}, **FULL_SEQ)
+                        sens_eps=SENS_EPS, sens_x_final_rel=sens, **{k: v for k, v in FULL.items()}, **FULL_SEQ)
 
 
 def main():

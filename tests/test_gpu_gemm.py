@@ -94,3 +94,37 @@ def test_conv_runtime_face(dev, T, IC, OC, K, pad, bias, tag):
         ref += b
     assert not np.isnan(y).any()
     assert rel_l2(y, ref) < 5e-5, tag   # f32 tensor-core accumulation over K up to 7168
+
+
+GEMV_CASES = [  # (N, K, bias, wf16): Runtime::gemv (src/net.mm:51-56); f16 rows of <= 1024 stream
+    (6144, 1024, True, True),        # one clip/text adaLN modulation
+    (1023, 1024, True, True),        # odd N: the last 8-row stage is ragged
+    (7, 200, False, True),           # a single partial stage, K not a multiple of 256
+    (1, 64, True, True),
+    (300, 2048, True, True),         # K above the streaming kernel's limit: the general kernel
+    (500, 512, True, False),         # f32 weights: the general kernel
+]
+
+
+@pytest.mark.parametrize("N,K,bias,wf16", GEMV_CASES)
+def test_gemv_runtime_face(dev, N, K, bias, wf16):
+    rng = np.random.default_rng(13)
+    x = rng.standard_normal(K, dtype=np.float32)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.03
+    if wf16:
+        w = w.astype(np.float16)
+        W = torch.from_numpy(w.view(np.uint16).astype(np.int16)).cuda()
+    else:
+        W = torch.from_numpy(w).cuda()
+    b = rng.standard_normal(N, dtype=np.float32)
+    Y = torch.full((N + 8,), float("nan"), dtype=torch.float32, device="cuda")
+    outs = []
+    for _ in range(2):
+        dev.gemv(W, torch.from_numpy(x).cuda(), Y, torch.from_numpy(b).cuda() if bias else None, N, K, 0, wf16)
+        dev.commit()
+        outs.append(Y.cpu().numpy())
+    y = outs[0]
+    assert np.isnan(y[N:]).all(), "wrote past the output"
+    ref = w.astype(np.float64) @ x.astype(np.float64) + (b if bias else 0)
+    assert rel_l2(y[:N], ref) < 1e-5     # f32 sums over K <= 2048
+    assert np.array_equal(outs[0], outs[1])

@@ -4,11 +4,15 @@ made by tests/golden/make_golden.py from oracle/_ref), and repeat runs bit-ident
 processes (tools/parity_dump.cpp:136-149 checks repeat runs the same way).
 
 Gates:
-* per-step flow (both arms) rel-L2 <= 1e-3 at steps 0, 11 and 23, each step fed the reference's
-  own x of that step (the north star's per-step flow gate);
-* x after the full 24-step run from the reference's initial latent: rel-L2 <= X_FINAL_TOL. The two
-  trajectories diverge only through the per-step flow error, which CFG 5 amplifies in the update
-  x += dt (fu + 5 (fc - fu)); the bound is stated here, not derived from the flow gate;
+* per-step flow (both arms) rel-L2 <= 1e-3 at steps 0, 1, 11, 12 and 23, each step fed the
+  reference's own x of that step (the north star's per-step flow gate);
+* one sampler step (both forwards + cfg_euler, src/pipeline.cpp:146-148) from the reference's x_s
+  at s = 0, 11, 23 lands within the distance the flow gate allows: |dt| (5 |dfc| + 4 |dfu|) with
+  |df| = 1e-3 |f| (the update is x += dt (fu + 5 (fc - fu)), so the bound is the triangle inequality);
+* x after the free-running 24-step run from the reference's initial latent: the trajectory is
+  chaotic with these synthetic weights (the reference's own run from an x0 perturbed by 1e-3, the
+  flow gate's size, ends sens_x_final_rel ~ 6e-2 away), so the GPU run must end no farther from the
+  reference than that perturbed reference run does;
 * the default forward (built-in tile table, no autotuning) gives the same bits in two fresh
   processes and in this one.
 """
@@ -26,7 +30,6 @@ from conftest import ROOT, SEED, make_inputs, rel_l2
 pytestmark = pytest.mark.gpu
 
 FLOW_TOL = 1e-3
-X_FINAL_TOL = 5e-3
 FULL = dict(H=1024, NH=16, F=4096, depth=21, fused_depth=14)
 T, C, TS = 188, 64, 77
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "full_sample.npz")
@@ -64,7 +67,7 @@ def test_per_step_flow_vs_reference(model, golden):
     errs = {}
     for s in golden["dump_steps"]:
         s = int(s)
-        t = float(np.float32(1.0) - np.float32(s) / np.float32(steps))   # src/pipeline.cpp:143, in f32
+        t, _ = schedule(s, steps)
         model.set_x(golden[f"x_s{s}"])
         flow = np.zeros((2, T, 64), np.float32)
         model.forward(t, flow)
@@ -73,15 +76,40 @@ def test_per_step_flow_vs_reference(model, golden):
     assert all(max(e) <= FLOW_TOL for e in errs.values()), errs
 
 
+def schedule(s, steps):
+    """t_s and dt_s as the sampler loop computes them in f32 (src/pipeline.cpp:143-145)."""
+    t = np.float32(1.0) - np.float32(s) / np.float32(steps)
+    t1 = np.float32(1.0) - np.float32(s + 1) / np.float32(steps)
+    return float(t), float(np.float32(t1 - t))
+
+
+def test_one_step_update_vs_reference(model, golden):
+    steps, cfg = int(golden["steps"]), float(golden["cfg"])
+    nxt = {0: "x_s1", 11: "x_s12", 23: "x_final"}
+    for s, key in nxt.items():
+        t, dt = schedule(s, steps)
+        model.set_x(golden[f"x_s{s}"])
+        model.step(t, cfg, dt)
+        x = np.zeros((T, 64), np.float32)
+        model.get_x(x)
+        bound = abs(dt) * FLOW_TOL * (cfg * np.linalg.norm(golden[f"fc_s{s}"]) +
+                                      (cfg - 1.0) * np.linalg.norm(golden[f"fu_s{s}"]))
+        d = float(np.linalg.norm(x.astype(np.float64) - golden[key]))
+        print(f"step {s}: |x_gpu - x_ref| = {d:.4g}, bound {bound:.4g}")
+        assert d <= bound, (s, d, bound)
+
+
 def test_sampler_24_steps_vs_reference(model, golden):
     model.set_x(golden["x0"])
     model.sample(int(golden["steps"]), float(golden["cfg"]))
     x = np.zeros((T, 64), np.float32)
     model.get_x(x)
     e = rel_l2(x, golden["x_final"])
-    print(f"x after {int(golden['steps'])} steps: rel-L2 {e:.3g} vs the reference")
+    sens = float(golden["sens_x_final_rel"])
+    print(f"x after {int(golden['steps'])} steps: rel-L2 {e:.3g} vs the reference; the reference from x0 "
+          f"perturbed by {float(golden['sens_eps']):g}: {sens:.3g}")
     assert np.isfinite(x).all()
-    assert e <= X_FINAL_TOL, e
+    assert e <= sens, (e, sens)
 
 
 CHILD = r"""

@@ -54,6 +54,8 @@ int tsn_device_create(int ordinal, tsn_device ** out) {
     CKR(configure_gemm_kernels());
     CKR(configure_attention());
     CKR(configure_attention_tc());
+    CKR(configure_attention_short());
+    CKR(configure_gemv());
     *out = d.release();
     return TSN_OK;
 }

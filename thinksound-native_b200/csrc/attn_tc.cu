@@ -282,7 +282,231 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
     }
 }
 
+// ================================================================================ short sequences
+// attn_short_kernel: the same product for sequences of at most SHORT_MAX_KT * 64 = 384 keys (the DiT's
+// 188-row fused blocks and 329-row joint blocks at the 8 s geometry, the encoders' 77 tokens), where
+// every key and value tile of an (arm, head) fits in shared memory at once and the whole score row
+// fits in TMEM. No online softmax: the UMMAs write S for every key tile as its K tile lands, the
+// softmax warps take the exact row maximum in one pass over TMEM, then write P (f16 pairs) over the
+// columns of S they have consumed, one 64-key tile at a time, and the PV product of tile j starts as
+// soon as P_j is written. One CTA per (128 query rows, head, arm), 192 threads:
+//   warp 4      TMA: Q (hi, lo) and every K and V tile (hi, lo), each on its own barrier
+//   warp 5      one thread issues S_j = Qh·Kh_j^T + Qh·Kl_j^T + Ql·Kh_j^T into TMEM columns
+//               [64 j, 64 j + 64), then O = sum_j P_j·(Vh_j + Vl_j) with P_j read from TMEM
+//   warps 0-3   one query row per thread: row max, p = 2^(s·scale_log2 + bias - max), row sum of
+//               the f32 p, P_j in f16 into TMEM, then O / sum as the split f16 output
+// With an additive logit bias (the text encoders' T5 relative-position bias / pad mask, CLIP's causal
+// and EOT mask; log2 units, -inf masks a key) the bias is added to the scaled logit of every key.
+// Every wait is bounded; an aborted CTA waits (bounded) for its issued copies and UMMAs before it
+// frees its TMEM and exits.
+constexpr int SHORT_MAX_KT = 6;
+constexpr int SH_OFF_K = 2 * Q_BYTES;                  // [tile][hi | lo], then V the same way
+__host__ __device__ constexpr int short_smem_bytes(int nkt) { return SH_OFF_K + 2 * nkt * 2 * KV_BYTES + 256; }
+
+__global__ void __launch_bounds__(192, 1)
+attn_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                  const __grid_constant__ CUtensorMap tv, const AttnArgs a, int * err) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    unsigned long long * tr = a.trace ? a.trace + 3 * ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
+    const int nkt = (a.S + 63) >> 6;
+    if ((smem_u32(smem) & 1023) || nkt < 1 || nkt > SHORT_MAX_KT) {
+        if (threadIdx.x == 0 && err) atomicCAS(err, 0, DEV_BAD_ARGS);
+        return;
+    }
+    const int off_v = SH_OFF_K + nkt * 2 * KV_BYTES, off_bar = off_v + nkt * 2 * KV_BYTES;
+    uint64_t * bar = (uint64_t *) (smem + off_bar);
+    uint64_t * q_full = bar;                           // Q landed
+    uint64_t * k_full = bar + 1;                       // [nkt] K tile j landed
+    uint64_t * v_full = k_full + SHORT_MAX_KT;         // [nkt] V tile j landed
+    uint64_t * p_ready = v_full + SHORT_MAX_KT;        // [nkt] P_j in TMEM (4 arrivals)
+    uint64_t * s_full = p_ready + SHORT_MAX_KT;        // every S_j in TMEM
+    uint64_t * o_full = s_full + 1;                    // O complete
+    uint64_t * drain = o_full + 1;                     // abort path: the issued UMMAs have completed
+    uint32_t * tslot = (uint32_t *) (drain + 1);
+    volatile int * abort_flag = (volatile int *) (tslot + 1);
+    const uint32_t tcols = nkt <= 3 ? 256u : 512u;
+    const uint32_t TM_OS = 64u * (uint32_t) nkt;      // O after the score columns
+
+    const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int head_row = (b * a.NH + h) * a.S_pad;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int j = 0; j < SHORT_MAX_KT; ++j) { mbar_init(&k_full[j], 1); mbar_init(&v_full[j], 1); mbar_init(&p_ready[j], 4); }
+        mbar_init(s_full, 1);
+        mbar_init(o_full, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        pdl_trigger();
+    }
+    if (warp == 4 && lane == 0) { tma_prefetch(&tq); tma_prefetch(&tk); tma_prefetch(&tv); }
+    if (warp == 5) tmem_alloc(tslot, tcols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            pdl_wait();
+            if (tr) tr[1] = global_ns();
+            mbar_expect_tx(q_full, 2 * Q_BYTES);
+            tma_load_3d(smem, &tq, q_full, 0, head_row + qt * 128, 0);
+            tma_load_3d(smem + Q_BYTES, &tq, q_full, 0, head_row + qt * 128, 1);
+            for (int j = 0; j < nkt; ++j) {
+                uint8_t * t = smem + SH_OFF_K + j * 2 * KV_BYTES;
+                mbar_expect_tx(&k_full[j], 2 * KV_BYTES);
+                tma_load_3d(t, &tk, &k_full[j], 0, head_row + j * 64, 0);
+                tma_load_3d(t + KV_BYTES, &tk, &k_full[j], 0, head_row + j * 64, 1);
+            }
+            for (int j = 0; j < nkt; ++j) {
+                uint8_t * t = smem + off_v + j * 2 * KV_BYTES;
+                mbar_expect_tx(&v_full[j], 2 * KV_BYTES);
+                tma_load_3d(t, &tv, &v_full[j], 0, head_row + j * 64, 0);
+                tma_load_3d(t + KV_BYTES, &tv, &v_full[j], 0, head_row + j * 64, 1);
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t id_s = umma_idesc_f16(64, 0), id_pv = umma_idesc_f16(64, 0, 1);
+            const uint64_t qh = umma_desc_sw128(smem), ql = umma_desc_sw128(smem + Q_BYTES);
+            bool ok = mbar_wait(q_full, 0, abort_flag, err, DEV_TIMEOUT_FULL);
+            for (int j = 0; j < nkt && ok; ++j) {      // S_j as K tile j lands
+                if (!(ok = mbar_wait(&k_full[j], 0, abort_flag, err, DEV_TIMEOUT_FULL))) break;
+                tc_fence_after();
+                const uint8_t * k = smem + SH_OFF_K + j * 2 * KV_BYTES;
+                const uint64_t kh = umma_desc_sw128(k), kl = umma_desc_sw128(k + KV_BYTES);
+                const uint32_t d = tmem + 64u * (uint32_t) j;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t o = (uint64_t) (2 * kk);
+                    umma_f16(d, qh + o, kh + o, id_s, kk != 0);
+                    umma_f16(d, qh + o, kl + o, id_s, 1u);
+                    umma_f16(d, ql + o, kh + o, id_s, 1u);
+                }
+            }
+            if (ok) umma_commit(s_full);
+            for (int j = 0; j < nkt && ok; ++j) {      // O += P_j (Vh_j + Vl_j) as P_j is written
+                if (!(ok = mbar_wait(&p_ready[j], 0, abort_flag, err, DEV_TIMEOUT_TMEM))) break;
+                if (!(ok = mbar_wait(&v_full[j], 0, abort_flag, err, DEV_TIMEOUT_FULL))) break;
+                tc_fence_after();
+                const uint8_t * v = smem + off_v + j * 2 * KV_BYTES;
+                const uint32_t p = tmem + 32u * (uint32_t) j;
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk) {
+                    const uint64_t vh = umma_desc_sw128_mn(v + kk * 2048), vl = umma_desc_sw128_mn(v + KV_BYTES + kk * 2048);
+                    umma_f16_ts(tmem + TM_OS, p + 8 * kk, vh, id_pv, (j | kk) != 0);
+                    umma_f16_ts(tmem + TM_OS, p + 8 * kk, vl, id_pv, 1u);
+                }
+            }
+            if (ok) umma_commit(o_full);
+            if (!ok) {   // let every UMMA issued so far complete before the TMEM is freed
+                umma_commit(drain);
+                const uint64_t t0 = global_ns();
+                while (!mbar_try_wait(drain, 0) && global_ns() - t0 < 1000000ull) {}
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ softmax warps
+        pdl_wait();
+        const int r = warp * 32 + lane;                          // query row within the tile
+        const int row = qt * 128 + r;                            // joint row
+        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        const float * lb = a.lbias ? a.lbias + (((size_t) b * a.NH + h) * a.S + (size_t) min(row, a.S - 1)) * a.S_pad
+                                   : nullptr;
+        bool ok = mbar_wait(s_full, 0, abort_flag, err, DEV_TIMEOUT_TMEM);
+        float m = -INFINITY, l = 0.0f;
+        if (ok) {
+            tc_fence_after();
+            // pass 1: the row maximum of the scaled (and biased) logits; keys >= S are masked
+            for (int c = 0; c < 2 * nkt; ++c) {
+                float v[32];
+                tmem_ld32(trow + 32u * (uint32_t) c, v);
+                float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const int key = c * 32 + e;
+                    float x = lb ? fmaf(v[e], a.scale_log2, lb[key]) : v[e] * a.scale_log2;
+                    if (key >= a.S) x = -INFINITY;
+                    mq[e & 3] = fmaxf(mq[e & 3], x);
+                }
+                m = fmaxf(m, fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])));
+            }
+            if (m == -INFINITY) m = 0.0f;                        // a row whose keys are all masked
+            // pass 2: p = 2^(x - m), its f32 row sum, P_j as f16 pairs over S_j's first half
+            for (int j = 0; j < nkt; ++j) {
+                float v[64];
+                tmem_ld32(trow + 64u * (uint32_t) j, v);
+                tmem_ld32(trow + 64u * (uint32_t) j + 32u, v + 32);
+                float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int e = 0; e < 64; ++e) {
+                    const int key = j * 64 + e;
+                    const float x = lb ? fmaf(v[e], a.scale_log2, lb[key]) - m : fmaf(v[e], a.scale_log2, -m);
+                    v[e] = key < a.S ? ex2(x) : 0.0f;
+                    sq[e & 3] += v[e];
+                }
+                l += (sq[0] + sq[1]) + (sq[2] + sq[3]);
+                uint32_t pk[32];
+#pragma unroll
+                for (int c = 0; c < 32; ++c) {
+                    const __half2 hv = __floats2half2_rn(v[2 * c], v[2 * c + 1]);
+                    pk[c] = *(const uint32_t *) &hv;
+                }
+                tmem_st32(trow + 32u * (uint32_t) j, pk);
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_ready[j]);
+            }
+            ok = mbar_wait(o_full, 0, abort_flag, err, DEV_TIMEOUT_TMEM);
+        }
+        if (ok) {
+            tc_fence_after();
+            float o[64];
+            tmem_ld32(trow + TM_OS, o);
+            tmem_ld32(trow + TM_OS + 32u, o + 32);
+            store_row(a, b, h, row, o, l);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag && warp == 4 && lane == 0) {
+        // copies issued but never consumed must land before this CTA's shared memory is reused
+        const uint64_t t0 = global_ns();
+        bool landed = mbar_try_wait(q_full, 0);
+        for (int j = 0; j < nkt; ++j) landed = landed && mbar_try_wait(&k_full[j], 0) && mbar_try_wait(&v_full[j], 0);
+        while (!landed && global_ns() - t0 < 1000000ull) {
+            landed = mbar_try_wait(q_full, 0);
+            for (int j = 0; j < nkt; ++j) landed = landed && mbar_try_wait(&k_full[j], 0) && mbar_try_wait(&v_full[j], 0);
+        }
+    }
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tcols);
+    }
+    if (tr && threadIdx.x == 0) tr[2] = global_ns();
+}
+
 } // namespace
+
+cudaError_t configure_attention_short() {
+    return cudaFuncSetAttribute(attn_short_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                short_smem_bytes(SHORT_MAX_KT));
+}
+
+bool attention_short_fits(int S) { return S >= 1 && S <= SHORT_MAX_KT * 64; }
+
+cudaError_t launch_attention_short(const AttnMaps & m, const AttnArgs & a, cudaStream_t s) {
+    if (!attention_short_fits(a.S)) return cudaErrorInvalidValue;
+    const int nkt = (a.S + 63) / 64;
+    return launch_ex(attn_short_kernel, dim3((a.S + 127) / 128, a.NH, a.B), dim3(192), short_smem_bytes(nkt), s, 1u, m.q,
+                     m.k, m.v, a, a.err);
+}
 
 cudaError_t configure_attention_tc() {
     return cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_TOTAL);

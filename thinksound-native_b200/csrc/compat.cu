@@ -361,6 +361,16 @@ int compat_gemm(DeviceCtx & c, int wf16, const void * W, const void * X, void * 
 
 int compat_gemv(DeviceCtx & c, int wf16, const void * W, const void * X, void * Y, const void * bias, uint32_t N,
                 uint32_t K, uint32_t ldw) {
+    if (N == 0) return TSN_OK;
+    // f16 weights with dense 16-byte-aligned rows of at most 1024: the weight-streaming GEMV
+    if (wf16 && ldw == K && K % 8 == 0 && K <= (uint32_t) GEMV_MAX_K && ((uintptr_t) W & 15) == 0) {
+        GemvJob j{W, (const float *) bias, (const float *) X, 0, nullptr, 0, (float *) Y, 0, (int) N, (int) K, 1, 0};
+        int sms = 148;
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c.ordinal);
+        cudaError_t e = launch_gemv(&j, 1, (int) N, 1, sms, 0, c.d_err, c.stream);
+        if (e != cudaSuccess) return fail(TSN_ERR_CUDA, std::string("gemv: ") + cudaGetErrorString(e));
+        return TSN_OK;
+    }
     GemmP p{1, N, K, K, ldw, N, bias ? 1u : 0u, 0};
     k_gemv<<<(N + 7) / 8, 256, 0, c.stream>>>(W, wf16, (const float *) X, (float *) Y, (const float *) bias, p);
     return launched("gemv");

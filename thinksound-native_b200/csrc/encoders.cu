@@ -647,7 +647,18 @@ struct EncModel {
                 at.out0 = att; at.n0 = n; at.H = d; at.qkv_lo = qkv_lo; at.out_lo0 = (long long) n * d;
                 at.err = dev->d_err;
                 at.lbias = lb;
-                ops.push_back([at](cudaStream_t s) { return launch_attention(at, s); });
+                // the tcgen05 short-sequence kernel with the logit-bias table (TSN_ATTN_MMA_SYNC=1:
+                // the earlier mma.sync kernel, for comparison)
+                AttnMaps mp{};
+                const uint64_t rows = (uint64_t) NH * S_pad;
+                const bool tc = attention_short_fits(n) && !std::getenv("TSN_ATTN_MMA_SYNC");
+                if (tc && !(make_head_map(&mp.q, q, rows, 128, (uint64_t) qkv_lo) &&
+                            make_head_map(&mp.k, k, rows, 64, (uint64_t) qkv_lo) &&
+                            make_head_map(&mp.v, v, rows, 64, (uint64_t) qkv_lo)))
+                    return fail(TSN_ERR_CUDA, "encoder attention: tensor map encode failed");
+                ops.push_back([at, mp, tc](cudaStream_t s) {
+                    return tc ? launch_attention_short(mp, at, s) : launch_attention(at, s);
+                });
                 op_names.push_back(bp + ".attn");
                 flops += 4.0 * n * (double) n * d;
             }

@@ -50,10 +50,10 @@ bool make_act_map_rows(CUtensorMap * m, const void * base, uint64_t K_in, uint64
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows) {
+bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows, uint64_t lo_elems) {
     if (!encoder() || ((uintptr_t) base & 15) || box_rows > 256) return false;
     const cuuint64_t dims[3] = {64, rows, 2};
-    const cuuint64_t strides[2] = {128, rows * 128};
+    const cuuint64_t strides[2] = {128, (lo_elems ? lo_elems : rows * 64) * 2};
     const cuuint32_t box[3] = {64, box_rows, 1};
     const cuuint32_t es[3] = {1, 1, 1};
     return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, (void *) base, dims, strides, box, es,

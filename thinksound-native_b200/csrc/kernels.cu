@@ -472,149 +472,171 @@ __device__ __forceinline__ void cvt8(uint4 w, int bf16, float * f) {
         f[e] = bf16 ? __uint_as_float((uint32_t) h[e] << 16) : __half2float(__ushort_as_half(h[e]));
 }
 
-// Blocks of four warps walk the (job, row) slots; each warp takes R = 2 consecutive rows of one
-// job per pass. Lane 0 brings a pass's weight rows (one contiguous 4 KB run at K = 1024) into the
-// warp's shared-memory stage with one bulk copy that completes on the stage's mbarrier; with
-// GEMV_STAGES stages per warp the next passes' copies are in flight while the warp sums the
-// current one from shared memory, and no registers hold weights in flight, so many warps fit on an
-// SM. The first copies are issued before the wait on the upstream kernel (weights do not depend
-// on it); the jobs travel as a kernel parameter. Each x chunk is loaded once per pass and used for
-// both rows. A lane sums its chunks in k order and a warp adds the 32 lane sums in a fixed
-// butterfly, so a row's result does not depend on the grid. Every wait is bounded (a timeout sets
-// the device error word). The launch is HBM-bound only when it has the GPU to itself: beside a
-// tcgen05 GEMM, whose tile loads already fill each SM's share of the L2-to-SM fabric, its loads
-// starve (and slow the GEMM), so the forward runs it in line.
-constexpr int GEMV_CHUNKS = 4;                          // K <= 256 x GEMV_CHUNKS
-constexpr int GEMV_R = 2, GEMV_WARPS = 4, GEMV_STAGES = 2;
-constexpr int GEMV_STAGE_BYTES = GEMV_R * 256 * GEMV_CHUNKS * 2;   // 4 KB
+// Weight streaming: one block per SM (grid = min(stages, SMs)) walks the batch's 8-row stages
+// (stage s of the concatenated jobs at blocks b, b + grid, ...). Warp 8's lane 0 streams each stage's
+// rows (one contiguous run of up to 8 x K x 2 bytes) into an 8-slot shared-memory ring with bulk
+// copies that complete on the slot's full barrier, up to 8 stages (128 KB at K = 1024) in flight per
+// SM; the first copies are issued before the wait on the upstream kernel (weights do not depend on
+// it). Warps 0-7 take one row of a stage each: every lane sums its 8-element runs of the row in k
+// order against x (all arms, held in shared memory, loaded once per block), the warp adds the 32 lane
+// sums in a fixed butterfly, so a row's result does not depend on the grid. A warp releases the slot
+// on its empty barrier (8 arrivals) once it has read it. Every job of a batch shares x, K and the arm
+// count. Every wait is bounded; a block that gives up waits (bounded) for the copies it issued
+// before it exits.
+constexpr int GS_ROWS = 8, GS_STAGES = 8, GS_WARPS = 8;
+constexpr int GS_THREADS = 32 * (GS_WARPS + 1);
 
-// slot s of the batch: its job, first row and row count (0: nothing to load)
-__device__ __forceinline__ int gemv_rows(const GemvBatch & jb, long long s, long long slots, int max_n, int & q, int & n0) {
-    if (s >= slots) return 0;
-    q = (int) (s / max_n);
-    n0 = (int) (s % max_n);
-    return n0 < jb.j[q].N ? min(GEMV_R, jb.j[q].N - n0) : 0;
+__host__ __device__ inline size_t gemv_smem_bytes(int K, int nb) {
+    return (size_t) GS_STAGES * GS_ROWS * K * 2 + (size_t) nb * K * 4 + 2 * GS_STAGES * 8 + 16;
+}
+
+// stage s of the batch: its job q, first row n0 and row count
+__device__ __forceinline__ int gemv_stage(const GemvBatch & jb, int njobs, long long s, int & q, int & n0) {
+    for (q = 0; q < njobs; ++q) {
+        const long long ns = (jb.j[q].N + GS_ROWS - 1) / GS_ROWS;
+        if (s < ns) { n0 = (int) s * GS_ROWS; return min(GS_ROWS, jb.j[q].N - n0); }
+        s -= ns;
+    }
+    return 0;
 }
 
 template <int NB>
-__global__ void __launch_bounds__(128) gemv_kernel(const __grid_constant__ GemvBatch jb, int njobs, int max_n, int ab_bf16,
-                                                   int * err) {
-    __shared__ __align__(128) uint8_t wbuf[GEMV_WARPS][GEMV_STAGES][GEMV_STAGE_BYTES];
-    __shared__ __align__(8) uint64_t bars[GEMV_WARPS][GEMV_STAGES];
-    __shared__ int abort_word;
-    pdl_trigger();
+__global__ void __launch_bounds__(GS_THREADS, 1) gemv_kernel(const __grid_constant__ GemvBatch jb, int njobs,
+                                                            long long total, int ab_bf16, int * err) {
+    extern __shared__ __align__(128) uint8_t gs_smem[];
+    const int K = jb.j[0].K, nb = jb.j[0].nb;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const long long slots = (long long) njobs * max_n;
-    const long long stride = (long long) gridDim.x * GEMV_WARPS * GEMV_R;
-    const long long s0 = ((long long) blockIdx.x * GEMV_WARPS + w) * GEMV_R;
-    if (threadIdx.x == 0) abort_word = 0;
-    if (lane == 0) {
-        for (int st = 0; st < GEMV_STAGES; ++st) mbar_init(&bars[w][st], 1);
+    uint8_t * ring = gs_smem;
+    const size_t stage_bytes = (size_t) GS_ROWS * K * 2;
+    float * xs = (float *) (gs_smem + GS_STAGES * stage_bytes);
+    uint64_t * full = (uint64_t *) (xs + (size_t) nb * K);
+    uint64_t * empty = full + GS_STAGES;
+    int * abort_word = (int *) (empty + GS_STAGES);
+    int * n_issued = abort_word + 1;
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < GS_STAGES; ++st) { mbar_init(&full[st], 1); mbar_init(&empty[st], GS_WARPS); }
+        *abort_word = 0;
+        *n_issued = 0;
         fence_mbar_init();
     }
     __syncthreads();
-    volatile int * abort_flag = &abort_word;
-    auto issue = [&](long long s, int st) {   // lane 0
-        int q = 0, n0 = 0;
-        const int rows = gemv_rows(jb, s, slots, max_n, q, n0);
-        if (!rows) return;
-        const uint32_t bytes = (uint32_t) rows * (uint32_t) jb.j[q].K * 2u;
-        mbar_expect_tx(&bars[w][st], bytes);
-        bulk_load(wbuf[w][st], (const uint16_t *) jb.j[q].W + (size_t) n0 * jb.j[q].K, bytes, &bars[w][st]);
-    };
-    if (lane == 0)
-        for (int st = 0; st < GEMV_STAGES; ++st) issue(s0 + st * stride, st);
-    pdl_wait();
-    uint32_t phase = 0;   // bit st: parity of stage st's next completion
-    bool ok = true;
-    for (int i = 0;; ++i) {
-        const long long s = s0 + (long long) i * stride;
-        if (s >= slots) break;
-        const int st = i % GEMV_STAGES;
-        int q = 0, n0 = 0;
-        const int rows = gemv_rows(jb, s, slots, max_n, q, n0);
-        if (rows) {
-            if (!mbar_wait(&bars[w][st], (phase >> st) & 1u, abort_flag, err, DEV_TIMEOUT_FULL)) { ok = false; break; }
-            phase ^= 1u << st;
+    pdl_trigger();
+    volatile int * abort_flag = abort_word;
+    const long long stride = gridDim.x;
+    if (w == GS_WARPS) {
+        // ---------------------------------------------------------------- producer
+        if (lane == 0) {
+            int i = 0;
+            for (;; ++i) {
+                const long long s = blockIdx.x + (long long) i * stride;
+                if (s >= total) break;
+                const int st = i % GS_STAGES;
+                if (i >= GS_STAGES && !mbar_wait(&empty[st], ((i / GS_STAGES) - 1) & 1, abort_flag, err, DEV_TIMEOUT_EMPTY))
+                    break;
+                fence_proxy_async_smem();
+                int q = 0, n0 = 0;
+                const int rows = gemv_stage(jb, njobs, s, q, n0);
+                const uint32_t bytes = (uint32_t) rows * (uint32_t) K * 2u;
+                mbar_expect_tx(&full[st], bytes);
+                bulk_load(ring + st * stage_bytes, (const uint16_t *) jb.j[q].W + (size_t) n0 * K, bytes, &full[st]);
+                *(volatile int *) n_issued = i + 1;
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- consumers
+        pdl_wait();
+        const GemvJob & j0 = jb.j[0];
+        const float * x = j0.x + (j0.x_step ? (long long) (*j0.x_step) * j0.x_step_stride : 0);
+        for (int e = threadIdx.x; e < nb * K; e += 32 * GS_WARPS) {
+            const int bb = e / K, k = e % K;
+            xs[e] = x[(long long) bb * j0.x_bs + k];
+        }
+        epi_bar_n(GS_WARPS * 32);
+        for (int i = 0;; ++i) {
+            const long long s = blockIdx.x + (long long) i * stride;
+            if (s >= total) break;
+            const int st = i % GS_STAGES;
+            if (!mbar_wait(&full[st], (i / GS_STAGES) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) break;
+            int q = 0, n0 = 0;
+            const int rows = gemv_stage(jb, njobs, s, q, n0);
             const GemvJob & j = jb.j[q];
-            const int K = j.K;
-            const float * x = j.x + (j.x_step ? (long long) (*j.x_step) * j.x_step_stride : 0);
-            const uint8_t * wb = wbuf[w][st];
-            float acc[GEMV_R][NB];
+            if (w < rows) {
+                const uint8_t * wr = ring + st * stage_bytes + (size_t) w * K * 2;
+                float acc[NB];
 #pragma unroll
-            for (int r = 0; r < GEMV_R; ++r)
+                for (int bb = 0; bb < NB; ++bb) acc[bb] = 0.0f;
+                for (int k = lane * 8; k < K; k += 256) {
+                    float wf[8];
+                    cvt8(*(const uint4 *) (wr + (size_t) k * 2), ab_bf16, wf);
 #pragma unroll
-                for (int bb = 0; bb < NB; ++bb) acc[r][bb] = 0.0f;
-#pragma unroll
-            for (int c = 0; c < GEMV_CHUNKS; ++c) {
-                const int k = c * 256 + lane * 8;
-                if (k >= K) break;
-                uint4 wr[GEMV_R];
-#pragma unroll
-                for (int r = 0; r < GEMV_R; ++r)
-                    wr[r] = r < rows ? *(const uint4 *) (wb + ((size_t) r * K + k) * 2) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-                for (int bb = 0; bb < NB; ++bb) {
-                    if (bb >= j.nb) break;
-                    const float * xb = x + bb * j.x_bs + k;
-                    const float4 x0 = *(const float4 *) xb, x1 = *(const float4 *) (xb + 4);
-#pragma unroll
-                    for (int r = 0; r < GEMV_R; ++r) {
-                        float wf[8];
-                        cvt8(wr[r], ab_bf16, wf);
-                        acc[r][bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
-                                      wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
+                    for (int bb = 0; bb < NB; ++bb) {
+                        if (bb >= nb) break;
+                        const float4 x0 = *(const float4 *) (xs + bb * K + k), x1 = *(const float4 *) (xs + bb * K + k + 4);
+                        acc[bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
+                                   wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
                     }
                 }
-            }
-            __syncwarp();   // every lane has read the stage before lane 0 refills it
-#pragma unroll
-            for (int r = 0; r < GEMV_R; ++r) {
-                if (r >= rows) break;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);      // the slot's row is read
 #pragma unroll
                 for (int bb = 0; bb < NB; ++bb) {
-                    if (bb >= j.nb) break;
-                    float val = acc[r][bb];
+                    if (bb >= nb) break;
+                    float val = acc[bb];
 #pragma unroll
                     for (int off = 16; off; off >>= 1) val += __shfl_xor_sync(0xffffffffu, val, off);
                     if (lane == 0) {
-                        if (j.bias) val += j.bias[n0 + r];
+                        if (j.bias) val += j.bias[n0 + w];
                         if (j.act == 1) val = val / (1.0f + expf(-val));
-                        j.y[bb * j.y_bs + n0 + r] = val;
+                        j.y[bb * j.y_bs + n0 + w] = val;
                     }
                 }
+            } else if (lane == 0) {
+                mbar_arrive(&empty[st]);
             }
         }
-        if (lane == 0) {
-            fence_proxy_async_smem();
-            issue(s + GEMV_STAGES * stride, st);
-        }
     }
-    if (!ok && lane == 0) {
-        // let copies that were issued but never waited for land before the block's smem is reused
-        const uint64_t t1 = global_ns();
-        while (global_ns() - t1 < 20000ull) {}
+    __syncthreads();
+    if (*abort_flag && w == GS_WARPS && lane == 0) {
+        // copies issued but never consumed must land before this block's shared memory is reused:
+        // wait (bounded) for the last GS_STAGES issued stages
+        const int ni = *(volatile int *) n_issued;
+        const uint64_t t0 = global_ns();
+        for (int i = ni > GS_STAGES ? ni - GS_STAGES : 0; i < ni; ++i)
+            while (!mbar_try_wait(&full[i % GS_STAGES], (i / GS_STAGES) & 1) && global_ns() - t0 < 1000000ull) {}
     }
 }
 
+cudaError_t configure_gemv() {
+    const int bytes = (int) gemv_smem_bytes(GEMV_MAX_K, 8);
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    return e;
+}
+
 cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s) {
-    if (njobs < 1 || max_n < 1 || max_n % GEMV_R || nb < 1 || nb > 8 || sms < 1) return cudaErrorInvalidValue;
+    if (njobs < 1 || max_n < 1 || nb < 1 || nb > 8 || sms < 1) return cudaErrorInvalidValue;
     for (int q0 = 0; q0 < njobs; q0 += GEMV_MAX_JOBS) {
         const int n = std::min(GEMV_MAX_JOBS, njobs - q0);
         GemvBatch jb{};
+        long long total = 0;
         for (int q = 0; q < n; ++q) {
-            jb.j[q] = jobs[q0 + q];
-            if (jb.j[q].K > 256 * GEMV_CHUNKS || jb.j[q].K % 8 || jb.j[q].nb > nb || jb.j[q].N > max_n ||
-                ((uintptr_t) jb.j[q].W & 15))
+            const GemvJob & j = jobs[q0 + q];
+            jb.j[q] = j;
+            if (j.K < 8 || j.K > GEMV_MAX_K || j.K % 8 || j.nb < 1 || j.nb > nb || j.N < 1 || j.N > max_n ||
+                ((uintptr_t) j.W & 15) || j.K != jobs[q0].K || j.nb != jobs[q0].nb || j.x != jobs[q0].x ||
+                j.x_bs != jobs[q0].x_bs || j.x_step != jobs[q0].x_step)
                 return cudaErrorInvalidValue;
+            total += (j.N + GS_ROWS - 1) / GS_ROWS;
         }
-        const long long slots = (long long) n * max_n, per_block = GEMV_WARPS * GEMV_R;
-        const dim3 grid((unsigned) std::min<long long>((slots + per_block - 1) / per_block, 6LL * sms));
+        const dim3 grid((unsigned) std::min<long long>(total, sms));
+        const size_t smem = gemv_smem_bytes(jb.j[0].K, jb.j[0].nb);
         cudaError_t e;
-        if (nb == 1) e = launch_ex(gemv_kernel<1>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
-        else if (nb == 2) e = launch_ex(gemv_kernel<2>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
-        else if (nb <= 4) e = launch_ex(gemv_kernel<4>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
-        else e = launch_ex(gemv_kernel<8>, grid, dim3(32 * GEMV_WARPS), 0, s, 1u, jb, n, max_n, ab_bf16, err);
+        if (nb == 1) e = launch_ex(gemv_kernel<1>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
+        else if (nb == 2) e = launch_ex(gemv_kernel<2>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
+        else if (nb <= 4) e = launch_ex(gemv_kernel<4>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
+        else e = launch_ex(gemv_kernel<8>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -66,8 +66,9 @@ struct GemmLaunch {
 bool make_act_map(CUtensorMap * m, const void * base, uint64_t K_in, uint64_t rows, uint64_t B,
                   uint32_t bt, uint32_t bb, int bf16);
 // Encode a 3-D TMA view {64, rows, 2} of a head-major [hi|lo][rows][64] f16 q/k/v buffer with a
-// {64, box_rows, 1} box (rows = B * NH * S_pad).
-bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows);
+// {64, box_rows, 1} box (rows = B * NH * S_pad); the lo half starts lo_elems elements after the hi
+// half (0: right after it, rows * 64).
+bool make_head_map(CUtensorMap * m, const void * base, uint64_t rows, uint32_t box_rows, uint64_t lo_elems = 0);
 // Encode a 4-D TMA view {N, rows, B, Z} of an f32 output out[z][b][t][n] (strides ldo, out_bs and
 // z_stride elements) with {32, 32, 1, 1} boxes of 128-byte rows in the 128-byte swizzle.
 bool make_out_map_f32(CUtensorMap * m, void * base, uint64_t N, uint64_t rows, uint64_t B, uint64_t Z, uint64_t ldo,
@@ -126,6 +127,12 @@ cudaError_t launch_attention(const AttnArgs & a, cudaStream_t s);
 struct AttnMaps { CUtensorMap q, k, v; };
 cudaError_t configure_attention_tc();
 cudaError_t launch_attention_tc(const AttnMaps & m, const AttnArgs & a, cudaStream_t s);
+// tcgen05 attention for S <= 384 (attn_tc.cu, attn_short_kernel): every key tile resident, exact
+// row maximum, no online rescaling; optional additive logit bias (AttnArgs::lbias). q map box 128
+// rows, k and v maps box 64 rows.
+cudaError_t configure_attention_short();
+bool attention_short_fits(int S);
+cudaError_t launch_attention_short(const AttnMaps & m, const AttnArgs & a, cudaStream_t s);
 
 // ---- adaLN LayerNorm + modulation -> f16 GEMM operand ----
 constexpr int MAX_PARTS = 12;   // most split-K partial tiles a gated GEMM leaves for the next adaLN
@@ -166,10 +173,13 @@ constexpr int GEMV_MAX_JOBS = 16;
 struct GemvBatch {
     GemvJob j[GEMV_MAX_JOBS];
 };
+constexpr int GEMV_MAX_K = 1024;
 // jobs: host array (copied into the launch's parameters; more than GEMV_MAX_JOBS take several
-// launches); nb: arms of the jobs (1..8, every job's nb <= it); max_n even; every K <= 1024 and a
-// multiple of 8, W 16-byte aligned; sms: the device's SM count (the grid holds at most six blocks
-// per SM); err: device error word for wait timeouts
+// launches), all sharing x (and x_step), x_bs, K and nb; nb: the kernel's arm capacity (1..8, every
+// job's nb <= it); every N <= max_n; K <= GEMV_MAX_K and a multiple of 8, W 16-byte aligned with
+// rows K apart; sms: the device's SM count (one block per SM at most); err: device error word for
+// wait timeouts
+cudaError_t configure_gemv();
 cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s);
 
 // ---- per-forward conditioning prologue (src/dit_fwd.cpp:131-140, 166-167) ----

@@ -1072,24 +1072,29 @@ struct Plan {
                    (long long) m.B * m.g.NH * m.S_pad * 64, m.B * m.T * H, m.B * m.C * H, m.B * m.TS * H};
         a.err = m.dev->d_err;
         const double flops = 4.0 * m.B * (double) S * S * m.g.H;
-        // Long sequences run on the tcgen05 kernel (attn_tc.cu, 128 query rows per CTA, TMA views of
-        // q/k/v [hi|lo][B*NH*S_pad][64]); below 256 rows its 128-row tiles leave most SMs idle and
-        // the 64-row mma.sync kernel (attn_kernel) is faster (measured: S 188: 9.2 vs 9.7 us;
-        // S 329: 16.2 vs 12.2 us; S 1021: 77.6 vs 34.0 us).
+        // Both kernels are tcgen05 (attn_tc.cu, 128 query rows per CTA, TMA views of q/k/v
+        // [hi|lo][B*NH*S_pad][64]): up to 384 keys every key tile stays resident and the softmax
+        // takes the exact row maximum (attn_short_kernel); longer sequences stream key tiles
+        // through rings with an online softmax (attn_tc_kernel). TSN_ATTN_MMA_SYNC=1 keeps the
+        // earlier mma.sync kernel (attn_kernel) for sequences below 256 rows, for comparison.
         const uint64_t rows = (uint64_t) m.B * m.g.NH * m.S_pad;
         AttnMaps mp{};
-        const bool tc = S >= 256;
-        if (tc && !(make_head_map(&mp.q, m.q, rows, 128) && make_head_map(&mp.k, m.k, rows, 64) &&
-                    make_head_map(&mp.v, m.v, rows, 64)))
+        const int kind = attention_short_fits(S) ? (S < 256 && std::getenv("TSN_ATTN_MMA_SYNC") ? 0 : 2) : 1;
+        if (kind && !(make_head_map(&mp.q, m.q, rows, 128) && make_head_map(&mp.k, m.k, rows, 64) &&
+                      make_head_map(&mp.v, m.v, rows, 64)))
             return fail(TSN_ERR_CUDA, "attention: tensor map encode failed");
-        Op op{[a, mp, tc](cudaStream_t s) { return tc ? launch_attention_tc(mp, a, s) : launch_attention(a, s); }, 1, flops,
-              "attention"};
-        op.traced = [a, mp, tc](cudaStream_t s, unsigned long long * tr) {
+        auto go = [mp, kind](const AttnArgs & x, cudaStream_t s) {
+            return kind == 2 ? launch_attention_short(mp, x, s) : kind == 1 ? launch_attention_tc(mp, x, s)
+                                                                            : launch_attention(x, s);
+        };
+        Op op{[a, go](cudaStream_t s) { return go(a, s); }, 1, flops, kind == 2 ? "attention" : "attention_stream"};
+        if (!kind) op.name = "attention_mma_sync";
+        op.traced = [a, go](cudaStream_t s, unsigned long long * tr) {
             AttnArgs t = a;
             t.trace = tr;
-            return tc ? launch_attention_tc(mp, t, s) : launch_attention(t, s);
+            return go(t, s);
         };
-        op.ctas = tc ? ((S + 127) / 128) * (int) m.g.NH * m.B : ((S + 63) / 64) * (int) m.g.NH * m.B;
+        op.ctas = kind ? ((S + 127) / 128) * (int) m.g.NH * m.B : ((S + 63) / 64) * (int) m.g.NH * m.B;
         op.trace_slots = 3;
         add(op);
         return TSN_OK;

@@ -299,5 +299,7 @@ __device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
 
 // named barrier over the 128 epilogue threads (warps 0-3)
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier 1 over the first n threads of the block (n a multiple of 32)
+__device__ __forceinline__ void epi_bar_n(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
 
 } // namespace tsn
