@@ -127,4 +127,4 @@ def test_gemv_runtime_face(dev, N, K, bias, wf16):
     assert np.isnan(y[N:]).all(), "wrote past the output"
     ref = w.astype(np.float64) @ x.astype(np.float64) + (b if bias else 0)
     assert rel_l2(y[:N], ref) < 1e-5     # f32 sums over K <= 2048
-    assert np.array_equal(outs[0], outs[1])
+    assert np.array_equal(outs[0][:N], outs[1][:N])

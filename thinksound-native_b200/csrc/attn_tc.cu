@@ -286,29 +286,66 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ C
 // attn_short_kernel: the same product for sequences of at most SHORT_MAX_KT * 64 = 384 keys (the DiT's
 // 188-row fused blocks and 329-row joint blocks at the 8 s geometry, the encoders' 77 tokens), where
 // every key and value tile of an (arm, head) fits in shared memory at once and the whole score row
-// fits in TMEM. No online softmax: the UMMAs write S for every key tile as its K tile lands, the
-// softmax warps take the exact row maximum in one pass over TMEM, then write P (f16 pairs) over the
-// columns of S they have consumed, one 64-key tile at a time, and the PV product of tile j starts as
-// soon as P_j is written. One CTA per (128 query rows, head, arm), 192 threads:
-//   warp 4      TMA: Q (hi, lo) and every K and V tile (hi, lo), each on its own barrier
-//   warp 5      one thread issues S_j = Qh·Kh_j^T + Qh·Kl_j^T + Ql·Kh_j^T into TMEM columns
-//               [64 j, 64 j + 64), then O = sum_j P_j·(Vh_j + Vl_j) with P_j read from TMEM
-//   warps 0-3   one query row per thread: row max, p = 2^(s·scale_log2 + bias - max), row sum of
-//               the f32 p, P_j in f16 into TMEM, then O / sum as the split f16 output
+// fits in TMEM. No online softmax: the UMMAs write S_j for key tile j as its K tile lands; the
+// softmax takes the exact row maximum, writes P_j (f16 pairs) over the first half of S_j's columns,
+// and the PV product of tile j starts as soon as P_j is written. One CTA per (128 query rows, head,
+// arm), 448 threads:
+//   warp 12     TMA: Q (hi, lo) and every K and V tile (hi, lo), each on its own barrier
+//   warp 13     one thread issues S_j = Qh·Kh_j^T + Qh·Kl_j^T + Ql·Kh_j^T into TMEM columns
+//               [64 j, 64 j + 64) (one commit per tile), then O = sum_j P_j·(Vh_j + Vl_j) with P_j
+//               read from TMEM
+//   warps 0-11  SHORT_G groups of four warps (warp w reads TMEM lanes 32 (w % 4) ..: one query row
+//               per thread); group g owns key tiles g, g + SHORT_G, ...: the row maximum and row sum
+//               of its tiles, combined across the groups through shared memory in group order (the
+//               result does not depend on timing), p = 2^(s·scale_log2 + bias - max) in f32 (pairs
+//               through the f32x2 FMA), P_j in f16 into TMEM; groups 0 and 1 write 32 columns each of
+//               O / sum as the split f16 output.
+// Spreading a row's keys over three warps per TMEM lane quadrant shortens the per-warp dependent
+// chain of the softmax threefold; the exponentials are bound by the SFU rate (16 per cycle per SM).
 // With an additive logit bias (the text encoders' T5 relative-position bias / pad mask, CLIP's causal
 // and EOT mask; log2 units, -inf masks a key) the bias is added to the scaled logit of every key.
 // Every wait is bounded; an aborted CTA waits (bounded) for its issued copies and UMMAs before it
 // frees its TMEM and exits.
 constexpr int SHORT_MAX_KT = 6;
-constexpr int SH_OFF_K = 2 * Q_BYTES;                  // [tile][hi | lo], then V the same way
+constexpr int SHORT_G = 3;                             // softmax warp groups
+constexpr int SHORT_THREADS = 32 * (4 * SHORT_G + 2);
+constexpr int SH_OFF_K = 2 * Q_BYTES;                  // K: [hi tile 0 .. nkt-1][lo tile 0 .. nkt-1], then V the same way
 __host__ __device__ constexpr int short_smem_bytes(int nkt) { return SH_OFF_K + 2 * nkt * 2 * KV_BYTES + 256; }
 
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float & a, float & b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+// (a0, a1) * (b0, b1) + (c0, c1), each lane rounded once
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__global__ void __launch_bounds__(SHORT_THREADS, 1)
 attn_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const AttnArgs a, int * err) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    unsigned long long * tr = a.trace ? a.trace + 3 * ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
+    constexpr int W_TMA = 4 * SHORT_G, W_MMA = 4 * SHORT_G + 1;
+    // stamps (globaltimer ns, 8 per CTA): 0 entry, 1 upstream done, 2 Q landed, 3 every S product
+    // complete, 4 row maximum known, 5 exit, 6 every P written, 7 O complete
+    unsigned long long * tr = a.trace ? a.trace + 8 * ((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) : nullptr;
     if (tr && threadIdx.x == 0) tr[0] = global_ns();
     const int nkt = (a.S + 63) >> 6;
     if ((smem_u32(smem) & 1023) || nkt < 1 || nkt > SHORT_MAX_KT) {
@@ -320,12 +357,16 @@ attn_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     uint64_t * q_full = bar;                           // Q landed
     uint64_t * k_full = bar + 1;                       // [nkt] K tile j landed
     uint64_t * v_full = k_full + SHORT_MAX_KT;         // [nkt] V tile j landed
-    uint64_t * p_ready = v_full + SHORT_MAX_KT;        // [nkt] P_j in TMEM (4 arrivals)
-    uint64_t * s_full = p_ready + SHORT_MAX_KT;        // every S_j in TMEM
-    uint64_t * o_full = s_full + 1;                    // O complete
+    uint64_t * s_full = v_full + SHORT_MAX_KT;         // [nkt] S_j in TMEM (and every S before it)
+    uint64_t * p_ready = s_full + SHORT_MAX_KT;        // [nkt] P_j in TMEM (4 arrivals)
+    uint64_t * o_full = p_ready + SHORT_MAX_KT;        // O complete
     uint64_t * drain = o_full + 1;                     // abort path: the issued UMMAs have completed
     uint32_t * tslot = (uint32_t *) (drain + 1);
     volatile int * abort_flag = (volatile int *) (tslot + 1);
+    // per-row partial maxima and sums of the softmax groups, in the Q tile's space once every S
+    // product (the only reader of Q) has completed
+    float * red_max = (float *) smem;                  // [SHORT_G][128]
+    float * red_sum = red_max + SHORT_G * 128;         // [SHORT_G][128]
     const uint32_t tcols = nkt <= 3 ? 256u : 512u;
     const uint32_t TM_OS = 64u * (uint32_t) nkt;      // O after the score columns
 
@@ -334,22 +375,23 @@ attn_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int j = 0; j < SHORT_MAX_KT; ++j) { mbar_init(&k_full[j], 1); mbar_init(&v_full[j], 1); mbar_init(&p_ready[j], 4); }
-        mbar_init(s_full, 1);
+        for (int j = 0; j < SHORT_MAX_KT; ++j) {
+            mbar_init(&k_full[j], 1); mbar_init(&v_full[j], 1); mbar_init(&s_full[j], 1); mbar_init(&p_ready[j], 4);
+        }
         mbar_init(o_full, 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbar_init();
         pdl_trigger();
     }
-    if (warp == 4 && lane == 0) { tma_prefetch(&tq); tma_prefetch(&tk); tma_prefetch(&tv); }
-    if (warp == 5) tmem_alloc(tslot, tcols);
+    if (warp == W_TMA && lane == 0) { tma_prefetch(&tq); tma_prefetch(&tk); tma_prefetch(&tv); }
+    if (warp == W_MMA) tmem_alloc(tslot, tcols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
 
-    if (warp == 4) {
+    if (warp == W_TMA) {
         if (lane == 0) {
             pdl_wait();
             if (tr) tr[1] = global_ns();
@@ -357,29 +399,37 @@ attn_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
             tma_load_3d(smem, &tq, q_full, 0, head_row + qt * 128, 0);
             tma_load_3d(smem + Q_BYTES, &tq, q_full, 0, head_row + qt * 128, 1);
             for (int j = 0; j < nkt; ++j) {
-                uint8_t * t = smem + SH_OFF_K + j * 2 * KV_BYTES;
+                uint8_t * t = smem + SH_OFF_K + j * KV_BYTES;
                 mbar_expect_tx(&k_full[j], 2 * KV_BYTES);
                 tma_load_3d(t, &tk, &k_full[j], 0, head_row + j * 64, 0);
-                tma_load_3d(t + KV_BYTES, &tk, &k_full[j], 0, head_row + j * 64, 1);
+                tma_load_3d(t + nkt * KV_BYTES, &tk, &k_full[j], 0, head_row + j * 64, 1);
             }
             for (int j = 0; j < nkt; ++j) {
-                uint8_t * t = smem + off_v + j * 2 * KV_BYTES;
+                uint8_t * t = smem + off_v + j * KV_BYTES;
                 mbar_expect_tx(&v_full[j], 2 * KV_BYTES);
                 tma_load_3d(t, &tv, &v_full[j], 0, head_row + j * 64, 0);
-                tma_load_3d(t + KV_BYTES, &tv, &v_full[j], 0, head_row + j * 64, 1);
+                tma_load_3d(t + nkt * KV_BYTES, &tv, &v_full[j], 0, head_row + j * 64, 1);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == W_MMA) {
         if (lane == 0) {
-            const uint32_t id_s = umma_idesc_f16(64, 0), id_pv = umma_idesc_f16(64, 0, 1);
+            const uint32_t id_pv = umma_idesc_f16(64, 0, 1);
             const uint64_t qh = umma_desc_sw128(smem), ql = umma_desc_sw128(smem + Q_BYTES);
             bool ok = mbar_wait(q_full, 0, abort_flag, err, DEV_TIMEOUT_FULL);
-            for (int j = 0; j < nkt && ok; ++j) {      // S_j as K tile j lands
-                if (!(ok = mbar_wait(&k_full[j], 0, abort_flag, err, DEV_TIMEOUT_FULL))) break;
+            if (tr) tr[2] = global_ns();
+            // S for key tiles [j0, j0 + w) in one set of UMMAs with N = 64 w (the hi and lo K tiles
+            // are each contiguous, so w tiles form one K-major operand): nkt in chunks of at most
+            // four, sizes as even as possible
+            const int nch = (nkt + 3) / 4;
+            for (int c = 0, j0 = 0; c < nch && ok; ++c) {
+                const int w = (nkt - j0 + (nch - c) - 1) / (nch - c);
+                for (int j = j0; j < j0 + w && ok; ++j) ok = mbar_wait(&k_full[j], 0, abort_flag, err, DEV_TIMEOUT_FULL);
+                if (!ok) break;
                 tc_fence_after();
-                const uint8_t * k = smem + SH_OFF_K + j * 2 * KV_BYTES;
-                const uint64_t kh = umma_desc_sw128(k), kl = umma_desc_sw128(k + KV_BYTES);
-                const uint32_t d = tmem + 64u * (uint32_t) j;
+                const uint8_t * k = smem + SH_OFF_K + j0 * KV_BYTES;
+                const uint64_t kh = umma_desc_sw128(k), kl = umma_desc_sw128(k + nkt * KV_BYTES);
+                const uint32_t id_s = umma_idesc_f16(64 * w, 0);
+                const uint32_t d = tmem + 64u * (uint32_t) j0;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t o = (uint64_t) (2 * kk);
@@ -387,17 +437,18 @@ attn_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
                     umma_f16(d, qh + o, kl + o, id_s, 1u);
                     umma_f16(d, ql + o, kh + o, id_s, 1u);
                 }
+                for (int j = j0; j < j0 + w; ++j) umma_commit(&s_full[j]);
+                j0 += w;
             }
-            if (ok) umma_commit(s_full);
             for (int j = 0; j < nkt && ok; ++j) {      // O += P_j (Vh_j + Vl_j) as P_j is written
                 if (!(ok = mbar_wait(&p_ready[j], 0, abort_flag, err, DEV_TIMEOUT_TMEM))) break;
                 if (!(ok = mbar_wait(&v_full[j], 0, abort_flag, err, DEV_TIMEOUT_FULL))) break;
                 tc_fence_after();
-                const uint8_t * v = smem + off_v + j * 2 * KV_BYTES;
+                const uint8_t * v = smem + off_v + j * KV_BYTES;
                 const uint32_t p = tmem + 32u * (uint32_t) j;
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t vh = umma_desc_sw128_mn(v + kk * 2048), vl = umma_desc_sw128_mn(v + KV_BYTES + kk * 2048);
+                    const uint64_t vh = umma_desc_sw128_mn(v + kk * 2048), vl = umma_desc_sw128_mn(v + nkt * KV_BYTES + kk * 2048);
                     umma_f16_ts(tmem + TM_OS, p + 8 * kk, vh, id_pv, (j | kk) != 0);
                     umma_f16_ts(tmem + TM_OS, p + 8 * kk, vl, id_pv, 1u);
                 }
@@ -412,84 +463,154 @@ attn_short_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     } else {
         // ------------------------------------------------------------------ softmax warps
         pdl_wait();
-        const int r = warp * 32 + lane;                          // query row within the tile
+        const int g = warp >> 2, qd = warp & 3;
+        const int r = qd * 32 + lane;                            // query row within the tile
         const int row = qt * 128 + r;                            // joint row
-        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        const uint32_t trow = tmem + ((uint32_t) (qd * 32) << 16);
         const float * lb = a.lbias ? a.lbias + (((size_t) b * a.NH + h) * a.S + (size_t) min(row, a.S - 1)) * a.S_pad
                                    : nullptr;
-        bool ok = mbar_wait(s_full, 0, abort_flag, err, DEV_TIMEOUT_TMEM);
-        float m = -INFINITY, l = 0.0f;
-        if (ok) {
+        bool ok = true;
+        // pass 1: this group's maximum of the scaled (and biased) logits; keys >= S are masked
+        float mloc = -INFINITY;
+        for (int j = g; j < nkt && ok; j += SHORT_G) {
+            if (!(ok = mbar_wait(&s_full[j], 0, abort_flag, err, DEV_TIMEOUT_TMEM))) break;
             tc_fence_after();
-            // pass 1: the row maximum of the scaled (and biased) logits; keys >= S are masked
-            for (int c = 0; c < 2 * nkt; ++c) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
                 float v[32];
-                tmem_ld32(trow + 32u * (uint32_t) c, v);
-                float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                tmem_ld32(trow + 64u * (uint32_t) j + 32u * (uint32_t) c, v);
+                const int key0 = j * 64 + c * 32;
+                if (lb) {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int key = c * 32 + e;
-                    float x = lb ? fmaf(v[e], a.scale_log2, lb[key]) : v[e] * a.scale_log2;
-                    if (key >= a.S) x = -INFINITY;
-                    mq[e & 3] = fmaxf(mq[e & 3], x);
+                    for (int e = 0; e < 32; ++e) v[e] = fmaf(v[e], a.scale_log2, lb[key0 + e]);
                 }
-                m = fmaxf(m, fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])));
+                if (key0 + 32 > a.S) {
+#pragma unroll
+                    for (int e = 0; e < 32; ++e)
+                        if (key0 + e >= a.S) v[e] = -INFINITY;
+                }
+                float mq[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+                for (int e = 4; e < 32; e += 8) {
+                    mq[0] = max3f(mq[0], v[e], v[e + 1]);
+                    mq[1] = max3f(mq[1], v[e + 2], v[e + 3]);
+                    mq[2] = max3f(mq[2], v[e + 4], v[e + 5]);
+                    mq[3] = max3f(mq[3], v[e + 6], v[e + 7]);
+                }
+                mloc = max3f(mloc, max3f(mq[0], mq[1], mq[2]), mq[3]);
             }
-            if (m == -INFINITY) m = 0.0f;                        // a row whose keys are all masked
-            // pass 2: p = 2^(x - m), its f32 row sum, P_j as f16 pairs over S_j's first half
-            for (int j = 0; j < nkt; ++j) {
-                float v[64];
-                tmem_ld32(trow + 64u * (uint32_t) j, v);
-                tmem_ld32(trow + 64u * (uint32_t) j + 32u, v + 32);
-                float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-                for (int e = 0; e < 64; ++e) {
-                    const int key = j * 64 + e;
-                    const float x = lb ? fmaf(v[e], a.scale_log2, lb[key]) - m : fmaf(v[e], a.scale_log2, -m);
-                    v[e] = key < a.S ? ex2(x) : 0.0f;
-                    sq[e & 3] += v[e];
-                }
-                l += (sq[0] + sq[1]) + (sq[2] + sq[3]);
-                uint32_t pk[32];
-#pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const __half2 hv = __floats2half2_rn(v[2 * c], v[2 * c + 1]);
-                    pk[c] = *(const uint32_t *) &hv;
-                }
-                tmem_st32(trow + 32u * (uint32_t) j, pk);
-                tmem_st_wait();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&p_ready[j]);
-            }
-            ok = mbar_wait(o_full, 0, abort_flag, err, DEV_TIMEOUT_TMEM);
         }
+        if (!lb && mloc != -INFINITY) mloc *= a.scale_log2;     // scale > 0: the max of the scaled logits
+        // every S product is complete once the last tile's commit has arrived: Q's space is free
+        if (ok) ok = mbar_wait(&s_full[nkt - 1], 0, abort_flag, err, DEV_TIMEOUT_TMEM);
+        if (tr && warp == 0 && lane == 0) tr[3] = global_ns();
+        if (ok) red_max[g * 128 + r] = mloc;
+        epi_bar_n(128 * SHORT_G);
+        if (tr && warp == 0 && lane == 0) tr[4] = global_ns();
+        float m = -INFINITY;
         if (ok) {
-            tc_fence_after();
-            float o[64];
-            tmem_ld32(trow + TM_OS, o);
-            tmem_ld32(trow + TM_OS + 32u, o + 32);
-            store_row(a, b, h, row, o, l);
+#pragma unroll
+            for (int q = 0; q < SHORT_G; ++q) m = fmaxf(m, red_max[q * 128 + r]);
+            if (m == -INFINITY) m = 0.0f;                        // a row whose keys are all masked
+        }
+        // pass 2: p = 2^(x - m), the f32 row sum, P_j as f16 pairs over S_j's first half
+        float lloc = 0.0f;
+        const uint64_t sc2 = f2_pack(a.scale_log2, a.scale_log2), nm2 = f2_pack(-m, -m);
+        for (int j = g; j < nkt && ok; j += SHORT_G) {
+            float v[64];
+            tmem_ld32(trow + 64u * (uint32_t) j, v);
+            tmem_ld32(trow + 64u * (uint32_t) j + 32u, v + 32);
+            uint64_t s2[4] = {0, 0, 0, 0};
+            uint32_t pk[32];
+#pragma unroll
+            for (int e = 0; e < 64; e += 2) {
+                const int key = j * 64 + e;
+                uint64_t x2 = lb ? fadd2(ffma2(f2_pack(v[e], v[e + 1]), sc2, f2_pack(lb[key], lb[key + 1])), nm2)
+                                 : ffma2(f2_pack(v[e], v[e + 1]), sc2, nm2);
+                float x0, x1;
+                f2_unpack(x2, x0, x1);
+                const float p0 = key < a.S ? ex2(x0) : 0.0f, p1 = key + 1 < a.S ? ex2(x1) : 0.0f;
+                const uint64_t p2 = f2_pack(p0, p1);
+                s2[(e >> 1) & 3] = fadd2(s2[(e >> 1) & 3], p2);
+                const __half2 hv = __floats2half2_rn(p0, p1);
+                pk[e >> 1] = *(const uint32_t *) &hv;
+            }
+            const uint64_t t2 = fadd2(fadd2(s2[0], s2[1]), fadd2(s2[2], s2[3]));
+            float t0, t1;
+            f2_unpack(t2, t0, t1);
+            lloc += t0 + t1;
+            tmem_st32(trow + 32u * (uint32_t) j, pk);
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_ready[j]);
+        }
+        if (ok) red_sum[g * 128 + r] = lloc;
+        epi_bar_n(128 * SHORT_G);
+        if (tr && warp == 0 && lane == 0) tr[6] = global_ns();
+        // O / l as split f16 halves, staged in shared memory over K and V (free once O is complete)
+        // as [hi | lo][128 rows][64 cols], the 16-byte chunk c of a row at c ^ (row & 7), so that
+        // the stores below write whole 128-byte row runs
+        uint8_t * stage = smem + SH_OFF_K;
+        if (ok && g < 2) {
+            float l = 0.0f;
+#pragma unroll
+            for (int q = 0; q < SHORT_G; ++q) l += red_sum[q * 128 + r];
+            if ((ok = mbar_wait(o_full, 0, abort_flag, err, DEV_TIMEOUT_TMEM))) {
+                if (tr && warp == 0 && lane == 0) tr[7] = global_ns();
+                tc_fence_after();
+                float o[32];
+                tmem_ld32(trow + TM_OS + 32u * (uint32_t) g, o);
+                const float inv = 1.0f / l;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    __align__(16) __half hv[8], lv[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        const float v = o[c * 8 + e] * inv;
+                        hv[e] = __float2half_rn(v);
+                        lv[e] = __float2half_rn(v - __half2float(hv[e]));
+                    }
+                    const int pc = ((4 * g + c) ^ (r & 7)) << 4;
+                    *(uint4 *) (stage + r * 128 + pc) = *(const uint4 *) hv;
+                    *(uint4 *) (stage + 128 * 128 + r * 128 + pc) = *(const uint4 *) lv;
+                }
+            }
+        }
+        epi_bar_n(128 * SHORT_G);
+        if (!*abort_flag) {
+            // 256 row runs (hi and lo of 128 rows) of 128 bytes, four per warp instruction
+            for (int seg = warp * 4 + (lane >> 3); seg < 256; seg += 4 * 4 * SHORT_G) {
+                const int half = seg >> 7, rr = seg & 127, srow = qt * 128 + rr, ch = lane & 7;
+                if (srow >= a.S) continue;
+                __half * dst;
+                long long olo;
+                if (srow < a.n0) { dst = a.out0 + ((size_t) b * a.n0 + srow) * a.H; olo = a.out_lo0; }
+                else if (srow < a.n0 + a.n1) { dst = a.out1 + ((size_t) b * a.n1 + (srow - a.n0)) * a.H; olo = a.out_lo1; }
+                else { dst = a.out2 + ((size_t) b * a.n2 + (srow - a.n0 - a.n1)) * a.H; olo = a.out_lo2; }
+                if (half && !olo) continue;
+                const uint4 v = *(const uint4 *) (stage + half * 128 * 128 + rr * 128 + ((ch ^ (rr & 7)) << 4));
+                *(uint4 *) (dst + (half ? olo : 0) + h * 64 + ch * 8) = v;
+            }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (*abort_flag && warp == 4 && lane == 0) {
+    if (*abort_flag && warp == W_TMA && lane == 0) {
         // copies issued but never consumed must land before this CTA's shared memory is reused
         const uint64_t t0 = global_ns();
-        bool landed = mbar_try_wait(q_full, 0);
-        for (int j = 0; j < nkt; ++j) landed = landed && mbar_try_wait(&k_full[j], 0) && mbar_try_wait(&v_full[j], 0);
+        bool landed = false;
         while (!landed && global_ns() - t0 < 1000000ull) {
             landed = mbar_try_wait(q_full, 0);
             for (int j = 0; j < nkt; ++j) landed = landed && mbar_try_wait(&k_full[j], 0) && mbar_try_wait(&v_full[j], 0);
         }
     }
     __syncthreads();
-    if (warp == 5) {
+    if (warp == W_MMA) {
         tc_fence_after();
         tmem_dealloc(tmem, tcols);
     }
-    if (tr && threadIdx.x == 0) tr[2] = global_ns();
+    if (tr && threadIdx.x == 0) tr[5] = global_ns();
 }
 
 } // namespace
@@ -504,7 +625,7 @@ bool attention_short_fits(int S) { return S >= 1 && S <= SHORT_MAX_KT * 64; }
 cudaError_t launch_attention_short(const AttnMaps & m, const AttnArgs & a, cudaStream_t s) {
     if (!attention_short_fits(a.S)) return cudaErrorInvalidValue;
     const int nkt = (a.S + 63) / 64;
-    return launch_ex(attn_short_kernel, dim3((a.S + 127) / 128, a.NH, a.B), dim3(192), short_smem_bytes(nkt), s, 1u, m.q,
+    return launch_ex(attn_short_kernel, dim3((a.S + 127) / 128, a.NH, a.B), dim3(SHORT_THREADS), short_smem_bytes(nkt), s, 1u, m.q,
                      m.k, m.v, a, a.err);
 }
 

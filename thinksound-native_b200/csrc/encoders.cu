@@ -647,11 +647,12 @@ struct EncModel {
                 at.out0 = att; at.n0 = n; at.H = d; at.qkv_lo = qkv_lo; at.out_lo0 = (long long) n * d;
                 at.err = dev->d_err;
                 at.lbias = lb;
-                // the tcgen05 short-sequence kernel with the logit-bias table (TSN_ATTN_MMA_SYNC=1:
+                // the tcgen05 short-sequence kernel with the logit-bias table (TSN_ATTN_KERNEL=mma:
                 // the earlier mma.sync kernel, for comparison)
                 AttnMaps mp{};
                 const uint64_t rows = (uint64_t) NH * S_pad;
-                const bool tc = attention_short_fits(n) && !std::getenv("TSN_ATTN_MMA_SYNC");
+                const char * ak = std::getenv("TSN_ATTN_KERNEL");
+                const bool tc = attention_short_fits(n) && !(ak && !strcmp(ak, "mma"));
                 if (tc && !(make_head_map(&mp.q, q, rows, 128, (uint64_t) qkv_lo) &&
                             make_head_map(&mp.k, k, rows, 64, (uint64_t) qkv_lo) &&
                             make_head_map(&mp.v, v, rows, 64, (uint64_t) qkv_lo)))

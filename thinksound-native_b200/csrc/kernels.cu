@@ -472,151 +472,202 @@ __device__ __forceinline__ void cvt8(uint4 w, int bf16, float * f) {
         f[e] = bf16 ? __uint_as_float((uint32_t) h[e] << 16) : __half2float(__ushort_as_half(h[e]));
 }
 
-// Weight streaming: one block per SM (grid = min(stages, SMs)) walks the batch's 8-row stages
-// (stage s of the concatenated jobs at blocks b, b + grid, ...). Warp 8's lane 0 streams each stage's
-// rows (one contiguous run of up to 8 x K x 2 bytes) into an 8-slot shared-memory ring with bulk
-// copies that complete on the slot's full barrier, up to 8 stages (128 KB at K = 1024) in flight per
-// SM; the first copies are issued before the wait on the upstream kernel (weights do not depend on
-// it). Warps 0-7 take one row of a stage each: every lane sums its 8-element runs of the row in k
-// order against x (all arms, held in shared memory, loaded once per block), the warp adds the 32 lane
-// sums in a fixed butterfly, so a row's result does not depend on the grid. A warp releases the slot
-// on its empty barrier (8 arrivals) once it has read it. Every job of a batch shares x, K and the arm
-// count. Every wait is bounded; a block that gives up waits (bounded) for the copies it issued
-// before it exits.
-constexpr int GS_ROWS = 8, GS_STAGES = 8, GS_WARPS = 8;
-constexpr int GS_THREADS = 32 * (GS_WARPS + 1);
+// Weight streaming: one block of GS_WARPS warps per SM (grid = min(ceil(slots / GS_WARPS), SMs));
+// the batch's rows are taken as slots of R = 2 consecutive rows of one job, and every warp walks its
+// own slots (warp-slot index i = block * GS_WARPS + warp, i + GS_WARPS * grid, ...) through its own
+// ring of three slots: lane 0 brings a slot's rows (one contiguous run of R x K x 2 bytes) into
+// shared memory with one bulk copy that completes on the stage's barrier, so 192 KB are in flight
+// per SM at K = 1024 and no warp waits on another. The first
+// copies are issued before the wait on the upstream kernel (weights do not depend on it). Lane l sums
+// the runs k = 128 c + 4 l .. + 3 of each row in c order against x, and the warp adds the 32 lane
+// sums in a fixed butterfly, so a row's result does not depend on the grid. x (every arm) is loaded
+// once: for up to two arms into registers (the kernel is otherwise bound by shared-memory reads of x,
+// one per row pair), else into shared memory (16-byte reads by consecutive lanes, free of bank
+// conflicts; each read serves both rows of a slot). Every job of a batch shares x, K and the arm count. Every wait
+// is bounded; a warp that gives up, or stops because another gave up, waits (bounded) for every copy
+// it issued and did not consume before the block exits.
+constexpr int GS_WARPS = 16, GS_RING = 12288;   // warps per block, ring bytes per warp at K = 1024
+constexpr int GS_THREADS = 32 * GS_WARPS;
+constexpr int GS_KC = GEMV_MAX_K / 128;             // 128-element runs per row
+__host__ __device__ constexpr int gemv_rows_per_slot(int) { return 2; }
+__host__ __device__ constexpr int gemv_stages(int nb) { return GS_RING / (gemv_rows_per_slot(nb) * GEMV_MAX_K * 2); }
 
 __host__ __device__ inline size_t gemv_smem_bytes(int K, int nb) {
-    return (size_t) GS_STAGES * GS_ROWS * K * 2 + (size_t) nb * K * 4 + 2 * GS_STAGES * 8 + 16;
+    return (size_t) GS_WARPS * gemv_stages(nb) * gemv_rows_per_slot(nb) * K * 2 + (nb > 2 ? (size_t) nb * K * 4 : 0) +
+           (size_t) GS_WARPS * gemv_stages(nb) * 8 + 16;
 }
 
-// stage s of the batch: its job q, first row n0 and row count
-__device__ __forceinline__ int gemv_stage(const GemvBatch & jb, int njobs, long long s, int & q, int & n0) {
-    for (q = 0; q < njobs; ++q) {
-        const long long ns = (jb.j[q].N + GS_ROWS - 1) / GS_ROWS;
-        if (s < ns) { n0 = (int) s * GS_ROWS; return min(GS_ROWS, jb.j[q].N - n0); }
-        s -= ns;
+// slot s of the batch (R consecutive rows of one job): its job q, first row n0 and row count. A warp
+// walks its slots in increasing order, so q only moves forward from the previous slot's job.
+template <int R>
+__device__ __forceinline__ int gemv_slot(const GemvBatch & jb, int njobs, int s, int & q, int & n0) {
+    while (q + 1 < njobs && s >= jb.slot_end[q]) ++q;
+    n0 = (s - (q ? jb.slot_end[q - 1] : 0)) * R;
+    return min(R, jb.j[q].N - n0);
+}
+__device__ __forceinline__ void cvt4(uint2 w, int bf16, float * f) {
+    if (bf16) {
+        f[0] = __uint_as_float(w.x << 16); f[1] = __uint_as_float(w.x & 0xFFFF0000u);
+        f[2] = __uint_as_float(w.y << 16); f[3] = __uint_as_float(w.y & 0xFFFF0000u);
+    } else {
+        const float2 a = __half22float2(*(const __half2 *) &w.x), b = __half22float2(*(const __half2 *) &w.y);
+        f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
     }
-    return 0;
 }
 
 template <int NB>
 __global__ void __launch_bounds__(GS_THREADS, 1) gemv_kernel(const __grid_constant__ GemvBatch jb, int njobs,
-                                                            long long total, int ab_bf16, int * err) {
+                                                            long long total, int ab_bf16, int * err,
+                                                            unsigned long long * trace) {
+    constexpr int GS_R = gemv_rows_per_slot(NB), GS_STAGES = gemv_stages(NB);
+    constexpr bool XREG = NB <= 2;
     extern __shared__ __align__(128) uint8_t gs_smem[];
+    // optional stamps (globaltimer ns, 3 per block): entry, upstream done, exit
+    unsigned long long * tr = trace ? trace + 3 * blockIdx.x : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = global_ns();
     const int K = jb.j[0].K, nb = jb.j[0].nb;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    uint8_t * ring = gs_smem;
-    const size_t stage_bytes = (size_t) GS_ROWS * K * 2;
-    float * xs = (float *) (gs_smem + GS_STAGES * stage_bytes);
-    uint64_t * full = (uint64_t *) (xs + (size_t) nb * K);
-    uint64_t * empty = full + GS_STAGES;
-    int * abort_word = (int *) (empty + GS_STAGES);
-    int * n_issued = abort_word + 1;
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < GS_STAGES; ++st) { mbar_init(&full[st], 1); mbar_init(&empty[st], GS_WARPS); }
-        *abort_word = 0;
-        *n_issued = 0;
+    const size_t slot_bytes = (size_t) GS_R * K * 2;
+    uint8_t * ring = gs_smem + (size_t) w * GS_STAGES * slot_bytes;          // this warp's ring
+    float * xs = (float *) (gs_smem + (size_t) GS_WARPS * GS_STAGES * slot_bytes);
+    const size_t xs_floats = XREG ? 0 : (size_t) nb * K;
+    uint64_t * bars = (uint64_t *) (xs + xs_floats) + w * GS_STAGES;        // this warp's barriers
+    int * abort_word = (int *) ((uint64_t *) (xs + xs_floats) + GS_WARPS * GS_STAGES);
+    if (threadIdx.x == 0) *abort_word = 0;
+    if (lane == 0) {
+        for (int st = 0; st < GS_STAGES; ++st) mbar_init(&bars[st], 1);
         fence_mbar_init();
     }
     __syncthreads();
     pdl_trigger();
     volatile int * abort_flag = abort_word;
-    const long long stride = gridDim.x;
-    if (w == GS_WARPS) {
-        // ---------------------------------------------------------------- producer
-        if (lane == 0) {
-            int i = 0;
-            for (;; ++i) {
-                const long long s = blockIdx.x + (long long) i * stride;
-                if (s >= total) break;
-                const int st = i % GS_STAGES;
-                if (i >= GS_STAGES && !mbar_wait(&empty[st], ((i / GS_STAGES) - 1) & 1, abort_flag, err, DEV_TIMEOUT_EMPTY))
-                    break;
-                fence_proxy_async_smem();
-                int q = 0, n0 = 0;
-                const int rows = gemv_stage(jb, njobs, s, q, n0);
-                const uint32_t bytes = (uint32_t) rows * (uint32_t) K * 2u;
-                mbar_expect_tx(&full[st], bytes);
-                bulk_load(ring + st * stage_bytes, (const uint16_t *) jb.j[q].W + (size_t) n0 * K, bytes, &full[st]);
-                *(volatile int *) n_issued = i + 1;
-            }
-        }
-    } else {
-        // ---------------------------------------------------------------- consumers
-        pdl_wait();
+    const long long stride = (long long) gridDim.x * GS_WARPS;
+    const long long s0 = (long long) blockIdx.x * GS_WARPS + w;
+    int qi = 0, qc = 0;                       // job cursors of the issuing lane and of the consumer
+    auto issue = [&](long long s, int st) {   // lane 0: slot s into stage st
+        if (s >= total) return;
+        int n0 = 0;
+        const int rows = gemv_slot<GS_R>(jb, njobs, (int) s, qi, n0);
+        const uint32_t bytes = (uint32_t) rows * (uint32_t) K * 2u;
+        mbar_expect_tx(&bars[st], bytes);
+        bulk_load(ring + st * slot_bytes, (const uint16_t *) jb.j[qi].W + (size_t) n0 * K, bytes, &bars[st]);
+    };
+    if (lane == 0)
+        for (int st = 0; st < GS_STAGES; ++st) issue(s0 + st * stride, st);
+    pdl_wait();
+    if (tr && threadIdx.x == 0) tr[1] = global_ns();
+    // this lane's x runs (k = 128 c + 4 lane) of every arm, or every arm's x in shared memory
+    float4 xr[XREG ? NB : 1][GS_KC];
+    {
         const GemvJob & j0 = jb.j[0];
         const float * x = j0.x + (j0.x_step ? (long long) (*j0.x_step) * j0.x_step_stride : 0);
-        for (int e = threadIdx.x; e < nb * K; e += 32 * GS_WARPS) {
-            const int bb = e / K, k = e % K;
-            xs[e] = x[(long long) bb * j0.x_bs + k];
+        if constexpr (XREG) {
+#pragma unroll
+            for (int bb = 0; bb < NB; ++bb)
+#pragma unroll
+                for (int c = 0; c < GS_KC; ++c) {
+                    const int k = c * 128 + lane * 4;
+                    xr[bb][c] = bb < nb && k < K ? *(const float4 *) (x + (long long) bb * j0.x_bs + k)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+        } else {
+            for (int e = threadIdx.x; e < nb * K; e += GS_THREADS) {
+                const int bb = e / K, k = e % K;
+                xs[e] = x[(long long) bb * j0.x_bs + k];
+            }
+            __syncthreads();
         }
-        epi_bar_n(GS_WARPS * 32);
-        for (int i = 0;; ++i) {
-            const long long s = blockIdx.x + (long long) i * stride;
-            if (s >= total) break;
-            const int st = i % GS_STAGES;
-            if (!mbar_wait(&full[st], (i / GS_STAGES) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) break;
-            int q = 0, n0 = 0;
-            const int rows = gemv_stage(jb, njobs, s, q, n0);
-            const GemvJob & j = jb.j[q];
-            if (w < rows) {
-                const uint8_t * wr = ring + st * stage_bytes + (size_t) w * K * 2;
-                float acc[NB];
+    }
+    int i = 0;
+    for (;; ++i) {
+        const long long s = s0 + (long long) i * stride;
+        if (s >= total) break;
+        const int st = i % GS_STAGES;
+        if (!mbar_wait(&bars[st], (i / GS_STAGES) & 1, abort_flag, err, DEV_TIMEOUT_FULL)) break;
+        int n0 = 0;
+        const int rows = gemv_slot<GS_R>(jb, njobs, (int) s, qc, n0);
+        const GemvJob & j = jb.j[qc];
+        const uint8_t * wb = ring + st * slot_bytes;
+        float acc[GS_R][NB];
 #pragma unroll
-                for (int bb = 0; bb < NB; ++bb) acc[bb] = 0.0f;
-                for (int k = lane * 8; k < K; k += 256) {
-                    float wf[8];
-                    cvt8(*(const uint4 *) (wr + (size_t) k * 2), ab_bf16, wf);
+        for (int r = 0; r < GS_R; ++r)
 #pragma unroll
-                    for (int bb = 0; bb < NB; ++bb) {
-                        if (bb >= nb) break;
-                        const float4 x0 = *(const float4 *) (xs + bb * K + k), x1 = *(const float4 *) (xs + bb * K + k + 4);
-                        acc[bb] += wf[0] * x0.x + wf[1] * x0.y + wf[2] * x0.z + wf[3] * x0.w +
-                                   wf[4] * x1.x + wf[5] * x1.y + wf[6] * x1.z + wf[7] * x1.w;
-                    }
+            for (int bb = 0; bb < NB; ++bb) acc[r][bb] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < GS_KC; ++c) {
+            const int k = c * 128 + lane * 4;
+            if (k >= K) break;
+            float wf[GS_R][4];
+#pragma unroll
+            for (int r = 0; r < GS_R; ++r) {
+                const uint2 wv = r < rows ? *(const uint2 *) (wb + ((size_t) r * K + k) * 2) : make_uint2(0u, 0u);
+                cvt4(wv, ab_bf16, wf[r]);
+            }
+#pragma unroll
+            for (int bb = 0; bb < NB; ++bb) {
+                if (bb >= nb) break;
+                const float4 xv = XREG ? xr[XREG ? bb : 0][c] : *(const float4 *) (xs + bb * K + k);
+#pragma unroll
+                for (int r = 0; r < GS_R; ++r)
+                    acc[r][bb] += wf[r][0] * xv.x + wf[r][1] * xv.y + wf[r][2] * xv.z + wf[r][3] * xv.w;
+            }
+        }
+        __syncwarp();   // every lane has read the stage before lane 0 refills it
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            issue(s + (long long) GS_STAGES * stride, st);
+        }
+#pragma unroll
+        for (int r = 0; r < GS_R; ++r) {
+            if (r >= rows) break;
+#pragma unroll
+            for (int bb = 0; bb < NB; ++bb) {
+                if (bb >= nb) break;
+                float val = acc[r][bb];
+#pragma unroll
+                for (int off = 16; off; off >>= 1) val += __shfl_xor_sync(0xffffffffu, val, off);
+                if (lane == 0) {
+                    if (j.bias) val += j.bias[n0 + r];
+                    if (j.act == 1) val = val / (1.0f + expf(-val));
+                    j.y[bb * j.y_bs + n0 + r] = val;
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[st]);      // the slot's row is read
-#pragma unroll
-                for (int bb = 0; bb < NB; ++bb) {
-                    if (bb >= nb) break;
-                    float val = acc[bb];
-#pragma unroll
-                    for (int off = 16; off; off >>= 1) val += __shfl_xor_sync(0xffffffffu, val, off);
-                    if (lane == 0) {
-                        if (j.bias) val += j.bias[n0 + w];
-                        if (j.act == 1) val = val / (1.0f + expf(-val));
-                        j.y[bb * j.y_bs + n0 + w] = val;
-                    }
-                }
-            } else if (lane == 0) {
-                mbar_arrive(&empty[st]);
             }
         }
     }
-    __syncthreads();
-    if (*abort_flag && w == GS_WARPS && lane == 0) {
-        // copies issued but never consumed must land before this block's shared memory is reused:
-        // wait (bounded) for the last GS_STAGES issued stages
-        const int ni = *(volatile int *) n_issued;
+    if (lane == 0) {
+        // a warp that stopped early: copies issued for slots i .. i + GS_STAGES - 1 that it did not
+        // consume must land before the block's shared memory is reused (bounded)
         const uint64_t t0 = global_ns();
-        for (int i = ni > GS_STAGES ? ni - GS_STAGES : 0; i < ni; ++i)
-            while (!mbar_try_wait(&full[i % GS_STAGES], (i / GS_STAGES) & 1) && global_ns() - t0 < 1000000ull) {}
+        for (int k = i; k < i + GS_STAGES; ++k) {
+            if (s0 + (long long) k * stride >= total) break;
+            while (!mbar_try_wait(&bars[k % GS_STAGES], (k / GS_STAGES) & 1) && global_ns() - t0 < 1000000ull) {}
+        }
+    }
+    if (tr) {
+        __syncthreads();
+        if (threadIdx.x == 0) tr[2] = global_ns();
     }
 }
 
 cudaError_t configure_gemv() {
-    const int bytes = (int) gemv_smem_bytes(GEMV_MAX_K, 8);
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) gemv_smem_bytes(GEMV_MAX_K, 1));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) gemv_smem_bytes(GEMV_MAX_K, 2));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) gemv_smem_bytes(GEMV_MAX_K, 4));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) gemv_smem_bytes(GEMV_MAX_K, 8));
     return e;
 }
 
-cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s) {
+int gemv_blocks(const GemvJob * jobs, int njobs, int nb, int sms) {
+    const int R = gemv_rows_per_slot(nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : 8);
+    long long total = 0;
+    for (int q = 0; q < njobs && q < GEMV_MAX_JOBS; ++q) total += (jobs[q].N + R - 1) / R;
+    return (int) std::min<long long>((total + GS_WARPS - 1) / GS_WARPS, sms);
+}
+
+cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s,
+                        unsigned long long * trace) {
     if (njobs < 1 || max_n < 1 || nb < 1 || nb > 8 || sms < 1) return cudaErrorInvalidValue;
+    const int nbk = nb <= 1 ? 1 : nb <= 2 ? 2 : nb <= 4 ? 4 : 8;   // the kernel instance's arm capacity
     for (int q0 = 0; q0 < njobs; q0 += GEMV_MAX_JOBS) {
         const int n = std::min(GEMV_MAX_JOBS, njobs - q0);
         GemvBatch jb{};
@@ -628,15 +679,20 @@ cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int 
                 ((uintptr_t) j.W & 15) || j.K != jobs[q0].K || j.nb != jobs[q0].nb || j.x != jobs[q0].x ||
                 j.x_bs != jobs[q0].x_bs || j.x_step != jobs[q0].x_step)
                 return cudaErrorInvalidValue;
-            total += (j.N + GS_ROWS - 1) / GS_ROWS;
+            total += (j.N + gemv_rows_per_slot(nbk) - 1) / gemv_rows_per_slot(nbk);
+            jb.slot_end[q] = (int) total;
         }
-        const dim3 grid((unsigned) std::min<long long>(total, sms));
-        const size_t smem = gemv_smem_bytes(jb.j[0].K, jb.j[0].nb);
+        const dim3 grid((unsigned) std::min<long long>((total + GS_WARPS - 1) / GS_WARPS, sms));
+        const size_t smem = gemv_smem_bytes(jb.j[0].K, nbk);
         cudaError_t e;
-        if (nb == 1) e = launch_ex(gemv_kernel<1>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
-        else if (nb == 2) e = launch_ex(gemv_kernel<2>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
-        else if (nb <= 4) e = launch_ex(gemv_kernel<4>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
-        else e = launch_ex(gemv_kernel<8>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err);
+        if (nb == 1) e = launch_ex(gemv_kernel<1>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err,
+                                    q0 ? nullptr : trace);
+        else if (nb == 2) e = launch_ex(gemv_kernel<2>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err,
+                                    q0 ? nullptr : trace);
+        else if (nb <= 4) e = launch_ex(gemv_kernel<4>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err,
+                                    q0 ? nullptr : trace);
+        else e = launch_ex(gemv_kernel<8>, grid, dim3(GS_THREADS), smem, s, 1u, jb, n, total, ab_bf16, err,
+                                    q0 ? nullptr : trace);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;

@@ -172,6 +172,7 @@ struct GemvJob {
 constexpr int GEMV_MAX_JOBS = 16;
 struct GemvBatch {
     GemvJob j[GEMV_MAX_JOBS];
+    int slot_end[GEMV_MAX_JOBS];   // set by launch_gemv: slots (row groups) of jobs 0..q
 };
 constexpr int GEMV_MAX_K = 1024;
 // jobs: host array (copied into the launch's parameters; more than GEMV_MAX_JOBS take several
@@ -180,7 +181,11 @@ constexpr int GEMV_MAX_K = 1024;
 // rows K apart; sms: the device's SM count (one block per SM at most); err: device error word for
 // wait timeouts
 cudaError_t configure_gemv();
-cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s);
+// trace: optional per-block stamps (3 per block: entry, upstream done, exit) of the first launch;
+// gemv_blocks gives its block count
+cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s,
+                        unsigned long long * trace = nullptr);
+int gemv_blocks(const GemvJob * jobs, int njobs, int nb, int sms);
 
 // ---- per-forward conditioning prologue (src/dit_fwd.cpp:131-140, 166-167) ----
 // B batch rows = G generations x A CFG arms (A = 2, or 1 for a single-arm model); the per-

@@ -1075,11 +1075,15 @@ struct Plan {
         // Both kernels are tcgen05 (attn_tc.cu, 128 query rows per CTA, TMA views of q/k/v
         // [hi|lo][B*NH*S_pad][64]): up to 384 keys every key tile stays resident and the softmax
         // takes the exact row maximum (attn_short_kernel); longer sequences stream key tiles
-        // through rings with an online softmax (attn_tc_kernel). TSN_ATTN_MMA_SYNC=1 keeps the
-        // earlier mma.sync kernel (attn_kernel) for sequences below 256 rows, for comparison.
+        // through rings with an online softmax (attn_tc_kernel). For comparison,
+        // TSN_ATTN_KERNEL=stream forces the streaming kernel and =mma the earlier mma.sync kernel
+        // (attn_kernel).
         const uint64_t rows = (uint64_t) m.B * m.g.NH * m.S_pad;
         AttnMaps mp{};
-        const int kind = attention_short_fits(S) ? (S < 256 && std::getenv("TSN_ATTN_MMA_SYNC") ? 0 : 2) : 1;
+        const char * ak = std::getenv("TSN_ATTN_KERNEL");
+        int kind = attention_short_fits(S) ? 2 : 1;
+        if (ak && !strcmp(ak, "stream")) kind = 1;
+        if (ak && !strcmp(ak, "mma")) kind = 0;
         if (kind && !(make_head_map(&mp.q, m.q, rows, 128) && make_head_map(&mp.k, m.k, rows, 64) &&
                       make_head_map(&mp.v, m.v, rows, 64)))
             return fail(TSN_ERR_CUDA, "attention: tensor map encode failed");
@@ -1095,7 +1099,7 @@ struct Plan {
             return go(t, s);
         };
         op.ctas = kind ? ((S + 127) / 128) * (int) m.g.NH * m.B : ((S + 63) / 64) * (int) m.g.NH * m.B;
-        op.trace_slots = 3;
+        op.trace_slots = kind == 2 ? 8 : 3;
         add(op);
         return TSN_OK;
     }
@@ -1189,8 +1193,16 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // the clip/text modulations of every joint block (HBM-bound GEMVs, ~160 MB of weights at the
     // 8 s geometry) in one launch with the GPU to itself: beside the modulation GEMM they starved
     // for L2-to-SM bandwidth and held SMs that the next GEMM's CTAs needed
-    p.add(Op{[jb, nmj, H, nbm, sms, bfl, derr](cudaStream_t s) { return launch_gemv(jb.data() + 2, nmj, 6 * H, nbm, sms, bfl, derr, s); }, 2, 0,
-             "adaln_gemv"});
+    {
+        Op go{[jb, nmj, H, nbm, sms, bfl, derr](cudaStream_t s) { return launch_gemv(jb.data() + 2, nmj, 6 * H, nbm, sms, bfl, derr, s); },
+              2, 0, "adaln_gemv"};
+        go.traced = [jb, nmj, H, nbm, sms, bfl, derr](cudaStream_t s, unsigned long long * tr) {
+            return launch_gemv(jb.data() + 2, nmj, 6 * H, nbm, sms, bfl, derr, s, tr);
+        };
+        go.ctas = gemv_blocks(jb.data() + 2, nmj, nbm, sms);
+        go.trace_slots = 3;
+        p.add(go);
+    }
     if (tp) {
         const size_t sH = (size_t) H, sTH = (size_t) T * H;
         p.tap("t_emb", te, sH * 4, [sH](const std::vector<uint8_t> & raw, int, std::vector<float> & out) {
@@ -1432,7 +1444,8 @@ int Model::timeline(std::vector<double> & rows) {
     for (size_t i = 0; i < ops_fwd.size(); ++i) {
         const Op & o = ops_fwd[i];
         if (!o.traced) continue;
-        const int sl = o.trace_slots, work = o.kind == 0 ? 2 : 1, end = o.kind == 0 ? 5 : 2;
+        // 8 stamps per CTA (GEMMs, the short attention): first work in slot 2, exit in 5; 3 stamps: 1, 2
+        const int sl = o.trace_slots, work = sl == 8 ? 2 : 1, end = sl == 8 ? 5 : 2;
         unsigned long long a0 = ~0ull, w0 = ~0ull, e1 = 0;
         std::vector<unsigned long long> ends;
         for (int c = 0; c < o.ctas; ++c) {
