@@ -58,6 +58,7 @@ def parse():
                     help="time every tile candidate at load instead of the library's built-in tile table (the tuned "
                          "forward may then differ from other processes' in the last bits)")
     ap.add_argument("--cfg-split", action="store_true", help="one CFG arm per rank, pairs of ranks per generation")
+    ap.add_argument("--cfg-split-eager", action="store_true", help="--cfg-split with the steps issued from the host")
     ap.add_argument("--long", action="store_true", help="BASELINE config 4 geometry: 30 s audio (T=704, clip 240, text 77)")
     ap.add_argument("--config5", action="store_true", help="64 generations x 24 steps, data-parallel, final gather")
     ap.add_argument("--gens-per-forward", type=int, default=4, help="config 5: generations batched per forward (1-4)")
@@ -453,14 +454,34 @@ def run_cfg_split(a):
         if a.autotune:
             m.autotune()
         sampler = cfg_split.CfgSplitSampler(m, dev, a.T, group=group)
-        x = torch.from_numpy(x0).cuda()
-        sampler.sample(x, a.warmup, a.cfg)
+        xs = torch.from_numpy(x0).cuda()
+        x = torch.empty_like(xs)
+        # each step (this arm's forward, the NCCL all-gather of the two flows, the CFG update) is
+        # replayed from one CUDA graph; --cfg-split-eager runs the steps from the host instead
+        if not a.cfg_split_eager:
+            sampler.graph_capture(xs, a.cfg)
+            sampler.graph_run(xs, a.warmup)
+        else:
+            x.copy_(xs)
+            sampler.sample(x, a.warmup, a.cfg)
         torch.cuda.synchronize()
         dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        sampler.sample(x, a.steps, a.cfg)
-        e1.record(stream)
+        if not a.cfg_split_eager:
+            m.set_x(xs)
+            m.split_schedule(a.steps)
+            e0.record(stream)
+            for _ in range(a.steps):
+                sampler.graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            m.get_x(x)
+            sampler.graph_release()
+        else:
+            x.copy_(xs)
+            e0.record(stream)
+            sampler.sample(x, a.steps, a.cfg)
+            e1.record(stream)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
         times = torch.tensor([ms], dtype=torch.float64, device="cuda")
@@ -479,7 +500,8 @@ def run_cfg_split(a):
                 "scaling": "weak", "vs_baseline": None, "dtype": "f16 (split hi+lo activations), f32 accumulate",
                 "data": "synthetic",
                 "config": workload(a),
-                "parallelism": f"cfg-split x{world // 2} (one CFG arm per GPU, NCCL all-gather of the flow every step)",
+                "parallelism": f"cfg-split x{world // 2} (one CFG arm per GPU, NCCL all-gather of the flow every step"
+                               f"{', steps from the host' if a.cfg_split_eager else ', every step one CUDA graph'})",
                 "step_roofline": {"compute_ms": compute_ms, "hbm_ms": hbm_ms, "roofline_ms": max(compute_ms, hbm_ms),
                                   "frac": max(compute_ms, hbm_ms) / step_ms,
                                   "peaks": f"{src}: {tf_sus} TFLOP/s sustained bf16, {hbm} GB/s"},

@@ -186,6 +186,22 @@ int tsn_dit_sample(tsn_dit * m, int steps, float cfg);
 /* Run `n` more steps of the schedule installed by the last tsn_dit_schedule (for timing loops). */
 int tsn_dit_schedule(tsn_dit * m, int steps, float cfg);
 int tsn_dit_run_steps(tsn_dit * m, int n);
+/* The sampler with the CFG pair split over two GPUs (src/pipeline.cpp:142-155 with the cond and
+ * uncond forwards of each step on different devices, arms = 1 on each), as three calls that only
+ * issue work on the device's stream (no synchronisation, no host copies, no allocation), so that a
+ * caller can capture a whole step, its own flow exchange included (e.g. an NCCL all-gather on the
+ * same stream), in one CUDA graph and replay it. Make one eager step before capturing (it loads
+ * kernels and creates the library's side streams); tsn_dit_split_schedule then rewinds.
+ * tsn_dit_split_schedule: install the t / dt schedule of src/pipeline.cpp:142-145 for `steps` steps
+ *   and rewind it to step 0 (synchronises; not for capture).
+ * tsn_dit_split_forward: this arm's forward at the schedule's current step; its flow [T,64] f32 is
+ *   copied to flow_dev (device memory).
+ * tsn_dit_split_update: x += dt_s (fu + cfg (fc - fu)) with fc, fu = flows2_dev[0], flows2_dev[1]
+ *   ([2][T,64] f32, device) and the current step's dt (shaders/ops_conv.metal:194-201), then advance
+ *   the schedule one step. */
+int tsn_dit_split_schedule(tsn_dit * m, int steps);
+int tsn_dit_split_forward(tsn_dit * m, float * flow_dev);
+int tsn_dit_split_update(tsn_dit * m, const float * flows2_dev, float cfg);
 /* End-to-end step through host memory: copy x_host_in to the device, one step, copy x back. */
 int tsn_dit_step_host(tsn_dit * m, const float * x_host_in, float * x_host_out, float t, float cfg, float dt);
 /* Number of kernels one step (forward + cfg_euler + schedule advance) launches. */

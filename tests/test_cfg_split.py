@@ -2,7 +2,9 @@
 
 The CPU test runs the pair as two gloo processes with the oracle as each rank's forward and checks
 that both ranks end with the same x as the single-process reference step loop, bit for bit. The
-GPU test runs the same protocol on two GPUs over NCCL (it needs two visible devices)."""
+GPU test runs the same protocol on two GPUs over NCCL (it needs two visible devices), once step by
+step from the host and once with every step replayed from one captured CUDA graph (forward, NCCL
+all-gather, update), which must give the same bits."""
 import os
 import socket
 
@@ -106,9 +108,14 @@ def _gpu_rank(rank, port, gguf, out_dir):
             m.prepare(T, C, TS, 1)
             m.set_conditioning(inp["clip_pp"], inp["sync_gather"], inp[f"text_pp_{sfx}"], inp[f"gcmlp_{sfx}"])
             x = torch.from_numpy(inp["x"]).cuda()
-            cfg_split.CfgSplitSampler(m, dev, T).sample(x, STEPS, CFG)
+            xg = x.clone()
+            sampler = cfg_split.CfgSplitSampler(m, dev, T)
+            sampler.sample(x, STEPS, CFG)
             torch.cuda.synchronize()
             np.save(os.path.join(out_dir, f"g{rank}.npy"), x.cpu().numpy())
+            sampler.sample_graph(xg, STEPS, CFG)          # every step replayed from one CUDA graph
+            torch.cuda.synchronize()
+            np.save(os.path.join(out_dir, f"gg{rank}.npy"), xg.cpu().numpy())
             m.close()
             dev.close()
     finally:
@@ -124,6 +131,8 @@ def test_cfg_split_two_gpus(tiny_gguf, tmp_path):
     mp.start_processes(_gpu_rank, args=(port, tiny_gguf, str(tmp_path)), nprocs=2, join=True, start_method="spawn")
     x0, x1 = np.load(tmp_path / "g0.npy"), np.load(tmp_path / "g1.npy")
     assert np.array_equal(x0, x1), "the two GPUs' replicas of x diverged"
+    # the graph-replayed sampler issues the same kernels in the same order: the same bits
+    assert np.array_equal(np.load(tmp_path / "gg0.npy"), x0) and np.array_equal(np.load(tmp_path / "gg1.npy"), x0)
     T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
     inp = make_inputs(T, C, TS, TINY["H"], seed=SEED + 7)
     orc = O.Oracle(tiny_gguf)

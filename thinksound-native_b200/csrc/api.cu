@@ -430,12 +430,8 @@ int tsn_dit_step(tsn_dit * m, float t, float cfg, float dt) {
     return M.dev->sync();
 }
 
-int tsn_dit_schedule(tsn_dit * m, int steps, float cfg) {
-    M_BEGIN NEED_PREPARED
-    if (M.A != 2) return fail(TSN_ERR_STATE, "the sampler needs both CFG arms (arms = 2 per generation)");
-    if (steps < 1 || steps > M.max_steps) return fail(TSN_ERR_ARG, "steps out of range");
-    TRY(ensure_step_graph(M, cfg));
-    // src/pipeline.cpp:142-145
+// the pipeline's schedule (src/pipeline.cpp:142-145) into the model's t-embedding and dt tables
+static int fill_schedule(Model & M, int steps) {
     std::vector<float> tb((size_t) steps * M.g.H), dts(steps);
     for (int s = 0; s < steps; ++s) {
         float t_curr = 1.0f - (float) s / steps;
@@ -447,6 +443,40 @@ int tsn_dit_schedule(tsn_dit * m, int steps, float cfg) {
     CKR(cudaMemcpy(M.dt_tab, dts.data(), dts.size() * 4, cudaMemcpyHostToDevice));
     CKR(cudaMemsetAsync(M.step, 0, 4, M.dev->stream));
     M.sched_steps = steps;
+    return TSN_OK;
+}
+
+int tsn_dit_schedule(tsn_dit * m, int steps, float cfg) {
+    M_BEGIN NEED_PREPARED
+    if (M.A != 2) return fail(TSN_ERR_STATE, "the sampler needs both CFG arms (arms = 2 per generation)");
+    if (steps < 1 || steps > M.max_steps) return fail(TSN_ERR_ARG, "steps out of range");
+    TRY(ensure_step_graph(M, cfg));
+    return fill_schedule(M, steps);
+}
+
+int tsn_dit_split_schedule(tsn_dit * m, int steps) {
+    M_BEGIN NEED_PREPARED
+    if (M.A != 1) return fail(TSN_ERR_STATE, "the CFG split runs one arm per device (arms = 1)");
+    if (steps < 1 || steps > M.max_steps) return fail(TSN_ERR_ARG, "steps out of range");
+    TRY(fill_schedule(M, steps));
+    return M.dev->sync();
+}
+
+int tsn_dit_split_forward(tsn_dit * m, float * flow_dev) {
+    M_BEGIN NEED_PREPARED
+    if (M.A != 1 || !M.sched_steps) return fail(TSN_ERR_STATE, "call tsn_dit_split_schedule on a one-arm model first");
+    if (!flow_dev) return fail(TSN_ERR_ARG, "null flow");
+    TRY(M.run_ops(M.ops_fwd));
+    CKR(cudaMemcpyAsync(flow_dev, M.flow, (size_t) M.T * M.g.latent_dim * 4, cudaMemcpyDeviceToDevice, M.dev->stream));
+    return TSN_OK;
+}
+
+int tsn_dit_split_update(tsn_dit * m, const float * flows2_dev, float cfg) {
+    M_BEGIN NEED_PREPARED
+    if (M.A != 1 || !M.sched_steps) return fail(TSN_ERR_STATE, "call tsn_dit_split_schedule on a one-arm model first");
+    if (!flows2_dev) return fail(TSN_ERR_ARG, "null flows");
+    CKR(launch_cfg_euler(flows2_dev, M.x, M.T * (int) M.g.latent_dim, 1, cfg, M.dt_tab, M.step, 0.0f, M.dev->stream));
+    CKR(launch_step_advance(M.step, M.dev->stream));
     return TSN_OK;
 }
 

@@ -422,6 +422,7 @@ void Model::release_activations() {
     ops_fwd.clear();
     ops_step.clear();
     prepared = false;
+    sched_steps = 0;
 }
 
 // reference timestep embedding on the host (src/dit_fwd.cpp:112-119)

@@ -115,6 +115,9 @@ _SIGS = [
     ("tsn_dit_sample", C.c_int, [C.c_void_p, C.c_int, C.c_float]),
     ("tsn_dit_schedule", C.c_int, [C.c_void_p, C.c_int, C.c_float]),
     ("tsn_dit_run_steps", C.c_int, [C.c_void_p, C.c_int]),
+    ("tsn_dit_split_schedule", C.c_int, [C.c_void_p, C.c_int]),
+    ("tsn_dit_split_forward", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("tsn_dit_split_update", C.c_int, [C.c_void_p, C.c_void_p, C.c_float]),
     ("tsn_dit_step_host", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_float, C.c_float, C.c_float]),
     ("tsn_dit_kernels_per_step", C.c_int, [C.c_void_p]),
     ("tsn_dit_profile_step", C.c_int, [C.c_void_p, C.POINTER(C.c_double)]),
@@ -372,6 +375,18 @@ class Dit:
 
     def run_steps(self, n: int):
         check(lib().tsn_dit_run_steps(self.h, n))
+
+    def split_schedule(self, steps: int):
+        """CFG split (arms = 1): install the sampler's t / dt schedule and rewind it."""
+        check(lib().tsn_dit_split_schedule(self.h, steps))
+
+    def split_forward(self, flow_dev):
+        """CFG split: issue this arm's forward at the schedule's step; flow [T, 64] f32 into flow_dev."""
+        check(lib().tsn_dit_split_forward(self.h, _p(flow_dev)))
+
+    def split_update(self, flows2_dev, cfg: float):
+        """CFG split: x += dt (fu + cfg (fc - fu)) from flows2_dev [2, T, 64]; advance the schedule."""
+        check(lib().tsn_dit_split_update(self.h, _p(flows2_dev), cfg))
 
     def step_host(self, x_in, x_out, t: float, cfg: float, dt: float):
         check(lib().tsn_dit_step_host(self.h, _p(x_in), _p(x_out), t, cfg, dt))

@@ -10,7 +10,9 @@ exchange.
 
 :func:`loop` is the protocol with the three steps passed in; :class:`CfgSplitSampler` binds them
 to the library (one ``Dit`` per rank) and to ``torch.distributed`` (NCCL all-gather on the stream
-the library runs on).
+the library runs on). :meth:`CfgSplitSampler.sample_graph` runs the same protocol with one step
+(this arm's forward, the all-gather, the update) captured in a CUDA graph and replayed, so a step
+costs no host round trip.
 """
 from __future__ import annotations
 
@@ -72,3 +74,50 @@ class CfgSplitSampler:
     def sample(self, x, steps: int, cfg: float):
         """x: this rank's replica of the latent [T, 64] f32 on the device, updated in place."""
         return loop(steps, cfg, x, self.forward, self.all_gather, self.euler)
+
+    # ------------------------------------------------------------------ one CUDA graph per step
+    def _one_step(self, cfg):
+        import torch.distributed as dist
+        self.dit.split_forward(self.mine)
+        dist.all_gather_into_tensor(self.flows, self.mine, group=self.group)
+        self.dit.split_update(self.flows, float(cfg))
+
+    def graph_capture(self, x0, cfg: float):
+        """Capture one sampler step in a CUDA graph: the library's stream-ordered split calls
+        (tsn_dit_split_forward / tsn_dit_split_update) and the NCCL all-gather, on the library's
+        stream (torch's current stream, which must not be the default stream). One eager step runs
+        first (it loads the kernels and warms the communicator). x0: device [T, 64]."""
+        import torch
+        self.dit.set_x(x0)
+        self.dit.split_schedule(1)
+        self._one_step(cfg)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=torch.cuda.current_stream()):
+            self._one_step(cfg)
+
+    def graph_run(self, x0, steps: int):
+        """The sampler from x0 over `steps` steps, each replayed from the captured graph (no host
+        round trip per step); x stays on the device (read it with the model's get_x)."""
+        self.dit.set_x(x0)
+        self.dit.split_schedule(steps)
+        for _ in range(steps):
+            self.graph.replay()
+
+    def graph_release(self):
+        """Release the graph (it holds NCCL work: release it before destroying the process group)."""
+        import torch
+        torch.cuda.synchronize()
+        self.graph = None
+
+    def sample_graph(self, x, steps: int, cfg: float):
+        """:meth:`sample` with each step replayed from one CUDA graph; x (device [T, 64]) is the start
+        latent and receives the result."""
+        x0 = x.clone()
+        self.graph_capture(x0, cfg)
+        try:
+            self.graph_run(x0, steps)
+            self.dit.get_x(x)
+        finally:
+            self.graph_release()
+        return x
