@@ -58,6 +58,8 @@ def parse():
                     help="time every tile candidate at load instead of the library's built-in tile table (the tuned "
                          "forward may then differ from other processes' in the last bits)")
     ap.add_argument("--cfg-split", action="store_true", help="one CFG arm per rank, pairs of ranks per generation")
+    ap.add_argument("--cpu-configs", action="store_true",
+                    help="time BASELINE configs 1 and 2 on the host cores (oracle port / reference build)")
     ap.add_argument("--cfg-split-eager", action="store_true", help="--cfg-split with the steps issued from the host")
     ap.add_argument("--long", action="store_true", help="BASELINE config 4 geometry: 30 s audio (T=704, clip 240, text 77)")
     ap.add_argument("--config5", action="store_true", help="64 generations x 24 steps, data-parallel, final gather")
@@ -734,6 +736,51 @@ def run_encoders(a):
         print(json.dumps(line), flush=True)
 
 
+def run_cpu_configs(a):
+    """The CPU baselines of BASELINE.md's table, on this host's cores: config 1 (one full joint block,
+    both CFG arms, T = 24, clip 8, text 77, H 1024, F 4096; the oracle port's joint block over a
+    two-joint-block synthetic file, inputs N(0,1) from the seed) and config 2 (one full CFG step of
+    the reference's host code, as the reference arm runs it); config 3 as 24 x config 2. One JSON line
+    each."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    threads = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    T, C, TS, H = 24, 8, 77, a.H
+    with tempfile.TemporaryDirectory(prefix="tsn_cfg1_") as d:
+        gguf = os.path.join(d, "two_joint.gguf")
+        O.write_synthetic_gguf(gguf, H=H, NH=H // 64, F=a.F, depth=2, fused_depth=0, seed=a.seed)
+        orc = O.Oracle(gguf)
+        rng = np.random.default_rng(a.seed)
+        f = lambda *sh: rng.standard_normal(sh, dtype=np.float32)  # noqa: E731
+        lat, clip, text, extc, gc = f(T, H), f(C, H), f(2, TS, H), f(T, H), f(2, H)
+        orc.joint_block(lat, clip, text[0], extc, gc[0])          # warm-up
+        secs = []
+        for _ in range(max(3, a.steps // 8)):
+            t0 = time.perf_counter()
+            for arm in (0, 1):
+                orc.joint_block(lat, clip, text[arm], extc, gc[arm])
+            secs.append(time.perf_counter() - t0)
+        orc.close()
+    c1 = min(secs)
+    print(json.dumps({"metric": "config 1 (CPU): one MMDiT joint block, both CFG arms", "value": c1 * 1e3, "unit": "ms",
+                      "higher_is_better": False, "cores": threads, "kind": "port", "reps": len(secs),
+                      "config": {"T": T, "clip_S": C, "text_S": TS, "H": H, "F": a.F, "arms": 2},
+                      "sample": "joint block 0 of the oracle port (scalar restatement of the reference kernels, "
+                                "bit-exact to the reference build), f32, OpenMP over output rows"}), flush=True)
+    step_secs, kind, sample = cpu_reference_steps(a, 2, threads)
+    c2 = min(step_secs)
+    print(json.dumps({"metric": "config 2 (CPU): one CFG step, 21 blocks, 8 s", "value": c2 * 1e3, "unit": "ms",
+                      "higher_is_better": False, "cores": threads, "kind": kind, "reps": len(step_secs),
+                      "config": workload(a), "sample": sample}), flush=True)
+    print(json.dumps({"metric": "config 3 (CPU, extrapolated): 24-step CFG-5 denoise, 8 s", "value": 24 * c2,
+                      "unit": "s", "higher_is_better": False, "cores": threads, "kind": kind,
+                      "sample": "24 x the config 2 step time (extrapolated, not run)"}), flush=True)
+
+
 def write_vae_fixture(a):
     import tempfile
 
@@ -747,7 +794,9 @@ def write_vae_fixture(a):
 def main():
     a = parse()
     apply_long(a)
-    if a.vae:
+    if a.cpu_configs:
+        run_cpu_configs(a)
+    elif a.vae:
         run_vae(a)
     elif a.encoders:
         run_encoders(a)

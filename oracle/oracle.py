@@ -45,6 +45,7 @@ class Oracle:
         L.oracle_step.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, C.c_float, C.c_float, C.c_float,
                                   _F, _F, _F, _F, _F, _F, _F, _F]
         L.oracle_prep.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int] + [_F] * 12
+        L.oracle_joint_block.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_int, _F, _F, _F, _F, _F]
         L.oracle_tap.restype = C.c_longlong
         L.oracle_tap.argtypes = [C.c_void_p, C.c_char_p, _F, C.c_longlong]
         self.h = L.oracle_load(gguf.encode())
@@ -68,6 +69,15 @@ class Oracle:
         self.L.oracle_forward(self.h, T, C_, TS, _f(args[0]), t, _f(args[1]), _f(args[2]), _f(args[3]),
                               _f(args[4]), _f(flow), int(taps))
         return flow
+
+    def joint_block(self, lat, clip, text, extc_silu, global_c_silu):
+        """Joint block 0 (src/dit_fwd.cpp:180-257) for one arm; returns the updated (lat, clip, text)."""
+        T, C_, TS = lat.shape[0], clip.shape[0], text.shape[0]
+        lat, clip, text = (np.array(v, np.float32, copy=True) for v in (lat, clip, text))
+        e, g = (np.ascontiguousarray(v, dtype=np.float32) for v in (extc_silu, global_c_silu))
+        if self.L.oracle_joint_block(self.h, T, C_, TS, _f(lat), _f(clip), _f(text), _f(e), _f(g)) != 0:
+            raise RuntimeError("oracle_joint_block needs two or more joint blocks")
+        return lat, clip, text
 
     def tap(self, name: str) -> np.ndarray:
         n = self.L.oracle_tap(self.h, name.encode(), None, 0)

@@ -342,6 +342,49 @@ struct Fwd {
     }
 
     // dit_fwd.cpp:104-304
+    // one joint block (dit_fwd.cpp:180-257) on lat [T,H] and the clip_s / text_s streams, with the
+    // conditioning already in extc_silu and global_c (silu applied)
+    void joint_block(uint32_t i, float * lat) {
+        const uint32_t H = m.H;
+        const float clip_fscale = (float) T / (float) C;
+        const bool pre_only = (i == m.n_joint - 1);
+        const std::string jb = "joint_blocks." + std::to_string(i);
+        rt.gemm(m.W(jb + ".latent_block.adaLN_modulation.1.weight"), extc_silu.data(), mod_lat.data(),
+                (const float *) m.W(jb + ".latent_block.adaLN_modulation.1.bias"), T, 6 * H, H);
+        pre_attn(jb + ".latent_block", lat, mod_lat.data(), true, T, 0, jointq.data(), pos_lat.data(), 1.0f, false, 6);
+        const uint32_t ct = pre_only ? 2u : 6u;
+        rt.gemv(m.W(jb + ".clip_block.adaLN_modulation.1.weight"), global_c.data(), mod_clip.data(),
+                (const float *) m.W(jb + ".clip_block.adaLN_modulation.1.bias"), ct * H, H, H);
+        pre_attn(jb + ".clip_block", clip_s.data(), mod_clip.data(), false, C, T,
+                 jointq.data() + (size_t) T * 3 * H, pos_clip.data(), clip_fscale, false, ct);
+        rt.gemv(m.W(jb + ".text_block.adaLN_modulation.1.weight"), global_c.data(), mod_text.data(),
+                (const float *) m.W(jb + ".text_block.adaLN_modulation.1.bias"), ct * H, H, H);
+        pre_attn(jb + ".text_block", text_s.data(), mod_text.data(), false, TS, T + C,
+                 jointq.data() + (size_t) (T + C) * 3 * H, nullptr, 1.0f, true, ct);
+        if (i == 0 && m.want_taps) {                                                     // :211-233
+            tap("text_xn", sc_f1.data(), (size_t) TS * H);
+            std::vector<float> q((size_t) S * H), k((size_t) S * H), v((size_t) S * H);
+            for (uint32_t s = 0; s < S; ++s) {
+                memcpy(q.data() + (size_t) s * H, sc_qkv.data() + (size_t) s * 3 * H, H * 4);
+                memcpy(k.data() + (size_t) s * H, sc_qkv.data() + (size_t) s * 3 * H + H, H * 4);
+                memcpy(v.data() + (size_t) s * H, sc_qkv.data() + (size_t) s * 3 * H + 2 * H, H * 4);
+            }
+            tap("a0_q", q.data(), q.size()); tap("a0_k", k.data(), k.size()); tap("a0_v", v.data(), v.size());
+        }
+        attention(S);
+        post_attn(jb + ".latent_block", lat, joint_att.data(), mod_lat.data(), true, T, false);
+        if (!pre_only) {
+            post_attn(jb + ".clip_block", clip_s.data(), joint_att.data() + (size_t) T * H, mod_clip.data(), false, C, false);
+            post_attn(jb + ".text_block", text_s.data(), joint_att.data() + (size_t) (T + C) * H, mod_text.data(), false, TS, true);
+        }
+        if (i == 0) {                                                                    // :245-256
+            tap("a0_out", joint_att.data(), (size_t) S * H);
+            tap("jb0_lat", lat, (size_t) T * H);
+            tap("jb0_clip", clip_s.data(), (size_t) C * H);
+            tap("jb0_text", text_s.data(), (size_t) TS * H);
+        }
+    }
+
     void forward(const float * x, float t, const float * clip_pp, const float * sync_gather,
                  const float * text_pp, const float * gcmlp, float * flow) {
         const uint32_t H = m.H;
@@ -382,45 +425,7 @@ struct Fwd {
         rt.copy(clip_pp, clip_s.data(), (size_t) C * H);
         rt.copy(text_pp, text_s.data(), (size_t) TS * H);
         float * lat = x_in.data();
-        const float clip_fscale = (float) T / (float) C;
-        for (uint32_t i = 0; i < m.n_joint; ++i) {
-            const bool pre_only = (i == m.n_joint - 1);
-            const std::string jb = "joint_blocks." + std::to_string(i);
-            rt.gemm(m.W(jb + ".latent_block.adaLN_modulation.1.weight"), extc_silu.data(), mod_lat.data(),
-                    (const float *) m.W(jb + ".latent_block.adaLN_modulation.1.bias"), T, 6 * H, H);
-            pre_attn(jb + ".latent_block", lat, mod_lat.data(), true, T, 0, jointq.data(), pos_lat.data(), 1.0f, false, 6);
-            const uint32_t ct = pre_only ? 2u : 6u;
-            rt.gemv(m.W(jb + ".clip_block.adaLN_modulation.1.weight"), global_c.data(), mod_clip.data(),
-                    (const float *) m.W(jb + ".clip_block.adaLN_modulation.1.bias"), ct * H, H, H);
-            pre_attn(jb + ".clip_block", clip_s.data(), mod_clip.data(), false, C, T,
-                     jointq.data() + (size_t) T * 3 * H, pos_clip.data(), clip_fscale, false, ct);
-            rt.gemv(m.W(jb + ".text_block.adaLN_modulation.1.weight"), global_c.data(), mod_text.data(),
-                    (const float *) m.W(jb + ".text_block.adaLN_modulation.1.bias"), ct * H, H, H);
-            pre_attn(jb + ".text_block", text_s.data(), mod_text.data(), false, TS, T + C,
-                     jointq.data() + (size_t) (T + C) * 3 * H, nullptr, 1.0f, true, ct);
-            if (i == 0 && m.want_taps) {                                                     // :211-233
-                tap("text_xn", sc_f1.data(), (size_t) TS * H);
-                std::vector<float> q((size_t) S * H), k((size_t) S * H), v((size_t) S * H);
-                for (uint32_t s = 0; s < S; ++s) {
-                    memcpy(q.data() + (size_t) s * H, sc_qkv.data() + (size_t) s * 3 * H, H * 4);
-                    memcpy(k.data() + (size_t) s * H, sc_qkv.data() + (size_t) s * 3 * H + H, H * 4);
-                    memcpy(v.data() + (size_t) s * H, sc_qkv.data() + (size_t) s * 3 * H + 2 * H, H * 4);
-                }
-                tap("a0_q", q.data(), q.size()); tap("a0_k", k.data(), k.size()); tap("a0_v", v.data(), v.size());
-            }
-            attention(S);
-            post_attn(jb + ".latent_block", lat, joint_att.data(), mod_lat.data(), true, T, false);
-            if (!pre_only) {
-                post_attn(jb + ".clip_block", clip_s.data(), joint_att.data() + (size_t) T * H, mod_clip.data(), false, C, false);
-                post_attn(jb + ".text_block", text_s.data(), joint_att.data() + (size_t) (T + C) * H, mod_text.data(), false, TS, true);
-            }
-            if (i == 0) {                                                                    // :245-256
-                tap("a0_out", joint_att.data(), (size_t) S * H);
-                tap("jb0_lat", lat, (size_t) T * H);
-                tap("jb0_clip", clip_s.data(), (size_t) C * H);
-                tap("jb0_text", text_s.data(), (size_t) TS * H);
-            }
-        }
+        for (uint32_t i = 0; i < m.n_joint; ++i) joint_block(i, lat);
         tap("after_joint", lat, (size_t) T * H);                                             // :259-265
         for (uint32_t i = 0; i < m.fused_depth; ++i) {                                       // :267-279
             const std::string fb = "fused_blocks." + std::to_string(i);
@@ -593,6 +598,26 @@ int oracle_step(void * h, int T, int C, int TS, float * x, float t, float cfg, f
     f.forward(x, t, clip_pp, sync_gather, text_pp_u, gcmlp_u, fu);
     CD p{cfg, dt, (uint32_t) ((size_t) T * m->latent_dim)};
     cfg_euler(fc, fu, x, p);
+    return 0;
+}
+
+// One full joint block (joint block 0, dit_fwd.cpp:180-257) for one arm: lat [T,H], clip [C,H] and
+// text [TS,H] are updated in place; extc_silu [T,H] and global_c_silu [H] are the block's
+// conditioning. Needs a model with at least two joint blocks (block 0 full).
+int oracle_joint_block(void * h, int T, int C, int TS, float * lat, float * clip, float * text, const float * extc_silu,
+                       const float * global_c_silu) {
+    Model * m = (Model *) h;
+    if (m->n_joint < 2) return -1;
+    m->want_taps = false;
+    Fwd f(*m, (uint32_t) T, (uint32_t) C, (uint32_t) TS);
+    const size_t H = m->H;
+    memcpy(f.extc_silu.data(), extc_silu, (size_t) T * H * 4);
+    memcpy(f.global_c.data(), global_c_silu, H * 4);
+    memcpy(f.clip_s.data(), clip, (size_t) C * H * 4);
+    memcpy(f.text_s.data(), text, (size_t) TS * H * 4);
+    f.joint_block(0, lat);
+    memcpy(clip, f.clip_s.data(), (size_t) C * H * 4);
+    memcpy(text, f.text_s.data(), (size_t) TS * H * 4);
     return 0;
 }
 

@@ -296,3 +296,18 @@ def test_clip_reference_build_matches_restatement(clip_gguf, tmp_path, n_tok):
     W, kv = gguf_read.device_weights(clip_gguf)
     p2, g2 = O.clip_encode_np(W, kv, ids)
     assert rel_l2(p2, pt) < 1e-5 and rel_l2(g2, pooled) < 1e-5
+
+
+def test_joint_block_entry_matches_forward_taps(tiny_gguf):
+    """oracle_joint_block (the CPU baseline of BASELINE config 1) is joint block 0 of the forward:
+    fed the forward's own x_in, conditioning and streams, it reproduces the jb0_* taps."""
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"])
+    orc = O.Oracle(tiny_gguf)
+    orc.forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"], inp["text_pp_cond"], inp["gcmlp_cond"],
+                taps=True)
+    silu = lambda v: (v / (1.0 + np.exp(-v.astype(np.float64)))).astype(np.float32)  # noqa: E731
+    lat, clip, text = orc.joint_block(orc.tap("x_in").reshape(T, -1), inp["clip_pp"], inp["text_pp_cond"],
+                                      silu(orc.tap("extended_c")).reshape(T, -1), silu(orc.tap("global_c")))
+    for got, name in ((lat, "jb0_lat"), (clip, "jb0_clip"), (text, "jb0_text")):
+        assert rel_l2(got, orc.tap(name)) < 1e-5, name
