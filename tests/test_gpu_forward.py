@@ -281,3 +281,27 @@ def test_generations_batched_match_single(dev, tiny_gguf, G):
         x1 = np.zeros((T, 64), np.float32)
         one.get_x(x1)
         assert rel_l2(xG[g] - inp["x"], x1 - inp["x"]) < tol
+
+
+def test_pair_kernel_swiglu_real_widths_vs_oracle(dev, wide_gguf):
+    """The CTA-pair GEMM with 192-token tiles pinned on the FFN w1/w3 GEMMs (SwiGLU epilogue through
+    the staged f16 tile) at real widths and the 8 s latent length: flow within the gate."""
+    T, C, TS = WIDE_SEQ["T"], WIDE_SEQ["C"], WIDE_SEQ["TS"]
+    inp = make_inputs(T, C, TS, WIDE["H"])
+    m = gpu_model(dev, wide_gguf, inp, T, C, TS)
+    gemms = [l for l in m.profile_ops().splitlines() if "bn=" in l]
+    t = m.tiles().copy()
+    # the single (not grouped) w1/w3 launches: fused blocks, the pre-only joint block, audio_in
+    w13 = [i for i, l in enumerate(gemms) if l.split()[1] in ("ffn_w13", "audio_in.w13") and "group=" not in l]
+    assert w13
+    for i in w13:
+        t[i, 1:] = (2192, 1)
+    m.set_tiles(t)
+    assert all(m.tiles()[i, 1] == 2192 for i in w13), "a w1/w3 GEMM did not take the pair tile"
+    flow = np.zeros((2, T, 64), np.float32)
+    m.forward(0.5, flow)
+    orc = O.Oracle(wide_gguf)
+    for arm, sfx in ((0, "cond"), (1, "unc")):
+        ref = orc.forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"], inp[f"text_pp_{sfx}"],
+                          inp[f"gcmlp_{sfx}"])
+        assert rel_l2(flow[arm], ref) < FLOW_TOL

@@ -200,14 +200,14 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
           }
         } else {
             // SwiGLU: rows come in groups of 64 = [32 w1 | 32 w3], so warps (0,1) and (2,3) hold
-            // matching w1 and w3 rows for output features g*32 + lane, g = (n0 + 64*pair) / 64.
-            // Each warp puts its 32 x 32 block in shared memory (the operand ring is free: every
-            // MMA of the pair has completed) and the pair splits the 32 tokens of the chunk.
+            // matching w1 and w3 rows for output features g*32 + lane, g = (n0 + 64*pw) / 64: the
+            // CTA's 64 output features are contiguous. Each warp puts its 32 x 32 block in shared
+            // memory (the operand ring is free: every MMA of the pair has completed), the pair
+            // writes silu(w1)·w3 of the chunk's 32 tokens into an f16 tile [NT tokens][64 features],
+            // and once every chunk is in, the four warps write the tile as whole 128-byte token rows.
             float * xb = (float *) smem + warp * 32 * 32;           // [token][lane]
+            __half * ot = (__half *) (smem + 4 * 32 * 32 * 4);      // [NT][64]
             const int pw = warp >> 1, odd = warp & 1;
-            const int f = ((n0 + 64 * pw) >> 6) * 32 + lane;        // output feature
-            __half * ob = (__half *) a.out + (long long) b * a.out_bs + f;
-            const bool fok = (n0 + 64 * pw) < a.N;
 #pragma unroll 1
             for (int c = 0; c < NT; c += 32) {
                 float v[32];
@@ -217,14 +217,21 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
                 asm volatile("bar.sync %0, 64;" ::"r"(2 + pw) : "memory");
                 const float * w1 = (const float *) smem + (2 * pw) * 32 * 32;
                 const float * w3 = w1 + 32 * 32;
-                if (ok && fok) {
 #pragma unroll 4
-                    for (int j = odd * 16; j < odd * 16 + 16; ++j) {
-                        const int t = t0 + c + j;
-                        if (t < a.rows) ob[(long long) t * a.ldo] = __float2half_rn(silu_f(w1[j * 32 + lane]) * w3[j * 32 + lane]);
-                    }
-                }
+                for (int j = odd * 16; j < odd * 16 + 16; ++j)
+                    ot[(c + j) * 64 + 32 * pw + lane] = __float2half_rn(silu_f(w1[j * 32 + lane]) * w3[j * 32 + lane]);
                 asm volatile("bar.sync %0, 64;" ::"r"(2 + pw) : "memory");
+            }
+            epi_bar();
+            const int f0 = (n0 >> 6) * 32;                           // the CTA's first output feature
+            const int nf = min(64, (a.N - n0) / 2);                  // output features of weight rows < N
+            if (ok && nf > 0) {
+                __half * ob = (__half *) a.out + (long long) b * a.out_bs + f0;
+                for (int i = threadIdx.x; i < NT * 8; i += 128) {
+                    const int tk = i >> 3, ch = i & 7, t = t0 + tk;
+                    if (t < a.rows && ch * 8 < nf)
+                        *(uint4 *) (ob + (long long) t * a.ldo + ch * 8) = *(const uint4 *) (ot + tk * 64 + ch * 8);
+                }
             }
         }
     }
