@@ -148,23 +148,18 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
             const float bl = a.bias && f0 + lane < a.N ? a.bias[f0 + lane] : 0.0f;
             uint8_t * boxes = smem + warp * (NT / 32) * 4096;
             const uint32_t chunk = (uint32_t) (lane >> 2), word = (uint32_t) (lane & 3) * 4;
-            // two register sets: chunk c + 1 is read from TMEM while chunk c is staged and stored
-            uint32_t rg[2][32];
-            tmem_ld32_issue(trow, rg[0]);
-            tmem_ld32_wait(rg[0]);
 #pragma unroll
             for (int ci = 0; ci < NT / 32; ++ci) {
                 const int c = ci * 32;
-                uint32_t (&cur)[32] = rg[ci & 1];
-                if (ci + 1 < NT / 32) tmem_ld32_issue(trow + c + 32, rg[(ci + 1) & 1]);
+                float cur[32];
+                tmem_ld32(trow + c, cur);
                 uint8_t * box = boxes + ci * 4096;
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    *(float *) (box + j * 128 + ((chunk ^ (uint32_t) (j & 7)) << 4) + word) = __uint_as_float(cur[j]) + bl;
+                    *(float *) (box + j * 128 + ((chunk ^ (uint32_t) (j & 7)) << 4) + word) = cur[j] + bl;
                 fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0 && ok && f0 < a.N && t0 + c < a.rows) tma_store_4d(&tmY, box, f0, t0 + c, b, (int) blockIdx.z);
-                if (ci + 1 < NT / 32) tmem_ld32_wait(rg[(ci + 1) & 1]);
             }
             if (lane == 0) {
                 bulk_commit();

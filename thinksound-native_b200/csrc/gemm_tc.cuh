@@ -426,17 +426,12 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
                 // bt is a multiple of 32.
                 const int rw = warp * 32, bw = b0 + rw / a.bt, tw = t0 + rw % a.bt;
                 uint8_t * boxes = smem + warp * (BN / 32) * 4096;
-                // two register sets: unit u + 1 is read from TMEM while unit u is staged and stored
-                uint32_t rg[2][32];
-                tmem_ld32_issue(trow, rg[0]);
-                tmem_ld32_wait(rg[0]);
 #pragma unroll
                 for (int u = 0; u < BN / 32; ++u) {
-                    uint32_t (&cur)[32] = rg[u & 1];
-                    if (u + 1 < BN / 32) tmem_ld32_issue(trow + (u + 1) * 32, rg[(u + 1) & 1]);
                     float v[32];
+                    tmem_ld32(trow + u * 32, v);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(cur[e]) + (ec.bias ? ec.bias[u * 32 + e] : 0.0f);
+                    for (int e = 0; e < 32; ++e) v[e] += ec.bias ? ec.bias[u * 32 + e] : 0.0f;
                     uint8_t * row = boxes + u * 4096 + lane * 128;
 #pragma unroll
                     for (int q = 0; q < 8; ++q)
@@ -445,7 +440,6 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
                     __syncwarp();
                     if (lane == 0 && ok && tw < a.rows && bw < a.B && n0 + u * 32 < a.N)
                         tma_store_4d(tmO, boxes + u * 4096, n0 + u * 32, tw, bw, z);
-                    if (u + 1 < BN / 32) tmem_ld32_wait(rg[(u + 1) & 1]);
                 }
                 if (lane == 0) {
                     bulk_commit();
