@@ -58,6 +58,8 @@ def parse():
                     help="time every tile candidate at load instead of the library's built-in tile table (the tuned "
                          "forward may then differ from other processes' in the last bits)")
     ap.add_argument("--cfg-split", action="store_true", help="one CFG arm per rank, pairs of ranks per generation")
+    ap.add_argument("--trace-ops", action="store_true",
+                    help="print per-CTA phase stamps (medians) of one launch of each op kind of a fused block to stderr")
     ap.add_argument("--cpu-configs", action="store_true",
                     help="time BASELINE configs 1 and 2 on the host cores (oracle port / reference build)")
     ap.add_argument("--cfg-split-eager", action="store_true", help="--cfg-split with the steps issued from the host")
@@ -359,6 +361,8 @@ def run_tsn(a):
     prof = m.profile_step()
     kps = m.kernels_per_step()
     ops_text = m.profile_ops()
+    if a.trace_ops and rank == 0:
+        trace_ops(m, ops_text)
     if a.profile_ops and rank == 0:
         print(ops_text, file=sys.stderr, flush=True)
     times = torch.tensor([ms, e2e_ms or 0.0], dtype=torch.float64, device="cuda")
@@ -419,6 +423,41 @@ def run_tsn(a):
     dev.close()
     if dist:
         dist.destroy_process_group()
+
+
+def trace_ops(m, ops_text):
+    """Per-CTA phase stamps (tsn_dit_trace_op) of the first launch of each op kind past the joint
+    blocks, as medians over the CTAs (us), one JSON line per launch on stderr. GEMMs and the short
+    attention stamp 8 phases (entry, setup / upstream done, first operand stage / Q landed, MMA done /
+    every score product done, epilogue done / row max known, exit), adaLN and GEMV launches 3 (entry,
+    upstream done, exit)."""
+    import numpy as np
+
+    names = {}
+    for line in ops_text.splitlines():
+        p = line.split()
+        if len(p) > 2 and p[0].isdigit():
+            names[int(p[0])] = (p[1], " ".join(p[2:]))
+    first = {}
+    start = max(names) // 3 if names else 0
+    for i, (n, _) in sorted(names.items()):
+        if i >= start and n not in first:
+            first[n] = i
+    for n, i in first.items():
+        try:
+            st = m.trace_op(i).astype(np.int64)
+        except Exception:   # not a stamped launch
+            continue
+        if len(st) == 0:
+            continue
+        med = lambda b, e: float(np.median(st[:, e] - st[:, b]) / 1e3)  # noqa: E731
+        if st[:, 5].max() > 0:
+            ph = {"upstream+setup": med(0, 1), "to_first_data": med(1, 2), "main": med(2, 3), "epilogue": med(3, 4),
+                  "to_exit": med(4, 5)}
+        else:
+            ph = {"to_upstream_done": med(0, 1), "work": med(1, 2)}
+        print(json.dumps({"trace_op": n, "op": i, "ctas": int(len(st)), "median_us": {k: round(v, 2) for k, v in ph.items()},
+                          "desc": names[i][1][:80]}), file=sys.stderr, flush=True)
 
 
 def run_cfg_split(a):

@@ -20,6 +20,10 @@ full_sample.npz   BASELINE config 3 at full size: the 24-step CFG-5 sampler (src
                   reference's own run from x0 perturbed by relative SENS_EPS (the size of the per-step
                   flow gate) Gaussian noise, as its rel-L2 distance from x_final.
                   `python tests/golden/make_golden.py full` writes only this.
+long_forward.npz  BASELINE config 4 at full depth: one DitModel::forward per CFG arm of the 21-block model
+                  at the 30 s geometry (T 704, clip 240, text 77; S = 1021), t = 0.5, inputs
+                  make_inputs(704, 240, 77, 1024) (stored as a SHA-256), flows of both arms.
+                  `python tests/golden/make_golden.py long` writes only this.
 small_clip.npz    ClipModel::encode (src/clip.cpp:30-101) of seeded ids (BOS, 20 tokens, EOS padded)
                   on the synthetic f32 MetaCLIP text model (hidden 256, 2 layers, 4 heads):
                   per_token [77, 256], pooled [256].
@@ -120,9 +124,33 @@ def make_full(d):
                         sens_eps=SENS_EPS, sens_x_final_rel=sens, **{k: v for k, v in FULL.items()}, **FULL_SEQ)
 
 
+LONG_SEQ = dict(T=704, C=240, TS=77)
+
+
+def make_long(d):
+    T, C, TS = LONG_SEQ["T"], LONG_SEQ["C"], LONG_SEQ["TS"]
+    gguf = os.path.join(d, "full.gguf")
+    if not os.path.exists(gguf):
+        tsn.write_synthetic_gguf(gguf, make_geom(**FULL), SEED)
+    inp = make_inputs(T, C, TS, FULL["H"])
+    O.write_inputs(os.path.join(d, "lin"), inp)
+    flows = {}
+    for arm in ("cond", "unc"):
+        od = os.path.join(d, "long_" + arm)
+        O.run_ref("forward", gguf, T, C, TS, os.path.join(d, "lin"), od, 0.5, arm, timeout=7200)
+        flows[f"flow_{arm}"] = np.fromfile(os.path.join(od, "flow.bin"), np.float32).reshape(T, 64)
+    np.savez_compressed(os.path.join(HERE, "long_forward.npz"), **flows, t=np.float32(0.5), inputs_sha256=inputs_sha(inp),
+                        **{k: v for k, v in FULL.items()}, **LONG_SEQ)
+
+
 def main():
     if not O.have_ref():
         raise SystemExit("oracle/_ref/ts_ref_dit not built (needs the reference tree)")
+    if sys.argv[1:] == ["long"]:
+        with tempfile.TemporaryDirectory() as d:
+            make_long(d)
+        print("wrote long_forward.npz")
+        return
     if sys.argv[1:] == ["full"]:
         with tempfile.TemporaryDirectory() as d:
             make_full(d)
