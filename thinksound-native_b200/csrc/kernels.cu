@@ -472,28 +472,30 @@ __device__ __forceinline__ void cvt8(uint4 w, int bf16, float * f) {
         f[e] = bf16 ? __uint_as_float((uint32_t) h[e] << 16) : __half2float(__ushort_as_half(h[e]));
 }
 
-// Weight streaming: one block of GS_WARPS warps per SM (grid = min(ceil(slots / GS_WARPS), SMs));
-// the batch's rows are taken as slots of R = 2 consecutive rows of one job, and every warp walks its
-// own slots (warp-slot index i = block * GS_WARPS + warp, i + GS_WARPS * grid, ...) through its own
-// ring of three slots: lane 0 brings a slot's rows (one contiguous run of R x K x 2 bytes) into
-// shared memory with one bulk copy that completes on the stage's barrier, so 192 KB are in flight
-// per SM at K = 1024 and no warp waits on another. The first
-// copies are issued before the wait on the upstream kernel (weights do not depend on it). Lane l sums
-// the runs k = 128 c + 4 l .. + 3 of each row in c order against x, and the warp adds the 32 lane
-// sums in a fixed butterfly, so a row's result does not depend on the grid. x (every arm) is loaded
-// once: for up to two arms into registers (the kernel is otherwise bound by shared-memory reads of x,
-// one per row pair), else into shared memory (16-byte reads by consecutive lanes, free of bank
-// conflicts; each read serves both rows of a slot). Every job of a batch shares x, K and the arm count. Every wait
-// is bounded; a warp that gives up, or stops because another gave up, waits (bounded) for every copy
-// it issued and did not consume before the block exits.
-constexpr int GS_WARPS = 16, GS_RING = 12288;   // warps per block, ring bytes per warp at K = 1024
+// Weight streaming: one block of GS_WARPS = 24 warps per SM (grid = min(ceil(slots / GS_WARPS),
+// SMs)); the batch's rows are taken as slots of R = 2 consecutive rows of one job, and every warp
+// walks its own slots (warp-slot index i = block * GS_WARPS + warp, i + GS_WARPS * grid, ...)
+// through its own two-slot ring: lane 0 brings a slot's rows (one contiguous run of R x K x 2 bytes)
+// into shared memory with one bulk copy that completes on the stage's barrier, so 192 KB are in
+// flight per SM at K = 1024 and no warp waits on another. The first copies are issued before the
+// wait on the upstream kernel (weights do not depend on it). Lane l sums the runs
+// k = 128 c + 4 l .. + 3 of each row in c order against x, and the warp adds the 32 lane sums in a
+// fixed butterfly, so a row's result does not depend on the grid. x (every arm) is loaded once per
+// block into shared memory; 16-byte x reads and 8-byte weight reads by consecutive lanes are free of
+// bank conflicts, and each x read serves both rows of a slot. (x held in registers, for up to two
+// arms, limited the block to 16 warps: 52 us against 44 us here for the step's modulation batch;
+// 16-row stages shared by all warps, 1-row slots and 12 warps were slower still.) Every job of a
+// batch shares x, K and the arm count. Every wait is bounded; a warp that gives up, or stops because
+// another gave up, waits (bounded) for every copy it issued and did not consume before the block
+// exits.
+constexpr int GS_WARPS = 24, GS_RING = 8192;    // warps per block, ring bytes per warp at K = 1024
 constexpr int GS_THREADS = 32 * GS_WARPS;
 constexpr int GS_KC = GEMV_MAX_K / 128;             // 128-element runs per row
 __host__ __device__ constexpr int gemv_rows_per_slot(int) { return 2; }
 __host__ __device__ constexpr int gemv_stages(int nb) { return GS_RING / (gemv_rows_per_slot(nb) * GEMV_MAX_K * 2); }
 
 __host__ __device__ inline size_t gemv_smem_bytes(int K, int nb) {
-    return (size_t) GS_WARPS * gemv_stages(nb) * gemv_rows_per_slot(nb) * K * 2 + (nb > 2 ? (size_t) nb * K * 4 : 0) +
+    return (size_t) GS_WARPS * gemv_stages(nb) * gemv_rows_per_slot(nb) * K * 2 + (size_t) nb * K * 4 +
            (size_t) GS_WARPS * gemv_stages(nb) * 8 + 16;
 }
 
@@ -520,7 +522,6 @@ __global__ void __launch_bounds__(GS_THREADS, 1) gemv_kernel(const __grid_consta
                                                             long long total, int ab_bf16, int * err,
                                                             unsigned long long * trace) {
     constexpr int GS_R = gemv_rows_per_slot(NB), GS_STAGES = gemv_stages(NB);
-    constexpr bool XREG = NB <= 2;
     extern __shared__ __align__(128) uint8_t gs_smem[];
     // optional stamps (globaltimer ns, 3 per block): entry, upstream done, exit
     unsigned long long * tr = trace ? trace + 3 * blockIdx.x : nullptr;
@@ -530,7 +531,7 @@ __global__ void __launch_bounds__(GS_THREADS, 1) gemv_kernel(const __grid_consta
     const size_t slot_bytes = (size_t) GS_R * K * 2;
     uint8_t * ring = gs_smem + (size_t) w * GS_STAGES * slot_bytes;          // this warp's ring
     float * xs = (float *) (gs_smem + (size_t) GS_WARPS * GS_STAGES * slot_bytes);
-    const size_t xs_floats = XREG ? 0 : (size_t) nb * K;
+    const size_t xs_floats = (size_t) nb * K;
     uint64_t * bars = (uint64_t *) (xs + xs_floats) + w * GS_STAGES;        // this warp's barriers
     int * abort_word = (int *) ((uint64_t *) (xs + xs_floats) + GS_WARPS * GS_STAGES);
     if (threadIdx.x == 0) *abort_word = 0;
@@ -556,27 +557,14 @@ __global__ void __launch_bounds__(GS_THREADS, 1) gemv_kernel(const __grid_consta
         for (int st = 0; st < GS_STAGES; ++st) issue(s0 + st * stride, st);
     pdl_wait();
     if (tr && threadIdx.x == 0) tr[1] = global_ns();
-    // this lane's x runs (k = 128 c + 4 lane) of every arm, or every arm's x in shared memory
-    float4 xr[XREG ? NB : 1][GS_KC];
-    {
+    {   // every arm's x into shared memory
         const GemvJob & j0 = jb.j[0];
         const float * x = j0.x + (j0.x_step ? (long long) (*j0.x_step) * j0.x_step_stride : 0);
-        if constexpr (XREG) {
-#pragma unroll
-            for (int bb = 0; bb < NB; ++bb)
-#pragma unroll
-                for (int c = 0; c < GS_KC; ++c) {
-                    const int k = c * 128 + lane * 4;
-                    xr[bb][c] = bb < nb && k < K ? *(const float4 *) (x + (long long) bb * j0.x_bs + k)
-                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-        } else {
-            for (int e = threadIdx.x; e < nb * K; e += GS_THREADS) {
-                const int bb = e / K, k = e % K;
-                xs[e] = x[(long long) bb * j0.x_bs + k];
-            }
-            __syncthreads();
+        for (int e = threadIdx.x; e < nb * K; e += GS_THREADS) {
+            const int bb = e / K, k = e % K;
+            xs[e] = x[(long long) bb * j0.x_bs + k];
         }
+        __syncthreads();
     }
     int i = 0;
     for (;; ++i) {
@@ -606,7 +594,7 @@ __global__ void __launch_bounds__(GS_THREADS, 1) gemv_kernel(const __grid_consta
 #pragma unroll
             for (int bb = 0; bb < NB; ++bb) {
                 if (bb >= nb) break;
-                const float4 xv = XREG ? xr[XREG ? bb : 0][c] : *(const float4 *) (xs + bb * K + k);
+                const float4 xv = *(const float4 *) (xs + bb * K + k);
 #pragma unroll
                 for (int r = 0; r < GS_R; ++r)
                     acc[r][bb] += wf[r][0] * xv.x + wf[r][1] * xv.y + wf[r][2] * xv.z + wf[r][3] * xv.w;
