@@ -85,11 +85,12 @@ def geom_kwargs(a):
     return dict(H=a.H, NH=a.H // 64, F=a.F, depth=a.depth, fused_depth=a.fused)
 
 
-def workload(a):
+def workload(a, what=None):
     geo = "30 s audio geometry (config 4)" if (a.T, a.C) == (704, 240) else "8 s audio geometry" if a.T == 188 else \
         f"T={a.T} geometry"
-    return {"workload": f"config{'4' if (a.T, a.C) == (704, 240) else '2/3'}: {a.depth}-block MMDiT CFG Euler step "
-                        f"({a.depth - a.fused} joint + {a.fused} fused), {geo}, cond+uncond batched",
+    what = what or (f"config{'4' if (a.T, a.C) == (704, 240) else '2/3'}: {a.depth}-block MMDiT CFG Euler step "
+                    f"({a.depth - a.fused} joint + {a.fused} fused), {geo}, cond+uncond batched")
+    return {"workload": what,
             "T": a.T, "clip_S": a.C, "text_S": a.TS, "H": a.H, "heads": a.H // 64, "F": a.F, "cfg": a.cfg,
             "weights": "synthetic BF16 N(0,0.02) -> f16 operands (reference weight conversion)",
             "l2": "inputs larger than L2: every step streams ~3.1 GB of weights from HBM (L2 126 MB)"}
@@ -540,7 +541,8 @@ def run_cfg_split(a):
                 "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_ms, "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f16 (split hi+lo activations), f32 accumulate",
                 "data": "synthetic",
-                "config": workload(a),
+                "config": workload(a, f"config2/3 CFG pair split: {a.depth}-block MMDiT CFG Euler step, one arm per GPU, "
+                                      f"8 s audio geometry" if a.T == 188 else None),
                 "parallelism": f"cfg-split x{world // 2} (one CFG arm per GPU, NCCL all-gather of the flow every step"
                                f"{', steps from the host' if a.cfg_split_eager else ', every step one CUDA graph'})",
                 "step_roofline": {"compute_ms": compute_ms, "hbm_ms": hbm_ms, "roofline_ms": max(compute_ms, hbm_ms),
@@ -634,7 +636,10 @@ def run_config5(a):
                 "value": gen_s, "unit": "generations/s", "n_gpus": world, "generations": a.generations,
                 "gens_per_forward": G, "steps_per_generation": steps, "seconds": ms * 1e-3,
                 "cfg_steps_per_s": gen_s * steps, "higher_is_better": True, "scaling": "strong",
-                "data": "synthetic", "config": workload(a), "parallelism": f"dp{world}, {G} generation(s) per forward",
+                "data": "synthetic",
+                "config": workload(a, f"config5: {a.generations} independent generations x {steps} CFG-{a.cfg:g} Euler "
+                                      f"steps, {a.depth}-block MMDiT, 8 s audio geometry, final latents gathered"),
+                "parallelism": f"dp{world}, {G} generation(s) per forward",
                 "x_finite": finite}), flush=True)
     m.close()
     dev.close()

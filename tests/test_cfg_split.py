@@ -90,6 +90,65 @@ def test_schedule_is_the_reference_f32_schedule():
         assert sch[0][0] == np.float32(1.0)
 
 
+class _RankFailed(RuntimeError):
+    pass
+
+
+def _failing_rank(rank, port, out_dir, fail_step):
+    """One rank of the pair; pair rank 1 fails in its forward of `fail_step` (a host exception, as a
+    failed library call would raise), leaves the loop and the group without joining that step's
+    all-gather, and exits 0. Pair rank 0 must see its all-gather end with an error (the peer closed
+    the group, or the group's 5 s timeout) instead of waiting for good."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=5))
+    calls = [0]
+
+    def forward(x, t):
+        if rank == 1 and calls[0] == fail_step:
+            raise _RankFailed(f"rank 1 forward failed at step {calls[0]}")
+        calls[0] += 1
+        return (x * np.float32(0.5 + 0.25 * rank)).astype(np.float32)
+
+    def all_gather(mine):
+        parts = [torch.empty(mine.shape) for _ in range(2)]
+        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(mine)))
+        return parts[0].numpy(), parts[1].numpy()
+
+    t0 = time.monotonic()
+    outcome = "finished"
+    try:
+        cfg_split.loop(4, CFG, np.ones((8, 64), np.float32), forward, all_gather, _euler_ref)
+    except _RankFailed:
+        outcome = "failed"
+    except RuntimeError:
+        outcome = "peer_lost"
+    finally:
+        try:
+            dist.destroy_process_group()
+        except RuntimeError:
+            pass
+    with open(os.path.join(out_dir, f"r{rank}.txt"), "w") as f:
+        f.write(f"{outcome} {calls[0]} {time.monotonic() - t0:.3f}")
+
+
+def test_cfg_split_rank_failure_ends_the_peer_collective(tmp_path):
+    """A rank that fails between steps (its forward raises before the step's all-gather) leaves the
+    pair; the other rank's next all-gather returns an error within the group's timeout, after the
+    steps both ranks completed. Host-only (gloo), no GPU."""
+    fail_step = 2
+    mp.start_processes(_failing_rank, args=(_free_port(), str(tmp_path), fail_step), nprocs=2, join=True,
+                       start_method="spawn")
+    o0, n0, s0 = (tmp_path / "r0.txt").read_text().split()
+    o1, n1, _ = (tmp_path / "r1.txt").read_text().split()
+    assert (o1, int(n1)) == ("failed", fail_step)
+    assert o0 == "peer_lost", "the surviving rank's collective did not end with an error"
+    assert int(n0) == fail_step + 1     # it ran its own forward of the failed step, then lost the peer
+    assert float(s0) < 60.0
+
+
 def _gpu_rank(rank, port, gguf, out_dir):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
