@@ -88,7 +88,7 @@ bool make_out_map_f32(CUtensorMap * m, void * base, uint64_t N, uint64_t rows, u
 // Pipeline depth: as many stages as fit in the 227 KB of shared memory a CTA may use (the qkv
 // epilogue also stages RoPE rows, which costs the 192-wide split tile one stage).
 constexpr int stages_for(int bn, bool split, int epi) {
-    return split ? (bn == 256 ? 3 : bn == 192 ? (epi == EPI_QKV ? 3 : 4) : bn == 128 ? 4 : 5)
+    return split ? (bn == 256 ? 3 : bn == 192 || bn == 176 ? (epi == EPI_QKV ? 3 : 4) : bn == 128 ? 4 : 5)
                  : (bn == 256 ? 4 : bn == 192 ? 5 : bn == 128 ? 6 : 8);
 }
 int gemm_stages(int bn, bool split, int epi) { return stages_for(bn, split, epi); }
@@ -117,6 +117,7 @@ size_t gemm_smem_bytes(int bn, bool split, int epi) {
         case 128: return split ? smem_of<128, true>(epi) : smem_of<128, false>(epi);
         case 192: return split ? smem_of<192, true>(epi) : smem_of<192, false>(epi);
         case 256: return split ? smem_of<256, true>(epi) : smem_of<256, false>(epi);
+        case 176: return split && epi == EPI_SWIGLU ? smem_total<176, true, EPI_SWIGLU>() : 0;
     }
     return 0;
 }
@@ -217,6 +218,9 @@ TileFn kernel_for(int bn, int epi, bool split) {
         case 128: return split ? pick_epi<128, true>(epi) : pick_epi<128, false>(epi);
         case 192: return split ? pick_epi<192, true>(epi) : pick_epi<192, false>(epi);
         case 256: return split ? pick_epi<256, true>(epi) : pick_epi<256, false>(epi);
+        // 11 column groups of [8 w1 | 8 w3]: the SwiGLU GEMMs whose 8192-wide output in 192-wide
+        // tiles leaves SMs idle (376 x 8192: 141 CTAs instead of 129)
+        case 176: return split && epi == EPI_SWIGLU ? pick<176, EPI_SWIGLU, true>() : nullptr;
     }
     return nullptr;
 }
@@ -391,7 +395,7 @@ cudaError_t launch_gemm_ws(const GemmLaunch & g, cudaStream_t s) {
 // Set the dynamic shared-memory limit of every instantiation once, outside any stream capture.
 cudaError_t configure_gemm_kernels() {
     for (int split = 0; split < 2; ++split)
-        for (int bn : {64, 128, 192, 256})
+        for (int bn : {64, 128, 176, 192, 256})
             for (int epi = 0; epi <= EPI_F16_GELUQ; ++epi) {
                 TileFn fn = kernel_for(bn, epi, split != 0);
                 if (!fn) continue;
@@ -453,6 +457,7 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
     }
     TileFn fn = kernel_for(g.bn, g.epi, g.split);
     if (!fn) return cudaErrorInvalidValue;
+    if (g.bn % 32 && g.args.splits != 1) return cudaErrorInvalidValue;   // cluster reductions: 32-column units
     // split-K: the K slices of one output tile form a cluster along grid.z
     return launch_ex(fn, g.grid, dim3(192), g.smem, s, g.args.splits > 1 ? (unsigned) g.args.splits : 1u,
                      g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args.tma_out ? g.to : g.tb, g.args, g.ab_bf16);

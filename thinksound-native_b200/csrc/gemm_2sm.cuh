@@ -194,31 +194,35 @@ gemm2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CU
             }
           }
         } else {
-            // SwiGLU: rows come in groups of 64 = [32 w1 | 32 w3], so warps (0,1) and (2,3) hold
-            // matching w1 and w3 rows for output features g*32 + lane, g = (n0 + 64*pw) / 64: the
-            // CTA's 64 output features are contiguous. Each warp puts its 32 x 32 block in shared
-            // memory (the operand ring is free: every MMA of the pair has completed), the pair
-            // writes silu(w1)·w3 of the chunk's 32 tokens into an f16 tile [NT tokens][64 features],
-            // and once every chunk is in, the four warps write the tile as whole 128-byte token rows.
-            float * xb = (float *) smem + warp * 32 * 32;           // [token][lane]
-            __half * ot = (__half *) (smem + 4 * 32 * 32 * 4);      // [NT][64]
-            const int pw = warp >> 1, odd = warp & 1;
+            // SwiGLU: weight rows come in groups of 16 = [8 w1 | 8 w3]; a warp's 32 rows hold two
+            // groups and give 16 consecutive output features (16 warp .. 16 warp + 15 of the CTA's
+            // 64, which start at n0 / 2). Per chunk of 32 tokens the warp turns its 32 x 32 block
+            // around through padded shared memory (the operand ring is free: every MMA of the pair
+            // has completed), so that lane j then holds token c + j: it forms its 16 outputs
+            // silu(w1)·w3 and puts them, 32 bytes, into an f16 tile [NT tokens][64 features]. Once
+            // every chunk is in, the four warps write the tile as whole 128-byte token rows.
+            float * xb = (float *) smem + warp * (32 * 33);          // [row][token], rows padded to 33
+            __half * ot = (__half *) (smem + 4 * 32 * 33 * 4);      // [NT][64]
 #pragma unroll 1
             for (int c = 0; c < NT; c += 32) {
                 float v[32];
-                tmem_ld32(trow + c, v);
+                tmem_ld32(trow + c, v);                             // weight row `lane`, tokens c .. c+31
 #pragma unroll
-                for (int j = 0; j < 32; ++j) xb[j * 32 + lane] = v[j];
-                asm volatile("bar.sync %0, 64;" ::"r"(2 + pw) : "memory");
-                const float * w1 = (const float *) smem + (2 * pw) * 32 * 32;
-                const float * w3 = w1 + 32 * 32;
-#pragma unroll 4
-                for (int j = odd * 16; j < odd * 16 + 16; ++j)
-                    ot[(c + j) * 64 + 32 * pw + lane] = __float2half_rn(silu_f(w1[j * 32 + lane]) * w3[j * 32 + lane]);
-                asm volatile("bar.sync %0, 64;" ::"r"(2 + pw) : "memory");
+                for (int j = 0; j < 32; ++j) xb[lane * 33 + j] = v[j];
+                __syncwarp();
+                __align__(16) __half h[16];
+#pragma unroll
+                for (int g = 0; g < 2; ++g)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                        h[8 * g + e] = __float2half_rn(silu_f(xb[(16 * g + e) * 33 + lane]) * xb[(16 * g + 8 + e) * 33 + lane]);
+                uint4 * dst = (uint4 *) (ot + (c + lane) * 64 + 16 * warp);
+                dst[0] = *(const uint4 *) h;
+                dst[1] = *(const uint4 *) (h + 8);
+                __syncwarp();
             }
             epi_bar();
-            const int f0 = (n0 >> 6) * 32;                           // the CTA's first output feature
+            const int f0 = n0 >> 1;                                  // the CTA's first output feature
             const int nf = min(64, (a.N - n0) / 2);                  // output features of weight rows < N
             if (ok && nf > 0) {
                 __half * ob = (__half *) a.out + (long long) b * a.out_bs + f0;

@@ -38,7 +38,7 @@ enum GemmEpi : int {
     EPI_F32 = 0,       // out f32 = acc (+bias)
     EPI_F16 = 1,       // out f16 = acc (+bias)
     EPI_F16_SILU = 2,  // out f16 = silu(acc + bias)
-    EPI_SWIGLU = 3,    // columns in groups of 64 = [32 w1 | 32 w3] -> out f16 = silu(a)*b
+    EPI_SWIGLU = 3,    // columns in groups of 16 = [8 w1 | 8 w3] -> out f16 = silu(a)*b
     EPI_QKV = 5,       // bias, per-head RMSNorm(q,k), RoPE(q,k), f16 head-major q/k/v
     EPI_F16_SNAKE = 6, // out split f16 = snake(acc + bias) with per-column e^alpha, e^-beta (VAE;
                        // hardware __sinf: a few 1e-6 absolute, far below the f16 rounding of the output)
@@ -127,10 +127,11 @@ __device__ __forceinline__ void store8_split(__half * o, long long lo, const flo
     }
 }
 
-// Columns one epilogue call handles: one 32-column chunk; a whole 64-column head for the qkv
-// epilogue (RMSNorm + RoPE need it); a [32 w1 | 32 w3] group for SwiGLU.
+// Columns one epilogue call handles: one 32-column chunk (for SwiGLU two [8 w1 | 8 w3] groups); a
+// whole 64-column head for the qkv epilogue (RMSNorm + RoPE need it); a [32 wi_0 | 32 wi_1] group
+// for GEGLU.
 template <int EPI> struct EpiUnit {
-    static constexpr int U = EPI == EPI_QKV || EPI == EPI_SWIGLU || EPI == EPI_GEGLU ? 64 : 32;
+    static constexpr int U = EPI == EPI_QKV || EPI == EPI_GEGLU ? 64 : 32;
 };
 
 // geglu_ (shaders/ops_conv.metal:15-24): tanh-approximated GELU of a, argument clamped to +-10
@@ -170,21 +171,17 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, va + q);
         }
     } else if constexpr (EPI == EPI_SWIGLU) {
-        {
-            const int j = 0;
-            float va[32], vb[32];
-            load32(c0, va);
-            load32(c0 + 32, vb);
-            if (valid) {
-                const long long nout = (long long) (n0 + c0) / 2 + j;
-                __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + nout;
+        // 32 columns = two [8 w1 | 8 w3] groups -> 16 consecutive output features from (n0 + c0) / 2
+        float v[32];
+        load32(c0, v);
+        if (valid) {
+            __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + (n0 + c0) / 2;
 #pragma unroll
-                for (int q = 0; q < 32; q += 8) {
-                    __align__(16) __half h[8];
+            for (int g = 0; g < 2; ++g) {
+                __align__(16) __half h[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(va[q + e]) * vb[q + e]);
-                    *(uint4 *) (o + q) = *(const uint4 *) h;
-                }
+                for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(v[16 * g + e]) * v[16 * g + 8 + e]);
+                *(uint4 *) (o + 8 * g) = *(const uint4 *) h;
             }
         }
     } else if constexpr (EPI == EPI_QKV) {
@@ -294,6 +291,7 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
                                           const CUtensorMap * tmO = nullptr) {
     using L = GemmSmem<BN, STAGES, SPLIT, EPI, WS>;
     static_assert(!WS || SPLIT, "split weights go with a split A operand");
+    static_assert(BN % 32 == 0 || (BN % 16 == 0 && EPI == EPI_SWIGLU), "tile widths not a multiple of 32: SwiGLU only");
     extern __shared__ uint8_t smem_raw[];
     uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
     uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
@@ -454,6 +452,20 @@ __device__ __forceinline__ void gemm_tile(const CUtensorMap * tmA, const CUtenso
             auto load_tmem = [&](int c, float * v) { tmem_ld32(trow + c, v); };
 #pragma unroll 1
             for (int u = 0; u < BN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, ec, r, u, n0, t0, b0, z, ok, load_tmem);
+            if constexpr (EPI == EPI_SWIGLU && BN % 32 == 16) {
+                // the last [8 w1 | 8 w3] group of a tile width that is an odd multiple of 16
+                constexpr int c0 = BN - 16;
+                float v[16];
+                tmem_ld16(trow + c0, v);
+                const int b = b0 + r / a.bt, t = t0 + r % a.bt;
+                if (ok && t < a.rows && b < a.B && n0 + c0 < a.N) {
+                    __align__(16) __half h[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(v[e]) * v[8 + e]);
+                    *(uint4 *) ((__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + (n0 + c0) / 2) =
+                        *(const uint4 *) h;
+                }
+            }
         } else {
             // stage this CTA's partial in its own shared memory as [BN/4][128] float4 (the stage ring
             // is free: every TMA load was consumed and every MMA has completed)

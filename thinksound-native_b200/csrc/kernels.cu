@@ -809,7 +809,7 @@ __global__ void prep_weight_kernel(uint16_t * dst, const void * src, const void 
         const void * s = src;
         long long row = n;
         if (mode == 1) row = (n % Hq) * 3 + n / Hq;
-        else if (mode == 2) { const long long g = n >> 6, w = n & 63; s = w < 32 ? src : src2; row = g * 32 + (w & 31); }
+        else if (mode == 2) { const long long g = n >> 4, w = n & 15; s = w < 8 ? src : src2; row = g * 8 + (w & 7); }
         const float f = src_value(s, type, (size_t) row * Kt + (size_t) ic * taps + tap);
         dst[idx] = out_bf16 ? tsn_f32_to_bf16(f) : tsn_ref_f32_to_f16(f);
     }

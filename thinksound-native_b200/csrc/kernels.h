@@ -222,7 +222,8 @@ cudaError_t launch_wait_selftest(int * err, unsigned long long limit_ns, cudaStr
 // ---- weight preparation ----
 // dst[n][tap*IC + ic] = cvt(src[row(n)][ic][tap]) for conv sources ([OC][IC][K], K=taps) or
 // dst[n][k] = cvt(src[row(n)][k]) for linear sources (taps = 1). row(n) by mode:
-//   0 identity; 1 qkv de-interleave (row j*Hq + c <- 3c + j); 2 [64 w1 | 64 w3] interleave.
+//   0 identity; 1 qkv de-interleave (row j*Hq + c <- 3c + j); 2 w1/w3 interleave in [8 w1 | 8 w3]
+//   row groups.
 // src_type: 0 f32, 1 f16, 30 bf16 (GGUF types); out_bf16 selects the compute operand type.
 cudaError_t launch_prep_weight(void * dst, const void * src, const void * src2, int src_type, int out_bf16,
                                long long N, int IC, int taps, int mode, int Hq, cudaStream_t s);

@@ -185,7 +185,8 @@ struct Loader {
         if (!rc && bias) rc = vec(p + ".bias", N, kind == 2 ? 1 : 0, &L.b);
         return rc;
     }
-    // w1 and w3 interleaved in [32 w1 rows | 32 w3 rows] groups -> one [2F][taps*K_in] matrix
+    // w1 and w3 interleaved in [8 w1 rows | 8 w3 rows] groups -> one [2F][taps*K_in] matrix (any
+    // tile width that is a multiple of 16 keeps each w1 row with its w3 row)
     int w13(const std::string & p, bool conv, int F, int K_in, Lin & L) {
         L.N = 2 * F; L.K_in = K_in; L.taps = conv ? 3 : 1;
         const GgufTensorInfo * t1, * t3;
@@ -603,14 +604,16 @@ struct Plan {
         const int smax = partial ? MAX_PARTS : 8;   // clusters hold at most 8 CTAs portably
         // tile widths that do not divide N leave the last column tile partly empty (its TMA rows
         // beyond N read zeros and its epilogue skips those columns)
-        for (int bn : {256, 192, 128, 64}) {
-            if (N % bn && (bn != 192 || N < 192)) continue;
-            const double kcost = split ? (bn == 256 ? 0.74 : bn == 192 ? 0.57 : bn == 128 ? 0.40 : 0.30)
+        const bool w176 = epi == EPI_SWIGLU && split;   // the 176-wide SwiGLU tile (no split-K cluster)
+        for (int bn : {256, 192, 176, 128, 64}) {
+            if (bn == 176 && !w176) continue;
+            if (N % bn && ((bn != 192 && bn != 176) || N < bn)) continue;
+            const double kcost = split ? (bn == 256 ? 0.74 : bn == 192 ? 0.57 : bn == 176 ? 0.53 : bn == 128 ? 0.40 : 0.30)
                                        : (bn == 256 ? 0.37 : bn == 192 ? 0.30 : bn == 128 ? 0.24 : 0.18);
             const int tiles = mtt * mtb * ((N + bn - 1) / bn);
             // the cost model searches up to 8 K slices; the autotuner also times up to MAX_PARTS
             for (int s = 1; s <= 8 && s <= kb; ++s) {
-                if (!splits_valid(kb, s, smax)) continue;
+                if (!splits_valid(kb, s, smax) || (bn == 176 && s > 1)) continue;
                 const int kbps = (kb + s - 1) / s;
                 const int cap = partial ? gemm_cluster_capacity(bn, epi, split, 1) : gemm_cluster_capacity(bn, epi, split, s);
                 if (cap <= 0) continue;
@@ -633,7 +636,7 @@ struct Plan {
         if (fb) {
             const bool pair = fb > 2000;
             if (pair ? (pair_ok && gemm2_smem_bytes(fb - 2000, split) && splits_valid(kb, fs, partial ? smax : 1))
-                     : (splits_valid(kb, fs, smax) && (fb == 192 || N % fb == 0))) {
+                     : (splits_valid(kb, fs, smax) && (fb == 192 || fb == 176 || N % fb == 0) && (fb != 176 || (w176 && fs == 1)))) {
                 bn_best = fb;
                 s_best = fs;
             }
@@ -1486,7 +1489,7 @@ int Model::autotune(std::string & report) {
         double best = 1e30;
         std::pair<int, int> bc{0, 0};
         std::string tried;
-        for (int bn : {256, 192, 128, 64, 2192, 2128, 2064, 2256})
+        for (int bn : {256, 192, 176, 128, 64, 2192, 2128, 2064, 2256})
             for (int sp = 1; sp <= MAX_PARTS; ++sp) {
                 gemm_force.clear();
                 gemm_force[gid] = {bn, sp};
