@@ -183,6 +183,45 @@ def test_tiny_step_vs_oracle(dev, tiny_gguf):
     assert rel_l2(x - inp["x"], xr - inp["x"]) < 5 * FLOW_TOL
 
 
+def test_step_host_buffers_match_device_step(dev, tiny_gguf):
+    """tsn_dit_step_host (copy in, schedule row, the step graph, copy out) gives the device step's
+    bits with pageable numpy buffers, with page-locked buffers, in place (x_in is x_out) and across
+    repeated calls at other t and dt."""
+    import torch
+    T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
+    inp = make_inputs(T, C, TS, TINY["H"], seed=SEED + 2)
+    m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
+    sched = [(1.0, -1.0 / 24), (0.75, -0.05), (0.5, -1.0 / 24)]
+
+    def device_steps(x0, n):
+        m.set_x(x0)
+        out = []
+        for t, dt in sched[:n]:
+            m.step(t, 5.0, dt)
+            x = np.zeros((T, 64), np.float32)
+            m.get_x(x)
+            out.append(x)
+        return out
+
+    ref = device_steps(inp["x"], 3)
+    # pageable buffers
+    xo = np.zeros((T, 64), np.float32)
+    m.step_host(np.ascontiguousarray(inp["x"]), xo, sched[0][0], 5.0, sched[0][1])
+    assert np.array_equal(xo, ref[0])
+    # page-locked buffers, then in place on the same pinned buffer for the next steps
+    xin = torch.from_numpy(inp["x"].copy()).pin_memory()
+    xout = torch.zeros_like(xin).pin_memory()
+    m.step_host(xin, xout, sched[0][0], 5.0, sched[0][1])
+    assert np.array_equal(xout.numpy(), ref[0])
+    for k in (1, 2):
+        m.step_host(xout, xout, sched[k][0], 5.0, sched[k][1])
+        assert np.array_equal(xout.numpy(), ref[k]), k
+    # the first pair again (its graph is cached): the same bits as the first time
+    m.step_host(xin, xout, sched[0][0], 5.0, sched[0][1])
+    assert np.array_equal(xout.numpy(), ref[0])
+    m.close()
+
+
 def test_bf16_operands_rejected(dev, tiny_gguf):
     """BF16 operands are refused loudly (they cannot meet the 1e-3 flow gate), not silently downgraded."""
     with pytest.raises(tsn.TsnError) as e:
