@@ -4,7 +4,7 @@ driver, built with src/gpu.mm replaced by the library's tn::gpu::Device
 (thinksound-native_b200/integration/gpu_tsn.cpp, oracle/_ref/ts_ref_dit_tsn), run on the GPU.
 Every named dispatch of that code then runs on the runtime face (tsn_dispatch and the compat
 kernels), and its results must match the same host code on the CPU device (the golden fixtures):
-flow rel-L2 <= 1e-3 and every parity tap <= 2e-3 (SURVEY's gates), the 4-step sample, the VAE
+flow rel-L2 <= 1e-3 and every parity tap <= 2e-3 (the path's parity gates), the 4-step sample, the VAE
 decode and both text encoders <= 1e-3.
 """
 import os
