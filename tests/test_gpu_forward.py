@@ -115,8 +115,9 @@ def test_tile_table_round_trip(dev, tiny_gguf):
 
 
 def test_pair_kernel_tiles_vs_oracle(dev, tiny_gguf, monkeypatch):
-    """The static tile plan, and the CTA-pair GEMM (tile code 2000 + NT, only ever picked by the
-    autotuner) pinned on every GEMM it can serve, without and with K slices: the flow stays within
+    """The static tile plan, and the CTA-pair GEMM (tile code 2000 + NT: picked by the autotuner and by
+    the tile table's 30 s entries) pinned on every GEMM it can serve, with 64- and 96-token tiles,
+    without and with K slices: the flow stays within
     the gate of the CPU oracle, and the f32 outputs written through TMA store views equal the
     per-lane store epilogues (TSN_NO_TMA_OUT=1) bit for bit."""
     T, C, TS = TINY_SEQ["T"], TINY_SEQ["C"], TINY_SEQ["TS"]
@@ -124,7 +125,7 @@ def test_pair_kernel_tiles_vs_oracle(dev, tiny_gguf, monkeypatch):
     orc = O.Oracle(tiny_gguf)
     refs = [orc.forward(T, C, TS, inp["x"], 0.5, inp["clip_pp"], inp["sync_gather"], inp[f"text_pp_{sfx}"],
                         inp[f"gcmlp_{sfx}"]) for sfx in ("cond", "unc")]
-    for slices in (0, 1, 2):   # 0: the static plan
+    for code, slices in ((0, 0), (2064, 1), (2064, 2), (2096, 1)):   # 0: the static plan
         flows = []
         for tma in (True, False):
             if tma:
@@ -134,15 +135,15 @@ def test_pair_kernel_tiles_vs_oracle(dev, tiny_gguf, monkeypatch):
             m = gpu_model(dev, tiny_gguf, inp, T, C, TS)
             if slices:
                 t = m.tiles().copy()
-                t[:, 1], t[:, 2] = 2064, slices
+                t[:, 1], t[:, 2] = code, slices
                 m.set_tiles(t)
-                assert (m.tiles()[:, 1] == 2064).any(), "no GEMM took the pair tile"
+                assert (m.tiles()[:, 1] == code).any(), "no GEMM took the pair tile"
             flow = np.zeros((2, T, 64), np.float32)
             m.forward(0.5, flow)
             for arm in (0, 1):
-                assert rel_l2(flow[arm], refs[arm]) < FLOW_TOL, (slices, tma, arm)
+                assert rel_l2(flow[arm], refs[arm]) < FLOW_TOL, (code, slices, tma, arm)
             flows.append(flow)
-        assert np.array_equal(flows[0], flows[1]), f"TMA-store and per-lane epilogues differ (K slices {slices})"
+        assert np.array_equal(flows[0], flows[1]), f"TMA-store and per-lane epilogues differ ({code}, K slices {slices})"
     monkeypatch.delenv("TSN_NO_TMA_OUT", raising=False)
 
 
@@ -322,9 +323,11 @@ def test_generations_batched_match_single(dev, tiny_gguf, G):
         assert rel_l2(xG[g] - inp["x"], x1 - inp["x"]) < tol
 
 
-def test_pair_kernel_swiglu_real_widths_vs_oracle(dev, wide_gguf):
-    """The CTA-pair GEMM with 192-token tiles pinned on the FFN w1/w3 GEMMs (SwiGLU epilogue through
-    the staged f16 tile) at real widths and the 8 s latent length: flow within the gate."""
+@pytest.mark.parametrize("code", [2192, 2096])
+def test_pair_kernel_swiglu_real_widths_vs_oracle(dev, wide_gguf, code):
+    """The CTA-pair GEMM with 192- and 96-token tiles (96: an arm's 188 latent rows as 96 + 92)
+    pinned on the FFN w1/w3 GEMMs (SwiGLU epilogue through the staged f16 tile) at real widths and
+    the 8 s latent length: flow within the gate."""
     T, C, TS = WIDE_SEQ["T"], WIDE_SEQ["C"], WIDE_SEQ["TS"]
     inp = make_inputs(T, C, TS, WIDE["H"])
     m = gpu_model(dev, wide_gguf, inp, T, C, TS)
@@ -334,9 +337,9 @@ def test_pair_kernel_swiglu_real_widths_vs_oracle(dev, wide_gguf):
     w13 = [i for i, l in enumerate(gemms) if l.split()[1] in ("ffn_w13", "audio_in.w13") and "group=" not in l]
     assert w13
     for i in w13:
-        t[i, 1:] = (2192, 1)
+        t[i, 1:] = (code, 1)
     m.set_tiles(t)
-    assert all(m.tiles()[i, 1] == 2192 for i in w13), "a w1/w3 GEMM did not take the pair tile"
+    assert all(m.tiles()[i, 1] == code for i in w13), "a w1/w3 GEMM did not take the pair tile"
     flow = np.zeros((2, T, 64), np.float32)
     m.forward(0.5, flow)
     orc = O.Oracle(wide_gguf)

@@ -133,12 +133,14 @@ size_t gemm_persistent_smem_bytes(int bn) {
 }
 
 constexpr int stages2(int nt, bool split) {
-    return split ? (nt == 256 ? 4 : nt == 192 ? 5 : nt == 128 ? 6 : 8) : (nt == 256 ? 6 : nt == 192 ? 7 : 8);
+    return split ? (nt == 256 ? 4 : nt == 192 ? 5 : nt == 128 ? 6 : nt == 96 ? 7 : 8) : (nt == 256 ? 6 : nt == 192 ? 7 : 8);
 }
 size_t gemm2_smem_bytes(int nt, bool split) {
     switch (nt * 2 + (split ? 1 : 0)) {
         case 64 * 2: return Gemm2Smem<64, stages2(64, false), false>::TOTAL;
         case 64 * 2 + 1: return Gemm2Smem<64, stages2(64, true), true>::TOTAL;
+        case 96 * 2: return Gemm2Smem<96, stages2(96, false), false>::TOTAL;
+        case 96 * 2 + 1: return Gemm2Smem<96, stages2(96, true), true>::TOTAL;
         case 128 * 2: return Gemm2Smem<128, stages2(128, false), false>::TOTAL;
         case 128 * 2 + 1: return Gemm2Smem<128, stages2(128, true), true>::TOTAL;
         case 192 * 2: return Gemm2Smem<192, stages2(192, false), false>::TOTAL;
@@ -165,6 +167,7 @@ Kernel2Fn pick2_epi(int epi, bool split) {
 Kernel2Fn gemm2_for(int nt, int epi, bool split) {
     switch (nt) {
         case 64: return pick2_epi<64>(epi, split);
+        case 96: return pick2_epi<96>(epi, split);   // 188 tokens of one arm as 96 + 92
         case 128: return pick2_epi<128>(epi, split);
         case 192: return pick2_epi<192>(epi, split);
         case 256: return pick2_epi<256>(epi, split);
@@ -427,7 +430,7 @@ cudaError_t configure_gemm_kernels() {
                                              (int) gemm_persistent_smem_bytes(bn));
         if (e != cudaSuccess) return e;
     }
-    for (int nt : {64, 128, 192, 256})
+    for (int nt : {64, 96, 128, 192, 256})
         for (int epi : {(int) EPI_F32, (int) EPI_SWIGLU})
             for (int split = 0; split < 2; ++split) {
                 cudaError_t e = cudaFuncSetAttribute((const void *) gemm2_for(nt, epi, split != 0),

@@ -1489,7 +1489,7 @@ int Model::autotune(std::string & report) {
         double best = 1e30;
         std::pair<int, int> bc{0, 0};
         std::string tried;
-        for (int bn : {256, 192, 176, 128, 64, 2192, 2128, 2064, 2256})
+        for (int bn : {256, 192, 176, 128, 64, 2192, 2128, 2096, 2064, 2256})
             for (int sp = 1; sp <= MAX_PARTS; ++sp) {
                 gemm_force.clear();
                 gemm_force[gid] = {bn, sp};
