@@ -323,6 +323,29 @@ def test_generations_batched_match_single(dev, tiny_gguf, G):
         assert rel_l2(xG[g] - inp["x"], x1 - inp["x"]) < tol
 
 
+def test_grouped_w13_persistent_text_tiles_same_bits(dev, wide_gguf, monkeypatch):
+    """The joint blocks' grouped w1/w3 launch runs the text stream as persistent 208-wide tile lists
+    on the SMs the latent and clip tiles leave free; its outputs are the same dot products as the
+    ordinary 256-wide tiles (TSN_NO_PERSIST_GROUP=1), so the flows are bit-identical."""
+    T, C, TS = WIDE_SEQ["T"], WIDE_SEQ["C"], WIDE_SEQ["TS"]
+    inp = make_inputs(T, C, TS, WIDE["H"])
+    flows = []
+    for off in (False, True):
+        if off:
+            monkeypatch.setenv("TSN_NO_PERSIST_GROUP", "1")
+        else:
+            monkeypatch.delenv("TSN_NO_PERSIST_GROUP", raising=False)
+        m = gpu_model(dev, wide_gguf, inp, T, C, TS)
+        ops = [l for l in m.profile_ops().splitlines() if "ffn_w13" in l and "group=" in l]
+        assert ops and all(("persist=" in l) != off for l in ops), ops
+        flow = np.zeros((2, T, 64), np.float32)
+        m.forward(0.5, flow)
+        flows.append(flow)
+        m.close()
+    monkeypatch.delenv("TSN_NO_PERSIST_GROUP", raising=False)
+    assert np.array_equal(flows[0], flows[1])
+
+
 @pytest.mark.parametrize("code", [2192, 2096])
 def test_pair_kernel_swiglu_real_widths_vs_oracle(dev, wide_gguf, code):
     """The CTA-pair GEMM with 192- and 96-token tiles (96: an arm's 188 latent rows as 96 + 92)

@@ -240,6 +240,13 @@ GroupFn group_epi(int epi, bool split) {
     if (epi == EPI_F32) return split ? pick_group<BN, EPI_F32, true>() : pick_group<BN, EPI_F32, false>();
     return nullptr;
 }
+// the grouped SwiGLU launch whose shallow member runs as 208-wide persistent tile lists
+constexpr int GROUP_P_BN = 208, GROUP_P_STAGES = 3;
+GroupFn group_p_for(int bn, int epi, bool split) {
+    if (bn == 256 && epi == EPI_SWIGLU && split)
+        return (GroupFn) gemm_tc_group_p<256, GROUP_P_BN, EPI_SWIGLU, stages_for(256, true, EPI_SWIGLU), GROUP_P_STAGES, true>;
+    return nullptr;
+}
 GroupFn group_for(int bn, int epi, bool split) {
     switch (bn) {
         case 64: return group_epi<64>(epi, split);
@@ -425,6 +432,12 @@ cudaError_t configure_gemm_kernels() {
                                          (int) gemm_ws_persistent_smem_bytes(bn, epi));
             if (e != cudaSuccess) return e;
         }
+    {
+        cudaError_t e = cudaFuncSetAttribute((const void *) group_p_for(256, EPI_SWIGLU, true),
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int) gemm_group_persist_smem_bytes(256, EPI_SWIGLU, true));
+        if (e != cudaSuccess) return e;
+    }
     for (int bn : {128, 192, 256}) {
         cudaError_t e = cudaFuncSetAttribute((const void *) persistent_for(bn), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int) gemm_persistent_smem_bytes(bn));
@@ -466,8 +479,14 @@ cudaError_t launch_gemm(const GemmLaunch & g, cudaStream_t s) {
                      g.ta, g.split ? g.ta2 : g.ta, g.tb, g.args.tma_out ? g.to : g.tb, g.args, g.ab_bf16);
 }
 
+int gemm_group_persist_bn(int bn, int epi, bool split) { return group_p_for(bn, epi, split) ? GROUP_P_BN : 0; }
+size_t gemm_group_persist_smem_bytes(int bn, int epi, bool split) {
+    if (!group_p_for(bn, epi, split)) return 0;
+    return std::max(gemm_smem_bytes(bn, split, epi), (size_t) PersistListSmem<GROUP_P_BN, GROUP_P_STAGES, true>::TOTAL);
+}
+
 cudaError_t launch_gemm_group(const GroupLaunch & g, cudaStream_t s) {
-    GroupFn fn = group_for(g.bn, g.epi, g.split);
+    GroupFn fn = g.args.persist_q >= 0 ? group_p_for(g.bn, g.epi, g.split) : group_for(g.bn, g.epi, g.split);
     const int n = g.args.n;
     if (!fn || n < 1 || n > MAX_GROUP || g.cluster < 1 || g.cluster > 8) return cudaErrorInvalidValue;
     for (int q = 0; q < n; ++q) {
@@ -477,6 +496,12 @@ cudaError_t launch_gemm_group(const GroupLaunch & g, cudaStream_t s) {
         if (g.cluster > 1 && (begin % g.cluster || g.args.slices[q] != g.cluster || g.args.p[q].splits != g.cluster))
             return cudaErrorInvalidValue;
         if (g.cluster == 1 && g.args.p[q].splits != 1) return cudaErrorInvalidValue;
+    }
+    if (g.args.persist_q >= 0) {   // the persistent member: its own CTA range, one CTA per tile run
+        const int q = g.args.persist_q, begin = q ? g.args.cta_end[q - 1] : 0;
+        if (q >= n || g.cluster != 1 || g.args.persist_ctas < 1 || g.args.persist_tiles < 1 ||
+            g.args.cta_end[q] - begin != g.args.persist_ctas)
+            return cudaErrorInvalidValue;
     }
     return launch_cl(fn, dim3((unsigned) g.args.cta_end[n - 1]), dim3(192), g.smem, s, dim3((unsigned) g.cluster, 1, 1),
                      g.maps, g.args, g.ab_bf16);

@@ -171,13 +171,15 @@ __device__ __forceinline__ void epi_unit(const GemmArgs & a, const EpiConst & ec
             for (int q = 0; q < 32; q += 8) store8_split(o + q, a.out_lo, va + q);
         }
     } else if constexpr (EPI == EPI_SWIGLU) {
-        // 32 columns = two [8 w1 | 8 w3] groups -> 16 consecutive output features from (n0 + c0) / 2
+        // 32 columns = two [8 w1 | 8 w3] groups -> 16 consecutive output features from (n0 + c0) / 2;
+        // a tile that overhangs N may end inside the unit: only whole groups below N are stored
         float v[32];
         load32(c0, v);
         if (valid) {
             __half * o = (__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + (n0 + c0) / 2;
 #pragma unroll
             for (int g = 0; g < 2; ++g) {
+                if (n0 + c0 + 16 * g >= a.N) break;
                 __align__(16) __half h[8];
 #pragma unroll
                 for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(v[16 * g + e]) * v[16 * g + 8 + e]);
@@ -576,6 +578,9 @@ struct GroupArgs {
     int cta_end[MAX_GROUP];    // exclusive end of each problem's CTA range in grid.x
     int slices[MAX_GROUP];     // K slices per tile
     int m_tiles[MAX_GROUP];    // M tiles per problem
+    // gemm_tc_group_p only: problem persist_q runs on persist_ctas persistent CTAs, each taking an
+    // equal run of its persist_tiles tiles (persist_bn wide, M tile fastest)
+    int persist_q = -1, persist_ctas = 0, persist_tiles = 0;
 };
 
 template <int BN, int EPI, int STAGES, bool SPLIT>
@@ -585,6 +590,199 @@ gemm_tc_group(const __grid_constant__ GroupMaps maps, const __grid_constant__ Gr
     int q = 0;
     while (q + 1 < g.n && x >= g.cta_end[q]) ++q;
     const int l = x - (q ? g.cta_end[q - 1] : 0);
+    const int S = g.slices[q], z = l % S, tile = l / S;
+    const int mi = tile % g.m_tiles[q], ni = tile / g.m_tiles[q];
+    gemm_tile<BN, EPI, STAGES, SPLIT>(&maps.a[q], &maps.a2[q], &maps.b[q], g.p[q], ab_bf16, mi, ni, z, x, nullptr, &maps.o[q]);
+}
+
+// ------------------------------------------------------------------------------------------
+// A run of output tiles [lo, hi) of one problem on one CTA (the shallow problem of a grouped
+// launch whose deep tiles leave some SMs free): tile t is (M tile t % m_tiles, N tile
+// t / m_tiles), PBN columns wide, no K slices. The operand ring runs on across tile boundaries and
+// two TMEM accumulators (columns 0 and 256) let the epilogue of tile i overlap the mainloop of
+// tile i + 1. Same warp roles as gemm_tile; epilogue through epi_unit (plus a 16-column tail for
+// SwiGLU widths that are odd multiples of 16). Shared memory: PSTAGES stages of split A + PBN
+// weight rows, then the barriers.
+template <int PBN, int PSTAGES, bool SPLIT>
+struct PersistListSmem {
+    static constexpr int A_BYTES = 128 * 128;
+    static constexpr int NA = SPLIT ? 2 : 1;
+    static constexpr int B_OFF = NA * A_BYTES;
+    static constexpr int STAGE = NA * A_BYTES + PBN * 128;
+    static constexpr int BAR_OFF = PSTAGES * STAGE;
+    static constexpr int TOTAL = BAR_OFF + 256 + 1024;   // barriers, TMEM slot, abort flag + alignment slack
+    static_assert(STAGE % 1024 == 0, "stages must stay 1024-byte aligned");
+};
+
+template <int PBN, int EPI, int PSTAGES, bool SPLIT>
+__device__ __forceinline__ void gemm_tile_list(const CUtensorMap * tmA, const CUtensorMap * tmA2, const CUtensorMap * tmB,
+                                               const GemmArgs & a, const int ab_bf16, const int m_tiles, const int lo,
+                                               const int hi) {
+    using L = PersistListSmem<PBN, PSTAGES, SPLIT>;
+    constexpr int ACC = 256;
+    static_assert(PBN <= ACC && PBN % 16 == 0, "tile width");
+    static_assert(PBN % 32 == 0 || EPI == EPI_SWIGLU, "odd multiples of 16: SwiGLU only");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * smem = (uint8_t *) (((uintptr_t) smem_raw + 1023) & ~(uintptr_t) 1023);
+    uint64_t * full = (uint64_t *) (smem + L::BAR_OFF);
+    uint64_t * empty = full + PSTAGES;
+    uint64_t * afull = empty + PSTAGES;      // [2] accumulator ready for the epilogue
+    uint64_t * aempty = afull + 2;           // [2] accumulator drained (one arrival per epilogue warp)
+    uint32_t * tslot = (uint32_t *) (aempty + 2);
+    volatile int * abort_flag = (volatile int *) (tslot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nk = a.k_blocks;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PSTAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&afull[b], 1); mbar_init(&aempty[b], 4); }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (threadIdx.x == 0) pdl_trigger();
+    if (warp == 4 && lane == 0) {
+        tma_prefetch(tmA);
+        if (SPLIT) tma_prefetch(tmA2);
+        tma_prefetch(tmB);
+    }
+    if (warp == 5) tmem_alloc(tslot, 2 * ACC);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    auto coords = [&](int tile, int & t0, int & b0, int & n0) {
+        const int mi = tile % m_tiles, ni = tile / m_tiles;
+        t0 = (mi % a.m_tiles_t) * a.bt;
+        b0 = (mi / a.m_tiles_t) * a.bb;
+        n0 = ni * PBN;
+    };
+    if (warp == 4) {
+        if (lane == 0) {
+            const uint32_t stage_tx = L::STAGE - (a.a_rows ? (uint32_t) (128 - a.a_rows) * 128u * (SPLIT ? 2u : 1u) : 0u);
+            int t0, b0, n0;
+            coords(lo, t0, b0, n0);
+            // the first tile's weight stages do not depend on the upstream kernel
+            const int pre = lo < hi ? (nk < PSTAGES ? nk : PSTAGES) : 0;
+            for (int i = 0; i < pre; ++i) {
+                mbar_expect_tx(&full[i], stage_tx);
+                tma_load_2d(smem + i * L::STAGE + L::B_OFF, tmB, &full[i], i * 64, n0);
+            }
+            pdl_wait();
+            int g = 0;   // k blocks issued so far (ring position)
+            bool stop = false;
+            for (int tile = lo; tile < hi && !stop; ++tile) {
+                coords(tile, t0, b0, n0);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % PSTAGES;
+                    if (g >= PSTAGES && !mbar_wait(&empty[s], ((g / PSTAGES) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_EMPTY)) {
+                        stop = true;
+                        break;
+                    }
+                    uint8_t * sa = smem + s * L::STAGE;
+                    if (g >= pre) {
+                        mbar_expect_tx(&full[s], stage_tx);
+                        tma_load_2d(sa + L::B_OFF, tmB, &full[s], kb * 64, n0);
+                    }
+                    const int tap = kb / a.ic_blocks, ic0 = (kb % a.ic_blocks) * 64;
+                    const int row = t0 + tap * (a.dil > 1 ? a.dil : 1) - a.pad;
+                    tma_load_3d(sa, tmA, &full[s], ic0, row, b0);
+                    if (SPLIT) tma_load_3d(sa + L::A_BYTES, tmA2, &full[s], ic0, row, b0);
+                }
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(PBN, ab_bf16);
+            int g = 0, i = 0;
+            bool stop = false;
+            for (int tile = lo; tile < hi && !stop; ++tile, ++i) {
+                const int buf = i & 1;
+                if (i >= 2 && !mbar_wait(&aempty[buf], ((i >> 1) - 1) & 1, abort_flag, a.err, DEV_TIMEOUT_TMEM)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t) (buf * ACC);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % PSTAGES;
+                    if (!mbar_wait(&full[s], (g / PSTAGES) & 1, abort_flag, a.err, DEV_TIMEOUT_FULL)) { stop = true; break; }
+                    tc_fence_after();
+                    const uint8_t * sa = smem + s * L::STAGE;
+                    const uint64_t ad = umma_desc_sw128(sa), bd = umma_desc_sw128(sa + L::B_OFF);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        umma_f16(d, ad + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, (kb | k) != 0);
+                        if (SPLIT) {
+                            const uint64_t al = umma_desc_sw128(sa + L::A_BYTES);
+                            umma_f16(d, al + (uint64_t) (2 * k), bd + (uint64_t) (2 * k), idesc, 1u);
+                        }
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (!stop) umma_commit(&afull[buf]);
+            }
+        }
+    } else {
+        pdl_wait();
+        const int r = warp * 32 + lane;
+        const uint32_t trow = tmem + ((uint32_t) (warp * 32) << 16);
+        int i = 0;
+        for (int tile = lo; tile < hi; ++tile, ++i) {
+            const int buf = i & 1;
+            const bool ok = mbar_wait(&afull[buf], (i >> 1) & 1, abort_flag, a.err, DEV_TIMEOUT_TMEM) && !*abort_flag;
+            if (!ok) break;
+            tc_fence_after();
+            int t0, b0, n0;
+            coords(tile, t0, b0, n0);
+            const uint32_t tb = trow + (uint32_t) (buf * ACC);
+            auto load_tmem = [&](int c, float * v) { tmem_ld32(tb + (uint32_t) c, v); };
+            const EpiConst ec{a.bias ? a.bias + n0 : nullptr, nullptr, nullptr, nullptr, t0};
+#pragma unroll 1
+            for (int u = 0; u < PBN / EpiUnit<EPI>::U; ++u) epi_unit<EPI>(a, ec, r, u, n0, t0, b0, 0, true, load_tmem);
+            if constexpr (EPI == EPI_SWIGLU && PBN % 32 == 16) {
+                constexpr int c0 = PBN - 16;
+                float v[16];
+                tmem_ld16(tb + (uint32_t) c0, v);
+                const int b = b0 + r / a.bt, t = t0 + r % a.bt;
+                if (t < a.rows && b < a.B && n0 + c0 < a.N) {
+                    __align__(16) __half h[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(silu_f(v[e]) * v[8 + e]);
+                    *(uint4 *) ((__half *) a.out + (long long) b * a.out_bs + (long long) t * a.ldo + (n0 + c0) / 2) =
+                        *(const uint4 *) h;
+                }
+            }
+            // this warp is done reading accumulator `buf`
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&aempty[buf])) : "memory");
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * ACC);
+    }
+    if (*abort_flag && threadIdx.x == 0) {
+        // let TMA copies that were issued but never consumed land before the CTA's smem is reused
+        const uint64_t t1 = global_ns();
+        while (global_ns() - t1 < 20000ull) {}
+    }
+}
+
+// A grouped launch whose problem g.persist_q runs as a tile list on g.persist_ctas persistent CTAs
+// (gemm_tile_list, PBN wide); the other problems' CTAs are ordinary tiles (gemm_tile, BN wide).
+// Dynamic shared memory: the larger of the two layouts.
+template <int BN, int PBN, int EPI, int STAGES, int PSTAGES, bool SPLIT>
+__global__ void __launch_bounds__(192, 1)
+gemm_tc_group_p(const __grid_constant__ GroupMaps maps, const __grid_constant__ GroupArgs g, const int ab_bf16) {
+    const int x = (int) blockIdx.x;
+    int q = 0;
+    while (q + 1 < g.n && x >= g.cta_end[q]) ++q;
+    const int l = x - (q ? g.cta_end[q - 1] : 0);
+    if (q == g.persist_q) {
+        const int P = g.persist_ctas, T = g.persist_tiles;
+        const int lo = (int) ((long long) T * l / P), hi = (int) ((long long) T * (l + 1) / P);
+        gemm_tile_list<PBN, EPI, PSTAGES, SPLIT>(&maps.a[q], &maps.a2[q], &maps.b[q], g.p[q], ab_bf16, g.m_tiles[q], lo, hi);
+        return;
+    }
     const int S = g.slices[q], z = l % S, tile = l / S;
     const int mi = tile % g.m_tiles[q], ni = tile / g.m_tiles[q];
     gemm_tile<BN, EPI, STAGES, SPLIT>(&maps.a[q], &maps.a2[q], &maps.b[q], g.p[q], ab_bf16, mi, ni, z, x, nullptr, &maps.o[q]);

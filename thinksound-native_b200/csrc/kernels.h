@@ -92,6 +92,10 @@ struct GroupLaunch {
     size_t smem = 0;
 };
 cudaError_t launch_gemm_group(const GroupLaunch & g, cudaStream_t s);
+// grouped launches with a persistent shallow member (GroupArgs::persist_q): its tile width (0: no
+// such kernel for this tile width / epilogue) and the launch's dynamic shared memory
+int gemm_group_persist_bn(int bn, int epi, bool split);
+size_t gemm_group_persist_smem_bytes(int bn, int epi, bool split);
 cudaError_t configure_gemm_kernels();
 int gemm_cluster_capacity(int bn, int epi, bool split, int cluster);
 bool gemm_group_supported(int bn, int epi, bool split);   // a grouped instantiation exists

@@ -877,8 +877,9 @@ struct Plan {
     }
     // one grouped launch of planned members; members with the deepest CTAs first, so that the
     // block scheduler starts the long CTAs before the short ones fill in behind them
+    // ws: the members' weights (in gl's order), for the persistent shallow member (below)
     void push_group(const char * name, const std::vector<GemmLaunch> & gl, const std::vector<int> & zs, bool partial, int s,
-                    double flops, const std::string & shape) {
+                    double flops, const std::string & shape, const std::vector<const Lin *> * ws = nullptr) {
         std::vector<int> ord(gl.size());
         for (size_t q = 0; q < ord.size(); ++q) ord[q] = (int) q;
         std::stable_sort(ord.begin(), ord.end(),
@@ -886,6 +887,30 @@ struct Plan {
         GroupLaunch G;
         G.bn = gl[0].bn; G.epi = gl[0].epi; G.split = gl[0].split; G.ab_bf16 = gl[0].ab_bf16; G.smem = gl[0].smem;
         G.cluster = partial ? 1 : s;
+        // When the deep members leave some SMs free and the shallowest member has more CTAs than
+        // that, the shallowest member runs as persistent tile lists on exactly the free SMs (the
+        // joint blocks' text-stream w1/w3: 64 tiles of 16 K blocks beside 128 tiles of 48), in
+        // narrower tiles so that the lists come out even (gemm_tile_list).
+        int pq = -1, pctas = 0, ptiles = 0;
+        CUtensorMap pmap{};
+        const int pbn = gemm_group_persist_bn(G.bn, G.epi, G.split);
+        if (ws && pbn && G.cluster == 1 && !partial && gl.size() >= 2 && !std::getenv("TSN_NO_PERSIST_GROUP")) {
+            int sms = 148;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m.dev->ordinal);
+            const int last = ord.back();
+            int deep = 0;
+            for (int q : ord)
+                if (q != last) deep += (int) (gl[q].grid.x * gl[q].grid.y) * zs[q];
+            const int free = sms - deep, last_ctas = (int) (gl[last].grid.x * gl[last].grid.y) * zs[last];
+            const Lin & W = *(*ws)[last];
+            if (2 * gl[last].args.kb_per_split <= gl[ord[0]].args.kb_per_split && zs[last] == 1 && free >= 4 &&
+                last_ctas > free && make_w_map(&pmap, W.w, (uint64_t) W.taps * W.K_in, W.N, pbn, m.bf16)) {
+                pq = last;
+                pctas = free;
+                ptiles = (int) gl[last].grid.x * ((W.N + pbn - 1) / pbn);
+                G.smem = gemm_group_persist_smem_bytes(G.bn, G.epi, G.split);
+            }
+        }
         int end = 0, n = 0;
         std::string kbs;
         const bool tma_out = G.epi == EPI_F32 && G.cluster == 1 && !std::getenv("TSN_NO_TMA_OUT");
@@ -893,7 +918,7 @@ struct Plan {
             const GemmLaunch & g = gl[q];
             G.maps.a[n] = g.ta;
             G.maps.a2[n] = g.split ? g.ta2 : g.ta;
-            G.maps.b[n] = g.tb;
+            G.maps.b[n] = q == pq ? pmap : g.tb;
             G.args.p[n] = g.args;
             G.args.p[n].tma_out = 0;
             const GemmArgs & ga = g.args;
@@ -904,15 +929,24 @@ struct Plan {
                 G.args.p[n].tma_out = 1;
             G.args.slices[n] = zs[q];
             G.args.m_tiles[n] = (int) g.grid.x;
-            end += (int) (g.grid.x * g.grid.y) * zs[q];
+            if (q == pq) {
+                G.args.persist_q = n;
+                G.args.persist_ctas = pctas;
+                G.args.persist_tiles = ptiles;
+                end += pctas;
+            } else {
+                end += (int) (g.grid.x * g.grid.y) * zs[q];
+            }
             G.args.cta_end[n] = end;
             kbs += (n ? "/" : "") + std::to_string(g.args.k_blocks) + "x" + std::to_string(zs[q]);
             ++n;
         }
         G.args.n = n;
-        char d[200];
-        snprintf(d, sizeof d, "bn=%d split=%d ksplit=%d %s group=%d ctas=%d kb=%s smem=%zu", G.bn, (int) G.split, s,
-                 partial ? "partial" : "cluster", n, end, kbs.c_str(), G.smem);
+        char d[256];
+        char pd[64] = "";
+        if (pq >= 0) snprintf(pd, sizeof pd, " persist=%dx%d/%d", pctas, pbn, ptiles);
+        snprintf(d, sizeof d, "bn=%d split=%d ksplit=%d %s group=%d ctas=%d kb=%s smem=%zu%s", G.bn, (int) G.split, s,
+                 partial ? "partial" : "cluster", n, end, kbs.c_str(), G.smem, pd);
         Op op{[G](cudaStream_t st) { return launch_gemm_group(G, st); }, 0, flops, name, d};
         op.gemm_id = m.gemm_seq++;
         op.tile_bn = G.bn;
@@ -1024,7 +1058,9 @@ struct Plan {
             GemmArgs & a = gl[q].args;
             a.out = st[q].h; a.ldo = F; a.out_bs = (long long) st[q].rows * F;
         }
-        push_group("ffn_w13", gl, zs, false, s, flops, shape);
+        std::vector<const Lin *> ws;
+        for (const Strm & x : st) ws.push_back(&x.b->w13);
+        push_group("ffn_w13", gl, zs, false, s, flops, shape, &ws);
         return gate_group("ffn_w2", st, true, 5);
     }
     // apply a pending gated update to x without normalising (taps read x between blocks)
