@@ -429,9 +429,13 @@ void Model::release_activations() {
 // reference timestep embedding on the host (src/dit_fwd.cpp:112-119)
 void Model::temb_host(float t, float * out) const {
     const int H_ = (int) g.H, half = H_ / 2;
-    const float fscale_t = 10000.0f / g.t_max_period;
+    if ((int) temb_fr.size() != half) {   // the frequencies depend on the geometry only: computed once
+        const float fscale_t = 10000.0f / g.t_max_period;
+        temb_fr.resize(half);
+        for (int kk = 0; kk < half; ++kk) temb_fr[kk] = fscale_t * powf(10000.0f, -2.0f * kk / (float) H_);
+    }
     for (int kk = 0; kk < half; ++kk) {
-        float fr = fscale_t * powf(10000.0f, -2.0f * kk / (float) H_);
+        const float fr = temb_fr[kk];
         out[kk] = cosf(t * fr);
         out[half + kk] = sinf(t * fr);
     }

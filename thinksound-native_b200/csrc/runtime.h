@@ -161,6 +161,7 @@ struct Model {
     int timeline(std::vector<double> & rows);
     int set_time(float t, float dt);
     void temb_host(float t, float * out) const;
+    mutable std::vector<float> temb_fr;   // temb_host's frequencies (the geometry's, computed on first use)
     void release_activations();
 };
 
