@@ -10,9 +10,9 @@
 //           then RMSNorm (T5) or LayerNorm (CLIP) written as the next GEMM's split f16 operand
 //   qkv     one GEMM over [q | k | v] weights concatenated at load, whose epilogue scatters q, k, v
 //           head-major as split f16 (EPI_QKV without the DiT's per-head norm and RoPE)
-//   attn    the flash-style mma.sync attention (attn_kernel) with an additive logit-bias table:
-//           T5's relative-position bias and pad mask, or CLIP's causal + EOT mask, built once per
-//           encode from the token ids; no score tensor in memory
+//   attn    the tcgen05 short-sequence attention (attn_short_kernel) with an additive logit-bias
+//           table: T5's relative-position bias and pad mask, or CLIP's causal + EOT mask, built once
+//           per encode from the token ids; no score tensor in memory
 //   o/out   GEMM whose K slices write partial tiles; the next norm adds them (and the bias)
 //   norm
 //   up      T5: wi_0 / wi_1 interleaved in 32-row groups, one GEMM whose epilogue applies

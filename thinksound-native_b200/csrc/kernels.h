@@ -122,7 +122,7 @@ struct AttnArgs {
     int * err;                                               // device error word (attn_tc_kernel)
     // optional additive logit bias in log2 units, [B][NH][S][S_pad] (key fastest; -inf masks a key):
     // the text encoders' T5 relative-position bias and pad mask, or CLIP's causal + EOT mask
-    // (attn_kernel only)
+    // (attn_short_kernel and attn_kernel)
     const float * lbias;
 };
 cudaError_t configure_attention();
