@@ -315,14 +315,15 @@ __device__ __forceinline__ void adaln_row(const AdaLnArgs & a, const int row, un
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         const int c = (i * TPR + tid) * 4;
-        v[i] = *(const float4 *) (xr + c);
+        v[i] = a.x_zero ? make_float4(0.f, 0.f, 0.f, 0.f) : *(const float4 *) (xr + c);
         if (a.out) {
             sh[i] = __ldg((const float4 *) (m + c));
             sc[i] = __ldg((const float4 *) (m + a.H + c));
         }
     }
     if (a.part) {
-        const float * g = a.gmod + (long long) b * a.gmod_bs + (a.gper_row ? (long long) t * a.gmod_ld : 0) + a.goff;
+        const float * g = a.gmod ? a.gmod + (long long) b * a.gmod_bs + (a.gper_row ? (long long) t * a.gmod_ld : 0) + a.goff
+                                 : nullptr;
         const float * p = a.part + (long long) b * a.x_bs + (long long) t * a.H;
         float4 acc[NV], pz[NV][MAX_PARTS - 1], gg[NV], bb[NV];
 #pragma unroll
@@ -332,7 +333,7 @@ __device__ __forceinline__ void adaln_row(const AdaLnArgs & a, const int row, un
 #pragma unroll
             for (int z = 1; z < MAX_PARTS; ++z)
                 if (z < a.nsplit) pz[i][z - 1] = __ldcg((const float4 *) (p + z * a.part_stride + c));
-            gg[i] = __ldg((const float4 *) (g + c));
+            gg[i] = g ? __ldg((const float4 *) (g + c)) : make_float4(1.f, 1.f, 1.f, 1.f);
             bb[i] = a.pbias ? __ldg((const float4 *) (a.pbias + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll

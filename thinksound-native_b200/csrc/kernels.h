@@ -152,7 +152,8 @@ struct AdaLnArgs {
     // applied to x first and written back: x += gate * (part[0] + ... + part[nsplit-1] + pbias).
     const float * part; long long part_stride; int nsplit;   // part[z][B][rows][H]; null: none
     const float * pbias;                                     // [H]
-    const float * gmod; long long gmod_bs, gmod_ld; int gper_row, goff;   // gate rows, like mod
+    const float * gmod; long long gmod_bs, gmod_ld; int gper_row, goff;   // gate rows, like mod; null: gate 1
+    int x_zero;                                              // the update starts the stream: x's old contents unused
 };
 cudaError_t launch_adaln(const AdaLnArgs & a, cudaStream_t s);
 // several streams' adaLNs (same H) in one launch; stream q owns blocks [end[q-1], end[q])

@@ -567,7 +567,8 @@ std::string shape_key(int rows, int N, int K_in, int taps, int epi, bool split, 
 struct Pending {
     const float * part; long long stride; int nsplit;
     const float * bias;
-    const float * gmod; long long gmod_ld, gmod_bs; int gper_row, goff;
+    const float * gmod; long long gmod_ld, gmod_bs; int gper_row, goff;   // gate rows; null: gate 1
+    int x_zero = 0;                                                        // the update starts the stream
 };
 
 struct Plan {
@@ -776,8 +777,10 @@ struct Plan {
     // res += gate * (A.W^T + bias) (linear1/ffn.w2 + gate_add, src/dit_fwd.cpp:61-79): the GEMM
     // writes its split-K partial sums into the stream's workspace, and the next adaLN of `res`
     // (or resolve()) adds them, applies bias and gate, and updates res in place.
+    // mod null: no gate (1); x_zero: the update starts res (its old contents are not read)
     int gate(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * res,
-             const float * mod, int per_row, long long mod_ld, long long mod_bs, int gate_idx, bool plain = false) {
+             const float * mod, int per_row, long long mod_ld, long long mod_bs, int gate_idx, bool plain = false,
+             bool x_zero = false) {
         GemmLaunch g;
         int rc = gemm(name, A, K_in, rows, W, pad, EPI_F32, g, plain, true);
         if (rc) return rc;
@@ -791,7 +794,7 @@ struct Plan {
         ops.back().part_bytes = (double) g.args.part_stride * 4;
         Pending & pd = pend[res];
         pd = Pending{ws, g.args.part_stride, (int) g.grid.z, W.b, mod, per_row ? mod_ld : 0, mod_bs, per_row,
-                     gate_idx * (int) H};
+                     gate_idx * (int) H, x_zero ? 1 : 0};
         return TSN_OK;
     }
     // ---------------------------------------------------------------- grouped launches
@@ -1092,6 +1095,7 @@ struct Plan {
             const Pending & pd = it->second;
             a.part = pd.part; a.part_stride = pd.stride; a.nsplit = pd.nsplit; a.pbias = pd.bias;
             a.gmod = pd.gmod; a.gmod_ld = pd.gmod_ld; a.gmod_bs = pd.gmod_bs; a.gper_row = pd.gper_row; a.goff = pd.goff;
+            a.x_zero = pd.x_zero;
             pend.erase(it);
         }
         return a;
@@ -1261,8 +1265,13 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // audio_input_proj: conv k3 + silu, convmlp                   src/dit_fwd.cpp:143-149
     if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H, (long long) B * T * H))) return rc;
     if ((rc = p.out_f16("audio_in.w13", EPI_SWIGLU, xn_l, H, T, ain13, 1, h_l, F))) return rc;
-    if ((rc = p.out_f32("audio_in.w2", h_l, F, T, ain2, 1, lat, H, true))) return rc;
-    if (tp) p.tap("x_in", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    // the latent stream's starting value as K-slice partial tiles that the first joint adaLN adds
+    // (no gate, nothing to add them to)
+    if ((rc = p.gate("audio_in.w2", h_l, F, T, ain2, 1, lat, nullptr, 0, 0, 0, 0, true, true))) return rc;
+    if (tp) {
+        p.resolve(lat, T);
+        p.tap("x_in", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
+    }
     // joint blocks                                                src/dit_fwd.cpp:180-257
     // The latent, clip and text streams of a joint block meet only at attention: the clip and text
     // chains run on their own CUDA streams (1, 2) and join the latent stream (0) through events.
