@@ -739,17 +739,41 @@ cudaError_t launch_cond(const CondArgs & a, cudaStream_t s) {
 }
 
 // =============================================================================== sampler
-__global__ void cfg_euler_kernel(const float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
-                                 const int * step, float dt_const) {
+// value e of the flow from fs.S partial slices (slice z at parts + z * stride) and the bias of
+// channel e % C, summed in slice order
+struct FlowParts { const float * parts; long long stride; int S; const float * bias; int C; };
+__device__ __forceinline__ float flow_at(const FlowParts & fs, long long e) {
+    float v = fs.parts[e];
+    for (int z = 1; z < fs.S; ++z) v += fs.parts[z * fs.stride + e];
+    return fs.bias ? v + fs.bias[e % fs.C] : v;
+}
+__global__ void cfg_euler_kernel(float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
+                                 const int * step, float dt_const, const FlowParts fs) {
     pdl_trigger();
     pdl_wait();
     const float dt = dt_table ? dt_table[*step] : dt_const;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n * gens; i += gridDim.x * blockDim.x) {
         const int g = i / n, j = i % n;
-        const float fc = flow2[(2LL * g) * n + j], fu = flow2[(2LL * g + 1) * n + j];
+        const long long ec = (2LL * g) * n + j, eu = (2LL * g + 1) * n + j;
+        float fc, fu;
+        if (fs.parts) {   // the final conv's partial tiles: the flow is formed (and kept) here
+            fc = flow_at(fs, ec);
+            fu = flow_at(fs, eu);
+            flow2[ec] = fc;
+            flow2[eu] = fu;
+        } else {
+            fc = flow2[ec];
+            fu = flow2[eu];
+        }
         const float v = __fadd_rn(fu, __fmul_rn(__fsub_rn(fc, fu), cfg));
         x[i] = __fadd_rn(x[i], __fmul_rn(dt, v));
     }
+}
+__global__ void flow_sum_kernel(float * flow, long long n, const FlowParts fs) {
+    pdl_trigger();
+    pdl_wait();
+    for (long long i = blockIdx.x * (long long) blockDim.x + threadIdx.x; i < n; i += (long long) gridDim.x * blockDim.x)
+        flow[i] = flow_at(fs, i);
 }
 __global__ void step_advance_kernel(int * step) {
     pdl_trigger();
@@ -758,9 +782,18 @@ __global__ void step_advance_kernel(int * step) {
 }
 
 cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
-                             const int * step, float dt_const, cudaStream_t s) {
-    return launch_ex(cfg_euler_kernel, dim3((n * gens + 255) / 256), dim3(256), 0, s, 1u, flow2, x, n, gens, cfg, dt_table,
-                     step, dt_const);
+                             const int * step, float dt_const, cudaStream_t s, const float * parts, long long part_stride,
+                             int nparts, const float * bias, int C) {
+    if (parts && (nparts < 1 || C < 1)) return cudaErrorInvalidValue;
+    const FlowParts fs{parts, part_stride, nparts, bias, C};
+    return launch_ex(cfg_euler_kernel, dim3((n * gens + 255) / 256), dim3(256), 0, s, 1u, (float *) flow2, x, n, gens, cfg,
+                     dt_table, step, dt_const, fs);
+}
+cudaError_t launch_flow_sum(float * flow, long long n, const float * parts, long long part_stride, int nparts,
+                            const float * bias, int C, cudaStream_t s) {
+    if (!parts || nparts < 1 || C < 1 || n < 1) return cudaErrorInvalidValue;
+    const FlowParts fs{parts, part_stride, nparts, bias, C};
+    return launch_ex(flow_sum_kernel, dim3((unsigned) ((n + 255) / 256)), dim3(256), 0, s, 1u, flow, n, fs);
 }
 cudaError_t launch_step_advance(int * step, cudaStream_t s) {
     return launch_ex(step_advance_kernel, dim3(1), dim3(1), 0, s, 1u, step);

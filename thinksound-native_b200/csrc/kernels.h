@@ -216,9 +216,15 @@ struct CondArgs {
 cudaError_t launch_cond(const CondArgs & a, cudaStream_t s);
 
 // ---- x += dt * (fu + cfg * (fc - fu)) (src/pipeline.cpp:148, shaders/ops_conv.metal:194-201) ----
-// x[g] += dt (fu + cfg (fc - fu)) for g < gens, with fc = flow[2g], fu = flow[2g + 1], n floats each
+// x[g] += dt (fu + cfg (fc - fu)) for g < gens, with fc = flow[2g], fu = flow[2g + 1], n floats each.
+// With parts: the flow is first formed from nparts partial slices (slice z at parts + z *
+// part_stride, the same layout as flow) plus bias[e % C], summed in slice order, and written to flow.
 cudaError_t launch_cfg_euler(const float * flow2, float * x, int n, int gens, float cfg, const float * dt_table,
-                             const int * step, float dt_const, cudaStream_t s);
+                             const int * step, float dt_const, cudaStream_t s, const float * parts = nullptr,
+                             long long part_stride = 0, int nparts = 0, const float * bias = nullptr, int C = 0);
+// flow[e] = parts[0][e] + ... + parts[nparts-1][e] + bias[e % C] for e < n (the final conv's K slices)
+cudaError_t launch_flow_sum(float * flow, long long n, const float * parts, long long part_stride, int nparts,
+                            const float * bias, int C, cudaStream_t s);
 cudaError_t launch_step_advance(int * step, cudaStream_t s);
 // failure-path self-test: one thread waits on an mbarrier that nothing arrives on, bounded by
 // limit_ns; records DEV_TIMEOUT_FULL in err when the bound runs out

@@ -777,6 +777,19 @@ struct Plan {
     // res += gate * (A.W^T + bias) (linear1/ffn.w2 + gate_add, src/dit_fwd.cpp:61-79): the GEMM
     // writes its split-K partial sums into the stream's workspace, and the next adaLN of `res`
     // (or resolve()) adds them, applies bias and gate, and updates res in place.
+    // out[z] = K slice z of A.W^T (no bias) as partial tiles [z][B][rows][N] in ws; nz: the slice count
+    int partial_out(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * ws, int & nz) {
+        GemmLaunch g;
+        int rc = gemm(name, A, K_in, rows, W, pad, EPI_F32, g, false, true);
+        if (rc) return rc;
+        g.args.out = ws; g.args.ldo = W.N; g.args.out_bs = (long long) rows * W.N;
+        g.args.part_stride = (long long) m.B * rows * W.N;
+        g.args.bias = nullptr;
+        if ((rc = bind_tma_out(name, g, rows))) return rc;
+        push(name, g, fl(m.B, rows, W));
+        nz = (int) g.grid.z;
+        return TSN_OK;
+    }
     // mod null: no gate (1); x_zero: the update starts res (its old contents are not read)
     int gate(const char * name, const void * A, int K_in, int rows, const Lin & W, int pad, float * res,
              const float * mod, int per_row, long long mod_ld, long long mod_bs, int gate_idx, bool plain = false,
@@ -1415,15 +1428,27 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
         p.tap("final_fx", xn_l, (size_t) B * T * H * 2, cvt_f16_arm((size_t) T * H));
         p.tap2d("final_mod", mf, (size_t) 2 * H * 4, (size_t) NA * 4, (size_t) B * T, cvt_f32_arm((size_t) T * 2 * H));
     }
-    if ((rc = p.out_f32("final_conv", xn_l, H, T, fconv, 3, flow, L))) return rc;
+    // the final conv's K slices as partial tiles in the latent workspace (free again: the final adaLN
+    // took the last block's); the sampler update adds them, or flow_sum does when the flow is the output
+    int fz = 0;
+    if ((rc = p.partial_out("final_conv", xn_l, H, T, fconv, 3, part_l, fz))) return rc;
+    const long long fstride = (long long) B * T * L;
+    const float * fparts = part_l, * fbias = fconv.b;
+    if (mode != 1) {
+        float * fl = flow;
+        ops.push_back(Op{[fl, fstride, fparts, fz, fbias, L](cudaStream_t s) {
+                             return launch_flow_sum(fl, fstride, fparts, fstride, fz, fbias, L, s);
+                         },
+                         2, 0, "flow_sum"});
+    }
     if (tp) p.tap("flow", flow, (size_t) B * T * L * 4, cvt_f32_arm((size_t) T * L));
     if (mode == 1) {   // sampler update (src/pipeline.cpp:148) and schedule advance
         float * fl = flow, * xx = x;
         const float * dtt = dt_tab;
         int * st = step;
         const int n = T * L, gens = G;
-        ops.push_back(Op{[fl, xx, n, gens, cfg, dtt, st](cudaStream_t s) {
-                             return launch_cfg_euler(fl, xx, n, gens, cfg, dtt, st, 0.0f, s);
+        ops.push_back(Op{[fl, xx, n, gens, cfg, dtt, st, fparts, fstride, fz, fbias, L](cudaStream_t s) {
+                             return launch_cfg_euler(fl, xx, n, gens, cfg, dtt, st, 0.0f, s, fparts, fstride, fz, fbias, L);
                          },
                          2, 0, "cfg_euler"});
         ops.push_back(Op{[st](cudaStream_t s) { return launch_step_advance(st, s); }, 2, 0, "step_advance"});
