@@ -690,7 +690,9 @@ cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int 
 // =============================================================================== conditioning
 __device__ __forceinline__ float silu_d(float v) { return v / (1.0f + expf(-v)); }
 
-__global__ void cond_kernel(const CondArgs a) {
+// part 0: everything; 1: the t-dependent conditioning (global_c, extended_c); 2: the rest (the clip
+// and text streams' restart, the latent's split operand)
+__global__ void cond_kernel(const CondArgs a, int part) {
     pdl_trigger();
     pdl_wait();
     const long long nA = (long long) a.B * a.H;
@@ -698,7 +700,8 @@ __global__ void cond_kernel(const CondArgs a) {
     const long long nC = nB + (long long) a.B * a.C * a.H;
     const long long nD = nC + (long long) a.B * a.TS * a.H;
     const long long nE = nD + (long long) a.B * a.T * a.L;
-    for (long long i = blockIdx.x * (long long) blockDim.x + threadIdx.x; i < nE; i += (long long) gridDim.x * blockDim.x) {
+    const long long i0 = part == 2 ? nB : 0, i1 = part == 1 ? nB : nE;
+    for (long long i = i0 + blockIdx.x * (long long) blockDim.x + threadIdx.x; i < i1; i += (long long) gridDim.x * blockDim.x) {
         if (i < nA) {
             const int b = (int) (i / a.H), c = (int) (i % a.H);
             const float gc = a.gcmlp[(long long) b * a.H + c] + a.te[c];           // dit_fwd.cpp:131
@@ -734,8 +737,9 @@ __global__ void cond_kernel(const CondArgs a) {
     }
 }
 
-cudaError_t launch_cond(const CondArgs & a, cudaStream_t s) {
-    return launch_ex(cond_kernel, dim3(592), dim3(256), 0, s, 1u, a);
+cudaError_t launch_cond(const CondArgs & a, cudaStream_t s, int part) {
+    if (part < 0 || part > 2) return cudaErrorInvalidValue;
+    return launch_ex(cond_kernel, dim3(592), dim3(256), 0, s, 1u, a, part);
 }
 
 // =============================================================================== sampler

@@ -213,7 +213,8 @@ struct CondArgs {
     long long extc_lo, x_lo;     // element offsets of the lo halves of extc16 and x16
     int A;                       // CFG arms per generation
 };
-cudaError_t launch_cond(const CondArgs & a, cudaStream_t s);
+// part 0: all of it; 1: global_c / extended_c (needs t_emb); 2: the clip/text restart and x's split operand
+cudaError_t launch_cond(const CondArgs & a, cudaStream_t s, int part = 0);
 
 // ---- x += dt * (fu + cfg * (fc - fu)) (src/pipeline.cpp:148, shaders/ops_conv.metal:194-201) ----
 // x[g] += dt (fu + cfg (fc - fu)) for g < gens, with fc = flow[2g], fu = flow[2g + 1], n floats each.

@@ -1250,7 +1250,23 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     CondArgs ca{te, gcmlp, sync_gather, clip_pp, text_pp, x, gc_silu, extc16, clip_s, text_s, x16,
                 tp ? tap_gc : nullptr, tp ? tap_extc : nullptr, B, T, C, TS, H, L,
                 (long long) B * T * H, (long long) B * T * L, A};
-    ops.push_back(Op{[ca](cudaStream_t s) { return launch_cond(ca, s); }, 2, 0, "cond"});
+    // The t-independent part of cond (the clip/text streams' restart, x's split operand) and
+    // audio_input_proj depend on x only: they run on a side stream beside the t-embedding chain
+    // (latency-bound, a few SMs) and join before the first joint block. TSN_PROLOGUE_SERIAL=1: in line.
+    const bool pside = std::getenv("TSN_PROLOGUE_SERIAL") == nullptr;
+    int ev_audio = -1;
+    if (pside) {
+        const int e0 = p.record();
+        p.cur = 1;
+        p.wait(e0);
+        { Op o{[ca](cudaStream_t s) { return launch_cond(ca, s, 2); }, 2, 0, "cond_x"}; p.add(o); }
+        if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H, (long long) B * T * H))) return rc;
+        if ((rc = p.out_f16("audio_in.w13", EPI_SWIGLU, xn_l, H, T, ain13, 1, h_l, F))) return rc;
+        if ((rc = p.gate("audio_in.w2", h_l, F, T, ain2, 1, lat, nullptr, 0, 0, 0, 0, true, true))) return rc;
+        ev_audio = p.record();
+        p.cur = 0;
+    }
+    ops.push_back(Op{[ca, pside](cudaStream_t s) { return launch_cond(ca, s, pside ? 1 : 0); }, 2, 0, "cond"});
     // the clip/text modulations of every joint block (HBM-bound GEMVs, ~160 MB of weights at the
     // 8 s geometry) in one launch with the GPU to itself: beside the modulation GEMM they starved
     // for L2-to-SM bandwidth and held SMs that the next GEMM's CTAs needed
@@ -1276,11 +1292,15 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // joint blocks, fused blocks and the final layer      src/dit_fwd.cpp:186-189, 271-274, 288-291
     if ((rc = p.out_f32("latent_adaln_all", extc16, H, T, mod_all, 0, modl, (int) NA))) return rc;
     // audio_input_proj: conv k3 + silu, convmlp                   src/dit_fwd.cpp:143-149
-    if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H, (long long) B * T * H))) return rc;
-    if ((rc = p.out_f16("audio_in.w13", EPI_SWIGLU, xn_l, H, T, ain13, 1, h_l, F))) return rc;
-    // the latent stream's starting value as K-slice partial tiles that the first joint adaLN adds
-    // (no gate, nothing to add them to)
-    if ((rc = p.gate("audio_in.w2", h_l, F, T, ain2, 1, lat, nullptr, 0, 0, 0, 0, true, true))) return rc;
+    if (!pside) {
+        if ((rc = p.out_f16("audio_in.0", EPI_F16_SILU, x16, L, T, ain0, 1, xn_l, H, (long long) B * T * H))) return rc;
+        if ((rc = p.out_f16("audio_in.w13", EPI_SWIGLU, xn_l, H, T, ain13, 1, h_l, F))) return rc;
+        // the latent stream's starting value as K-slice partial tiles that the first joint adaLN adds
+        // (no gate, nothing to add them to)
+        if ((rc = p.gate("audio_in.w2", h_l, F, T, ain2, 1, lat, nullptr, 0, 0, 0, 0, true, true))) return rc;
+    } else {
+        p.wait(ev_audio);
+    }
     if (tp) {
         p.resolve(lat, T);
         p.tap("x_in", lat, (size_t) B * T * H * 4, cvt_f32_arm((size_t) T * H));
