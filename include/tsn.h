@@ -76,6 +76,15 @@ double tsn_last_gpu_ms(tsn_device * dev);
  * way every pipeline wait of this library is bounded. Expected result: TSN_ERR_TIMEOUT, with the
  * device still usable afterwards. */
 int tsn_selftest_device_timeout(tsn_device * dev, uint32_t limit_us);
+/* No counterpart in the reference (a test hook for the batched GEMV that carries the t-embedding
+ * and every clip/text modulation of a step; each job is one Runtime::gemv, src/net.mm:51-56).
+ * njobs jobs (1..64), job q: Y_q[b][n] = act(sum_k W_q[n][k] x[b][k] + bias_q[n]) for b < nb,
+ * n < N[q]; act 0 none, 1 SiLU. W: the jobs' f16 rows of K back to back (job q from row sum N[<q]);
+ * bias: f32, laid out the same way, or null; x: [nb][K] f32; Y: [nb][sum N] f32, job q's arm b at
+ * b * sum N + sum N[<q]. K a multiple of 8 up to 1024; nb <= nb_cap <= 8 (the kernel instance's arm
+ * capacity); blocks: the grid's cap (>= 1; results do not depend on it). Synchronises. */
+int tsn_selftest_gemv_jobs(tsn_device * dev, const void * W, const void * bias, const void * x, void * Y,
+                           const uint32_t * N, int njobs, uint32_t K, int nb, int nb_cap, int act, int blocks);
 
 /* ------------------------------------------------------------------ runtime face (src/net.h) */
 /* Runtime::gemm (src/net.h:23-24): Y[M,N] = X[M,K]·W[N,K]^T (+bias), X/Y f32, W f16 (wf16=1) or

@@ -128,3 +128,41 @@ def test_gemv_runtime_face(dev, N, K, bias, wf16):
     ref = w.astype(np.float64) @ x.astype(np.float64) + (b if bias else 0)
     assert rel_l2(y[:N], ref) < 1e-5     # f32 sums over K <= 2048
     assert np.array_equal(outs[0][:N], outs[1][:N])
+
+
+GEMV_JOB_CASES = [  # (Ns, K, nb, nb_cap, act): the step's batched GEMV (t-embedding, clip/text modulations)
+    ((6144, 1000, 7, 1), 1024, 2, 2, 0),       # ragged jobs below the largest N, odd N, one-row job
+    ((333, 64, 1023), 64, 1, 1, 1),            # short rows, odd last slots, SiLU
+    ((5, 6144, 17), 200, 3, 4, 0),             # three arms in the four-arm instance, K not a multiple of 128
+    ((1024, 255, 999, 8), 1024, 8, 8, 0),      # eight arms (eight generations in one batch)
+    ((7,), 8, 5, 8, 1),                        # the smallest K
+    ((3,) * 20, 128, 2, 2, 0),                 # more jobs than one launch carries
+]
+
+
+@pytest.mark.parametrize("Ns,K,nb,nb_cap,act", GEMV_JOB_CASES)
+def test_gemv_jobs_ragged_vs_f64(dev, Ns, K, nb, nb_cap, act):
+    """gemv_kernel over several jobs of different row counts (src/net.mm:51-56 per job): every row
+    within f32 summation error of float64 and, since a row's lane sums and butterfly do not depend on
+    which warp or block takes its slot, bit-identical for grids of 148, 37 and 1 blocks."""
+    rng = np.random.default_rng(29)
+    total = int(sum(Ns))
+    w = (rng.standard_normal((total, K), dtype=np.float32) * 0.03).astype(np.float16)
+    b = rng.standard_normal(total, dtype=np.float32)
+    x = rng.standard_normal((nb, K), dtype=np.float32)
+    W = torch.from_numpy(w.view(np.uint16).astype(np.int16)).cuda()
+    bd, xd = torch.from_numpy(b).cuda(), torch.from_numpy(x).cuda()
+    Y = torch.empty(nb * total + 8, dtype=torch.float32, device="cuda")
+    outs = []
+    for blocks in (148, 37, 1):
+        Y.fill_(float("nan"))
+        dev.selftest_gemv_jobs(W, bd, xd, Y, list(Ns), K, nb, nb_cap, act, blocks)
+        outs.append(Y.cpu().numpy())
+    y = outs[0]
+    assert np.isnan(y[nb * total:]).all(), "wrote past the output"
+    ref = x.astype(np.float64) @ w.astype(np.float64).T + b
+    if act:
+        ref = ref / (1.0 + np.exp(-ref))
+    assert rel_l2(y[:nb * total].reshape(nb, total), ref) < 1e-5
+    for o in outs[1:]:
+        assert np.array_equal(o[:nb * total], y[:nb * total]), "result depends on the grid"

@@ -204,6 +204,28 @@ int tsn_selftest_device_timeout(tsn_device * dev, uint32_t limit_us) {
     return c.sync();
 }
 
+int tsn_selftest_gemv_jobs(tsn_device * dev, const void * W, const void * bias, const void * x, void * Y,
+                           const uint32_t * N, int njobs, uint32_t K, int nb, int nb_cap, int act, int blocks) {
+    if (!dev || !W || !x || !Y || !N) return fail(TSN_ERR_ARG, "null argument");
+    if (njobs < 1 || njobs > 64 || blocks < 1 || act < 0 || act > 1) return fail(TSN_ERR_ARG, "bad job count, blocks or act");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    DeviceCtx & c = dev->ctx;
+    TRY(c.activate());
+    long long total = 0;
+    uint32_t max_n = 0;
+    for (int q = 0; q < njobs; ++q) { total += N[q]; max_n = std::max(max_n, N[q]); }
+    std::vector<GemvJob> jobs((size_t) njobs);
+    long long row = 0;
+    for (int q = 0; q < njobs; ++q) {
+        jobs[(size_t) q] = GemvJob{(const __half *) W + row * K, bias ? (const float *) bias + row : nullptr,
+                                   (const float *) x, (long long) K, nullptr, 0, (float *) Y + row, total,
+                                   (int) N[q], (int) K, nb, act};
+        row += N[q];
+    }
+    CKR(launch_gemv(jobs.data(), njobs, (int) max_n, nb_cap, blocks, 0, c.d_err, c.stream));
+    return c.sync();
+}
+
 // ------------------------------------------------------------------------------- runtime face
 #define RT_BEGIN                                                         \
     if (!dev) return fail(TSN_ERR_ARG, "null device");                  \

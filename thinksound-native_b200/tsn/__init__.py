@@ -61,6 +61,9 @@ _SIGS = [
     ("tsn_exec_width", C.c_uint32, [C.c_void_p, C.c_char_p]),
     ("tsn_last_gpu_ms", C.c_double, [C.c_void_p]),
     ("tsn_selftest_device_timeout", C.c_int, [C.c_void_p, C.c_uint32]),
+    ("tsn_selftest_gemv_jobs", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.POINTER(C.c_uint32), C.c_int, C.c_uint32, C.c_int, C.c_int, C.c_int,
+                                         C.c_int]),
     ("tsn_gemm", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                            C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
     ("tsn_gemm_noalloc", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -221,6 +224,12 @@ class Device:
         """Run the bounded-wait self-test (a wait nothing completes); raises TsnError (TSN_ERR_TIMEOUT
         expected) unless the wait somehow completed."""
         check(lib().tsn_selftest_device_timeout(self.h, limit_us))
+
+    def selftest_gemv_jobs(self, W, bias, x, Y, Ns, K, nb, nb_cap, act=0, blocks=148):
+        """The step's batched GEMV over several jobs (f16 rows back to back, Y [nb][sum Ns]); synchronises."""
+        arr = (C.c_uint32 * len(Ns))(*Ns)
+        check(lib().tsn_selftest_gemv_jobs(self.h, _p(W), _p(bias), _p(x), _p(Y), arr, len(Ns), K, nb, nb_cap,
+                                           act, blocks))
 
     # --- net.h Runtime
     def gemm(self, wf16, W, X, Y, bias, M, N, K, ldx=0, ldw=0, ldy=0):
