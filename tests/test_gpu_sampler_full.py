@@ -147,3 +147,21 @@ def test_default_forward_bit_identical_across_processes(model, tmp_path):
         flows.append(np.fromfile(out, np.float32).reshape(2, T, 64))
     assert np.array_equal(flows[0], flows[1]), "two fresh processes disagree"
     assert np.array_equal(flows[0], here), "a fresh process disagrees with this one"
+
+
+def test_prologue_side_stream_same_bits_as_in_line(model, tmp_path):
+    """The step prologue's x-only work (cond's clip/text restart and x operand, audio_input_proj) runs
+    on a second stream beside the t-embedding chain by default; TSN_PROLOGUE_SERIAL=1 issues it in
+    line. The two schedules run the same kernels on the same data, so the flows must agree bit for bit."""
+    inp = make_inputs(T, C, TS, FULL["H"])
+    model.set_x(inp["x"])
+    here = np.zeros((2, T, 64), np.float32)
+    model.forward(0.5, here)
+    code = CHILD.format(pkg=os.path.join(ROOT, "thinksound-native_b200"), tests=os.path.dirname(__file__), T=T, C=C,
+                        TS=TS, full=FULL, seed=SEED)
+    out = str(tmp_path / "flow_serial.bin")
+    env = dict(os.environ, TSN_PROLOGUE_SERIAL="1")
+    r = subprocess.run([sys.executable, "-c", code, out], capture_output=True, text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    serial = np.fromfile(out, np.float32).reshape(2, T, 64)
+    assert np.array_equal(serial, here), "the in-line prologue gives other bits than the side-stream one"
