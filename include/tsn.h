@@ -76,6 +76,16 @@ double tsn_last_gpu_ms(tsn_device * dev);
  * way every pipeline wait of this library is bounded. Expected result: TSN_ERR_TIMEOUT, with the
  * device still usable afterwards. */
 int tsn_selftest_device_timeout(tsn_device * dev, uint32_t limit_us);
+/* No counterpart in the reference (a test hook for an experimental GEMM, not used by any model
+ * path). Y[M,N] = X·W^T (+bias) with X f32 [M][K], W f16 [N][K], Y f32 [M][N]. mode 0: X split into
+ * an f16 high part on the f16 tensor path and its residual, scaled by 2^12, as e4m3 against an e4m3
+ * copy of W scaled by 2^wexp (tile width bn 128, 176 or 256); mode 1: the library's split f16 GEMM
+ * (bn 128 or 256); mode + 4: the same without the L2-evicting write between launches. Operands are
+ * prepared outside the timing; each of reps launches (1..100) is timed alone, and *ms (may be null)
+ * receives the mean. K a multiple of 64.
+ * Allocates its scratch; synchronises. */
+int tsn_selftest_gemm_lo8(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias, uint32_t M,
+                          uint32_t N, uint32_t K, int wexp, int mode, int bn, int reps, float * ms);
 /* No counterpart in the reference (a test hook for the batched GEMV that carries the t-embedding
  * and every clip/text modulation of a step; each job is one Runtime::gemv, src/net.mm:51-56).
  * njobs jobs (1..64), job q: Y_q[b][n] = act(sum_k W_q[n][k] x[b][k] + bias_q[n]) for b < nb,

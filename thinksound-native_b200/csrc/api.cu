@@ -16,6 +16,8 @@ namespace tsn {
 const std::string & last_error();
 int gemm_noalloc(DeviceCtx & c, const void * W, const void * X, void * Y, const void * bias, uint32_t M, uint32_t N,
                  uint32_t K, uint32_t ldx, uint32_t ldw, uint32_t ldy);
+int selftest_gemm_lo8(DeviceCtx & c, const void * W, const void * X, void * Y, const void * bias, uint32_t M, uint32_t N,
+                      uint32_t K, int wexp, int mode, int bn, int reps, float * ms);
 }
 
 struct tsn_dit { Model m; };
@@ -202,6 +204,16 @@ int tsn_selftest_device_timeout(tsn_device * dev, uint32_t limit_us) {
     TRY(c.sync());    // a timeout reported below is this call's own
     CKR(launch_wait_selftest(c.d_err, 1000ull * limit_us, c.stream));
     return c.sync();
+}
+
+int tsn_selftest_gemm_lo8(tsn_device * dev, const void * W, const void * X, void * Y, const void * bias, uint32_t M,
+                          uint32_t N, uint32_t K, int wexp, int mode, int bn, int reps, float * ms) {
+    if (!dev) return fail(TSN_ERR_ARG, "null device");
+    std::lock_guard<std::mutex> lk(dev->ctx.mu);
+    DeviceCtx & c = dev->ctx;
+    TRY(c.activate());
+    TRY(c.sync());
+    return selftest_gemm_lo8(c, W, X, Y, bias, M, N, K, wexp, mode, bn, reps, ms);
 }
 
 int tsn_selftest_gemv_jobs(tsn_device * dev, const void * W, const void * bias, const void * x, void * Y,

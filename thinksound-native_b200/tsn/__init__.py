@@ -61,6 +61,9 @@ _SIGS = [
     ("tsn_exec_width", C.c_uint32, [C.c_void_p, C.c_char_p]),
     ("tsn_last_gpu_ms", C.c_double, [C.c_void_p]),
     ("tsn_selftest_device_timeout", C.c_int, [C.c_void_p, C.c_uint32]),
+    ("tsn_selftest_gemm_lo8", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint32,
+                                        C.c_uint32, C.c_uint32, C.c_int, C.c_int, C.c_int, C.c_int,
+                                        C.POINTER(C.c_float)]),
     ("tsn_selftest_gemv_jobs", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.POINTER(C.c_uint32), C.c_int, C.c_uint32, C.c_int, C.c_int, C.c_int,
                                          C.c_int]),
@@ -224,6 +227,14 @@ class Device:
         """Run the bounded-wait self-test (a wait nothing completes); raises TsnError (TSN_ERR_TIMEOUT
         expected) unless the wait somehow completed."""
         check(lib().tsn_selftest_device_timeout(self.h, limit_us))
+
+    def selftest_gemm_lo8(self, W, X, Y, bias, M, N, K, wexp, mode, bn, reps=1) -> float:
+        """Experimental GEMM with an e4m3 low-order product (mode 0) or the split f16 GEMM (mode 1);
+        returns the mean event-timed milliseconds of one launch."""
+        ms = C.c_float(0.0)
+        check(lib().tsn_selftest_gemm_lo8(self.h, _p(W), _p(X), _p(Y), _p(bias), M, N, K, wexp, mode, bn, reps,
+                                          C.byref(ms)))
+        return ms.value
 
     def selftest_gemv_jobs(self, W, bias, x, Y, Ns, K, nb, nb_cap, act=0, blocks=148):
         """The step's batched GEMV over several jobs (f16 rows back to back, Y [nb][sum Ns]); synchronises."""
