@@ -80,7 +80,8 @@ int tsn_selftest_device_timeout(tsn_device * dev, uint32_t limit_us);
  * path). Y[M,N] = X·W^T (+bias) with X f32 [M][K], W f16 [N][K], Y f32 [M][N]. mode 0: X split into
  * an f16 high part on the f16 tensor path and its residual, scaled by 2^12, as e4m3 against an e4m3
  * copy of W scaled by 2^wexp (tile width bn 128, 176 or 256); mode 1: the library's split f16 GEMM
- * (bn 128 or 256); mode + 4: the same without the L2-evicting write between launches. Operands are
+ * (bn 128 or 256); modes 2 and 3: a split f16 GEMM with K blocks of 64 or 32, so twice the stages
+ * (bn 128, 176 or 256); mode + 4: the same without the L2-evicting write between launches. Operands are
  * prepared outside the timing; each of reps launches (1..100) is timed alone, and *ms (may be null)
  * receives the mean. K a multiple of 64.
  * Allocates its scratch; synchronises. */

@@ -57,16 +57,18 @@ def test_lo8_gemm_vs_float64(dev, M, N, K, bn):
     assert e < 2e-5 and e < single / 8, (e, single)
 
 
-@pytest.mark.parametrize("bn", [128, 256])
-def test_split_f16_through_the_hook_vs_float64(dev, bn):
-    M, N, K = 376, 512, 1024
+@pytest.mark.parametrize("mode,bn,N", [(1, 128, 512), (1, 256, 512), (2, 176, 1000), (3, 176, 1000), (3, 256, 512),
+                                       (3, 128, 250)])
+def test_split_f16_through_the_hook_vs_float64(dev, mode, bn, N):
+    """mode 1: the library's split GEMM; modes 2 and 3: the same product with 64- and 32-wide K blocks."""
+    M, K = 376, 1024
     x, w, b, ref = operands(M, N, K)
     # the f16 residual itself rounds (and goes subnormal below 2^-14): ~4e-6 on these operands
-    assert rel_l2(run(dev, x, w, b, M, N, K, 1, bn), ref) < 2e-5
+    assert rel_l2(run(dev, x, w, b, M, N, K, mode, bn), ref) < 2e-5
 
 
 def test_lo8_gemm_timing_vs_split(dev):
-    """Times both forms at the shapes of the step's w1/w3 (376 x 8192 x 3072), modulation
+    """Times the forms at the shapes of the step's w1/w3 (376 x 8192 x 3072), modulation
     (376 x 131072 x 1024) and qkv (376 x 3072 x 1024) GEMMs: the mean of 10 launches, each timed alone
     after an L2-evicting write, and (+ "warm") without it. Prints the table; asserts only that every
     configuration ran."""
@@ -76,9 +78,10 @@ def test_lo8_gemm_timing_vs_split(dev):
         x = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda()
         w = torch.from_numpy((rng.standard_normal((N, K), dtype=np.float32) * 0.03).astype(np.float16).view(np.int16)).cuda()
         Y = torch.empty(M * N, dtype=torch.float32, device="cuda")
-        for mode, bn in [(1, 128), (1, 256), (0, 128), (0, 176), (0, 256), (5, 256), (4, 256), (4, 176)]:
+        for mode, bn in [(1, 128), (1, 256), (0, 128), (0, 176), (0, 256), (5, 256), (4, 256), (4, 176),
+                         (2, 176), (3, 176), (2, 256), (3, 256), (6, 176), (7, 176)]:
             ms = dev.selftest_gemm_lo8(w, x, Y, None, M, N, K, WEXP, mode, bn, reps=10)
-            name = ("split f16" if mode & 3 else "e4m3 lo") + (", warm L2" if mode & 4 else "")
+            name = ["e4m3 lo", "split f16", "split f16 kb64", "split f16 kb32"][mode & 3] + (", warm L2" if mode & 4 else "")
             rows.append((tag, name, bn, ms * 1e3, 2.0 * M * N * K / (ms * 1e-3) / 1e12))
         del w, Y
     for r in rows:
