@@ -14,7 +14,10 @@
 // 128-byte swizzle, Xl8 and W8 with 64-byte swizzle), warp 5's elected thread issues the UMMAs into
 // two TMEM accumulators (hi at column 0, lo at column BN), warps 0-3 combine them and store f32
 // rows. Every wait is bounded; a CTA that gives up lets its issued UMMAs complete (bounded) before
-// the TMEM is freed. Reached through tsn_selftest_gemm_lo8 only: no model path uses it.
+// the TMEM is freed. Reached through tsn_selftest_gemm_lo8 only: no model path uses it. The file
+// also holds gemm_splitkb_kernel, the split f16 product with 64- or 32-wide K blocks, the control
+// these experiments are timed against. Measured at the step's GEMM shapes, neither form beats
+// the production kernel's 64-wide K blocks and 4-stage ring at 176-wide tiles.
 #include <cudaTypedefs.h>
 #include <cuda_fp8.h>
 
