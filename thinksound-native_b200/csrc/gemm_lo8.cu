@@ -375,16 +375,16 @@ __global__ void k_w8(const __half * w, long long n, float scale, __nv_fp8_storag
 // 2-D tensor map over a row-major [rows][K] array of esize-byte elements; box {inner, box_rows}
 bool make_map_2d(CUtensorMap * m, const void * base, CUtensorMapDataType dt, uint32_t esize, uint64_t K, uint64_t rows,
                  uint32_t inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
-    static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
-    if (!enc) {
+    // looked up once; a function-local static is initialised once even when threads race to it
+    static const PFN_cuTensorMapEncodeTiled_v12000 enc = [] {
         cudaDriverEntryPointQueryResult q{};
         void * fn = nullptr;
         if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) != cudaSuccess ||
             q != cudaDriverEntryPointSuccess)
-            return false;
-        enc = (PFN_cuTensorMapEncodeTiled_v12000) fn;
-    }
-    if (((uintptr_t) base & 15) || (K * esize) % 16 || K % inner || box_rows == 0 || box_rows > 256) return false;
+            fn = nullptr;
+        return (PFN_cuTensorMapEncodeTiled_v12000) fn;
+    }();
+    if (!enc || ((uintptr_t) base & 15) || (K * esize) % 16 || K % inner || box_rows == 0 || box_rows > 256) return false;
     const cuuint64_t dims[2] = {K, rows};
     const cuuint64_t strides[1] = {K * esize};
     const cuuint32_t box[2] = {inner, box_rows};
