@@ -93,9 +93,11 @@ int tsn_selftest_gemm_lo8(tsn_device * dev, const void * W, const void * X, void
  * n < N[q]; act 0 none, 1 SiLU. W: the jobs' f16 rows of K back to back (job q from row sum N[<q]);
  * bias: f32, laid out the same way, or null; x: [nb][K] f32; Y: [nb][sum N] f32, job q's arm b at
  * b * sum N + sum N[<q]. K a multiple of 8 up to 1024; nb <= nb_cap <= 8 (the kernel instance's arm
- * capacity); blocks: the grid's cap (>= 1; results do not depend on it). Synchronises. */
+ * capacity); blocks: the grid's cap (>= 1; results do not depend on it). tc = 1: the tensor-core form
+ * the model uses for its modulation jobs (K a multiple of 64, act 0, at most 16 jobs; nb_cap unused).
+ * Synchronises. */
 int tsn_selftest_gemv_jobs(tsn_device * dev, const void * W, const void * bias, const void * x, void * Y,
-                           const uint32_t * N, int njobs, uint32_t K, int nb, int nb_cap, int act, int blocks);
+                           const uint32_t * N, int njobs, uint32_t K, int nb, int nb_cap, int act, int blocks, int tc);
 
 /* ------------------------------------------------------------------ runtime face (src/net.h) */
 /* Runtime::gemm (src/net.h:23-24): Y[M,N] = X[M,K]·W[N,K]^T (+bias), X/Y f32, W f16 (wf16=1) or

@@ -140,6 +140,41 @@ GEMV_JOB_CASES = [  # (Ns, K, nb, nb_cap, act): the step's batched GEMV (t-embed
 ]
 
 
+GEMV_TC_CASES = [  # (Ns, K, nb): the tensor-core form the model runs its clip/text modulations on
+    ((6144, 1000, 7, 1), 1024, 2),             # ragged jobs: partial 128-row tiles, one-row job
+    ((333, 64, 1023), 64, 1),                  # the smallest K, one arm
+    ((1024, 255, 999, 8), 1024, 8),            # eight arms: all 16 rows of the N tile
+    ((6144,) * 12 + (2048,) * 2, 1024, 2),     # the step's 14 jobs at the 8 s geometry
+    ((130, 129), 512, 3),
+]
+
+
+@pytest.mark.parametrize("Ns,K,nb", GEMV_TC_CASES)
+def test_gemv_tc_jobs_vs_f64(dev, Ns, K, nb):
+    """gemv_tc_kernel: weights as the tcgen05 M operand, the arms' split x as a 16-row N operand; every
+    row within f32 accumulation error of float64 and bit-identical for grids of 148, 37 and 1 CTAs (a
+    row's products run in one fixed order whichever CTA takes its tile)."""
+    rng = np.random.default_rng(31)
+    total = int(sum(Ns))
+    w = (rng.standard_normal((total, K), dtype=np.float32) * 0.03).astype(np.float16)
+    b = rng.standard_normal(total, dtype=np.float32)
+    x = rng.standard_normal((nb, K), dtype=np.float32)
+    W = torch.from_numpy(w.view(np.uint16).astype(np.int16)).cuda()
+    bd, xd = torch.from_numpy(b).cuda(), torch.from_numpy(x).cuda()
+    Y = torch.empty(nb * total + 8, dtype=torch.float32, device="cuda")
+    outs = []
+    for blocks in (148, 37, 1):
+        Y.fill_(float("nan"))
+        dev.selftest_gemv_jobs(W, bd, xd, Y, list(Ns), K, nb, nb, 0, blocks, tc=True)
+        outs.append(Y.cpu().numpy())
+    y = outs[0]
+    assert np.isnan(y[nb * total:]).all(), "wrote past the output"
+    ref = x.astype(np.float64) @ w.astype(np.float64).T + b
+    assert rel_l2(y[:nb * total].reshape(nb, total), ref) < 1e-5
+    for o in outs[1:]:
+        assert np.array_equal(o[:nb * total], y[:nb * total]), "result depends on the grid"
+
+
 @pytest.mark.parametrize("Ns,K,nb,nb_cap,act", GEMV_JOB_CASES)
 def test_gemv_jobs_ragged_vs_f64(dev, Ns, K, nb, nb_cap, act):
     """gemv_kernel over several jobs of different row counts (src/net.mm:51-56 per job): every row

@@ -58,6 +58,7 @@ int tsn_device_create(int ordinal, tsn_device ** out) {
     CKR(configure_attention_tc());
     CKR(configure_attention_short());
     CKR(configure_gemv());
+    CKR(configure_gemv_tc());
     *out = d.release();
     return TSN_OK;
 }
@@ -217,7 +218,7 @@ int tsn_selftest_gemm_lo8(tsn_device * dev, const void * W, const void * X, void
 }
 
 int tsn_selftest_gemv_jobs(tsn_device * dev, const void * W, const void * bias, const void * x, void * Y,
-                           const uint32_t * N, int njobs, uint32_t K, int nb, int nb_cap, int act, int blocks) {
+                           const uint32_t * N, int njobs, uint32_t K, int nb, int nb_cap, int act, int blocks, int tc) {
     if (!dev || !W || !x || !Y || !N) return fail(TSN_ERR_ARG, "null argument");
     if (njobs < 1 || njobs > 64 || blocks < 1 || act < 0 || act > 1) return fail(TSN_ERR_ARG, "bad job count, blocks or act");
     std::lock_guard<std::mutex> lk(dev->ctx.mu);
@@ -234,7 +235,12 @@ int tsn_selftest_gemv_jobs(tsn_device * dev, const void * W, const void * bias, 
                                    (int) N[q], (int) K, nb, act};
         row += N[q];
     }
-    CKR(launch_gemv(jobs.data(), njobs, (int) max_n, nb_cap, blocks, 0, c.d_err, c.stream));
+    if (tc) {
+        if (act || njobs > GEMV_MAX_JOBS) return fail(TSN_ERR_ARG, "the tensor-core GEMV takes no act and at most 16 jobs");
+        CKR(launch_gemv_tc(jobs.data(), njobs, blocks, c.d_err, c.stream));
+    } else {
+        CKR(launch_gemv(jobs.data(), njobs, (int) max_n, nb_cap, blocks, 0, c.d_err, c.stream));
+    }
     return c.sync();
 }
 

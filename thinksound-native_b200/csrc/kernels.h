@@ -191,6 +191,13 @@ cudaError_t configure_gemv();
 cudaError_t launch_gemv(const GemvJob * jobs, int njobs, int max_n, int nb, int sms, int ab_bf16, int * err, cudaStream_t s,
                         unsigned long long * trace = nullptr);
 int gemv_blocks(const GemvJob * jobs, int njobs, int nb, int sms);
+// The same jobs on the tensor cores (gemv_tc.cu): weights as the M operand in 128-row tiles, the
+// arms' split x as a resident 16-row N operand, one CTA per SM over all jobs' tiles. Jobs share x,
+// x_bs, K (64..GEMV_MAX_K, a multiple of 64) and nb (<= 8); f16 weights; no x_step, no act.
+cudaError_t configure_gemv_tc();
+cudaError_t launch_gemv_tc(const GemvJob * jobs, int njobs, int sms, int * err, cudaStream_t s,
+                           unsigned long long * trace = nullptr);
+int gemv_tc_blocks(const GemvJob * jobs, int njobs, int sms);
 
 // ---- per-forward conditioning prologue (src/dit_fwd.cpp:131-140, 166-167) ----
 // B batch rows = G generations x A CFG arms (A = 2, or 1 for a single-arm model); the per-

@@ -1270,7 +1270,17 @@ int Model::build_ops(std::vector<Op> & ops, int mode, float cfg) {
     // the clip/text modulations of every joint block (HBM-bound GEMVs, ~160 MB of weights at the
     // 8 s geometry) in one launch with the GPU to itself: beside the modulation GEMM they starved
     // for L2-to-SM bandwidth and held SMs that the next GEMM's CTAs needed
-    {
+    // on the tensor cores (gemv_tc.cu) with f16 weights; TSN_GEMV_CUDA_CORE=1: the CUDA-core gemv_kernel
+    if (!bfl && nmj <= GEMV_MAX_JOBS && std::getenv("TSN_GEMV_CUDA_CORE") == nullptr) {
+        Op go{[jb, nmj, sms, derr](cudaStream_t s) { return launch_gemv_tc(jb.data() + 2, nmj, sms, derr, s); }, 2, 0,
+              "adaln_gemv"};
+        go.traced = [jb, nmj, sms, derr](cudaStream_t s, unsigned long long * tr) {
+            return launch_gemv_tc(jb.data() + 2, nmj, sms, derr, s, tr);
+        };
+        go.ctas = gemv_tc_blocks(jb.data() + 2, nmj, sms);
+        go.trace_slots = 3;
+        p.add(go);
+    } else {
         Op go{[jb, nmj, H, nbm, sms, bfl, derr](cudaStream_t s) { return launch_gemv(jb.data() + 2, nmj, 6 * H, nbm, sms, bfl, derr, s); },
               2, 0, "adaln_gemv"};
         go.traced = [jb, nmj, H, nbm, sms, bfl, derr](cudaStream_t s, unsigned long long * tr) {

@@ -66,7 +66,7 @@ _SIGS = [
                                         C.POINTER(C.c_float)]),
     ("tsn_selftest_gemv_jobs", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.POINTER(C.c_uint32), C.c_int, C.c_uint32, C.c_int, C.c_int, C.c_int,
-                                         C.c_int]),
+                                         C.c_int, C.c_int]),
     ("tsn_gemm", C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                            C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
     ("tsn_gemm_noalloc", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -236,11 +236,12 @@ class Device:
                                           C.byref(ms)))
         return ms.value
 
-    def selftest_gemv_jobs(self, W, bias, x, Y, Ns, K, nb, nb_cap, act=0, blocks=148):
-        """The step's batched GEMV over several jobs (f16 rows back to back, Y [nb][sum Ns]); synchronises."""
+    def selftest_gemv_jobs(self, W, bias, x, Y, Ns, K, nb, nb_cap, act=0, blocks=148, tc=False):
+        """The step's batched GEMV over several jobs (f16 rows back to back, Y [nb][sum Ns]), on the CUDA
+        cores or (tc) the tensor cores; synchronises."""
         arr = (C.c_uint32 * len(Ns))(*Ns)
         check(lib().tsn_selftest_gemv_jobs(self.h, _p(W), _p(bias), _p(x), _p(Y), arr, len(Ns), K, nb, nb_cap,
-                                           act, blocks))
+                                           act, blocks, int(tc)))
 
     # --- net.h Runtime
     def gemm(self, wf16, W, X, Y, bias, M, N, K, ldx=0, ldw=0, ldy=0):
